@@ -1,0 +1,258 @@
+"""Generate golden vectors from the reference's own Triton kernels.
+
+Run in a container that has the reference package mounted (read-only) at
+``--ref`` (default ``/root/reference``)::
+
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+
+The reference cannot be imported as a package here (it needs ``torch_mlu``
+and Cambricon's Triton backend), so this script loads its kernel files by
+path under the Triton CPU interpreter with three shims, and copies no
+reference source into this repository:
+
+* ``torch_mlu_ops.triton.utils.get_total_core_num`` -> a constant core count;
+* ``device="mlu"`` allocations -> CPU tensors;
+* the package names ``torch_mlu_ops.triton.fla.*`` -> the files by path.
+
+The chunk path additionally needs two substitutions that the Cambricon
+toolchain provides and upstream Triton lacks (see ``_load_chunk_modules``).
+Outputs: ``*.npz`` files next to this script with inputs and outputs.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import os
+import sys
+import types
+import zlib
+
+os.environ.setdefault("TRITON_INTERPRET", "1")
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _install_shims(ref: str):
+    pkg = types.ModuleType("torch_mlu_ops")
+    pkg.__path__ = [ref]
+    sys.modules["torch_mlu_ops"] = pkg
+    tri = types.ModuleType("torch_mlu_ops.triton")
+    tri.__path__ = [os.path.join(ref, "triton")]
+    sys.modules["torch_mlu_ops.triton"] = tri
+    fla = types.ModuleType("torch_mlu_ops.triton.fla")
+    fla.__path__ = [os.path.join(ref, "triton", "fla")]
+    sys.modules["torch_mlu_ops.triton.fla"] = fla
+    utils = types.ModuleType("torch_mlu_ops.triton.utils")
+    utils.get_total_core_num = lambda: 8
+    sys.modules["torch_mlu_ops.triton.utils"] = utils
+
+    # "mlu" device requests become CPU allocations.
+    def _cpu(kw):
+        if str(kw.get("device", "")) == "mlu":
+            kw["device"] = "cpu"
+        return kw
+
+    for name in ("empty_like", "empty", "zeros"):
+        orig = getattr(torch, name)
+
+        def wrap(*a, _orig=orig, **kw):
+            return _orig(*a, **_cpu(kw))
+        setattr(torch, name, wrap)
+    orig_new_empty = torch.Tensor.new_empty
+    torch.Tensor.new_empty = lambda self, *a, **kw: orig_new_empty(self, *a, **_cpu(kw))
+
+
+def _load(modname: str, path: str, source_patch=None):
+    if source_patch is None:
+        spec = importlib.util.spec_from_file_location(modname, path)
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[modname] = mod
+        spec.loader.exec_module(mod)
+        return mod
+    with open(path) as f:
+        src = f.read()
+    src = source_patch(src)
+    mod = types.ModuleType(modname)
+    mod.__file__ = path
+    sys.modules[modname] = mod
+    # Triton's interpreter reads kernel source through inspect/linecache:
+    # register the in-memory text under the module's file name.
+    import linecache
+    fake = path + ".interp"
+    linecache.cache[fake] = (len(src), None, src.splitlines(True), fake)
+    exec(compile(src, fake, "exec"), mod.__dict__)
+    return mod
+
+
+def _rng_inputs(seed, B, T, H, HV, K, V, dtype=torch.float32):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, T, H, K, generator=g).to(dtype)
+    k = torch.randn(B, T, H, K, generator=g).to(dtype)
+    v = torch.randn(B, T, HV, V, generator=g).to(dtype)
+    gg = torch.nn.functional.logsigmoid(torch.randn(B, T, HV, generator=g))
+    beta = torch.sigmoid(torch.randn(B, T, HV, generator=g))
+    return q, k, v, gg, beta, g
+
+
+def _np(x):
+    return None if x is None else x.detach().float().numpy() if x.dtype != torch.int64 else x.numpy()
+
+
+def gen_recurrent_fn(ref: str):
+    """Decode kernel with a V-first slot cache (``fused_recurrent_fn.py``)."""
+    mod = _load("torch_mlu_ops.triton.fla.fused_recurrent_fn",
+                os.path.join(ref, "triton/fla/fused_recurrent_fn.py"))
+    cases = []
+    # (name, N, T, H, HV, K, V, l2norm, spec, inplace, pad, beta_per_v)
+    cases.append(("decode_basic", 6, 1, 2, 4, 16, 16, True, False, True, True, False))
+    cases.append(("decode_nonorm_betav", 5, 1, 2, 2, 16, 8, False, False, True, False, True))
+    cases.append(("decode_spec", 4, 3, 1, 2, 8, 16, True, True, True, True, False))
+    cases.append(("decode_notinplace", 3, 1, 2, 4, 16, 16, True, False, False, False, False))
+    for (name, N, T, H, HV, K, V, l2, spec, inplace, pad, bpv) in cases:
+        q, k, v, gg, beta, gen = _rng_inputs(zlib.crc32(name.encode()) % 1000, 1, N * T, H, HV, K, V)
+        if bpv:
+            beta = torch.sigmoid(torch.randn(1, N * T, HV, V, generator=gen))
+        slots = 3 * N + 2
+        cache = torch.randn(slots, HV, V, K, generator=gen) * 0.5
+        cu = torch.arange(0, N * T + 1, T, dtype=torch.int64)
+        perm = torch.randperm(slots, generator=gen)
+        idx = perm[: N * max(T, 1)].reshape(N, T).clone() if inplace else perm[:N].clone()
+        if pad:
+            idx[1, 0] = -1
+        nacc = None
+        if spec:
+            # the initial state is read from column nacc-1 of each index row
+            nacc = torch.randint(1, T + 1, (N,), generator=gen)
+        cache_in = cache.clone()
+        o, ht = mod.fused_recurrent_gated_delta_rule(
+            q, k, v, gg, beta, 0.37, cache, inplace_final_state=inplace, cu_seqlens=cu,
+            ssm_state_indices=idx, num_accepted_tokens=nacc, use_qk_l2norm_in_kernel=l2)
+        np.savez_compressed(
+            os.path.join(HERE, f"rfn_{name}.npz"),
+            q=_np(q), k=_np(k), v=_np(v), g=_np(gg), beta=_np(beta), scale=np.float64(0.37),
+            cache_in=_np(cache_in), cu_seqlens=cu.numpy(), ssm_state_indices=idx.numpy(),
+            num_accepted_tokens=(nacc.numpy() if nacc is not None else np.zeros(0, np.int64)),
+            l2norm=np.bool_(l2), inplace=np.bool_(inplace), o=_np(o), final_state=_np(ht))
+        print("wrote", name)
+
+
+def gen_recurrent(ref: str):
+    """Plain K-first recurrence (``fused_recurrent.py``), incl. config 0 shape."""
+    mod = _load("torch_mlu_ops.triton.fla.fused_recurrent",
+                os.path.join(ref, "triton/fla/fused_recurrent.py"))
+    # (name, B, T, H, HV, K, V, l2norm, varlen, h0)
+    cases = [("plain_gva", 1, 37, 2, 4, 16, 16, True, False, True),
+             ("plain_varlen", 1, 50, 2, 2, 16, 8, False, True, True),
+             ("cfg0_t64", 1, 64, 4, 4, 64, 64, True, False, False)]
+    for (name, B, T, H, HV, K, V, l2, varlen, use_h0) in cases:
+        q, k, v, gg, beta, gen = _rng_inputs(zlib.crc32(name.encode()) % 1000 + 7, B, T, H, HV, K, V)
+        cu = torch.tensor([0, 11, 11, 30, T], dtype=torch.int64) if varlen else None
+        N = B if cu is None else len(cu) - 1
+        h0 = torch.randn(N, HV, K, V, generator=gen) * 0.3 if use_h0 else None
+        o, ht = mod.fused_recurrent_gated_delta_rule_fwd(
+            q, k, v, g=gg, beta=beta, scale=K ** -0.5, initial_state=h0,
+            output_final_state=True, use_qk_l2norm_in_kernel=l2, cu_seqlens=cu)
+        np.savez_compressed(
+            os.path.join(HERE, f"rec_{name}.npz"),
+            q=_np(q), k=_np(k), v=_np(v), g=_np(gg), beta=_np(beta), scale=np.float64(K ** -0.5),
+            h0=(_np(h0) if h0 is not None else np.zeros(0, np.float32)),
+            cu_seqlens=(cu.numpy() if cu is not None else np.zeros(0, np.int64)),
+            l2norm=np.bool_(l2), o=_np(o), final_state=_np(ht))
+        print("wrote", name)
+
+
+def _load_chunk_modules(ref: str):
+    """Load the chunk-path kernels.  Two substitutions are needed to run them
+    on upstream Triton: the Cambricon-only integer row indexing of a register
+    block in the KK^T kernel is expressed as a masked row reduction, and the
+    absent native ``torch_mlu_ops.solve_tril`` is served by the same file's
+    own Triton merge kernel (``solve_tril.py``'s ``merge_16x16_to_64x64``
+    path, which the reference keeps as its non-native implementation)."""
+    _load("torch_mlu_ops.triton.fla.utils", os.path.join(ref, "triton/fla/utils.py"))
+    _load("torch_mlu_ops.triton.fla.index", os.path.join(ref, "triton/fla/index.py"))
+    _load("torch_mlu_ops.triton.fla.op", os.path.join(ref, "triton/fla/op.py"))
+
+    def cumsum_patch(src):
+        return "import warnings\n" + src
+
+    _load("torch_mlu_ops.triton.fla.cumsum", os.path.join(ref, "triton/fla/cumsum.py"), cumsum_patch)
+
+    def kkt_patch(src):
+        row = "tl.sum(tl.where(tl.arange(0, H)[:, None] == id_h, {0}, 0), 0)"
+        src = src.replace("b_beta[id_h,:]", row.format("b_beta"))
+        src = src.replace("b_g[id_h,:]", row.format("b_g"))
+        return src
+
+    _load("torch_mlu_ops.triton.fla.chunk_scaled_dot_kkt",
+          os.path.join(ref, "triton/fla/chunk_scaled_dot_kkt.py"), kkt_patch)
+    st = _load("torch_mlu_ops.triton.fla.solve_tril", os.path.join(ref, "triton/fla/solve_tril.py"))
+    for m in ("wy_fast", "chunk_delta_h", "chunk_o"):
+        _load(f"torch_mlu_ops.triton.fla.{m}", os.path.join(ref, f"triton/fla/{m}.py"))
+    return st
+
+
+def gen_chunk(ref: str):
+    st = _load_chunk_modules(ref)
+    names = [n for n in dir(st) if "merge_16x16_to_64x64" in n]
+    if not names:
+        print("solve_tril merge kernel not found; chunk fixtures skipped")
+        return
+    merge = getattr(st, names[0])
+
+    def native_solve_tril(A, output, cu_seqlens):
+        # The merge kernel stores only the 16x16 blocks that hold valid rows;
+        # the native op returns a full block (zeros outside the triangle), so
+        # clear the output first.
+        import triton
+        output.zero_()
+        B, T, H, BT = A.shape
+        index = sys.modules["torch_mlu_ops.triton.fla.index"]
+        ci = index.prepare_chunk_indices(cu_seqlens, BT) if cu_seqlens is not None else None
+        NT = triton.cdiv(T, BT) if cu_seqlens is None else len(ci)
+        merge[NT, B * H](A=A, Ai=output, cu_seqlens=cu_seqlens, chunk_indices=ci, T=T, H=H, BT=BT,
+              USE_TMA=False, DOT_PRECISION="ieee")
+
+    torch.ops.torch_mlu_ops = types.SimpleNamespace(solve_tril=native_solve_tril)
+    chunk = _load("torch_mlu_ops.triton.fla.chunk", os.path.join(ref, "triton/fla/chunk.py"))
+    # H == HV only: the reference KK^T kernel indexes k by v-head (see oracle).
+    cases = [("chunk_t130", 1, 130, 2, 2, 32, 32, False, True),
+             ("chunk_varlen", 1, 200, 2, 2, 32, 16, True, True)]
+    for (name, B, T, H, HV, K, V, varlen, use_h0) in cases:
+        q, k, v, gg, beta, gen = _rng_inputs(zlib.crc32(name.encode()) % 1000 + 11, B, T, H, HV, K, V)
+        q = torch.nn.functional.normalize(q, dim=-1)
+        k = torch.nn.functional.normalize(k, dim=-1)
+        cu = torch.tensor([0, 64, 90, T], dtype=torch.int64) if varlen else None
+        N = B if cu is None else len(cu) - 1
+        h0 = torch.randn(N, HV, K, V, generator=gen) * 0.3 if use_h0 else None
+        o, ht, *_ = chunk.chunk_gated_delta_rule_fwd(
+            q, k, v, gg, beta, K ** -0.5, h0, True, cu_seqlens=cu, allow_tf32=False)
+        np.savez_compressed(
+            os.path.join(HERE, f"chk_{name}.npz"),
+            q=_np(q), k=_np(k), v=_np(v), g=_np(gg), beta=_np(beta), scale=np.float64(K ** -0.5),
+            h0=(_np(h0) if h0 is not None else np.zeros(0, np.float32)),
+            cu_seqlens=(cu.numpy() if cu is not None else np.zeros(0, np.int64)),
+            o=_np(o), final_state=_np(ht))
+        print("wrote", name)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", default="")
+    a = ap.parse_args()
+    _install_shims(a.ref)
+    torch.manual_seed(0)
+    if a.only in ("", "rfn"):
+        gen_recurrent_fn(a.ref)
+    if a.only in ("", "rec"):
+        gen_recurrent(a.ref)
+    if a.only in ("", "chunk"):
+        gen_chunk(a.ref)
+
+
+if __name__ == "__main__":
+    main()
