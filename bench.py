@@ -1,0 +1,515 @@
+"""Benchmark of the B200 GDN forward (driver contract: one JSON line on rank 0).
+
+Headline workload: Qwen3-Next GDN layer chunked prefill,
+B=1, T=8192, 16 q/k heads, 32 v heads, d=128, bf16 q/k/v, fp32 g/beta, in-kernel
+q/k L2 norm, fp32 final state.  A "step" is one ``chunk_gated_delta_rule``
+call over that batch.  With N GPUs (torchrun) every rank runs its own
+config-1 sequence (sharding by sequence, no collective on the data path):
+weak scaling, ``value`` = N * 8192 tokens / max-over-ranks time.
+
+Also reported: recurrent decode microseconds per step and
+its fraction of measured HBM bandwidth; a CPU baseline (the oracle's fp32
+chunked restatement of the reference algorithm) timed on the host's cores.
+
+``--impl reference`` times that CPU restatement alone on the same config (a
+bounded token sample per step), since the reference itself targets Cambricon
+MLUs and cannot run here.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# BASELINE config 1 / 3 shapes
+CFG1 = dict(B=1, T=8192, H=16, HV=32, K=128, V=128)
+CFG3 = dict(N=256, slots=1024, H=16, HV=32, K=128, V=128)
+BT = 64
+CPU_SAMPLE_TOKENS = 2048
+
+
+def flops_per_token_head(K, V, bt=BT):
+    # 2 * (BT*(3K+2V) + 3KV): KK^T, w, u, w.h, K^T v_new, q.h, qK^T, A v_new
+    return 2 * (bt * (3 * K + 2 * V) + 3 * K * V)
+
+
+def stage_flops_per_token_head(K, V, bt=BT):
+    """Algorithmic FLOPs per token per v-head of each stage (bf16 GEMMs)."""
+    return {
+        "wy": 2 * bt * K + 2 * bt * K + 2 * bt * V,       # KK^T, w, u
+        "state": 2 * K * V + 2 * K * V,                     # w.h, K^T v_new
+        "out": 2 * K * V + 2 * bt * K + 2 * bt * V,         # q.h, qK^T, A v_new
+    }
+
+
+def prefill_bytes(T, H, HV, K, V, nseq, state_out=True):
+    b = T * (2 * H * K * 2 + 2 * HV * V * 2 + 2 * HV * 4)
+    if state_out:
+        b += nseq * HV * K * V * 4
+    return b
+
+
+def _load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def _load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        return json.load(open(p))
+    except Exception:
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling in the background during timing."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.uuid:
+            cmd += ["-i", self.uuid]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            parts = [x.strip() for x in l.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[3:7]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------
+# CPU baseline: the oracle's fp32 chunked restatement, heads split over cores
+# --------------------------------------------------------------------------
+
+def _cpu_worker(args):
+    import numpy as np
+    import oracle
+    q, k, v, g, beta = args
+    t0 = time.perf_counter()
+    oracle.chunk_gated_delta_rule(q, k, v, g, beta, None, None, True, None, True, dtype=np.float32)
+    return time.perf_counter() - t0
+
+
+def _cpu_inputs(T, H, HV, K, V, seed=1):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((1, T, H, K)).astype(np.float32)
+    k = rng.standard_normal((1, T, H, K)).astype(np.float32)
+    v = rng.standard_normal((1, T, HV, V)).astype(np.float32)
+    g = -np.log1p(np.exp(-rng.standard_normal((1, T, HV)))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((1, T, HV))))).astype(np.float32)
+    G = HV // H
+    parts = []
+    for h in range(H):  # one q/k head and its v-heads per task
+        parts.append((q[:, :, h:h + 1], k[:, :, h:h + 1], v[:, :, h * G:(h + 1) * G],
+                      g[:, :, h * G:(h + 1) * G], beta[:, :, h * G:(h + 1) * G]))
+    return parts
+
+
+class CpuBaseline:
+    def __init__(self, cfg, sample_tokens=CPU_SAMPLE_TOKENS):
+        import multiprocessing as mp
+        self.cores = os.cpu_count() or 1
+        # one single-threaded BLAS per worker process: no oversubscription
+        for var in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS"):
+            os.environ[var] = "1"
+        self.pool = mp.get_context("spawn").Pool(min(self.cores, cfg["H"]))
+        for var in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS"):
+            os.environ.pop(var, None)
+        self.parts = _cpu_inputs(sample_tokens, cfg["H"], cfg["HV"], cfg["K"], cfg["V"])
+        self.tokens = sample_tokens
+
+    def step(self):
+        t0 = time.perf_counter()
+        self.pool.map(_cpu_worker, self.parts, chunksize=1)
+        return time.perf_counter() - t0
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+
+def _cpu_model():
+    try:
+        for l in open("/proc/cpuinfo"):
+            if l.startswith("model name"):
+                return l.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+# --------------------------------------------------------------------------
+
+def _dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def _max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def run_ours(a):
+    import ctypes
+
+    import torch
+
+    import domesticated_torch_mlu_ops_b200 as ops
+    from domesticated_torch_mlu_ops_b200 import _lib
+
+    world, rank, local = _dist_setup(a.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    hbm, tc_burst, tc_sust, peak_kind = _load_peaks()
+    cfg = dict(CFG1)
+    B, T, H, HV, K, V = (cfg[x] for x in ("B", "T", "H", "HV", "K", "V"))
+
+    cpu = CpuBaseline(cfg) if (rank == 0 and world == 1 and not a.no_cpu) else None
+
+    gen = torch.Generator().manual_seed(1 + rank)
+    q_h = torch.randn(B, T, H, K, generator=gen).bfloat16().pin_memory()
+    k_h = torch.randn(B, T, H, K, generator=gen).bfloat16().pin_memory()
+    v_h = torch.randn(B, T, HV, V, generator=gen).bfloat16().pin_memory()
+    g_h = torch.nn.functional.logsigmoid(torch.randn(B, T, HV, generator=gen)).pin_memory()
+    b_h = torch.sigmoid(torch.randn(B, T, HV, generator=gen)).pin_memory()
+    q, k, v, g, beta = (x.to(dev) for x in (q_h, k_h, v_h, g_h, b_h))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    lib = _lib.load()
+
+    def step():
+        return ops.chunk_gated_delta_rule(q, k, v, g, beta, None, None, True,
+                                          use_qk_l2norm_in_kernel=True)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- device-resident timing (per-step events, L2 flushed between) ----
+    stream = torch.cuda.current_stream(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(a.steps)]
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        pass
+    _barrier(world)
+    torch.cuda.synchronize()
+    n0 = lib.gdn_kernel_launch_count()
+    with ClockSampler(uuid) as clk:
+        for i in range(a.steps):
+            flush.zero_()
+            evs[i][0].record(stream)
+            step()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+    _barrier(world)
+    launches = lib.gdn_kernel_launch_count() - n0
+    step_ms = [s.elapsed_time(e) for s, e in evs]
+    ms_local = sum(step_ms) / len(step_ms)
+    ms = _max_over_ranks(ms_local, world)
+
+    # ---- per-kernel timing with the library's stage events ----
+    nst = 8
+    sev = [torch.cuda.Event(enable_timing=True) for _ in range(nst)]
+    handles = (ctypes.c_void_p * nst)(*[ctypes.c_void_p(e.cuda_event) for e in sev])
+    stage_ms = {}
+    names = None
+    reps = max(3, min(a.steps, 10))
+    for _ in range(reps):
+        flush.zero_()
+        o, ht, info = _chunk_with_events(ops, q, k, v, g, beta, handles, nst)
+        torch.cuda.synchronize()
+        names = info["stages"]
+        for i, nm in enumerate(names):
+            stage_ms.setdefault(nm, []).append(sev[i].elapsed_time(sev[i + 1]))
+    stage_avg = {nm: sum(x) / len(x) for nm, x in stage_ms.items()}
+
+    # ---- end-to-end through the public API with host buffers ----
+    o_h = torch.empty(B, T, HV, V, dtype=torch.bfloat16).pin_memory()
+    ht_h = torch.empty(B, HV, K, V, dtype=torch.float32).pin_memory()
+    e2e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(a.steps)]
+    _barrier(world)
+    torch.cuda.synchronize()
+    for i in range(a.steps):
+        flush.zero_()
+        e2e_evs[i][0].record(stream)
+        qd, kd, vd, gd, bd = (x.to(dev, non_blocking=True) for x in (q_h, k_h, v_h, g_h, b_h))
+        o, ht = ops.chunk_gated_delta_rule(qd, kd, vd, gd, bd, None, None, True,
+                                           use_qk_l2norm_in_kernel=True)
+        o_h.copy_(o, non_blocking=True)
+        ht_h.copy_(ht, non_blocking=True)
+        e2e_evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(sum(s.elapsed_time(e) for s, e in e2e_evs) / a.steps, world)
+    h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, g_h, b_h))
+    d2h = o_h.numel() * o_h.element_size() + ht_h.numel() * ht_h.element_size()
+
+    # ---- decode (config 3) ----
+    dec = _decode_bench(ops, dev, a, hbm, flush) if not a.no_decode else None
+
+    # ---- CPU baseline (rank 0, N=1) ----
+    cpu_line = None
+    if cpu is not None:
+        cpu.step()  # warm-up (imports in the workers)
+        t_cpu = []
+        t_end = time.perf_counter() + 20.0
+        while time.perf_counter() < t_end and len(t_cpu) < 5:
+            t_cpu.append(cpu.step())
+        cpu.close()
+        best = min(t_cpu)
+        cpu_line = {"value": cpu.tokens / best, "unit": "tokens/s", "cores": cpu.cores,
+                    "kind": "port",
+                    "sample": f"{cpu.tokens} tokens of the config-1 shape (all 32 v-heads), numpy fp32 "
+                              f"chunked restatement, {cpu.cores} worker processes, best of {len(t_cpu)}; "
+                              f"host {_cpu_model()}"}
+
+    if rank == 0:
+        tokens = world * B * T
+        value = tokens / (ms / 1e3)
+        fl_tok = flops_per_token_head(K, V)
+        total_flops = B * T * HV * fl_tok
+        sfl = stage_flops_per_token_head(K, V)
+        dom = max(stage_avg, key=stage_avg.get)
+        dom_key = dom.split(":")[0]
+        dom_flops = B * T * HV * sfl.get(dom_key, 0)
+        traffic = _load_traffic().get(dom)
+        roof = {"kernel": dom, "bound": "tensor", "achieved": dom_flops / (stage_avg[dom] * 1e-3) / 1e12,
+                "peak": tc_burst, "unit": "TFLOP/s", "peak_kind": f"{peak_kind} bf16 burst",
+                "traffic": traffic}
+        roof["frac"] = roof["achieved"] / roof["peak"]
+        pbytes = prefill_bytes(B * T, H, HV, K, V, B)
+        line = {
+            "metric": "prefill tokens/s (Qwen3-Next GDN layer chunked prefill, BASELINE config 1)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q/k/v, "
+            "logsigmoid/sigmoid gates; BASELINE config 1 distributions)",
+            "config": {"workload": "config1: chunk_gated_delta_rule B=1 T=8192 H=16 HV=32 K=V=128 "
+                       "bf16, in-kernel q/k L2 norm, fp32 final state", "tokens_per_gpu": B * T,
+                       "parallelism": f"sequence-sharded x{world} (one sequence per rank)",
+                       "l2": "256 MiB buffer written between timed steps"},
+            "roofline": roof,
+            "path_roofline": {"flops": total_flops, "tflops": total_flops / (ms * 1e-3) / 1e12,
+                              "frac_tensor": total_flops / (ms * 1e-3) / 1e12 / tc_burst,
+                              "algorithmic_bytes": pbytes,
+                              "frac_hbm": pbytes / (ms * 1e-3) / 1e9 / hbm},
+            "stages_ms": stage_avg,
+            "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "decode": dec,
+            "cpu_baseline": cpu_line,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def _chunk_with_events(ops, q, k, v, g, beta, handles, nst):
+    """One chunk_gated_delta_rule call with the library's stage events set."""
+    import ctypes
+
+    import torch
+
+    from domesticated_torch_mlu_ops_b200 import _lib, gdn
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    o = torch.empty_like(v)
+    ht = torch.empty(B, HV, K, V, dtype=torch.float32, device=q.device)
+    args = _lib.ChunkArgs(
+        q=gdn._ptr(q), k=gdn._ptr(k), v=gdn._ptr(v), g=gdn._ptr(g), beta=gdn._ptr(beta),
+        initial_state=None, o=gdn._ptr(o), final_state=gdn._ptr(ht), cu_seqlens=None,
+        B=B, T=T, N=B, H=H, HV=HV, K=K, V=V, qkv_dtype=_lib.GDN_BF16, cu_dtype=_lib.GDN_I64,
+        scale=0.0, use_qk_l2norm=1, state_v_first=0, force_generic=0,
+        stage_events=ctypes.cast(handles, ctypes.POINTER(ctypes.c_void_p)), n_stage_events=nst)
+    lib = _lib.load()
+    nbytes = lib.gdn_chunk_workspace_size(ctypes.byref(args))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    args.workspace = ctypes.c_void_p(ws.data_ptr())
+    args.workspace_bytes = nbytes
+    n0 = lib.gdn_kernel_launch_count()
+    _lib.check(lib.gdn_chunk_fwd(ctypes.byref(args), gdn._stream(q.device)))
+    n = lib.gdn_kernel_launch_count() - n0
+    return o, ht, {"stages": _stage_names(n)}
+
+
+def _stage_names(n):
+    # launch order of the chunk path (see the launchers in csrc/)
+    if n == 6:
+        return ["plan", "prep:q", "prep:k", "wy", "state", "out"]
+    if n == 3:
+        return ["wy", "state", "out"]
+    if n == 4:
+        return ["plan", "wy", "state", "out"]
+    return [f"k{i}" for i in range(n)]
+
+
+def _decode_bench(ops, dev, a, hbm, flush):
+    import torch
+    c = CFG3
+    N, S, H, HV, K, V = c["N"], c["slots"], c["H"], c["HV"], c["K"], c["V"]
+    gen = torch.Generator().manual_seed(3)
+    q = torch.randn(1, N, H, K, generator=gen).bfloat16().to(dev)
+    k = torch.randn(1, N, H, K, generator=gen).bfloat16().to(dev)
+    v = torch.randn(1, N, HV, V, generator=gen).bfloat16().to(dev)
+    g = torch.nn.functional.logsigmoid(torch.randn(1, N, HV, generator=gen)).to(dev)
+    beta = torch.sigmoid(torch.randn(1, N, HV, generator=gen)).to(dev)
+    cache = (torch.randn(S, HV, V, K, generator=gen) * 0.02).to(dev)
+    idx = torch.randperm(S, generator=gen)[:N].to(dev)
+    cu = torch.arange(N + 1, device=dev)
+
+    def step():
+        ops.fused_recurrent_gated_delta_rule_fn(q, k, v, g, beta, K ** -0.5, cache, True, cu, idx,
+                                                None, True)
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(max(a.steps, 10))]
+    for s, e in ev:
+        flush.zero_()
+        s.record()
+        step()
+        e.record()
+    torch.cuda.synchronize()
+    us = sum(s.elapsed_time(e) for s, e in ev) / len(ev) * 1e3
+    nbytes = N * (2 * HV * K * V * 4 + 2 * H * K * 2 + 2 * HV * V * 2 + 2 * HV * 4 + 8)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"workload": "config3: 256 sequences x 1 token, cache [1024,32,128,128] f32",
+            "us_per_step": us, "algorithmic_bytes": nbytes, "achieved_gbs": gbs,
+            "peak_gbs": hbm, "frac_hbm": gbs / hbm}
+
+
+def run_reference(a):
+    """CPU restatement of the reference algorithm (the oracle port), timed on
+    the host's cores on a bounded sample of the config-1 workload."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = dict(CFG1)
+    cpu = CpuBaseline(cfg, sample_tokens=a.ref_tokens)
+    for _ in range(max(1, min(a.warmup, 2))):
+        cpu.step()
+    t = [cpu.step() for _ in range(a.steps)]
+    cpu.close()
+    sec = sum(t) / len(t)
+    value = cpu.tokens / sec
+    line = {
+        "impl": "reference",
+        "metric": "prefill tokens/s (Qwen3-Next GDN layer chunked prefill, BASELINE config 1)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config1: chunk_gated_delta_rule B=1 T=8192 H=16 HV=32 K=V=128, "
+                   f"timed on a {cpu.tokens}-token sample per step"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu.cores, "kind": "port",
+                         "sample": f"{cpu.tokens} tokens of config 1 per step, numpy fp32 chunked "
+                                   f"restatement of the reference's six stages; host {_cpu_model()}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode measurement")
+    ap.add_argument("--ref-tokens", type=int, default=2048)
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

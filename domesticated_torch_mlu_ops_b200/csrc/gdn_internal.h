@@ -1,0 +1,63 @@
+// Internal launch interface between the C-ABI layer (gdn_api.cu) and the
+// kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "gdn_b200.h"
+
+namespace gdn {
+
+// Workspace carve-up shared by the chunk paths.  Offsets are 256-byte aligned.
+struct ChunkWorkspace {
+  size_t err;            // int32[4] device error word
+  size_t chunk_offsets;  // int64[N + 1]
+  size_t gc;             // f32 [Ttot][HV] chunk-local cumsum of g
+  size_t qn, kn;         // f32 [Ttot][H][K] (generic path: normalised q, k)
+  size_t w, u, vnew;     // generic: f32 [Ttot][HV][K|V]
+  size_t hs;             // generic: f32 [chunks][HV][K][V]
+  size_t total;
+};
+
+// Count of kernels launched by this library (gdn_kernel_launch_count).
+void note_launch(int n = 1);
+
+// Per-call launch instrumentation: records the caller's optional stage
+// events (gdn_chunk_args::stage_events) and counts launches.
+struct LaunchHooks {
+  void* const* events;
+  int n;
+  int next = 0;
+  LaunchHooks(void* const* e, int count) : events(e), n(count) {}
+  void pre(cudaStream_t s) {
+    if (events && next < n) cudaEventRecord(static_cast<cudaEvent_t>(events[next++]), s);
+    note_launch();
+  }
+  void end(cudaStream_t s) {
+    if (events && next < n) cudaEventRecord(static_cast<cudaEvent_t>(events[next++]), s);
+  }
+};
+
+// Upper bound on the number of 64-token chunks of a packed batch.
+inline int64_t chunk_upper_bound(int64_t total_tokens, int64_t nseq) {
+  return (total_tokens + 63) / 64 + nseq;
+}
+
+ChunkWorkspace plan_generic_workspace(const gdn_chunk_args& a);
+bool tc_path_applies(const gdn_chunk_args& a);
+size_t tc_workspace_bytes(const gdn_chunk_args& a);
+
+cudaError_t launch_recurrent_vfirst(const gdn_recurrent_args& a, cudaStream_t s);
+cudaError_t launch_recurrent_kfirst(const gdn_recurrent_plain_args& a, cudaStream_t s);
+cudaError_t launch_chunk_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s);
+cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s);
+cudaError_t launch_solve_tril(const float* A, void* out, int out_dtype, const void* cu,
+                              int cu_dtype, int64_t N, int64_t B, int64_t T, int H, int BT,
+                              cudaStream_t s);
+// chunk_offsets[0..N] from cu_seqlens (or the equal-length batch).
+cudaError_t launch_chunk_plan(const void* cu, int cu_dtype, int64_t N, int64_t T,
+                              int64_t* chunk_offsets, cudaStream_t s, int chunk = 64);
+
+}  // namespace gdn

@@ -1,0 +1,330 @@
+"""Public gated delta-rule (GDN) forward ops, drop-in for ``torch_mlu_ops.triton_ops``.
+
+Same names, argument order, keyword names, defaults and return values as the
+reference facade (``triton_ops.py:81-285``); the work runs in
+``libgdn_b200.so`` (hand-written sm_100a CUDA) through its C ABI.  There is no
+CPU or Triton path: the ops raise if the tensors are not on a CUDA device or
+the library is not built.
+
+Differences from the reference, all supersets:
+
+* ``chunk_gated_delta_rule`` takes ``use_qk_l2norm_in_kernel`` (q and k are
+  divided by ``sqrt(sum(x^2) + 1e-6)``, the formula of
+  ``triton/fla/fused_recurrent_fn.py:110-112``).
+* ``allow_tf32`` is accepted and ignored: fp32 inputs always take the
+  full-precision fp32 path; bf16/fp16 inputs take the tensor-core path with
+  fp32 accumulation.
+* ``scale=None`` selects ``K ** -0.5`` in every op (the recurrent reference
+  kernels would fail on ``None``).
+* ``fused_recurrent_gated_delta_rule`` also accepts ``ssm_state_indices``,
+  ``inplace_final_state`` and ``num_accepted_tokens``; with
+  ``ssm_state_indices`` it runs the slot-indexed decode of
+  ``fused_recurrent_gated_delta_rule_fn``.
+* Outputs of PAD sequences (negative initial slot index) are zero instead of
+  left unwritten.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.GDN_F32, torch.bfloat16: _lib.GDN_BF16, torch.float16: _lib.GDN_F16}
+_IDT = {torch.int32: _lib.GDN_I32, torch.int64: _lib.GDN_I64}
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(dev):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _cuda(name, *ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError(f"{name}: every tensor must be on a CUDA device (got {t.device})")
+
+
+def _qkv_dtype(q, k, v):
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError(f"q, k, v must share a dtype (got {q.dtype}, {k.dtype}, {v.dtype})")
+    if q.dtype not in _DT:
+        raise ValueError(f"unsupported dtype {q.dtype}: expected float32, bfloat16 or float16")
+    return _DT[q.dtype]
+
+
+def _f32(t):
+    return None if t is None else t.to(torch.float32).contiguous()
+
+
+def _idx(t):
+    if t is None:
+        return None, _lib.GDN_I64
+    if t.dtype not in _IDT:
+        t = t.to(torch.int64)
+    return t, _IDT[t.dtype]
+
+
+def _check_shapes(q, k, v):
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("q, k must be [B, T, H, K] and v must be [B, T, HV, V]")
+    if q.shape != k.shape:
+        raise ValueError(f"q {tuple(q.shape)} and k {tuple(k.shape)} must have the same shape")
+    if v.shape[:2] != k.shape[:2]:
+        raise ValueError(f"v {tuple(v.shape)} must match k {tuple(k.shape)} in [B, T]")
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    if HV % H != 0:
+        raise ValueError(f"HV={HV} must be a multiple of H={H}")
+    return B, T, H, HV, K, V
+
+
+# ---------------------------------------------------------------------------
+# chunked prefill
+# ---------------------------------------------------------------------------
+
+def chunk_gated_delta_rule(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    g: torch.Tensor,
+    beta: torch.Tensor,
+    scale: float | None = None,
+    initial_state: torch.Tensor = None,
+    output_final_state: bool = False,
+    cu_seqlens: torch.LongTensor | None = None,
+    chunk_indices: torch.Tensor | None = None,
+    chunk_offsets: torch.Tensor | None = None,
+    allow_tf32: bool = True,
+    state_v_first: bool = False,
+    use_qk_l2norm_in_kernel: bool = False,
+    *,
+    force_generic: bool = False,
+):
+    """Chunked gated delta-rule forward (``triton_ops.py:81-165``).
+
+    q, k ``[B, T, H, K]``; v ``[B, T, HV, V]``; g, beta ``[B, T, HV]``;
+    initial_state ``[N, HV, K, V]`` (``[N, HV, V, K]`` with ``state_v_first``).
+    Returns ``(o [B, T, HV, V] in q.dtype, final_state fp32 or None)``.
+    ``chunk_indices`` / ``chunk_offsets`` are accepted for signature
+    compatibility; the chunk table is built on the device from ``cu_seqlens``.
+    """
+    del chunk_indices, chunk_offsets, allow_tf32
+    _cuda("chunk_gated_delta_rule", q, k, v, g, beta, initial_state, cu_seqlens)
+    B, T, H, HV, K, V = _check_shapes(q, k, v)
+    if K > 128 or V > 128:
+        raise ValueError(f"K={K}, V={V}: both must be <= 128 (triton/fla/chunk.py:27-28)")
+    if g.shape != v.shape[:3] or beta.shape != v.shape[:3]:
+        raise ValueError(f"g {tuple(g.shape)} and beta {tuple(beta.shape)} must be [B, T, HV]")
+    if cu_seqlens is not None and B != 1:
+        raise ValueError("cu_seqlens requires batch size 1 (packed sequences)")
+    qkv = _qkv_dtype(q, k, v)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    g, beta = _f32(g), _f32(beta)
+    cu, cu_dt = _idx(cu_seqlens)
+    N = B if cu is None else cu.numel() - 1
+    shape_state = (N, HV, V, K) if state_v_first else (N, HV, K, V)
+    h0 = None
+    if initial_state is not None:
+        if tuple(initial_state.shape) != shape_state:
+            raise ValueError(f"initial_state must be {shape_state}, got {tuple(initial_state.shape)}")
+        h0 = _f32(initial_state)
+    dev = q.device
+    o = torch.empty_like(v, dtype=q.dtype)
+    ht = torch.empty(shape_state, dtype=torch.float32, device=dev) if output_final_state else None
+    args = _lib.ChunkArgs(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta),
+        initial_state=_ptr(h0), o=_ptr(o), final_state=_ptr(ht), cu_seqlens=_ptr(cu),
+        workspace=None, workspace_bytes=0, B=B, T=T, N=N, H=H, HV=HV, K=K, V=V,
+        qkv_dtype=qkv, cu_dtype=cu_dt, scale=float(scale) if scale is not None else 0.0,
+        use_qk_l2norm=int(bool(use_qk_l2norm_in_kernel)), state_v_first=int(bool(state_v_first)),
+        force_generic=int(bool(force_generic)))
+    lib = _lib.load()
+    nbytes = lib.gdn_chunk_workspace_size(ctypes.byref(args))
+    if nbytes == 0:
+        _lib.check(_lib.GDN_ERR_INVALID)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    args.workspace = ctypes.c_void_p(ws.data_ptr())
+    args.workspace_bytes = nbytes
+    with torch.cuda.device(dev):
+        _lib.check(lib.gdn_chunk_fwd(ctypes.byref(args), _stream(dev)))
+    return o, ht
+
+
+# ---------------------------------------------------------------------------
+# recurrent forms
+# ---------------------------------------------------------------------------
+
+def fused_recurrent_gated_delta_rule_fn(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    g: torch.Tensor | None = None,
+    beta: torch.Tensor | None = None,
+    scale: float = None,
+    initial_state: torch.Tensor = None,
+    inplace_final_state: bool = True,
+    cu_seqlens: torch.LongTensor | None = None,
+    ssm_state_indices: torch.Tensor = None,
+    num_accepted_tokens: torch.Tensor = None,
+    use_qk_l2norm_in_kernel: bool = False,
+):
+    """Slot-indexed recurrent decode (``triton_ops.py:228-285`` ->
+    ``triton/fla/fused_recurrent_fn.py:161-233``).
+
+    The state cache is V-first ``[slots, HV, V, K]`` fp32 (the kernel's
+    layout, ``fused_recurrent_fn.py:101-104``).  With
+    ``inplace_final_state=True`` the cache is updated in place at
+    ``ssm_state_indices[n, t]`` and returned; otherwise a fresh
+    ``[B*T, HV, V, K]`` tensor receives the state after every token.
+    """
+    _cuda("fused_recurrent_gated_delta_rule_fn", q, k, v, g, beta, initial_state, cu_seqlens,
+          ssm_state_indices, num_accepted_tokens)
+    B, T, H, HV, K, V = _check_shapes(q, k, v)
+    if K > 128 or V > 128:
+        raise ValueError(f"K={K}, V={V}: both must be <= 128 (fused_recurrent_fn.py:181-182)")
+    if cu_seqlens is not None and B != 1:
+        raise ValueError("cu_seqlens requires batch size 1 (packed sequences)")
+    qkv = _qkv_dtype(q, k, v)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    if beta is None:
+        beta = torch.ones(v.shape[:3], dtype=torch.float32, device=v.device)
+    beta_per_v = beta.dim() == v.dim()
+    g, beta = _f32(g), _f32(beta)
+    cu, cu_dt = _idx(cu_seqlens)
+    N = B if cu is None else cu.numel() - 1
+    idx, idx_dt = _idx(ssm_state_indices)
+    nacc, nacc_dt = _idx(num_accepted_tokens)
+    if scale is None:
+        scale = K ** -0.5
+    if initial_state is not None:
+        if initial_state.dtype != torch.float32:
+            raise ValueError("initial_state must be float32")
+        if initial_state.dim() != 4 or tuple(initial_state.shape[1:]) != (HV, V, K):
+            raise ValueError(f"initial_state must be [slots, {HV}, {V}, {K}] (V-first), "
+                             f"got {tuple(initial_state.shape)}")
+        if initial_state.stride()[1:] != (V * K, K, 1):
+            raise ValueError("initial_state rows must be contiguous [HV, V, K] blocks")
+    if inplace_final_state:
+        if initial_state is None or idx is None:
+            raise ValueError("inplace_final_state=True needs initial_state and ssm_state_indices")
+        final_state = initial_state
+    else:
+        final_state = torch.empty(B * T, HV, V, K, dtype=torch.float32, device=q.device)
+    if idx is None:
+        s_seq, s_tok = 1, 1
+    elif idx.dim() == 1:
+        s_seq, s_tok = idx.stride(0), 1
+    else:
+        s_seq, s_tok = idx.stride()
+    o = torch.empty_like(v)
+    args = _lib.RecurrentArgs(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta),
+        initial_state=_ptr(initial_state), o=_ptr(o), final_state=_ptr(final_state),
+        cu_seqlens=_ptr(cu), ssm_state_indices=_ptr(idx), num_accepted_tokens=_ptr(nacc),
+        B=B, T=T, N=N, H=H, HV=HV, K=K, V=V, qkv_dtype=qkv, cu_dtype=cu_dt,
+        idx_dtype=idx_dt, nacc_dtype=nacc_dt,
+        stride_init_state_token=initial_state.stride(0) if initial_state is not None else 0,
+        stride_final_state_token=final_state.stride(0),
+        stride_indices_seq=s_seq, stride_indices_tok=s_tok, scale=float(scale),
+        use_qk_l2norm=int(bool(use_qk_l2norm_in_kernel)), beta_per_v=int(beta_per_v),
+        inplace_final_state=int(bool(inplace_final_state)))
+    dev = q.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().gdn_fused_recurrent_fwd(ctypes.byref(args), _stream(dev)))
+    return o, final_state
+
+
+def fused_recurrent_gated_delta_rule(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    g: torch.Tensor | None = None,
+    gk: torch.Tensor | None = None,
+    gv: torch.Tensor | None = None,
+    beta: torch.Tensor | None = None,
+    scale: float = None,
+    initial_state: torch.Tensor = None,
+    output_final_state: bool = False,
+    use_qk_l2norm_in_kernel: bool = False,
+    cu_seqlens: torch.LongTensor | None = None,
+    *,
+    ssm_state_indices: torch.Tensor | None = None,
+    inplace_final_state: bool = True,
+    num_accepted_tokens: torch.Tensor | None = None,
+):
+    """Recurrent gated delta rule (``triton_ops.py:168-226`` ->
+    ``triton/fla/fused_recurrent.py:134-187``): K-first state
+    ``[N, HV, K, V]``, optional per-channel decays ``gk`` / ``gv``.
+
+    Given ``ssm_state_indices`` it is the slot-indexed decode of
+    :func:`fused_recurrent_gated_delta_rule_fn` on a V-first cache instead.
+    """
+    if ssm_state_indices is not None:
+        if gk is not None or gv is not None:
+            raise ValueError("gk/gv are not supported with ssm_state_indices")
+        return fused_recurrent_gated_delta_rule_fn(
+            q, k, v, g, beta, scale, initial_state, inplace_final_state, cu_seqlens,
+            ssm_state_indices, num_accepted_tokens, use_qk_l2norm_in_kernel)
+    _cuda("fused_recurrent_gated_delta_rule", q, k, v, g, gk, gv, beta, initial_state, cu_seqlens)
+    B, T, H, HV, K, V = _check_shapes(q, k, v)
+    if K > 128 or V > 128:
+        raise ValueError(f"K={K}, V={V}: both must be <= 128 (fused_recurrent.py:155-156)")
+    if cu_seqlens is not None and B != 1:
+        raise ValueError("cu_seqlens requires batch size 1 (packed sequences)")
+    qkv = _qkv_dtype(q, k, v)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    if beta is None:
+        beta = torch.ones(v.shape[:3], dtype=torch.float32, device=v.device)
+    beta_per_v = beta.dim() == v.dim()
+    g, gk, gv, beta = _f32(g), _f32(gk), _f32(gv), _f32(beta)
+    cu, cu_dt = _idx(cu_seqlens)
+    N = B if cu is None else cu.numel() - 1
+    h0 = None
+    if initial_state is not None:
+        if tuple(initial_state.shape) != (N, HV, K, V):
+            raise ValueError(f"initial_state must be {(N, HV, K, V)}, got {tuple(initial_state.shape)}")
+        h0 = _f32(initial_state)
+    o = torch.empty_like(v)
+    ht = torch.empty(N, HV, K, V, dtype=torch.float32, device=q.device) if output_final_state else None
+    args = _lib.RecurrentPlainArgs(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), gk=_ptr(gk), gv=_ptr(gv), beta=_ptr(beta),
+        initial_state=_ptr(h0), o=_ptr(o), final_state=_ptr(ht), cu_seqlens=_ptr(cu),
+        B=B, T=T, N=N, H=H, HV=HV, K=K, V=V, qkv_dtype=qkv, cu_dtype=cu_dt,
+        scale=float(scale) if scale is not None else 0.0,
+        use_qk_l2norm=int(bool(use_qk_l2norm_in_kernel)), beta_per_v=int(beta_per_v))
+    dev = q.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().gdn_recurrent_plain_fwd(ctypes.byref(args), _stream(dev)))
+    return o, ht
+
+
+def solve_tril(input: torch.Tensor, output: torch.Tensor = None, cu_seqlens: torch.Tensor = None,
+               out_dtype: torch.dtype = torch.float):
+    """(I + input)^-1 per chunk block (``_ops.py:6232-6257``; native op
+    ``include/torch_mlu_ops.h:1052-1054``).  input fp32 ``[B, T, H, BT]``,
+    BT in {16, 32, 64}; output bf16/fp16/fp32 of the same shape."""
+    _cuda("solve_tril", input, output, cu_seqlens)
+    if input.dtype != torch.float32 or input.dim() != 4:
+        raise ValueError("input must be a float32 [B, T, H, BT] tensor")
+    if output is None:
+        output = torch.empty(input.shape, device=input.device, dtype=out_dtype)
+    if output.shape != input.shape or output.dtype not in _DT:
+        raise ValueError("output must match input's shape with dtype float32/bfloat16/float16")
+    B, T, H, BT = input.shape
+    x = input.contiguous()
+    out = output if output.is_contiguous() else torch.empty_like(output)
+    cu, cu_dt = _idx(cu_seqlens)
+    N = B if cu is None else cu.numel() - 1
+    dev = input.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().gdn_solve_tril(
+            _ptr(x), _ptr(out), _DT[out.dtype], _ptr(cu), cu_dt, N, B, T, H, BT, _stream(dev)))
+    if out is not output:
+        output.copy_(out)
+    return output

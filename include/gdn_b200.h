@@ -1,0 +1,206 @@
+/*
+ * gdn_b200.h - C ABI of the B200 gated delta-rule (GDN) forward library
+ * (libgdn_b200.so).
+ *
+ * Plain pointers and sizes only; no torch types.  Every tensor is a dense,
+ * row-major (C-contiguous) device buffer in the reference's shapes.  Callers
+ * allocate every input, output and workspace buffer; the library never
+ * allocates or frees device memory and keeps no pointer after a call returns.
+ * Work is enqueued on the caller's stream (`stream` is a cudaStream_t passed
+ * as void*; NULL = legacy default stream) and calls do not synchronise.
+ *
+ * Return codes: GDN_OK (0) or a negative GDN_ERR_*; gdn_last_error() gives a
+ * thread-local message for the last failing call on this thread.
+ *
+ * Reference interfaces replaced (paths inside the torch_mlu_ops package):
+ *   gdn_chunk_fwd          <- triton_ops.py:81-165 chunk_gated_delta_rule
+ *                             -> triton/fla/chunk.py:10-74 chunk_gated_delta_rule_fwd
+ *   gdn_fused_recurrent_fwd<- triton_ops.py:228-285 fused_recurrent_gated_delta_rule_fn
+ *                             -> triton/fla/fused_recurrent_fn.py:161-233
+ *   gdn_recurrent_plain_fwd<- triton_ops.py:168-226 fused_recurrent_gated_delta_rule
+ *                             -> triton/fla/fused_recurrent.py:134-187
+ *   gdn_solve_tril         <- include/torch_mlu_ops.h:1052-1054 tmo::torch_api::solve_tril
+ *                             (Python: _ops.py:6232-6257; AOTI shim config_inductor.py:484-490)
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+enum {
+  GDN_OK = 0,
+  GDN_ERR_INVALID = -1,      /* bad argument: null pointer, shape, dtype */
+  GDN_ERR_UNSUPPORTED = -2,  /* valid for the reference but not built here */
+  GDN_ERR_CUDA = -3,         /* a CUDA runtime call failed */
+  GDN_ERR_WORKSPACE = -4,    /* workspace missing or smaller than required */
+  GDN_ERR_DEVICE = -5        /* a kernel reported a failure in the error word */
+};
+
+/* Element types of tensor arguments. */
+enum { GDN_F32 = 0, GDN_BF16 = 1, GDN_F16 = 2, GDN_I32 = 3, GDN_I64 = 4 };
+
+/*
+ * Chunked prefill.  Shapes (C-contiguous):
+ *   q, k [B, T, H, K]; v, o [B, T, HV, V] (all of qkv_dtype: f32/bf16/f16)
+ *   g, beta [B, T, HV] f32 (g: log decay; beta: write strength)
+ *   initial_state / final_state f32 [N, HV, K, V], or [N, HV, V, K] when
+ *   state_v_first; either may be NULL (zeros in / no state out).
+ *   cu_seqlens [N+1] (cu_dtype I32/I64) or NULL: with it B must be 1 and the
+ *   N sequences are packed along T; without it N = B sequences of T tokens.
+ * HV must be a multiple of H (v-head hv reads q/k head hv / (HV/H)).
+ * K, V <= 128.  scale <= 0 selects K^-0.5.  With use_qk_l2norm, q and k rows
+ * are divided by sqrt(sum(x^2) + 1e-6) first.  Chunk size is 64 tokens.
+ */
+typedef struct gdn_chunk_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const float* beta;
+  const float* initial_state;
+  void* o;
+  float* final_state;
+  const void* cu_seqlens;
+  void* workspace;
+  size_t workspace_bytes;
+  int64_t B, T, N;
+  int32_t H, HV, K, V;
+  int32_t qkv_dtype;
+  int32_t cu_dtype;
+  float scale;
+  int32_t use_qk_l2norm;
+  int32_t state_v_first;
+  int32_t force_generic;  /* 1: use the SIMT fp32 path even where tcgen05 applies */
+  /* Optional instrumentation: an array of n_stage_events cudaEvent_t
+   * handles.  When non-NULL, event i is recorded on `stream` just before the
+   * i-th kernel of the call and the last event after the final kernel
+   * (recording stops when the array runs out).  NULL for normal use. */
+  void* const* stage_events;
+  int32_t n_stage_events;
+} gdn_chunk_args;
+
+/* Workspace bytes gdn_chunk_fwd needs for these arguments (pointer fields
+ * are ignored).  Returns 0 and sets the last error for invalid arguments. */
+GDN_API size_t gdn_chunk_workspace_size(const gdn_chunk_args* args);
+
+GDN_API int gdn_chunk_fwd(const gdn_chunk_args* args, void* stream);
+
+/* Reads back (synchronously, on `stream`) the device error word that the
+ * chunk kernels keep in `workspace`; returns GDN_OK or GDN_ERR_DEVICE and
+ * clears the word. */
+GDN_API int gdn_chunk_check_device_error(void* workspace, void* stream);
+
+/*
+ * Recurrent forward with a V-first state cache: the slot-indexed decode of
+ * fused_recurrent_gated_delta_rule_fn.
+ *   q, k [B, T, H, K]; v, o [B, T, HV, V] (qkv_dtype); g [B, T, HV] f32 or NULL;
+ *   beta [B, T, HV] f32, or [B, T, HV, V] when beta_per_v.
+ *   initial_state f32 rows of [HV, V, K], row r at initial_state +
+ *   r * stride_init_state_token (elements); NULL = zero state.
+ *   final_state: with inplace_final_state the per-token state of token t of
+ *   sequence n is written to row ssm_state_indices[n, t] (skipped when
+ *   negative), usually aliasing initial_state; otherwise to row bos + t.
+ *   ssm_state_indices [N] or [N, *] (idx_dtype I32/I64, strides in elements)
+ *   or NULL (then the initial state row of sequence n is bos, as in the
+ *   reference).  num_accepted_tokens [N] (nacc_dtype) or NULL: the initial
+ *   state is read from column num_accepted_tokens[n]-1 of the index row.
+ *   A sequence whose initial index is negative (PAD) is skipped and its
+ *   output rows are set to zero.
+ * K, V <= 128 and K a multiple of 4.
+ */
+typedef struct gdn_recurrent_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const float* beta;
+  const float* initial_state;
+  void* o;
+  float* final_state;
+  const void* cu_seqlens;
+  const void* ssm_state_indices;
+  const void* num_accepted_tokens;
+  int64_t B, T, N;
+  int32_t H, HV, K, V;
+  int32_t qkv_dtype, cu_dtype, idx_dtype, nacc_dtype;
+  int64_t stride_init_state_token;
+  int64_t stride_final_state_token;
+  int64_t stride_indices_seq;
+  int64_t stride_indices_tok;
+  float scale;
+  int32_t use_qk_l2norm;
+  int32_t beta_per_v;
+  int32_t inplace_final_state;
+} gdn_recurrent_args;
+
+GDN_API int gdn_fused_recurrent_fwd(const gdn_recurrent_args* args, void* stream);
+
+/*
+ * Plain recurrence with a K-first state, fused_recurrent_gated_delta_rule.
+ *   q, k [B, T, H, K]; v, o [B, T, HV, V]; g [B, T, HV] f32 or NULL;
+ *   gk [B, T, HV, K] f32 or NULL; gv [B, T, HV, V] f32 or NULL;
+ *   beta [B, T, HV] f32, or [B, T, HV, V] when beta_per_v.
+ *   initial_state [N, HV, K, V] f32 or NULL; final_state [N, HV, K, V] f32 or
+ *   NULL.  scale <= 0 selects K^-0.5.
+ */
+typedef struct gdn_recurrent_plain_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const float* gk;
+  const float* gv;
+  const float* beta;
+  const float* initial_state;
+  void* o;
+  float* final_state;
+  const void* cu_seqlens;
+  int64_t B, T, N;
+  int32_t H, HV, K, V;
+  int32_t qkv_dtype, cu_dtype;
+  float scale;
+  int32_t use_qk_l2norm;
+  int32_t beta_per_v;
+} gdn_recurrent_plain_args;
+
+GDN_API int gdn_recurrent_plain_fwd(const gdn_recurrent_plain_args* args, void* stream);
+
+/*
+ * (I + A)^-1 for every BT x BT chunk block of a strictly lower-triangular A.
+ *   A f32 [B, T, H, BT]; out [B, T, H, BT] of out_dtype (F32/BF16/F16);
+ *   cu_seqlens [N+1] (I32/I64, B == 1) or NULL.  BT in {16, 32, 64}.
+ * Entries above the diagonal and columns past a partial chunk's end are
+ * written as zero.  Mirrors solve_tril(input, output, cu_seqlens).
+ */
+GDN_API int gdn_solve_tril(const float* A, void* out, int32_t out_dtype,
+                   const void* cu_seqlens, int32_t cu_dtype, int64_t N,
+                   int64_t B, int64_t T, int32_t H, int32_t BT, void* stream);
+
+/* Message for the last failing call on this thread ("" if none). */
+GDN_API const char* gdn_last_error(void);
+
+/* Number of kernels this library has launched in the process so far
+ * (monotonic, all threads).  Lets a caller count launches in a region. */
+GDN_API uint64_t gdn_kernel_launch_count(void);
+
+/* GDN_ABI_VERSION of the built library. */
+GDN_API int gdn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */

@@ -1,0 +1,108 @@
+"""CPU checks of the C ABI: the library loads, exports every function that
+include/gdn_b200.h declares, its struct layouts match the ctypes mirrors, and
+argument validation returns status codes (no GPU needed for any of this)."""
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from domesticated_torch_mlu_ops_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gdn_b200.h")
+
+
+def _declared():
+    txt = open(HEADER).read()
+    return re.findall(r"GDN_API\s+[\w\s\*]*?\b(gdn_\w+)\s*\(", txt)
+
+
+def test_header_declares_expected_api():
+    assert sorted(_declared()) == sorted(_lib.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert lib.gdn_abi_version() == 1
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True).stdout
+    exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
+    assert set(_declared()) <= exported
+    # nothing but the C ABI is exported
+    assert {s for s in exported if not s.startswith("gdn_")} <= {"_init", "_fini"}
+
+
+@pytest.mark.parametrize("struct,cname", [(_lib.ChunkArgs, "gdn_chunk_args"),
+                                          (_lib.RecurrentArgs, "gdn_recurrent_args"),
+                                          (_lib.RecurrentPlainArgs, "gdn_recurrent_plain_args")])
+def test_struct_layout_matches_c(tmp_path, struct, cname):
+    fields = [f[0] for f in struct._fields_]
+    src = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', 'int main(void){',
+           f'printf("%zu\\n", sizeof({cname}));']
+    src += [f'printf("%zu\\n", offsetof({cname}, {f}));' for f in fields]
+    src += ['return 0;}']
+    c = tmp_path / "layout.c"
+    c.write_text("\n".join(src))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-o", str(exe), str(c)], check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    assert vals[0] == ctypes.sizeof(struct)
+    assert vals[1:] == [getattr(struct, f).offset for f in fields]
+
+
+def _chunk_args(**kw):
+    base = dict(B=1, T=8192, N=1, H=16, HV=32, K=128, V=128, qkv_dtype=_lib.GDN_BF16,
+                cu_dtype=_lib.GDN_I64)
+    base.update(kw)
+    return _lib.ChunkArgs(**base)
+
+
+def test_workspace_size_and_validation():
+    lib = _lib.load()
+    ok = lib.gdn_chunk_workspace_size(ctypes.byref(_chunk_args()))
+    assert ok > 0
+    # HV not a multiple of H
+    assert lib.gdn_chunk_workspace_size(ctypes.byref(_chunk_args(HV=24, H=16))) == 0
+    assert b"multiple" in lib.gdn_last_error()
+    # K > 128 (reference asserts K <= 128, triton/fla/chunk.py:27)
+    assert lib.gdn_chunk_workspace_size(ctypes.byref(_chunk_args(K=256))) == 0
+    # bad dtype
+    assert lib.gdn_chunk_workspace_size(ctypes.byref(_chunk_args(qkv_dtype=7))) == 0
+    # varlen needs B == 1
+    a = _chunk_args(B=2, N=3)
+    a.cu_seqlens = ctypes.c_void_p(16)
+    assert lib.gdn_chunk_workspace_size(ctypes.byref(a)) == 0
+
+
+def test_invalid_calls_return_codes_without_touching_the_gpu():
+    lib = _lib.load()
+    a = _chunk_args()
+    # null input pointers
+    assert lib.gdn_chunk_fwd(ctypes.byref(a), None) == _lib.GDN_ERR_INVALID
+    # workspace too small
+    for name in ("q", "k", "v", "g", "beta", "o"):
+        setattr(a, name, ctypes.c_void_p(256))
+    a.workspace = ctypes.c_void_p(256)
+    a.workspace_bytes = 16
+    assert lib.gdn_chunk_fwd(ctypes.byref(a), None) == _lib.GDN_ERR_WORKSPACE
+    r = _lib.RecurrentArgs(B=1, T=1, N=1, H=2, HV=4, K=6, V=8, qkv_dtype=_lib.GDN_BF16)
+    assert lib.gdn_fused_recurrent_fwd(ctypes.byref(r), None) == _lib.GDN_ERR_UNSUPPORTED
+    r = _lib.RecurrentArgs(B=1, T=1, N=1, H=2, HV=4, K=8, V=8, qkv_dtype=_lib.GDN_BF16)
+    for name in ("q", "k", "v", "beta", "o", "initial_state", "final_state"):
+        setattr(r, name, ctypes.c_void_p(256))
+    r.inplace_final_state = 1
+    assert lib.gdn_fused_recurrent_fwd(ctypes.byref(r), None) == _lib.GDN_ERR_INVALID
+    assert b"ssm_state_indices" in lib.gdn_last_error()
+    assert lib.gdn_solve_tril(None, None, 0, None, 0, 1, 1, 64, 2, 48, None) == _lib.GDN_ERR_INVALID
+
+
+def test_python_errors_are_value_errors():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.GDN_ERR_INVALID)
+    with pytest.raises(_lib.GdnError):
+        _lib.check(_lib.GDN_ERR_CUDA)

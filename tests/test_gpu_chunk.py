@@ -1,0 +1,150 @@
+"""GPU parity of the chunked prefill against the fp64 oracle and the
+reference's golden vectors (tests/golden/chk_*.npz)."""
+
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gdn_testutil import (BF16_MAX_ABS, BF16_REL_RMS, FP32_REL_RMS, make_inputs, max_abs, np64,
+                          rel_rms)
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def ops():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import domesticated_torch_mlu_ops_b200 as m
+    return m
+
+
+def _t(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "chk_*.npz"))),
+                         ids=os.path.basename)
+def test_chunk_matches_reference_golden(ops, path):
+    d = dict(np.load(path))
+    h0 = _t(d["h0"]) if d["h0"].size else None
+    cu = _t(d["cu_seqlens"]) if d["cu_seqlens"].size else None
+    o, ht = ops.chunk_gated_delta_rule(_t(d["q"]), _t(d["k"]), _t(d["v"]), _t(d["g"]),
+                                       _t(d["beta"]), float(d["scale"]), h0, True, cu)
+    assert rel_rms(np64(o), d["o"]) < FP32_REL_RMS
+    assert rel_rms(np64(ht), d["final_state"]) < FP32_REL_RMS
+
+
+def _check(ops, seed, B, T, H, HV, K, V, dtype, cu=None, h0_std=0.0, l2=True, state_v_first=False,
+           force_generic=False, scale=None):
+    N = B if cu is None else len(cu) - 1
+    q, k, v, g, beta, h0 = make_inputs(seed, B, T, H, HV, K, V, dtype=dtype,
+                                       nseq_state=N if h0_std else None, state_std=h0_std)
+    if h0 is not None and state_v_first:
+        h0 = h0.transpose(-1, -2).contiguous()
+    cut = None if cu is None else torch.tensor(cu, dtype=torch.int32).cuda()
+    o, ht = ops.chunk_gated_delta_rule(q, k, v, g, beta, scale, h0, True, cut, None, None, True,
+                                       state_v_first, l2, force_generic=force_generic)
+    ro, rht = oracle.chunk_gated_delta_rule(np64(q), np64(k), np64(v), np64(g), np64(beta), scale,
+                                            np64(h0), True, cu, l2, state_v_first)
+    e_o, e_h = rel_rms(np64(o), ro), rel_rms(np64(ht), rht)
+    if dtype == torch.float32:
+        assert e_o < FP32_REL_RMS and e_h < FP32_REL_RMS, (e_o, e_h)
+    else:
+        m_o = max_abs(np64(o), ro)
+        assert e_o < BF16_REL_RMS and m_o < BF16_MAX_ABS, (e_o, m_o)
+        assert e_h < BF16_REL_RMS, e_h
+    return o, ht
+
+
+def test_config0_fp32(ops):
+    """fp32, B=1 T=256 H=4 d=64, zero initial state."""
+    _check(ops, 0, 1, 256, 4, 4, 64, 64, torch.float32)
+
+
+@pytest.mark.parametrize("T", [1, 17, 64, 65, 200])
+def test_fp32_lengths(ops, T):
+    _check(ops, 40 + T, 2, T, 2, 4, 32, 48, torch.float32, h0_std=0.1)
+
+
+def test_fp32_state_v_first_varlen(ops):
+    _check(ops, 5, 1, 300, 2, 4, 64, 32, torch.float32, cu=[0, 1, 64, 64, 150, 300], h0_std=0.05,
+           state_v_first=True)
+
+
+@pytest.mark.parametrize("force_generic", [False, True])
+def test_bf16_qwen_shape(ops, force_generic):
+    _check(ops, 1, 1, 1024, 16, 32, 128, 128, torch.bfloat16, force_generic=force_generic)
+
+
+@pytest.mark.parametrize("force_generic", [False, True])
+def test_bf16_varlen_with_states(ops, force_generic):
+    cu = [0, 100, 164, 700, 701, 1500]
+    _check(ops, 2, 1, 1500, 16, 32, 128, 128, torch.bfloat16, cu=cu, h0_std=0.02,
+           force_generic=force_generic)
+
+
+def test_fp16_small(ops):
+    _check(ops, 3, 2, 130, 2, 2, 128, 128, torch.float16, h0_std=0.02, scale=0.1)
+
+
+def test_bf16_config1_full_size(ops):
+    """B=1, T=8192, 16 q/k heads, 32 v heads, d=128, bf16."""
+    _check(ops, 1, 1, 8192, 16, 32, 128, 128, torch.bfloat16)
+
+
+def test_config2_full_size_packing_equivalence(ops):
+    """BASELINE config 2 (16 sequences, lengths U[512, 8192], states N(0, 0.02)):
+    the packed varlen call must equal running every sequence alone (a
+    size-independent property), and stay finite."""
+    rng = np.random.default_rng(2)
+    lens = rng.integers(512, 8193, size=16)
+    cu = np.concatenate([[0], np.cumsum(lens)])
+    T = int(cu[-1])
+    q, k, v, g, beta, h0 = make_inputs(2, 1, T, 16, 32, 128, 128, nseq_state=16, state_std=0.02)
+    cut = torch.from_numpy(cu).cuda()
+    o, ht = ops.chunk_gated_delta_rule(q, k, v, g, beta, None, h0, True, cut,
+                                       use_qk_l2norm_in_kernel=True)
+    assert torch.isfinite(o.float()).all() and torch.isfinite(ht).all()
+    for n in (0, 7, 15):
+        s, e = int(cu[n]), int(cu[n + 1])
+        o1, h1 = ops.chunk_gated_delta_rule(q[:, s:e], k[:, s:e], v[:, s:e], g[:, s:e],
+                                            beta[:, s:e], None, h0[n:n + 1], True,
+                                            use_qk_l2norm_in_kernel=True)
+        assert torch.equal(o1, o[:, s:e])
+        assert torch.equal(h1[0], ht[n])
+
+
+def test_chunk_equals_recurrent_on_gpu(ops):
+    """The chunked op and the token-by-token op agree (fp32)."""
+    q, k, v, g, beta, h0 = make_inputs(9, 1, 333, 2, 4, 64, 64, dtype=torch.float32,
+                                       nseq_state=1, state_std=0.1)
+    o1, h1 = ops.chunk_gated_delta_rule(q, k, v, g, beta, 0.125, h0, True,
+                                        use_qk_l2norm_in_kernel=True)
+    o2, h2 = ops.fused_recurrent_gated_delta_rule(q, k, v, g, None, None, beta, 0.125, h0, True, True)
+    assert rel_rms(np64(o1), np64(o2)) < FP32_REL_RMS
+    assert rel_rms(np64(h1), np64(h2)) < FP32_REL_RMS
+
+
+def test_solve_tril(ops):
+    rng = np.random.default_rng(4)
+    for BT, cu in ((64, None), (32, np.array([0, 10, 80, 100])), (16, None)):
+        B = 2 if cu is None else 1
+        T = 100
+        H = 3
+        A = np.zeros((B, T, H, BT), np.float32)
+        bounds = oracle.seq_bounds(B, T, cu)
+        flatA = A.reshape(B * T, H, BT)
+        for bos, eos in bounds:
+            for s in range(bos, eos, BT):
+                L = min(BT, eos - s)
+                blk = np.tril(rng.standard_normal((H, L, L)) * 0.2, -1)
+                flatA[s:s + L, :, :L] = blk.transpose(1, 0, 2)
+        ref = oracle.solve_tril(flatA.astype(np.float64), bounds, BT).reshape(B, T, H, BT)
+        for dt, tol in ((torch.float32, 1e-6), (torch.bfloat16, 1e-2)):
+            out = ops.solve_tril(_t(A), None, None if cu is None else _t(cu), dt)
+            assert rel_rms(np64(out), ref) < tol
