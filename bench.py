@@ -290,6 +290,9 @@ def run_ours(a):
     # ---- per-kernel timing with the library's stage events ----
     nst = 8
     sev = [torch.cuda.Event(enable_timing=True) for _ in range(nst)]
+    for e in sev:  # torch creates the CUDA event on first record
+        e.record(stream)
+    torch.cuda.synchronize()
     handles = (ctypes.c_void_p * nst)(*[ctypes.c_void_p(e.cuda_event) for e in sev])
     stage_ms = {}
     names = None

@@ -1,10 +1,673 @@
-// tcgen05 chunk path (bf16/fp16, K = V = 128).  Placeholder until the
-// tensor-core kernels land: the generic path serves every shape.
+// Tensor-core (tcgen05) chunked gated delta-rule forward for bf16/fp16 inputs
+// with K = V = 128 and 64-token chunks: the Qwen3-Next GDN prefill.
+//
+// Two kernels replace the reference's six stages (triton/fla/chunk.py:10-74):
+//
+// tc_wy_kernel, one CTA per (chunk, v-head), fully parallel:
+//   * q, k, v chunk tiles staged with cp.async into no-swizzle UMMA images;
+//   * L2-norm factors r_q, r_k of every row (fused_recurrent_fn.py:110-112
+//     formula) and the chunk-local cumsum G of g (cumsum.py:20-77);
+//   * S_kk = K K^T and S_qk = Q K^T on tcgen05 (bf16 in, fp32 in TMEM);
+//   * A = beta_i exp(G_i - G_j) r_k,i r_k,j S_kk, strictly lower
+//     (chunk_scaled_dot_kkt.py:25-100); (I + A)^-1 by column forward
+//     substitution in fp32 shared memory (the native solve_tril,
+//     include/torch_mlu_ops.h:1052);
+//   * W = T diag(beta exp(G) r_k) K and U = T diag(beta) V on tcgen05
+//     (wy_fast.py:18-119), with the row scalings folded into the bf16 A
+//     operand exactly where the reference rounds to bf16;
+//   * P = tril_incl(exp(G_i - G_j) r_q,i r_k,j S_qk) (chunk_o.py:133-160);
+//   * per-row output / decay scales a_i = scale exp(G_i) r_q,i,
+//     b_i = exp(G_last - G_i) r_k,i and gamma = exp(G_last).
+//   W and P are written as ready-to-use UMMA operand images.
+//
+// tc_state_kernel, one CTA per (sequence, v-head, V-slice of VS columns),
+// serial over the sequence's chunks (chunk_delta_h.py:28-197 fused with
+// chunk_o.py:30-170).  The fp32 state slice h (128 x VS) lives in registers
+// (thread t owns row t); its bf16 copy in shared memory is the B operand of
+//   X = W h,  Y = Q h                         (tcgen05, M=64)
+//   v_new = U - X, V~ = diag(b) v_new         (epilogue, fp32 -> bf16)
+//   dH = K^T V~,  O = P v_new                 (tcgen05, M=128 / M=64)
+//   h <- gamma h + dH,  o = a * Y + scale * O  (epilogue)
+// so h and v_new never leave the SM.  The next chunk's operands are
+// prefetched with cp.async while the current chunk computes.
+//
+// Every mbarrier wait is bounded; on timeout the kernel records an error in
+// the workspace error word, frees its TMEM and exits.
+
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
+#include "umma.cuh"
+
+#include <type_traits>
 
 namespace gdn {
-bool tc_path_applies(const gdn_chunk_args&) { return false; }
-size_t tc_workspace_bytes(const gdn_chunk_args&) { return 0; }
-cudaError_t launch_chunk_tc(const gdn_chunk_args&, cudaStream_t) { return cudaErrorNotSupported; }
+
+namespace tc {
+
+constexpr int D = 128;                  // K = V = 128
+constexpr int kImg64x128 = 64 * D * 2;  // 16 KiB
+constexpr int kImg64x64 = 64 * 64 * 2;  // 8 KiB
+constexpr int RS128 = (D / 8) * 128;    // image row stride of a 128-column tile
+constexpr int RS64 = (64 / 8) * 128;    // image row stride of a 64-column tile
+
+enum ErrSite { kSiteWyMma1 = 1, kSiteWyMma2 = 2, kSiteStMma1 = 3, kSiteStMma2 = 4 };
+
+struct Work {
+  const int64_t* coff;  // [N+1] chunk offsets
+  int* err;             // device error word
+  uint8_t* wimg;        // [HV][NCU][16 KiB]
+  __nv_bfloat16* u;     // [HV][NCU][64][128] (element type of q/k/v)
+  uint8_t* pimg;        // [HV][NCU][8 KiB]
+  float* avec;          // [HV][NCU][64]
+  float* bvec;          // [HV][NCU][64]
+  float* gam;           // [HV][NCU]
+  int64_t ncu;          // chunk capacity
+};
+
+struct Layout {
+  size_t err, coff, wimg, u, pimg, avec, bvec, gam, total;
+};
+
+inline Layout plan(const gdn_chunk_args& a) {
+  auto al = [](size_t x) { return (x + 1023) & ~static_cast<size_t>(1023); };
+  const int64_t ncu = chunk_upper_bound(a.B * a.T, a.N);
+  const size_t hc = static_cast<size_t>(a.HV) * ncu;
+  Layout l{};
+  size_t o = 0;
+  l.err = o; o += al(16);
+  l.coff = o; o += al(sizeof(int64_t) * (a.N + 1));
+  l.wimg = o; o += al(hc * kImg64x128);
+  l.u = o; o += al(hc * 64 * D * 2);
+  l.pimg = o; o += al(hc * kImg64x64);
+  l.avec = o; o += al(hc * 64 * 4);
+  l.bvec = o; o += al(hc * 64 * 4);
+  l.gam = o; o += al(hc * 4);
+  l.total = o;
+  return l;
+}
+
+__device__ __forceinline__ void record_error(int* err, int code, int site) {
+  if (atomicCAS(err, 0, code) == 0) {
+    err[1] = site;
+    err[2] = static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+    err[3] = threadIdx.x;
+  }
+}
+
+// Stage rows [s, s+L) of a [*, heads, 128] tensor (head `hd`) into a 64x128
+// no-swizzle image; rows >= L are zero-filled.  Each warp instruction moves
+// 8 rows x 64 contiguous bytes, and every 8 lanes fill one 128-byte core
+// matrix (conflict-free shared stores).
+template <typename T>
+__device__ __forceinline__ void stage_rows(uint8_t* img, const T* base, int64_t s, int L,
+                                           int heads, int hd) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r8 = lane & 7, cc = lane >> 3;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int id = warp * 8 + j;          // 0..31
+    const int row = (id >> 2) * 8 + r8;   // 0..63
+    const int col = ((id & 3) * 4 + cc) * 8;
+    const bool ok = row < L;
+    const T* src = base + ((s + (ok ? row : 0)) * heads + hd) * D + col;
+    umma::cp_async16(img + umma::img_off(row, col, RS128), src, ok ? 16u : 0u);
+  }
+}
+
+// 16-byte-chunk copy of a contiguous image.
+__device__ __forceinline__ void stage_copy(uint8_t* dst, const uint8_t* src, int bytes) {
+  for (int o = threadIdx.x * 16; o < bytes; o += blockDim.x * 16) umma::cp_async16(dst + o, src + o, 16u);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* x) {
+  uint4 r;
+  if constexpr (std::is_same<T, __half>::value) {
+    r.x = pack_h2(x[0], x[1]); r.y = pack_h2(x[2], x[3]);
+    r.z = pack_h2(x[4], x[5]); r.w = pack_h2(x[6], x[7]);
+  } else {
+    r.x = pack_bf16x2(x[0], x[1]); r.y = pack_bf16x2(x[2], x[3]);
+    r.z = pack_bf16x2(x[4], x[5]); r.w = pack_bf16x2(x[6], x[7]);
+  }
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ void unpack8(uint4 u, float* x) {
+  const T* p = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = to_f<T>(p[i]);
+}
+
+// ---------------------------------------------------------------------------
+// WY kernel
+// ---------------------------------------------------------------------------
+
+struct WySmem {
+  static constexpr int kK = 0;
+  static constexpr int kQ = kK + kImg64x128;
+  static constexpr int kV = kQ + kImg64x128;
+  static constexpr int kT1 = kV + kImg64x128;
+  static constexpr int kT2 = kT1 + kImg64x64;
+  static constexpr int kA = kT2 + kImg64x64;     // f32 [64][65]
+  static constexpr int kT = kA + 64 * 65 * 4;    // f32 [64][65]
+  static constexpr int kVec = kT + 64 * 65 * 4;  // gam, beta, rk, rq, cw, cu: f32 [6][64]
+  static constexpr int kBar = kVec + 6 * 64 * 4;
+  static constexpr int kTmem = kBar + 8;
+  static constexpr int kBytes = kTmem + 8;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(128)
+tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  uint8_t* kimg = sm + WySmem::kK;
+  uint8_t* qimg = sm + WySmem::kQ;
+  uint8_t* vimg = sm + WySmem::kV;
+  uint8_t* t1img = sm + WySmem::kT1;
+  uint8_t* t2img = sm + WySmem::kT2;
+  float* Af = reinterpret_cast<float*>(sm + WySmem::kA);
+  float* Tf = reinterpret_cast<float*>(sm + WySmem::kT);
+  float* gam = reinterpret_cast<float*>(sm + WySmem::kVec);
+  float* bet = gam + 64;
+  float* rk = bet + 64;
+  float* rq = rk + 64;
+  float* cw = rq + 64;
+  float* cu = cw + 64;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + WySmem::kBar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + WySmem::kTmem);
+
+  int64_t n, lc;
+  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  const int64_t c = blockIdx.x;
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int64_t s = bos + lc * kChunk;
+  const int L = static_cast<int>(min64(kChunk, eos - s));
+
+  stage_rows<T>(kimg, static_cast<const T*>(p.k), s, L, p.H, h);
+  stage_rows<T>(qimg, static_cast<const T*>(p.q), s, L, p.H, h);
+  umma::cp_async_commit();
+  stage_rows<T>(vimg, static_cast<const T*>(p.v), s, L, p.HV, hv);
+  umma::cp_async_commit();
+
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, 256);
+    umma::fence_before_sync();
+  }
+  if (tid == 0) {
+    umma::mbar_init(bar, 1);
+    umma::mbar_fence_init();
+  }
+  if (warp == 0) {  // chunk-local inclusive cumsum of g over 64 rows
+    float g0 = lane < L ? p.g[(s + lane) * p.HV + hv] : 0.f;
+    float g1 = lane + 32 < L ? p.g[(s + lane + 32) * p.HV + hv] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      float y0 = __shfl_up_sync(0xffffffffu, g0, o), y1 = __shfl_up_sync(0xffffffffu, g1, o);
+      if (lane >= o) { g0 += y0; g1 += y1; }
+    }
+    g1 += __shfl_sync(0xffffffffu, g0, 31);
+    gam[lane] = g0;
+    gam[lane + 32] = g1;
+  } else if (warp == 1) {
+    bet[lane] = lane < L ? p.beta[(s + lane) * p.HV + hv] : 0.f;
+    bet[lane + 32] = lane + 32 < L ? p.beta[(s + lane + 32) * p.HV + hv] : 0.f;
+  }
+  umma::cp_async_wait<1>();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tslot;
+
+  {  // L2-norm factors from the staged rows: threads 0..63 -> k, 64..127 -> q
+    const int row = tid & 63;
+    const uint8_t* img = tid < 64 ? kimg : qimg;
+    float ss = 0.f;
+#pragma unroll
+    for (int cch = 0; cch < 16; ++cch) {
+      float x[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(img + umma::img_off(row, cch * 8, RS128)), x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
+    }
+    const float r = p.use_qk_l2norm ? 1.f / sqrtf(ss + 1e-6f) : 1.f;
+    if (tid < 64) rk[row] = r; else rq[row] = r;
+  }
+  umma::fence_proxy_async();
+  __syncthreads();
+
+  constexpr bool kBf16 = !std::is_same<T, __half>::value;
+  if (tid == 0) {
+    umma::fence_after_sync();
+    const uint32_t id = umma::idesc_f16(64, 64, kBf16, false, false);
+    const uint32_t ka = umma::smem_u32(kimg), qa = umma::smem_u32(qimg);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const uint64_t bk = umma::smem_desc(ka + ks * 256, 128, RS128);
+      umma::mma_f16(tmem + 0, umma::smem_desc(ka + ks * 256, 128, RS128), bk, id, ks > 0);
+      umma::mma_f16(tmem + 64, umma::smem_desc(qa + ks * 256, 128, RS128), bk, id, ks > 0);
+    }
+    umma::mma_commit(umma::smem_u32(bar));
+  }
+  if (tid < 64) {
+    cw[tid] = bet[tid] * expf(gam[tid]) * rk[tid];
+    cu[tid] = bet[tid];
+  }
+  bool ok = umma::mbar_wait(umma::smem_u32(bar), 0);
+  if (!ok) record_error(w.err, 1, kSiteWyMma1);
+  if (__syncthreads_or(!ok)) goto teardown;
+  umma::fence_after_sync();
+
+  {  // A (fp32, shared) and P (bf16 image, global) rows from S_kk, S_qk
+    const int i = warp * 16 + (lane & 15);
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    uint8_t* pimg = w.pimg + (static_cast<int64_t>(hv) * w.ncu + c) * kImg64x64;
+    const float gi = gam[i & 63], ri = rk[i & 63], qi = rq[i & 63], bi = bet[i & 63];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float skk[32], sqk[32];
+      umma::tmem_ld32(tmem + lane_base + half * 32, skk);
+      umma::tmem_ld32(tmem + lane_base + 64 + half * 32, sqk);
+      if (lane < 16) {
+        float pv[32];
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = half * 32 + jj;
+          const float dec = expf(gi - gam[j]);
+          Af[i * 65 + j] = (j < i && i < L) ? bi * dec * ri * rk[j] * skk[jj] : 0.f;
+          pv[jj] = (j <= i && i < L) ? dec * qi * rk[j] * sqk[jj] : 0.f;
+        }
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8)
+          *reinterpret_cast<uint4*>(pimg + umma::img_off(i, half * 32 + q8 * 8, RS64)) =
+              pack8<T>(pv + q8 * 8);
+      }
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+
+  if (tid < 64) {  // column tid of (I + A)^-1
+    const int j = tid;
+    for (int i = 0; i < 64; ++i) Tf[i * 65 + j] = (i == j && j < L) ? 1.f : 0.f;
+    for (int i = j + 1; i < L; ++i) {
+      float acc = 0.f;
+      for (int m = j; m < i; ++m) acc += Af[i * 65 + m] * Tf[m * 65 + j];
+      Tf[i * 65 + j] = -acc;
+    }
+  }
+  __syncthreads();
+  {  // bf16 A operands T' = T diag(cw), T'' = T diag(beta): thread -> (row, 32 cols)
+    const int i = tid >> 1, c0 = (tid & 1) * 32;
+#pragma unroll
+    for (int q8 = 0; q8 < 4; ++q8) {
+      float x1[8], x2[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int j = c0 + q8 * 8 + e;
+        const float t = Tf[i * 65 + j];
+        x1[e] = t * cw[j];
+        x2[e] = t * cu[j];
+      }
+      *reinterpret_cast<uint4*>(t1img + umma::img_off(i, c0 + q8 * 8, RS64)) = pack8<T>(x1);
+      *reinterpret_cast<uint4*>(t2img + umma::img_off(i, c0 + q8 * 8, RS64)) = pack8<T>(x2);
+    }
+  }
+  umma::cp_async_wait<0>();
+  umma::fence_proxy_async();
+  __syncthreads();
+  if (tid == 0) {
+    umma::fence_after_sync();
+    const uint32_t id = umma::idesc_f16(64, D, kBf16, false, true);
+    const uint32_t t1 = umma::smem_u32(t1img), t2 = umma::smem_u32(t2img);
+    const uint32_t ka = umma::smem_u32(kimg), va = umma::smem_u32(vimg);
+#pragma unroll
+    for (int ks = 0; ks < 64 / 16; ++ks) {
+      umma::mma_f16(tmem + 0, umma::smem_desc(t1 + ks * 256, 128, RS64),
+                    umma::smem_desc(ka + ks * 2 * RS128, RS128, 128), id, ks > 0);
+      umma::mma_f16(tmem + 128, umma::smem_desc(t2 + ks * 256, 128, RS64),
+                    umma::smem_desc(va + ks * 2 * RS128, RS128, 128), id, ks > 0);
+    }
+    umma::mma_commit(umma::smem_u32(bar));
+  }
+  ok = umma::mbar_wait(umma::smem_u32(bar), 1);
+  if (!ok) record_error(w.err, 1, kSiteWyMma2);
+  if (__syncthreads_or(!ok)) goto teardown;
+  umma::fence_after_sync();
+
+  {  // W image and U rows to the workspace
+    const int i = warp * 16 + (lane & 15);
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c;
+    uint8_t* wdst = w.wimg + hc * kImg64x128;
+    T* udst = reinterpret_cast<T*>(w.u) + hc * 64 * D + static_cast<int64_t>(i) * D;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float x[32], y[32];
+      umma::tmem_ld32(tmem + lane_base + q * 32, x);
+      umma::tmem_ld32(tmem + lane_base + 128 + q * 32, y);
+      if (lane < 16) {
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          *reinterpret_cast<uint4*>(wdst + umma::img_off(i, q * 32 + q8 * 8, RS128)) = pack8<T>(x + q8 * 8);
+          *reinterpret_cast<uint4*>(udst + q * 32 + q8 * 8) = pack8<T>(y + q8 * 8);
+        }
+      }
+    }
+    if (tid < 64) {
+      const int64_t o = (static_cast<int64_t>(hv) * w.ncu + c) * 64 + tid;
+      const float glast = gam[L - 1];
+      w.avec[o] = tid < L ? scale * expf(gam[tid]) * rq[tid] : 0.f;
+      w.bvec[o] = tid < L ? expf(glast - gam[tid]) * rk[tid] : 0.f;
+      if (tid == 0) w.gam[static_cast<int64_t>(hv) * w.ncu + c] = expf(glast);
+    }
+  }
+
+teardown:
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------------------
+// State + output kernel
+// ---------------------------------------------------------------------------
+
+template <int VS>
+struct StSmem {
+  static constexpr int kUBytes = 64 * VS * 2;
+  static constexpr int kStage = 2 * kImg64x128 + kImg64x128 + kImg64x64 + kUBytes + 2 * 64 * 4;
+  // per stage: W image, Q image, K image, P image, U slice, a, b
+  static constexpr int kW = 0;
+  static constexpr int kQ = kW + kImg64x128;
+  static constexpr int kKimg = kQ + kImg64x128;
+  static constexpr int kP = kKimg + kImg64x128;
+  static constexpr int kU = kP + kImg64x64;
+  static constexpr int kA = kU + kUBytes;
+  static constexpr int kB = kA + 64 * 4;
+  static constexpr int kStageBytes = kB + 64 * 4;
+  static constexpr int kH = 2 * kStageBytes;            // h image 128 x VS
+  static constexpr int kVt = kH + D * VS * 2;           // V~ image 64 x VS
+  static constexpr int kVn = kVt + 64 * VS * 2;         // v_new image 64 x VS
+  static constexpr int kBar = kVn + 64 * VS * 2;
+  static constexpr int kTmem = kBar + 8;
+  static constexpr int kBytes = kTmem + 8;
+  static constexpr int kTmemCols = 4 * VS < 32 ? 32 : 4 * VS;
+};
+
+template <typename T, int VS>
+__global__ void __launch_bounds__(128)
+tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
+  using S = StSmem<VS>;
+  constexpr int RSV = (VS / 8) * 128;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  uint8_t* himg = sm + S::kH;
+  uint8_t* vtimg = sm + S::kVt;
+  uint8_t* vnimg = sm + S::kVn;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + S::kBar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::kTmem);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t n = blockIdx.x;
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  const int v0 = blockIdx.z * VS;
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int64_t nch = eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0;
+  const int64_t c0 = w.coff[n];
+
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, S::kTmemCols);
+    umma::fence_before_sync();
+  }
+  if (tid == 0) {
+    umma::mbar_init(bar, 1);
+    umma::mbar_fence_init();
+  }
+
+  auto prefetch = [&](int64_t lc, int st) {
+    uint8_t* base = sm + st * S::kStageBytes;
+    const int64_t s = bos + lc * kChunk;
+    const int L = static_cast<int>(min64(kChunk, eos - s));
+    const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c0 + lc;
+    stage_copy(base + S::kW, w.wimg + hc * kImg64x128, kImg64x128);
+    stage_copy(base + S::kP, w.pimg + hc * kImg64x64, kImg64x64);
+    stage_rows<T>(base + S::kQ, static_cast<const T*>(p.q), s, L, p.H, h);
+    stage_rows<T>(base + S::kKimg, static_cast<const T*>(p.k), s, L, p.H, h);
+    const T* usrc = reinterpret_cast<const T*>(w.u) + hc * 64 * D + v0;
+    for (int e = tid; e < 64 * (VS / 8); e += 128) {
+      const int r = e / (VS / 8), cc = e % (VS / 8);
+      umma::cp_async16(base + S::kU + (r * VS + cc * 8) * 2, usrc + r * D + cc * 8, 16u);
+    }
+    if (tid < 16) umma::cp_async16(base + S::kA + tid * 16, w.avec + hc * 64 + tid * 4, 16u);
+    else if (tid < 32) umma::cp_async16(base + S::kB + (tid - 16) * 16, w.bvec + hc * 64 + (tid - 16) * 4, 16u);
+  };
+
+  // initial state slice: thread t owns row t (key dim) of h[:, v0:v0+VS]
+  float hreg[VS];
+#pragma unroll
+  for (int j = 0; j < VS; ++j) {
+    float x = 0.f;
+    if (p.initial_state) {
+      const int64_t base = (n * p.HV + hv) * D * D;
+      x = p.state_v_first ? p.initial_state[base + static_cast<int64_t>(v0 + j) * D + tid]
+                          : p.initial_state[base + static_cast<int64_t>(tid) * D + v0 + j];
+    }
+    hreg[j] = x;
+  }
+#pragma unroll
+  for (int j8 = 0; j8 < VS / 8; ++j8)
+    *reinterpret_cast<uint4*>(himg + umma::img_off(tid, j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
+
+  if (nch > 0) prefetch(0, 0);
+  umma::cp_async_commit();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint32_t tX = tmem, tY = tmem + VS, tDH = tmem + 2 * VS, tO = tmem + 3 * VS;
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  constexpr bool kBf16 = !std::is_same<T, __half>::value;
+  T* obase = static_cast<T*>(p.o);
+  bool ok = true;
+
+  for (int64_t lc = 0; lc < nch; ++lc) {
+    const int st = static_cast<int>(lc & 1);
+    uint8_t* base = sm + st * S::kStageBytes;
+    if (lc + 1 < nch) prefetch(lc + 1, st ^ 1);
+    umma::cp_async_commit();
+    umma::cp_async_wait<1>();
+    umma::fence_proxy_async();
+    __syncthreads();
+    const int64_t s = bos + lc * kChunk;
+    const int L = static_cast<int>(min64(kChunk, eos - s));
+    const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c0 + lc;
+
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t id = umma::idesc_f16(64, VS, kBf16, false, true);
+      const uint32_t wa = umma::smem_u32(base + S::kW), qa = umma::smem_u32(base + S::kQ);
+      const uint32_t ha = umma::smem_u32(himg);
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const uint64_t bh = umma::smem_desc(ha + ks * 2 * RSV, RSV, 128);
+        umma::mma_f16(tX, umma::smem_desc(wa + ks * 256, 128, RS128), bh, id, ks > 0);
+        umma::mma_f16(tY, umma::smem_desc(qa + ks * 256, 128, RS128), bh, id, ks > 0);
+      }
+      umma::mma_commit(umma::smem_u32(bar));
+    }
+    ok = umma::mbar_wait(umma::smem_u32(bar), 0);
+    if (!ok) record_error(w.err, 1, kSiteStMma1);
+    if (__syncthreads_or(!ok)) break;
+    umma::fence_after_sync();
+
+    {  // v_new = U - X; images of v_new and diag(b) v_new
+      const int i = warp * 16 + (lane & 15);
+      const float bi = reinterpret_cast<const float*>(base + S::kB)[i & 63];
+      const uint8_t* urow = base + S::kU + (i & 63) * VS * 2;
+#pragma unroll
+      for (int q = 0; q < VS / 32; ++q) {
+        float x[32];
+        umma::tmem_ld32(tX + lane_base + q * 32, x);
+        if (lane < 16) {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            float u8[8], vn[8], vt[8];
+            unpack8<T>(*reinterpret_cast<const uint4*>(urow + (q * 32 + q8 * 8) * 2), u8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              vn[e] = u8[e] - x[q8 * 8 + e];
+              vt[e] = bi * vn[e];
+            }
+            *reinterpret_cast<uint4*>(vnimg + umma::img_off(i, q * 32 + q8 * 8, RSV)) = pack8<T>(vn);
+            *reinterpret_cast<uint4*>(vtimg + umma::img_off(i, q * 32 + q8 * 8, RSV)) = pack8<T>(vt);
+          }
+        }
+      }
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t id128 = umma::idesc_f16(128, VS, kBf16, true, true);
+      const uint32_t id64 = umma::idesc_f16(64, VS, kBf16, false, true);
+      const uint32_t ka = umma::smem_u32(base + S::kKimg), pa = umma::smem_u32(base + S::kP);
+      const uint32_t vt = umma::smem_u32(vtimg), vn = umma::smem_u32(vnimg);
+#pragma unroll
+      for (int ks = 0; ks < 64 / 16; ++ks) {
+        umma::mma_f16(tDH, umma::smem_desc(ka + ks * 2 * RS128, RS128, 128),
+                      umma::smem_desc(vt + ks * 2 * RSV, RSV, 128), id128, ks > 0);
+        umma::mma_f16(tO, umma::smem_desc(pa + ks * 256, 128, RS64),
+                      umma::smem_desc(vn + ks * 2 * RSV, RSV, 128), id64, ks > 0);
+      }
+      umma::mma_commit(umma::smem_u32(bar));
+    }
+    ok = umma::mbar_wait(umma::smem_u32(bar), 1);
+    if (!ok) record_error(w.err, 1, kSiteStMma2);
+    if (__syncthreads_or(!ok)) break;
+    umma::fence_after_sync();
+
+    {  // h <- gamma h + dH (row tid), and its bf16 image
+      const float g = w.gam[hc];
+#pragma unroll
+      for (int q = 0; q < VS / 32; ++q) {
+        float x[32];
+        umma::tmem_ld32(tDH + lane_base + q * 32, x);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) hreg[q * 32 + e] = g * hreg[q * 32 + e] + x[e];
+      }
+#pragma unroll
+      for (int j8 = 0; j8 < VS / 8; ++j8)
+        *reinterpret_cast<uint4*>(himg + umma::img_off(tid, j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
+    }
+    {  // o = a * Y + scale * O for the chunk's valid rows
+      const int i = warp * 16 + (lane & 15);
+      const float ai = reinterpret_cast<const float*>(base + S::kA)[i & 63];
+      T* orow = obase + ((s + (i & 63)) * p.HV + hv) * D + v0;
+#pragma unroll
+      for (int q = 0; q < VS / 32; ++q) {
+        float y[32], z[32];
+        umma::tmem_ld32(tY + lane_base + q * 32, y);
+        umma::tmem_ld32(tO + lane_base + q * 32, z);
+        if (lane < 16 && i < L) {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            float ov[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ov[e] = ai * y[q8 * 8 + e] + scale * z[q8 * 8 + e];
+            *reinterpret_cast<uint4*>(orow + q * 32 + q8 * 8) = pack8<T>(ov);
+          }
+        }
+      }
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    __syncthreads();
+  }
+  umma::cp_async_wait<0>();
+
+  if (ok && p.final_state) {
+    const int64_t base = (n * p.HV + hv) * D * D;
+#pragma unroll
+    for (int j = 0; j < VS; ++j) {
+      if (p.state_v_first) p.final_state[base + static_cast<int64_t>(v0 + j) * D + tid] = hreg[j];
+      else p.final_state[base + static_cast<int64_t>(tid) * D + v0 + j] = hreg[j];
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, S::kTmemCols);
+}
+
+template <typename T, int VS>
+cudaError_t launch_state(const gdn_chunk_args& a, const Work& w, float scale, cudaStream_t s,
+                         LaunchHooks& hk) {
+  auto kern = tc_state_kernel<T, VS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       StSmem<VS>::kBytes);
+  if (e != cudaSuccess) return e;
+  hk.pre(s);
+  kern<<<dim3(static_cast<unsigned>(a.N), a.HV, D / VS), 128, StSmem<VS>::kBytes, s>>>(a, w, scale);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
+  const Layout l = plan(a);
+  uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+  Work w;
+  w.coff = reinterpret_cast<const int64_t*>(ws + l.coff);
+  w.err = reinterpret_cast<int*>(ws + l.err);
+  w.wimg = ws + l.wimg;
+  w.u = reinterpret_cast<__nv_bfloat16*>(ws + l.u);
+  w.pimg = ws + l.pimg;
+  w.avec = reinterpret_cast<float*>(ws + l.avec);
+  w.bvec = reinterpret_cast<float*>(ws + l.bvec);
+  w.gam = reinterpret_cast<float*>(ws + l.gam);
+  w.ncu = chunk_upper_bound(a.B * a.T, a.N);
+  const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
+  LaunchHooks hk(a.stage_events, a.n_stage_events);
+  hk.pre(s);
+  cudaError_t e = launch_chunk_plan(a.cu_seqlens, a.cu_dtype, a.N, a.T,
+                                    reinterpret_cast<int64_t*>(ws + l.coff), s);
+  if (e != cudaSuccess) return e;
+  if (w.ncu > 0 && a.B * a.T > 0) {
+    auto wy = tc_wy_kernel<T>;
+    if ((e = cudaFuncSetAttribute(wy, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  WySmem::kBytes)) != cudaSuccess)
+      return e;
+    hk.pre(s);
+    wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), 128, WySmem::kBytes, s>>>(a, w, scale);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  const int64_t rec = a.N * a.HV;
+  if (rec <= 148) e = launch_state<T, 32>(a, w, scale, s, hk);
+  else if (rec <= 512) e = launch_state<T, 64>(a, w, scale, s, hk);
+  else e = launch_state<T, 128>(a, w, scale, s, hk);
+  if (e != cudaSuccess) return e;
+  hk.end(s);
+  return cudaSuccess;
+}
+
+}  // namespace tc
+
+bool tc_path_applies(const gdn_chunk_args& a) {
+  return (a.qkv_dtype == GDN_BF16 || a.qkv_dtype == GDN_F16) && a.K == tc::D && a.V == tc::D;
+}
+
+size_t tc_workspace_bytes(const gdn_chunk_args& a) { return tc::plan(a).total; }
+
+cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s) {
+  return a.qkv_dtype == GDN_F16 ? tc::run<__half>(a, s) : tc::run<__nv_bfloat16>(a, s);
+}
+
 }  // namespace gdn
