@@ -42,8 +42,13 @@ def flops_per_token_head(K, V, bt=BT):
     return 2 * (bt * (3 * K + 2 * V) + 3 * K * V)
 
 
-def stage_flops_per_token_head(K, V, bt=BT):
-    """Algorithmic FLOPs per token per v-head of each stage (bf16 GEMMs)."""
+def stage_flops_per_token_head(K, V, bt=BT, path="tc"):
+    """Algorithmic FLOPs per token per v-head of each kernel (bf16 GEMMs).
+    tcgen05 path: the WY kernel does KK^T, qK^T, w, u; the state kernel does
+    w.h, q.h, K^T v_new and A v_new.  Generic path: wy / state / out."""
+    if path == "tc":
+        return {"wy": 2 * bt * K + 2 * bt * K + 2 * bt * K + 2 * bt * V,
+                "state": 2 * K * V * 3 + 2 * bt * V}
     return {
         "wy": 2 * bt * K + 2 * bt * K + 2 * bt * V,       # KK^T, w, u
         "state": 2 * K * V + 2 * K * V,                     # w.h, K^T v_new
@@ -239,6 +244,8 @@ def run_ours(a):
     dev = torch.device("cuda", torch.cuda.current_device())
     hbm, tc_burst, tc_sust, peak_kind = _load_peaks()
     cfg = dict(CFG1)
+    if a.tokens:
+        cfg["T"] = a.tokens
     B, T, H, HV, K, V = (cfg[x] for x in ("B", "T", "H", "HV", "K", "V"))
 
     cpu = CpuBaseline(cfg) if (rank == 0 and world == 1 and not a.no_cpu) else None
@@ -307,25 +314,27 @@ def run_ours(a):
     stage_avg = {nm: sum(x) / len(x) for nm, x in stage_ms.items()}
 
     # ---- end-to-end through the public API with host buffers ----
-    o_h = torch.empty(B, T, HV, V, dtype=torch.bfloat16).pin_memory()
-    ht_h = torch.empty(B, HV, K, V, dtype=torch.float32).pin_memory()
-    e2e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(a.steps)]
-    _barrier(world)
-    torch.cuda.synchronize()
-    for i in range(a.steps):
-        flush.zero_()
-        e2e_evs[i][0].record(stream)
-        qd, kd, vd, gd, bd = (x.to(dev, non_blocking=True) for x in (q_h, k_h, v_h, g_h, b_h))
-        o, ht = ops.chunk_gated_delta_rule(qd, kd, vd, gd, bd, None, None, True,
-                                           use_qk_l2norm_in_kernel=True)
-        o_h.copy_(o, non_blocking=True)
-        ht_h.copy_(ht, non_blocking=True)
-        e2e_evs[i][1].record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = _max_over_ranks(sum(s.elapsed_time(e) for s, e in e2e_evs) / a.steps, world)
-    h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, g_h, b_h))
-    d2h = o_h.numel() * o_h.element_size() + ht_h.numel() * ht_h.element_size()
+    e2e_ms, h2d, d2h = None, 0, 0
+    if not a.no_e2e:
+        o_h = torch.empty(B, T, HV, V, dtype=torch.bfloat16).pin_memory()
+        ht_h = torch.empty(B, HV, K, V, dtype=torch.float32).pin_memory()
+        e2e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(a.steps)]
+        _barrier(world)
+        torch.cuda.synchronize()
+        for i in range(a.steps):
+            flush.zero_()
+            e2e_evs[i][0].record(stream)
+            qd, kd, vd, gd, bd = (x.to(dev, non_blocking=True) for x in (q_h, k_h, v_h, g_h, b_h))
+            o, ht = ops.chunk_gated_delta_rule(qd, kd, vd, gd, bd, None, None, True,
+                                               use_qk_l2norm_in_kernel=True)
+            o_h.copy_(o, non_blocking=True)
+            ht_h.copy_(ht, non_blocking=True)
+            e2e_evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = _max_over_ranks(sum(s.elapsed_time(e) for s, e in e2e_evs) / a.steps, world)
+        h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, g_h, b_h))
+        d2h = o_h.numel() * o_h.element_size() + ht_h.numel() * ht_h.element_size()
 
     # ---- decode (config 3) ----
     dec = _decode_bench(ops, dev, a, hbm, flush) if not a.no_decode else None
@@ -351,7 +360,7 @@ def run_ours(a):
         value = tokens / (ms / 1e3)
         fl_tok = flops_per_token_head(K, V)
         total_flops = B * T * HV * fl_tok
-        sfl = stage_flops_per_token_head(K, V)
+        sfl = stage_flops_per_token_head(K, V, path="tc" if "plan" in stage_avg and len(stage_avg) == 3 else "generic")
         dom = max(stage_avg, key=stage_avg.get)
         dom_key = dom.split(":")[0]
         dom_flops = B * T * HV * sfl.get(dom_key, 0)
@@ -377,8 +386,9 @@ def run_ours(a):
                               "algorithmic_bytes": pbytes,
                               "frac_hbm": pbytes / (ms * 1e-3) / 1e9 / hbm},
             "stages_ms": stage_avg,
-            "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": None if e2e_ms is None else {
+                "value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
             "decode": dec,
@@ -419,13 +429,11 @@ def _chunk_with_events(ops, q, k, v, g, beta, handles, nst):
 
 
 def _stage_names(n):
-    # launch order of the chunk path (see the launchers in csrc/)
-    if n == 6:
+    # launch order of the chunk paths (launchers in domesticated_torch_mlu_ops_b200/csrc/)
+    if n == 6:  # generic fp32 path
         return ["plan", "prep:q", "prep:k", "wy", "state", "out"]
-    if n == 3:
-        return ["wy", "state", "out"]
-    if n == 4:
-        return ["plan", "wy", "state", "out"]
+    if n == 3:  # tcgen05 path
+        return ["plan", "wy", "state"]
     return [f"k{i}" for i in range(n)]
 
 
@@ -506,6 +514,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode measurement")
     ap.add_argument("--ref-tokens", type=int, default=2048)
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="override config 1's T (small cases for ncu captures; not a bench line)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":

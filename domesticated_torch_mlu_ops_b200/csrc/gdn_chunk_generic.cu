@@ -13,6 +13,7 @@
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
+#include "solve_tril.cuh"
 
 namespace gdn {
 
@@ -103,6 +104,7 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
   float* gcs = Tm + 64 * 65;      // [64]
   float* bs = gcs + 64;           // [64]
   float* cw = bs + 64;            // [64] beta * exp(G)
+  float* Zs = cw + 64;            // [64][17] solve scratch
   int64_t n, lc;
   if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
@@ -147,16 +149,7 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
     A[i * 65 + j] = a;
   }
   __syncthreads();
-  if (tid < 64) {  // column tid of (I + A)^-1 by forward substitution
-    const int j = tid;
-    for (int i = 0; i < 64; ++i) Tm[i * 65 + j] = (i == j && j < L) ? 1.f : 0.f;
-    for (int i = j + 1; i < L; ++i) {
-      float acc = 0.f;
-      for (int m = j; m < i; ++m) acc += A[i * 65 + m] * Tm[m * 65 + j];
-      Tm[i * 65 + j] = -acc;
-    }
-  }
-  __syncthreads();
+  solve_tril64(A, Tm, Zs);  // (I + A)^-1; ends with a barrier
   for (int e = tid; e < L * K; e += blockDim.x) {
     const int i = e / K, kk = e % K;
     float acc = 0.f;
@@ -342,7 +335,7 @@ static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
-  const size_t wy_smem = sizeof(float) * (64 * a.K + 64 * a.V + 2 * 64 * 65 + 3 * 64);
+  const size_t wy_smem = sizeof(float) * (64 * a.K + 64 * a.V + 2 * 64 * 65 + 3 * 64 + 64 * 17);
   const size_t st_smem = sizeof(float) * (a.K * kStateCols + 64 * kStateCols + 2 * 64 * a.K + 64);
   const size_t out_smem = sizeof(float) * (2 * 64 * a.K + 64 * 65 + 64);
   if ((e = cudaFuncSetAttribute(chunk_wy_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -36,6 +36,7 @@
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
+#include "solve_tril.cuh"
 #include "umma.cuh"
 
 #include <type_traits>
@@ -49,6 +50,7 @@ constexpr int kImg64x128 = 64 * D * 2;  // 16 KiB
 constexpr int kImg64x64 = 64 * 64 * 2;  // 8 KiB
 constexpr int RS128 = (D / 8) * 128;    // image row stride of a 128-column tile
 constexpr int RS64 = (64 / 8) * 128;    // image row stride of a 64-column tile
+constexpr int kScal = 132;              // per-(head, chunk) scalars: a[64], b[64], gamma, pad
 
 enum ErrSite { kSiteWyMma1 = 1, kSiteWyMma2 = 2, kSiteStMma1 = 3, kSiteStMma2 = 4 };
 
@@ -58,14 +60,12 @@ struct Work {
   uint8_t* wimg;        // [HV][NCU][16 KiB]
   __nv_bfloat16* u;     // [HV][NCU][64][128] (element type of q/k/v)
   uint8_t* pimg;        // [HV][NCU][8 KiB]
-  float* avec;          // [HV][NCU][64]
-  float* bvec;          // [HV][NCU][64]
-  float* gam;           // [HV][NCU]
+  float* scal;          // [HV][NCU][kScal]: a[64], b[64], gamma, pad
   int64_t ncu;          // chunk capacity
 };
 
 struct Layout {
-  size_t err, coff, wimg, u, pimg, avec, bvec, gam, total;
+  size_t err, coff, wimg, u, pimg, scal, total;
 };
 
 inline Layout plan(const gdn_chunk_args& a) {
@@ -79,9 +79,7 @@ inline Layout plan(const gdn_chunk_args& a) {
   l.wimg = o; o += al(hc * kImg64x128);
   l.u = o; o += al(hc * 64 * D * 2);
   l.pimg = o; o += al(hc * kImg64x64);
-  l.avec = o; o += al(hc * 64 * 4);
-  l.bvec = o; o += al(hc * 64 * 4);
-  l.gam = o; o += al(hc * 4);
+  l.scal = o; o += al(hc * kScal * 4);
   l.total = o;
   return l;
 }
@@ -158,7 +156,8 @@ struct WySmem {
   static constexpr int kT2 = kT1 + kImg64x64;
   static constexpr int kA = kT2 + kImg64x64;     // f32 [64][65]
   static constexpr int kT = kA + 64 * 65 * 4;    // f32 [64][65]
-  static constexpr int kVec = kT + 64 * 65 * 4;  // gam, beta, rk, rq, cw, cu: f32 [6][64]
+  static constexpr int kZ = kT + 64 * 65 * 4;    // f32 [64][17] solve scratch
+  static constexpr int kVec = kZ + 64 * 17 * 4;  // gam, beta, rk, rq, cw, cu: f32 [6][64]
   static constexpr int kBar = kVec + 6 * 64 * 4;
   static constexpr int kTmem = kBar + 8;
   static constexpr int kBytes = kTmem + 8;
@@ -175,6 +174,7 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
   uint8_t* t2img = sm + WySmem::kT2;
   float* Af = reinterpret_cast<float*>(sm + WySmem::kA);
   float* Tf = reinterpret_cast<float*>(sm + WySmem::kT);
+  float* Zs = reinterpret_cast<float*>(sm + WySmem::kZ);
   float* gam = reinterpret_cast<float*>(sm + WySmem::kVec);
   float* bet = gam + 64;
   float* rk = bet + 64;
@@ -296,16 +296,7 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
   umma::fence_before_sync();
   __syncthreads();
 
-  if (tid < 64) {  // column tid of (I + A)^-1
-    const int j = tid;
-    for (int i = 0; i < 64; ++i) Tf[i * 65 + j] = (i == j && j < L) ? 1.f : 0.f;
-    for (int i = j + 1; i < L; ++i) {
-      float acc = 0.f;
-      for (int m = j; m < i; ++m) acc += Af[i * 65 + m] * Tf[m * 65 + j];
-      Tf[i * 65 + j] = -acc;
-    }
-  }
-  __syncthreads();
+  solve_tril64(Af, Tf, Zs);  // T = (I + A)^-1, ends with a barrier
   {  // bf16 A operands T' = T diag(cw), T'' = T diag(beta): thread -> (row, 32 cols)
     const int i = tid >> 1, c0 = (tid & 1) * 32;
 #pragma unroll
@@ -364,11 +355,11 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
       }
     }
     if (tid < 64) {
-      const int64_t o = (static_cast<int64_t>(hv) * w.ncu + c) * 64 + tid;
+      float* sc = w.scal + (static_cast<int64_t>(hv) * w.ncu + c) * kScal;
       const float glast = gam[L - 1];
-      w.avec[o] = tid < L ? scale * expf(gam[tid]) * rq[tid] : 0.f;
-      w.bvec[o] = tid < L ? expf(glast - gam[tid]) * rk[tid] : 0.f;
-      if (tid == 0) w.gam[static_cast<int64_t>(hv) * w.ncu + c] = expf(glast);
+      sc[tid] = tid < L ? scale * expf(gam[tid]) * rq[tid] : 0.f;
+      sc[64 + tid] = tid < L ? expf(glast - gam[tid]) * rk[tid] : 0.f;
+      if (tid < 4) sc[128 + tid] = tid == 0 ? expf(glast) : 0.f;
     }
   }
 
@@ -384,24 +375,26 @@ teardown:
 
 template <int VS>
 struct StSmem {
+  // per stage: W image, Q image, K image, P image, U slice, scalars (a, b, gamma)
   static constexpr int kUBytes = 64 * VS * 2;
-  static constexpr int kStage = 2 * kImg64x128 + kImg64x128 + kImg64x64 + kUBytes + 2 * 64 * 4;
-  // per stage: W image, Q image, K image, P image, U slice, a, b
   static constexpr int kW = 0;
   static constexpr int kQ = kW + kImg64x128;
   static constexpr int kKimg = kQ + kImg64x128;
   static constexpr int kP = kKimg + kImg64x128;
   static constexpr int kU = kP + kImg64x64;
-  static constexpr int kA = kU + kUBytes;
-  static constexpr int kB = kA + 64 * 4;
-  static constexpr int kStageBytes = kB + 64 * 4;
-  static constexpr int kH = 2 * kStageBytes;            // h image 128 x VS
-  static constexpr int kVt = kH + D * VS * 2;           // V~ image 64 x VS
-  static constexpr int kVn = kVt + 64 * VS * 2;         // v_new image 64 x VS
+  static constexpr int kScalOff = kU + kUBytes;
+  static constexpr int kStageBytes = kScalOff + kScal * 4;
+  static constexpr int kH = ((2 * kStageBytes + 1023) / 1024) * 1024;  // h image 128 x VS
+  static constexpr int kVt = kH + D * VS * 2;                         // V~ image 64 x VS
+  static constexpr int kVn = kVt + 64 * VS * 2;                       // v_new image 64 x VS
   static constexpr int kBar = kVn + 64 * VS * 2;
   static constexpr int kTmem = kBar + 8;
   static constexpr int kBytes = kTmem + 8;
-  static constexpr int kTmemCols = 4 * VS < 32 ? 32 : 4 * VS;
+  // TMEM columns: X, dH, then Y/O, double-buffered when they fit in 512
+  static constexpr bool kDbl = 6 * VS <= 512;
+  static constexpr int kCols = kDbl ? 6 * VS : 4 * VS;
+  static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
+                                   : kCols <= 256 ? 256 : 512;
 };
 
 template <typename T, int VS>
@@ -440,16 +433,16 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
     const int L = static_cast<int>(min64(kChunk, eos - s));
     const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c0 + lc;
     stage_copy(base + S::kW, w.wimg + hc * kImg64x128, kImg64x128);
-    stage_copy(base + S::kP, w.pimg + hc * kImg64x64, kImg64x64);
     stage_rows<T>(base + S::kQ, static_cast<const T*>(p.q), s, L, p.H, h);
     stage_rows<T>(base + S::kKimg, static_cast<const T*>(p.k), s, L, p.H, h);
+    stage_copy(base + S::kP, w.pimg + hc * kImg64x64, kImg64x64);
     const T* usrc = reinterpret_cast<const T*>(w.u) + hc * 64 * D + v0;
     for (int e = tid; e < 64 * (VS / 8); e += 128) {
       const int r = e / (VS / 8), cc = e % (VS / 8);
       umma::cp_async16(base + S::kU + (r * VS + cc * 8) * 2, usrc + r * D + cc * 8, 16u);
     }
-    if (tid < 16) umma::cp_async16(base + S::kA + tid * 16, w.avec + hc * 64 + tid * 4, 16u);
-    else if (tid < 32) umma::cp_async16(base + S::kB + (tid - 16) * 16, w.bvec + hc * 64 + (tid - 16) * 4, 16u);
+    if (tid < kScal / 4)
+      umma::cp_async16(base + S::kScalOff + tid * 16, w.scal + hc * kScal + tid * 4, 16u);
   };
 
   // initial state slice: thread t owns row t (key dim) of h[:, v0:v0+VS]
@@ -470,28 +463,49 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
 
   if (nch > 0) prefetch(0, 0);
   umma::cp_async_commit();
+  umma::cp_async_wait<0>();
+  umma::fence_proxy_async();
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tslot;
-  const uint32_t tX = tmem, tY = tmem + VS, tDH = tmem + 2 * VS, tO = tmem + 3 * VS;
+  const uint32_t tX = tmem, tDH = tmem + VS;
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   constexpr bool kBf16 = !std::is_same<T, __half>::value;
   T* obase = static_cast<T*>(p.o);
+  const int i_row = warp * 16 + (lane & 15);  // chunk row held by this lane in M=64 results
   bool ok = true;
 
+  // Output rows of a finished chunk: o = a * Y + scale * O (TMEM buffers yo).
+  auto emit = [&](uint32_t yo, int64_t s, int L, float ai) {
+    T* orow = obase + ((s + i_row) * p.HV + hv) * D + v0;
+#pragma unroll
+    for (int q = 0; q < VS / 32; ++q) {
+      float y[32], z[32];
+      umma::tmem_ld32(yo + lane_base + q * 32, y);
+      umma::tmem_ld32(yo + VS + lane_base + q * 32, z);
+      if (lane < 16 && i_row < L) {
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          float ov[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ov[e] = ai * y[q8 * 8 + e] + scale * z[q8 * 8 + e];
+          *reinterpret_cast<uint4*>(orow + q * 32 + q8 * 8) = pack8<T>(ov);
+        }
+      }
+    }
+  };
+
+  int64_t s_prev = 0;
+  int L_prev = 0;
+  float a_prev = 0.f;
   for (int64_t lc = 0; lc < nch; ++lc) {
     const int st = static_cast<int>(lc & 1);
     uint8_t* base = sm + st * S::kStageBytes;
-    if (lc + 1 < nch) prefetch(lc + 1, st ^ 1);
-    umma::cp_async_commit();
-    umma::cp_async_wait<1>();
-    umma::fence_proxy_async();
-    __syncthreads();
     const int64_t s = bos + lc * kChunk;
     const int L = static_cast<int>(min64(kChunk, eos - s));
-    const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c0 + lc;
+    const uint32_t tYO = tmem + 2 * VS + (S::kDbl ? st * 2 * VS : 0);
 
-    if (tid == 0) {
+    if (tid == 0) {  // X = W h, Y = Q h
       umma::fence_after_sync();
       const uint32_t id = umma::idesc_f16(64, VS, kBf16, false, true);
       const uint32_t wa = umma::smem_u32(base + S::kW), qa = umma::smem_u32(base + S::kQ);
@@ -500,19 +514,23 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
       for (int ks = 0; ks < D / 16; ++ks) {
         const uint64_t bh = umma::smem_desc(ha + ks * 2 * RSV, RSV, 128);
         umma::mma_f16(tX, umma::smem_desc(wa + ks * 256, 128, RS128), bh, id, ks > 0);
-        umma::mma_f16(tY, umma::smem_desc(qa + ks * 256, 128, RS128), bh, id, ks > 0);
+        umma::mma_f16(tYO, umma::smem_desc(qa + ks * 256, 128, RS128), bh, id, ks > 0);
       }
       umma::mma_commit(umma::smem_u32(bar));
     }
+    if (lc + 1 < nch) prefetch(lc + 1, st ^ 1);
+    umma::cp_async_commit();
+    if (S::kDbl && lc > 0) emit(tmem + 2 * VS + (st ^ 1) * 2 * VS, s_prev, L_prev, a_prev);
+
     ok = umma::mbar_wait(umma::smem_u32(bar), 0);
     if (!ok) record_error(w.err, 1, kSiteStMma1);
     if (__syncthreads_or(!ok)) break;
     umma::fence_after_sync();
 
     {  // v_new = U - X; images of v_new and diag(b) v_new
-      const int i = warp * 16 + (lane & 15);
-      const float bi = reinterpret_cast<const float*>(base + S::kB)[i & 63];
-      const uint8_t* urow = base + S::kU + (i & 63) * VS * 2;
+      const float* sc = reinterpret_cast<const float*>(base + S::kScalOff);
+      const float bi = sc[64 + (i_row & 63)];
+      const uint8_t* urow = base + S::kU + (i_row & 63) * VS * 2;
 #pragma unroll
       for (int q = 0; q < VS / 32; ++q) {
         float x[32];
@@ -527,8 +545,8 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
               vn[e] = u8[e] - x[q8 * 8 + e];
               vt[e] = bi * vn[e];
             }
-            *reinterpret_cast<uint4*>(vnimg + umma::img_off(i, q * 32 + q8 * 8, RSV)) = pack8<T>(vn);
-            *reinterpret_cast<uint4*>(vtimg + umma::img_off(i, q * 32 + q8 * 8, RSV)) = pack8<T>(vt);
+            *reinterpret_cast<uint4*>(vnimg + umma::img_off(i_row, q * 32 + q8 * 8, RSV)) = pack8<T>(vn);
+            *reinterpret_cast<uint4*>(vtimg + umma::img_off(i_row, q * 32 + q8 * 8, RSV)) = pack8<T>(vt);
           }
         }
       }
@@ -536,7 +554,7 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
     umma::fence_proxy_async();
     umma::fence_before_sync();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0) {  // dH = K^T V~, O = P v_new
       umma::fence_after_sync();
       const uint32_t id128 = umma::idesc_f16(128, VS, kBf16, true, true);
       const uint32_t id64 = umma::idesc_f16(64, VS, kBf16, false, true);
@@ -546,53 +564,41 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
       for (int ks = 0; ks < 64 / 16; ++ks) {
         umma::mma_f16(tDH, umma::smem_desc(ka + ks * 2 * RS128, RS128, 128),
                       umma::smem_desc(vt + ks * 2 * RSV, RSV, 128), id128, ks > 0);
-        umma::mma_f16(tO, umma::smem_desc(pa + ks * 256, 128, RS64),
+        umma::mma_f16(tYO + VS, umma::smem_desc(pa + ks * 256, 128, RS64),
                       umma::smem_desc(vn + ks * 2 * RSV, RSV, 128), id64, ks > 0);
       }
       umma::mma_commit(umma::smem_u32(bar));
     }
+    const float* scv = reinterpret_cast<const float*>(base + S::kScalOff);
+    const float g = scv[128];
+    const float ai = scv[i_row & 63];
     ok = umma::mbar_wait(umma::smem_u32(bar), 1);
     if (!ok) record_error(w.err, 1, kSiteStMma2);
     if (__syncthreads_or(!ok)) break;
     umma::fence_after_sync();
 
-    {  // h <- gamma h + dH (row tid), and its bf16 image
-      const float g = w.gam[hc];
+    // h <- gamma h + dH (row tid), and its bf16 image for the next chunk
 #pragma unroll
-      for (int q = 0; q < VS / 32; ++q) {
-        float x[32];
-        umma::tmem_ld32(tDH + lane_base + q * 32, x);
+    for (int q = 0; q < VS / 32; ++q) {
+      float x[32];
+      umma::tmem_ld32(tDH + lane_base + q * 32, x);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) hreg[q * 32 + e] = g * hreg[q * 32 + e] + x[e];
-      }
-#pragma unroll
-      for (int j8 = 0; j8 < VS / 8; ++j8)
-        *reinterpret_cast<uint4*>(himg + umma::img_off(tid, j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
+      for (int e = 0; e < 32; ++e) hreg[q * 32 + e] = g * hreg[q * 32 + e] + x[e];
     }
-    {  // o = a * Y + scale * O for the chunk's valid rows
-      const int i = warp * 16 + (lane & 15);
-      const float ai = reinterpret_cast<const float*>(base + S::kA)[i & 63];
-      T* orow = obase + ((s + (i & 63)) * p.HV + hv) * D + v0;
 #pragma unroll
-      for (int q = 0; q < VS / 32; ++q) {
-        float y[32], z[32];
-        umma::tmem_ld32(tY + lane_base + q * 32, y);
-        umma::tmem_ld32(tO + lane_base + q * 32, z);
-        if (lane < 16 && i < L) {
-#pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) {
-            float ov[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) ov[e] = ai * y[q8 * 8 + e] + scale * z[q8 * 8 + e];
-            *reinterpret_cast<uint4*>(orow + q * 32 + q8 * 8) = pack8<T>(ov);
-          }
-        }
-      }
-    }
+    for (int j8 = 0; j8 < VS / 8; ++j8)
+      *reinterpret_cast<uint4*>(himg + umma::img_off(tid, j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
+    if (!S::kDbl) emit(tYO, s, L, ai);
+    s_prev = s;
+    L_prev = L;
+    a_prev = ai;
+    umma::cp_async_wait<0>();
     umma::fence_proxy_async();
     umma::fence_before_sync();
     __syncthreads();
   }
+  if (ok && S::kDbl && nch > 0)
+    emit(tmem + 2 * VS + static_cast<uint32_t>((nch - 1) & 1) * 2 * VS, s_prev, L_prev, a_prev);
   umma::cp_async_wait<0>();
 
   if (ok && p.final_state) {
@@ -630,9 +636,7 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
   w.wimg = ws + l.wimg;
   w.u = reinterpret_cast<__nv_bfloat16*>(ws + l.u);
   w.pimg = ws + l.pimg;
-  w.avec = reinterpret_cast<float*>(ws + l.avec);
-  w.bvec = reinterpret_cast<float*>(ws + l.bvec);
-  w.gam = reinterpret_cast<float*>(ws + l.gam);
+  w.scal = reinterpret_cast<float*>(ws + l.scal);
   w.ncu = chunk_upper_bound(a.B * a.T, a.N);
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
   LaunchHooks hk(a.stage_events, a.n_stage_events);

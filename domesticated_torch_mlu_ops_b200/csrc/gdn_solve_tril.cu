@@ -7,48 +7,41 @@
 //
 // The op has no workspace argument, so the grid is (sequence, head, slice)
 // and slice z of a sequence solves its chunks z, z + S, z + 2S, ...; no chunk
-// table is needed.  Each block is staged in shared memory; thread j
-// forward-substitutes column j (columns are independent), then the block is
-// written with explicit zeros above the diagonal and past a partial chunk's
-// last row.
+// table is needed.  Each block is zero-padded to 64 x 64 in shared memory and
+// inverted with the blocked solver of solve_tril.cuh, then written with
+// explicit zeros above the diagonal and past a partial chunk's last row.
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
+#include "solve_tril.cuh"
 
 namespace gdn {
 
 template <typename TO>
-__global__ void solve_tril_kernel(const float* __restrict__ A, TO* __restrict__ out,
-                                  const void* cu, int cu_dtype, int64_t T, int H, int BT) {
-  __shared__ float As[64][65];
-  __shared__ float Ts[64][65];
+__global__ void __launch_bounds__(128)
+solve_tril_kernel(const float* __restrict__ A, TO* __restrict__ out, const void* cu, int cu_dtype,
+                  int64_t T, int H, int BT) {
+  __shared__ float As[64 * kTrilStride];
+  __shared__ float Ts[64 * kTrilStride];
+  __shared__ float Zs[64 * kTrilZStride];
   const int64_t n = blockIdx.x;
   const int h = blockIdx.y;
   int64_t bos, eos;
   seq_bounds(cu, cu_dtype, n, T, bos, eos);
   for (int64_t s = bos + static_cast<int64_t>(blockIdx.z) * BT; s < eos;
        s += static_cast<int64_t>(gridDim.z) * BT) {
-  const int L = static_cast<int>(min64(BT, eos - s));
-  for (int e = threadIdx.x; e < BT * BT; e += blockDim.x) {
-    const int i = e / BT, j = e % BT;
-    As[i][j] = (i < L && j < i) ? A[((s + i) * H + h) * BT + j] : 0.f;
-  }
-  __syncthreads();
-  if (threadIdx.x < BT) {
-    const int j = threadIdx.x;
-    for (int i = 0; i < BT; ++i) Ts[i][j] = (i == j && j < L) ? 1.f : 0.f;
-    for (int i = j + 1; i < L; ++i) {
-      float acc = 0.f;
-      for (int m = j; m < i; ++m) acc += As[i][m] * Ts[m][j];
-      Ts[i][j] = -acc;
+    const int L = static_cast<int>(min64(BT, eos - s));
+    for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {  // zero-padded to 64 x 64
+      const int i = e >> 6, j = e & 63;
+      As[i * kTrilStride + j] = (i < L && j < i) ? A[((s + i) * H + h) * BT + j] : 0.f;
     }
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < L * BT; e += blockDim.x) {
-    const int i = e / BT, j = e % BT;
-    out[((s + i) * H + h) * BT + j] = from_f<TO>(Ts[i][j]);
-  }
-  __syncthreads();
+    __syncthreads();
+    solve_tril64(As, Ts, Zs);
+    for (int e = threadIdx.x; e < L * BT; e += blockDim.x) {
+      const int i = e / BT, j = e % BT;
+      out[((s + i) * H + h) * BT + j] = from_f<TO>(j < L ? Ts[i * kTrilStride + j] : 0.f);
+    }
+    __syncthreads();
   }
 }
 
@@ -63,13 +56,13 @@ cudaError_t launch_solve_tril(const float* A, void* out, int out_dtype, const vo
   note_launch();
   switch (out_dtype) {
     case GDN_F32:
-      solve_tril_kernel<float><<<grid, 64, 0, s>>>(A, static_cast<float*>(out), cu, cu_dtype, T, H, BT);
+      solve_tril_kernel<float><<<grid, 128, 0, s>>>(A, static_cast<float*>(out), cu, cu_dtype, T, H, BT);
       break;
     case GDN_BF16:
-      solve_tril_kernel<__nv_bfloat16><<<grid, 64, 0, s>>>(A, static_cast<__nv_bfloat16*>(out), cu, cu_dtype, T, H, BT);
+      solve_tril_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(A, static_cast<__nv_bfloat16*>(out), cu, cu_dtype, T, H, BT);
       break;
     case GDN_F16:
-      solve_tril_kernel<__half><<<grid, 64, 0, s>>>(A, static_cast<__half*>(out), cu, cu_dtype, T, H, BT);
+      solve_tril_kernel<__half><<<grid, 128, 0, s>>>(A, static_cast<__half*>(out), cu, cu_dtype, T, H, BT);
       break;
     default:
       return cudaErrorInvalidValue;
