@@ -95,6 +95,9 @@ int gdn_chunk_fwd(const gdn_chunk_args* a, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (!a->force_generic && gdn::tc_path_applies(*a)) {
+    auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!aligned(a->q) || !aligned(a->k) || !aligned(a->v))
+      return fail(GDN_ERR_INVALID, "q, k and v must be 16-byte aligned for the tensor-core path");
     e = gdn::launch_chunk_tc(*a, s);
     if (e != cudaSuccess) return cuda_fail(e, "gdn_chunk_fwd (tcgen05 path)");
   } else {

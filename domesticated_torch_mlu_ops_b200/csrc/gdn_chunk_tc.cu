@@ -4,21 +4,20 @@
 // Two kernels replace the reference's six stages (triton/fla/chunk.py:10-74):
 //
 // tc_wy_kernel, one CTA per (chunk, v-head), fully parallel:
-//   * q, k, v chunk tiles staged with cp.async into no-swizzle UMMA images;
+//   * q, k, v chunk tiles fetched by TMA (128-byte swizzled);
 //   * L2-norm factors r_q, r_k of every row (fused_recurrent_fn.py:110-112
 //     formula) and the chunk-local cumsum G of g (cumsum.py:20-77);
 //   * S_kk = K K^T and S_qk = Q K^T on tcgen05 (bf16 in, fp32 in TMEM);
 //   * A = beta_i exp(G_i - G_j) r_k,i r_k,j S_kk, strictly lower
-//     (chunk_scaled_dot_kkt.py:25-100); (I + A)^-1 by column forward
-//     substitution in fp32 shared memory (the native solve_tril,
-//     include/torch_mlu_ops.h:1052);
+//     (chunk_scaled_dot_kkt.py:25-100); (I + A)^-1 with the blocked solver
+//     of solve_tril.cuh (the native solve_tril, include/torch_mlu_ops.h:1052);
 //   * W = T diag(beta exp(G) r_k) K and U = T diag(beta) V on tcgen05
 //     (wy_fast.py:18-119), with the row scalings folded into the bf16 A
 //     operand exactly where the reference rounds to bf16;
 //   * P = tril_incl(exp(G_i - G_j) r_q,i r_k,j S_qk) (chunk_o.py:133-160);
 //   * per-row output / decay scales a_i = scale exp(G_i) r_q,i,
 //     b_i = exp(G_last - G_i) r_k,i and gamma = exp(G_last).
-//   W and P are written as ready-to-use UMMA operand images.
+//   W and P are written as ready-to-use UMMA operand images, U as V-slices.
 //
 // tc_state_kernel, one CTA per (sequence, v-head, V-slice of VS columns),
 // serial over the sequence's chunks (chunk_delta_h.py:28-197 fused with
@@ -28,18 +27,20 @@
 //   v_new = U - X, V~ = diag(b) v_new         (epilogue, fp32 -> bf16)
 //   dH = K^T V~,  O = P v_new                 (tcgen05, M=128 / M=64)
 //   h <- gamma h + dH,  o = a * Y + scale * O  (epilogue)
-// so h and v_new never leave the SM.  The next chunk's operands are
-// prefetched with cp.async while the current chunk computes.
+// so h and v_new never leave the SM.  One thread streams the next chunk's
+// operands in with TMA / bulk copies while the current chunk computes.
 //
 // Every mbarrier wait is bounded; on timeout the kernel records an error in
 // the workspace error word, frees its TMEM and exits.
+
+#include <cuda.h>
+
+#include <type_traits>
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 #include "solve_tril.cuh"
 #include "umma.cuh"
-
-#include <type_traits>
 
 namespace gdn {
 
@@ -51,17 +52,20 @@ constexpr int kImg64x64 = 64 * 64 * 2;  // 8 KiB
 constexpr int RS128 = (D / 8) * 128;    // image row stride of a 128-column tile
 constexpr int RS64 = (64 / 8) * 128;    // image row stride of a 64-column tile
 constexpr int kScal = 132;              // per-(head, chunk) scalars: a[64], b[64], gamma, pad
+constexpr int kAtom = 64 * 128;         // one 64-row x 128-byte swizzled atom (8 KiB)
 
-enum ErrSite { kSiteWyMma1 = 1, kSiteWyMma2 = 2, kSiteStMma1 = 3, kSiteStMma2 = 4 };
+enum ErrSite { kSiteWyLoad = 1, kSiteWyMma1 = 2, kSiteWyMma2 = 3, kSiteStLoad = 4,
+               kSiteStMma1 = 5, kSiteStMma2 = 6 };
 
 struct Work {
   const int64_t* coff;  // [N+1] chunk offsets
   int* err;             // device error word
   uint8_t* wimg;        // [HV][NCU][16 KiB]
-  __nv_bfloat16* u;     // [HV][NCU][64][128] (element type of q/k/v)
+  uint8_t* u;           // [HV][NCU][128/VS][64][VS] elements of the q/k/v type
   uint8_t* pimg;        // [HV][NCU][8 KiB]
   float* scal;          // [HV][NCU][kScal]: a[64], b[64], gamma, pad
   int64_t ncu;          // chunk capacity
+  int vs;               // V-slice width of the state kernel (U layout)
 };
 
 struct Layout {
@@ -92,31 +96,6 @@ __device__ __forceinline__ void record_error(int* err, int code, int site) {
   }
 }
 
-// Stage rows [s, s+L) of a [*, heads, 128] tensor (head `hd`) into a 64x128
-// no-swizzle image; rows >= L are zero-filled.  Each warp instruction moves
-// 8 rows x 64 contiguous bytes, and every 8 lanes fill one 128-byte core
-// matrix (conflict-free shared stores).
-template <typename T>
-__device__ __forceinline__ void stage_rows(uint8_t* img, const T* base, int64_t s, int L,
-                                           int heads, int hd) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r8 = lane & 7, cc = lane >> 3;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int id = warp * 8 + j;          // 0..31
-    const int row = (id >> 2) * 8 + r8;   // 0..63
-    const int col = ((id & 3) * 4 + cc) * 8;
-    const bool ok = row < L;
-    const T* src = base + ((s + (ok ? row : 0)) * heads + hd) * D + col;
-    umma::cp_async16(img + umma::img_off(row, col, RS128), src, ok ? 16u : 0u);
-  }
-}
-
-// 16-byte-chunk copy of a contiguous image.
-__device__ __forceinline__ void stage_copy(uint8_t* dst, const uint8_t* src, int bytes) {
-  for (int o = threadIdx.x * 16; o < bytes; o += blockDim.x * 16) umma::cp_async16(dst + o, src + o, 16u);
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -144,32 +123,50 @@ __device__ __forceinline__ void unpack8(uint4 u, float* x) {
   for (int i = 0; i < 8; ++i) x[i] = to_f<T>(p[i]);
 }
 
+// K-major descriptor of k-step ks (16 elements) of a 64-row swizzled tile.
+__device__ __forceinline__ uint64_t sw_kmajor(uint32_t base, int ks) {
+  return umma::smem_desc_sw128(base + (ks >> 2) * kAtom + (ks & 3) * 32, 16, 1024);
+}
+// MN-major descriptor (MN = the 128 tile columns, K = the 64 rows) of k-step ks.
+__device__ __forceinline__ uint64_t sw_mnmajor(uint32_t base, int ks) {
+  return umma::smem_desc_sw128(base + ks * 2048, kAtom, 1024);
+}
+// Both 64-column boxes of rows [s, s+64) of head hd of a [T, heads, 128] tensor.
+__device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* map, int hd, int64_t s,
+                                         uint32_t bar) {
+  umma::tma_load_3d(dst, map, 0, hd, static_cast<int>(s), bar);
+  umma::tma_load_3d(dst + kAtom, map, 64, hd, static_cast<int>(s), bar);
+}
+
 // ---------------------------------------------------------------------------
 // WY kernel
 // ---------------------------------------------------------------------------
 
 struct WySmem {
-  static constexpr int kK = 0;
+  static constexpr int kK = 0;                   // swizzled tiles (1 KiB aligned)
   static constexpr int kQ = kK + kImg64x128;
   static constexpr int kV = kQ + kImg64x128;
-  static constexpr int kT1 = kV + kImg64x128;
-  static constexpr int kT2 = kT1 + kImg64x64;
+  static constexpr int kT1 = kV + kImg64x128;    // T' image
+  static constexpr int kT2 = kT1 + kImg64x64;    // T'' image
   static constexpr int kA = kT2 + kImg64x64;     // f32 [64][65]
   static constexpr int kT = kA + 64 * 65 * 4;    // f32 [64][65]
   static constexpr int kZ = kT + 64 * 65 * 4;    // f32 [64][17] solve scratch
   static constexpr int kVec = kZ + 64 * 17 * 4;  // gam, beta, rk, rq, cw, cu: f32 [6][64]
-  static constexpr int kBar = kVec + 6 * 64 * 4;
-  static constexpr int kTmem = kBar + 8;
-  static constexpr int kBytes = kTmem + 8;
+  static constexpr int kBar = kVec + 6 * 64 * 4; // 3 mbarriers
+  static constexpr int kTmem = kBar + 24;
+  static constexpr int kBytes = kTmem + 8 + 1024;  // + slack for 1 KiB alignment
 };
 
 template <typename T>
 __global__ void __launch_bounds__(128)
-tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
-  extern __shared__ __align__(1024) uint8_t sm[];
-  uint8_t* kimg = sm + WySmem::kK;
-  uint8_t* qimg = sm + WySmem::kQ;
-  uint8_t* vimg = sm + WySmem::kV;
+tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
+             const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+             const __grid_constant__ CUtensorMap tv) {
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* kbuf = sm + WySmem::kK;
+  uint8_t* qbuf = sm + WySmem::kQ;
+  uint8_t* vbuf = sm + WySmem::kV;
   uint8_t* t1img = sm + WySmem::kT1;
   uint8_t* t2img = sm + WySmem::kT2;
   float* Af = reinterpret_cast<float*>(sm + WySmem::kA);
@@ -181,8 +178,10 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
   float* rq = rk + 64;
   float* cw = rq + 64;
   float* cu = cw + 64;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + WySmem::kBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + WySmem::kBar);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + WySmem::kTmem);
+  const uint32_t bar_kq = umma::smem_u32(bars), bar_v = umma::smem_u32(bars + 1),
+                 bar_mma = umma::smem_u32(bars + 2);
 
   int64_t n, lc;
   if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
@@ -194,21 +193,22 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
   const int64_t s = bos + lc * kChunk;
   const int L = static_cast<int>(min64(kChunk, eos - s));
 
-  stage_rows<T>(kimg, static_cast<const T*>(p.k), s, L, p.H, h);
-  stage_rows<T>(qimg, static_cast<const T*>(p.q), s, L, p.H, h);
-  umma::cp_async_commit();
-  stage_rows<T>(vimg, static_cast<const T*>(p.v), s, L, p.HV, hv);
-  umma::cp_async_commit();
-
+  if (tid == 0) {
+    umma::mbar_init(bars, 1);
+    umma::mbar_init(bars + 1, 1);
+    umma::mbar_init(bars + 2, 1);
+    umma::mbar_fence_init();
+    umma::mbar_arrive_expect_tx(bar_kq, 2 * kImg64x128);
+    tma_tile(kbuf, &tk, h, s, bar_kq);
+    tma_tile(qbuf, &tq, h, s, bar_kq);
+    umma::mbar_arrive_expect_tx(bar_v, kImg64x128);
+    tma_tile(vbuf, &tv, hv, s, bar_v);
+  }
   if (warp == 0) {
     umma::tmem_alloc(tslot, 256);
     umma::fence_before_sync();
   }
-  if (tid == 0) {
-    umma::mbar_init(bar, 1);
-    umma::mbar_fence_init();
-  }
-  if (warp == 0) {  // chunk-local inclusive cumsum of g over 64 rows
+  if (warp == 1) {  // chunk-local inclusive cumsum of g over 64 rows
     float g0 = lane < L ? p.g[(s + lane) * p.HV + hv] : 0.f;
     float g1 = lane + 32 < L ? p.g[(s + lane + 32) * p.HV + hv] : 0.f;
 #pragma unroll
@@ -219,50 +219,50 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
     g1 += __shfl_sync(0xffffffffu, g0, 31);
     gam[lane] = g0;
     gam[lane + 32] = g1;
-  } else if (warp == 1) {
+  } else if (warp == 2) {
     bet[lane] = lane < L ? p.beta[(s + lane) * p.HV + hv] : 0.f;
     bet[lane + 32] = lane + 32 < L ? p.beta[(s + lane + 32) * p.HV + hv] : 0.f;
   }
-  umma::cp_async_wait<1>();
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tslot;
+  constexpr bool kBf16 = !std::is_same<T, __half>::value;
 
-  {  // L2-norm factors from the staged rows: threads 0..63 -> k, 64..127 -> q
+  bool ok = umma::mbar_wait(bar_kq, 0);
+  if (!ok) record_error(w.err, 1, kSiteWyLoad);
+  if (__syncthreads_or(!ok)) goto teardown;
+  if (tid == 0) {
+    umma::fence_after_sync();
+    const uint32_t id = umma::idesc_f16(64, 64, kBf16, false, false);
+    const uint32_t ka = umma::smem_u32(kbuf), qa = umma::smem_u32(qbuf);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const uint64_t bk = sw_kmajor(ka, ks);
+      umma::mma_f16(tmem + 0, bk, bk, id, ks > 0);
+      umma::mma_f16(tmem + 64, sw_kmajor(qa, ks), bk, id, ks > 0);
+    }
+    umma::mma_commit(bar_mma);
+  }
+  {  // L2-norm factors from the swizzled rows: threads 0..63 -> k, 64..127 -> q
     const int row = tid & 63;
-    const uint8_t* img = tid < 64 ? kimg : qimg;
+    const uint8_t* tile = tid < 64 ? kbuf : qbuf;
     float ss = 0.f;
 #pragma unroll
     for (int cch = 0; cch < 16; ++cch) {
       float x[8];
-      unpack8<T>(*reinterpret_cast<const uint4*>(img + umma::img_off(row, cch * 8, RS128)), x);
+      unpack8<T>(*reinterpret_cast<const uint4*>(tile + umma::sw128_off(row, cch * 8, 64)), x);
 #pragma unroll
       for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
     }
-    const float r = p.use_qk_l2norm ? 1.f / sqrtf(ss + 1e-6f) : 1.f;
+    const float r = p.use_qk_l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
     if (tid < 64) rk[row] = r; else rq[row] = r;
   }
-  umma::fence_proxy_async();
   __syncthreads();
-
-  constexpr bool kBf16 = !std::is_same<T, __half>::value;
-  if (tid == 0) {
-    umma::fence_after_sync();
-    const uint32_t id = umma::idesc_f16(64, 64, kBf16, false, false);
-    const uint32_t ka = umma::smem_u32(kimg), qa = umma::smem_u32(qimg);
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      const uint64_t bk = umma::smem_desc(ka + ks * 256, 128, RS128);
-      umma::mma_f16(tmem + 0, umma::smem_desc(ka + ks * 256, 128, RS128), bk, id, ks > 0);
-      umma::mma_f16(tmem + 64, umma::smem_desc(qa + ks * 256, 128, RS128), bk, id, ks > 0);
-    }
-    umma::mma_commit(umma::smem_u32(bar));
-  }
   if (tid < 64) {
-    cw[tid] = bet[tid] * expf(gam[tid]) * rk[tid];
+    cw[tid] = bet[tid] * __expf(gam[tid]) * rk[tid];
     cu[tid] = bet[tid];
   }
-  bool ok = umma::mbar_wait(umma::smem_u32(bar), 0);
+  ok = umma::mbar_wait(bar_mma, 0);
   if (!ok) record_error(w.err, 1, kSiteWyMma1);
   if (__syncthreads_or(!ok)) goto teardown;
   umma::fence_after_sync();
@@ -282,9 +282,9 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
           const int j = half * 32 + jj;
-          const float dec = expf(gi - gam[j]);
-          Af[i * 65 + j] = (j < i && i < L) ? bi * dec * ri * rk[j] * skk[jj] : 0.f;
-          pv[jj] = (j <= i && i < L) ? dec * qi * rk[j] * sqk[jj] : 0.f;
+          const float dec = j <= i ? __expf(gi - gam[j]) * rk[j] : 0.f;
+          Af[i * 65 + j] = (j < i && i < L) ? bi * dec * ri * skk[jj] : 0.f;
+          pv[jj] = i < L ? dec * qi * sqk[jj] : 0.f;
         }
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8)
@@ -295,7 +295,6 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
   }
   umma::fence_before_sync();
   __syncthreads();
-
   solve_tril64(Af, Tf, Zs);  // T = (I + A)^-1, ends with a barrier
   {  // bf16 A operands T' = T diag(cw), T'' = T diag(beta): thread -> (row, 32 cols)
     const int i = tid >> 1, c0 = (tid & 1) * 32;
@@ -313,34 +312,41 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
       *reinterpret_cast<uint4*>(t2img + umma::img_off(i, c0 + q8 * 8, RS64)) = pack8<T>(x2);
     }
   }
-  umma::cp_async_wait<0>();
   umma::fence_proxy_async();
   __syncthreads();
+  ok = umma::mbar_wait(bar_v, 0);
+  if (!ok) record_error(w.err, 1, kSiteWyLoad);
+  if (__syncthreads_or(!ok)) goto teardown;
   if (tid == 0) {
     umma::fence_after_sync();
     const uint32_t id = umma::idesc_f16(64, D, kBf16, false, true);
     const uint32_t t1 = umma::smem_u32(t1img), t2 = umma::smem_u32(t2img);
-    const uint32_t ka = umma::smem_u32(kimg), va = umma::smem_u32(vimg);
+    const uint32_t ka = umma::smem_u32(kbuf), va = umma::smem_u32(vbuf);
 #pragma unroll
     for (int ks = 0; ks < 64 / 16; ++ks) {
-      umma::mma_f16(tmem + 0, umma::smem_desc(t1 + ks * 256, 128, RS64),
-                    umma::smem_desc(ka + ks * 2 * RS128, RS128, 128), id, ks > 0);
-      umma::mma_f16(tmem + 128, umma::smem_desc(t2 + ks * 256, 128, RS64),
-                    umma::smem_desc(va + ks * 2 * RS128, RS128, 128), id, ks > 0);
+      umma::mma_f16(tmem + 0, umma::smem_desc(t1 + ks * 256, 128, RS64), sw_mnmajor(ka, ks), id, ks > 0);
+      umma::mma_f16(tmem + 128, umma::smem_desc(t2 + ks * 256, 128, RS64), sw_mnmajor(va, ks), id, ks > 0);
     }
-    umma::mma_commit(umma::smem_u32(bar));
+    umma::mma_commit(bar_mma);
   }
-  ok = umma::mbar_wait(umma::smem_u32(bar), 1);
+  if (tid < 64) {
+    float* sc = w.scal + (static_cast<int64_t>(hv) * w.ncu + c) * kScal;
+    const float glast = gam[L - 1];
+    sc[tid] = tid < L ? scale * __expf(gam[tid]) * rq[tid] : 0.f;
+    sc[64 + tid] = tid < L ? __expf(glast - gam[tid]) * rk[tid] : 0.f;
+    if (tid < 4) sc[128 + tid] = tid == 0 ? __expf(glast) : 0.f;
+  }
+  ok = umma::mbar_wait(bar_mma, 1);
   if (!ok) record_error(w.err, 1, kSiteWyMma2);
   if (__syncthreads_or(!ok)) goto teardown;
   umma::fence_after_sync();
 
-  {  // W image and U rows to the workspace
+  {  // W image and U V-slices to the workspace
     const int i = warp * 16 + (lane & 15);
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c;
     uint8_t* wdst = w.wimg + hc * kImg64x128;
-    T* udst = reinterpret_cast<T*>(w.u) + hc * 64 * D + static_cast<int64_t>(i) * D;
+    T* ubase = reinterpret_cast<T*>(w.u) + hc * 64 * D;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       float x[32], y[32];
@@ -349,17 +355,13 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale) {
       if (lane < 16) {
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
-          *reinterpret_cast<uint4*>(wdst + umma::img_off(i, q * 32 + q8 * 8, RS128)) = pack8<T>(x + q8 * 8);
-          *reinterpret_cast<uint4*>(udst + q * 32 + q8 * 8) = pack8<T>(y + q8 * 8);
+          const int col = q * 32 + q8 * 8;
+          *reinterpret_cast<uint4*>(wdst + umma::img_off(i, col, RS128)) = pack8<T>(x + q8 * 8);
+          const int sl = col / w.vs, wc = col % w.vs;
+          *reinterpret_cast<uint4*>(ubase + (static_cast<int64_t>(sl) * 64 + i) * w.vs + wc) =
+              pack8<T>(y + q8 * 8);
         }
       }
-    }
-    if (tid < 64) {
-      float* sc = w.scal + (static_cast<int64_t>(hv) * w.ncu + c) * kScal;
-      const float glast = gam[L - 1];
-      sc[tid] = tid < L ? scale * expf(gam[tid]) * rq[tid] : 0.f;
-      sc[64 + tid] = tid < L ? expf(glast - gam[tid]) * rk[tid] : 0.f;
-      if (tid < 4) sc[128 + tid] = tid == 0 ? expf(glast) : 0.f;
     }
   }
 
@@ -375,21 +377,23 @@ teardown:
 
 template <int VS>
 struct StSmem {
-  // per stage: W image, Q image, K image, P image, U slice, scalars (a, b, gamma)
+  // per stage (1 KiB aligned): Q, K (swizzled TMA tiles), W image, P image,
+  // U slice [64][VS], scalars (a, b, gamma)
   static constexpr int kUBytes = 64 * VS * 2;
-  static constexpr int kW = 0;
-  static constexpr int kQ = kW + kImg64x128;
-  static constexpr int kKimg = kQ + kImg64x128;
-  static constexpr int kP = kKimg + kImg64x128;
+  static constexpr int kQ = 0;
+  static constexpr int kKt = kQ + kImg64x128;
+  static constexpr int kW = kKt + kImg64x128;
+  static constexpr int kP = kW + kImg64x128;
   static constexpr int kU = kP + kImg64x64;
   static constexpr int kScalOff = kU + kUBytes;
-  static constexpr int kStageBytes = kScalOff + kScal * 4;
-  static constexpr int kH = ((2 * kStageBytes + 1023) / 1024) * 1024;  // h image 128 x VS
-  static constexpr int kVt = kH + D * VS * 2;                         // V~ image 64 x VS
-  static constexpr int kVn = kVt + 64 * VS * 2;                       // v_new image 64 x VS
-  static constexpr int kBar = kVn + 64 * VS * 2;
-  static constexpr int kTmem = kBar + 8;
-  static constexpr int kBytes = kTmem + 8;
+  static constexpr int kStageBytes = ((kScalOff + kScal * 4 + 1023) / 1024) * 1024;
+  static constexpr uint32_t kTx = 3 * kImg64x128 + kImg64x64 + kUBytes + kScal * 4;
+  static constexpr int kH = 2 * kStageBytes;             // h image 128 x VS
+  static constexpr int kVt = kH + D * VS * 2;            // V~ image 64 x VS
+  static constexpr int kVn = kVt + 64 * VS * 2;          // v_new image 64 x VS
+  static constexpr int kBar = kVn + 64 * VS * 2;         // full[2], mma
+  static constexpr int kTmem = kBar + 24;
+  static constexpr int kBytes = kTmem + 8 + 1024;
   // TMEM columns: X, dH, then Y/O, double-buffered when they fit in 512
   static constexpr bool kDbl = 6 * VS <= 512;
   static constexpr int kCols = kDbl ? 6 * VS : 4 * VS;
@@ -399,51 +403,54 @@ struct StSmem {
 
 template <typename T, int VS>
 __global__ void __launch_bounds__(128)
-tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
+tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
+                const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk) {
   using S = StSmem<VS>;
   constexpr int RSV = (VS / 8) * 128;
-  extern __shared__ __align__(1024) uint8_t sm[];
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* himg = sm + S::kH;
   uint8_t* vtimg = sm + S::kVt;
   uint8_t* vnimg = sm + S::kVn;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + S::kBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBar);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::kTmem);
+  const uint32_t bar_mma = umma::smem_u32(bars + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t n = blockIdx.x;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
-  const int v0 = blockIdx.z * VS;
+  const int vsl = blockIdx.z, v0 = vsl * VS;
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
   const int64_t nch = eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0;
   const int64_t c0 = w.coff[n];
 
+  // Issue all of chunk lc's operand copies into stage st (one thread).
+  auto fetch = [&](int64_t lc, int st) {
+    uint8_t* base = sm + st * S::kStageBytes;
+    const uint32_t bar = umma::smem_u32(bars + st);
+    const int64_t s = bos + lc * kChunk;
+    const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c0 + lc;
+    umma::mbar_arrive_expect_tx(bar, S::kTx);
+    tma_tile(base + S::kQ, &tq, h, s, bar);
+    tma_tile(base + S::kKt, &tk, h, s, bar);
+    umma::bulk_g2s(base + S::kW, w.wimg + hc * kImg64x128, kImg64x128, bar);
+    umma::bulk_g2s(base + S::kP, w.pimg + hc * kImg64x64, kImg64x64, bar);
+    umma::bulk_g2s(base + S::kU, w.u + ((hc * (D / VS) + vsl) * 64 * VS) * 2, S::kUBytes, bar);
+    umma::bulk_g2s(base + S::kScalOff, w.scal + hc * kScal, kScal * 4, bar);
+  };
+
+  if (tid == 0) {
+    umma::mbar_init(bars, 1);
+    umma::mbar_init(bars + 1, 1);
+    umma::mbar_init(bars + 2, 1);
+    umma::mbar_fence_init();
+    if (nch > 0) fetch(0, 0);
+  }
   if (warp == 0) {
     umma::tmem_alloc(tslot, S::kTmemCols);
     umma::fence_before_sync();
   }
-  if (tid == 0) {
-    umma::mbar_init(bar, 1);
-    umma::mbar_fence_init();
-  }
-
-  auto prefetch = [&](int64_t lc, int st) {
-    uint8_t* base = sm + st * S::kStageBytes;
-    const int64_t s = bos + lc * kChunk;
-    const int L = static_cast<int>(min64(kChunk, eos - s));
-    const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c0 + lc;
-    stage_copy(base + S::kW, w.wimg + hc * kImg64x128, kImg64x128);
-    stage_rows<T>(base + S::kQ, static_cast<const T*>(p.q), s, L, p.H, h);
-    stage_rows<T>(base + S::kKimg, static_cast<const T*>(p.k), s, L, p.H, h);
-    stage_copy(base + S::kP, w.pimg + hc * kImg64x64, kImg64x64);
-    const T* usrc = reinterpret_cast<const T*>(w.u) + hc * 64 * D + v0;
-    for (int e = tid; e < 64 * (VS / 8); e += 128) {
-      const int r = e / (VS / 8), cc = e % (VS / 8);
-      umma::cp_async16(base + S::kU + (r * VS + cc * 8) * 2, usrc + r * D + cc * 8, 16u);
-    }
-    if (tid < kScal / 4)
-      umma::cp_async16(base + S::kScalOff + tid * 16, w.scal + hc * kScal + tid * 4, 16u);
-  };
 
   // initial state slice: thread t owns row t (key dim) of h[:, v0:v0+VS]
   float hreg[VS];
@@ -461,9 +468,6 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
   for (int j8 = 0; j8 < VS / 8; ++j8)
     *reinterpret_cast<uint4*>(himg + umma::img_off(tid, j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
 
-  if (nch > 0) prefetch(0, 0);
-  umma::cp_async_commit();
-  umma::cp_async_wait<0>();
   umma::fence_proxy_async();
   __syncthreads();
   umma::fence_after_sync();
@@ -505,7 +509,10 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
     const int L = static_cast<int>(min64(kChunk, eos - s));
     const uint32_t tYO = tmem + 2 * VS + (S::kDbl ? st * 2 * VS : 0);
 
-    if (tid == 0) {  // X = W h, Y = Q h
+    ok = umma::mbar_wait(umma::smem_u32(bars + st), static_cast<uint32_t>((lc >> 1) & 1));
+    if (!ok) record_error(w.err, 1, kSiteStLoad);
+    if (__syncthreads_or(!ok)) break;
+    if (tid == 0) {  // X = W h, Y = Q h; then stream in the next chunk
       umma::fence_after_sync();
       const uint32_t id = umma::idesc_f16(64, VS, kBf16, false, true);
       const uint32_t wa = umma::smem_u32(base + S::kW), qa = umma::smem_u32(base + S::kQ);
@@ -514,22 +521,21 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
       for (int ks = 0; ks < D / 16; ++ks) {
         const uint64_t bh = umma::smem_desc(ha + ks * 2 * RSV, RSV, 128);
         umma::mma_f16(tX, umma::smem_desc(wa + ks * 256, 128, RS128), bh, id, ks > 0);
-        umma::mma_f16(tYO, umma::smem_desc(qa + ks * 256, 128, RS128), bh, id, ks > 0);
+        umma::mma_f16(tYO, sw_kmajor(qa, ks), bh, id, ks > 0);
       }
-      umma::mma_commit(umma::smem_u32(bar));
+      umma::mma_commit(bar_mma);
+      if (lc + 1 < nch) fetch(lc + 1, st ^ 1);
     }
-    if (lc + 1 < nch) prefetch(lc + 1, st ^ 1);
-    umma::cp_async_commit();
     if (S::kDbl && lc > 0) emit(tmem + 2 * VS + (st ^ 1) * 2 * VS, s_prev, L_prev, a_prev);
 
-    ok = umma::mbar_wait(umma::smem_u32(bar), 0);
+    ok = umma::mbar_wait(bar_mma, 0);
     if (!ok) record_error(w.err, 1, kSiteStMma1);
     if (__syncthreads_or(!ok)) break;
     umma::fence_after_sync();
 
+    const float* scv = reinterpret_cast<const float*>(base + S::kScalOff);
     {  // v_new = U - X; images of v_new and diag(b) v_new
-      const float* sc = reinterpret_cast<const float*>(base + S::kScalOff);
-      const float bi = sc[64 + (i_row & 63)];
+      const float bi = scv[64 + (i_row & 63)];
       const uint8_t* urow = base + S::kU + (i_row & 63) * VS * 2;
 #pragma unroll
       for (int q = 0; q < VS / 32; ++q) {
@@ -558,21 +564,19 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
       umma::fence_after_sync();
       const uint32_t id128 = umma::idesc_f16(128, VS, kBf16, true, true);
       const uint32_t id64 = umma::idesc_f16(64, VS, kBf16, false, true);
-      const uint32_t ka = umma::smem_u32(base + S::kKimg), pa = umma::smem_u32(base + S::kP);
+      const uint32_t ka = umma::smem_u32(base + S::kKt), pa = umma::smem_u32(base + S::kP);
       const uint32_t vt = umma::smem_u32(vtimg), vn = umma::smem_u32(vnimg);
 #pragma unroll
       for (int ks = 0; ks < 64 / 16; ++ks) {
-        umma::mma_f16(tDH, umma::smem_desc(ka + ks * 2 * RS128, RS128, 128),
-                      umma::smem_desc(vt + ks * 2 * RSV, RSV, 128), id128, ks > 0);
+        umma::mma_f16(tDH, sw_mnmajor(ka, ks), umma::smem_desc(vt + ks * 2 * RSV, RSV, 128), id128, ks > 0);
         umma::mma_f16(tYO + VS, umma::smem_desc(pa + ks * 256, 128, RS64),
                       umma::smem_desc(vn + ks * 2 * RSV, RSV, 128), id64, ks > 0);
       }
-      umma::mma_commit(umma::smem_u32(bar));
+      umma::mma_commit(bar_mma);
     }
-    const float* scv = reinterpret_cast<const float*>(base + S::kScalOff);
     const float g = scv[128];
     const float ai = scv[i_row & 63];
-    ok = umma::mbar_wait(umma::smem_u32(bar), 1);
+    ok = umma::mbar_wait(bar_mma, 1);
     if (!ok) record_error(w.err, 1, kSiteStMma2);
     if (__syncthreads_or(!ok)) break;
     umma::fence_after_sync();
@@ -592,14 +596,12 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
     s_prev = s;
     L_prev = L;
     a_prev = ai;
-    umma::cp_async_wait<0>();
     umma::fence_proxy_async();
     umma::fence_before_sync();
     __syncthreads();
   }
   if (ok && S::kDbl && nch > 0)
     emit(tmem + 2 * VS + static_cast<uint32_t>((nch - 1) & 1) * 2 * VS, s_prev, L_prev, a_prev);
-  umma::cp_async_wait<0>();
 
   if (ok && p.final_state) {
     const int64_t base = (n * p.HV + hv) * D * D;
@@ -609,55 +611,119 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale) {
       else p.final_state[base + static_cast<int64_t>(tid) * D + v0 + j] = hreg[j];
     }
   }
+  if (!ok) {
+    // an operand copy may still be in flight after a timeout: wait (bounded)
+    // for both stages before the CTA exits and its shared memory is reused
+    umma::mbar_wait(umma::smem_u32(bars), 0, 20000000LL);
+    umma::mbar_wait(umma::smem_u32(bars + 1), 0, 20000000LL);
+  }
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, S::kTmemCols);
 }
 
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;  // resolved once; the entry point never changes
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// [Ttot, heads, 128] tensor, 64 x 64 boxes with 128-byte swizzle.
+cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, bool f16) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(heads),
+                              static_cast<cuuint64_t>(ttot)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2,
+                                 static_cast<cuuint64_t>(heads) * D * 2};
+  const cuuint32_t box[3] = {64, 1, 64};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                  const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 template <typename T, int VS>
-cudaError_t launch_state(const gdn_chunk_args& a, const Work& w, float scale, cudaStream_t s,
-                         LaunchHooks& hk) {
+cudaError_t launch_state(const gdn_chunk_args& a, const Work& w, float scale, const CUtensorMap& tq,
+                         const CUtensorMap& tk, cudaStream_t s, LaunchHooks& hk) {
   auto kern = tc_state_kernel<T, VS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        StSmem<VS>::kBytes);
   if (e != cudaSuccess) return e;
   hk.pre(s);
-  kern<<<dim3(static_cast<unsigned>(a.N), a.HV, D / VS), 128, StSmem<VS>::kBytes, s>>>(a, w, scale);
+  kern<<<dim3(static_cast<unsigned>(a.N), a.HV, D / VS), 128, StSmem<VS>::kBytes, s>>>(a, w, scale, tq, tk);
   return cudaGetLastError();
+}
+
+int choose_vs(const gdn_chunk_args& a) {
+  const int64_t rec = a.N * a.HV;
+  if (rec <= 148) return 32;
+  if (rec <= 512) return 64;
+  return 128;
 }
 
 template <typename T>
 cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
+  constexpr bool kF16 = std::is_same<T, __half>::value;
   const Layout l = plan(a);
   uint8_t* ws = static_cast<uint8_t*>(a.workspace);
   Work w;
   w.coff = reinterpret_cast<const int64_t*>(ws + l.coff);
   w.err = reinterpret_cast<int*>(ws + l.err);
   w.wimg = ws + l.wimg;
-  w.u = reinterpret_cast<__nv_bfloat16*>(ws + l.u);
+  w.u = ws + l.u;
   w.pimg = ws + l.pimg;
   w.scal = reinterpret_cast<float*>(ws + l.scal);
   w.ncu = chunk_upper_bound(a.B * a.T, a.N);
+  w.vs = choose_vs(a);
+  const int64_t ttot = a.B * a.T;
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
+  CUtensorMap tq, tk, tv;
+  cudaError_t e;
+  if (ttot > 0) {
+    if ((e = make_map(&tq, a.q, a.H, ttot, kF16)) != cudaSuccess) return e;
+    if ((e = make_map(&tk, a.k, a.H, ttot, kF16)) != cudaSuccess) return e;
+    if ((e = make_map(&tv, a.v, a.HV, ttot, kF16)) != cudaSuccess) return e;
+  }
   LaunchHooks hk(a.stage_events, a.n_stage_events);
   hk.pre(s);
-  cudaError_t e = launch_chunk_plan(a.cu_seqlens, a.cu_dtype, a.N, a.T,
-                                    reinterpret_cast<int64_t*>(ws + l.coff), s);
+  e = launch_chunk_plan(a.cu_seqlens, a.cu_dtype, a.N, a.T, reinterpret_cast<int64_t*>(ws + l.coff), s);
   if (e != cudaSuccess) return e;
-  if (w.ncu > 0 && a.B * a.T > 0) {
+  if (ttot > 0) {
     auto wy = tc_wy_kernel<T>;
-    if ((e = cudaFuncSetAttribute(wy, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  WySmem::kBytes)) != cudaSuccess)
+    if ((e = cudaFuncSetAttribute(wy, cudaFuncAttributeMaxDynamicSharedMemorySize, WySmem::kBytes)) !=
+        cudaSuccess)
       return e;
     hk.pre(s);
-    wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), 128, WySmem::kBytes, s>>>(a, w, scale);
+    wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), 128, WySmem::kBytes, s>>>(a, w, scale, tq, tk, tv);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if (w.vs == 32) e = launch_state<T, 32>(a, w, scale, tq, tk, s, hk);
+    else if (w.vs == 64) e = launch_state<T, 64>(a, w, scale, tq, tk, s, hk);
+    else e = launch_state<T, 128>(a, w, scale, tq, tk, s, hk);
+    if (e != cudaSuccess) return e;
+  } else if (a.final_state) {  // no tokens: the final states are the initial ones
+    const size_t bytes = static_cast<size_t>(a.N) * a.HV * D * D * sizeof(float);
+    e = a.initial_state ? cudaMemcpyAsync(a.final_state, a.initial_state, bytes, cudaMemcpyDeviceToDevice, s)
+                        : cudaMemsetAsync(a.final_state, 0, bytes, s);
+    if (e != cudaSuccess) return e;
   }
-  const int64_t rec = a.N * a.HV;
-  if (rec <= 148) e = launch_state<T, 32>(a, w, scale, s, hk);
-  else if (rec <= 512) e = launch_state<T, 64>(a, w, scale, s, hk);
-  else e = launch_state<T, 128>(a, w, scale, s, hk);
-  if (e != cudaSuccess) return e;
   hk.end(s);
   return cudaSuccess;
 }
@@ -665,7 +731,8 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
 }  // namespace tc
 
 bool tc_path_applies(const gdn_chunk_args& a) {
-  return (a.qkv_dtype == GDN_BF16 || a.qkv_dtype == GDN_F16) && a.K == tc::D && a.V == tc::D;
+  return (a.qkv_dtype == GDN_BF16 || a.qkv_dtype == GDN_F16) && a.K == tc::D && a.V == tc::D &&
+         a.B * a.T < (int64_t(1) << 31);
 }
 
 size_t tc_workspace_bytes(const gdn_chunk_args& a) { return tc::plan(a).total; }

@@ -35,6 +35,23 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   return d;                             // base offset 0, layout type 0 (no swizzle)
 }
 
+// Shared-memory matrix descriptor for a 128-byte-swizzled tile (the layout a
+// TMA load with CU_TENSOR_MAP_SWIZZLE_128B writes): rows of 128 bytes, 16-byte
+// chunk j of row r stored at chunk j ^ (r % 8); tile base 1024-byte aligned.
+//   K-major:  LBO unused (16), SBO = 1024 (8-row group stride); the start
+//             address advances 32 bytes per 16 bf16 along K inside an atom.
+//   MN-major: LBO = stride between 64-element atoms along MN, SBO = 1024.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return smem_desc(saddr, lbo, sbo) | (static_cast<uint64_t>(2) << 61);
+}
+
+// Byte offset of element (r, c) of a [rows][cols] bf16 tile stored as
+// 64-column swizzled atoms of rows x 128 bytes.
+__host__ __device__ constexpr uint32_t sw128_off(int r, int c, int rows) {
+  return static_cast<uint32_t>((c >> 6) * rows * 128 + r * 128 +
+                               ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2);
+}
+
 // Instruction descriptor for kind::f16: fp32 accumulate, A/B both bf16 (or
 // both f16), dense.  a_mn / b_mn select MN-major operands.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a_mn, bool b_mn) {
@@ -132,6 +149,29 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
     if (clock64() - t0 > limit_cycles) return false;
   }
   return true;
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes)
+               : "memory");
+}
+
+// ---- TMA / bulk copies (global -> shared, completion on an mbarrier) --------
+// 1-D bulk copy: addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      :: "r"(smem_u32(dst_smem)), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+// 3-D tiled tensor load (no multicast).  c0 * element size must be a
+// multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_3d(void* dst_smem, const void* tmap, int c0, int c1,
+                                            int c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];"
+      :: "r"(smem_u32(dst_smem)), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(bar) : "memory");
 }
 
 // ---- cp.async (16 bytes, zero-filled when src_bytes == 0) ------------------

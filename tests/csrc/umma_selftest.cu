@@ -1,7 +1,9 @@
 // Test-only kernel: one tcgen05 MMA D[M][N] = sum_k A(m,k) B(n,k) with the
-// operand images, descriptors and TMEM read-back conventions of the product
+// operand layouts, descriptors and TMEM read-back conventions of the product
 // kernels (domesticated_torch_mlu_ops_b200/csrc/umma.cuh).  A is given as
 // [M][K] (K-major) or [K][M] (a_mn), B as [N][K] or [K][N] (b_mn), bf16.
+// Each operand is stored either as a no-swizzle image or as 128-byte
+// swizzled atoms (the layout TMA writes with SWIZZLE_128B).
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -9,26 +11,37 @@
 
 using namespace gdn::umma;
 
-template <int M, int N, int K, bool AMN, bool BMN>
+template <int ROWS, int COLS, bool SW>
+__device__ uint32_t tile_off(int r, int c) {
+  return SW ? sw128_off(r, c, ROWS) : img_off(r, c, (COLS / 8) * 128);
+}
+
+template <int ROWS, int COLS, bool MN, bool SW>
+__device__ uint64_t op_desc(uint32_t base, int ks) {
+  if (SW) {
+    if (MN) return smem_desc_sw128(base + ks * 16 * 128, ROWS * 128, 1024);
+    return smem_desc_sw128(base + ((ks * 16) >> 6) * ROWS * 128 + ((ks * 16) & 63) * 2, 16, 1024);
+  }
+  constexpr int RS = (COLS / 8) * 128;
+  if (MN) return smem_desc(base + ks * 2 * RS, RS, 128);
+  return smem_desc(base + ks * 256, 128, RS);
+}
+
+template <int M, int N, int K, bool AMN, bool BMN, bool ASW, bool BSW>
 __global__ void __launch_bounds__(128) selftest(const __nv_bfloat16* A, const __nv_bfloat16* B,
                                                 float* Dout, int* status) {
   extern __shared__ __align__(1024) uint8_t sm[];
   constexpr int ACOLS = AMN ? M : K, AROWS = AMN ? K : M;
   constexpr int BCOLS = BMN ? N : K, BROWS = BMN ? K : N;
-  constexpr int RSA = (ACOLS / 8) * 128, RSB = (BCOLS / 8) * 128;
   uint8_t* aimg = sm;
-  uint8_t* bimg = sm + AROWS * ACOLS * 2;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(bimg + BROWS * BCOLS * 2);
+  uint8_t* bimg = sm + ((AROWS * ACOLS * 2 + 1023) / 1024) * 1024;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(bimg + ((BROWS * BCOLS * 2 + 1023) / 1024) * 1024);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int e = tid; e < AROWS * ACOLS; e += 128) {
-    const int r = e / ACOLS, c = e % ACOLS;
-    *reinterpret_cast<__nv_bfloat16*>(aimg + img_off(r, c, RSA)) = A[e];
-  }
-  for (int e = tid; e < BROWS * BCOLS; e += 128) {
-    const int r = e / BCOLS, c = e % BCOLS;
-    *reinterpret_cast<__nv_bfloat16*>(bimg + img_off(r, c, RSB)) = B[e];
-  }
+  for (int e = tid; e < AROWS * ACOLS; e += 128)
+    *reinterpret_cast<__nv_bfloat16*>(aimg + tile_off<AROWS, ACOLS, ASW>(e / ACOLS, e % ACOLS)) = A[e];
+  for (int e = tid; e < BROWS * BCOLS; e += 128)
+    *reinterpret_cast<__nv_bfloat16*>(bimg + tile_off<BROWS, BCOLS, BSW>(e / BCOLS, e % BCOLS)) = B[e];
   if (warp == 0) { tmem_alloc(tslot, 256); fence_before_sync(); }
   if (tid == 0) { mbar_init(bar, 1); mbar_fence_init(); }
   fence_proxy_async();
@@ -38,11 +51,9 @@ __global__ void __launch_bounds__(128) selftest(const __nv_bfloat16* A, const __
   if (tid == 0) {
     const uint32_t id = idesc_f16(M, N, true, AMN, BMN);
     const uint32_t aa = smem_u32(aimg), ba = smem_u32(bimg);
-    for (int ks = 0; ks < K / 16; ++ks) {
-      const uint64_t ad = AMN ? smem_desc(aa + ks * 2 * RSA, RSA, 128) : smem_desc(aa + ks * 256, 128, RSA);
-      const uint64_t bd = BMN ? smem_desc(ba + ks * 2 * RSB, RSB, 128) : smem_desc(ba + ks * 256, 128, RSB);
-      mma_f16(tmem, ad, bd, id, ks > 0);
-    }
+    for (int ks = 0; ks < K / 16; ++ks)
+      mma_f16(tmem, op_desc<AROWS, ACOLS, AMN, ASW>(aa, ks), op_desc<BROWS, BCOLS, BMN, BSW>(ba, ks),
+              id, ks > 0);
     mma_commit(smem_u32(bar));
   }
   const bool ok = mbar_wait(smem_u32(bar), 0, 200000000LL);
@@ -63,10 +74,10 @@ __global__ void __launch_bounds__(128) selftest(const __nv_bfloat16* A, const __
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
-template <int M, int N, int K, bool AMN, bool BMN>
+template <int M, int N, int K, bool AMN, bool BMN, bool ASW = false, bool BSW = false>
 static int run(const void* A, const void* B, float* D, int* st) {
-  auto k = selftest<M, N, K, AMN, BMN>;
-  const int smem = (M * K + N * K) * 2 + 64;
+  auto k = selftest<M, N, K, AMN, BMN, ASW, BSW>;
+  const int smem = (M * K + N * K) * 2 + 4096;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   k<<<1, 128, smem>>>(static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(B), D, st);
   return static_cast<int>(cudaDeviceSynchronize());
@@ -74,12 +85,17 @@ static int run(const void* A, const void* B, float* D, int* st) {
 
 extern "C" int umma_selftest(int which, const void* A, const void* B, float* D, int* st) {
   switch (which) {
-    case 0: return run<64, 64, 128, false, false>(A, B, D, st);   // S = K K^T
+    case 0: return run<64, 64, 128, false, false>(A, B, D, st);   // S = K K^T (no swizzle)
     case 1: return run<64, 128, 64, false, true>(A, B, D, st);    // W = T' K
     case 2: return run<128, 32, 64, true, true>(A, B, D, st);     // dH = K^T V~
     case 3: return run<64, 32, 128, false, true>(A, B, D, st);    // X = W h
     case 4: return run<128, 128, 64, true, true>(A, B, D, st);    // dH, VS = 128
     case 5: return run<64, 64, 64, false, true>(A, B, D, st);     // O = P v_new, VS = 64
+    case 6: return run<64, 64, 128, false, false, true, true>(A, B, D, st);   // S = K K^T, TMA tiles
+    case 7: return run<64, 128, 64, false, true, false, true>(A, B, D, st);   // W = T' K, K swizzled
+    case 8: return run<128, 32, 64, true, true, true, false>(A, B, D, st);    // dH = K^T V~, K swizzled
+    case 9: return run<64, 32, 128, false, true, true, false>(A, B, D, st);   // Y = Q h, Q swizzled
+    case 10: return run<128, 128, 64, true, true, true, false>(A, B, D, st);  // dH, VS = 128
     default: return -1;
   }
 }

@@ -12,7 +12,11 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 CASES = {0: (64, 64, 128, False, False), 1: (64, 128, 64, False, True),
          2: (128, 32, 64, True, True), 3: (64, 32, 128, False, True),
-         4: (128, 128, 64, True, True), 5: (64, 64, 64, False, True)}
+         4: (128, 128, 64, True, True), 5: (64, 64, 64, False, True),
+         # 128-byte swizzled (TMA-written) operands
+         6: (64, 64, 128, False, False), 7: (64, 128, 64, False, True),
+         8: (128, 32, 64, True, True), 9: (64, 32, 128, False, True),
+         10: (128, 128, 64, True, True)}
 
 
 @pytest.fixture(scope="module")
