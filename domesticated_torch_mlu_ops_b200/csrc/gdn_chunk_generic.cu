@@ -100,11 +100,11 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
   float* ks = sm;                 // [64][K]
   float* vs = ks + 64 * K;        // [64][V]
   float* A = vs + 64 * V;         // [64][65]
-  float* Tm = A + 64 * 65;        // [64][65]
-  float* gcs = Tm + 64 * 65;      // [64]
+  float* Tm = A + 64 * 68;        // [64][kTS] (A rows use 65, padded to 68)
+  float* gcs = Tm + 64 * kTS;     // [64]
   float* bs = gcs + 64;           // [64]
   float* cw = bs + 64;            // [64] beta * exp(G)
-  float* Zs = cw + 64;            // [64][17] solve scratch
+  float* Zs = cw + 64;            // kTrilScratch floats of solve scratch
   int64_t n, lc;
   if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
@@ -153,13 +153,13 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
   for (int e = tid; e < L * K; e += blockDim.x) {
     const int i = e / K, kk = e % K;
     float acc = 0.f;
-    for (int j = 0; j <= i; ++j) acc += Tm[i * 65 + j] * cw[j] * ks[j * K + kk];
+    for (int j = 0; j <= i; ++j) acc += Tm[i * kTS + j] * cw[j] * ks[j * K + kk];
     w.w[((s + i) * p.HV + hv) * K + kk] = acc;
   }
   for (int e = tid; e < L * V; e += blockDim.x) {
     const int i = e / V, vv = e % V;
     float acc = 0.f;
-    for (int j = 0; j <= i; ++j) acc += Tm[i * 65 + j] * bs[j] * vs[j * V + vv];
+    for (int j = 0; j <= i; ++j) acc += Tm[i * kTS + j] * bs[j] * vs[j * V + vv];
     w.u[((s + i) * p.HV + hv) * V + vv] = acc;
   }
 }
@@ -335,7 +335,7 @@ static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
-  const size_t wy_smem = sizeof(float) * (64 * a.K + 64 * a.V + 2 * 64 * 65 + 3 * 64 + 64 * 17);
+  const size_t wy_smem = sizeof(float) * (64 * a.K + 64 * a.V + 2 * 64 * 68 + 3 * 64 + kTrilScratch);
   const size_t st_smem = sizeof(float) * (a.K * kStateCols + 64 * kStateCols + 2 * 64 * a.K + 64);
   const size_t out_smem = sizeof(float) * (2 * 64 * a.K + 64 * 65 + 64);
   if ((e = cudaFuncSetAttribute(chunk_wy_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -17,16 +17,18 @@
 //   * P = tril_incl(exp(G_i - G_j) r_q,i r_k,j S_qk) (chunk_o.py:133-160);
 //   * per-row output / decay scales a_i = scale exp(G_i) r_q,i,
 //     b_i = exp(G_last - G_i) r_k,i and gamma = exp(G_last).
-//   W and P are written as ready-to-use UMMA operand images, U as V-slices.
+//   W (swizzled) and P are written as ready-to-use UMMA operand images, U as
+//   V-slices.  [K;Q] K^T and [T';T''] [K|V] are single M=128 MMAs, so every
+//   thread of the epilogues owns one row of the result.
 //
 // tc_state_kernel, one CTA per (sequence, v-head, V-slice of VS columns),
 // serial over the sequence's chunks (chunk_delta_h.py:28-197 fused with
 // chunk_o.py:30-170).  The fp32 state slice h (128 x VS) lives in registers
 // (thread t owns row t); its bf16 copy in shared memory is the B operand of
-//   X = W h,  Y = Q h                         (tcgen05, M=64)
-//   v_new = U - X, V~ = diag(b) v_new         (epilogue, fp32 -> bf16)
-//   dH = K^T V~,  O = P v_new                 (tcgen05, M=128 / M=64)
-//   h <- gamma h + dH,  o = a * Y + scale * O  (epilogue)
+//   [X; Y] = [W; Q] h                          (tcgen05, M=128)
+//   v_new = U - X, V~ = diag(b) v_new          (threads 0..63, fp32 -> bf16)
+//   dH = K^T V~,  [.; O] = [0; P] v_new        (tcgen05, M=128)
+//   h <- gamma h + dH,  o = a * Y + scale * O  (all threads / threads 64..127)
 // so h and v_new never leave the SM.  One thread streams the next chunk's
 // operands in with TMA / bulk copies while the current chunk computes.
 //
@@ -53,6 +55,7 @@ constexpr int RS128 = (D / 8) * 128;    // image row stride of a 128-column tile
 constexpr int RS64 = (64 / 8) * 128;    // image row stride of a 64-column tile
 constexpr int kScal = 132;              // per-(head, chunk) scalars: a[64], b[64], gamma, pad
 constexpr int kAtom = 64 * 128;         // one 64-row x 128-byte swizzled atom (8 KiB)
+constexpr float kLog2e = 1.4426950408889634f;
 
 enum ErrSite { kSiteWyLoad = 1, kSiteWyMma1 = 2, kSiteWyMma2 = 3, kSiteStLoad = 4,
                kSiteStMma1 = 5, kSiteStMma2 = 6 };
@@ -142,19 +145,21 @@ __device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* map, i
 // WY kernel
 // ---------------------------------------------------------------------------
 
+// Shared memory of the WY kernel.  [K;Q] is one 128-row swizzled operand
+// (64-column atoms of K rows then Q rows, 16 KiB apart) and, with V's atoms
+// at 32 KiB and 48 KiB, [K|V] is one N=256 MN-major operand with a uniform
+// 16 KiB atom stride.  The gaps between V's atoms hold small arrays.
 struct WySmem {
-  static constexpr int kK = 0;                   // swizzled tiles (1 KiB aligned)
-  static constexpr int kQ = kK + kImg64x128;
-  static constexpr int kV = kQ + kImg64x128;
-  static constexpr int kT1 = kV + kImg64x128;    // T' image
-  static constexpr int kT2 = kT1 + kImg64x64;    // T'' image
-  static constexpr int kA = kT2 + kImg64x64;     // f32 [64][65]
-  static constexpr int kT = kA + 64 * 65 * 4;    // f32 [64][65]
-  static constexpr int kZ = kT + 64 * 65 * 4;    // f32 [64][17] solve scratch
-  static constexpr int kVec = kZ + 64 * 17 * 4;  // gam, beta, rk, rq, cw, cu: f32 [6][64]
+  static constexpr int kKQ = 0;                  // K a0 | Q a0 | K a1 | Q a1
+  static constexpr int kV = 32768;               // V a0 at +0, V a1 at +16 KiB
+  static constexpr int kZ = kV + kAtom;          // f32 solve scratch (gap after V a0)
+  static constexpr int kVec = kV + 3 * kAtom;    // f32 [6][64] (gap after V a1)
   static constexpr int kBar = kVec + 6 * 64 * 4; // 3 mbarriers
   static constexpr int kTmem = kBar + 24;
-  static constexpr int kBytes = kTmem + 8 + 1024;  // + slack for 1 KiB alignment
+  static constexpr int kA = 65536;               // f32 [64][65]; then the [T';T''] image
+  static constexpr int kT = kA + 64 * kTrilStride * 4;  // f32 [64][kTS]
+  static constexpr int kBytes = kT + 64 * kTS * 4 + 1024;  // + slack for 1 KiB alignment
+  static_assert(kTrilScratch * 4 <= kAtom, "solve scratch must fit the gap");
 };
 
 template <typename T>
@@ -164,11 +169,9 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
              const __grid_constant__ CUtensorMap tv) {
   extern __shared__ uint8_t sm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* kbuf = sm + WySmem::kK;
-  uint8_t* qbuf = sm + WySmem::kQ;
+  uint8_t* kq = sm + WySmem::kKQ;
   uint8_t* vbuf = sm + WySmem::kV;
-  uint8_t* t1img = sm + WySmem::kT1;
-  uint8_t* t2img = sm + WySmem::kT2;
+  uint8_t* timg = sm + WySmem::kA;  // [T';T''] 128 x 64 image, written after the solve
   float* Af = reinterpret_cast<float*>(sm + WySmem::kA);
   float* Tf = reinterpret_cast<float*>(sm + WySmem::kT);
   float* Zs = reinterpret_cast<float*>(sm + WySmem::kZ);
@@ -199,10 +202,13 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     umma::mbar_init(bars + 2, 1);
     umma::mbar_fence_init();
     umma::mbar_arrive_expect_tx(bar_kq, 2 * kImg64x128);
-    tma_tile(kbuf, &tk, h, s, bar_kq);
-    tma_tile(qbuf, &tq, h, s, bar_kq);
+    umma::tma_load_3d(kq, &tk, 0, h, static_cast<int>(s), bar_kq);
+    umma::tma_load_3d(kq + kAtom, &tq, 0, h, static_cast<int>(s), bar_kq);
+    umma::tma_load_3d(kq + 2 * kAtom, &tk, 64, h, static_cast<int>(s), bar_kq);
+    umma::tma_load_3d(kq + 3 * kAtom, &tq, 64, h, static_cast<int>(s), bar_kq);
     umma::mbar_arrive_expect_tx(bar_v, kImg64x128);
-    tma_tile(vbuf, &tv, hv, s, bar_v);
+    umma::tma_load_3d(vbuf, &tv, 0, hv, static_cast<int>(s), bar_v);
+    umma::tma_load_3d(vbuf + 2 * kAtom, &tv, 64, hv, static_cast<int>(s), bar_v);
   }
   if (warp == 0) {
     umma::tmem_alloc(tslot, 256);
@@ -217,8 +223,8 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
       if (lane >= o) { g0 += y0; g1 += y1; }
     }
     g1 += __shfl_sync(0xffffffffu, g0, 31);
-    gam[lane] = g0;
-    gam[lane + 32] = g1;
+    gam[lane] = g0 * kLog2e;  // G in the log2 domain: exp(G_i - G_j) = exp2(gam_i - gam_j)
+    gam[lane + 32] = g1 * kLog2e;
   } else if (warp == 2) {
     bet[lane] = lane < L ? p.beta[(s + lane) * p.HV + hv] : 0.f;
     bet[lane + 32] = lane + 32 < L ? p.beta[(s + lane + 32) * p.HV + hv] : 0.f;
@@ -226,40 +232,39 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tslot;
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   constexpr bool kBf16 = !std::is_same<T, __half>::value;
 
   bool ok = umma::mbar_wait(bar_kq, 0);
   if (!ok) record_error(w.err, 1, kSiteWyLoad);
   if (__syncthreads_or(!ok)) goto teardown;
-  if (tid == 0) {
+  if (tid == 0) {  // [S_kk; S_qk] = [K; Q] K^T  (M = 128, N = 64, K = 128)
     umma::fence_after_sync();
-    const uint32_t id = umma::idesc_f16(64, 64, kBf16, false, false);
-    const uint32_t ka = umma::smem_u32(kbuf), qa = umma::smem_u32(qbuf);
+    const uint32_t id = umma::idesc_f16(128, 64, kBf16, false, false);
+    const uint64_t d0 = umma::smem_desc_sw128(umma::smem_u32(kq), 16, 1024);
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
-      const uint64_t bk = sw_kmajor(ka, ks);
-      umma::mma_f16(tmem + 0, bk, bk, id, ks > 0);
-      umma::mma_f16(tmem + 64, sw_kmajor(qa, ks), bk, id, ks > 0);
+      const uint64_t d = d0 + (((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4);
+      umma::mma_f16(tmem, d, d, id, ks > 0);
     }
     umma::mma_commit(bar_mma);
   }
-  {  // L2-norm factors from the swizzled rows: threads 0..63 -> k, 64..127 -> q
-    const int row = tid & 63;
-    const uint8_t* tile = tid < 64 ? kbuf : qbuf;
+  {  // L2-norm factors: thread t < 64 -> k row t, t >= 64 -> q row t - 64
     float ss = 0.f;
 #pragma unroll
     for (int cch = 0; cch < 16; ++cch) {
       float x[8];
-      unpack8<T>(*reinterpret_cast<const uint4*>(tile + umma::sw128_off(row, cch * 8, 64)), x);
+      const uint32_t off = (cch >> 3) * 2 * kAtom + tid * 128 + ((((cch & 7) ^ (tid & 7))) << 4);
+      unpack8<T>(*reinterpret_cast<const uint4*>(kq + off), x);
 #pragma unroll
       for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
     }
     const float r = p.use_qk_l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
-    if (tid < 64) rk[row] = r; else rq[row] = r;
+    if (tid < 64) rk[tid] = r; else rq[tid - 64] = r;
   }
   __syncthreads();
   if (tid < 64) {
-    cw[tid] = bet[tid] * __expf(gam[tid]) * rk[tid];
+    cw[tid] = bet[tid] * exp2f(gam[tid]) * rk[tid];
     cu[tid] = bet[tid];
   }
   ok = umma::mbar_wait(bar_mma, 0);
@@ -267,49 +272,49 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   if (__syncthreads_or(!ok)) goto teardown;
   umma::fence_after_sync();
 
-  {  // A (fp32, shared) and P (bf16 image, global) rows from S_kk, S_qk
-    const int i = warp * 16 + (lane & 15);
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  {  // row tid of [S_kk; S_qk]: A row (fp32, shared) or P row (bf16 image, global)
+    const bool is_p = tid >= 64;
+    const int i = tid & 63;
+    const float gi = gam[i], ri = is_p ? rq[i] : rk[i] * bet[i];
+    const int jmax = i < L ? (is_p ? i : i - 1) : -1;  // last nonzero column
     uint8_t* pimg = w.pimg + (static_cast<int64_t>(hv) * w.ncu + c) * kImg64x64;
-    const float gi = gam[i & 63], ri = rk[i & 63], qi = rq[i & 63], bi = bet[i & 63];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-      float skk[32], sqk[32];
-      umma::tmem_ld32(tmem + lane_base + half * 32, skk);
-      umma::tmem_ld32(tmem + lane_base + 64 + half * 32, sqk);
-      if (lane < 16) {
-        float pv[32];
+      float sv[32];
+      umma::tmem_ld32(tmem + lane_base + half * 32, sv);
+      float pv[32];
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = half * 32 + jj;
-          const float dec = j <= i ? __expf(gi - gam[j]) * rk[j] : 0.f;
-          Af[i * 65 + j] = (j < i && i < L) ? bi * dec * ri * skk[jj] : 0.f;
-          pv[jj] = i < L ? dec * qi * sqk[jj] : 0.f;
-        }
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const int j = half * 32 + j4 * 4;
+        const float4 gj = ld4(gam + j), rj = ld4(rk + j);
+        pv[j4 * 4 + 0] = j + 0 <= jmax ? exp2f(gi - gj.x) * ri * rj.x * sv[j4 * 4 + 0] : 0.f;
+        pv[j4 * 4 + 1] = j + 1 <= jmax ? exp2f(gi - gj.y) * ri * rj.y * sv[j4 * 4 + 1] : 0.f;
+        pv[j4 * 4 + 2] = j + 2 <= jmax ? exp2f(gi - gj.z) * ri * rj.z * sv[j4 * 4 + 2] : 0.f;
+        pv[j4 * 4 + 3] = j + 3 <= jmax ? exp2f(gi - gj.w) * ri * rj.w * sv[j4 * 4 + 3] : 0.f;
+      }
+      if (is_p) {
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8)
           *reinterpret_cast<uint4*>(pimg + umma::img_off(i, half * 32 + q8 * 8, RS64)) =
               pack8<T>(pv + q8 * 8);
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) Af[i * kTrilStride + half * 32 + jj] = pv[jj];
       }
     }
   }
   umma::fence_before_sync();
   __syncthreads();
   solve_tril64(Af, Tf, Zs);  // T = (I + A)^-1, ends with a barrier
-  {  // bf16 A operands T' = T diag(cw), T'' = T diag(beta): thread -> (row, 32 cols)
-    const int i = tid >> 1, c0 = (tid & 1) * 32;
+  {  // [T'; T''] image (A is dead): row tid < 64 -> T diag(cw), else T diag(beta)
+    const int i = tid & 63;
+    const float* coef = tid < 64 ? cw : cu;
 #pragma unroll
-    for (int q8 = 0; q8 < 4; ++q8) {
-      float x1[8], x2[8];
+    for (int q8 = 0; q8 < 8; ++q8) {
+      float x[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int j = c0 + q8 * 8 + e;
-        const float t = Tf[i * 65 + j];
-        x1[e] = t * cw[j];
-        x2[e] = t * cu[j];
-      }
-      *reinterpret_cast<uint4*>(t1img + umma::img_off(i, c0 + q8 * 8, RS64)) = pack8<T>(x1);
-      *reinterpret_cast<uint4*>(t2img + umma::img_off(i, c0 + q8 * 8, RS64)) = pack8<T>(x2);
+      for (int e = 0; e < 8; ++e) x[e] = Tf[i * kTS + q8 * 8 + e] * coef[q8 * 8 + e];
+      *reinterpret_cast<uint4*>(timg + umma::img_off(tid, q8 * 8, RS64)) = pack8<T>(x);
     }
   }
   umma::fence_proxy_async();
@@ -317,49 +322,48 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   ok = umma::mbar_wait(bar_v, 0);
   if (!ok) record_error(w.err, 1, kSiteWyLoad);
   if (__syncthreads_or(!ok)) goto teardown;
-  if (tid == 0) {
+  if (tid == 0) {  // [T' K | . ; . | T'' V] = [T'; T''] [K | V]  (M = 128, N = 256, K = 64)
     umma::fence_after_sync();
-    const uint32_t id = umma::idesc_f16(64, D, kBf16, false, true);
-    const uint32_t t1 = umma::smem_u32(t1img), t2 = umma::smem_u32(t2img);
-    const uint32_t ka = umma::smem_u32(kbuf), va = umma::smem_u32(vbuf);
+    const uint32_t id = umma::idesc_f16(128, 256, kBf16, false, true);
+    const uint64_t da = umma::smem_desc(umma::smem_u32(timg), 128, RS64);
+    const uint64_t db = umma::smem_desc_sw128(umma::smem_u32(kq), 2 * kAtom, 1024);
 #pragma unroll
-    for (int ks = 0; ks < 64 / 16; ++ks) {
-      umma::mma_f16(tmem + 0, umma::smem_desc(t1 + ks * 256, 128, RS64), sw_mnmajor(ka, ks), id, ks > 0);
-      umma::mma_f16(tmem + 128, umma::smem_desc(t2 + ks * 256, 128, RS64), sw_mnmajor(va, ks), id, ks > 0);
-    }
+    for (int ks = 0; ks < 64 / 16; ++ks)
+      umma::mma_f16(tmem, da + ((ks * 256) >> 4), db + ((ks * 2048) >> 4), id, ks > 0);
     umma::mma_commit(bar_mma);
   }
   if (tid < 64) {
     float* sc = w.scal + (static_cast<int64_t>(hv) * w.ncu + c) * kScal;
     const float glast = gam[L - 1];
-    sc[tid] = tid < L ? scale * __expf(gam[tid]) * rq[tid] : 0.f;
-    sc[64 + tid] = tid < L ? __expf(glast - gam[tid]) * rk[tid] : 0.f;
-    if (tid < 4) sc[128 + tid] = tid == 0 ? __expf(glast) : 0.f;
+    sc[tid] = tid < L ? scale * exp2f(gam[tid]) * rq[tid] : 0.f;
+    sc[64 + tid] = tid < L ? exp2f(glast - gam[tid]) * rk[tid] : 0.f;
+    if (tid < 4) sc[128 + tid] = tid == 0 ? exp2f(glast) : 0.f;
   }
   ok = umma::mbar_wait(bar_mma, 1);
   if (!ok) record_error(w.err, 1, kSiteWyMma2);
   if (__syncthreads_or(!ok)) goto teardown;
   umma::fence_after_sync();
 
-  {  // W image and U V-slices to the workspace
-    const int i = warp * 16 + (lane & 15);
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  {  // row tid < 64: W row (swizzled image); tid >= 64: U row (V-slices)
+    const int i = tid & 63;
     const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c;
+    const uint32_t col0 = tid < 64 ? 0 : 128;
     uint8_t* wdst = w.wimg + hc * kImg64x128;
     T* ubase = reinterpret_cast<T*>(w.u) + hc * 64 * D;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      float x[32], y[32];
-      umma::tmem_ld32(tmem + lane_base + q * 32, x);
-      umma::tmem_ld32(tmem + lane_base + 128 + q * 32, y);
-      if (lane < 16) {
+      float x[32];
+      umma::tmem_ld32(tmem + lane_base + col0 + q * 32, x);
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          const int col = q * 32 + q8 * 8;
-          *reinterpret_cast<uint4*>(wdst + umma::img_off(i, col, RS128)) = pack8<T>(x + q8 * 8);
+      for (int q8 = 0; q8 < 4; ++q8) {
+        const int col = q * 32 + q8 * 8;
+        if (tid < 64) {
+          const uint32_t off = (col >> 6) * kAtom + i * 128 + ((((col & 63) >> 3) ^ (i & 7)) << 4);
+          *reinterpret_cast<uint4*>(wdst + off) = pack8<T>(x + q8 * 8);
+        } else {
           const int sl = col / w.vs, wc = col % w.vs;
           *reinterpret_cast<uint4*>(ubase + (static_cast<int64_t>(sl) * 64 + i) * w.vs + wc) =
-              pack8<T>(y + q8 * 8);
+              pack8<T>(x + q8 * 8);
         }
       }
     }
@@ -377,26 +381,29 @@ teardown:
 
 template <int VS>
 struct StSmem {
-  // per stage (1 KiB aligned): Q, K (swizzled TMA tiles), W image, P image,
-  // U slice [64][VS], scalars (a, b, gamma)
+  // Per stage (1 KiB aligned):
+  //   [W;Q]  one 128-row swizzled operand: W a0 | Q a0 | W a1 | Q a1
+  //   K      swizzled 64-row tile (atoms 8 KiB apart)
+  //   [0;P]  128 x 64 no-swizzle image whose top half stays zero
+  //   U slice [64][VS], scalars (a, b, gamma)
   static constexpr int kUBytes = 64 * VS * 2;
-  static constexpr int kQ = 0;
-  static constexpr int kKt = kQ + kImg64x128;
-  static constexpr int kW = kKt + kImg64x128;
-  static constexpr int kP = kW + kImg64x128;
-  static constexpr int kU = kP + kImg64x64;
+  static constexpr int kWQ = 0;
+  static constexpr int kKt = 4 * kAtom;
+  static constexpr int kZP = kKt + 2 * kAtom;
+  static constexpr int kU = kZP + 2 * kImg64x64;
   static constexpr int kScalOff = kU + kUBytes;
   static constexpr int kStageBytes = ((kScalOff + kScal * 4 + 1023) / 1024) * 1024;
   static constexpr uint32_t kTx = 3 * kImg64x128 + kImg64x64 + kUBytes + kScal * 4;
+  static constexpr int kBar = kScalOff + kScal * 4;      // in stage 0's tail padding
+  static constexpr int kTmem = kBar + 24;
   static constexpr int kH = 2 * kStageBytes;             // h image 128 x VS
   static constexpr int kVt = kH + D * VS * 2;            // V~ image 64 x VS
   static constexpr int kVn = kVt + 64 * VS * 2;          // v_new image 64 x VS
-  static constexpr int kBar = kVn + 64 * VS * 2;         // full[2], mma
-  static constexpr int kTmem = kBar + 24;
-  static constexpr int kBytes = kTmem + 8 + 1024;
-  // TMEM columns: X, dH, then Y/O, double-buffered when they fit in 512
-  static constexpr bool kDbl = 6 * VS <= 512;
-  static constexpr int kCols = kDbl ? 6 * VS : 4 * VS;
+  static constexpr int kBytes = kVn + 64 * VS * 2 + 1024;
+  static_assert(kTmem + 8 <= kStageBytes, "barriers must fit in the stage padding");
+  // TMEM columns: [X;Y] and O double-buffered when they fit, plus dH
+  static constexpr bool kDbl = 5 * VS <= 512;
+  static constexpr int kCols = kDbl ? 5 * VS : 3 * VS;
   static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
                                    : kCols <= 256 ? 256 : 512;
 };
@@ -416,7 +423,7 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::kTmem);
   const uint32_t bar_mma = umma::smem_u32(bars + 2);
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t n = blockIdx.x;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
   const int vsl = blockIdx.z, v0 = vsl * VS;
@@ -429,13 +436,17 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
   auto fetch = [&](int64_t lc, int st) {
     uint8_t* base = sm + st * S::kStageBytes;
     const uint32_t bar = umma::smem_u32(bars + st);
-    const int64_t s = bos + lc * kChunk;
+    const int s = static_cast<int>(bos + lc * kChunk);
     const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c0 + lc;
+    const uint8_t* wsrc = w.wimg + hc * kImg64x128;
     umma::mbar_arrive_expect_tx(bar, S::kTx);
-    tma_tile(base + S::kQ, &tq, h, s, bar);
-    tma_tile(base + S::kKt, &tk, h, s, bar);
-    umma::bulk_g2s(base + S::kW, w.wimg + hc * kImg64x128, kImg64x128, bar);
-    umma::bulk_g2s(base + S::kP, w.pimg + hc * kImg64x64, kImg64x64, bar);
+    umma::bulk_g2s(base + S::kWQ, wsrc, kAtom, bar);
+    umma::tma_load_3d(base + S::kWQ + kAtom, &tq, 0, h, s, bar);
+    umma::bulk_g2s(base + S::kWQ + 2 * kAtom, wsrc + kAtom, kAtom, bar);
+    umma::tma_load_3d(base + S::kWQ + 3 * kAtom, &tq, 64, h, s, bar);
+    umma::tma_load_3d(base + S::kKt, &tk, 0, h, s, bar);
+    umma::tma_load_3d(base + S::kKt + kAtom, &tk, 64, h, s, bar);
+    umma::bulk_g2s(base + S::kZP + kImg64x64, w.pimg + hc * kImg64x64, kImg64x64, bar);
     umma::bulk_g2s(base + S::kU, w.u + ((hc * (D / VS) + vsl) * 64 * VS) * 2, S::kUBytes, bar);
     umma::bulk_g2s(base + S::kScalOff, w.scal + hc * kScal, kScal * 4, bar);
   };
@@ -450,6 +461,10 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
   if (warp == 0) {
     umma::tmem_alloc(tslot, S::kTmemCols);
     umma::fence_before_sync();
+  }
+  for (int e = tid; e < kImg64x64 / 16; e += 128) {  // zero top halves of both [0;P]
+    reinterpret_cast<uint4*>(sm + S::kZP)[e] = make_uint4(0, 0, 0, 0);
+    reinterpret_cast<uint4*>(sm + S::kStageBytes + S::kZP)[e] = make_uint4(0, 0, 0, 0);
   }
 
   // initial state slice: thread t owns row t (key dim) of h[:, v0:v0+VS]
@@ -472,22 +487,30 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tslot;
-  const uint32_t tX = tmem, tDH = tmem + VS;
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  // TMEM: [X;Y] at xy(par), O at o(par) (rows 64..127), dH
+  auto xy_col = [&](int par) { return tmem + (S::kDbl ? par * VS : 0); };
+  auto o_col = [&](int par) { return tmem + (S::kDbl ? 2 * VS + par * VS : VS); };
+  const uint32_t tDH = tmem + (S::kDbl ? 4 * VS : 2 * VS);
   constexpr bool kBf16 = !std::is_same<T, __half>::value;
+  const uint32_t id_xy = umma::idesc_f16(128, VS, kBf16, false, true);
+  const uint32_t id_dh = umma::idesc_f16(128, VS, kBf16, true, true);
+  const uint64_t d_h = umma::smem_desc(umma::smem_u32(himg), RSV, 128);
+  const uint64_t d_vt = umma::smem_desc(umma::smem_u32(vtimg), RSV, 128);
+  const uint64_t d_vn = umma::smem_desc(umma::smem_u32(vnimg), RSV, 128);
   T* obase = static_cast<T*>(p.o);
-  const int i_row = warp * 16 + (lane & 15);  // chunk row held by this lane in M=64 results
+  const int i_row = tid & 63;  // chunk row of this thread in [X;Y] / [.;O] results
   bool ok = true;
 
-  // Output rows of a finished chunk: o = a * Y + scale * O (TMEM buffers yo).
-  auto emit = [&](uint32_t yo, int64_t s, int L, float ai) {
+  // Output rows of a finished chunk (threads 64..127): o = a * Y + scale * O.
+  auto emit = [&](int par, int64_t s, int L, float ai) {
     T* orow = obase + ((s + i_row) * p.HV + hv) * D + v0;
 #pragma unroll
     for (int q = 0; q < VS / 32; ++q) {
       float y[32], z[32];
-      umma::tmem_ld32(yo + lane_base + q * 32, y);
-      umma::tmem_ld32(yo + VS + lane_base + q * 32, z);
-      if (lane < 16 && i_row < L) {
+      umma::tmem_ld32(xy_col(par) + lane_base + q * 32, y);
+      umma::tmem_ld32(o_col(par) + lane_base + q * 32, z);
+      if (i_row < L) {
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
           float ov[8];
@@ -504,29 +527,25 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
   float a_prev = 0.f;
   for (int64_t lc = 0; lc < nch; ++lc) {
     const int st = static_cast<int>(lc & 1);
+    const int par = S::kDbl ? st : 0;
     uint8_t* base = sm + st * S::kStageBytes;
     const int64_t s = bos + lc * kChunk;
     const int L = static_cast<int>(min64(kChunk, eos - s));
-    const uint32_t tYO = tmem + 2 * VS + (S::kDbl ? st * 2 * VS : 0);
 
     ok = umma::mbar_wait(umma::smem_u32(bars + st), static_cast<uint32_t>((lc >> 1) & 1));
     if (!ok) record_error(w.err, 1, kSiteStLoad);
     if (__syncthreads_or(!ok)) break;
-    if (tid == 0) {  // X = W h, Y = Q h; then stream in the next chunk
+    if (tid == 0) {  // [X; Y] = [W; Q] h  (M = 128, N = VS, K = 128)
       umma::fence_after_sync();
-      const uint32_t id = umma::idesc_f16(64, VS, kBf16, false, true);
-      const uint32_t wa = umma::smem_u32(base + S::kW), qa = umma::smem_u32(base + S::kQ);
-      const uint32_t ha = umma::smem_u32(himg);
+      const uint64_t da = umma::smem_desc_sw128(umma::smem_u32(base + S::kWQ), 16, 1024);
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        const uint64_t bh = umma::smem_desc(ha + ks * 2 * RSV, RSV, 128);
-        umma::mma_f16(tX, umma::smem_desc(wa + ks * 256, 128, RS128), bh, id, ks > 0);
-        umma::mma_f16(tYO, sw_kmajor(qa, ks), bh, id, ks > 0);
-      }
+      for (int ks = 0; ks < D / 16; ++ks)
+        umma::mma_f16(xy_col(par), da + (((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4),
+                      d_h + ((ks * 2 * RSV) >> 4), id_xy, ks > 0);
       umma::mma_commit(bar_mma);
       if (lc + 1 < nch) fetch(lc + 1, st ^ 1);
     }
-    if (S::kDbl && lc > 0) emit(tmem + 2 * VS + (st ^ 1) * 2 * VS, s_prev, L_prev, a_prev);
+    if (S::kDbl && lc > 0 && tid >= 64) emit(par ^ 1, s_prev, L_prev, a_prev);
 
     ok = umma::mbar_wait(bar_mma, 0);
     if (!ok) record_error(w.err, 1, kSiteStMma1);
@@ -534,48 +553,43 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
     umma::fence_after_sync();
 
     const float* scv = reinterpret_cast<const float*>(base + S::kScalOff);
-    {  // v_new = U - X; images of v_new and diag(b) v_new
-      const float bi = scv[64 + (i_row & 63)];
-      const uint8_t* urow = base + S::kU + (i_row & 63) * VS * 2;
+    if (tid < 64) {  // v_new = U - X; images of v_new and diag(b) v_new (row tid)
+      const float bi = scv[64 + i_row];
+      const uint8_t* urow = base + S::kU + i_row * VS * 2;
 #pragma unroll
       for (int q = 0; q < VS / 32; ++q) {
         float x[32];
-        umma::tmem_ld32(tX + lane_base + q * 32, x);
-        if (lane < 16) {
+        umma::tmem_ld32(xy_col(par) + lane_base + q * 32, x);
 #pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) {
-            float u8[8], vn[8], vt[8];
-            unpack8<T>(*reinterpret_cast<const uint4*>(urow + (q * 32 + q8 * 8) * 2), u8);
+        for (int q8 = 0; q8 < 4; ++q8) {
+          float u8[8], vn[8], vt[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(urow + (q * 32 + q8 * 8) * 2), u8);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              vn[e] = u8[e] - x[q8 * 8 + e];
-              vt[e] = bi * vn[e];
-            }
-            *reinterpret_cast<uint4*>(vnimg + umma::img_off(i_row, q * 32 + q8 * 8, RSV)) = pack8<T>(vn);
-            *reinterpret_cast<uint4*>(vtimg + umma::img_off(i_row, q * 32 + q8 * 8, RSV)) = pack8<T>(vt);
+          for (int e = 0; e < 8; ++e) {
+            vn[e] = u8[e] - x[q8 * 8 + e];
+            vt[e] = bi * vn[e];
           }
+          *reinterpret_cast<uint4*>(vnimg + umma::img_off(i_row, q * 32 + q8 * 8, RSV)) = pack8<T>(vn);
+          *reinterpret_cast<uint4*>(vtimg + umma::img_off(i_row, q * 32 + q8 * 8, RSV)) = pack8<T>(vt);
         }
       }
     }
     umma::fence_proxy_async();
     umma::fence_before_sync();
     __syncthreads();
-    if (tid == 0) {  // dH = K^T V~, O = P v_new
+    if (tid == 0) {  // dH = K^T V~ ; [.; O] = [0; P] v_new
       umma::fence_after_sync();
-      const uint32_t id128 = umma::idesc_f16(128, VS, kBf16, true, true);
-      const uint32_t id64 = umma::idesc_f16(64, VS, kBf16, false, true);
-      const uint32_t ka = umma::smem_u32(base + S::kKt), pa = umma::smem_u32(base + S::kP);
-      const uint32_t vt = umma::smem_u32(vtimg), vn = umma::smem_u32(vnimg);
+      const uint64_t dk = umma::smem_desc_sw128(umma::smem_u32(base + S::kKt), kAtom, 1024);
+      const uint64_t dp = umma::smem_desc(umma::smem_u32(base + S::kZP), 128, RS64);
 #pragma unroll
       for (int ks = 0; ks < 64 / 16; ++ks) {
-        umma::mma_f16(tDH, sw_mnmajor(ka, ks), umma::smem_desc(vt + ks * 2 * RSV, RSV, 128), id128, ks > 0);
-        umma::mma_f16(tYO + VS, umma::smem_desc(pa + ks * 256, 128, RS64),
-                      umma::smem_desc(vn + ks * 2 * RSV, RSV, 128), id64, ks > 0);
+        umma::mma_f16(tDH, dk + ((ks * 2048) >> 4), d_vt + ((ks * 2 * RSV) >> 4), id_dh, ks > 0);
+        umma::mma_f16(o_col(par), dp + ((ks * 256) >> 4), d_vn + ((ks * 2 * RSV) >> 4), id_xy, ks > 0);
       }
       umma::mma_commit(bar_mma);
     }
     const float g = scv[128];
-    const float ai = scv[i_row & 63];
+    const float ai = scv[i_row];
     ok = umma::mbar_wait(bar_mma, 1);
     if (!ok) record_error(w.err, 1, kSiteStMma2);
     if (__syncthreads_or(!ok)) break;
@@ -592,7 +606,7 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
 #pragma unroll
     for (int j8 = 0; j8 < VS / 8; ++j8)
       *reinterpret_cast<uint4*>(himg + umma::img_off(tid, j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
-    if (!S::kDbl) emit(tYO, s, L, ai);
+    if (!S::kDbl && tid >= 64) emit(par, s, L, ai);
     s_prev = s;
     L_prev = L;
     a_prev = ai;
@@ -600,8 +614,8 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
     umma::fence_before_sync();
     __syncthreads();
   }
-  if (ok && S::kDbl && nch > 0)
-    emit(tmem + 2 * VS + static_cast<uint32_t>((nch - 1) & 1) * 2 * VS, s_prev, L_prev, a_prev);
+  if (ok && S::kDbl && nch > 0 && tid >= 64)
+    emit(static_cast<int>((nch - 1) & 1), s_prev, L_prev, a_prev);
 
   if (ok && p.final_state) {
     const int64_t base = (n * p.HV + hv) * D * D;

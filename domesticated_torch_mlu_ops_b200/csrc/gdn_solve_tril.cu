@@ -21,9 +21,9 @@ template <typename TO>
 __global__ void __launch_bounds__(128)
 solve_tril_kernel(const float* __restrict__ A, TO* __restrict__ out, const void* cu, int cu_dtype,
                   int64_t T, int H, int BT) {
-  __shared__ float As[64 * kTrilStride];
-  __shared__ float Ts[64 * kTrilStride];
-  __shared__ float Zs[64 * kTrilZStride];
+  __shared__ __align__(16) float As[64 * kTrilStride];
+  __shared__ __align__(16) float Ts[64 * kTS];
+  __shared__ __align__(16) float Zs[kTrilScratch];
   const int64_t n = blockIdx.x;
   const int h = blockIdx.y;
   int64_t bos, eos;
@@ -39,7 +39,7 @@ solve_tril_kernel(const float* __restrict__ A, TO* __restrict__ out, const void*
     solve_tril64(As, Ts, Zs);
     for (int e = threadIdx.x; e < L * BT; e += blockDim.x) {
       const int i = e / BT, j = e % BT;
-      out[((s + i) * H + h) * BT + j] = from_f<TO>(j < L ? Ts[i * kTrilStride + j] : 0.f);
+      out[((s + i) * H + h) * BT + j] = from_f<TO>(j < L ? Ts[i * kTS + j] : 0.f);
     }
     __syncthreads();
   }

@@ -16,7 +16,11 @@ CASES = {0: (64, 64, 128, False, False), 1: (64, 128, 64, False, True),
          # 128-byte swizzled (TMA-written) operands
          6: (64, 64, 128, False, False), 7: (64, 128, 64, False, True),
          8: (128, 32, 64, True, True), 9: (64, 32, 128, False, True),
-         10: (128, 128, 64, True, True)}
+         10: (128, 128, 64, True, True),
+         # stacked M=128 operands, N=256 with spread-out atoms
+         11: (128, 64, 128, False, False), 12: (128, 256, 64, False, True),
+         13: (128, 32, 128, False, True), 14: (128, 32, 64, False, True),
+         15: (128, 128, 128, False, True)}
 
 
 @pytest.fixture(scope="module")
