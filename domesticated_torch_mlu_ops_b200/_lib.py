@@ -24,6 +24,7 @@ GDN_F32, GDN_BF16, GDN_F16, GDN_I32, GDN_I64 = 0, 1, 2, 3, 4
 EXPORTED = (
     "gdn_chunk_workspace_size",
     "gdn_chunk_fwd",
+    "gdn_chunk_fwd_noalloc",
     "gdn_chunk_check_device_error",
     "gdn_fused_recurrent_fwd",
     "gdn_recurrent_plain_fwd",
@@ -96,6 +97,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.gdn_chunk_workspace_size.restype = ctypes.c_size_t
     lib.gdn_chunk_fwd.argtypes = [ctypes.POINTER(ChunkArgs), _vp]
     lib.gdn_chunk_fwd.restype = ctypes.c_int
+    lib.gdn_chunk_fwd_noalloc.argtypes = [ctypes.POINTER(ChunkArgs), _vp]
+    lib.gdn_chunk_fwd_noalloc.restype = ctypes.c_int
     lib.gdn_chunk_check_device_error.argtypes = [_vp, _vp]
     lib.gdn_chunk_check_device_error.restype = ctypes.c_int
     lib.gdn_fused_recurrent_fwd.argtypes = [ctypes.POINTER(RecurrentArgs), _vp]

@@ -69,6 +69,14 @@ size_t workspace_bytes(const gdn_chunk_args& a) {
 
 }  // namespace
 
+int gdn::set_last_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
 extern "C" {
 
 const char* gdn_last_error(void) { return g_last_error; }

@@ -24,6 +24,9 @@ struct ChunkWorkspace {
 // Count of kernels launched by this library (gdn_kernel_launch_count).
 void note_launch(int n = 1);
 
+// Sets the thread-local message returned by gdn_last_error; returns `code`.
+int set_last_error(int code, const char* fmt, ...);
+
 // Per-call launch instrumentation: records the caller's optional stage
 // events (gdn_chunk_args::stage_events) and counts launches.
 struct LaunchHooks {

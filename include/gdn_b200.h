@@ -98,6 +98,21 @@ GDN_API size_t gdn_chunk_workspace_size(const gdn_chunk_args* args);
 
 GDN_API int gdn_chunk_fwd(const gdn_chunk_args* args, void* stream);
 
+/*
+ * Allocation-free variant of gdn_chunk_fwd (no counterpart in the reference).
+ * For callers that cannot allocate device memory: C hosts without an
+ * allocator of their own, code running inside CUDA graph capture, engines
+ * whose memory pool is fully reserved.  args->workspace and
+ * args->workspace_bytes are ignored; the workspace comes from a 32 MiB scratch
+ * array built into the library (held on every GPU that loads the library
+ * until exit).  Calls whose workspace (gdn_chunk_workspace_size) exceeds
+ * 32 MiB return GDN_ERR_WORKSPACE.  The first call on a device looks up the
+ * array's device address (make it before any stream capture).  All calls
+ * share the one array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  Allocates nothing.
+ */
+GDN_API int gdn_chunk_fwd_noalloc(const gdn_chunk_args* args, void* stream);
+
 /* Reads back (synchronously, on `stream`) the device error word that the
  * chunk kernels keep in `workspace`; returns GDN_OK or GDN_ERR_DEVICE and
  * clears the word. */
