@@ -53,6 +53,8 @@ bool tc_path_applies(const gdn_chunk_args& a);
 size_t tc_workspace_bytes(const gdn_chunk_args& a);
 
 cudaError_t launch_recurrent_vfirst(const gdn_recurrent_args& a, cudaStream_t s);
+bool decode_stream_applies(const gdn_recurrent_args& a);
+cudaError_t launch_decode_stream(const gdn_recurrent_args& a, cudaStream_t s);
 cudaError_t launch_recurrent_kfirst(const gdn_recurrent_plain_args& a, cudaStream_t s);
 cudaError_t launch_chunk_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s);
 cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s);

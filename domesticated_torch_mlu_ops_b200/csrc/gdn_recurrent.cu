@@ -11,6 +11,8 @@
 //   each holding a 128-bit segment, and the two dot products are reduced
 //   together; the state is streamed with no-allocate loads and evict-first
 //   stores.  This kernel is HBM-bound: 2 * HV * V * K * 4 bytes per sequence.
+//   With K = 128 and aligned buffers the persistent streaming kernel of
+//   gdn_decode_stream.cu is used instead.
 //
 // recurrent_kfirst_kernel: the plain recurrence of
 //   fused_recurrent_gated_delta_rule (triton/fla/fused_recurrent.py:15-131)
@@ -23,10 +25,10 @@
 
 namespace gdn {
 
-template <typename T, int TPR, int RW>
-__global__ void __launch_bounds__(128)
+template <typename T, int TPR, int RW, int kThreads>
+__global__ void __launch_bounds__(kThreads)
 recurrent_vfirst_kernel(const gdn_recurrent_args p) {
-  constexpr int kWarps = 4;
+  constexpr int kWarps = kThreads / 32;
   constexpr int RPP = 32 / TPR;                  // rows per warp per slot
   constexpr int kRowsPerCta = kWarps * RPP * RW;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -205,12 +207,12 @@ __global__ void recurrent_kfirst_kernel(const gdn_recurrent_plain_args p) {
 
 // ---- launchers ---------------------------------------------------------------
 
-template <typename T, int TPR, int RW>
+template <typename T, int TPR, int RW, int kThreads = 128>
 static cudaError_t launch_vfirst_t(const gdn_recurrent_args& a, cudaStream_t s) {
-  constexpr int kRowsPerCta = 4 * (32 / TPR) * RW;
+  constexpr int kRowsPerCta = (kThreads / 32) * (32 / TPR) * RW;
   dim3 grid(static_cast<unsigned>(a.N * a.HV), (a.V + kRowsPerCta - 1) / kRowsPerCta);
   note_launch();
-  recurrent_vfirst_kernel<T, TPR, RW><<<grid, 128, 0, s>>>(a);
+  recurrent_vfirst_kernel<T, TPR, RW, kThreads><<<grid, kThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -228,6 +230,7 @@ static cudaError_t launch_vfirst_k(const gdn_recurrent_args& a, cudaStream_t s) 
 }
 
 cudaError_t launch_recurrent_vfirst(const gdn_recurrent_args& a, cudaStream_t s) {
+  if (decode_stream_applies(a)) return launch_decode_stream(a, s);
   switch (a.qkv_dtype) {
     case GDN_F32: return launch_vfirst_k<float>(a, s);
     case GDN_BF16: return launch_vfirst_k<__nv_bfloat16>(a, s);
