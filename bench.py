@@ -471,7 +471,8 @@ def _decode_bench(ops, dev, a, hbm, flush):
     gbs = nbytes / (us * 1e-6) / 1e9
     return {"workload": "config3: 256 sequences x 1 token, cache [1024,32,128,128] f32",
             "us_per_step": us, "algorithmic_bytes": nbytes, "achieved_gbs": gbs,
-            "peak_gbs": hbm, "frac_hbm": gbs / hbm}
+            "peak_gbs": hbm, "frac_hbm": gbs / hbm, "peak_kind": "measured HBM copy",
+            "kernel": "decode_stream_kernel", "traffic": _load_traffic().get("decode")}
 
 
 def run_reference(a):
