@@ -395,7 +395,7 @@ struct StSmem {
   static constexpr int kStageBytes = ((kScalOff + kScal * 4 + 1023) / 1024) * 1024;
   static constexpr uint32_t kTx = 3 * kImg64x128 + kImg64x64 + kUBytes + kScal * 4;
   static constexpr int kBar = kScalOff + kScal * 4;      // in stage 0's tail padding
-  static constexpr int kTmem = kBar + 24;
+  static constexpr int kTmem = kBar + 32;
   static constexpr int kH = 2 * kStageBytes;             // h image 128 x VS
   static constexpr int kVt = kH + D * VS * 2;            // V~ image 64 x VS
   static constexpr int kVn = kVt + 64 * VS * 2;          // v_new image 64 x VS
@@ -419,9 +419,9 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
   uint8_t* himg = sm + S::kH;
   uint8_t* vtimg = sm + S::kVt;
   uint8_t* vnimg = sm + S::kVn;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBar);  // full[2], mma1, mma2
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::kTmem);
-  const uint32_t bar_mma = umma::smem_u32(bars + 2);
+  const uint32_t bar_mma1 = umma::smem_u32(bars + 2), bar_mma2 = umma::smem_u32(bars + 3);
 
   const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t n = blockIdx.x;
@@ -454,7 +454,8 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
   if (tid == 0) {
     umma::mbar_init(bars, 1);
     umma::mbar_init(bars + 1, 1);
-    umma::mbar_init(bars + 2, 1);
+    umma::mbar_init(bars + 2, 1);  // [X;Y] MMAs: one committing warp
+    umma::mbar_init(bars + 3, 2);  // dH and O MMAs: two committing warps
     umma::mbar_fence_init();
     if (nch > 0) fetch(0, 0);
   }
@@ -535,19 +536,21 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
     ok = umma::mbar_wait(umma::smem_u32(bars + st), static_cast<uint32_t>((lc >> 1) & 1));
     if (!ok) record_error(w.err, 1, kSiteStLoad);
     if (__syncthreads_or(!ok)) break;
-    if (tid == 0) {  // [X; Y] = [W; Q] h  (M = 128, N = VS, K = 128)
+    if (warp == 0) {  // [X; Y] = [W; Q] h  (M = 128, N = VS, K = 128), one elected lane issues
       umma::fence_after_sync();
       const uint64_t da = umma::smem_desc_sw128(umma::smem_u32(base + S::kWQ), 16, 1024);
 #pragma unroll
       for (int ks = 0; ks < D / 16; ++ks)
-        umma::mma_f16(xy_col(par), da + (((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4),
-                      d_h + ((ks * 2 * RSV) >> 4), id_xy, ks > 0);
-      umma::mma_commit(bar_mma);
-      if (lc + 1 < nch) fetch(lc + 1, st ^ 1);
+        if (umma::elect_one())
+          umma::mma_f16(xy_col(par), da + (((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4),
+                        d_h + ((ks * 2 * RSV) >> 4), id_xy, ks > 0);
+      if (umma::elect_one()) umma::mma_commit(bar_mma1);
+    } else if (warp == 3) {  // stream in the next chunk meanwhile
+      if (lc + 1 < nch && umma::elect_one()) fetch(lc + 1, st ^ 1);
     }
     if (S::kDbl && lc > 0 && tid >= 64) emit(par ^ 1, s_prev, L_prev, a_prev);
 
-    ok = umma::mbar_wait(bar_mma, 0);
+    ok = umma::mbar_wait(bar_mma1, static_cast<uint32_t>(lc & 1));
     if (!ok) record_error(w.err, 1, kSiteStMma1);
     if (__syncthreads_or(!ok)) break;
     umma::fence_after_sync();
@@ -577,20 +580,26 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
     umma::fence_proxy_async();
     umma::fence_before_sync();
     __syncthreads();
-    if (tid == 0) {  // dH = K^T V~ ; [.; O] = [0; P] v_new
+    if (warp == 0) {  // dH = K^T V~
       umma::fence_after_sync();
       const uint64_t dk = umma::smem_desc_sw128(umma::smem_u32(base + S::kKt), kAtom, 1024);
+#pragma unroll
+      for (int ks = 0; ks < 64 / 16; ++ks)
+        if (umma::elect_one())
+          umma::mma_f16(tDH, dk + ((ks * 2048) >> 4), d_vt + ((ks * 2 * RSV) >> 4), id_dh, ks > 0);
+      if (umma::elect_one()) umma::mma_commit(bar_mma2);
+    } else if (warp == 1) {  // [.; O] = [0; P] v_new, issued in parallel from another warp
+      umma::fence_after_sync();
       const uint64_t dp = umma::smem_desc(umma::smem_u32(base + S::kZP), 128, RS64);
 #pragma unroll
-      for (int ks = 0; ks < 64 / 16; ++ks) {
-        umma::mma_f16(tDH, dk + ((ks * 2048) >> 4), d_vt + ((ks * 2 * RSV) >> 4), id_dh, ks > 0);
-        umma::mma_f16(o_col(par), dp + ((ks * 256) >> 4), d_vn + ((ks * 2 * RSV) >> 4), id_xy, ks > 0);
-      }
-      umma::mma_commit(bar_mma);
+      for (int ks = 0; ks < 64 / 16; ++ks)
+        if (umma::elect_one())
+          umma::mma_f16(o_col(par), dp + ((ks * 256) >> 4), d_vn + ((ks * 2 * RSV) >> 4), id_xy, ks > 0);
+      if (umma::elect_one()) umma::mma_commit(bar_mma2);
     }
     const float g = scv[128];
     const float ai = scv[i_row];
-    ok = umma::mbar_wait(bar_mma, 1);
+    ok = umma::mbar_wait(bar_mma2, static_cast<uint32_t>(lc & 1));
     if (!ok) record_error(w.err, 1, kSiteStMma2);
     if (__syncthreads_or(!ok)) break;
     umma::fence_after_sync();

@@ -64,6 +64,17 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool a
          | ((static_cast<uint32_t>(M) >> 4) << 24);  // M / 16
 }
 
+// True on exactly one (the lowest active) lane of the warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r));
+  return r != 0;
+}
+
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                         uint32_t idesc, uint32_t accumulate) {
   asm volatile(
