@@ -145,32 +145,31 @@ __device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* map, i
 // WY kernel
 // ---------------------------------------------------------------------------
 
-// Shared memory of the WY kernel.  [K;Q] is one 128-row swizzled operand
-// (64-column atoms of K rows then Q rows, 16 KiB apart) and, with V's atoms
-// at 32 KiB and 48 KiB, [K|V] is one N=256 MN-major operand with a uniform
-// 16 KiB atom stride.  The gaps between V's atoms hold small arrays.
+// Shared memory of the WY kernel (about 74 KB, so 3 CTAs fit per SM).  The
+// first 32 KiB hold four 64-row swizzled atoms: K(cols 0-63), Q(0-63),
+// K(64-127), Q(64-127).  Read 16 KiB at a time they form the 128-row operand
+// [K;Q]; once [K;Q]K^T is done, V is loaded over the Q atoms, and the atoms
+// read 8 KiB apart form [K_0:64 | V_0:64 | K_64:128 | V_64:128], a valid
+// N=256 MN-major operand (uniform atom stride).
 struct WySmem {
-  static constexpr int kKQ = 0;                  // K a0 | Q a0 | K a1 | Q a1
-  static constexpr int kV = 32768;               // V a0 at +0, V a1 at +16 KiB
-  static constexpr int kZ = kV + kAtom;          // f32 solve scratch (gap after V a0)
-  static constexpr int kVec = kV + 3 * kAtom;    // f32 [6][64] (gap after V a1)
-  static constexpr int kBar = kVec + 6 * 64 * 4; // 3 mbarriers
-  static constexpr int kTmem = kBar + 24;
-  static constexpr int kA = 65536;               // f32 [64][65]; then the [T';T''] image
+  static constexpr int kOps = 0;                      // 4 atoms
+  static constexpr int kA = 4 * kAtom;                // f32 [64][65]; later the [T';T''] image
   static constexpr int kT = kA + 64 * kTrilStride * 4;  // f32 [64][kTS]
-  static constexpr int kBytes = kT + 64 * kTS * 4 + 1024;  // + slack for 1 KiB alignment
-  static_assert(kTrilScratch * 4 <= kAtom, "solve scratch must fit the gap");
+  static constexpr int kZ = kT + 64 * kTS * 4;        // f32 solve scratch
+  static constexpr int kVec = kZ + kTrilScratch * 4;  // gam, beta, rk, rq, cw, cu: f32 [6][64]
+  static constexpr int kBar = kVec + 6 * 64 * 4;      // 3 mbarriers
+  static constexpr int kTmem = kBar + 24;
+  static constexpr int kBytes = kTmem + 8 + 1024;     // + slack for 1 KiB alignment
 };
 
 template <typename T>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, 3)
 tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
              const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
              const __grid_constant__ CUtensorMap tv) {
   extern __shared__ uint8_t sm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* kq = sm + WySmem::kKQ;
-  uint8_t* vbuf = sm + WySmem::kV;
+  uint8_t* ops = sm + WySmem::kOps;
   uint8_t* timg = sm + WySmem::kA;  // [T';T''] 128 x 64 image, written after the solve
   float* Af = reinterpret_cast<float*>(sm + WySmem::kA);
   float* Tf = reinterpret_cast<float*>(sm + WySmem::kT);
@@ -202,16 +201,13 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     umma::mbar_init(bars + 2, 1);
     umma::mbar_fence_init();
     umma::mbar_arrive_expect_tx(bar_kq, 2 * kImg64x128);
-    umma::tma_load_3d(kq, &tk, 0, h, static_cast<int>(s), bar_kq);
-    umma::tma_load_3d(kq + kAtom, &tq, 0, h, static_cast<int>(s), bar_kq);
-    umma::tma_load_3d(kq + 2 * kAtom, &tk, 64, h, static_cast<int>(s), bar_kq);
-    umma::tma_load_3d(kq + 3 * kAtom, &tq, 64, h, static_cast<int>(s), bar_kq);
-    umma::mbar_arrive_expect_tx(bar_v, kImg64x128);
-    umma::tma_load_3d(vbuf, &tv, 0, hv, static_cast<int>(s), bar_v);
-    umma::tma_load_3d(vbuf + 2 * kAtom, &tv, 64, hv, static_cast<int>(s), bar_v);
+    umma::tma_load_3d(ops, &tk, 0, h, static_cast<int>(s), bar_kq);
+    umma::tma_load_3d(ops + kAtom, &tq, 0, h, static_cast<int>(s), bar_kq);
+    umma::tma_load_3d(ops + 2 * kAtom, &tk, 64, h, static_cast<int>(s), bar_kq);
+    umma::tma_load_3d(ops + 3 * kAtom, &tq, 64, h, static_cast<int>(s), bar_kq);
   }
   if (warp == 0) {
-    umma::tmem_alloc(tslot, 256);
+    umma::tmem_alloc(tslot, 128);
     umma::fence_before_sync();
   }
   if (warp == 1) {  // chunk-local inclusive cumsum of g over 64 rows
@@ -238,16 +234,16 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   bool ok = umma::mbar_wait(bar_kq, 0);
   if (!ok) record_error(w.err, 1, kSiteWyLoad);
   if (__syncthreads_or(!ok)) goto teardown;
-  if (tid == 0) {  // [S_kk; S_qk] = [K; Q] K^T  (M = 128, N = 64, K = 128)
+  if (warp == 0) {  // [S_kk; S_qk] = [K; Q] K^T  (M = 128, N = 64, K = 128)
     umma::fence_after_sync();
     const uint32_t id = umma::idesc_f16(128, 64, kBf16, false, false);
-    const uint64_t d0 = umma::smem_desc_sw128(umma::smem_u32(kq), 16, 1024);
+    const uint64_t d0 = umma::smem_desc_sw128(umma::smem_u32(ops), 16, 1024);
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
       const uint64_t d = d0 + (((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4);
-      umma::mma_f16(tmem, d, d, id, ks > 0);
+      if (umma::elect_one()) umma::mma_f16(tmem, d, d, id, ks > 0);
     }
-    umma::mma_commit(bar_mma);
+    if (umma::elect_one()) umma::mma_commit(bar_mma);
   }
   {  // L2-norm factors: thread t < 64 -> k row t, t >= 64 -> q row t - 64
     float ss = 0.f;
@@ -255,13 +251,14 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     for (int cch = 0; cch < 16; ++cch) {
       float x[8];
       const uint32_t off = (cch >> 3) * 2 * kAtom + tid * 128 + ((((cch & 7) ^ (tid & 7))) << 4);
-      unpack8<T>(*reinterpret_cast<const uint4*>(kq + off), x);
+      unpack8<T>(*reinterpret_cast<const uint4*>(ops + off), x);
 #pragma unroll
       for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
     }
     const float r = p.use_qk_l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
     if (tid < 64) rk[tid] = r; else rq[tid - 64] = r;
   }
+  umma::fence_proxy_async();
   __syncthreads();
   if (tid < 64) {
     cw[tid] = bet[tid] * exp2f(gam[tid]) * rk[tid];
@@ -271,6 +268,11 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   if (!ok) record_error(w.err, 1, kSiteWyMma1);
   if (__syncthreads_or(!ok)) goto teardown;
   umma::fence_after_sync();
+  if (warp == 3 && umma::elect_one()) {  // Q is dead: bring V into its atoms
+    umma::mbar_arrive_expect_tx(bar_v, kImg64x128);
+    umma::tma_load_3d(ops + kAtom, &tv, 0, hv, static_cast<int>(s), bar_v);
+    umma::tma_load_3d(ops + 3 * kAtom, &tv, 64, hv, static_cast<int>(s), bar_v);
+  }
 
   {  // row tid of [S_kk; S_qk]: A row (fp32, shared) or P row (bf16 image, global)
     const bool is_p = tid >= 64;
@@ -280,17 +282,22 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     uint8_t* pimg = w.pimg + (static_cast<int64_t>(hv) * w.ncu + c) * kImg64x64;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-      float sv[32];
-      umma::tmem_ld32(tmem + lane_base + half * 32, sv);
       float pv[32];
+      if (half == 1 && (warp & 1) == 0) {  // rows 0..31: columns 32..63 are all masked
 #pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        const int j = half * 32 + j4 * 4;
-        const float4 gj = ld4(gam + j), rj = ld4(rk + j);
-        pv[j4 * 4 + 0] = j + 0 <= jmax ? exp2f(gi - gj.x) * ri * rj.x * sv[j4 * 4 + 0] : 0.f;
-        pv[j4 * 4 + 1] = j + 1 <= jmax ? exp2f(gi - gj.y) * ri * rj.y * sv[j4 * 4 + 1] : 0.f;
-        pv[j4 * 4 + 2] = j + 2 <= jmax ? exp2f(gi - gj.z) * ri * rj.z * sv[j4 * 4 + 2] : 0.f;
-        pv[j4 * 4 + 3] = j + 3 <= jmax ? exp2f(gi - gj.w) * ri * rj.w * sv[j4 * 4 + 3] : 0.f;
+        for (int jj = 0; jj < 32; ++jj) pv[jj] = 0.f;
+      } else {
+        float sv[32];
+        umma::tmem_ld32(tmem + lane_base + half * 32, sv);
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const int j = half * 32 + j4 * 4;
+          const float4 gj = ld4(gam + j), rj = ld4(rk + j);
+          pv[j4 * 4 + 0] = j + 0 <= jmax ? exp2f(gi - gj.x) * ri * rj.x * sv[j4 * 4 + 0] : 0.f;
+          pv[j4 * 4 + 1] = j + 1 <= jmax ? exp2f(gi - gj.y) * ri * rj.y * sv[j4 * 4 + 1] : 0.f;
+          pv[j4 * 4 + 2] = j + 2 <= jmax ? exp2f(gi - gj.z) * ri * rj.z * sv[j4 * 4 + 2] : 0.f;
+          pv[j4 * 4 + 3] = j + 3 <= jmax ? exp2f(gi - gj.w) * ri * rj.w * sv[j4 * 4 + 3] : 0.f;
+        }
       }
       if (is_p) {
 #pragma unroll
@@ -317,21 +324,6 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
       *reinterpret_cast<uint4*>(timg + umma::img_off(tid, q8 * 8, RS64)) = pack8<T>(x);
     }
   }
-  umma::fence_proxy_async();
-  __syncthreads();
-  ok = umma::mbar_wait(bar_v, 0);
-  if (!ok) record_error(w.err, 1, kSiteWyLoad);
-  if (__syncthreads_or(!ok)) goto teardown;
-  if (tid == 0) {  // [T' K | . ; . | T'' V] = [T'; T''] [K | V]  (M = 128, N = 256, K = 64)
-    umma::fence_after_sync();
-    const uint32_t id = umma::idesc_f16(128, 256, kBf16, false, true);
-    const uint64_t da = umma::smem_desc(umma::smem_u32(timg), 128, RS64);
-    const uint64_t db = umma::smem_desc_sw128(umma::smem_u32(kq), 2 * kAtom, 1024);
-#pragma unroll
-    for (int ks = 0; ks < 64 / 16; ++ks)
-      umma::mma_f16(tmem, da + ((ks * 256) >> 4), db + ((ks * 2048) >> 4), id, ks > 0);
-    umma::mma_commit(bar_mma);
-  }
   if (tid < 64) {
     float* sc = w.scal + (static_cast<int64_t>(hv) * w.ncu + c) * kScal;
     const float glast = gam[L - 1];
@@ -339,40 +331,64 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     sc[64 + tid] = tid < L ? exp2f(glast - gam[tid]) * rk[tid] : 0.f;
     if (tid < 4) sc[128 + tid] = tid == 0 ? exp2f(glast) : 0.f;
   }
-  ok = umma::mbar_wait(bar_mma, 1);
-  if (!ok) record_error(w.err, 1, kSiteWyMma2);
+  umma::fence_proxy_async();
+  __syncthreads();
+  ok = umma::mbar_wait(bar_v, 0);
+  if (!ok) record_error(w.err, 1, kSiteWyLoad);
   if (__syncthreads_or(!ok)) goto teardown;
-  umma::fence_after_sync();
 
-  {  // row tid < 64: W row (swizzled image); tid >= 64: U row (V-slices)
-    const int i = tid & 63;
-    const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c;
-    const uint32_t col0 = tid < 64 ? 0 : 128;
-    uint8_t* wdst = w.wimg + hc * kImg64x128;
-    T* ubase = reinterpret_cast<T*>(w.u) + hc * 64 * D;
+  // [T'; T''] [K_half | V_half] for column halves 0..63 and 64..127 (M = 128,
+  // N = 128, K = 64): rows 0..63 of columns 0..63 are W, rows 64..127 of
+  // columns 64..127 are U.
+#pragma unroll 1
+  for (int part = 0; part < 2; ++part) {
+    if (warp == 0) {
+      umma::fence_after_sync();
+      const uint32_t id = umma::idesc_f16(128, 128, kBf16, false, true);
+      const uint64_t da = umma::smem_desc(umma::smem_u32(timg), 128, RS64);
+      const uint64_t db = umma::smem_desc_sw128(umma::smem_u32(ops + part * 2 * kAtom), kAtom, 1024);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float x[32];
-      umma::tmem_ld32(tmem + lane_base + col0 + q * 32, x);
+      for (int ks = 0; ks < 64 / 16; ++ks)
+        if (umma::elect_one())
+          umma::mma_f16(tmem, da + ((ks * 256) >> 4), db + ((ks * 2048) >> 4), id, ks > 0);
+      if (umma::elect_one()) umma::mma_commit(bar_mma);
+    }
+    ok = umma::mbar_wait(bar_mma, static_cast<uint32_t>((part + 1) & 1));
+    if (!ok) record_error(w.err, 1, kSiteWyMma2);
+    if (__syncthreads_or(!ok)) goto teardown;
+    umma::fence_after_sync();
+    {  // row tid < 64: W row (swizzled image); tid >= 64: U row (V-slices)
+      const int i = tid & 63;
+      const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c;
+      const uint32_t col0 = tid < 64 ? 0 : 64;
+      uint8_t* wdst = w.wimg + hc * kImg64x128;
+      T* ubase = reinterpret_cast<T*>(w.u) + hc * 64 * D;
 #pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) {
-        const int col = q * 32 + q8 * 8;
-        if (tid < 64) {
-          const uint32_t off = (col >> 6) * kAtom + i * 128 + ((((col & 63) >> 3) ^ (i & 7)) << 4);
-          *reinterpret_cast<uint4*>(wdst + off) = pack8<T>(x + q8 * 8);
-        } else {
-          const int sl = col / w.vs, wc = col % w.vs;
-          *reinterpret_cast<uint4*>(ubase + (static_cast<int64_t>(sl) * 64 + i) * w.vs + wc) =
-              pack8<T>(x + q8 * 8);
+      for (int q = 0; q < 2; ++q) {
+        float x[32];
+        umma::tmem_ld32(tmem + lane_base + col0 + q * 32, x);
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int col = part * 64 + q * 32 + q8 * 8;
+          if (tid < 64) {
+            const uint32_t off = (col >> 6) * kAtom + i * 128 + ((((col & 63) >> 3) ^ (i & 7)) << 4);
+            *reinterpret_cast<uint4*>(wdst + off) = pack8<T>(x + q8 * 8);
+          } else {
+            const int sl = col / w.vs, wc = col % w.vs;
+            *reinterpret_cast<uint4*>(ubase + (static_cast<int64_t>(sl) * 64 + i) * w.vs + wc) =
+                pack8<T>(x + q8 * 8);
+          }
         }
       }
     }
+    umma::fence_before_sync();
+    __syncthreads();
   }
 
 teardown:
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tmem, 256);
+  if (warp == 0) umma::tmem_dealloc(tmem, 128);
 }
 
 // ---------------------------------------------------------------------------
