@@ -156,8 +156,8 @@ struct WySmem {
   static constexpr int kA = 4 * kAtom;                // f32 [64][65]; later the [T';T''] image
   static constexpr int kT = kA + 64 * kTrilStride * 4;  // f32 [64][kTS]
   static constexpr int kZ = kT + 64 * kTS * 4;        // f32 solve scratch
-  static constexpr int kVec = kZ + kTrilScratch * 4;  // gam, beta, rk, rq, cw, cu: f32 [6][64]
-  static constexpr int kBar = kVec + 6 * 64 * 4;      // 3 mbarriers
+  static constexpr int kVec = kZ + kTrilScratch * 4;  // gam, beta, rk, rq, cw, cu, cf: f32 [7][64]
+  static constexpr int kBar = kVec + 7 * 64 * 4;      // 3 mbarriers
   static constexpr int kTmem = kBar + 24;
   static constexpr int kBytes = kTmem + 8 + 1024;     // + slack for 1 KiB alignment
 };
@@ -180,6 +180,7 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   float* rq = rk + 64;
   float* cw = rq + 64;
   float* cu = cw + 64;
+  float* cf = cu + 64;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + WySmem::kBar);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + WySmem::kTmem);
   const uint32_t bar_kq = umma::smem_u32(bars), bar_v = umma::smem_u32(bars + 1),
@@ -263,6 +264,7 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   if (tid < 64) {
     cw[tid] = bet[tid] * exp2f(gam[tid]) * rk[tid];
     cu[tid] = bet[tid];
+    cf[tid] = rk[tid] * exp2f(0.5f * (gam[0] + gam[L - 1]) - gam[tid]);
   }
   ok = umma::mbar_wait(bar_mma, 0);
   if (!ok) record_error(w.err, 1, kSiteWyMma1);
@@ -277,8 +279,14 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   {  // row tid of [S_kk; S_qk]: A row (fp32, shared) or P row (bf16 image, global)
     const bool is_p = tid >= 64;
     const int i = tid & 63;
-    const float gi = gam[i], ri = is_p ? rq[i] : rk[i] * bet[i];
     const int jmax = i < L ? (is_p ? i : i - 1) : -1;  // last nonzero column
+    // exp2(gam_i - gam_j) = exp2(gam_i - mid) * exp2(mid - gam_j) when the
+    // chunk's decay range keeps both factors far inside fp32 (gam is
+    // non-increasing along the chunk); otherwise one exp2 per element.
+    const float mid = 0.5f * (gam[0] + gam[L - 1]);
+    const bool factored = gam[0] - gam[L - 1] < 200.f;
+    const float ri = (is_p ? rq[i] : rk[i] * bet[i]) * (factored ? exp2f(gam[i] - mid) : 1.f);
+    const float gi = gam[i];
     uint8_t* pimg = w.pimg + (static_cast<int64_t>(hv) * w.ncu + c) * kImg64x64;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
@@ -289,14 +297,26 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
       } else {
         float sv[32];
         umma::tmem_ld32(tmem + lane_base + half * 32, sv);
+        if (factored) {
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          const int j = half * 32 + j4 * 4;
-          const float4 gj = ld4(gam + j), rj = ld4(rk + j);
-          pv[j4 * 4 + 0] = j + 0 <= jmax ? exp2f(gi - gj.x) * ri * rj.x * sv[j4 * 4 + 0] : 0.f;
-          pv[j4 * 4 + 1] = j + 1 <= jmax ? exp2f(gi - gj.y) * ri * rj.y * sv[j4 * 4 + 1] : 0.f;
-          pv[j4 * 4 + 2] = j + 2 <= jmax ? exp2f(gi - gj.z) * ri * rj.z * sv[j4 * 4 + 2] : 0.f;
-          pv[j4 * 4 + 3] = j + 3 <= jmax ? exp2f(gi - gj.w) * ri * rj.w * sv[j4 * 4 + 3] : 0.f;
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const int j = half * 32 + j4 * 4;
+            const float4 cj = ld4(cf + j);
+            pv[j4 * 4 + 0] = j + 0 <= jmax ? ri * cj.x * sv[j4 * 4 + 0] : 0.f;
+            pv[j4 * 4 + 1] = j + 1 <= jmax ? ri * cj.y * sv[j4 * 4 + 1] : 0.f;
+            pv[j4 * 4 + 2] = j + 2 <= jmax ? ri * cj.z * sv[j4 * 4 + 2] : 0.f;
+            pv[j4 * 4 + 3] = j + 3 <= jmax ? ri * cj.w * sv[j4 * 4 + 3] : 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const int j = half * 32 + j4 * 4;
+            const float4 gj = ld4(gam + j), rj = ld4(rk + j);
+            pv[j4 * 4 + 0] = j + 0 <= jmax ? exp2f(gi - gj.x) * ri * rj.x * sv[j4 * 4 + 0] : 0.f;
+            pv[j4 * 4 + 1] = j + 1 <= jmax ? exp2f(gi - gj.y) * ri * rj.y * sv[j4 * 4 + 1] : 0.f;
+            pv[j4 * 4 + 2] = j + 2 <= jmax ? exp2f(gi - gj.z) * ri * rj.z * sv[j4 * 4 + 2] : 0.f;
+            pv[j4 * 4 + 3] = j + 3 <= jmax ? exp2f(gi - gj.w) * ri * rj.w * sv[j4 * 4 + 3] : 0.f;
+          }
         }
       }
       if (is_p) {
