@@ -235,9 +235,9 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   bool ok = umma::mbar_wait(bar_kq, 0);
   if (!ok) record_error(w.err, 1, kSiteWyLoad);
   if (__syncthreads_or(!ok)) goto teardown;
-  if (warp == 0) {  // [S_kk; S_qk] = [K; Q] K^T  (M = 128, N = 64, K = 128)
+  if (warp == 0) {  // [K; Q] [K; Q]^T  (M = 128, N = 128, K = 128): S_kk, S_qk and both Gram diagonals
     umma::fence_after_sync();
-    const uint32_t id = umma::idesc_f16(128, 64, kBf16, false, false);
+    const uint32_t id = umma::idesc_f16(128, 128, kBf16, false, false);
     const uint64_t d0 = umma::smem_desc_sw128(umma::smem_u32(ops), 16, 1024);
 #pragma unroll
     for (int ks = 0; ks < D / 16; ++ks) {
@@ -246,30 +246,27 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     }
     if (umma::elect_one()) umma::mma_commit(bar_mma);
   }
-  {  // L2-norm factors: thread t < 64 -> k row t, t >= 64 -> q row t - 64
-    float ss = 0.f;
+  ok = umma::mbar_wait(bar_mma, 0);
+  if (!ok) record_error(w.err, 1, kSiteWyMma1);
+  if (__syncthreads_or(!ok)) goto teardown;
+  umma::fence_after_sync();
+  {  // L2-norm factors from the Gram diagonal: row tid's |k|^2 or |q|^2 sits in column tid
+    float x[32];
+    umma::tmem_ld32(tmem + lane_base + warp * 32, x);
+    float d = 0.f;
 #pragma unroll
-    for (int cch = 0; cch < 16; ++cch) {
-      float x[8];
-      const uint32_t off = (cch >> 3) * 2 * kAtom + tid * 128 + ((((cch & 7) ^ (tid & 7))) << 4);
-      unpack8<T>(*reinterpret_cast<const uint4*>(ops + off), x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
-    }
-    const float r = p.use_qk_l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
+    for (int jj = 0; jj < 32; ++jj) d = jj == lane ? x[jj] : d;
+    const float r = p.use_qk_l2norm ? rsqrtf(d + 1e-6f) : 1.f;
     if (tid < 64) rk[tid] = r; else rq[tid - 64] = r;
   }
-  umma::fence_proxy_async();
   __syncthreads();
   if (tid < 64) {
     cw[tid] = bet[tid] * exp2f(gam[tid]) * rk[tid];
     cu[tid] = bet[tid];
     cf[tid] = rk[tid] * exp2f(0.5f * (gam[0] + gam[L - 1]) - gam[tid]);
   }
-  ok = umma::mbar_wait(bar_mma, 0);
-  if (!ok) record_error(w.err, 1, kSiteWyMma1);
-  if (__syncthreads_or(!ok)) goto teardown;
-  umma::fence_after_sync();
+  umma::fence_proxy_async();
+  __syncthreads();
   if (warp == 3 && umma::elect_one()) {  // Q is dead: bring V into its atoms
     umma::mbar_arrive_expect_tx(bar_v, kImg64x128);
     umma::tma_load_3d(ops + kAtom, &tv, 0, hv, static_cast<int>(s), bar_v);
