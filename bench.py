@@ -246,22 +246,28 @@ def run_ours(a):
     cfg = dict(CFG1)
     if a.tokens:
         cfg["T"] = a.tokens
-    B, T, H, HV, K, V = (cfg[x] for x in ("B", "T", "H", "HV", "K", "V"))
+    H, HV, K, V = (cfg[x] for x in ("H", "HV", "K", "V"))
+    wl = _workload(a.workload, world, rank, cfg)
+    B, T, cu_list, nseq_total, tokens_total = wl["B"], wl["T"], wl["cu"], wl["nseq"], wl["tokens"]
+    N = B if cu_list is None else len(cu_list) - 1
 
-    cpu = CpuBaseline(cfg) if (rank == 0 and world == 1 and not a.no_cpu) else None
+    cpu = (CpuBaseline(cfg) if (rank == 0 and world == 1 and not a.no_cpu and a.workload == "cfg1")
+           else None)
 
-    gen = torch.Generator().manual_seed(1 + rank)
+    gen = torch.Generator().manual_seed(wl["seed"] + rank)
     q_h = torch.randn(B, T, H, K, generator=gen).bfloat16().pin_memory()
     k_h = torch.randn(B, T, H, K, generator=gen).bfloat16().pin_memory()
     v_h = torch.randn(B, T, HV, V, generator=gen).bfloat16().pin_memory()
     g_h = torch.nn.functional.logsigmoid(torch.randn(B, T, HV, generator=gen)).pin_memory()
     b_h = torch.sigmoid(torch.randn(B, T, HV, generator=gen)).pin_memory()
+    h0 = (torch.randn(N, HV, K, V, generator=gen) * 0.02).to(dev) if wl["h0"] else None
+    cu = None if cu_list is None else torch.tensor(cu_list, dtype=torch.int64, device=dev)
     q, k, v, g, beta = (x.to(dev) for x in (q_h, k_h, v_h, g_h, b_h))
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     lib = _lib.load()
 
     def step():
-        return ops.chunk_gated_delta_rule(q, k, v, g, beta, None, None, True,
+        return ops.chunk_gated_delta_rule(q, k, v, g, beta, None, h0, True, cu,
                                           use_qk_l2norm_in_kernel=True)
 
     for _ in range(a.warmup):
@@ -306,7 +312,7 @@ def run_ours(a):
     reps = max(3, min(a.steps, 10))
     for _ in range(reps):
         flush.zero_()
-        o, ht, info = _chunk_with_events(ops, q, k, v, g, beta, handles, nst)
+        o, ht, info = _chunk_with_events(ops, q, k, v, g, beta, handles, nst, cu, h0)
         torch.cuda.synchronize()
         names = info["stages"]
         for i, nm in enumerate(names):
@@ -317,23 +323,25 @@ def run_ours(a):
     e2e_ms, h2d, d2h = None, 0, 0
     if not a.no_e2e:
         o_h = torch.empty(B, T, HV, V, dtype=torch.bfloat16).pin_memory()
-        ht_h = torch.empty(B, HV, K, V, dtype=torch.float32).pin_memory()
+        ht_h = torch.empty(N, HV, K, V, dtype=torch.float32).pin_memory()
         e2e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(a.steps)]
+        extra_h = [] if h0 is None else [h0.cpu().pin_memory(), cu.cpu().pin_memory()]
         _barrier(world)
         torch.cuda.synchronize()
         for i in range(a.steps):
             flush.zero_()
             e2e_evs[i][0].record(stream)
             qd, kd, vd, gd, bd = (x.to(dev, non_blocking=True) for x in (q_h, k_h, v_h, g_h, b_h))
-            o, ht = ops.chunk_gated_delta_rule(qd, kd, vd, gd, bd, None, None, True,
+            h0d, cud = (x.to(dev, non_blocking=True) for x in extra_h) if extra_h else (None, cu)
+            o, ht = ops.chunk_gated_delta_rule(qd, kd, vd, gd, bd, None, h0d, True, cud,
                                                use_qk_l2norm_in_kernel=True)
             o_h.copy_(o, non_blocking=True)
             ht_h.copy_(ht, non_blocking=True)
             e2e_evs[i][1].record(stream)
         torch.cuda.synchronize()
         e2e_ms = _max_over_ranks(sum(s.elapsed_time(e) for s, e in e2e_evs) / a.steps, world)
-        h2d = sum(x.numel() * x.element_size() for x in (q_h, k_h, v_h, g_h, b_h))
+        h2d = sum(x.numel() * x.element_size() for x in [q_h, k_h, v_h, g_h, b_h] + extra_h)
         d2h = o_h.numel() * o_h.element_size() + ht_h.numel() * ht_h.element_size()
 
     # ---- decode (config 3) ----
@@ -356,29 +364,28 @@ def run_ours(a):
                               f"host {_cpu_model()}"}
 
     if rank == 0:
-        tokens = world * B * T
+        tokens = tokens_total if wl["scaling"] == "strong" else world * B * T
         value = tokens / (ms / 1e3)
         fl_tok = flops_per_token_head(K, V)
-        total_flops = B * T * HV * fl_tok
+        total_flops = B * T * HV * fl_tok  # this rank's share (rank 0)
         sfl = stage_flops_per_token_head(K, V, path="tc" if "plan" in stage_avg and len(stage_avg) == 3 else "generic")
         dom = max(stage_avg, key=stage_avg.get)
         dom_key = dom.split(":")[0]
         dom_flops = B * T * HV * sfl.get(dom_key, 0)
-        traffic = _load_traffic().get(dom)
+        traffic = _load_traffic().get(dom) if a.workload == "cfg1" and not a.tokens else None
         roof = {"kernel": dom, "bound": "tensor", "achieved": dom_flops / (stage_avg[dom] * 1e-3) / 1e12,
                 "peak": tc_burst, "unit": "TFLOP/s", "peak_kind": f"{peak_kind} bf16 burst",
                 "traffic": traffic}
         roof["frac"] = roof["achieved"] / roof["peak"]
-        pbytes = prefill_bytes(B * T, H, HV, K, V, B)
+        pbytes = prefill_bytes(B * T, H, HV, K, V, N)
         line = {
-            "metric": "prefill tokens/s (Qwen3-Next GDN layer chunked prefill, BASELINE config 1)",
+            "metric": wl["metric"],
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": wl["scaling"],
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q/k/v, "
-            "logsigmoid/sigmoid gates; BASELINE config 1 distributions)",
-            "config": {"workload": "config1: chunk_gated_delta_rule B=1 T=8192 H=16 HV=32 K=V=128 "
-                       "bf16, in-kernel q/k L2 norm, fp32 final state", "tokens_per_gpu": B * T,
-                       "parallelism": f"sequence-sharded x{world} (one sequence per rank)",
+            "logsigmoid/sigmoid gates; BASELINE config distributions)",
+            "config": {"workload": wl["desc"], "tokens_per_gpu": B * T,
+                       "parallelism": wl["par"],
                        "l2": "256 MiB buffer written between timed steps"},
             "roofline": roof,
             "path_roofline": {"flops": total_flops, "tflops": total_flops / (ms * 1e-3) / 1e12,
@@ -400,7 +407,46 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
-def _chunk_with_events(ops, q, k, v, g, beta, handles, nst):
+def _workload(name, world, rank, cfg):
+    """Per-rank shape of a BASELINE prefill config.
+
+    cfg1: one B=1, T=8192 sequence per rank (weak scaling).
+    cfg2: 16 sequences, lengths U[512, 8192] (seed 2), packed with cu_seqlens,
+          initial states N(0, 0.02); sequences split across ranks by token
+          count (strong scaling).
+    cfg4: 64 sequences x 4096 tokens split evenly across ranks (strong scaling).
+    """
+    from domesticated_torch_mlu_ops_b200 import shard
+    if name == "cfg1":
+        return dict(B=1, T=cfg["T"], cu=None, nseq=world, tokens=world * cfg["T"], seed=1, h0=False,
+                    scaling="weak", par=f"sequence-sharded x{world} (one sequence per rank)",
+                    metric="prefill tokens/s (Qwen3-Next GDN layer chunked prefill, BASELINE config 1)",
+                    desc=f"config1: chunk_gated_delta_rule B=1 T={cfg['T']} H=16 HV=32 K=V=128 bf16, "
+                         "in-kernel q/k L2 norm, fp32 final state")
+    if name == "cfg4":
+        if 64 % world:
+            raise SystemExit("cfg4 needs the GPU count to divide 64")
+        b = 64 // world
+        return dict(B=b, T=4096, cu=None, nseq=64, tokens=64 * 4096, seed=4, h0=False,
+                    scaling="strong", par=f"sequence-sharded x{world} ({b} sequences per rank)",
+                    metric="prefill tokens/s (GDN box-scale sharded prefill, BASELINE config 4)",
+                    desc="config4: 64 x 4096 tokens, H=16 HV=32 K=V=128 bf16, in-kernel q/k L2 norm")
+    if name == "cfg2":
+        import numpy as np
+        lens = np.random.default_rng(2).integers(512, 8193, size=16).tolist()
+        mine = shard.partition_sequences(lens, world)[rank]
+        cu = [0]
+        for i in mine:
+            cu.append(cu[-1] + lens[i])
+        return dict(B=1, T=cu[-1], cu=cu, nseq=16, tokens=int(sum(lens)), seed=2, h0=True,
+                    scaling="strong", par=f"sequences bin-packed over {world} ranks",
+                    metric="prefill tokens/s (GDN varlen packed prefill, BASELINE config 2)",
+                    desc=f"config2: 16 sequences U[512,8192] ({sum(lens)} tokens) packed via cu_seqlens, "
+                         "h0 N(0,0.02), H=16 HV=32 K=V=128 bf16")
+    raise SystemExit(f"unknown workload {name}")
+
+
+def _chunk_with_events(ops, q, k, v, g, beta, handles, nst, cu=None, h0=None):
     """One chunk_gated_delta_rule call with the library's stage events set."""
     import ctypes
 
@@ -409,12 +455,13 @@ def _chunk_with_events(ops, q, k, v, g, beta, handles, nst):
     from domesticated_torch_mlu_ops_b200 import _lib, gdn
     B, T, H, K = k.shape
     HV, V = v.shape[2], v.shape[3]
+    N = B if cu is None else cu.numel() - 1
     o = torch.empty_like(v)
-    ht = torch.empty(B, HV, K, V, dtype=torch.float32, device=q.device)
+    ht = torch.empty(N, HV, K, V, dtype=torch.float32, device=q.device)
     args = _lib.ChunkArgs(
         q=gdn._ptr(q), k=gdn._ptr(k), v=gdn._ptr(v), g=gdn._ptr(g), beta=gdn._ptr(beta),
-        initial_state=None, o=gdn._ptr(o), final_state=gdn._ptr(ht), cu_seqlens=None,
-        B=B, T=T, N=B, H=H, HV=HV, K=K, V=V, qkv_dtype=_lib.GDN_BF16, cu_dtype=_lib.GDN_I64,
+        initial_state=gdn._ptr(h0), o=gdn._ptr(o), final_state=gdn._ptr(ht), cu_seqlens=gdn._ptr(cu),
+        B=B, T=T, N=N, H=H, HV=HV, K=K, V=V, qkv_dtype=_lib.GDN_BF16, cu_dtype=_lib.GDN_I64,
         scale=0.0, use_qk_l2norm=1, state_v_first=0, force_generic=0,
         stage_events=ctypes.cast(handles, ctypes.POINTER(ctypes.c_void_p)), n_stage_events=nst)
     lib = _lib.load()
@@ -518,6 +565,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=0,
                     help="override config 1's T (small cases for ncu captures; not a bench line)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg4"],
+                    help="BASELINE prefill config (default cfg1, the headline)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     if a.impl == "reference":
