@@ -149,7 +149,7 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
     A[i * 65 + j] = a;
   }
   __syncthreads();
-  solve_tril64(A, Tm, Zs);  // (I + A)^-1; ends with a barrier
+  solve_tril64_nt<256>(A, Tm, Zs);  // (I + A)^-1; ends with a barrier
   for (int e = tid; e < L * K; e += blockDim.x) {
     const int i = e / K, kk = e % K;
     float acc = 0.f;

@@ -64,7 +64,7 @@ struct Work {
   const int64_t* coff;  // [N+1] chunk offsets
   int* err;             // device error word
   uint8_t* wimg;        // [HV][NCU][16 KiB]
-  uint8_t* u;           // [HV][NCU][128/VS][64][VS] elements of the q/k/v type
+  uint8_t* u;           // [HV][NCU][128/S][64][S] (S = min(vs, 64), rows swizzled; u_off)
   uint8_t* pimg;        // [HV][NCU][8 KiB]
   float* scal;          // [HV][NCU][kScal]: a[64], b[64], gamma, pad
   int64_t ncu;          // chunk capacity
@@ -150,20 +150,35 @@ __device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* map, i
 // K(64-127), Q(64-127).  Read 16 KiB at a time they form the 128-row operand
 // [K;Q]; once [K;Q]K^T is done, V is loaded over the Q atoms, and the atoms
 // read 8 KiB apart form [K_0:64 | V_0:64 | K_64:128 | V_64:128], a valid
-// N=256 MN-major operand (uniform atom stride).
+// N=256 MN-major operand (uniform atom stride).  W and U leave through
+// shared-memory staging and bulk stores: columns 0-63 staged over T, columns
+// 64-127 over the operand atoms once the last MMA has read them.
 struct WySmem {
-  static constexpr int kOps = 0;                      // 4 atoms
-  static constexpr int kA = 4 * kAtom;                // f32 [64][65]; later the [T';T''] image
-  static constexpr int kT = kA + 64 * kTrilStride * 4;  // f32 [64][kTS]
-  static constexpr int kZ = kT + 64 * kTS * 4;        // f32 solve scratch
-  static constexpr int kVec = kZ + kTrilScratch * 4;  // gam, beta, rk, rq, cw, cu, cf: f32 [7][64]
-  static constexpr int kBar = kVec + 7 * 64 * 4;      // 3 mbarriers
+  static constexpr int kOps = 0;                 // 4 atoms
+  static constexpr int kA = 4 * kAtom;           // f32 [64][kMS]; later the [T';T''] image
+  static constexpr int kT = kA + 64 * kMS * 4;   // f32 [64][kMS]; later W/U staging
+  static constexpr int kZ = kT + 64 * kMS * 4;   // f32 solve scratch
+  static constexpr int kVec = kZ + kMScratch * 4;  // gam, beta, rk, rq, cw, cu, cf: f32 [7][64]
+  static constexpr int kBar = kVec + 7 * 64 * 4;   // 3 mbarriers
   static constexpr int kTmem = kBar + 24;
-  static constexpr int kBytes = kTmem + 8 + 1024;     // + slack for 1 KiB alignment
+  static constexpr int kBytes = kTmem + 8 + 1024;  // + slack for 1 KiB alignment
+  static_assert(kT % 16 == 0 && 64 * kMS * 4 >= 2 * kAtom, "W/U staging must fit over T");
+  static_assert(3 * (kBytes + 1024) <= 228 * 1024, "three CTAs per SM");
 };
+constexpr int kWyThreads = 256;
+
+// Element offset of (row i, column c) in a U tile of S-column slices
+// ([128/S][64][S], S = 32 or 64).  The 16-byte chunks of each row are
+// XOR-swizzled so that eight consecutive rows touch distinct bank groups.
+__device__ __forceinline__ int u_off(int i, int c, int S) {
+  const int C = S >> 3;  // 16-byte chunks per row
+  const int sw = (i / (8 / C)) & (C - 1);
+  const int sl = c / S, wc = c % S;
+  return (sl * 64 + i) * S + ((((wc >> 3) ^ sw)) << 3) + (wc & 7);
+}
 
 template <typename T>
-__global__ void __launch_bounds__(128, 3)
+__global__ void __launch_bounds__(kWyThreads, 3)
 tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
              const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
              const __grid_constant__ CUtensorMap tv) {
@@ -189,12 +204,18 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   int64_t n, lc;
   if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // TMEM lane quadrant (rows quad*32 .. +31 of every M=128 result) and the
+  // 32-column half of the epilogues this warp covers
+  const int quad = warp & 3, colh = warp >> 2;
+  const int row = quad * 32 + lane;  // result row of this thread (0..127)
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
   const int64_t c = blockIdx.x;
+  const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c;
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
   const int64_t s = bos + lc * kChunk;
   const int L = static_cast<int>(min64(kChunk, eos - s));
+  const int us = w.vs < 64 ? w.vs : 64;  // U slice width
 
   if (tid == 0) {
     umma::mbar_init(bars, 1);
@@ -229,10 +250,13 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tslot;
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
   constexpr bool kBf16 = !std::is_same<T, __half>::value;
+  bool issued_store = false;
 
-  bool ok = umma::mbar_wait(bar_kq, 0);
+  // One warp waits on each mbarrier; the block learns the outcome at the
+  // barrier that follows (tcgen05 readers fence after it).
+  bool ok = warp == 0 ? umma::mbar_wait(bar_kq, 0) : true;
   if (!ok) record_error(w.err, 1, kSiteWyLoad);
   if (__syncthreads_or(!ok)) goto teardown;
   if (warp == 0) {  // [K; Q] [K; Q]^T  (M = 128, N = 128, K = 128): S_kk, S_qk and both Gram diagonals
@@ -246,18 +270,18 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     }
     if (umma::elect_one()) umma::mma_commit(bar_mma);
   }
-  ok = umma::mbar_wait(bar_mma, 0);
+  ok = warp == 0 ? umma::mbar_wait(bar_mma, 0) : true;
   if (!ok) record_error(w.err, 1, kSiteWyMma1);
   if (__syncthreads_or(!ok)) goto teardown;
   umma::fence_after_sync();
-  {  // L2-norm factors from the Gram diagonal: row tid's |k|^2 or |q|^2 sits in column tid
+  if (colh == 0) {  // L2-norm factors from the Gram diagonal: row r's |k|^2 or |q|^2 sits in column r
     float x[32];
-    umma::tmem_ld32(tmem + lane_base + warp * 32, x);
+    umma::tmem_ld32(tmem + lane_base + quad * 32, x);
     float d = 0.f;
 #pragma unroll
     for (int jj = 0; jj < 32; ++jj) d = jj == lane ? x[jj] : d;
     const float r = p.use_qk_l2norm ? rsqrtf(d + 1e-6f) : 1.f;
-    if (tid < 64) rk[tid] = r; else rq[tid - 64] = r;
+    if (row < 64) rk[row] = r; else rq[row - 64] = r;
   }
   __syncthreads();
   if (tid < 64) {
@@ -273,9 +297,13 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     umma::tma_load_3d(ops + 3 * kAtom, &tv, 64, hv, static_cast<int>(s), bar_v);
   }
 
-  {  // row tid of [S_kk; S_qk]: A row (fp32, shared) or P row (bf16 image, global)
-    const bool is_p = tid >= 64;
-    const int i = tid & 63;
+  // Row `row` of [S_kk; S_qk], columns colh*32 .. +31: an A row (fp32, shared)
+  // or a P row (bf16 image, global).  A rows 0..31 have nothing to the right
+  // of column 31 and the solve never reads there; P rows 0..31 get zeros.
+  // Blocks below the diagonal of a full chunk need no mask.
+  if (!(colh == 1 && quad == 0)) {
+    const bool is_p = row >= 64;
+    const int i = row & 63;
     const int jmax = i < L ? (is_p ? i : i - 1) : -1;  // last nonzero column
     // exp2(gam_i - gam_j) = exp2(gam_i - mid) * exp2(mid - gam_j) when the
     // chunk's decay range keeps both factors far inside fp32 (gam is
@@ -284,65 +312,74 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     const bool factored = gam[0] - gam[L - 1] < 200.f;
     const float ri = (is_p ? rq[i] : rk[i] * bet[i]) * (factored ? exp2f(gam[i] - mid) : 1.f);
     const float gi = gam[i];
-    uint8_t* pimg = w.pimg + (static_cast<int64_t>(hv) * w.ncu + c) * kImg64x64;
+    const bool masked = colh == (quad & 1) || L < kChunk;  // warp-uniform
+    float pv[32];
+    if (colh == 1 && quad == 2) {  // P rows 0..31, columns 32..63: all masked
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      float pv[32];
-      if (half == 1 && (warp & 1) == 0) {  // rows 0..31: columns 32..63 are all masked
+      for (int jj = 0; jj < 32; ++jj) pv[jj] = 0.f;
+    } else {
+      float sv[32];
+      umma::tmem_ld32(tmem + lane_base + colh * 32, sv);
+      if (factored) {
+        const float2 r2 = make_float2(ri, ri);
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) pv[jj] = 0.f;
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const float4 cj = ld4(cf + colh * 32 + j4 * 4);
+          const float2 p0 = __fmul2_rn(r2, __fmul2_rn(make_float2(cj.x, cj.y), make_float2(sv[j4 * 4], sv[j4 * 4 + 1])));
+          const float2 p1 = __fmul2_rn(r2, __fmul2_rn(make_float2(cj.z, cj.w), make_float2(sv[j4 * 4 + 2], sv[j4 * 4 + 3])));
+          pv[j4 * 4 + 0] = p0.x;
+          pv[j4 * 4 + 1] = p0.y;
+          pv[j4 * 4 + 2] = p1.x;
+          pv[j4 * 4 + 3] = p1.y;
+        }
       } else {
-        float sv[32];
-        umma::tmem_ld32(tmem + lane_base + half * 32, sv);
-        if (factored) {
 #pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            const int j = half * 32 + j4 * 4;
-            const float4 cj = ld4(cf + j);
-            pv[j4 * 4 + 0] = j + 0 <= jmax ? ri * cj.x * sv[j4 * 4 + 0] : 0.f;
-            pv[j4 * 4 + 1] = j + 1 <= jmax ? ri * cj.y * sv[j4 * 4 + 1] : 0.f;
-            pv[j4 * 4 + 2] = j + 2 <= jmax ? ri * cj.z * sv[j4 * 4 + 2] : 0.f;
-            pv[j4 * 4 + 3] = j + 3 <= jmax ? ri * cj.w * sv[j4 * 4 + 3] : 0.f;
-          }
-        } else {
-#pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            const int j = half * 32 + j4 * 4;
-            const float4 gj = ld4(gam + j), rj = ld4(rk + j);
-            pv[j4 * 4 + 0] = j + 0 <= jmax ? exp2f(gi - gj.x) * ri * rj.x * sv[j4 * 4 + 0] : 0.f;
-            pv[j4 * 4 + 1] = j + 1 <= jmax ? exp2f(gi - gj.y) * ri * rj.y * sv[j4 * 4 + 1] : 0.f;
-            pv[j4 * 4 + 2] = j + 2 <= jmax ? exp2f(gi - gj.z) * ri * rj.z * sv[j4 * 4 + 2] : 0.f;
-            pv[j4 * 4 + 3] = j + 3 <= jmax ? exp2f(gi - gj.w) * ri * rj.w * sv[j4 * 4 + 3] : 0.f;
-          }
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const int j = colh * 32 + j4 * 4;
+          const float4 gj = ld4(gam + j), rj = ld4(rk + j);
+          pv[j4 * 4 + 0] = exp2f(gi - gj.x) * ri * rj.x * sv[j4 * 4 + 0];
+          pv[j4 * 4 + 1] = exp2f(gi - gj.y) * ri * rj.y * sv[j4 * 4 + 1];
+          pv[j4 * 4 + 2] = exp2f(gi - gj.z) * ri * rj.z * sv[j4 * 4 + 2];
+          pv[j4 * 4 + 3] = exp2f(gi - gj.w) * ri * rj.w * sv[j4 * 4 + 3];
         }
       }
-      if (is_p) {
+      if (masked) {
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8)
-          *reinterpret_cast<uint4*>(pimg + umma::img_off(i, half * 32 + q8 * 8, RS64)) =
-              pack8<T>(pv + q8 * 8);
-      } else {
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) Af[i * kTrilStride + half * 32 + jj] = pv[jj];
+        for (int jj = 0; jj < 32; ++jj) pv[jj] = colh * 32 + jj <= jmax ? pv[jj] : 0.f;
       }
+    }
+    if (is_p) {
+      uint8_t* pimg = w.pimg + hc * kImg64x64;
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8)
+        *reinterpret_cast<uint4*>(pimg + umma::img_off(i, colh * 32 + q8 * 8, RS64)) = pack8<T>(pv + q8 * 8);
+    } else {
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4)
+        st4(Af + i * kMS + colh * 32 + j4 * 4, make_float4(pv[j4 * 4], pv[j4 * 4 + 1], pv[j4 * 4 + 2], pv[j4 * 4 + 3]));
     }
   }
   umma::fence_before_sync();
   __syncthreads();
-  solve_tril64(Af, Tf, Zs);  // T = (I + A)^-1, ends with a barrier
-  {  // [T'; T''] image (A is dead): row tid < 64 -> T diag(cw), else T diag(beta)
-    const int i = tid & 63;
-    const float* coef = tid < 64 ? cw : cu;
+  solve_tril64_mma(Af, Tf, Zs);  // T = (I + A)^-1, ends with a barrier
+  {  // [T'; T''] image (A is dead): row r < 64 -> T diag(cw), else T diag(beta); 32 columns per thread
+    const int r = tid & 127, i = r & 63, half = tid >> 7;
+    const float* coef = r < 64 ? cw : cu;
 #pragma unroll
-    for (int q8 = 0; q8 < 8; ++q8) {
-      float x[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = Tf[i * kTS + q8 * 8 + e] * coef[q8 * 8 + e];
-      *reinterpret_cast<uint4*>(timg + umma::img_off(tid, q8 * 8, RS64)) = pack8<T>(x);
+    for (int q8 = 0; q8 < 4; ++q8) {
+      const int col = half * 32 + q8 * 8;
+      const float4 t0 = ld4(Tf + i * kMS + col), t1 = ld4(Tf + i * kMS + col + 4);
+      const float4 c0 = ld4(coef + col), c1 = ld4(coef + col + 4);
+      const float2 x0 = __fmul2_rn(make_float2(t0.x, t0.y), make_float2(c0.x, c0.y));
+      const float2 x1 = __fmul2_rn(make_float2(t0.z, t0.w), make_float2(c0.z, c0.w));
+      const float2 x2 = __fmul2_rn(make_float2(t1.x, t1.y), make_float2(c1.x, c1.y));
+      const float2 x3 = __fmul2_rn(make_float2(t1.z, t1.w), make_float2(c1.z, c1.w));
+      const float x[8] = {x0.x, x0.y, x1.x, x1.y, x2.x, x2.y, x3.x, x3.y};
+      *reinterpret_cast<uint4*>(timg + umma::img_off(r, col, RS64)) = pack8<T>(x);
     }
   }
   if (tid < 64) {
-    float* sc = w.scal + (static_cast<int64_t>(hv) * w.ncu + c) * kScal;
+    float* sc = w.scal + hc * kScal;
     const float glast = gam[L - 1];
     sc[tid] = tid < L ? scale * exp2f(gam[tid]) * rq[tid] : 0.f;
     sc[64 + tid] = tid < L ? exp2f(glast - gam[tid]) * rk[tid] : 0.f;
@@ -350,13 +387,14 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   }
   umma::fence_proxy_async();
   __syncthreads();
-  ok = umma::mbar_wait(bar_v, 0);
+  ok = warp == 0 ? umma::mbar_wait(bar_v, 0) : true;
   if (!ok) record_error(w.err, 1, kSiteWyLoad);
   if (__syncthreads_or(!ok)) goto teardown;
 
   // [T'; T''] [K_half | V_half] for column halves 0..63 and 64..127 (M = 128,
   // N = 128, K = 64): rows 0..63 of columns 0..63 are W, rows 64..127 of
-  // columns 64..127 are U.
+  // columns 64..127 are U.  Each half is staged as one 8 KiB W atom and one
+  // 8 KiB run of U slices, both contiguous in global memory.
 #pragma unroll 1
   for (int part = 0; part < 2; ++part) {
     if (warp == 0) {
@@ -370,39 +408,39 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
           umma::mma_f16(tmem, da + ((ks * 256) >> 4), db + ((ks * 2048) >> 4), id, ks > 0);
       if (umma::elect_one()) umma::mma_commit(bar_mma);
     }
-    ok = umma::mbar_wait(bar_mma, static_cast<uint32_t>((part + 1) & 1));
+    ok = warp == 0 ? umma::mbar_wait(bar_mma, static_cast<uint32_t>((part + 1) & 1)) : true;
     if (!ok) record_error(w.err, 1, kSiteWyMma2);
     if (__syncthreads_or(!ok)) goto teardown;
     umma::fence_after_sync();
-    {  // row tid < 64: W row (swizzled image); tid >= 64: U row (V-slices)
-      const int i = tid & 63;
-      const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c;
-      const uint32_t col0 = tid < 64 ? 0 : 64;
-      uint8_t* wdst = w.wimg + hc * kImg64x128;
-      T* ubase = reinterpret_cast<T*>(w.u) + hc * 64 * D;
+    uint8_t* stage = part == 0 ? sm + WySmem::kT : ops;  // W atom, then the U run
+    {  // row < 64: W row; row >= 64: U row; 32 of the half's 64 columns per thread
+      const int i = row & 63;
+      float x[32];
+      umma::tmem_ld32(tmem + lane_base + (row < 64 ? 0 : 64) + colh * 32, x);
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        float x[32];
-        umma::tmem_ld32(tmem + lane_base + col0 + q * 32, x);
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          const int col = part * 64 + q * 32 + q8 * 8;
-          if (tid < 64) {
-            const uint32_t off = (col >> 6) * kAtom + i * 128 + ((((col & 63) >> 3) ^ (i & 7)) << 4);
-            *reinterpret_cast<uint4*>(wdst + off) = pack8<T>(x + q8 * 8);
-          } else {
-            const int sl = col / w.vs, wc = col % w.vs;
-            *reinterpret_cast<uint4*>(ubase + (static_cast<int64_t>(sl) * 64 + i) * w.vs + wc) =
-                pack8<T>(x + q8 * 8);
-          }
+      for (int q8 = 0; q8 < 4; ++q8) {
+        const int lcol = colh * 32 + q8 * 8;  // column within the half
+        if (row < 64) {
+          *reinterpret_cast<uint4*>(stage + i * 128 + ((((lcol >> 3) ^ (i & 7))) << 4)) = pack8<T>(x + q8 * 8);
+        } else {
+          T* ust = reinterpret_cast<T*>(stage + kAtom);
+          *reinterpret_cast<uint4*>(ust + u_off(i, lcol, us)) = pack8<T>(x + q8 * 8);
         }
       }
     }
+    umma::fence_proxy_async();
     umma::fence_before_sync();
     __syncthreads();
+    if (tid == 0) {
+      umma::bulk_s2g(w.wimg + hc * kImg64x128 + part * kAtom, stage, kAtom);
+      umma::bulk_s2g(w.u + hc * (64 * D * 2) + part * kAtom, stage + kAtom, kAtom);
+      umma::bulk_commit();
+      issued_store = true;
+    }
   }
 
 teardown:
+  if (issued_store) umma::bulk_wait_read_all();  // staging must stay until the copies have read it
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, 128);
@@ -418,7 +456,8 @@ struct StSmem {
   //   [W;Q]  one 128-row swizzled operand: W a0 | Q a0 | W a1 | Q a1
   //   K      swizzled 64-row tile (atoms 8 KiB apart)
   //   [0;P]  128 x 64 no-swizzle image whose top half stays zero
-  //   U slice [64][VS], scalars (a, b, gamma)
+  //   U slice (64 x VS, as [VS/S][64][S] swizzled slices of S = min(VS, 64)),
+  //   scalars (a, b, gamma)
   static constexpr int kUBytes = 64 * VS * 2;
   static constexpr int kWQ = 0;
   static constexpr int kKt = 4 * kAtom;
@@ -591,7 +630,8 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
     const float* scv = reinterpret_cast<const float*>(base + S::kScalOff);
     if (tid < 64) {  // v_new = U - X; images of v_new and diag(b) v_new (row tid)
       const float bi = scv[64 + i_row];
-      const uint8_t* urow = base + S::kU + i_row * VS * 2;
+      const T* ut = reinterpret_cast<const T*>(base + S::kU);
+      constexpr int kUS = VS < 64 ? VS : 64;  // U slice width of the staged layout
 #pragma unroll
       for (int q = 0; q < VS / 32; ++q) {
         float x[32];
@@ -599,7 +639,7 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
           float u8[8], vn[8], vt[8];
-          unpack8<T>(*reinterpret_cast<const uint4*>(urow + (q * 32 + q8 * 8) * 2), u8);
+          unpack8<T>(*reinterpret_cast<const uint4*>(ut + u_off(i_row, q * 32 + q8 * 8, kUS)), u8);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             vn[e] = u8[e] - x[q8 * 8 + e];
@@ -768,7 +808,7 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
         cudaSuccess)
       return e;
     hk.pre(s);
-    wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), 128, WySmem::kBytes, s>>>(a, w, scale, tq, tk, tv);
+    wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem::kBytes, s>>>(a, w, scale, tq, tk, tv);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (w.vs == 32) e = launch_state<T, 32>(a, w, scale, tq, tk, s, hk);
     else if (w.vs == 64) e = launch_state<T, 64>(a, w, scale, tq, tk, s, hk);
