@@ -719,6 +719,297 @@ tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
 }
 
 // ---------------------------------------------------------------------------
+// Warp-specialised state + output kernel (32-column V-slices)
+// ---------------------------------------------------------------------------
+//
+// The recurrence of tc_state_kernel with the work of each chunk spread over
+// nine warps, so that only the dependent chain stays serial:
+//   MMA1  [X; Y] = [W; Q] h                  warp 0 issues (8 tcgen05.mma)
+//   E1    v = U - X, V~ = diag(b) v          warps 0,1,4,5 (rows 0..63)
+//   MMA2  dH = K^T V~ (chain), O = [. ; P] v  warp 0 issues, separate commits
+//   E2    h <- gamma h + dH, image of h      warps 0..7 (rows 0..127)
+// while, off the chain, warps 2,3,6,7 write o = a Y + scale O of the previous
+// chunk during MMA1, and warp 8 waits on the loads and streams chunk c+2 into
+// a three-stage ring.  A tcgen05.mma costs about the same at N = 32 as at
+// N = 64, so the chain is bounded by its twelve MMAs and two epilogues.
+// Rows 0..63 of the O product read the K tile that precedes P in its stage
+// and are never used.
+
+struct St3 {
+  static constexpr int VS = 32;
+  // stage: W a0 | Q a0 | W a1 | Q a1 | K a0 | K a1 | P | U | scalars
+  static constexpr int kWQ = 0;
+  static constexpr int kK = 4 * kAtom;
+  static constexpr int kP = kK + 2 * kAtom;
+  static constexpr int kU = kP + kImg64x64;
+  static constexpr int kUBytes = 64 * VS * 2;
+  static constexpr int kSc = kU + kUBytes;
+  static constexpr int kStage = ((kSc + kScal * 4 + 1023) / 1024) * 1024;
+  static constexpr uint32_t kTx = 4 * kAtom + 2 * kAtom + kImg64x64 + kUBytes + kScal * 4;
+  static constexpr int kStages = 3;
+  static constexpr int kH = kStages * kStage;    // h image 128 x VS
+  static constexpr int kVn = kH + D * VS * 2;    // v image 64 x VS
+  static constexpr int kVt = kVn + 64 * VS * 2;  // diag(b) v image 64 x VS
+  static constexpr int kBar = kVt + 64 * VS * 2; // full[3], mma1, dh, o
+  static constexpr int kTmem = kBar + 6 * 8;
+  static constexpr int kBytes = kTmem + 8 + 1024;
+  // TMEM columns: acc[2], dH, O[2] (VS each)
+  static constexpr int kAcc = 0, kDH = 2 * VS, kO = 3 * VS, kCols = 256;
+  static_assert(kO + 2 * VS <= kCols, "TMEM columns");
+  static_assert(kBytes <= 227 * 1024, "shared memory");
+};
+constexpr int kSt3Threads = 288;  // 8 epilogue warps + 1 load warp
+
+template <typename T>
+__global__ void __launch_bounds__(kSt3Threads, 1)
+tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
+                 const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk) {
+  using S = St3;
+  constexpr int VS = S::VS;
+  constexpr int RSV = (VS / 8) * 128;
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* himg = sm + S::kH;
+  uint8_t* vnimg = sm + S::kVn;
+  uint8_t* vtimg = sm + S::kVt;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBar);  // full[3], mma1, dh, o
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::kTmem);
+  const uint32_t bar_mma1 = umma::smem_u32(bars + 3), bar_dh = umma::smem_u32(bars + 4),
+                 bar_o = umma::smem_u32(bars + 5);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool producer = warp == 8;
+  const int quad = warp & 3, colh = (warp >> 2) & 1;  // TMEM lane quadrant, column half
+  const int row = quad * 32 + lane;
+  const int64_t n = blockIdx.x;
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  const int vsl = blockIdx.z, v0 = vsl * VS;
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int nch = static_cast<int>(eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0);
+  const int64_t c0 = w.coff[n];
+  auto stage = [&](int x) { return sm + (x % S::kStages) * S::kStage; };
+  auto full = [&](int x) { return umma::smem_u32(bars + x % S::kStages); };
+
+  // every operand of chunk x into its stage (one thread)
+  auto fetch = [&](int x) {
+    uint8_t* b = stage(x);
+    const uint32_t bar = full(x);
+    const int s = static_cast<int>(bos + static_cast<int64_t>(x) * kChunk);
+    const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c0 + x;
+    const uint8_t* wsrc = w.wimg + hc * kImg64x128;
+    umma::mbar_arrive_expect_tx(bar, S::kTx);
+    umma::bulk_g2s(b + S::kWQ, wsrc, kAtom, bar);
+    umma::tma_load_3d(b + S::kWQ + kAtom, &tq, 0, h, s, bar);
+    umma::bulk_g2s(b + S::kWQ + 2 * kAtom, wsrc + kAtom, kAtom, bar);
+    umma::tma_load_3d(b + S::kWQ + 3 * kAtom, &tq, 64, h, s, bar);
+    umma::tma_load_3d(b + S::kK, &tk, 0, h, s, bar);
+    umma::tma_load_3d(b + S::kK + kAtom, &tk, 64, h, s, bar);
+    umma::bulk_g2s(b + S::kP, w.pimg + hc * kImg64x64, kImg64x64, bar);
+    umma::bulk_g2s(b + S::kU, w.u + ((hc * (D / VS) + vsl) * 64 * VS) * 2, S::kUBytes, bar);
+    umma::bulk_g2s(b + S::kSc, w.scal + hc * kScal, kScal * 4, bar);
+  };
+
+  if (tid == 256) {
+    for (int i = 0; i < 6; ++i) umma::mbar_init(bars + i, 1);
+    umma::mbar_fence_init();
+    if (nch > 0) fetch(0);
+    if (nch > 1) fetch(1);
+  }
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, S::kCols);
+    umma::fence_before_sync();
+  }
+  // state slice: thread `row` (warps 0..7) owns h[row][v0 + colh*16 .. +16] in fp32
+  float hreg[16];
+  if (!producer) {
+    const int64_t base = (n * p.HV + hv) * D * D;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int col = v0 + colh * 16 + j;
+      hreg[j] = !p.initial_state ? 0.f
+                : p.state_v_first ? p.initial_state[base + static_cast<int64_t>(col) * D + row]
+                                  : p.initial_state[base + static_cast<int64_t>(row) * D + col];
+    }
+#pragma unroll
+    for (int j8 = 0; j8 < 2; ++j8)
+      *reinterpret_cast<uint4*>(himg + umma::img_off(row, colh * 16 + j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
+  }
+  umma::fence_proxy_async();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+  const uint32_t t_dh = tmem + S::kDH;
+  auto t_acc = [&](int x) { return tmem + S::kAcc + static_cast<uint32_t>(x & 1) * VS; };
+  auto t_o = [&](int x) { return tmem + S::kO + static_cast<uint32_t>(x & 1) * VS; };
+  constexpr bool kBf16 = !std::is_same<T, __half>::value;
+  const uint32_t id_xy = umma::idesc_f16(128, VS, kBf16, false, true);
+  const uint32_t id_dh = umma::idesc_f16(128, VS, kBf16, true, true);
+  const uint64_t d_h = umma::smem_desc(umma::smem_u32(himg), RSV, 128);
+  const uint64_t d_vt = umma::smem_desc(umma::smem_u32(vtimg), RSV, 128);
+  const uint64_t d_vn = umma::smem_desc(umma::smem_u32(vnimg), RSV, 128);
+  T* obase = static_cast<T*>(p.o);
+
+  // o rows of chunk x (warps of quadrants 2, 3): o = a Y + scale O
+  auto emit = [&](int x, float ai) {
+    const int64_t s = bos + static_cast<int64_t>(x) * kChunk;
+    const int L = static_cast<int>(min64(kChunk, eos - s));
+    const int i = row - 64;
+    float y[16], z[16];
+    umma::tmem_ld16x2(t_acc(x) + lane_base + colh * 16, t_o(x) + lane_base + colh * 16, y, z);
+    if (i < L) {
+      T* orow = obase + ((s + i) * p.HV + hv) * D + v0 + colh * 16;
+#pragma unroll
+      for (int j8 = 0; j8 < 2; ++j8) {
+        float ov[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ov[e] = fmaf(ai, y[j8 * 8 + e], scale * z[j8 * 8 + e]);
+        *reinterpret_cast<uint4*>(orow + j8 * 8) = pack8<T>(ov);
+      }
+    }
+  };
+
+  bool ok = true;   // uniform: changes only at block-wide barriers
+  bool mine = true; // this thread's own waits since the last barrier
+  float a_prev = 0.f;  // emit warps: a of the previous chunk's row
+  if (producer && nch > 0) {
+    mine = umma::mbar_wait(full(0), 0);
+    if (!mine) record_error(w.err, 1, kSiteStLoad);
+  }
+  for (int c = 0; c < nch; ++c) {
+    if (__syncthreads_or(!mine)) { ok = false; break; }
+    umma::fence_after_sync();
+    uint8_t* b = stage(c);
+    const float* sc = reinterpret_cast<const float*>(b + S::kSc);
+    if (warp == 0) {  // MMA1: [X; Y] = [W; Q] h
+      if (umma::elect_one()) {
+        const uint64_t da = umma::smem_desc_sw128(umma::smem_u32(b + S::kWQ), 16, 1024);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma::mma_f16(t_acc(c), da + (((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4),
+                        d_h + ((ks * 2 * RSV) >> 4), id_xy, ks > 0);
+        umma::mma_commit(bar_mma1);
+      }
+      __syncwarp();
+    }
+    if (producer) {
+      // chunk c+2 goes where chunk c-1 was: its O product must be done
+      if (c >= 1) {
+        mine = umma::mbar_wait(bar_o, static_cast<uint32_t>((c - 1) & 1));
+        if (!mine) record_error(w.err, 1, kSiteStMma2);
+      }
+      if (mine && c + 2 < nch && umma::elect_one()) fetch(c + 2);
+      __syncwarp();
+      if (mine && c + 1 < nch) {  // operands of the next chunk
+        mine = umma::mbar_wait(full(c + 1), static_cast<uint32_t>(((c + 1) / S::kStages) & 1));
+        if (!mine) record_error(w.err, 1, kSiteStLoad);
+      }
+      continue;
+    }
+    if (quad >= 2) {  // off the chain: the previous chunk's output rows
+      if (c >= 1) {
+        mine = umma::mbar_wait(bar_o, static_cast<uint32_t>((c - 1) & 1));
+        if (!mine) record_error(w.err, 1, kSiteStMma2);
+        umma::fence_after_sync();
+        if (mine) emit(c - 1, a_prev);
+      }
+      a_prev = sc[row - 64];
+    } else {  // E1 (rows 0..63): v = U - X, V~ = diag(b) v
+      mine = umma::mbar_wait(bar_mma1, static_cast<uint32_t>(c & 1));
+      if (!mine) record_error(w.err, 1, kSiteStMma1);
+      umma::fence_after_sync();
+      uint32_t rx[16];
+      umma::tmem_ld16_nw(t_acc(c) + lane_base + colh * 16, rx);
+      umma::tmem_wait_ld();
+      umma::reg_fence16(rx);
+      const int i = row;
+      const float bi = sc[64 + i];
+      const T* ut = reinterpret_cast<const T*>(b + S::kU);
+#pragma unroll
+      for (int j8 = 0; j8 < 2; ++j8) {
+        const int col = colh * 16 + j8 * 8;
+        float u8[8], vn[8], vt[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(ut + u_off(i, col, VS)), u8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          vn[e] = u8[e] - __uint_as_float(rx[j8 * 8 + e]);
+          vt[e] = bi * vn[e];
+        }
+        *reinterpret_cast<uint4*>(vnimg + umma::img_off(i, col, RSV)) = pack8<T>(vn);
+        *reinterpret_cast<uint4*>(vtimg + umma::img_off(i, col, RSV)) = pack8<T>(vt);
+      }
+      umma::fence_proxy_async();
+      umma::fence_before_sync();
+      umma::named_sync(1, 128);  // warps 0, 1, 4, 5
+      if (warp == 0) {  // MMA2: dH = K^T V~ (the chain), then O = [. ; P] v
+        umma::fence_after_sync();
+        if (umma::elect_one()) {
+          const uint64_t dk = umma::smem_desc_sw128(umma::smem_u32(b + S::kK), kAtom, 1024);
+#pragma unroll
+          for (int ks = 0; ks < 64 / 16; ++ks)
+            umma::mma_f16(t_dh, dk + ((ks * 2048) >> 4), d_vt + ((ks * 2 * RSV) >> 4), id_dh, ks > 0);
+          umma::mma_commit(bar_dh);
+          const uint64_t dp = umma::smem_desc(umma::smem_u32(b + S::kP - kImg64x64), 128, RS64);
+#pragma unroll
+          for (int ks = 0; ks < 64 / 16; ++ks)
+            umma::mma_f16(t_o(c), dp + ((ks * 256) >> 4), d_vn + ((ks * 2 * RSV) >> 4), id_xy, ks > 0);
+          umma::mma_commit(bar_o);
+        }
+        __syncwarp();
+      }
+    }
+    // E2 (rows 0..127): h <- gamma h + dH and the image of h for the next MMA1
+    if (mine) {
+      mine = umma::mbar_wait(bar_dh, static_cast<uint32_t>(c & 1));
+      if (!mine) record_error(w.err, 1, kSiteStMma2);
+    }
+    umma::fence_after_sync();
+    if (mine) {
+      float d[16];
+      umma::tmem_ld16(t_dh + lane_base + colh * 16, d);
+      const float g = sc[128];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) hreg[j] = fmaf(g, hreg[j], d[j]);
+      if (c + 1 < nch) {
+#pragma unroll
+        for (int j8 = 0; j8 < 2; ++j8)
+          *reinterpret_cast<uint4*>(himg + umma::img_off(row, colh * 16 + j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
+      }
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+  }
+  if (ok && nch > 0) {  // the last chunk's output rows
+    ok = !__syncthreads_or(!mine);
+    if (ok && !producer && quad >= 2) {
+      mine = umma::mbar_wait(bar_o, static_cast<uint32_t>((nch - 1) & 1));
+      if (!mine) record_error(w.err, 1, kSiteStMma2);
+      umma::fence_after_sync();
+      if (mine) emit(nch - 1, a_prev);
+    }
+    ok = !__syncthreads_or(!mine);
+  }
+  if (ok && !producer && p.final_state) {
+    const int64_t base = (n * p.HV + hv) * D * D;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int col = v0 + colh * 16 + j;
+      if (p.state_v_first) p.final_state[base + static_cast<int64_t>(col) * D + row] = hreg[j];
+      else p.final_state[base + static_cast<int64_t>(row) * D + col] = hreg[j];
+    }
+  }
+  if (!ok && tid == 256) {
+    // operand copies may still be in flight after a timeout: wait (bounded)
+    // for every stage before the CTA exits and its shared memory is reused
+    for (int x = 0; x < S::kStages; ++x) umma::mbar_wait(umma::smem_u32(bars + x), 0, 20000000LL);
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, S::kCols);
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -768,6 +1059,17 @@ cudaError_t launch_state(const gdn_chunk_args& a, const Work& w, float scale, co
   return cudaGetLastError();
 }
 
+template <typename T>
+cudaError_t launch_state3(const gdn_chunk_args& a, const Work& w, float scale, const CUtensorMap& tq,
+                          const CUtensorMap& tk, cudaStream_t s, LaunchHooks& hk) {
+  auto kern = tc_state3_kernel<T>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, St3::kBytes);
+  if (e != cudaSuccess) return e;
+  hk.pre(s);
+  kern<<<dim3(static_cast<unsigned>(a.N), a.HV, D / St3::VS), kSt3Threads, St3::kBytes, s>>>(a, w, scale, tq, tk);
+  return cudaGetLastError();
+}
+
 int choose_vs(const gdn_chunk_args& a) {
   const int64_t rec = a.N * a.HV;
   if (rec <= 148) return 32;
@@ -810,7 +1112,7 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
     hk.pre(s);
     wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem::kBytes, s>>>(a, w, scale, tq, tk, tv);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (w.vs == 32) e = launch_state<T, 32>(a, w, scale, tq, tk, s, hk);
+    if (w.vs == 32) e = launch_state3<T>(a, w, scale, tq, tk, s, hk);
     else if (w.vs == 64) e = launch_state<T, 64>(a, w, scale, tq, tk, s, hk);
     else e = launch_state<T, 128>(a, w, scale, tq, tk, s, hk);
     if (e != cudaSuccess) return e;
