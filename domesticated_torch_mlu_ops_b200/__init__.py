@@ -1,10 +1,11 @@
 """B200-native gated delta-rule (GDN) forward: drop-in for the GDN entry
-points of ``torch_mlu_ops.triton_ops``.
+points of ``torch_mlu_ops.triton_ops`` and the causal conv1d that feeds them.
 
 The ops run hand-written sm_100a CUDA kernels in ``libgdn_b200.so``, called
 through its C ABI (``include/gdn_b200.h``).
 """
 
+from .conv import causal_conv1d, causal_conv1d_fn, causal_conv1d_update  # noqa: F401
 from .gdn import (  # noqa: F401
     chunk_gated_delta_rule,
     fused_recurrent_gated_delta_rule,
@@ -13,6 +14,9 @@ from .gdn import (  # noqa: F401
 )
 
 __all__ = [
+    "causal_conv1d",
+    "causal_conv1d_fn",
+    "causal_conv1d_update",
     "chunk_gated_delta_rule",
     "fused_recurrent_gated_delta_rule",
     "fused_recurrent_gated_delta_rule_fn",

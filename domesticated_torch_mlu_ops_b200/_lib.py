@@ -20,6 +20,7 @@ GDN_ERR_WORKSPACE = -4
 GDN_ERR_DEVICE = -5
 
 GDN_F32, GDN_BF16, GDN_F16, GDN_I32, GDN_I64 = 0, 1, 2, 3, 4
+GDN_ACT_NONE, GDN_ACT_SILU = 0, 1
 
 EXPORTED = (
     "gdn_chunk_workspace_size",
@@ -29,6 +30,9 @@ EXPORTED = (
     "gdn_fused_recurrent_fwd",
     "gdn_recurrent_plain_fwd",
     "gdn_solve_tril",
+    "gdn_causal_conv1d_fwd",
+    "gdn_causal_conv1d_fn",
+    "gdn_causal_conv1d_update",
     "gdn_last_error",
     "gdn_abi_version",
     "gdn_kernel_launch_count",
@@ -80,6 +84,38 @@ class RecurrentPlainArgs(ctypes.Structure):
     ]
 
 
+class Conv1dArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("weight", _vp), ("bias", _vp), ("residual", _vp), ("initial_state", _vp),
+        ("y", _vp), ("cu_seqlens", _vp),
+        ("B", _i64), ("T", _i64), ("N", _i64), ("D", _i64),
+        ("W", _i32), ("x_dtype", _i32), ("w_dtype", _i32), ("state_dtype", _i32), ("cu_dtype", _i32),
+        ("activation", _i32),
+    ]
+
+
+class Conv1dFnArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("out", _vp), ("weight", _vp), ("bias", _vp), ("conv_states", _vp),
+        ("query_start_loc", _vp), ("cache_indices", _vp), ("has_initial_state", _vp),
+        ("stride_x_token", _i64), ("stride_o_token", _i64),
+        ("stride_state_seq", _i64), ("stride_state_tok", _i64), ("num_cache_lines", _i64),
+        ("batch", _i64), ("dim", _i64), ("total_tokens", _i64),
+        ("pad_slot_id", _i64), ("null_block_id", _i64),
+        ("has_null_block", _i32), ("W", _i32),
+        ("x_dtype", _i32), ("w_dtype", _i32), ("state_dtype", _i32), ("qsl_dtype", _i32), ("idx_dtype", _i32),
+        ("activation", _i32),
+    ]
+
+
+class Conv1dUpdateArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", _vp), ("cache", _vp), ("residual", _vp), ("weight", _vp), ("bias", _vp), ("y", _vp),
+        ("stride_x_n", _i64), ("N", _i64), ("D", _i64),
+        ("W", _i32), ("x_dtype", _i32), ("cache_dtype", _i32), ("w_dtype", _i32), ("activation", _i32),
+    ]
+
+
 _lib = None
 
 
@@ -107,6 +143,12 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.gdn_recurrent_plain_fwd.restype = ctypes.c_int
     lib.gdn_solve_tril.argtypes = [_vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i32, _i32, _vp]
     lib.gdn_solve_tril.restype = ctypes.c_int
+    lib.gdn_causal_conv1d_fwd.argtypes = [ctypes.POINTER(Conv1dArgs), _vp]
+    lib.gdn_causal_conv1d_fwd.restype = ctypes.c_int
+    lib.gdn_causal_conv1d_fn.argtypes = [ctypes.POINTER(Conv1dFnArgs), _vp]
+    lib.gdn_causal_conv1d_fn.restype = ctypes.c_int
+    lib.gdn_causal_conv1d_update.argtypes = [ctypes.POINTER(Conv1dUpdateArgs), _vp]
+    lib.gdn_causal_conv1d_update.restype = ctypes.c_int
     lib.gdn_last_error.argtypes = []
     lib.gdn_last_error.restype = ctypes.c_char_p
     lib.gdn_abi_version.argtypes = []

@@ -1,0 +1,467 @@
+// Causal depthwise conv1d (the short convolution in front of the GDN layer),
+// the three reference ops behind torch_mlu_ops.triton_ops:
+//   causal_conv1d       -> triton/conv/ops.py:35-99,   kernels.py:24-153
+//   causal_conv1d_fn    -> triton/conv/ops.py:101-349, kernels.py:157-609
+//   causal_conv1d_update-> triton/conv/ops.py:584-644, kernels.py:850-934
+//
+// All three are HBM streams (W <= 4 taps per channel), so the kernels are
+// built for bandwidth, not tensor cores:
+//   * channel-last tiles: a thread owns one 16-byte vector of channels
+//     (8 x bf16/f16 or 4 x f32) and walks a 64-token tile, so every warp load
+//     is 512 contiguous bytes; the W-1 previous inputs stay in registers and
+//     each input is read once (plus a W-1 token halo per tile);
+//   * tiles run over the flat token range and find their sequence by binary
+//     search in cu_seqlens / query_start_loc on the device (no host sync);
+//     at a sequence start the window is refilled from the initial state (or
+//     zeros), so tiles may straddle sequences;
+//   * the vLLM cache update (each sequence's last W-1 tokens into its line)
+//     is a second small kernel, so no tile reads a line another tile has
+//     already overwritten (the reference orders this inside one program);
+//   * the decode update is one thread per channel.
+// Accumulation is fp32; outputs are rounded to nearest even.
+
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+
+#include <cstdarg>
+#include <cstdio>
+
+namespace gdn {
+namespace conv {
+
+constexpr int kTT = 64;        // tokens per tile
+constexpr int kThreads = 128;  // threads per CTA (each owns one channel vector)
+constexpr int kMaxW = 16;
+
+__device__ __forceinline__ float ld_any(const void* p, int dtype, int64_t i) {
+  if (dtype == GDN_F32) return static_cast<const float*>(p)[i];
+  if (dtype == GDN_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+__device__ __forceinline__ void st_any(void* p, int dtype, int64_t i, float v) {
+  if (dtype == GDN_F32) static_cast<float*>(p)[i] = v;
+  else if (dtype == GDN_BF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else static_cast<__half*>(p)[i] = __float2half_rn(v);
+}
+
+// VEC consecutive elements <-> floats; one 128-bit access when VEC fills 16 B.
+template <typename T, int VEC>
+__device__ __forceinline__ void ldv(const T* p, float* v) {
+  if constexpr (VEC * sizeof(T) == 16) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) v[i] = to_f<T>(e[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) v[i] = to_f<T>(p[i]);
+  }
+}
+template <typename T, int VEC>
+__device__ __forceinline__ void stv(T* p, const float* v) {
+  if constexpr (VEC * sizeof(T) == 16) {
+    uint4 u;
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) e[i] = from_f<T>(v[i]);
+    *reinterpret_cast<uint4*>(p) = u;
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) p[i] = from_f<T>(v[i]);
+  }
+}
+
+__device__ __forceinline__ float silu(float y) { return y / (1.f + expf(-y)); }
+
+struct FwdParams {
+  const void* x;
+  void* y;
+  const void* residual;  // fla only, [total, D] contiguous
+  const void* weight;    // [D, W]
+  const void* bias;      // [D]
+  const void* init;      // fla: initial_state [N, D, W]; fn: conv_states
+  const void* cu;        // [nseq + 1] or null (fla equal-length batch)
+  const void* cache_indices;
+  const uint8_t* has_init;
+  int64_t total, D, T, nseq;
+  int64_t sx, sy;          // token strides of x, y (elements)
+  int64_t st_seq, st_tok;  // fn: conv_states strides (elements)
+  int64_t pad_slot, null_block;
+  int has_null, fn_mode;
+  int W, w_dtype, init_dtype, cu_dtype, idx_dtype, act;
+};
+
+// Sequence n with cu[n] <= t < cu[n+1] (the last such n when empty
+// sequences share the boundary).
+__device__ __forceinline__ void find_seq(const FwdParams& p, int64_t t, int64_t& n, int64_t& bos,
+                                         int64_t& eos) {
+  if (!p.cu) {
+    n = t / p.T;
+    bos = n * p.T;
+    eos = bos + p.T;
+    return;
+  }
+  int64_t lo = 0, hi = p.nseq;  // cu[lo] <= t < cu[hi]
+  while (hi - lo > 1) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (load_index(p.cu, p.cu_dtype, mid) <= t) lo = mid; else hi = mid;
+  }
+  n = lo;
+  bos = load_index(p.cu, p.cu_dtype, n);
+  eos = load_index(p.cu, p.cu_dtype, n + 1);
+}
+
+template <typename T, int VEC, int KW>
+__global__ void __launch_bounds__(kThreads) conv_fwd_kernel(const FwdParams p) {
+  constexpr int WM = KW > 0 ? KW : kMaxW;
+  const int W = KW > 0 ? KW : p.W;
+  const int64_t c = (static_cast<int64_t>(blockIdx.y) * kThreads + threadIdx.x) * VEC;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kTT;
+  if (c >= p.D || t0 >= p.total) return;
+  const int64_t t1 = min64(t0 + kTT, p.total);
+  const T* x = static_cast<const T*>(p.x);
+  T* y = static_cast<T*>(p.y);
+  const T* res = static_cast<const T*>(p.residual);
+
+  float w[WM][VEC], bias[VEC];
+#pragma unroll
+  for (int i = 0; i < WM; ++i)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) w[i][e] = i < W ? ld_any(p.weight, p.w_dtype, (c + e) * W + i) : 0.f;
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) bias[e] = p.bias ? ld_any(p.bias, p.w_dtype, c + e) : 0.f;
+
+  int64_t n, bos, eos;
+  find_seq(p, t0, n, bos, eos);
+  float win[WM][VEC];  // win[j] = input at token t - (W-1) + j, j < W-1
+  bool fresh = true, skip = false;
+
+  // one output token from its input xv; shifts the window
+  auto step = [&](int64_t t, const float* xv) {
+    float acc[VEC];
+    if (skip) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] = bias[e];
+#pragma unroll
+      for (int j = 0; j < WM - 1; ++j)
+        if (j < W - 1)
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[e] = fmaf(w[j][e], win[j][e], acc[e]);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] = fmaf(w[W - 1][e], xv[e], acc[e]);
+      if (p.act == GDN_ACT_SILU)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[e] = silu(acc[e]);
+      if (res) {
+        float r[VEC];
+        ldv<T, VEC>(res + t * p.D + c, r);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[e] += r[e];
+      }
+    }
+    stv<T, VEC>(y + t * p.sy + c, acc);
+#pragma unroll
+    for (int j = 0; j + 1 < WM - 1; ++j)
+      if (j + 1 < W - 1)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) win[j][e] = win[j + 1][e];
+    if (W >= 2)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) win[W - 2][e] = xv[e];
+  };
+
+  int64_t t = t0;
+  while (t < t1) {
+    while (t >= eos) {  // next (possibly empty) sequence
+      ++n;
+      bos = eos;
+      eos = p.cu ? load_index(p.cu, p.cu_dtype, n + 1) : bos + p.T;
+      fresh = true;
+    }
+    if (fresh) {  // window from the sequence's own inputs, its initial state or zeros
+      fresh = false;
+      bool hinit;
+      int64_t line = n;
+      if (p.fn_mode) {
+        if (p.cache_indices) line = load_index(p.cache_indices, p.idx_dtype, n);
+        skip = (p.has_null && line == p.null_block) || line == p.pad_slot;
+        hinit = p.has_init && p.has_init[n];
+      } else {
+        hinit = p.init != nullptr;
+      }
+#pragma unroll
+      for (int j = 0; j < WM - 1; ++j) {
+        if (j >= W - 1) break;
+        const int64_t u = t - (W - 1) + j;
+        if (u >= bos) {
+          ldv<T, VEC>(x + u * p.sx + c, win[j]);
+        } else if (hinit && !skip) {
+          const int64_t local = u - bos;  // -(W-1) .. -1
+#pragma unroll
+          for (int e = 0; e < VEC; ++e)
+            win[j][e] = p.fn_mode
+                ? ld_any(p.init, p.init_dtype, line * p.st_seq + (local + W - 1) * p.st_tok + c + e)
+                : ld_any(p.init, p.init_dtype, (n * p.D + c + e) * W + local + W);
+        } else {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) win[j][e] = 0.f;
+        }
+      }
+    }
+    const int64_t end = min64(t1, eos);
+    if (t + 4 <= end) {  // four independent loads in flight
+      float xv[4][VEC];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) ldv<T, VEC>(x + (t + k) * p.sx + c, xv[k]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) step(t + k, xv[k]);
+      t += 4;
+    } else {
+      float xv[VEC];
+      ldv<T, VEC>(x + t * p.sx + c, xv);
+      step(t, xv);
+      ++t;
+    }
+  }
+}
+
+// vLLM cache update: line <- the last W-1 entries of [old line (or zeros),
+// the sequence's inputs] (kernels.py:381-484).  Runs after conv_fwd_kernel.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kThreads) conv_state_kernel(const FwdParams p) {
+  const int64_t s = blockIdx.x;
+  const int64_t c = (static_cast<int64_t>(blockIdx.y) * kThreads + threadIdx.x) * VEC;
+  if (c >= p.D) return;
+  const int sl = p.W - 1;
+  const int64_t line = p.cache_indices ? load_index(p.cache_indices, p.idx_dtype, s) : s;
+  if ((p.has_null && line == p.null_block) || line == p.pad_slot) return;
+  const bool hinit = p.has_init && p.has_init[s];
+  const int64_t bos = load_index(p.cu, p.cu_dtype, s), L = load_index(p.cu, p.cu_dtype, s + 1) - bos;
+  if (L <= 0) return;  // an empty sequence runs no program and leaves its line alone
+  const T* x = static_cast<const T*>(p.x);
+  float nv[3][VEC];  // W <= 4
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    if (j >= sl) break;
+    const int64_t u = L + j;  // index into [line ; inputs]
+    if (u < sl) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e)
+        nv[j][e] = hinit ? ld_any(p.init, p.init_dtype, line * p.st_seq + u * p.st_tok + c + e) : 0.f;
+    } else {
+      ldv<T, VEC>(x + (bos + u - sl) * p.sx + c, nv[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    if (j >= sl) break;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e)
+      st_any(const_cast<void*>(p.init), p.init_dtype, line * p.st_seq + j * p.st_tok + c + e, nv[j][e]);
+  }
+}
+
+struct UpdParams {
+  const void* x;
+  void* cache;
+  const void* residual;
+  const void* weight;
+  const void* bias;
+  void* y;
+  int64_t sxn, N, D;
+  int W, cache_dtype, w_dtype, act;
+};
+
+template <typename T, int KW>
+__global__ void __launch_bounds__(kThreads) conv_update_kernel(const UpdParams p) {
+  constexpr int WM = KW > 0 ? KW : kMaxW;
+  const int W = KW > 0 ? KW : p.W;
+  const int64_t n = blockIdx.y;
+  const int64_t d = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (d >= p.D) return;
+  const float xv = to_f<T>(static_cast<const T*>(p.x)[n * p.sxn + d]);
+  const int64_t cb = (n * p.D + d) * W;
+  float win[WM];
+#pragma unroll
+  for (int j = 0; j < WM; ++j) {
+    if (j >= W) break;
+    win[j] = !p.cache ? 0.f : j + 1 < W ? ld_any(p.cache, p.cache_dtype, cb + j + 1) : xv;
+  }
+  float acc = p.bias ? ld_any(p.bias, p.w_dtype, d) : 0.f;
+#pragma unroll
+  for (int j = 0; j < WM; ++j) {
+    if (j >= W) break;
+    acc = fmaf(win[j], p.weight ? ld_any(p.weight, p.w_dtype, d * W + j) : 1.f, acc);
+  }
+  if (p.act == GDN_ACT_SILU) acc = silu(acc);
+  if (p.residual) acc += to_f<T>(static_cast<const T*>(p.residual)[n * p.D + d]);
+  static_cast<T*>(p.y)[n * p.D + d] = from_f<T>(acc);
+  if (p.cache)
+#pragma unroll
+    for (int j = 0; j < WM; ++j) {
+      if (j >= W) break;
+      st_any(p.cache, p.cache_dtype, cb + j, win[j]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  return set_last_error(code, "%s", buf);
+}
+bool fdtype_ok(int d) { return d == GDN_F32 || d == GDN_BF16 || d == GDN_F16; }
+bool idtype_ok(int d) { return d == GDN_I32 || d == GDN_I64; }
+int esize(int d) { return d == GDN_F32 ? 4 : 2; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <typename T, int VEC>
+cudaError_t launch_fwd_v(const FwdParams& p, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>((p.total + kTT - 1) / kTT),
+                  static_cast<unsigned>((p.D + VEC * kThreads - 1) / (VEC * kThreads)));
+  note_launch();
+  switch (p.W) {
+    case 2: conv_fwd_kernel<T, VEC, 2><<<grid, kThreads, 0, s>>>(p); break;
+    case 3: conv_fwd_kernel<T, VEC, 3><<<grid, kThreads, 0, s>>>(p); break;
+    case 4: conv_fwd_kernel<T, VEC, 4><<<grid, kThreads, 0, s>>>(p); break;
+    default: conv_fwd_kernel<T, VEC, 0><<<grid, kThreads, 0, s>>>(p); break;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || !p.fn_mode) return e;
+  const dim3 g2(static_cast<unsigned>(p.nseq),
+                static_cast<unsigned>((p.D + VEC * kThreads - 1) / (VEC * kThreads)));
+  note_launch();
+  conv_state_kernel<T, VEC><<<g2, kThreads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_fwd(const FwdParams& p, cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  const bool vec = p.D % V == 0 && p.sx % V == 0 && p.sy % V == 0 && aligned16(p.x) && aligned16(p.y) &&
+                   (!p.residual || aligned16(p.residual));
+  return vec ? launch_fwd_v<T, V>(p, s) : launch_fwd_v<T, 1>(p, s);
+}
+
+cudaError_t dispatch_fwd(const FwdParams& p, int x_dtype, cudaStream_t s) {
+  if (x_dtype == GDN_F32) return launch_fwd<float>(p, s);
+  if (x_dtype == GDN_BF16) return launch_fwd<__nv_bfloat16>(p, s);
+  return launch_fwd<__half>(p, s);
+}
+
+template <typename T>
+cudaError_t launch_update(const UpdParams& p, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>((p.D + kThreads - 1) / kThreads), static_cast<unsigned>(p.N));
+  note_launch();
+  switch (p.W) {
+    case 2: conv_update_kernel<T, 2><<<grid, kThreads, 0, s>>>(p); break;
+    case 3: conv_update_kernel<T, 3><<<grid, kThreads, 0, s>>>(p); break;
+    case 4: conv_update_kernel<T, 4><<<grid, kThreads, 0, s>>>(p); break;
+    default: conv_update_kernel<T, 0><<<grid, kThreads, 0, s>>>(p); break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace conv
+}  // namespace gdn
+
+using namespace gdn;
+using namespace gdn::conv;
+
+extern "C" GDN_API int gdn_causal_conv1d_fwd(const gdn_conv1d_args* a, void* stream) {
+  if (!a) return fail(GDN_ERR_INVALID, "null args");
+  if (!a->x || !a->weight || !a->y) return fail(GDN_ERR_INVALID, "x, weight and y must be non-null");
+  if (a->B <= 0 || a->T < 0 || a->D <= 0) return fail(GDN_ERR_INVALID, "bad shape B=%lld T=%lld D=%lld",
+                                                      (long long)a->B, (long long)a->T, (long long)a->D);
+  if (a->W < 1 || a->W > kMaxW) return fail(GDN_ERR_UNSUPPORTED, "kernel width W=%d outside [1, %d]", a->W, kMaxW);
+  if (!fdtype_ok(a->x_dtype) || !fdtype_ok(a->w_dtype) || (a->initial_state && !fdtype_ok(a->state_dtype)))
+    return fail(GDN_ERR_INVALID, "x, weight and state dtypes must be F32, BF16 or F16");
+  if (a->activation != GDN_ACT_NONE && a->activation != GDN_ACT_SILU)
+    return fail(GDN_ERR_INVALID, "activation must be GDN_ACT_NONE or GDN_ACT_SILU");
+  int64_t nseq = a->B;
+  if (a->cu_seqlens) {
+    if (!idtype_ok(a->cu_dtype)) return fail(GDN_ERR_INVALID, "cu_seqlens dtype must be I32 or I64");
+    if (a->B != 1) return fail(GDN_ERR_INVALID, "cu_seqlens requires B == 1 (got B=%lld)", (long long)a->B);
+    if (a->N < 1) return fail(GDN_ERR_INVALID, "cu_seqlens needs N >= 1 sequences");
+    nseq = a->N;
+  } else if (a->N != a->B) {
+    return fail(GDN_ERR_INVALID, "without cu_seqlens N must equal B (N=%lld B=%lld)", (long long)a->N,
+                (long long)a->B);
+  }
+  FwdParams p{};
+  p.x = a->x; p.y = a->y; p.residual = a->residual; p.weight = a->weight; p.bias = a->bias;
+  p.init = a->initial_state; p.cu = a->cu_seqlens; p.cu_dtype = a->cu_dtype;
+  p.total = a->B * a->T; p.D = a->D; p.T = a->T; p.nseq = nseq;
+  p.sx = a->D; p.sy = a->D;
+  p.W = a->W; p.w_dtype = a->w_dtype; p.init_dtype = a->state_dtype; p.act = a->activation;
+  p.pad_slot = INT64_MIN;
+  if (p.total == 0) return GDN_OK;
+  cudaError_t e = dispatch_fwd(p, a->x_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "gdn_causal_conv1d_fwd: %s", cudaGetErrorString(e));
+  return GDN_OK;
+}
+
+extern "C" GDN_API int gdn_causal_conv1d_fn(const gdn_conv1d_fn_args* a, void* stream) {
+  if (!a) return fail(GDN_ERR_INVALID, "null args");
+  if (!a->x || !a->out || !a->weight || !a->conv_states || !a->query_start_loc)
+    return fail(GDN_ERR_INVALID, "x, out, weight, conv_states and query_start_loc must be non-null");
+  if (a->batch < 0 || a->dim <= 0 || a->total_tokens < 0 || a->num_cache_lines < 0)
+    return fail(GDN_ERR_INVALID, "bad shape batch=%lld dim=%lld total=%lld", (long long)a->batch,
+                (long long)a->dim, (long long)a->total_tokens);
+  if (a->W < 2 || a->W > 4) return fail(GDN_ERR_UNSUPPORTED, "kernel width W=%d outside [2, 4]", a->W);
+  if (!fdtype_ok(a->x_dtype) || !fdtype_ok(a->w_dtype) || !fdtype_ok(a->state_dtype))
+    return fail(GDN_ERR_INVALID, "x, weight and conv_states dtypes must be F32, BF16 or F16");
+  if (!idtype_ok(a->qsl_dtype) || (a->cache_indices && !idtype_ok(a->idx_dtype)))
+    return fail(GDN_ERR_INVALID, "query_start_loc and cache_indices dtypes must be I32 or I64");
+  if (a->activation != GDN_ACT_NONE && a->activation != GDN_ACT_SILU)
+    return fail(GDN_ERR_INVALID, "activation must be GDN_ACT_NONE or GDN_ACT_SILU");
+  if (a->stride_x_token < a->dim || a->stride_o_token < a->dim)
+    return fail(GDN_ERR_INVALID, "token strides must be >= dim (channel-last layout)");
+  FwdParams p{};
+  p.x = a->x; p.y = a->out; p.weight = a->weight; p.bias = a->bias; p.init = a->conv_states;
+  p.cu = a->query_start_loc; p.cu_dtype = a->qsl_dtype;
+  p.cache_indices = a->cache_indices; p.idx_dtype = a->idx_dtype; p.has_init = a->has_initial_state;
+  p.total = a->total_tokens; p.D = a->dim; p.nseq = a->batch;
+  p.sx = a->stride_x_token; p.sy = a->stride_o_token;
+  p.st_seq = a->stride_state_seq; p.st_tok = a->stride_state_tok;
+  p.pad_slot = a->pad_slot_id; p.null_block = a->null_block_id; p.has_null = a->has_null_block;
+  p.fn_mode = 1; p.W = a->W; p.w_dtype = a->w_dtype; p.init_dtype = a->state_dtype; p.act = a->activation;
+  if (p.total == 0 || p.nseq == 0) return GDN_OK;
+  cudaError_t e = dispatch_fwd(p, a->x_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "gdn_causal_conv1d_fn: %s", cudaGetErrorString(e));
+  return GDN_OK;
+}
+
+extern "C" GDN_API int gdn_causal_conv1d_update(const gdn_conv1d_update_args* a, void* stream) {
+  if (!a) return fail(GDN_ERR_INVALID, "null args");
+  if (!a->x || !a->y) return fail(GDN_ERR_INVALID, "x and y must be non-null");
+  if (a->N < 0 || a->D <= 0 || a->stride_x_n < a->D)
+    return fail(GDN_ERR_INVALID, "bad shape N=%lld D=%lld stride=%lld", (long long)a->N, (long long)a->D,
+                (long long)a->stride_x_n);
+  if (a->W < 1 || a->W > kMaxW) return fail(GDN_ERR_UNSUPPORTED, "kernel width W=%d outside [1, %d]", a->W, kMaxW);
+  if (!fdtype_ok(a->x_dtype) || ((a->weight || a->bias) && !fdtype_ok(a->w_dtype)) ||
+      (a->cache && !fdtype_ok(a->cache_dtype)))
+    return fail(GDN_ERR_INVALID, "x, weight and cache dtypes must be F32, BF16 or F16");
+  if (a->activation != GDN_ACT_NONE && a->activation != GDN_ACT_SILU)
+    return fail(GDN_ERR_INVALID, "activation must be GDN_ACT_NONE or GDN_ACT_SILU");
+  if (a->N == 0) return GDN_OK;
+  UpdParams p{};
+  p.x = a->x; p.cache = a->cache; p.residual = a->residual; p.weight = a->weight; p.bias = a->bias; p.y = a->y;
+  p.sxn = a->stride_x_n; p.N = a->N; p.D = a->D; p.W = a->W;
+  p.cache_dtype = a->cache_dtype; p.w_dtype = a->w_dtype; p.act = a->activation;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = a->x_dtype == GDN_F32    ? launch_update<float>(p, s)
+                  : a->x_dtype == GDN_BF16 ? launch_update<__nv_bfloat16>(p, s)
+                                           : launch_update<__half>(p, s);
+  if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "gdn_causal_conv1d_update: %s", cudaGetErrorString(e));
+  return GDN_OK;
+}

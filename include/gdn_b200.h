@@ -21,6 +21,11 @@
  *                             -> triton/fla/fused_recurrent.py:134-187
  *   gdn_solve_tril         <- include/torch_mlu_ops.h:1052-1054 tmo::torch_api::solve_tril
  *                             (Python: _ops.py:6232-6257; AOTI shim config_inductor.py:484-490)
+ *   gdn_causal_conv1d_fwd  <- triton_ops.py:287-363 causal_conv1d
+ *                             -> triton/conv/ops.py:35-99 causal_conv1d_fwd_fla
+ *   gdn_causal_conv1d_fn   <- triton_ops.py:366-459 causal_conv1d_fn
+ *                             -> triton/conv/ops.py:101-349 causal_conv1d_fwd_vllm
+ *   gdn_causal_conv1d_update <- triton/conv/ops.py:584-644 causal_conv1d_update
  */
 #ifndef GDN_B200_H_
 #define GDN_B200_H_
@@ -203,6 +208,89 @@ GDN_API int gdn_recurrent_plain_fwd(const gdn_recurrent_plain_args* args, void* 
 GDN_API int gdn_solve_tril(const float* A, void* out, int32_t out_dtype,
                    const void* cu_seqlens, int32_t cu_dtype, int64_t N,
                    int64_t B, int64_t T, int32_t H, int32_t BT, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Causal depthwise conv1d (the short convolution before the GDN layer)
+ * ------------------------------------------------------------------------ */
+#define GDN_ACT_NONE 0
+#define GDN_ACT_SILU 1 /* "silu" / "swish": y / (1 + exp(-y)) */
+
+/* causal_conv1d (FLA layout).  y_t = sum_i x_{t-W+1+i} w_i, then + bias,
+ * activation, + residual, per channel.  Tokens before a sequence start come
+ * from initial_state or are zero.
+ *   x, residual, y  [B, T, D] of x_dtype (residual may be NULL);
+ *   weight [D, W], bias [D] (or NULL) of w_dtype;
+ *   initial_state [N, D, W] of state_dtype or NULL (column j = token j - W);
+ *   cu_seqlens [N+1] (I32/I64) or NULL: with it, B == 1 and the T tokens are
+ *   N packed sequences.  1 <= W <= 16. */
+typedef struct gdn_conv1d_args {
+  const void* x;
+  const void* weight;
+  const void* bias;
+  const void* residual;
+  const void* initial_state;
+  void* y;
+  const void* cu_seqlens;
+  int64_t B, T, N, D;
+  int32_t W;
+  int32_t x_dtype, w_dtype, state_dtype, cu_dtype;
+  int32_t activation; /* GDN_ACT_* */
+} gdn_conv1d_args;
+GDN_API int gdn_causal_conv1d_fwd(const gdn_conv1d_args* args, void* stream);
+
+/* causal_conv1d_fn (vLLM layout, continuous batching, slot-indexed state).
+ *   x (dim, total) with unit channel stride: element (c, t) at
+ *     x[t * stride_x_token + c]; out likewise with stride_o_token;
+ *   weight (dim, W) row-major, bias (dim) or NULL, both of w_dtype;
+ *   conv_states (lines, dim, >= W-1) of state_dtype with unit channel
+ *     stride: element (l, c, j) at l * stride_state_seq + j * stride_state_tok
+ *     + c; updated in place to each processed sequence's last W-1 tokens;
+ *   query_start_loc [batch+1] (qsl_dtype I32/I64); cache_indices [batch]
+ *     (idx_dtype) or NULL for line = sequence; has_initial_state [batch]
+ *     bytes (bool) or NULL for none.
+ * A sequence whose line equals null_block_id (when has_null_block) or
+ * pad_slot_id is skipped: its out tokens are written as zero and its line is
+ * left alone.  2 <= W <= 4. */
+typedef struct gdn_conv1d_fn_args {
+  const void* x;
+  void* out;
+  const void* weight;
+  const void* bias;
+  void* conv_states;
+  const void* query_start_loc;
+  const void* cache_indices;
+  const uint8_t* has_initial_state;
+  int64_t stride_x_token, stride_o_token;
+  int64_t stride_state_seq, stride_state_tok, num_cache_lines;
+  int64_t batch, dim, total_tokens;
+  int64_t pad_slot_id, null_block_id;
+  int32_t has_null_block;
+  int32_t W;
+  int32_t x_dtype, w_dtype, state_dtype, qsl_dtype, idx_dtype;
+  int32_t activation;
+} gdn_conv1d_fn_args;
+GDN_API int gdn_causal_conv1d_fn(const gdn_conv1d_fn_args* args, void* stream);
+
+/* causal_conv1d_update: one decode token per sequence.
+ *   x [N, D] (row stride stride_x_n), residual [N, D] (or NULL), y [N, D]
+ *     contiguous, all of x_dtype;
+ *   cache [N, D, W] of cache_dtype (or NULL: an all-zero window, no state),
+ *     shifted left by one with x entering the last column, in place;
+ *   weight [D, W] (or NULL: taps of one), bias [D] (or NULL) of w_dtype. */
+typedef struct gdn_conv1d_update_args {
+  const void* x;
+  void* cache;
+  const void* residual;
+  const void* weight;
+  const void* bias;
+  void* y;
+  int64_t stride_x_n;
+  int64_t N, D;
+  int32_t W;
+  int32_t x_dtype, cache_dtype, w_dtype;
+  int32_t activation;
+} gdn_conv1d_update_args;
+GDN_API int gdn_causal_conv1d_update(const gdn_conv1d_update_args* args, void* stream);
 
 /* Message for the last failing call on this thread ("" if none). */
 GDN_API const char* gdn_last_error(void);

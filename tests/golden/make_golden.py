@@ -239,6 +239,138 @@ def gen_chunk(ref: str):
         print("wrote", name)
 
 
+def _load_conv_modules(ref: str):
+    """Load ``triton/conv`` by path.  Four substitutions: the fla forward
+    launcher passes a Cambricon compiler option (``bottleneck=``) that
+    upstream Triton does not accept, which is dropped; the autotune lists
+    keep one block size each, since the interpreter has no device to
+    benchmark configurations on (the block size only tiles the channels);
+    and the fla forward's no-initial-state branch, which loads one
+    (BT + W - 1)-row block and slices it per tap (a non-power-of-2 block and
+    register slicing, both Cambricon extensions), is expressed as the same
+    kernel's per-tap block loads from its initial-state branch
+    (``kernels.py:114-122``): the same sum over taps of shifted rows; the
+    vLLM launcher's metadata grid callback no longer writes its (identical)
+    program tables back into the launch arguments."""
+    _load("torch_mlu_ops.triton.fla.utils", os.path.join(ref, "triton/fla/utils.py"))
+    _load("torch_mlu_ops.triton.fla.index", os.path.join(ref, "triton/fla/index.py"))
+    conv = types.ModuleType("torch_mlu_ops.triton.conv")
+    conv.__path__ = [os.path.join(ref, "triton", "conv")]
+    sys.modules["torch_mlu_ops.triton.conv"] = conv
+
+    def kernels_patch(src):
+        src = src.replace("for BD in [128, 256]", "for BD in [128]").replace(
+            "for num_stages in [2,4]", "for num_stages in [2]")
+        head = "        if not USE_INITIAL_STATE:\n"
+        tail = "        elif i_t * BT >= W:\n"
+        i, j = src.index(head), src.index(tail)
+        per_tap = (head +
+                   "            for i_w in tl.static_range(-W + 1, 1):\n"
+                   "                p_yi = tl.make_block_ptr(p_x, (T, D), (stride_x_t, stride_x_d), "
+                   "(i_t * BT + i_w, i_d * BD), (BT, BD), (1, 0))\n"
+                   "                b_yi = tl.load(p_yi, boundary_check=(0, 1)).to(tl.float32)\n"
+                   "                if HAS_WEIGHT:\n"
+                   "                    b_yi *= tl.sum(b_w * (o_w == (i_w + W - 1)), 1)\n"
+                   "                b_y += b_yi\n")
+        return src[:i] + per_tap + src[j:]
+
+    _load("torch_mlu_ops.triton.conv.kernels", os.path.join(ref, "triton/conv/kernels.py"), kernels_patch)
+
+    def ops_patch(src):
+        # (the metadata grid callback re-assigns the program tables into the
+        # launch arguments; under the interpreter that replaces the converted
+        # pointers with raw tensors, so the re-assignment of the very same
+        # tensors is dropped)
+        src = src.replace('bottleneck="simd",', "")
+        src = src.replace('META["batch_ptr"] = nums_dict', '_same_table = nums_dict')
+        return src.replace('META["token_chunk_offset_ptr"] = nums_dict', '_same_table = nums_dict')
+
+    return _load("torch_mlu_ops.triton.conv.ops", os.path.join(ref, "triton/conv/ops.py"), ops_patch)
+
+
+def gen_conv(ref: str):
+    """Causal conv1d: the fla forward, the vLLM forward with a slot cache,
+    and the decode update (``triton/conv/ops.py``)."""
+    ops = _load_conv_modules(ref)
+    g = torch.Generator().manual_seed(zlib.crc32(b"conv") % 1000)
+
+    # fla forward: (name, B, T, D, W, bias, residual, init, act, cu)
+    fla_cases = [("fla_basic", 2, 100, 40, 4, True, True, False, "silu", None),
+                 ("fla_init", 2, 70, 24, 3, True, False, True, None, None),
+                 ("fla_varlen", 1, 131, 16, 4, False, True, True, "swish", [0, 30, 31, 131])]
+    for (name, B, T, D, W, hb, hr, hi, act, cu) in fla_cases:
+        x = torch.randn(B, T, D, generator=g)
+        w = torch.randn(D, W, generator=g) * 0.5
+        b = torch.randn(D, generator=g) if hb else None
+        r = torch.randn(B, T, D, generator=g) if hr else None
+        cut = torch.tensor(cu, dtype=torch.int64) if cu is not None else None
+        N = B if cu is None else len(cu) - 1
+        h0 = torch.randn(N, D, W, generator=g) if hi else None
+        y, _ = ops.causal_conv1d_fwd_fla(x, w, b, r, h0, False, act, cut)
+        np.savez_compressed(os.path.join(HERE, f"conv_{name}.npz"), x=_np(x), weight=_np(w),
+                            bias=_np(b) if b is not None else np.zeros(0, np.float32),
+                            residual=_np(r) if r is not None else np.zeros(0, np.float32),
+                            initial_state=_np(h0) if h0 is not None else np.zeros(0, np.float32),
+                            cu_seqlens=np.array(cu if cu is not None else [], np.int64),
+                            activation=np.str_(act or ""), y=_np(y))
+        print("wrote", name)
+
+    # vLLM forward: (name, dim, W, lens, has_init, cache_indices, lines, bias, act)
+    vllm_cases = [("fn_basic", 64, 4, [5, 1, 3, 70], [1, 0, 1, 1], [3, 7, 1, 5], 8, True, "silu"),
+                  ("fn_short", 48, 3, [2, 65, 1, 1], [0, 1, 1, 0], [2, 4, 6, 1], 7, False, None),
+                  ("fn_null", 32, 2, [4, 9, 130], [1, 1, 0], [0, 2, 5], 6, True, "silu")]
+    for (name, dim, W, lens, hin, idx, lines, hb, act) in vllm_cases:
+        total = sum(lens)
+        xt = torch.randn(total, dim, generator=g)       # channel-last storage
+        x = xt.t()                                      # (dim, total), stride(0) == 1
+        w = torch.randn(dim, W, generator=g) * 0.5
+        b = torch.randn(dim, generator=g) if hb else None
+        st = torch.randn(lines, W - 1, dim, generator=g)
+        cs = st.transpose(1, 2)                         # (lines, dim, W-1), stride(1) == 1
+        cs0 = cs.clone()
+        qsl = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+        ci = torch.tensor(idx, dtype=torch.int32)
+        hi = torch.tensor(hin, dtype=torch.bool)
+        # The launcher's default path sizes its program table through
+        # tensor methods that the interpreter's grid callback does not
+        # expose; the reference's own ``metadata`` path takes the same table
+        # precomputed (one program per 64-token block of each sequence).
+        nums = [-(-n // 64) for n in lens]
+        mlist = np.repeat(np.arange(len(nums)), nums).astype(np.int32)
+        offs = np.concatenate([np.arange(n) for n in nums]).astype(np.int32)
+        bp, tp = torch.from_numpy(mlist), torch.from_numpy(offs)
+        md = types.SimpleNamespace(batch_ptr=bp, token_chunk_offset_ptr=tp, nums_dict={64: dict(
+            tot=int(sum(nums)), mlist=bp, mlist_len=len(mlist), offsetlist=tp, batch_ptr=bp,
+            token_chunk_offset_ptr=tp)})
+        out = ops.causal_conv1d_fwd_vllm(x, w, b, cs, qsl, ci, hi, act, metadata=md)
+        np.savez_compressed(os.path.join(HERE, f"conv_{name}.npz"), x=_np(x.contiguous()), weight=_np(w),
+                            bias=_np(b) if b is not None else np.zeros(0, np.float32),
+                            conv_states_in=_np(cs0.contiguous()), conv_states_out=_np(cs.contiguous()),
+                            query_start_loc=qsl.numpy(), cache_indices=ci.numpy(), has_initial_state=hi.numpy(),
+                            activation=np.str_(act or ""), out=_np(out.contiguous()))
+        print("wrote", name)
+
+    # decode update: (name, N, D, W, bias, residual, act, x layout)
+    upd_cases = [("upd_basic", 5, 48, 4, True, True, "silu", "nd"),
+                 ("upd_w3", 3, 40, 3, False, False, None, "n1d"),
+                 ("upd_1nd", 4, 16, 2, True, False, "swish", "1nd")]
+    for (name, N, D, W, hb, hr, act, lay) in upd_cases:
+        x2 = torch.randn(N, D, generator=g)
+        x = {"nd": x2, "n1d": x2[:, None], "1nd": x2[None]}[lay]
+        cache = torch.randn(N, D, W, generator=g)
+        cache0 = cache.clone()
+        w = torch.randn(D, W, generator=g) * 0.5
+        b = torch.randn(D, generator=g) if hb else None
+        r = torch.randn(N, D, generator=g) if hr else None
+        y, _ = ops.causal_conv1d_update(x, cache, r, w, b, act)
+        np.savez_compressed(os.path.join(HERE, f"conv_{name}.npz"), x=_np(x2), weight=_np(w),
+                            bias=_np(b) if b is not None else np.zeros(0, np.float32),
+                            residual=_np(r) if r is not None else np.zeros(0, np.float32),
+                            cache_in=_np(cache0), cache_out=_np(cache), activation=np.str_(act or ""),
+                            layout=np.str_(lay), y=_np(y.reshape(N, D)))
+        print("wrote", name)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -252,6 +384,8 @@ def main():
         gen_recurrent(a.ref)
     if a.only in ("", "chunk"):
         gen_chunk(a.ref)
+    if a.only in ("", "conv"):
+        gen_conv(a.ref)
 
 
 if __name__ == "__main__":

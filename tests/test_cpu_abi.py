@@ -39,7 +39,10 @@ def test_library_exports_every_declared_symbol():
 
 @pytest.mark.parametrize("struct,cname", [(_lib.ChunkArgs, "gdn_chunk_args"),
                                           (_lib.RecurrentArgs, "gdn_recurrent_args"),
-                                          (_lib.RecurrentPlainArgs, "gdn_recurrent_plain_args")])
+                                          (_lib.RecurrentPlainArgs, "gdn_recurrent_plain_args"),
+                                          (_lib.Conv1dArgs, "gdn_conv1d_args"),
+                                          (_lib.Conv1dFnArgs, "gdn_conv1d_fn_args"),
+                                          (_lib.Conv1dUpdateArgs, "gdn_conv1d_update_args")])
 def test_struct_layout_matches_c(tmp_path, struct, cname):
     fields = [f[0] for f in struct._fields_]
     src = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', 'int main(void){',
@@ -99,6 +102,33 @@ def test_invalid_calls_return_codes_without_touching_the_gpu():
     assert lib.gdn_fused_recurrent_fwd(ctypes.byref(r), None) == _lib.GDN_ERR_INVALID
     assert b"ssm_state_indices" in lib.gdn_last_error()
     assert lib.gdn_solve_tril(None, None, 0, None, 0, 1, 1, 64, 2, 48, None) == _lib.GDN_ERR_INVALID
+
+
+def test_conv_validation_returns_codes_without_touching_the_gpu():
+    lib = _lib.load()
+    a = _lib.Conv1dArgs(B=1, T=8, N=1, D=16, W=4)
+    assert lib.gdn_causal_conv1d_fwd(ctypes.byref(a), None) == _lib.GDN_ERR_INVALID  # null pointers
+    for name in ("x", "weight", "y"):
+        setattr(a, name, ctypes.c_void_p(256))
+    a.W = 17
+    assert lib.gdn_causal_conv1d_fwd(ctypes.byref(a), None) == _lib.GDN_ERR_UNSUPPORTED
+    a.W, a.B = 4, 2
+    a.cu_seqlens = ctypes.c_void_p(256)
+    a.cu_dtype = _lib.GDN_I64
+    assert lib.gdn_causal_conv1d_fwd(ctypes.byref(a), None) == _lib.GDN_ERR_INVALID
+    assert b"B == 1" in lib.gdn_last_error()
+    f = _lib.Conv1dFnArgs(batch=2, dim=16, total_tokens=8, W=5)
+    for name in ("x", "out", "weight", "conv_states", "query_start_loc"):
+        setattr(f, name, ctypes.c_void_p(256))
+    f.stride_x_token = f.stride_o_token = 16
+    assert lib.gdn_causal_conv1d_fn(ctypes.byref(f), None) == _lib.GDN_ERR_UNSUPPORTED
+    f.W, f.stride_x_token = 4, 8  # token stride below dim
+    f.qsl_dtype = f.idx_dtype = _lib.GDN_I32
+    assert lib.gdn_causal_conv1d_fn(ctypes.byref(f), None) == _lib.GDN_ERR_INVALID
+    u = _lib.Conv1dUpdateArgs(N=2, D=16, W=4, stride_x_n=16, activation=3)
+    u.x = u.y = ctypes.c_void_p(256)
+    assert lib.gdn_causal_conv1d_update(ctypes.byref(u), None) == _lib.GDN_ERR_INVALID
+    assert b"activation" in lib.gdn_last_error()
 
 
 def test_python_errors_are_value_errors():
