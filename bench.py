@@ -344,8 +344,9 @@ def run_ours(a):
         h2d = sum(x.numel() * x.element_size() for x in [q_h, k_h, v_h, g_h, b_h] + extra_h)
         d2h = o_h.numel() * o_h.element_size() + ht_h.numel() * ht_h.element_size()
 
-    # ---- decode (config 3) ----
+    # ---- decode (config 3) and the causal conv1d in front of the layer ----
     dec = _decode_bench(ops, dev, a, hbm, flush) if not a.no_decode else None
+    conv = _conv_bench(ops, dev, a, hbm, flush) if not a.no_decode and rank == 0 else None
 
     # ---- CPU baseline (rank 0, N=1) ----
     cpu_line = None
@@ -399,6 +400,7 @@ def run_ours(a):
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
             "decode": dec,
+            "conv1d": conv,
             "cpu_baseline": cpu_line,
         }
         print(json.dumps(line), flush=True)
@@ -522,6 +524,53 @@ def _decode_bench(ops, dev, a, hbm, flush):
             "kernel": "decode_stream_kernel", "traffic": _load_traffic().get("decode")}
 
 
+def _conv_bench(ops, dev, a, hbm, flush):
+    """The causal conv1d in front of the GDN layer at the config-1 prefill
+    shape (q/k/v conv channels 2*16*128 + 32*128 = 8192, 8192 tokens,
+    width 4, SiLU, bf16, vLLM layout with a slot cache) and one decode
+    update for the config-3 batch (256 sequences)."""
+    import torch
+    D, T, W, N = 8192, CFG1["T"], 4, CFG3["N"]
+    gen = torch.Generator().manual_seed(4)
+    x = torch.randn(T, D, generator=gen).bfloat16().to(dev)
+    w = (torch.randn(D, W, generator=gen) * 0.3).bfloat16().to(dev)
+    b = torch.randn(D, generator=gen).bfloat16().to(dev)
+    cs = torch.zeros(2, W - 1, D, dtype=torch.bfloat16, device=dev).transpose(1, 2)
+    qsl = torch.tensor([0, T], dtype=torch.int32, device=dev)
+    ci = torch.tensor([1], dtype=torch.int32, device=dev)
+    hi = torch.tensor([True], device=dev)
+    xu = torch.randn(N, D, generator=gen).bfloat16().to(dev)
+    cache = torch.randn(N, D, W, generator=gen).bfloat16().to(dev)
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for st, en in ev:
+            flush.zero_()
+            st.record()
+            fn()
+            en.record()
+        torch.cuda.synchronize()
+        return sum(st.elapsed_time(en) for st, en in ev) / reps * 1e3
+
+    us_fn = timed(lambda: ops.causal_conv1d_fn(x.t(), w, b, cs, qsl, ci, hi, "silu"), max(a.steps, 10))
+    us_up = timed(lambda: ops.causal_conv1d_update(xu, cache, None, w, b, "silu"), max(a.steps, 10))
+    b_fn = 2 * T * D * 2 + D * W * 2 + D * 2 + 2 * D * (W - 1) * 2
+    b_up = N * D * (2 + 2 * W * 2 + 2) + D * W * 2 + D * 2
+    return {
+        "prefill": {"workload": "causal_conv1d_fn: dim 8192 x 8192 tokens, width 4, SiLU, bf16, slot cache",
+                    "us_per_call": us_fn, "algorithmic_bytes": b_fn,
+                    "achieved_gbs": b_fn / (us_fn * 1e-6) / 1e9, "frac_hbm": b_fn / (us_fn * 1e-6) / 1e9 / hbm,
+                    "kernels": "conv_fwd_kernel + conv_state_kernel"},
+        "update": {"workload": "causal_conv1d_update: 256 sequences x 8192 channels, width 4, bf16 cache",
+                   "us_per_call": us_up, "algorithmic_bytes": b_up,
+                   "achieved_gbs": b_up / (us_up * 1e-6) / 1e9, "frac_hbm": b_up / (us_up * 1e-6) / 1e9 / hbm,
+                   "kernels": "conv_update_kernel"},
+        "peak_gbs": hbm, "peak_kind": "measured HBM copy"}
+
+
 def run_reference(a):
     """CPU restatement of the reference algorithm (the oracle port), timed on
     the host's cores on a bounded sample of the config-1 workload."""
@@ -560,7 +609,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--no-decode", action="store_true", help="skip the decode measurement")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode and conv1d measurements")
     ap.add_argument("--ref-tokens", type=int, default=2048)
     ap.add_argument("--tokens", type=int, default=0,
                     help="override config 1's T (small cases for ncu captures; not a bench line)")

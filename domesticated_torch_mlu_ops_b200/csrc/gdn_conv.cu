@@ -23,6 +23,7 @@
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 
@@ -30,6 +31,7 @@ namespace gdn {
 namespace conv {
 
 constexpr int kTT = 64;        // tokens per tile
+constexpr int kU = 8;          // tokens loaded ahead per thread (vector path)
 constexpr int kThreads = 128;  // threads per CTA (each owns one channel vector)
 constexpr int kMaxW = 16;
 
@@ -71,7 +73,35 @@ __device__ __forceinline__ void stv(T* p, const float* v) {
   }
 }
 
-__device__ __forceinline__ float silu(float y) { return y / (1.f + expf(-y)); }
+// y * sigmoid(y) with the hardware exponential and divide (a few ulp).
+__device__ __forceinline__ float silu(float y) { return __fdividef(y, 1.f + __expf(-y)); }
+
+// For 16-bit outputs: y * sigmoid(y) = h + h * tanh(h) with h = y / 2, one
+// special-function instruction (tanh.approx, relative error about 2^-11,
+// under half an output ulp of bf16 and at the half-ulp of fp16).
+__device__ __forceinline__ float silu16(float y) {
+  const float h = 0.5f * y;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return fmaf(h, t, h);
+}
+
+// acc += w * x over VEC lanes, two lanes per packed fp32 FMA when VEC is even.
+template <int VEC>
+__device__ __forceinline__ void fma_vec(float* acc, const float* w, const float* x) {
+  if constexpr (VEC % 2 == 0) {
+#pragma unroll
+    for (int e = 0; e < VEC; e += 2) {
+      const float2 r = __ffma2_rn(make_float2(w[e], w[e + 1]), make_float2(x[e], x[e + 1]),
+                                  make_float2(acc[e], acc[e + 1]));
+      acc[e] = r.x;
+      acc[e + 1] = r.y;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[e] = fmaf(w[e], x[e], acc[e]);
+  }
+}
 
 struct FwdParams {
   const void* x;
@@ -87,6 +117,7 @@ struct FwdParams {
   int64_t sx, sy;          // token strides of x, y (elements)
   int64_t st_seq, st_tok;  // fn: conv_states strides (elements)
   int64_t pad_slot, null_block;
+  int64_t nblk, upc;  // channel blocks; tokens per CTA run
   int has_null, fn_mode;
   int W, w_dtype, init_dtype, cu_dtype, idx_dtype, act;
 };
@@ -112,13 +143,18 @@ __device__ __forceinline__ void find_seq(const FwdParams& p, int64_t t, int64_t&
 }
 
 template <typename T, int VEC, int KW>
-__global__ void __launch_bounds__(kThreads) conv_fwd_kernel(const FwdParams p) {
+__global__ void __launch_bounds__(kThreads, 3) conv_fwd_kernel(const FwdParams p) {
   constexpr int WM = KW > 0 ? KW : kMaxW;
   const int W = KW > 0 ? KW : p.W;
-  const int64_t c = (static_cast<int64_t>(blockIdx.y) * kThreads + threadIdx.x) * VEC;
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kTT;
-  if (c >= p.D || t0 >= p.total) return;
-  const int64_t t1 = min64(t0 + kTT, p.total);
+  // CTA b owns channel block b % nblk over the (b / nblk)-th equal run of
+  // tokens, so the nblk CTAs of one run (adjacent in launch order) stream
+  // whole token rows together.
+  for (int once = 0; once < 1; ++once) {
+  const int64_t cb = blockIdx.x % p.nblk, share = blockIdx.x / p.nblk;
+  const int64_t t0 = share * p.upc;
+  const int64_t t1 = min64(p.total, t0 + p.upc);
+  const int64_t c = (cb * kThreads + threadIdx.x) * VEC;
+  if (c >= p.D || t0 >= t1) continue;
   const T* x = static_cast<const T*>(p.x);
   T* y = static_cast<T*>(p.y);
   const T* res = static_cast<const T*>(p.residual);
@@ -147,14 +183,11 @@ __global__ void __launch_bounds__(kThreads) conv_fwd_kernel(const FwdParams p) {
       for (int e = 0; e < VEC; ++e) acc[e] = bias[e];
 #pragma unroll
       for (int j = 0; j < WM - 1; ++j)
-        if (j < W - 1)
-#pragma unroll
-          for (int e = 0; e < VEC; ++e) acc[e] = fmaf(w[j][e], win[j][e], acc[e]);
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) acc[e] = fmaf(w[W - 1][e], xv[e], acc[e]);
+        if (j < W - 1) fma_vec<VEC>(acc, w[j], win[j]);
+      fma_vec<VEC>(acc, w[W - 1], xv);
       if (p.act == GDN_ACT_SILU)
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) acc[e] = silu(acc[e]);
+        for (int e = 0; e < VEC; ++e) acc[e] = sizeof(T) == 2 ? silu16(acc[e]) : silu(acc[e]);
       if (res) {
         float r[VEC];
         ldv<T, VEC>(res + t * p.D + c, r);
@@ -212,7 +245,22 @@ __global__ void __launch_bounds__(kThreads) conv_fwd_kernel(const FwdParams p) {
       }
     }
     const int64_t end = min64(t1, eos);
-    if (t + 4 <= end) {  // four independent loads in flight
+    if (VEC * sizeof(T) == 16 && t + kU <= end) {  // kU independent loads in flight, kept packed
+      if constexpr (VEC * sizeof(T) == 16) {
+        uint4 raw[kU];
+#pragma unroll
+        for (int k = 0; k < kU; ++k) raw[k] = __ldg(reinterpret_cast<const uint4*>(x + (t + k) * p.sx + c));
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+          float xv[VEC];
+          const T* e = reinterpret_cast<const T*>(&raw[k]);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) xv[i] = to_f<T>(e[i]);
+          step(t + k, xv);
+        }
+      }
+      t += kU;
+    } else if (t + 4 <= end) {  // four loads in flight
       float xv[4][VEC];
 #pragma unroll
       for (int k = 0; k < 4; ++k) ldv<T, VEC>(x + (t + k) * p.sx + c, xv[k]);
@@ -225,6 +273,7 @@ __global__ void __launch_bounds__(kThreads) conv_fwd_kernel(const FwdParams p) {
       step(t, xv);
       ++t;
     }
+  }
   }
 }
 
@@ -296,7 +345,7 @@ __global__ void __launch_bounds__(kThreads) conv_update_kernel(const UpdParams p
     if (j >= W) break;
     acc = fmaf(win[j], p.weight ? ld_any(p.weight, p.w_dtype, d * W + j) : 1.f, acc);
   }
-  if (p.act == GDN_ACT_SILU) acc = silu(acc);
+  if (p.act == GDN_ACT_SILU) acc = sizeof(T) == 2 ? silu16(acc) : silu(acc);
   if (p.residual) acc += to_f<T>(static_cast<const T*>(p.residual)[n * p.D + d]);
   static_cast<T*>(p.y)[n * p.D + d] = from_f<T>(acc);
   if (p.cache)
@@ -305,6 +354,53 @@ __global__ void __launch_bounds__(kThreads) conv_update_kernel(const UpdParams p
       if (j >= W) break;
       st_any(p.cache, p.cache_dtype, cb + j, win[j]);
     }
+}
+
+// Vectorised decode update for the common layout (x, cache, weight, bias,
+// residual, y all of type T; D a multiple of 8; 16-byte aligned): a thread
+// owns 8 consecutive channels, whose cache rows, weights, inputs and
+// outputs are contiguous runs moved with 128-bit accesses.
+template <typename T, int KW>
+__global__ void __launch_bounds__(kThreads) conv_update_vec_kernel(const UpdParams p) {
+  static_assert(sizeof(T) == 2, "16-bit types");
+  constexpr int C8 = 8;                // channels per thread
+  constexpr int NV = C8 * KW / 8;      // 16-byte vectors in the thread's cache run
+  const int64_t n = blockIdx.y;
+  const int64_t d = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * C8;
+  if (d >= p.D) return;
+  const T* xs = static_cast<const T*>(p.x) + n * p.sxn + d;
+  T* cache = static_cast<T*>(p.cache) + (n * p.D + d) * KW;
+  const T* wt = static_cast<const T*>(p.weight) + d * KW;
+  float xv[C8], cf[C8 * KW], wf[C8 * KW], acc[C8];
+  ldv<T, C8>(xs, xv);
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    ldv<T, 8>(cache + v * 8, cf + v * 8);
+    ldv<T, 8>(wt + v * 8, wf + v * 8);
+  }
+  if (p.bias) ldv<T, C8>(static_cast<const T*>(p.bias) + d, acc);
+  else
+#pragma unroll
+    for (int e = 0; e < C8; ++e) acc[e] = 0.f;
+#pragma unroll
+  for (int e = 0; e < C8; ++e) {
+#pragma unroll
+    for (int j = 0; j < KW; ++j) {
+      const float v = j + 1 < KW ? cf[e * KW + j + 1] : xv[e];
+      cf[e * KW + j] = v;  // shifted window, in place
+      acc[e] = fmaf(v, wf[e * KW + j], acc[e]);
+    }
+    if (p.act == GDN_ACT_SILU) acc[e] = silu16(acc[e]);
+  }
+  if (p.residual) {
+    float r[C8];
+    ldv<T, C8>(static_cast<const T*>(p.residual) + n * p.D + d, r);
+#pragma unroll
+    for (int e = 0; e < C8; ++e) acc[e] += r[e];
+  }
+  stv<T, C8>(static_cast<T*>(p.y) + n * p.D + d, acc);
+#pragma unroll
+  for (int v = 0; v < NV; ++v) stv<T, 8>(cache + v * 8, cf + v * 8);
 }
 
 // ---------------------------------------------------------------------------
@@ -324,18 +420,44 @@ bool idtype_ok(int d) { return d == GDN_I32 || d == GDN_I64; }
 int esize(int d) { return d == GDN_F32 ? 4 : 2; }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Resident CTAs of a kernel on this device (queried once per kernel).
+template <typename K>
+int resident_ctas(K kern) {
+  static int cached = 0;
+  if (!cached) {
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0);
+    cached = sms * (per_sm > 0 ? per_sm : 1);
+  }
+  return cached;
+}
+
+template <typename T, int VEC, int KW>
+cudaError_t launch_fwd_w(FwdParams p, cudaStream_t s) {
+  auto kern = conv_fwd_kernel<T, VEC, KW>;
+  p.nblk = (p.D + VEC * kThreads - 1) / (VEC * kThreads);
+  // as many equal token runs (of at least kTT tokens) as the resident CTAs
+  // cover with every channel block: one wave, no tail
+  const int64_t shares = std::max<int64_t>(
+      1, std::min<int64_t>(resident_ctas(kern) / std::max<int64_t>(p.nblk, 1), (p.total + kTT - 1) / kTT));
+  p.upc = (p.total + shares - 1) / shares;  // tokens per run
+  const int64_t grid = p.nblk * shares;
+  note_launch();
+  kern<<<static_cast<unsigned>(grid), kThreads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
 template <typename T, int VEC>
 cudaError_t launch_fwd_v(const FwdParams& p, cudaStream_t s) {
-  const dim3 grid(static_cast<unsigned>((p.total + kTT - 1) / kTT),
-                  static_cast<unsigned>((p.D + VEC * kThreads - 1) / (VEC * kThreads)));
-  note_launch();
+  cudaError_t e;
   switch (p.W) {
-    case 2: conv_fwd_kernel<T, VEC, 2><<<grid, kThreads, 0, s>>>(p); break;
-    case 3: conv_fwd_kernel<T, VEC, 3><<<grid, kThreads, 0, s>>>(p); break;
-    case 4: conv_fwd_kernel<T, VEC, 4><<<grid, kThreads, 0, s>>>(p); break;
-    default: conv_fwd_kernel<T, VEC, 0><<<grid, kThreads, 0, s>>>(p); break;
+    case 2: e = launch_fwd_w<T, VEC, 2>(p, s); break;
+    case 3: e = launch_fwd_w<T, VEC, 3>(p, s); break;
+    case 4: e = launch_fwd_w<T, VEC, 4>(p, s); break;
+    default: e = launch_fwd_w<T, VEC, 0>(p, s); break;
   }
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !p.fn_mode) return e;
   const dim3 g2(static_cast<unsigned>(p.nseq),
                 static_cast<unsigned>((p.D + VEC * kThreads - 1) / (VEC * kThreads)));
@@ -359,7 +481,21 @@ cudaError_t dispatch_fwd(const FwdParams& p, int x_dtype, cudaStream_t s) {
 }
 
 template <typename T>
-cudaError_t launch_update(const UpdParams& p, cudaStream_t s) {
+cudaError_t launch_update(const UpdParams& p, int x_dtype, cudaStream_t s) {
+  if constexpr (sizeof(T) == 2) {
+    const bool vec = p.cache && p.weight && p.cache_dtype == x_dtype && p.w_dtype == x_dtype &&
+                     p.W >= 2 && p.W <= 4 && p.D % 8 == 0 && p.sxn % 8 == 0 && aligned16(p.x) &&
+                     aligned16(p.cache) && aligned16(p.weight) && aligned16(p.y) &&
+                     (!p.bias || aligned16(p.bias)) && (!p.residual || aligned16(p.residual));
+    if (vec) {
+      const dim3 grid(static_cast<unsigned>((p.D / 8 + kThreads - 1) / kThreads), static_cast<unsigned>(p.N));
+      note_launch();
+      if (p.W == 4) conv_update_vec_kernel<T, 4><<<grid, kThreads, 0, s>>>(p);
+      else if (p.W == 3) conv_update_vec_kernel<T, 3><<<grid, kThreads, 0, s>>>(p);
+      else conv_update_vec_kernel<T, 2><<<grid, kThreads, 0, s>>>(p);
+      return cudaGetLastError();
+    }
+  }
   const dim3 grid(static_cast<unsigned>((p.D + kThreads - 1) / kThreads), static_cast<unsigned>(p.N));
   note_launch();
   switch (p.W) {
@@ -459,9 +595,9 @@ extern "C" GDN_API int gdn_causal_conv1d_update(const gdn_conv1d_update_args* a,
   p.sxn = a->stride_x_n; p.N = a->N; p.D = a->D; p.W = a->W;
   p.cache_dtype = a->cache_dtype; p.w_dtype = a->w_dtype; p.act = a->activation;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = a->x_dtype == GDN_F32    ? launch_update<float>(p, s)
-                  : a->x_dtype == GDN_BF16 ? launch_update<__nv_bfloat16>(p, s)
-                                           : launch_update<__half>(p, s);
+  cudaError_t e = a->x_dtype == GDN_F32    ? launch_update<float>(p, a->x_dtype, s)
+                  : a->x_dtype == GDN_BF16 ? launch_update<__nv_bfloat16>(p, a->x_dtype, s)
+                                           : launch_update<__half>(p, a->x_dtype, s);
   if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "gdn_causal_conv1d_update: %s", cudaGetErrorString(e));
   return GDN_OK;
 }
