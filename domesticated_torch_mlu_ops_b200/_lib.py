@@ -105,6 +105,9 @@ class Conv1dFnArgs(ctypes.Structure):
         ("has_null_block", _i32), ("W", _i32),
         ("x_dtype", _i32), ("w_dtype", _i32), ("state_dtype", _i32), ("qsl_dtype", _i32), ("idx_dtype", _i32),
         ("activation", _i32),
+        ("block_idx_first", _vp), ("block_idx_last", _vp), ("initial_state_idx", _vp),
+        ("num_computed_tokens", _vp), ("stride_cache_indices", _i64), ("block_size_to_align", _i64),
+        ("apc_dtype", _i32),
     ]
 
 

@@ -17,9 +17,10 @@ Differences from the reference, all supersets or stricter checks:
   ``cache_indices=None`` maps sequence i to line i.
 * Products are accumulated in fp32 from the inputs as given (the reference
   first casts x to the ``conv_states`` dtype and multiplies in that dtype).
-* The prefix-caching block arguments of ``causal_conv1d_fn``
-  (``block_idx_*``, ``initial_state_idx``, ``num_computed_tokens``) are not
-  supported yet and raise ``NotImplementedError``.
+* Prefix caching (``block_idx_*``, ``initial_state_idx``,
+  ``num_computed_tokens``, ``block_size_to_align``) follows the reference
+  kernel; ``block_size_to_align`` must be a positive multiple of 64 (the
+  reference checks that only with ``validate_data``).
 * An unknown ``activation`` string raises ``ValueError`` (the reference
   kernels silently apply none).
 """
@@ -138,9 +139,6 @@ def causal_conv1d_fn(
         raise ValueError("[CausalConv1d] x.shape[0] must be equal to weight.shape[0].")
     if weight is not None and weight.shape[-1] > 4:
         raise ValueError("[CausalConv1d] weight.shape[-1] must be less than or equal to 4.")
-    if any(t is not None for t in (block_idx_first_scheduled_token, block_idx_last_scheduled_token,
-                                   initial_state_idx, num_computed_tokens)):
-        raise NotImplementedError("[CausalConv1d] prefix-caching block states are not supported")
     if weight is None or x.dim() != 2:
         raise ValueError("[CausalConv1d] x must be (dim, tokens) and weight (dim, width)")
     _cuda("causal_conv1d_fn", x, weight, bias, conv_states, query_start_loc, cache_indices, has_initial_state)
@@ -161,13 +159,27 @@ def causal_conv1d_fn(
     b = None if bias is None else bias.to(w.dtype).contiguous()
     qsl = query_start_loc if query_start_loc.dtype in _IDT else query_start_loc.to(torch.int32)
     batch = qsl.numel() - 1
+    apc = block_idx_last_scheduled_token is not None
     ci = None
     idx_dt = _lib.GDN_I32
     if cache_indices is not None:
         ci = (cache_indices if cache_indices.dtype in _IDT else cache_indices.to(torch.int32)).contiguous()
         idx_dt = _IDT[ci.dtype]
-        if ci.dim() != 1 or ci.numel() != batch:
-            raise ValueError(f"[CausalConv1d] cache_indices must be ({batch},)")
+        if ci.dim() not in (1, 2) or ci.shape[0] != batch or (ci.dim() == 2 and not apc):
+            raise ValueError(f"[CausalConv1d] cache_indices must be ({batch},) (or ({batch}, blocks) "
+                             "with prefix caching)")
+    blocks = [None] * 4
+    if apc:
+        if cache_indices is None:
+            raise ValueError("[CausalConv1d] prefix caching needs cache_indices")
+        if ci.dim() == 1:
+            ci = ci[:, None]
+        blocks = [t if t is None else t.to(torch.int32).contiguous()
+                  for t in (block_idx_first_scheduled_token, block_idx_last_scheduled_token,
+                            initial_state_idx, num_computed_tokens)]
+        if any(t is None for t in blocks):
+            raise ValueError("[CausalConv1d] prefix caching needs block_idx_first_scheduled_token, "
+                             "block_idx_last_scheduled_token, initial_state_idx and num_computed_tokens")
     hi = None
     if has_initial_state is not None:
         hi = has_initial_state.to(torch.bool).contiguous()
@@ -182,7 +194,10 @@ def causal_conv1d_fn(
         pad_slot_id=int(pad_slot_id), null_block_id=0 if null_block_id is None else int(null_block_id),
         has_null_block=0 if null_block_id is None else 1, W=W,
         x_dtype=_fdt(x, "x"), w_dtype=_fdt(w, "weight"), state_dtype=_fdt(conv_states, "conv_states"),
-        qsl_dtype=_IDT[qsl.dtype], idx_dtype=idx_dt, activation=_act(activation))
+        qsl_dtype=_IDT[qsl.dtype], idx_dtype=idx_dt, activation=_act(activation),
+        block_idx_first=_ptr(blocks[0]), block_idx_last=_ptr(blocks[1]), initial_state_idx=_ptr(blocks[2]),
+        num_computed_tokens=_ptr(blocks[3]), stride_cache_indices=ci.stride(0) if ci is not None else 0,
+        block_size_to_align=int(block_size_to_align or 0), apc_dtype=_lib.GDN_I32)
     with torch.cuda.device(x.device):
         _lib.check(_lib.load().gdn_causal_conv1d_fn(args, _stream(x.device)))
     return out

@@ -120,7 +120,18 @@ struct FwdParams {
   int64_t nblk, upc;  // channel blocks; tokens per CTA run
   int has_null, fn_mode;
   int W, w_dtype, init_dtype, cu_dtype, idx_dtype, act;
+  // fn prefix caching (apc_last non-null): 2-D cache_indices, block states
+  const void *apc_first, *apc_last, *apc_init, *apc_ncomp;
+  int64_t ci_stride, bsz;
+  int apc_dtype;
 };
+
+// Cache line holding sequence n's initial window (fn mode).
+__device__ __forceinline__ int64_t input_line(const FwdParams& p, int64_t n) {
+  if (!p.cache_indices) return n;
+  const int64_t col = p.apc_last ? load_index(p.apc_init, p.apc_dtype, n) : 0;
+  return load_index(p.cache_indices, p.idx_dtype, n * p.ci_stride + col);
+}
 
 // Sequence n with cu[n] <= t < cu[n+1] (the last such n when empty
 // sequences share the boundary).
@@ -219,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 3) conv_fwd_kernel(const FwdParams p
       bool hinit;
       int64_t line = n;
       if (p.fn_mode) {
-        if (p.cache_indices) line = load_index(p.cache_indices, p.idx_dtype, n);
+        line = input_line(p, n);
         skip = (p.has_null && line == p.null_block) || line == p.pad_slot;
         hinit = p.has_init && p.has_init[n];
       } else {
@@ -285,11 +296,16 @@ __global__ void __launch_bounds__(kThreads) conv_state_kernel(const FwdParams p)
   const int64_t c = (static_cast<int64_t>(blockIdx.y) * kThreads + threadIdx.x) * VEC;
   if (c >= p.D) return;
   const int sl = p.W - 1;
-  const int64_t line = p.cache_indices ? load_index(p.cache_indices, p.idx_dtype, s) : s;
+  const int64_t line = input_line(p, s);
   if ((p.has_null && line == p.null_block) || line == p.pad_slot) return;
   const bool hinit = p.has_init && p.has_init[s];
   const int64_t bos = load_index(p.cu, p.cu_dtype, s), L = load_index(p.cu, p.cu_dtype, s + 1) - bos;
   if (L <= 0) return;  // an empty sequence runs no program and leaves its line alone
+  // final state: to the scheduled last block (prefix caching) when the
+  // sequence covers W-1 inputs, else shifted within the initial line
+  const int64_t out_line = p.apc_last && L >= sl
+      ? load_index(p.cache_indices, p.idx_dtype, s * p.ci_stride + load_index(p.apc_last, p.apc_dtype, s))
+      : line;
   const T* x = static_cast<const T*>(p.x);
   float nv[3][VEC];  // W <= 4
 #pragma unroll
@@ -309,7 +325,33 @@ __global__ void __launch_bounds__(kThreads) conv_state_kernel(const FwdParams p)
     if (j >= sl) break;
 #pragma unroll
     for (int e = 0; e < VEC; ++e)
-      st_any(const_cast<void*>(p.init), p.init_dtype, line * p.st_seq + j * p.st_tok + c + e, nv[j][e]);
+      st_any(const_cast<void*>(p.init), p.init_dtype, out_line * p.st_seq + j * p.st_tok + c + e, nv[j][e]);
+  }
+  if (!p.apc_last) return;
+  // prefix caching: the W-1 inputs before each block-aligned block end, one
+  // block per 64-token chunk after the first (kernels.py:519-554)
+  const int64_t first = load_index(p.apc_first, p.apc_dtype, s);
+  const int64_t nb = load_index(p.apc_last, p.apc_dtype, s) - first;
+  const int64_t B = p.bsz;
+  const int64_t comp_off = B - load_index(p.apc_ncomp, p.apc_dtype, s) % B;
+  const int64_t end_off = (L - comp_off) % B;  // remainder with the dividend's sign
+  const int64_t last_full = bos + L - end_off - (end_off == 0 ? B : 0);
+  const int64_t nchunks = (L + 63) / 64;
+  for (int64_t j = 0; j < nb && j + 1 < nchunks; ++j) {
+    const int64_t start = last_full - (nb - j - 1) * B - sl;
+    const int64_t bl = load_index(p.cache_indices, p.idx_dtype, s * p.ci_stride + first + j);
+    for (int u = 0; u < sl; ++u) {
+      float v[VEC];
+      if (start + u >= 0) {
+        ldv<T, VEC>(x + (start + u) * p.sx + c, v);
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) v[e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e)
+        st_any(const_cast<void*>(p.init), p.init_dtype, bl * p.st_seq + u * p.st_tok + c + e, v[e]);
+    }
   }
 }
 
@@ -571,6 +613,18 @@ extern "C" GDN_API int gdn_causal_conv1d_fn(const gdn_conv1d_fn_args* a, void* s
   p.st_seq = a->stride_state_seq; p.st_tok = a->stride_state_tok;
   p.pad_slot = a->pad_slot_id; p.null_block = a->null_block_id; p.has_null = a->has_null_block;
   p.fn_mode = 1; p.W = a->W; p.w_dtype = a->w_dtype; p.init_dtype = a->state_dtype; p.act = a->activation;
+  p.ci_stride = a->cache_indices ? (a->stride_cache_indices > 0 ? a->stride_cache_indices : 1) : 0;
+  if (a->block_idx_last) {
+    if (!a->block_idx_first || !a->initial_state_idx || !a->num_computed_tokens || !a->cache_indices)
+      return fail(GDN_ERR_INVALID, "prefix caching needs cache_indices and all four block arrays");
+    if (!idtype_ok(a->apc_dtype)) return fail(GDN_ERR_INVALID, "block array dtype must be I32 or I64");
+    if (a->block_size_to_align <= 0 || a->block_size_to_align % 64 != 0)
+      return fail(GDN_ERR_INVALID, "block_size_to_align=%lld must be a positive multiple of 64",
+                  (long long)a->block_size_to_align);
+    p.apc_first = a->block_idx_first; p.apc_last = a->block_idx_last;
+    p.apc_init = a->initial_state_idx; p.apc_ncomp = a->num_computed_tokens;
+    p.apc_dtype = a->apc_dtype; p.bsz = a->block_size_to_align;
+  }
   if (p.total == 0 || p.nseq == 0) return GDN_OK;
   cudaError_t e = dispatch_fwd(p, a->x_dtype, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "gdn_causal_conv1d_fn: %s", cudaGetErrorString(e));

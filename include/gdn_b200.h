@@ -250,7 +250,15 @@ GDN_API int gdn_causal_conv1d_fwd(const gdn_conv1d_args* args, void* stream);
  *     bytes (bool) or NULL for none.
  * A sequence whose line equals null_block_id (when has_null_block) or
  * pad_slot_id is skipped: its out tokens are written as zero and its line is
- * left alone.  2 <= W <= 4. */
+ * left alone.  2 <= W <= 4.
+ * Prefix caching (block_idx_last non-NULL; all four block arrays [batch] of
+ * apc_dtype): cache_indices is (batch, blocks) with row stride
+ * stride_cache_indices; the initial window comes from line
+ * cache_indices[s, initial_state_idx[s]], the final state goes to
+ * cache_indices[s, block_idx_last[s]], and the W-1 inputs before each
+ * block_size_to_align-aligned block end j < last - first go to
+ * cache_indices[s, block_idx_first[s] + j] (triton/conv/kernels.py:254-289,
+ * 519-554). */
 typedef struct gdn_conv1d_fn_args {
   const void* x;
   void* out;
@@ -268,6 +276,13 @@ typedef struct gdn_conv1d_fn_args {
   int32_t W;
   int32_t x_dtype, w_dtype, state_dtype, qsl_dtype, idx_dtype;
   int32_t activation;
+  const void* block_idx_first;
+  const void* block_idx_last;
+  const void* initial_state_idx;
+  const void* num_computed_tokens;
+  int64_t stride_cache_indices; /* elements between rows of cache_indices */
+  int64_t block_size_to_align;
+  int32_t apc_dtype;
 } gdn_conv1d_fn_args;
 GDN_API int gdn_causal_conv1d_fn(const gdn_conv1d_fn_args* args, void* stream);
 

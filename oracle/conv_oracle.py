@@ -77,8 +77,16 @@ def causal_conv1d(x, weight, bias=None, residual=None, initial_state=None, activ
     return y
 
 
+def _cmod(a, b):
+    """Integer remainder with the sign of the dividend (the device semantics
+    of ``%`` on signed integers in the reference kernel)."""
+    return a - b * int(a / b)
+
+
 def causal_conv1d_fn(x, weight, bias, conv_states, query_start_loc, cache_indices=None,
-                     has_initial_state=None, activation="silu", pad_slot_id=-1, null_block_id=0):
+                     has_initial_state=None, activation="silu", pad_slot_id=-1, null_block_id=0,
+                     block_idx_first_scheduled_token=None, block_idx_last_scheduled_token=None,
+                     initial_state_idx=None, num_computed_tokens=None, block_size_to_align=0):
     """vLLM-layout forward with a slot-indexed state cache
     (``ops.py:101-349``, ``kernels.py:157-609``).
 
@@ -94,6 +102,16 @@ def causal_conv1d_fn(x, weight, bias, conv_states, query_start_loc, cache_indice
     when the sequence is shorter (``kernels.py:381-484``).  Output token t is
     sum_i ext_{t+i} w_i + bias, then SiLU (``kernels.py:562-608``).
 
+    Prefix caching (``block_idx_last_scheduled_token`` given,
+    ``kernels.py:254-289, 389-417, 519-554``): ``cache_indices`` is
+    ``(batch, blocks)``; the initial window comes from line
+    ``cache_indices[s, initial_state_idx[s]]``, the final state goes to
+    ``cache_indices[s, last[s]]`` (to the initial line when the sequence is
+    shorter than W-1), and block j < last[s] - first[s] (when the sequence
+    has more than j+1 64-token chunks) stores the W-1 inputs before its
+    block-aligned end into ``cache_indices[s, first[s] + j]``; token indices
+    there are absolute and negative ones read zero.
+
     Returns ``(out, new_conv_states, processed)``: out ``(dim, total)`` with
     zeros for skipped sequences, a copy of the updated cache, and a boolean
     mask of processed sequences.
@@ -107,8 +125,15 @@ def causal_conv1d_fn(x, weight, bias, conv_states, query_start_loc, cache_indice
     qsl = [int(c) for c in query_start_loc]
     out = np.zeros_like(x)
     processed = []
+    apc = block_idx_last_scheduled_token is not None
     for s in range(len(qsl) - 1):
-        line = s if cache_indices is None else int(cache_indices[s])
+        if apc:
+            row = [int(c) for c in np.asarray(cache_indices)[s]]
+            line = row[int(initial_state_idx[s])]
+            out_line = row[int(block_idx_last_scheduled_token[s])]
+        else:
+            line = s if cache_indices is None else int(cache_indices[s])
+            out_line = line
         if (null_block_id is not None and line == null_block_id) or line == pad_slot_id:
             processed.append(False)
             continue
@@ -128,7 +153,27 @@ def causal_conv1d_fn(x, weight, bias, conv_states, query_start_loc, cache_indice
         if bias is not None:
             acc += np.asarray(bias, np.float64)[:, None]
         out[:, a:e] = _act(acc, activation)
-        cs[line][:, :sl] = ext[:, L:L + sl]
+        if L >= sl:
+            cs[out_line][:, :sl] = ext[:, L:L + sl]
+        else:
+            cs[line][:, :sl] = ext[:, L:L + sl]
+        if apc:
+            first = int(block_idx_first_scheduled_token[s])
+            nb = int(block_idx_last_scheduled_token[s]) - first
+            B = int(block_size_to_align)
+            comp_off = B - _cmod(int(num_computed_tokens[s]), B)
+            end_off = _cmod(L - comp_off, B)
+            last_full = e - end_off - (B if end_off == 0 else 0)
+            nchunks = -(-L // 64)
+            for j in range(nb):
+                if j + 1 >= nchunks:
+                    break
+                start = last_full - (nb - j - 1) * B - sl
+                blk = np.zeros((dim, sl))
+                for u in range(sl):
+                    if start + u >= 0:
+                        blk[:, u] = x[:, start + u]
+                cs[row[first + j]][:, :sl] = blk
     return out, cs, np.array(processed, bool)
 
 

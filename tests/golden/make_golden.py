@@ -350,6 +350,41 @@ def gen_conv(ref: str):
                             activation=np.str_(act or ""), out=_np(out.contiguous()))
         print("wrote", name)
 
+    # vLLM forward with prefix caching: 2-D cache_indices, block states every
+    # block_size_to_align tokens (kernels.py:254-289, :519-554)
+    dim, W, lens, bsz = 32, 4, [150, 70, 10, 130], 128
+    total = sum(lens)
+    xt = torch.randn(total, dim, generator=g)
+    x = xt.t()
+    w = torch.randn(dim, W, generator=g) * 0.5
+    b = torch.randn(dim, generator=g)
+    lines = 16
+    cs = torch.randn(lines, W - 1, dim, generator=g).transpose(1, 2)
+    cs0 = cs.clone()
+    qsl = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    ci = torch.tensor([[1, 2, 3, 4], [5, 6, 7, 15], [8, 9, 10, 11], [12, 13, 14, 15]], dtype=torch.int32)
+    first = torch.tensor([0, 1, 1, 0], dtype=torch.int32)
+    last = torch.tensor([2, 2, 1, 1], dtype=torch.int32)
+    init_idx = torch.tensor([0, 0, 3, 2], dtype=torch.int32)
+    ncomp = torch.tensor([10, 100, 5, 64], dtype=torch.int32)  # operands of the block arithmetic stay >= 0
+    hi = torch.tensor([1, 1, 0, 1], dtype=torch.bool)
+    nums = [-(-n // 64) for n in lens]
+    mlist = np.repeat(np.arange(len(nums)), nums).astype(np.int32)
+    offs = np.concatenate([np.arange(n) for n in nums]).astype(np.int32)
+    bp, tp = torch.from_numpy(mlist), torch.from_numpy(offs)
+    md = types.SimpleNamespace(batch_ptr=bp, token_chunk_offset_ptr=tp, nums_dict={64: dict(
+        tot=int(sum(nums)), mlist=bp, mlist_len=len(mlist), offsetlist=tp, batch_ptr=bp,
+        token_chunk_offset_ptr=tp)})
+    out = ops.causal_conv1d_fwd_vllm(x, w, b, cs, qsl, ci, hi, "silu", -1, 0, first, last, init_idx, ncomp,
+                                     bsz, metadata=md)
+    np.savez_compressed(os.path.join(HERE, "conv_fn_apc.npz"), x=_np(x.contiguous()), weight=_np(w), bias=_np(b),
+                        conv_states_in=_np(cs0.contiguous()), conv_states_out=_np(cs.contiguous()),
+                        query_start_loc=qsl.numpy(), cache_indices=ci.numpy(), has_initial_state=hi.numpy(),
+                        block_idx_first=first.numpy(), block_idx_last=last.numpy(), initial_state_idx=init_idx.numpy(),
+                        num_computed_tokens=ncomp.numpy(), block_size=np.int64(bsz), activation=np.str_("silu"),
+                        out=_np(out.contiguous()))
+    print("wrote fn_apc")
+
     # decode update: (name, N, D, W, bias, residual, act, x layout)
     upd_cases = [("upd_basic", 5, 48, 4, True, True, "silu", "nd"),
                  ("upd_w3", 3, 40, 3, False, False, None, "n1d"),

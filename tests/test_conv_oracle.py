@@ -20,7 +20,7 @@ def _opt(a):
 
 def test_fixtures_present():
     names = {os.path.basename(f) for f in FIXTURES}
-    for n in ("fla_basic", "fla_init", "fla_varlen", "fn_basic", "fn_short", "fn_null",
+    for n in ("fla_basic", "fla_init", "fla_varlen", "fn_basic", "fn_short", "fn_null", "fn_apc",
               "upd_basic", "upd_w3", "upd_1nd"):
         assert f"conv_{n}.npz" in names
 
@@ -35,9 +35,15 @@ def test_oracle_matches_reference_kernels(path):
                             _opt(d["initial_state"]), act, _opt(d["cu_seqlens"]))
         assert np.abs(y - d["y"]).max() < 1e-5
     elif name.startswith("fn"):
+        apc = {}
+        if "block_idx_last" in d:
+            apc = dict(block_idx_first_scheduled_token=d["block_idx_first"],
+                       block_idx_last_scheduled_token=d["block_idx_last"],
+                       initial_state_idx=d["initial_state_idx"], num_computed_tokens=d["num_computed_tokens"],
+                       block_size_to_align=int(d["block_size"]))
         out, cs, proc = C.causal_conv1d_fn(d["x"], d["weight"], _opt(d["bias"]), d["conv_states_in"],
                                            d["query_start_loc"], d["cache_indices"],
-                                           d["has_initial_state"], act)
+                                           d["has_initial_state"], act, **apc)
         qsl = d["query_start_loc"]
         for s in range(len(qsl) - 1):
             if proc[s]:  # skipped sequences are left unwritten by the reference

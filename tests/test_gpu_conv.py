@@ -58,14 +58,21 @@ def test_matches_reference_golden(ops, path):
         x = _t(d["x"].T.copy()).t()  # channel-last (dim, tokens)
         cs = _t(np.ascontiguousarray(d["conv_states_in"].transpose(0, 2, 1))).transpose(1, 2)
         qsl = torch.tensor(d["query_start_loc"], device="cuda")
+        apc = {}
+        if "block_idx_last" in d:
+            apc = dict(block_idx_first_scheduled_token=torch.tensor(d["block_idx_first"], device="cuda"),
+                       block_idx_last_scheduled_token=torch.tensor(d["block_idx_last"], device="cuda"),
+                       initial_state_idx=torch.tensor(d["initial_state_idx"], device="cuda"),
+                       num_computed_tokens=torch.tensor(d["num_computed_tokens"], device="cuda"),
+                       block_size_to_align=int(d["block_size"]))
         out = ops.causal_conv1d_fn(x, _t(d["weight"]), _t(_opt(d["bias"])), cs, qsl,
                                    torch.tensor(d["cache_indices"], device="cuda"),
-                                   torch.tensor(d["has_initial_state"], device="cuda"), act)
+                                   torch.tensor(d["has_initial_state"], device="cuda"), act, **apc)
         assert out.stride(0) == 1
         o = out.cpu().numpy()
         q = d["query_start_loc"]
         for s in range(len(q) - 1):
-            if d["cache_indices"][s] == 0:  # null block: skipped (zeros here, unwritten there)
+            if np.ndim(d["cache_indices"]) == 1 and d["cache_indices"][s] == 0:  # null block: skipped
                 assert not o[:, q[s]:q[s + 1]].any()
                 continue
             np.testing.assert_allclose(o[:, q[s]:q[s + 1]], d["out"][:, q[s]:q[s + 1]], atol=2e-5, rtol=0)
@@ -246,3 +253,36 @@ def test_errors_match_reference(ops):
     with pytest.raises(ValueError, match="less than or equal to 4"):
         ops.causal_conv1d_fn(x[0].t(), torch.randn(16, 5, device="cuda"), None,
                              torch.zeros(1, 16, 4, device="cuda"), torch.tensor([0, 8], device="cuda"))
+
+
+def test_fn_prefix_caching_random(ops):
+    """Prefix-caching block states against the oracle on random metadata
+    whose block arithmetic stays non-negative (as vLLM schedules it)."""
+    rng = np.random.default_rng(11)
+    dim, W, B = 96, 4, 128
+    lens = [300, 64, 129, 5, 257]
+    total = sum(lens)
+    qsl = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    x = rng.standard_normal((total, dim)).astype(np.float32)
+    w = (rng.standard_normal((dim, W)) * 0.5).astype(np.float32)
+    lines = 40
+    st = rng.standard_normal((lines, W - 1, dim)).astype(np.float32)
+    ci = rng.permutation(np.arange(1, lines)).astype(np.int32)[: len(lens) * 6].reshape(len(lens), 6)
+    first = np.array([0, 1, 2, 0, 1], np.int32)
+    last = np.array([2, 1, 3, 0, 3], np.int32)
+    init = np.array([5, 0, 4, 3, 0], np.int32)
+    ncomp = np.array([100, 64, 70, 0, 120], np.int32)
+    has = np.array([1, 1, 0, 1, 1], bool)
+    cs = _t(st).transpose(1, 2)
+    cs_in = cs.cpu().numpy()
+    out = ops.causal_conv1d_fn(_t(x).t(), _t(w), None, cs, torch.tensor(qsl, device="cuda"),
+                               torch.tensor(ci, device="cuda"), torch.tensor(has, device="cuda"), "silu",
+                               block_idx_first_scheduled_token=torch.tensor(first, device="cuda"),
+                               block_idx_last_scheduled_token=torch.tensor(last, device="cuda"),
+                               initial_state_idx=torch.tensor(init, device="cuda"),
+                               num_computed_tokens=torch.tensor(ncomp, device="cuda"), block_size_to_align=B)
+    ref, cs_ref, _ = C.causal_conv1d_fn(x.T, w, None, cs_in, qsl, ci, has, "silu",
+                                        block_idx_first_scheduled_token=first, block_idx_last_scheduled_token=last,
+                                        initial_state_idx=init, num_computed_tokens=ncomp, block_size_to_align=B)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=2e-5, rtol=0)
+    np.testing.assert_allclose(cs.cpu().numpy(), cs_ref, atol=0, rtol=0)
