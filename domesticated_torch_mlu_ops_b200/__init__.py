@@ -8,6 +8,7 @@ through its C ABI (``include/gdn_b200.h``).
 from .conv import causal_conv1d, causal_conv1d_fn, causal_conv1d_update  # noqa: F401
 from .gdn import (  # noqa: F401
     chunk_gated_delta_rule,
+    chunk_gated_delta_rule_bwd,
     fused_recurrent_gated_delta_rule,
     fused_recurrent_gated_delta_rule_fn,
     solve_tril,
@@ -18,6 +19,7 @@ __all__ = [
     "causal_conv1d_fn",
     "causal_conv1d_update",
     "chunk_gated_delta_rule",
+    "chunk_gated_delta_rule_bwd",
     "fused_recurrent_gated_delta_rule",
     "fused_recurrent_gated_delta_rule_fn",
     "solve_tril",

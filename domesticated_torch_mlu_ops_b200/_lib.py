@@ -27,6 +27,8 @@ EXPORTED = (
     "gdn_chunk_fwd",
     "gdn_chunk_fwd_noalloc",
     "gdn_chunk_check_device_error",
+    "gdn_chunk_bwd_workspace_size",
+    "gdn_chunk_bwd",
     "gdn_fused_recurrent_fwd",
     "gdn_recurrent_plain_fwd",
     "gdn_solve_tril",
@@ -54,6 +56,20 @@ class ChunkArgs(ctypes.Structure):
         ("scale", ctypes.c_float),
         ("use_qk_l2norm", _i32), ("state_v_first", _i32), ("force_generic", _i32),
         ("stage_events", ctypes.POINTER(_vp)), ("n_stage_events", _i32),
+    ]
+
+
+class ChunkBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", _vp), ("k", _vp), ("v", _vp), ("g", _vp), ("beta", _vp),
+        ("initial_state", _vp), ("cu_seqlens", _vp), ("dout", _vp), ("dht", _vp),
+        ("dq", _vp), ("dk", _vp), ("dv", _vp), ("dg", _vp), ("dbeta", _vp), ("dh0", _vp),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("B", _i64), ("T", _i64), ("N", _i64),
+        ("H", _i32), ("HV", _i32), ("K", _i32), ("V", _i32),
+        ("qkv_dtype", _i32), ("cu_dtype", _i32),
+        ("scale", ctypes.c_float),
+        ("use_qk_l2norm", _i32), ("state_v_first", _i32),
     ]
 
 
@@ -140,6 +156,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.gdn_chunk_fwd_noalloc.restype = ctypes.c_int
     lib.gdn_chunk_check_device_error.argtypes = [_vp, _vp]
     lib.gdn_chunk_check_device_error.restype = ctypes.c_int
+    lib.gdn_chunk_bwd_workspace_size.argtypes = [ctypes.POINTER(ChunkBwdArgs)]
+    lib.gdn_chunk_bwd_workspace_size.restype = ctypes.c_size_t
+    lib.gdn_chunk_bwd.argtypes = [ctypes.POINTER(ChunkBwdArgs), _vp]
+    lib.gdn_chunk_bwd.restype = ctypes.c_int
     lib.gdn_fused_recurrent_fwd.argtypes = [ctypes.POINTER(RecurrentArgs), _vp]
     lib.gdn_fused_recurrent_fwd.restype = ctypes.c_int
     lib.gdn_recurrent_plain_fwd.argtypes = [ctypes.POINTER(RecurrentPlainArgs), _vp]

@@ -115,6 +115,31 @@ int gdn_chunk_fwd(const gdn_chunk_args* a, void* stream) {
   return GDN_OK;
 }
 
+size_t gdn_chunk_bwd_workspace_size(const gdn_chunk_bwd_args* a) {
+  if (!a) return fail(GDN_ERR_INVALID, "null args"), 0;
+  if (check_heads(a->B, a->T, a->N, a->H, a->HV, a->K, a->V, a->cu_seqlens, a->cu_dtype)) return 0;
+  if (!qkv_dtype_ok(a->qkv_dtype)) return fail(GDN_ERR_INVALID, "qkv dtype must be F32, BF16 or F16"), 0;
+  return gdn::plan_bwd_workspace(*a).total;
+}
+
+int gdn_chunk_bwd(const gdn_chunk_bwd_args* a, void* stream) {
+  if (!a) return fail(GDN_ERR_INVALID, "null args");
+  int rc = check_heads(a->B, a->T, a->N, a->H, a->HV, a->K, a->V, a->cu_seqlens, a->cu_dtype);
+  if (rc) return rc;
+  if (!qkv_dtype_ok(a->qkv_dtype)) return fail(GDN_ERR_INVALID, "qkv dtype must be F32, BF16 or F16");
+  const int64_t Ttot = a->B * a->T;
+  if (Ttot > 0 && (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->dout || !a->dq || !a->dk || !a->dv ||
+                   !a->dg || !a->dbeta))
+    return fail(GDN_ERR_INVALID, "q, k, v, g, beta, dout, dq, dk, dv, dg and dbeta must be non-null");
+  const size_t need = gdn::plan_bwd_workspace(*a).total;
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", a->workspace_bytes, need);
+  if (a->N == 0) return GDN_OK;
+  cudaError_t e = gdn::launch_chunk_bwd(*a, gdn::plan_bwd_workspace(*a), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_chunk_bwd");
+  return GDN_OK;
+}
+
 int gdn_chunk_check_device_error(void* workspace, void* stream) {
   if (!workspace) return fail(GDN_ERR_INVALID, "null workspace");
   int32_t h[4] = {0, 0, 0, 0};

@@ -1,0 +1,613 @@
+// Backward of the chunked gated delta-rule forward: the autograd backward of
+// chunk_gated_delta_rule (triton/fla/chunk.py:188-251 ChunkGatedDeltaRuleFunction,
+// stages at chunk.py:76-186: recompute w, u, h; chunk_bwd_dv_local;
+// chunk_gated_delta_rule_bwd_dhu; chunk_bwd_dqkwg; prepare_wy_repr_bwd;
+// reverse chunk-local cumsum of dg).
+//
+// fp32 SIMT kernels over the fp32 intermediates that the generic forward
+// leaves in the workspace (chunk-local cumsum G, normalised q/k, W, U, v_new
+// and the state h at every chunk start).  Per chunk of L <= 64 tokens and
+// v-head, with Gam_i = exp(G_i), gam = Gam_{L-1}, D_ij = exp(G_i - G_j),
+// c_i = gam / Gam_i, S = Q K^T, M = causal mask (j <= i):
+//   A = tril_strict(diag(b) D * K K^T), T = (I + A)^-1
+//   W = T diag(b Gam) K, U = T diag(b) V, v = U - W h
+//   o = scale (diag(Gam) Q h + (M * D * S) v),  h' = gam h + K^T diag(c) v
+// Given dO and dh' (the gradient of the state after the chunk):
+//   bwd_state_kernel (reverse over a sequence's chunks):
+//     dv = scale (M * D * S)^T dO + diag(c) K dh'
+//     dh = gam dh' + scale Q^T diag(Gam) dO - W^T dv          (dh0 at the first chunk)
+//   bwd_dqkw_kernel (per chunk and v-head):
+//     dP = scale M * D * (dO v^T)
+//     dQ = scale diag(Gam) dO h^T + dP K,  dK = dP^T Q + diag(c) v dh'^T,  dW = -dv h^T
+//   bwd_wy_kernel (per chunk and v-head):
+//     dR_w = T^T dW, dR_u = T^T dv, dT = dW R_w^T + dv R_u^T (R_w = diag(b Gam) K,
+//     R_u = diag(b) V), dA = -T^T dT T^T on the strictly lower triangle,
+//     dK += diag(b Gam) dR_w + (dS + dS^T) K with dS = diag(b) D * dA, dV = diag(b) dR_u
+//   dG collects every use of G (through Gam, gam, c, D) and db every use of b;
+//   bwd_qk_kernel sums dq, dk over the v-heads of each q/k head (then the L2
+//   norm backward when the forward normalised q, k); bwd_dg_kernel turns dG
+//   into dg by a reverse cumsum within each chunk (G is a forward cumsum of g).
+
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+#include "solve_tril.cuh"
+
+namespace gdn {
+namespace {
+
+constexpr int kT = 256;                     // threads per CTA
+constexpr int LD = 129;                     // row stride of 64 x 128 fp32 tiles
+constexpr int kP = 65;                      // row stride of 64 x 64 fp32 tiles
+constexpr int kStage = 64 * 17 + 16 * 129;  // gemm staging floats
+constexpr int kVS = 32;                     // V columns per bwd_state_kernel CTA
+
+// C[i][n] (= or +=) alpha * sum_{k < Kd} A(i, k) B(k, n) for i < 64, n < N.
+// A(i, k) = a[i*asi + k*ask] (zero for i >= ma); B(k, n) = b[k*bsk + n*bsn]
+// (zero for n >= nb); operands fp32 or 16-bit, in global or shared memory.
+// C (fp32, shared or global, row stride ldc) is stored for rows i < mc.  Each
+// thread owns a 4 x NJ micro-tile (columns tc + 16 j); operands are staged 16
+// deep through `st`.  All kT threads call it; it starts and ends with a barrier.
+template <int NJ, bool ACC, typename TA, typename TB>
+__device__ __forceinline__ void gemm_tile(float* C, int64_t ldc, int mc, int N, int Kd, const TA* a,
+                                          int64_t asi, int64_t ask, int ma, const TB* b, int64_t bsk,
+                                          int64_t bsn, int nb, float alpha, float* st) {
+  constexpr int NC = 16 * NJ;
+  float* As = st;            // [64][17]
+  float* Bs = st + 64 * 17;  // [16][129]
+  const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  float acc[4][NJ];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) acc[r][j] = 0.f;
+  __syncthreads();
+  for (int k0 = 0; k0 < Kd; k0 += 16) {
+    for (int e = tid; e < 64 * 16; e += kT) {
+      const int i = e >> 4, kk = e & 15, k = k0 + kk;
+      As[i * 17 + kk] = (i < ma && k < Kd) ? to_f<TA>(a[i * asi + k * ask]) : 0.f;
+    }
+    for (int e = tid; e < 16 * NC; e += kT) {
+      const int kk = e / NC, n = e % NC, k = k0 + kk;
+      Bs[kk * 129 + n] = (k < Kd && n < nb) ? to_f<TB>(b[k * bsk + n * bsn]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float av[4], bv[NJ];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) av[r] = As[(tr * 4 + r) * 17 + kk];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) bv[j] = Bs[kk * 129 + tc + 16 * j];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) acc[r][j] = fmaf(av[r], bv[j], acc[r][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = tr * 4 + r;
+    if (i >= mc) continue;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int n = tc + 16 * j;
+      if (n < N) {
+        float* c = C + i * ldc + n;
+        *c = ACC ? *c + alpha * acc[r][j] : alpha * acc[r][j];
+      }
+    }
+  }
+  __syncthreads();
+}
+
+template <bool ACC, typename TA, typename TB>
+__device__ __forceinline__ void gemm(float* C, int64_t ldc, int mc, int N, int Kd, const TA* a, int64_t asi,
+                                     int64_t ask, int ma, const TB* b, int64_t bsk, int64_t bsn, int nb,
+                                     float alpha, float* st) {
+  if (N <= 64) gemm_tile<4, ACC>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
+  else gemm_tile<8, ACC>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
+}
+
+// Block-wide sum of one value per thread (returned to every thread).
+__device__ __forceinline__ float block_sum(float x, float* red) {
+  x = group_sum<32>(x);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kT / 32; ++i) t += red[i];
+  __syncthreads();
+  return t;
+}
+
+struct BwdPtrs {
+  const int64_t* coff;                        // chunk offsets [N + 1]
+  const float *gc, *qn, *kn, *w, *vnew, *hs;  // forward intermediates
+  float *dvn, *dhn, *dqh, *dkh, *dw, *dG;     // backward intermediates
+};
+
+// Reverse recurrence over one sequence's chunks for one (v-head, 32-column
+// slice of V): stores dh' per chunk and dv (of v_new), then dh0.
+template <typename T>
+__global__ void __launch_bounds__(kT) bwd_state_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
+  extern __shared__ float sm[];
+  const int K = p.K, V = p.V;
+  float* qc = sm;               // [64][LD]
+  float* kc = qc + 64 * LD;     // [64][LD]
+  float* wc = kc + 64 * LD;     // [64][LD]
+  float* P = wc + 64 * LD;      // [64][kP] M * D * Q K^T
+  float* dh = P + 64 * kP;      // [K][kVS]
+  float* dO = dh + 128 * kVS;   // [64][kVS]
+  float* dvs = dO + 64 * kVS;   // [64][kVS]
+  float* gcs = dvs + 64 * kVS;  // [64]
+  float* st = gcs + 64;         // gemm staging
+  const int64_t n = blockIdx.x;
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  const int v0 = blockIdx.z * kVS;
+  const int tid = threadIdx.x;
+  const int64_t rowQ = static_cast<int64_t>(p.H) * K, rowV = static_cast<int64_t>(p.HV) * V,
+                rowK = static_cast<int64_t>(p.HV) * K;
+  const T* dout = static_cast<const T*>(p.dout);
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  for (int e = tid; e < K * kVS; e += kT) {
+    const int kk = e / kVS, vv = v0 + e % kVS;
+    float x = 0.f;
+    if (p.dht && vv < V)
+      x = p.state_v_first ? p.dht[((n * p.HV + hv) * V + vv) * K + kk] : p.dht[((n * p.HV + hv) * K + kk) * V + vv];
+    dh[e] = x;
+  }
+  const int64_t nch = eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0;
+  for (int64_t lc = nch - 1; lc >= 0; --lc) {
+    const int64_t s = bos + lc * kChunk;
+    const int L = static_cast<int>(min64(kChunk, eos - s));
+    const int64_t cidx = w.coff[n] + lc;
+    __syncthreads();  // dh of the previous iteration is complete
+    float* dhn = w.dhn + (cidx * p.HV + hv) * static_cast<int64_t>(K) * V;
+    for (int e = tid; e < K * kVS; e += kT) {
+      const int kk = e / kVS, vv = v0 + e % kVS;
+      if (vv < V) dhn[kk * V + vv] = dh[e];
+    }
+    for (int e = tid; e < 64 * K; e += kT) {
+      const int i = e / K, kk = e % K;
+      const bool ok = i < L;
+      qc[i * LD + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
+      kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
+      wc[i * LD + kk] = ok ? w.w[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] : 0.f;
+    }
+    for (int e = tid; e < 64 * kVS; e += kT) {
+      const int i = e / kVS, vv = v0 + e % kVS;
+      dO[e] = (i < L && vv < V) ? to_f<T>(dout[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv]) : 0.f;
+    }
+    if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
+    gemm<false>(P, kP, 64, 64, K, qc, LD, 1, 64, kc, 1, LD, 64, 1.f, st);  // Q K^T
+    for (int e = tid; e < 64 * 64; e += kT) {
+      const int i = e >> 6, j = e & 63;
+      P[i * kP + j] = (i < L && j <= i) ? P[i * kP + j] * expf(gcs[i] - gcs[j]) : 0.f;
+    }
+    __syncthreads();
+    const float glast = gcs[L - 1], eg = expf(glast);
+    for (int e = tid; e < 64 * kVS; e += kT) {  // dv = scale P^T dO + diag(c) K dh'
+      const int i = e / kVS, c = e % kVS;
+      float x = 0.f;
+      if (i < L) {
+        float a = 0.f, b = 0.f;
+        for (int ii = i; ii < L; ++ii) a = fmaf(P[ii * kP + i], dO[ii * kVS + c], a);
+        for (int kk = 0; kk < K; ++kk) b = fmaf(kc[i * LD + kk], dh[kk * kVS + c], b);
+        x = scale * a + expf(glast - gcs[i]) * b;
+      }
+      dvs[e] = x;
+    }
+    __syncthreads();
+    for (int e = tid; e < 64 * kVS; e += kT) {
+      const int i = e / kVS, vv = v0 + e % kVS;
+      if (i < L && vv < V) w.dvn[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv] = dvs[e];
+      dO[e] *= scale * expf(gcs[i]);  // scale diag(Gam) dO (rows >= L are zero)
+    }
+    __syncthreads();
+    for (int e = tid; e < K * kVS; e += kT) {  // dh = gam dh' + scale Q^T diag(Gam) dO - W^T dv
+      const int kk = e / kVS, c = e % kVS;
+      float a = 0.f;
+      for (int i = 0; i < L; ++i) {
+        a = fmaf(qc[i * LD + kk], dO[i * kVS + c], a);
+        a = fmaf(-wc[i * LD + kk], dvs[i * kVS + c], a);
+      }
+      dh[e] = fmaf(eg, dh[e], a);
+    }
+  }
+  __syncthreads();
+  if (p.dh0) {
+    for (int e = tid; e < K * kVS; e += kT) {
+      const int kk = e / kVS, vv = v0 + e % kVS;
+      if (vv >= V) continue;
+      if (p.state_v_first) p.dh0[((n * p.HV + hv) * V + vv) * K + kk] = dh[e];
+      else p.dh0[((n * p.HV + hv) * K + kk) * V + vv] = dh[e];
+    }
+  }
+}
+
+// dq, dk (per v-head, fp32), dW and the dG terms of the output and state
+// paths for one (chunk, v-head).
+template <typename T>
+__global__ void __launch_bounds__(kT) bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
+  extern __shared__ float sm[];
+  const int K = p.K, V = p.V;
+  float* qc = sm;               // [64][LD]
+  float* kc = qc + 64 * LD;     // [64][LD]
+  float* dq = kc + 64 * LD;     // [64][LD]
+  float* dk = dq + 64 * LD;     // [64][LD]
+  float* dP = dk + 64 * LD;     // [64][kP]
+  float* Sq = dP + 64 * kP;     // [64][kP] Q K^T
+  float* gcs = Sq + 64 * kP;    // [64]
+  float* dG = gcs + 64;         // [64]
+  float* red = dG + 64;         // [32]
+  float* st = red + 32;         // gemm staging
+  int64_t n, lc;
+  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int64_t s = bos + lc * kChunk;
+  const int L = static_cast<int>(min64(kChunk, eos - s));
+  const int64_t cidx = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int64_t rowQ = static_cast<int64_t>(p.H) * K, rowV = static_cast<int64_t>(p.HV) * V,
+                rowK = static_cast<int64_t>(p.HV) * K;
+  const float* hst = w.hs + (cidx * p.HV + hv) * static_cast<int64_t>(K) * V;   // h [K][V]
+  const float* dhn = w.dhn + (cidx * p.HV + hv) * static_cast<int64_t>(K) * V;  // dh' [K][V]
+  const float* vn = w.vnew + s * rowV + static_cast<int64_t>(hv) * V;          // rows, stride rowV
+  const float* dvn = w.dvn + s * rowV + static_cast<int64_t>(hv) * V;
+  const T* dO = static_cast<const T*>(p.dout) + s * rowV + static_cast<int64_t>(hv) * V;
+  for (int e = tid; e < 64 * K; e += kT) {
+    const int i = e / K, kk = e % K;
+    const bool ok = i < L;
+    qc[i * LD + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
+    kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
+  }
+  if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
+  gemm<false>(Sq, kP, 64, 64, K, qc, LD, 1, 64, kc, 1, LD, 64, 1.f, st);
+  gemm<false>(dP, kP, 64, 64, V, dO, rowV, 1, L, vn, 1, rowV, L, 1.f, st);  // dO v^T
+  for (int e = tid; e < 64 * 64; e += kT) {
+    const int i = e >> 6, j = e & 63;
+    dP[i * kP + j] = (i < L && j <= i) ? scale * expf(gcs[i] - gcs[j]) * dP[i * kP + j] : 0.f;
+  }
+  gemm<false>(dq, LD, 64, K, V, dO, rowV, 1, L, hst, 1, V, K, scale, st);  // scale dO h^T
+  const float glast = gcs[L - 1], eg = expf(glast);
+  if (tid < 64) {  // dQ = diag(Gam) (scale dO h^T); dG_i = q_i . dQ_i
+    const float gi = tid < L ? expf(gcs[tid]) : 0.f;
+    float a = 0.f;
+    for (int kk = 0; kk < K; ++kk) {
+      const float x = gi * dq[tid * LD + kk];
+      dq[tid * LD + kk] = x;
+      a = fmaf(qc[tid * LD + kk], x, a);
+    }
+    float b = 0.f;  // P path: sum_j dP_ij S_ij - sum_i dP_ij S_ij
+    for (int j = 0; j < 64; ++j) b += dP[tid * kP + j] * Sq[tid * kP + j] - dP[j * kP + tid] * Sq[j * kP + tid];
+    dG[tid] = a + b;
+  }
+  gemm<true>(dq, LD, 64, K, 64, dP, kP, 1, 64, kc, LD, 1, K, 1.f, st);   // + dP K
+  gemm<false>(dk, LD, 64, K, V, vn, rowV, 1, L, dhn, 1, V, K, 1.f, st);  // v dh'^T
+  float part = 0.f;
+  for (int e = tid; e < K * V; e += kT) part = fmaf(dhn[e], hst[e], part);
+  const float hh = block_sum(part, red);  // <dh', h>
+  float E = 0.f;
+  if (tid < 64) {  // dK = diag(c) v dh'^T; E_i = k_i . dK_i
+    const float c = tid < L ? expf(glast - gcs[tid]) : 0.f;
+    for (int kk = 0; kk < K; ++kk) {
+      const float x = c * dk[tid * LD + kk];
+      dk[tid * LD + kk] = x;
+      E = fmaf(kc[tid * LD + kk], x, E);
+    }
+  }
+  const float Esum = block_sum(tid < 64 ? E : 0.f, red);
+  if (tid < 64) dG[tid] += (tid == L - 1 ? eg * hh + Esum : 0.f) - E;
+  gemm<true>(dk, LD, 64, K, 64, dP, 1, kP, 64, qc, LD, 1, K, 1.f, st);  // + dP^T Q
+  // dW = -dv h^T straight to the workspace
+  gemm<false>(w.dw + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, V, dvn, rowV, 1, L, hst, 1, V, K,
+              -1.f, st);
+  for (int e = tid; e < L * K; e += kT) {
+    const int i = e / K, kk = e % K;
+    w.dqh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dq[i * LD + kk];
+    w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dk[i * LD + kk];
+  }
+  if (tid < L) w.dG[(s + tid) * p.HV + hv] = dG[tid];
+}
+
+// Backward through W = T diag(b Gam) K and U = T diag(b) V for one
+// (chunk, v-head): dv, db, and the dK and dG terms of the WY form.
+template <typename T>
+__global__ void __launch_bounds__(kT) bwd_wy_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w) {
+  extern __shared__ float sm[];
+  const int K = p.K, V = p.V;
+  float* Tm = sm;                 // [64][kTS] (16-byte aligned)
+  float* Zs = Tm + 64 * kTS;      // solve scratch (16-byte aligned)
+  float* kc = Zs + kTrilScratch;  // [64][LD]
+  float* b1 = kc + 64 * LD;       // [64][LD] dW, then dR_u
+  float* b2 = b1 + 64 * LD;       // [64][LD] dR_w, then dK
+  float* Sk = b2 + 64 * LD;       // [64][kP] K K^T
+  float* Am = Sk + 64 * kP;       // [64][kP] A, then dS
+  float* dT = Am + 64 * kP;       // [64][kP] dT, then dA
+  float* tm = dT + 64 * kP;       // [64][kP]
+  float* gcs = tm + 64 * kP;      // [64]
+  float* bs = gcs + 64;           // [64] beta
+  float* cw = bs + 64;            // [64] beta Gam
+  float* db = cw + 64;            // [64]
+  float* dG = db + 64;            // [64]
+  float* st = dG + 64;            // gemm staging
+  int64_t n, lc;
+  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int64_t s = bos + lc * kChunk;
+  const int L = static_cast<int>(min64(kChunk, eos - s));
+  const int tid = threadIdx.x;
+  const int64_t rowQ = static_cast<int64_t>(p.H) * K, rowV = static_cast<int64_t>(p.HV) * V,
+                rowK = static_cast<int64_t>(p.HV) * K;
+  const T* vin = static_cast<const T*>(p.v) + s * rowV + static_cast<int64_t>(hv) * V;
+  const float* dvn = w.dvn + s * rowV + static_cast<int64_t>(hv) * V;
+  const float* dwp = w.dw + s * rowK + static_cast<int64_t>(hv) * K;
+  for (int e = tid; e < 64 * K; e += kT) {
+    const int i = e / K, kk = e % K;
+    const bool ok = i < L;
+    kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
+    b1[i * LD + kk] = ok ? dwp[i * rowK + kk] : 0.f;
+  }
+  if (tid < 64) {
+    const bool ok = tid < L;
+    const float g = ok ? w.gc[(s + tid) * p.HV + hv] : 0.f;
+    const float bt = ok ? p.beta[(s + tid) * p.HV + hv] : 0.f;
+    gcs[tid] = g;
+    bs[tid] = bt;
+    cw[tid] = ok ? bt * expf(g) : 0.f;
+  }
+  gemm<false>(Sk, kP, 64, 64, K, kc, LD, 1, 64, kc, 1, LD, 64, 1.f, st);  // K K^T
+  for (int e = tid; e < 64 * 64; e += kT) {
+    const int i = e >> 6, j = e & 63;
+    Am[i * kP + j] = (i < L && j < i) ? bs[i] * expf(gcs[i] - gcs[j]) * Sk[i * kP + j] : 0.f;
+  }
+  __syncthreads();
+  solve_tril64_nt<kT>(Am, Tm, Zs);  // T = (I + A)^-1
+  gemm<false>(dT, kP, 64, 64, K, b1, LD, 1, 64, kc, 1, LD, 64, 1.f, st);     // dW K^T
+  gemm<false>(tm, kP, 64, 64, V, dvn, rowV, 1, L, vin, 1, rowV, L, 1.f, st);  // dv V^T
+  for (int e = tid; e < 64 * 64; e += kT) {
+    const int i = e >> 6, j = e & 63;
+    dT[i * kP + j] = dT[i * kP + j] * cw[j] + tm[i * kP + j] * bs[j];
+  }
+  gemm<false>(b2, LD, 64, K, 64, Tm, 1, kTS, 64, b1, LD, 1, K, 1.f, st);     // dR_w = T^T dW
+  gemm<false>(b1, LD, 64, V, L, Tm, 1, kTS, 64, dvn, rowV, 1, V, 1.f, st);   // dR_u = T^T dv
+  gemm<false>(tm, kP, 64, 64, 64, dT, kP, 1, 64, Tm, 1, kTS, 64, 1.f, st);   // dT T^T
+  gemm<false>(dT, kP, 64, 64, 64, Tm, 1, kTS, 64, tm, kP, 1, 64, -1.f, st);  // dA = -T^T (dT T^T)
+  T* dv = static_cast<T*>(p.dv) + s * rowV + static_cast<int64_t>(hv) * V;
+  for (int e = tid; e < L * V; e += kT) {
+    const int i = e / V, vv = e % V;
+    dv[i * rowV + vv] = from_f<T>(bs[i] * b1[i * LD + vv]);
+  }
+  if (tid < 64) {
+    const int i = tid;
+    float dbi = 0.f, dgi = 0.f;
+    if (i < L) {
+      float a = 0.f;  // U path: V_i . dR_u_i
+      for (int vv = 0; vv < V; ++vv) a = fmaf(to_f<T>(vin[i * rowV + vv]), b1[i * LD + vv], a);
+      float r = 0.f;  // W path: K_i . dR_w_i
+      for (int kk = 0; kk < K; ++kk) r = fmaf(kc[i * LD + kk], b2[i * LD + kk], r);
+      dbi = a + expf(gcs[i]) * r;
+      dgi = cw[i] * r;
+      float t = 0.f;  // A path: sum_j dA_ij D_ij S_ij
+      for (int j = 0; j < i; ++j) t += dT[i * kP + j] * expf(gcs[i] - gcs[j]) * Sk[i * kP + j];
+      dbi += t;
+    }
+    db[i] = dbi;
+    dG[i] = dgi;
+  }
+  __syncthreads();
+  for (int e = tid; e < 64 * 64; e += kT) {  // dS = diag(b) D * dA (strictly lower, rows < L)
+    const int i = e >> 6, j = e & 63;
+    Am[i * kP + j] = (i < L && j < i) ? bs[i] * expf(gcs[i] - gcs[j]) * dT[i * kP + j] : 0.f;
+  }
+  for (int e = tid; e < 64 * K; e += kT) {  // dK = diag(b Gam) dR_w
+    const int i = e / K, kk = e % K;
+    b2[i * LD + kk] *= cw[i];
+  }
+  __syncthreads();
+  if (tid < 64) {  // D path of A: F = dS * S; dG_i += sum_j F_ij - sum_j F_ji
+    float f = 0.f;
+    for (int j = 0; j < 64; ++j) f += Am[tid * kP + j] * Sk[tid * kP + j] - Am[j * kP + tid] * Sk[j * kP + tid];
+    dG[tid] += f;
+  }
+  gemm<true>(b2, LD, 64, K, 64, Am, kP, 1, 64, kc, LD, 1, K, 1.f, st);  // + dS K
+  gemm<true>(b2, LD, 64, K, 64, Am, 1, kP, 64, kc, LD, 1, K, 1.f, st);  // + dS^T K
+  for (int e = tid; e < L * K; e += kT) {
+    const int i = e / K, kk = e % K;
+    w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] += b2[i * LD + kk];
+  }
+  if (tid < L) {
+    p.dbeta[(s + tid) * p.HV + hv] = db[tid];
+    w.dG[(s + tid) * p.HV + hv] += dG[tid];
+  }
+}
+
+// One warp per (token, q/k head): dq and dk summed over the head's v-heads
+// in a fixed order, then the L2-norm backward dx = r (dy - y (y . dy)) with
+// y = x r, r = 1 / sqrt(sum(x^2) + 1e-6) when the forward normalised q, k.
+template <typename T>
+__global__ void bwd_qk_kernel(const gdn_chunk_bwd_args p, const float* __restrict__ dqh,
+                              const float* __restrict__ dkh, int64_t rows) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int K = p.K, G = p.HV / p.H;
+  const int64_t t = row / p.H;
+  const int hh = static_cast<int>(row % p.H);
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+    const float* src = which ? dkh : dqh;
+    const T* x = static_cast<const T*>(which ? p.k : p.q) + row * K;
+    T* out = static_cast<T*>(which ? p.dk : p.dq) + row * K;
+    float dy[4], xv[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int kk = lane + 32 * u;
+      float a = 0.f, xx = 0.f;
+      if (kk < K) {
+        for (int j = 0; j < G; ++j) a += src[(t * p.HV + hh * G + j) * K + kk];
+        xx = to_f<T>(x[kk]);
+      }
+      dy[u] = a;
+      xv[u] = xx;
+      ss = fmaf(xx, xx, ss);
+    }
+    if (p.use_qk_l2norm) {
+      ss = group_sum<32>(ss);
+      const float r = 1.f / sqrtf(ss + 1e-6f);
+      float dot = 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) dot = fmaf(xv[u] * r, dy[u], dot);
+      dot = group_sum<32>(dot);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) dy[u] = r * (dy[u] - xv[u] * r * dot);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int kk = lane + 32 * u;
+      if (kk < K) out[kk] = from_f<T>(dy[u]);
+    }
+  }
+}
+
+// dg = reverse cumsum of dG within each chunk; one thread per (chunk, v-head).
+__global__ void bwd_dg_kernel(const gdn_chunk_bwd_args p, const int64_t* __restrict__ coff,
+                              const float* __restrict__ dG) {
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nchunks = coff[p.N];
+  if (e >= nchunks * p.HV) return;
+  const int64_t c = e / p.HV;
+  const int hv = static_cast<int>(e % p.HV);
+  int64_t n, lc;
+  if (!locate_chunk(coff, p.N, c, n, lc)) return;
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int64_t s = bos + lc * kChunk;
+  const int L = static_cast<int>(min64(kChunk, eos - s));
+  float acc = 0.f;
+  for (int i = L - 1; i >= 0; --i) {
+    acc += dG[(s + i) * p.HV + hv];
+    p.dg[(s + i) * p.HV + hv] = acc;
+  }
+}
+
+constexpr size_t kStateSmem = sizeof(float) * (3 * 64 * LD + 64 * kP + 128 * kVS + 2 * 64 * kVS + 64 + kStage);
+constexpr size_t kDqkwSmem = sizeof(float) * (4 * 64 * LD + 2 * 64 * kP + 2 * 64 + 32 + kStage);
+constexpr size_t kWySmem =
+    sizeof(float) * (64 * kTS + kTrilScratch + 3 * 64 * LD + 4 * 64 * kP + 5 * 64 + kStage);
+static_assert(kWySmem <= 227 * 1024, "bwd_wy_kernel shared memory");
+static_assert((64 * kTS) % 4 == 0, "solve scratch must stay 16-byte aligned");
+
+gdn_chunk_args forward_args(const gdn_chunk_bwd_args& b) {
+  gdn_chunk_args a{};
+  a.q = b.q;
+  a.k = b.k;
+  a.v = b.v;
+  a.g = b.g;
+  a.beta = b.beta;
+  a.initial_state = b.initial_state;
+  a.cu_seqlens = b.cu_seqlens;
+  a.workspace = b.workspace;
+  a.workspace_bytes = b.workspace_bytes;
+  a.B = b.B;
+  a.T = b.T;
+  a.N = b.N;
+  a.H = b.H;
+  a.HV = b.HV;
+  a.K = b.K;
+  a.V = b.V;
+  a.qkv_dtype = b.qkv_dtype;
+  a.cu_dtype = b.cu_dtype;
+  a.scale = b.scale;
+  a.use_qk_l2norm = b.use_qk_l2norm;
+  a.state_v_first = b.state_v_first;
+  a.force_generic = 1;
+  return a;
+}
+
+template <typename T>
+cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStream_t s) {
+  const gdn_chunk_args a = forward_args(b);
+  cudaError_t e = launch_chunk_generic_recompute(a, ws.fwd, s);
+  if (e != cudaSuccess) return e;
+  char* base = static_cast<char*>(b.workspace);
+  BwdPtrs w;
+  w.coff = reinterpret_cast<const int64_t*>(base + ws.fwd.chunk_offsets);
+  w.gc = reinterpret_cast<const float*>(base + ws.fwd.gc);
+  w.qn = reinterpret_cast<const float*>(base + ws.fwd.qn);
+  w.kn = reinterpret_cast<const float*>(base + ws.fwd.kn);
+  w.w = reinterpret_cast<const float*>(base + ws.fwd.w);
+  w.vnew = reinterpret_cast<const float*>(base + ws.fwd.vnew);
+  w.hs = reinterpret_cast<const float*>(base + ws.fwd.hs);
+  w.dvn = reinterpret_cast<float*>(base + ws.dvn);
+  w.dhn = reinterpret_cast<float*>(base + ws.dhn);
+  w.dqh = reinterpret_cast<float*>(base + ws.dqh);
+  w.dkh = reinterpret_cast<float*>(base + ws.dkh);
+  w.dw = reinterpret_cast<float*>(base + ws.dw);
+  w.dG = reinterpret_cast<float*>(base + ws.dG);
+  const int64_t Ttot = b.B * b.T;
+  const int64_t nc = chunk_upper_bound(Ttot, b.N);
+  const float scale = b.scale > 0.f ? b.scale : 1.f / sqrtf(static_cast<float>(b.K));
+  if ((e = cudaFuncSetAttribute(bwd_state_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kStateSmem))) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(bwd_dqkw_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kDqkwSmem))) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(bwd_wy_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kWySmem))) != cudaSuccess) return e;
+  note_launch();
+  bwd_state_kernel<T><<<dim3(static_cast<unsigned>(b.N), b.HV, (b.V + kVS - 1) / kVS), kT, kStateSmem, s>>>(
+      b, w, scale);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (nc > 0) {
+    note_launch(2);
+    bwd_dqkw_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kDqkwSmem, s>>>(b, w, scale);
+    bwd_wy_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kWySmem, s>>>(b, w);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  const int64_t rows = Ttot * b.H;
+  if (rows > 0) {
+    note_launch(2);
+    bwd_qk_kernel<T><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(b, w.dqh, w.dkh, rows);
+    const int64_t ng = nc * b.HV;
+    bwd_dg_kernel<<<static_cast<unsigned>((ng + 255) / 256), 256, 0, s>>>(b, w.coff, w.dG);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace
+
+BwdWorkspace plan_bwd_workspace(const gdn_chunk_bwd_args& b) {
+  auto al = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  BwdWorkspace w{};
+  w.fwd = plan_generic_workspace(forward_args(b));
+  const int64_t Ttot = b.B * b.T;
+  const int64_t nc = chunk_upper_bound(Ttot, b.N);
+  size_t o = w.fwd.total;
+  w.dvn = o; o += al(sizeof(float) * Ttot * b.HV * b.V);
+  w.dhn = o; o += al(sizeof(float) * nc * b.HV * b.K * b.V);
+  w.dqh = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
+  w.dkh = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
+  w.dw = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
+  w.dG = o; o += al(sizeof(float) * Ttot * b.HV);
+  w.total = o;
+  return w;
+}
+
+cudaError_t launch_chunk_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStream_t s) {
+  switch (b.qkv_dtype) {
+    case GDN_F32: return run_bwd<float>(b, ws, s);
+    case GDN_BF16: return run_bwd<__nv_bfloat16>(b, ws, s);
+    case GDN_F16: return run_bwd<__half>(b, ws, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace gdn

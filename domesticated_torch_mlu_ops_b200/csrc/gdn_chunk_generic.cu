@@ -305,7 +305,8 @@ ChunkWorkspace plan_generic_workspace(const gdn_chunk_args& a) {
 }
 
 template <typename T>
-static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s) {
+static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s,
+                               bool with_output) {
   char* base = static_cast<char*>(a.workspace);
   GenericPtrs w;
   w.coff = reinterpret_cast<const int64_t*>(base + ws.chunk_offsets);
@@ -353,7 +354,7 @@ static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws
   chunk_state_kernel<<<dim3(static_cast<unsigned>(a.N), a.HV, (a.V + kStateCols - 1) / kStateCols),
                        256, st_smem, s>>>(a, w);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  if (nc > 0) {
+  if (nc > 0 && with_output) {
     hk.pre(s);
     chunk_out_kernel<T><<<dim3(static_cast<unsigned>(nc), a.HV), 256, out_smem, s>>>(a, w, scale);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -364,9 +365,18 @@ static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws
 
 cudaError_t launch_chunk_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s) {
   switch (a.qkv_dtype) {
-    case GDN_F32: return run_generic<float>(a, ws, s);
-    case GDN_BF16: return run_generic<__nv_bfloat16>(a, ws, s);
-    case GDN_F16: return run_generic<__half>(a, ws, s);
+    case GDN_F32: return run_generic<float>(a, ws, s, true);
+    case GDN_BF16: return run_generic<__nv_bfloat16>(a, ws, s, true);
+    case GDN_F16: return run_generic<__half>(a, ws, s, true);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_chunk_generic_recompute(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s) {
+  switch (a.qkv_dtype) {
+    case GDN_F32: return run_generic<float>(a, ws, s, false);
+    case GDN_BF16: return run_generic<__nv_bfloat16>(a, ws, s, false);
+    case GDN_F16: return run_generic<__half>(a, ws, s, false);
     default: return cudaErrorInvalidValue;
   }
 }

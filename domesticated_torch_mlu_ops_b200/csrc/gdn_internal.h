@@ -21,6 +21,18 @@ struct ChunkWorkspace {
   size_t total;
 };
 
+// Backward workspace: the generic forward's intermediates followed by the
+// backward's fp32 buffers.
+struct BwdWorkspace {
+  ChunkWorkspace fwd;
+  size_t dvn;       // f32 [Ttot][HV][V] gradient of v_new
+  size_t dhn;       // f32 [chunks][HV][K][V] gradient of the state after each chunk
+  size_t dqh, dkh;  // f32 [Ttot][HV][K] per-v-head dq, dk
+  size_t dw;        // f32 [Ttot][HV][K] gradient of W
+  size_t dG;        // f32 [Ttot][HV] gradient of the chunk-local cumsum of g
+  size_t total;
+};
+
 // Count of kernels launched by this library (gdn_kernel_launch_count).
 void note_launch(int n = 1);
 
@@ -57,6 +69,11 @@ bool decode_stream_applies(const gdn_recurrent_args& a);
 cudaError_t launch_decode_stream(const gdn_recurrent_args& a, cudaStream_t s);
 cudaError_t launch_recurrent_kfirst(const gdn_recurrent_plain_args& a, cudaStream_t s);
 cudaError_t launch_chunk_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s);
+// The generic forward without its output stage: leaves G, q/k, W, U, v_new
+// and the per-chunk states in the workspace for the backward.
+cudaError_t launch_chunk_generic_recompute(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s);
+BwdWorkspace plan_bwd_workspace(const gdn_chunk_bwd_args& a);
+cudaError_t launch_chunk_bwd(const gdn_chunk_bwd_args& a, const BwdWorkspace& ws, cudaStream_t s);
 cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s);
 cudaError_t launch_solve_tril(const float* A, void* out, int out_dtype, const void* cu,
                               int cu_dtype, int64_t N, int64_t B, int64_t T, int H, int BT,

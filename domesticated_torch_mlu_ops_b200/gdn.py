@@ -1,4 +1,4 @@
-"""Public gated delta-rule (GDN) forward ops, drop-in for ``torch_mlu_ops.triton_ops``.
+"""Public gated delta-rule (GDN) ops, drop-in for ``torch_mlu_ops.triton_ops``.
 
 Same names, argument order, keyword names, defaults and return values as the
 reference facade (``triton_ops.py:81-285``); the work runs in
@@ -88,6 +88,109 @@ def _check_shapes(q, k, v):
 # chunked prefill
 # ---------------------------------------------------------------------------
 
+def _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first):
+    B, T, H, HV, K, V = _check_shapes(q, k, v)
+    if K > 128 or V > 128:
+        raise ValueError(f"K={K}, V={V}: both must be <= 128 (triton/fla/chunk.py:27-28)")
+    if g.shape != v.shape[:3] or beta.shape != v.shape[:3]:
+        raise ValueError(f"g {tuple(g.shape)} and beta {tuple(beta.shape)} must be [B, T, HV]")
+    if cu_seqlens is not None and B != 1:
+        raise ValueError("cu_seqlens requires batch size 1 (packed sequences)")
+    qkv = _qkv_dtype(q, k, v)
+    cu, cu_dt = _idx(cu_seqlens)
+    N = B if cu is None else cu.numel() - 1
+    shape_state = (N, HV, V, K) if state_v_first else (N, HV, K, V)
+    if initial_state is not None and tuple(initial_state.shape) != shape_state:
+        raise ValueError(f"initial_state must be {shape_state}, got {tuple(initial_state.shape)}")
+    return (B, T, N, H, HV, K, V), qkv, cu, cu_dt, shape_state
+
+
+def _chunk_fwd(q, k, v, g, beta, scale, h0, output_final_state, cu, cu_dt, dims, qkv, shape_state,
+               state_v_first, use_qk_l2norm, force_generic):
+    B, T, N, H, HV, K, V = dims
+    dev = q.device
+    o = torch.empty_like(v, dtype=q.dtype)
+    ht = torch.empty(shape_state, dtype=torch.float32, device=dev) if output_final_state else None
+    args = _lib.ChunkArgs(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta),
+        initial_state=_ptr(h0), o=_ptr(o), final_state=_ptr(ht), cu_seqlens=_ptr(cu),
+        workspace=None, workspace_bytes=0, B=B, T=T, N=N, H=H, HV=HV, K=K, V=V,
+        qkv_dtype=qkv, cu_dtype=cu_dt, scale=float(scale) if scale is not None else 0.0,
+        use_qk_l2norm=int(bool(use_qk_l2norm)), state_v_first=int(bool(state_v_first)),
+        force_generic=int(bool(force_generic)))
+    lib = _lib.load()
+    nbytes = lib.gdn_chunk_workspace_size(ctypes.byref(args))
+    if nbytes == 0:
+        _lib.check(_lib.GDN_ERR_INVALID)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    args.workspace = ctypes.c_void_p(ws.data_ptr())
+    args.workspace_bytes = nbytes
+    with torch.cuda.device(dev):
+        _lib.check(lib.gdn_chunk_fwd(ctypes.byref(args), _stream(dev)))
+    return o, ht
+
+
+def _chunk_bwd(q, k, v, g, beta, scale, h0, cu, cu_dt, dims, qkv, shape_state, state_v_first,
+               use_qk_l2norm, do, dht):
+    B, T, N, H, HV, K, V = dims
+    dev = q.device
+    do = do.to(q.dtype).contiguous()
+    dht = None if dht is None else dht.to(torch.float32).contiguous()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg = torch.empty(v.shape[:3], dtype=torch.float32, device=dev)
+    db = torch.empty(v.shape[:3], dtype=torch.float32, device=dev)
+    dh0 = torch.empty(shape_state, dtype=torch.float32, device=dev) if h0 is not None else None
+    args = _lib.ChunkBwdArgs(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta), initial_state=_ptr(h0),
+        cu_seqlens=_ptr(cu), dout=_ptr(do), dht=_ptr(dht), dq=_ptr(dq), dk=_ptr(dk), dv=_ptr(dv),
+        dg=_ptr(dg), dbeta=_ptr(db), dh0=_ptr(dh0), workspace=None, workspace_bytes=0,
+        B=B, T=T, N=N, H=H, HV=HV, K=K, V=V, qkv_dtype=qkv, cu_dtype=cu_dt,
+        scale=float(scale) if scale is not None else 0.0,
+        use_qk_l2norm=int(bool(use_qk_l2norm)), state_v_first=int(bool(state_v_first)))
+    lib = _lib.load()
+    nbytes = lib.gdn_chunk_bwd_workspace_size(ctypes.byref(args))
+    if nbytes == 0:
+        _lib.check(_lib.GDN_ERR_INVALID)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    args.workspace = ctypes.c_void_p(ws.data_ptr())
+    args.workspace_bytes = nbytes
+    with torch.cuda.device(dev):
+        _lib.check(lib.gdn_chunk_bwd(ctypes.byref(args), _stream(dev)))
+    return dq, dk, dv, dg, db, dh0
+
+
+class ChunkGatedDeltaRuleFunction(torch.autograd.Function):
+    """Autograd node of the chunked forward (``triton/fla/chunk.py:188-251``):
+    the forward saves its inputs only and the backward recomputes the
+    intermediates (``chunk.py:76-186``) inside ``gdn_chunk_bwd``."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens,
+                state_v_first, use_qk_l2norm, force_generic):
+        dims, qkv, cu, cu_dt, shape_state = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens,
+                                                           state_v_first)
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        g32, b32, h0 = _f32(g), _f32(beta), _f32(initial_state)
+        o, ht = _chunk_fwd(q, k, v, g32, b32, scale, h0, output_final_state, cu, cu_dt, dims, qkv,
+                           shape_state, state_v_first, use_qk_l2norm, force_generic)
+        ctx.save_for_backward(q, k, v, g32, b32, h0, cu)
+        ctx.meta = (scale, cu_dt, dims, qkv, shape_state, state_v_first, use_qk_l2norm,
+                    g.dtype, beta.dtype, None if initial_state is None else initial_state.dtype)
+        return o, ht
+
+    @staticmethod
+    def backward(ctx, do, dht):
+        q, k, v, g32, b32, h0, cu = ctx.saved_tensors
+        scale, cu_dt, dims, qkv, shape_state, svf, l2, g_dt, b_dt, h0_dt = ctx.meta
+        if do is None:
+            do = torch.zeros_like(v, dtype=q.dtype)
+        dq, dk, dv, dg, db, dh0 = _chunk_bwd(q, k, v, g32, b32, scale, h0, cu, cu_dt, dims, qkv,
+                                             shape_state, svf, l2, do, dht)
+        if dh0 is not None:
+            dh0 = dh0.to(h0_dt)
+        return (dq, dk, dv, dg.to(g_dt), db.to(b_dt), None, dh0, None, None, None, None, None)
+
+
 def chunk_gated_delta_rule(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -113,47 +216,40 @@ def chunk_gated_delta_rule(
     Returns ``(o [B, T, HV, V] in q.dtype, final_state fp32 or None)``.
     ``chunk_indices`` / ``chunk_offsets`` are accepted for signature
     compatibility; the chunk table is built on the device from ``cu_seqlens``.
+
+    Differentiable like the reference (``ChunkGatedDeltaRuleFunction``,
+    ``triton/fla/chunk.py:188-251``): when grad mode is on and an input
+    requires grad, the backward (``gdn_chunk_bwd``) gives dq, dk, dv, dg,
+    dbeta and d(initial_state).
     """
     del chunk_indices, chunk_offsets, allow_tf32
     _cuda("chunk_gated_delta_rule", q, k, v, g, beta, initial_state, cu_seqlens)
-    B, T, H, HV, K, V = _check_shapes(q, k, v)
-    if K > 128 or V > 128:
-        raise ValueError(f"K={K}, V={V}: both must be <= 128 (triton/fla/chunk.py:27-28)")
-    if g.shape != v.shape[:3] or beta.shape != v.shape[:3]:
-        raise ValueError(f"g {tuple(g.shape)} and beta {tuple(beta.shape)} must be [B, T, HV]")
-    if cu_seqlens is not None and B != 1:
-        raise ValueError("cu_seqlens requires batch size 1 (packed sequences)")
-    qkv = _qkv_dtype(q, k, v)
+    if torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (q, k, v, g, beta, initial_state)):
+        return ChunkGatedDeltaRuleFunction.apply(
+            q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens, state_v_first,
+            use_qk_l2norm_in_kernel, force_generic)
+    dims, qkv, cu, cu_dt, shape_state = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens,
+                                                       state_v_first)
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-    g, beta = _f32(g), _f32(beta)
-    cu, cu_dt = _idx(cu_seqlens)
-    N = B if cu is None else cu.numel() - 1
-    shape_state = (N, HV, V, K) if state_v_first else (N, HV, K, V)
-    h0 = None
-    if initial_state is not None:
-        if tuple(initial_state.shape) != shape_state:
-            raise ValueError(f"initial_state must be {shape_state}, got {tuple(initial_state.shape)}")
-        h0 = _f32(initial_state)
-    dev = q.device
-    o = torch.empty_like(v, dtype=q.dtype)
-    ht = torch.empty(shape_state, dtype=torch.float32, device=dev) if output_final_state else None
-    args = _lib.ChunkArgs(
-        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta),
-        initial_state=_ptr(h0), o=_ptr(o), final_state=_ptr(ht), cu_seqlens=_ptr(cu),
-        workspace=None, workspace_bytes=0, B=B, T=T, N=N, H=H, HV=HV, K=K, V=V,
-        qkv_dtype=qkv, cu_dtype=cu_dt, scale=float(scale) if scale is not None else 0.0,
-        use_qk_l2norm=int(bool(use_qk_l2norm_in_kernel)), state_v_first=int(bool(state_v_first)),
-        force_generic=int(bool(force_generic)))
-    lib = _lib.load()
-    nbytes = lib.gdn_chunk_workspace_size(ctypes.byref(args))
-    if nbytes == 0:
-        _lib.check(_lib.GDN_ERR_INVALID)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    args.workspace = ctypes.c_void_p(ws.data_ptr())
-    args.workspace_bytes = nbytes
-    with torch.cuda.device(dev):
-        _lib.check(lib.gdn_chunk_fwd(ctypes.byref(args), _stream(dev)))
-    return o, ht
+    return _chunk_fwd(q, k, v, _f32(g), _f32(beta), scale, _f32(initial_state), output_final_state, cu,
+                      cu_dt, dims, qkv, shape_state, state_v_first, use_qk_l2norm_in_kernel, force_generic)
+
+
+def chunk_gated_delta_rule_bwd(q, k, v, g, beta, scale, initial_state, dout, dht,
+                               cu_seqlens=None, state_v_first=False, use_qk_l2norm_in_kernel=False):
+    """Backward of :func:`chunk_gated_delta_rule` as a plain call
+    (``triton/fla/chunk.py:76-186``, minus the saved ``A``, which is
+    recomputed).  Returns ``(dq, dk, dv, db, dg, dh0)`` in the reference's
+    order; dq, dk, dv in q's dtype, db and dg fp32, dh0 fp32 or None."""
+    _cuda("chunk_gated_delta_rule_bwd", q, k, v, g, beta, initial_state, dout, dht, cu_seqlens)
+    dims, qkv, cu, cu_dt, shape_state = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens,
+                                                       state_v_first)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    dq, dk, dv, dg, db, dh0 = _chunk_bwd(q, k, v, _f32(g), _f32(beta), scale, _f32(initial_state), cu,
+                                         cu_dt, dims, qkv, shape_state, state_v_first,
+                                         use_qk_l2norm_in_kernel, dout, dht)
+    return dq, dk, dv, db, dg, dh0
 
 
 # ---------------------------------------------------------------------------

@@ -15,6 +15,8 @@
  * Reference interfaces replaced (paths inside the torch_mlu_ops package):
  *   gdn_chunk_fwd          <- triton_ops.py:81-165 chunk_gated_delta_rule
  *                             -> triton/fla/chunk.py:10-74 chunk_gated_delta_rule_fwd
+ *   gdn_chunk_bwd          <- triton/fla/chunk.py:239-251 ChunkGatedDeltaRuleFunction.backward
+ *                             -> triton/fla/chunk.py:76-186 chunk_gated_delta_rule_bwd
  *   gdn_fused_recurrent_fwd<- triton_ops.py:228-285 fused_recurrent_gated_delta_rule_fn
  *                             -> triton/fla/fused_recurrent_fn.py:161-233
  *   gdn_recurrent_plain_fwd<- triton_ops.py:168-226 fused_recurrent_gated_delta_rule
@@ -117,6 +119,54 @@ GDN_API int gdn_chunk_fwd(const gdn_chunk_args* args, void* stream);
  * serialised by the caller.  Allocates nothing.
  */
 GDN_API int gdn_chunk_fwd_noalloc(const gdn_chunk_args* args, void* stream);
+
+/*
+ * Backward of gdn_chunk_fwd (the autograd backward of chunk_gated_delta_rule).
+ * Inputs q, k, v, g, beta, initial_state, cu_seqlens and the sizes mean what
+ * they mean in gdn_chunk_args (the forward's arguments, unchanged).
+ *   dout [B, T, HV, V] (qkv_dtype): gradient of o.
+ *   dht: gradient of final_state in the state layout, or NULL (zero).
+ *   dq, dk, dv: outputs of qkv_dtype in the shapes of q, k, v.
+ *   dg, dbeta [B, T, HV] f32: gradients of g and beta.
+ *   dh0: gradient of initial_state in the state layout, or NULL (not
+ *   written).  With use_qk_l2norm the gradients of q and k are taken
+ *   through the normalisation.
+ * The forward intermediates are recomputed in fp32 inside the call; the
+ * workspace (gdn_chunk_bwd_workspace_size) holds them and the backward's own
+ * fp32 buffers.  Every output element is written (no accumulation).
+ */
+typedef struct gdn_chunk_bwd_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const float* beta;
+  const float* initial_state;
+  const void* cu_seqlens;
+  const void* dout;
+  const float* dht;
+  void* dq;
+  void* dk;
+  void* dv;
+  float* dg;
+  float* dbeta;
+  float* dh0;
+  void* workspace;
+  size_t workspace_bytes;
+  int64_t B, T, N;
+  int32_t H, HV, K, V;
+  int32_t qkv_dtype;
+  int32_t cu_dtype;
+  float scale;
+  int32_t use_qk_l2norm;
+  int32_t state_v_first;
+} gdn_chunk_bwd_args;
+
+/* Workspace bytes gdn_chunk_bwd needs (0 and the last error for invalid
+ * arguments). */
+GDN_API size_t gdn_chunk_bwd_workspace_size(const gdn_chunk_bwd_args* args);
+
+GDN_API int gdn_chunk_bwd(const gdn_chunk_bwd_args* args, void* stream);
 
 /* Reads back (synchronously, on `stream`) the device error word that the
  * chunk kernels keep in `workspace`; returns GDN_OK or GDN_ERR_DEVICE and

@@ -239,6 +239,84 @@ def gen_chunk(ref: str):
         print("wrote", name)
 
 
+def gen_chunk_bwd(ref: str):
+    """Backward fixtures from ``chunk_gated_delta_rule_bwd`` (``chunk.py:76-186``).
+
+    Under the interpreter the backward kernels need two more changes: their
+    autotune lists are cut to the first config (the interpreter cannot time
+    configs), and two Cambricon-only forms are rewritten: a row of a
+    ones-vector product taken with ``[0, :]`` becomes the equivalent row
+    reduction, and the ``[0, :]`` of a [1, BT] block before a store becomes a
+    reshape."""
+    import re
+
+    import triton
+    orig_autotune = triton.autotune
+    triton.autotune = lambda configs, key, **kw: orig_autotune(configs[:1], key, **kw)
+    orig_load = _load
+
+    def bwd_patch(src):
+        src = re.sub(r"tl\.dot\((\w+)_ones_vec, tl\.trans\((.*?)\), allow_tf32=False\)\[0,\s*:\]",
+                     r"tl.sum(\2, axis=1)", src)
+        return src.replace("b_dg.to(p_dg.dtype.element_ty)[0,:]",
+                           "tl.reshape(b_dg.to(p_dg.dtype.element_ty), (BT,))")
+
+    def load_patched(modname, path, source_patch=None):
+        def patch(src):
+            return bwd_patch(source_patch(src) if source_patch is not None else src)
+        return orig_load(modname, path, patch)
+
+    globals()["_load"] = load_patched
+    try:
+        st = _load_chunk_modules(ref)
+        merge = getattr(st, [n for n in dir(st) if "merge_16x16_to_64x64" in n][0])
+
+        def native_solve_tril(A, output, cu_seqlens):
+            output.zero_()
+            B, T, H, BT = A.shape
+            index = sys.modules["torch_mlu_ops.triton.fla.index"]
+            ci = index.prepare_chunk_indices(cu_seqlens, BT) if cu_seqlens is not None else None
+            NT = triton.cdiv(T, BT) if cu_seqlens is None else len(ci)
+            merge[NT, B * H](A=A, Ai=output, cu_seqlens=cu_seqlens, chunk_indices=ci, T=T, H=H, BT=BT,
+                  USE_TMA=False, DOT_PRECISION="ieee")
+
+        torch.ops.torch_mlu_ops = types.SimpleNamespace(solve_tril=native_solve_tril)
+        chunk = _load("torch_mlu_ops.triton.fla.chunk", os.path.join(ref, "triton/fla/chunk.py"))
+        # (name, B, T, H, K, V, cu_seqlens, h0, dht); H == HV as in gen_chunk
+        cases = [("t130", 1, 130, 2, 32, 32, None, True, True),
+                 ("varlen", 1, 200, 2, 32, 16, [0, 64, 90, 200], True, True),
+                 ("batch_nostate", 2, 71, 1, 16, 32, None, False, False)]
+        for (name, B, T, H, K, V, cu_l, use_h0, use_dht) in cases:
+            q, k, v, gg, beta, gen = _rng_inputs(zlib.crc32(name.encode()) % 1000 + 31, B, T, H, H, K, V)
+            q = torch.nn.functional.normalize(q, dim=-1)
+            k = torch.nn.functional.normalize(k, dim=-1)
+            cu = torch.tensor(cu_l, dtype=torch.int64) if cu_l is not None else None
+            N = B if cu is None else len(cu) - 1
+            h0 = torch.randn(N, H, K, V, generator=gen) * 0.3 if use_h0 else None
+            scale = K ** -0.5
+            o, ht, A, gcum, _ = chunk.chunk_gated_delta_rule_fwd(
+                q, k, v, gg, beta, scale, h0, True, cu_seqlens=cu, allow_tf32=False)
+            do = torch.randn(o.shape, generator=gen)
+            # the reference's dh kernel reads dht unconditionally (its zero
+            # initialisation is commented out, chunk_delta_h.py:338): pass zeros
+            dht = torch.randn(ht.shape, generator=gen) if use_dht else torch.zeros(ht.shape)
+            dq, dk, dv, db, dg, dh0 = chunk.chunk_gated_delta_rule_bwd(
+                q, k, v, gcum, beta, A, scale, h0, do, dht, cu_seqlens=cu, allow_tf32=False)
+            empty = np.zeros(0, np.float32)
+            np.savez_compressed(
+                os.path.join(HERE, f"bwd_{name}.npz"),
+                q=_np(q), k=_np(k), v=_np(v), g=_np(gg), beta=_np(beta), scale=np.float64(scale),
+                h0=_np(h0) if h0 is not None else empty,
+                cu_seqlens=cu.numpy() if cu is not None else np.zeros(0, np.int64),
+                do=_np(do), dht=_np(dht) if dht is not None else empty,
+                dq=_np(dq), dk=_np(dk), dv=_np(dv), db=_np(db), dg=_np(dg),
+                dh0=_np(dh0) if (dh0 is not None and h0 is not None) else empty)
+            print("wrote bwd", name)
+    finally:
+        triton.autotune = orig_autotune
+        globals()["_load"] = orig_load
+
+
 def _load_conv_modules(ref: str):
     """Load ``triton/conv`` by path.  Four substitutions: the fla forward
     launcher passes a Cambricon compiler option (``bottleneck=``) that
@@ -421,6 +499,8 @@ def main():
         gen_chunk(a.ref)
     if a.only in ("", "conv"):
         gen_conv(a.ref)
+    if a.only in ("", "bwd"):
+        gen_chunk_bwd(a.ref)
 
 
 if __name__ == "__main__":

@@ -38,6 +38,7 @@ def test_library_exports_every_declared_symbol():
 
 
 @pytest.mark.parametrize("struct,cname", [(_lib.ChunkArgs, "gdn_chunk_args"),
+                                          (_lib.ChunkBwdArgs, "gdn_chunk_bwd_args"),
                                           (_lib.RecurrentArgs, "gdn_recurrent_args"),
                                           (_lib.RecurrentPlainArgs, "gdn_recurrent_plain_args"),
                                           (_lib.Conv1dArgs, "gdn_conv1d_args"),
@@ -102,6 +103,25 @@ def test_invalid_calls_return_codes_without_touching_the_gpu():
     assert lib.gdn_fused_recurrent_fwd(ctypes.byref(r), None) == _lib.GDN_ERR_INVALID
     assert b"ssm_state_indices" in lib.gdn_last_error()
     assert lib.gdn_solve_tril(None, None, 0, None, 0, 1, 1, 64, 2, 48, None) == _lib.GDN_ERR_INVALID
+
+
+def test_bwd_validation_returns_codes_without_touching_the_gpu():
+    lib = _lib.load()
+    b = _lib.ChunkBwdArgs(B=1, T=130, N=1, H=2, HV=4, K=64, V=64, qkv_dtype=_lib.GDN_F32)
+    need = lib.gdn_chunk_bwd_workspace_size(ctypes.byref(b))
+    # forward intermediates (generic layout) plus the backward's own buffers
+    fwd = lib.gdn_chunk_workspace_size(ctypes.byref(_chunk_args(T=130, H=2, HV=4, K=64, V=64,
+                                                                  qkv_dtype=_lib.GDN_F32, force_generic=1)))
+    assert need > fwd > 0
+    assert lib.gdn_chunk_bwd(ctypes.byref(b), None) == _lib.GDN_ERR_INVALID  # null pointers
+    assert b"dout" in lib.gdn_last_error()
+    for name in ("q", "k", "v", "g", "beta", "dout", "dq", "dk", "dv", "dg", "dbeta"):
+        setattr(b, name, ctypes.c_void_p(256))
+    b.workspace, b.workspace_bytes = ctypes.c_void_p(256), need - 1
+    assert lib.gdn_chunk_bwd(ctypes.byref(b), None) == _lib.GDN_ERR_WORKSPACE
+    b.HV = 3
+    assert lib.gdn_chunk_bwd_workspace_size(ctypes.byref(b)) == 0
+    assert b"multiple" in lib.gdn_last_error()
 
 
 def test_conv_validation_returns_codes_without_touching_the_gpu():
