@@ -347,6 +347,7 @@ def run_ours(a):
     # ---- decode (config 3) and the causal conv1d in front of the layer ----
     dec = _decode_bench(ops, dev, a, hbm, flush) if not a.no_decode else None
     conv = _conv_bench(ops, dev, a, hbm, flush) if not a.no_decode and rank == 0 else None
+    bwd = _bwd_bench(ops, dev, a, flush, tc_burst) if not a.no_bwd and rank == 0 else None
 
     # ---- CPU baseline (rank 0, N=1) ----
     cpu_line = None
@@ -401,6 +402,7 @@ def run_ours(a):
             "clocks": clk.summary(),
             "decode": dec,
             "conv1d": conv,
+            "backward": bwd,
             "cpu_baseline": cpu_line,
         }
         print(json.dumps(line), flush=True)
@@ -571,6 +573,62 @@ def _conv_bench(ops, dev, a, hbm, flush):
         "peak_gbs": hbm, "peak_kind": "measured HBM copy"}
 
 
+FP32_SIMT_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # 148 SMs x 128 fp32 lanes x FMA x max clock
+
+
+def bwd_flops_per_chunk_head(K, V):
+    """Matmul FLOPs of one (64-token chunk, v-head) of the backward, forward
+    recompute included: the products that gdn_chunk_bwd.cu and the generic
+    forward's W/U/state kernels compute (2 FLOPs per multiply-add)."""
+    aK, aV, b, c = 64 * 64 * K, 64 * 64 * V, 64 * K * V, 64 ** 3
+    fwd = 2 * aK + aV + 2 * b                       # K K^T, W, U, W h, K^T v_new
+    dvl = aK + aV                                   # Q K^T, P^T dO
+    state = 3 * b                                   # K dh', [Q; W]^T [dO; dv]
+    dqkw = aV + 3 * b + 2 * aK                      # dO v^T, v dh'^T, dO h^T, dv h^T, dP K, dP^T Q
+    wy = 4 * aK + 2 * aV + 2 * c + 2 * aK           # K K^T, dW K^T, dv V^T, T^T dW, T^T dv, dA, dS K, dS^T K
+    return 2 * (fwd + dvl + state + dqkw + wy)
+
+
+def _bwd_bench(ops, dev, a, flush, tc_burst):
+    """Backward (training) of the config-1 prefill shape: gdn_chunk_bwd with
+    dO given and no final-state gradient, q/k L2 norm on."""
+    import torch
+    B, T, H, HV, K, V = (CFG1[x] for x in ("B", "T", "H", "HV", "K", "V"))
+    gen = torch.Generator().manual_seed(5)
+    q = torch.randn(B, T, H, K, generator=gen).bfloat16().to(dev)
+    k = torch.randn(B, T, H, K, generator=gen).bfloat16().to(dev)
+    v = torch.randn(B, T, HV, V, generator=gen).bfloat16().to(dev)
+    g = torch.nn.functional.logsigmoid(torch.randn(B, T, HV, generator=gen)).to(dev)
+    beta = torch.sigmoid(torch.randn(B, T, HV, generator=gen)).to(dev)
+    do = torch.randn(B, T, HV, V, generator=gen).bfloat16().to(dev)
+
+    def call():
+        return ops.chunk_gated_delta_rule_bwd(q, k, v, g, beta, None, None, do, None,
+                                              use_qk_l2norm_in_kernel=True)
+
+    for _ in range(2):
+        call()
+    torch.cuda.synchronize()
+    reps = max(3, min(a.steps, 5))
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for st, en in ev:
+        flush.zero_()
+        st.record()
+        call()
+        en.record()
+    torch.cuda.synchronize()
+    ms = sum(st.elapsed_time(en) for st, en in ev) / reps
+    flops = (T // 64) * B * HV * bwd_flops_per_chunk_head(K, V)
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"workload": "chunk_gated_delta_rule backward, config-1 shape (B=1 T=8192 H=16 HV=32 K=V=128 "
+                        "bf16, q/k L2 norm, dO given, no final-state gradient), forward recompute included",
+            "ms_per_call": ms, "tokens_per_s": B * T / (ms * 1e-3), "flops": flops, "tflops": tf,
+            "frac_fp32_simt_nominal": tf / FP32_SIMT_NOMINAL_TFLOPS,
+            "frac_tensor_bf16_measured": tf / tc_burst,
+            "kernels": "generic fp32 forward recompute (chunk_wy, chunk_state) + bwd_dvlocal, bwd_state, "
+                       "bwd_dqkw, bwd_wy, bwd_qk, bwd_dg (fp32 SIMT)"}
+
+
 def run_reference(a):
     """CPU restatement of the reference algorithm (the oracle port), timed on
     the host's cores on a bounded sample of the config-1 workload."""
@@ -610,6 +668,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode and conv1d measurements")
+    ap.add_argument("--no-bwd", action="store_true", help="skip the backward measurement")
     ap.add_argument("--ref-tokens", type=int, default=2048)
     ap.add_argument("--tokens", type=int, default=0,
                     help="override config 1's T (small cases for ncu captures; not a bench line)")

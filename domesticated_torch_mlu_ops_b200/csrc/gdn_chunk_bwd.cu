@@ -13,8 +13,9 @@
 //   W = T diag(b Gam) K, U = T diag(b) V, v = U - W h
 //   o = scale (diag(Gam) Q h + (M * D * S) v),  h' = gam h + K^T diag(c) v
 // Given dO and dh' (the gradient of the state after the chunk):
+//   bwd_dvlocal_kernel (per chunk and v-head): dv_local = scale (M * D * S)^T dO
 //   bwd_state_kernel (reverse over a sequence's chunks):
-//     dv = scale (M * D * S)^T dO + diag(c) K dh'
+//     dv = dv_local + diag(c) K dh'
 //     dh = gam dh' + scale Q^T diag(Gam) dO - W^T dv          (dh0 at the first chunk)
 //   bwd_dqkw_kernel (per chunk and v-head):
 //     dP = scale M * D * (dO v^T)
@@ -30,95 +31,23 @@
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
+#include "simt_gemm.cuh"
 #include "solve_tril.cuh"
 
 namespace gdn {
 namespace {
 
-constexpr int kT = 256;                     // threads per CTA
-constexpr int LD = 129;                     // row stride of 64 x 128 fp32 tiles
-constexpr int kP = 65;                      // row stride of 64 x 64 fp32 tiles
-constexpr int kStage = 64 * 17 + 16 * 129;  // gemm staging floats
-constexpr int kVS = 32;                     // V columns per bwd_state_kernel CTA
-
-// C[i][n] (= or +=) alpha * sum_{k < Kd} A(i, k) B(k, n) for i < 64, n < N.
-// A(i, k) = a[i*asi + k*ask] (zero for i >= ma); B(k, n) = b[k*bsk + n*bsn]
-// (zero for n >= nb); operands fp32 or 16-bit, in global or shared memory.
-// C (fp32, shared or global, row stride ldc) is stored for rows i < mc.  Each
-// thread owns a 4 x NJ micro-tile (columns tc + 16 j); operands are staged 16
-// deep through `st`.  All kT threads call it; it starts and ends with a barrier.
-template <int NJ, bool ACC, typename TA, typename TB>
-__device__ __forceinline__ void gemm_tile(float* C, int64_t ldc, int mc, int N, int Kd, const TA* a,
-                                          int64_t asi, int64_t ask, int ma, const TB* b, int64_t bsk,
-                                          int64_t bsn, int nb, float alpha, float* st) {
-  constexpr int NC = 16 * NJ;
-  float* As = st;            // [64][17]
-  float* Bs = st + 64 * 17;  // [16][129]
-  const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
-  float acc[4][NJ];
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) acc[r][j] = 0.f;
-  __syncthreads();
-  for (int k0 = 0; k0 < Kd; k0 += 16) {
-    for (int e = tid; e < 64 * 16; e += kT) {
-      const int i = e >> 4, kk = e & 15, k = k0 + kk;
-      As[i * 17 + kk] = (i < ma && k < Kd) ? to_f<TA>(a[i * asi + k * ask]) : 0.f;
-    }
-    for (int e = tid; e < 16 * NC; e += kT) {
-      const int kk = e / NC, n = e % NC, k = k0 + kk;
-      Bs[kk * 129 + n] = (k < Kd && n < nb) ? to_f<TB>(b[k * bsk + n * bsn]) : 0.f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-      float av[4], bv[NJ];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) av[r] = As[(tr * 4 + r) * 17 + kk];
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) bv[j] = Bs[kk * 129 + tc + 16 * j];
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) acc[r][j] = fmaf(av[r], bv[j], acc[r][j]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int i = tr * 4 + r;
-    if (i >= mc) continue;
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      const int n = tc + 16 * j;
-      if (n < N) {
-        float* c = C + i * ldc + n;
-        *c = ACC ? *c + alpha * acc[r][j] : alpha * acc[r][j];
-      }
-    }
-  }
-  __syncthreads();
-}
+constexpr int kT = kGemmThreads;  // threads per CTA
+constexpr int LD = 129;           // row stride of 64 x 128 fp32 tiles
+constexpr int kP = 65;            // row stride of 64 x 64 fp32 tiles
+constexpr int kStage = kGemmStage;
+constexpr int kVS = 32;           // V columns per bwd_state_kernel CTA
 
 template <bool ACC, typename TA, typename TB>
 __device__ __forceinline__ void gemm(float* C, int64_t ldc, int mc, int N, int Kd, const TA* a, int64_t asi,
                                      int64_t ask, int ma, const TB* b, int64_t bsk, int64_t bsn, int nb,
                                      float alpha, float* st) {
-  if (N <= 64) gemm_tile<4, ACC>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
-  else gemm_tile<8, ACC>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
-}
-
-// Block-wide sum of one value per thread (returned to every thread).
-__device__ __forceinline__ float block_sum(float x, float* red) {
-  x = group_sum<32>(x);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
-  __syncthreads();
-  float t = 0.f;
-#pragma unroll
-  for (int i = 0; i < kT / 32; ++i) t += red[i];
-  __syncthreads();
-  return t;
+  gemm_staged<ACC>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
 }
 
 struct BwdPtrs {
@@ -127,21 +56,70 @@ struct BwdPtrs {
   float *dvn, *dhn, *dqh, *dkh, *dw, *dG;     // backward intermediates
 };
 
+// dv_local = scale (M * D * Q K^T)^T dO for one (chunk, v-head): the part of
+// dv that does not depend on the state gradient (chunk_bwd_dv_local), into
+// the dv workspace, which bwd_state_kernel then completes.
+template <typename T>
+__global__ void __launch_bounds__(kT) bwd_dvlocal_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
+  extern __shared__ float sm[];
+  const int K = p.K, V = p.V;
+  float* qc = sm;             // [64][LD]
+  float* kc = qc + 64 * LD;   // [64][LD]
+  float* dO = kc + 64 * LD;   // [64][LD]
+  float* P = dO + 64 * LD;    // [64][kP]
+  float* gcs = P + 64 * kP;   // [64]
+  int64_t n, lc;
+  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int64_t s = bos + lc * kChunk;
+  const int L = static_cast<int>(min64(kChunk, eos - s));
+  const int tid = threadIdx.x;
+  const int64_t rowQ = static_cast<int64_t>(p.H) * K, rowV = static_cast<int64_t>(p.HV) * V;
+  const T* dout = static_cast<const T*>(p.dout) + s * rowV + static_cast<int64_t>(hv) * V;
+  for (int e = tid; e < 64 * K; e += kT) {
+    const int i = e / K, kk = e % K;
+    const bool ok = i < L;
+    qc[i * LD + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
+    kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
+  }
+  for (int e = tid; e < 64 * V; e += kT) {
+    const int i = e / V, vv = e % V;
+    dO[i * LD + vv] = i < L ? to_f<T>(dout[i * rowV + vv]) : 0.f;
+  }
+  if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
+  gemm_smem<false>(P, kP, 64, 64, K, qc, LD, 1, kc, 1, LD);  // Q K^T
+  for (int e = tid; e < 64 * 64; e += kT) {
+    const int i = e >> 6, j = e & 63;
+    P[i * kP + j] = (i < L && j <= i) ? P[i * kP + j] * expf(gcs[i] - gcs[j]) : 0.f;
+  }
+  gemm_smem<false>(w.dvn + s * rowV + static_cast<int64_t>(hv) * V, rowV, L, V, 64, P, 1, kP, dO, LD, 1, scale);
+}
+
+// Per-chunk tiles of bwd_state_kernel: [Q; W] (128 rows), K, and the small
+// per-chunk vectors, filled by cp.async one step ahead of their use.
+constexpr int kSqw = 128 * LD;             // [Q; W] rows of K floats
+constexpr int kSk = 64 * LD;               // K rows
+constexpr int kSvec = 64 * kVS + 2 * 64;   // dv_local slice, G (2 stages)
+
 // Reverse recurrence over one sequence's chunks for one (v-head, 32-column
-// slice of V): stores dh' per chunk and dv (of v_new), then dh0.
+// slice of V).  Per chunk, given dh' (gradient of the state after it):
+//   dv = dv_local + diag(c) K dh'                      (stored: dv of v_new)
+//   dh = gam dh' + [Q; W]^T [scale diag(Gam) dO; -dv]  (one stacked product)
+// dh' is stored per chunk for the parallel kernels; dh0 at the end.  The
+// [Q; W] tiles of a chunk are copied in during its dv step and the next
+// chunk's K, dv_local and G during its dh step.
 template <typename T>
 __global__ void __launch_bounds__(kT) bwd_state_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
-  float* qc = sm;               // [64][LD]
-  float* kc = qc + 64 * LD;     // [64][LD]
-  float* wc = kc + 64 * LD;     // [64][LD]
-  float* P = wc + 64 * LD;      // [64][kP] M * D * Q K^T
-  float* dh = P + 64 * kP;      // [K][kVS]
-  float* dO = dh + 128 * kVS;   // [64][kVS]
-  float* dvs = dO + 64 * kVS;   // [64][kVS]
-  float* gcs = dvs + 64 * kVS;  // [64]
-  float* st = gcs + 64;         // gemm staging
+  float* qw = sm;                   // [128][LD]: Q rows 0..63, W rows 64..127
+  float* kc = qw + kSqw;            // [64][LD]
+  float* dvl = kc + kSk;            // [64][kVS] dv_local slice
+  float* gsb = dvl + 64 * kVS;      // [2][64] G per stage
+  float* dh = gsb + 2 * 64;         // [128][kVS]
+  float* rhs = dh + 128 * kVS;      // [128][kVS]: scale Gam dO rows 0..63, -dv rows 64..127
   const int64_t n = blockIdx.x;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
   const int v0 = blockIdx.z * kVS;
@@ -151,70 +129,83 @@ __global__ void __launch_bounds__(kT) bwd_state_kernel(const gdn_chunk_bwd_args 
   const T* dout = static_cast<const T*>(p.dout);
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
-  for (int e = tid; e < K * kVS; e += kT) {
+  for (int e = tid; e < 128 * kVS; e += kT) {
     const int kk = e / kVS, vv = v0 + e % kVS;
     float x = 0.f;
-    if (p.dht && vv < V)
+    if (p.dht && vv < V && kk < K)
       x = p.state_v_first ? p.dht[((n * p.HV + hv) * V + vv) * K + kk] : p.dht[((n * p.HV + hv) * K + kk) * V + vv];
     dh[e] = x;
   }
   const int64_t nch = eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0;
+  auto chunk_len = [&](int64_t lc) { return static_cast<int>(min64(kChunk, eos - (bos + lc * kChunk))); };
+  auto issue_k = [&](int64_t lc) {  // K, dv_local slice, G of chunk lc
+    const int64_t s = bos + lc * kChunk;
+    const int L = chunk_len(lc);
+    for (int e = tid; e < 64 * K; e += kT) {
+      const int i = e / K, kk = e % K;
+      const bool ok = i < L;
+      cp_async4(kc + i * LD + kk, ok ? w.kn + (s + i) * rowQ + h * K + kk : w.kn, ok);
+    }
+    for (int e = tid; e < 64 * kVS; e += kT) {
+      const int i = e / kVS, vv = v0 + e % kVS;
+      const bool ok = i < L && vv < V;
+      cp_async4(dvl + e, ok ? w.dvn + (s + i) * rowV + static_cast<int64_t>(hv) * V + vv : w.dvn, ok);
+    }
+    if (tid < 64) cp_async4(gsb + (lc & 1) * 64 + tid, tid < L ? w.gc + (s + tid) * p.HV + hv : w.gc, tid < L);
+    cp_async_commit();
+  };
+  auto issue_qw = [&](int64_t lc) {  // Q and W of chunk lc
+    const int64_t s = bos + lc * kChunk;
+    const int L = chunk_len(lc);
+    for (int e = tid; e < 64 * K; e += kT) {
+      const int i = e / K, kk = e % K;
+      const bool ok = i < L;
+      cp_async4(qw + i * LD + kk, ok ? w.qn + (s + i) * rowQ + h * K + kk : w.qn, ok);
+      cp_async4(qw + (64 + i) * LD + kk, ok ? w.w + (s + i) * rowK + static_cast<int64_t>(hv) * K + kk : w.w, ok);
+    }
+    cp_async_commit();
+  };
+  if (nch > 0) issue_k(nch - 1);
   for (int64_t lc = nch - 1; lc >= 0; --lc) {
     const int64_t s = bos + lc * kChunk;
-    const int L = static_cast<int>(min64(kChunk, eos - s));
+    const int L = chunk_len(lc);
     const int64_t cidx = w.coff[n] + lc;
-    __syncthreads();  // dh of the previous iteration is complete
+    const float* gs = gsb + (lc & 1) * 64;
+    // ---- dv step: needs K, dv_local, G of this chunk
+    issue_qw(lc);  // [Q; W] was last read by the previous dh step, which ended with a barrier
+    cp_async_wait<1>();
+    __syncthreads();
     float* dhn = w.dhn + (cidx * p.HV + hv) * static_cast<int64_t>(K) * V;
     for (int e = tid; e < K * kVS; e += kT) {
       const int kk = e / kVS, vv = v0 + e % kVS;
       if (vv < V) dhn[kk * V + vv] = dh[e];
     }
-    for (int e = tid; e < 64 * K; e += kT) {
-      const int i = e / K, kk = e % K;
-      const bool ok = i < L;
-      qc[i * LD + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
-      kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
-      wc[i * LD + kk] = ok ? w.w[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] : 0.f;
-    }
+    const float glast = gs[L - 1], eg = expf(glast);
     for (int e = tid; e < 64 * kVS; e += kT) {
       const int i = e / kVS, vv = v0 + e % kVS;
-      dO[e] = (i < L && vv < V) ? to_f<T>(dout[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv]) : 0.f;
+      const float d = (i < L && vv < V) ? to_f<T>(dout[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv]) : 0.f;
+      rhs[e] = i < L ? scale * expf(gs[i]) * d : 0.f;
     }
-    if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
-    gemm<false>(P, kP, 64, 64, K, qc, LD, 1, 64, kc, 1, LD, 64, 1.f, st);  // Q K^T
-    for (int e = tid; e < 64 * 64; e += kT) {
-      const int i = e >> 6, j = e & 63;
-      P[i * kP + j] = (i < L && j <= i) ? P[i * kP + j] * expf(gcs[i] - gcs[j]) : 0.f;
-    }
-    __syncthreads();
-    const float glast = gcs[L - 1], eg = expf(glast);
-    for (int e = tid; e < 64 * kVS; e += kT) {  // dv = scale P^T dO + diag(c) K dh'
-      const int i = e / kVS, c = e % kVS;
+    gemm_smem<false>(rhs + 64 * kVS, kVS, 64, kVS, K, kc, LD, 1, dh, kVS, 1);  // K dh'
+    for (int e = tid; e < 64 * kVS; e += kT) {
+      const int i = e / kVS, vv = v0 + e % kVS;
       float x = 0.f;
-      if (i < L) {
-        float a = 0.f, b = 0.f;
-        for (int ii = i; ii < L; ++ii) a = fmaf(P[ii * kP + i], dO[ii * kVS + c], a);
-        for (int kk = 0; kk < K; ++kk) b = fmaf(kc[i * LD + kk], dh[kk * kVS + c], b);
-        x = scale * a + expf(glast - gcs[i]) * b;
-      }
-      dvs[e] = x;
+      if (i < L) x = dvl[e] + expf(glast - gs[i]) * rhs[64 * kVS + e];
+      if (i < L && vv < V) w.dvn[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv] = x;
+      rhs[64 * kVS + e] = -x;
+    }
+    // ---- dh step: needs [Q; W]; K, dv_local of the next chunk come in meanwhile
+    __syncthreads();  // K and dv_local of this chunk are no longer read
+    if (lc > 0) {
+      issue_k(lc - 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
-    for (int e = tid; e < 64 * kVS; e += kT) {
-      const int i = e / kVS, vv = v0 + e % kVS;
-      if (i < L && vv < V) w.dvn[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv] = dvs[e];
-      dO[e] *= scale * expf(gcs[i]);  // scale diag(Gam) dO (rows >= L are zero)
-    }
-    __syncthreads();
-    for (int e = tid; e < K * kVS; e += kT) {  // dh = gam dh' + scale Q^T diag(Gam) dO - W^T dv
-      const int kk = e / kVS, c = e % kVS;
-      float a = 0.f;
-      for (int i = 0; i < L; ++i) {
-        a = fmaf(qc[i * LD + kk], dO[i * kVS + c], a);
-        a = fmaf(-wc[i * LD + kk], dvs[i * kVS + c], a);
-      }
-      dh[e] = fmaf(eg, dh[e], a);
-    }
+    for (int e = tid; e < 128 * kVS; e += kT) dh[e] *= eg;
+    gemm_smem<true>(dh, kVS, min(K, 64), kVS, 128, qw, 1, LD, rhs, kVS, 1);
+    if (K > 64) gemm_smem<true>(dh + 64 * kVS, kVS, K - 64, kVS, 128, qw + 64, 1, LD, rhs, kVS, 1);
   }
   __syncthreads();
   if (p.dh0) {
@@ -228,20 +219,23 @@ __global__ void __launch_bounds__(kT) bwd_state_kernel(const gdn_chunk_bwd_args 
 }
 
 // dq, dk (per v-head, fp32), dW and the dG terms of the output and state
-// paths for one (chunk, v-head).
+// paths for one (chunk, v-head).  With dq, dk complete for these paths,
+// dG_i = q_i . dq_i - k_i . dk_i, plus gam <dh', h> + sum_i E_i on the last row
+// (E_i = k_i . (diag(c) v dh'^T)_i): the Q K^T products of the P path cancel
+// into the two row dots.
 template <typename T>
-__global__ void __launch_bounds__(kT) bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
+__global__ void __launch_bounds__(kT, 1) bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
   float* qc = sm;               // [64][LD]
   float* kc = qc + 64 * LD;     // [64][LD]
-  float* dq = kc + 64 * LD;     // [64][LD]
+  float* dOs = kc + 64 * LD;    // [64][LD] dO
+  float* X = dOs + 64 * LD;     // [64][LD] v_new, then dv
+  float* dq = X + 64 * LD;      // [64][LD]
   float* dk = dq + 64 * LD;     // [64][LD]
   float* dP = dk + 64 * LD;     // [64][kP]
-  float* Sq = dP + 64 * kP;     // [64][kP] Q K^T
-  float* gcs = Sq + 64 * kP;    // [64]
-  float* dG = gcs + 64;         // [64]
-  float* red = dG + 64;         // [32]
+  float* gcs = dP + 64 * kP;    // [64]
+  float* red = gcs + 64;        // [32]
   float* st = red + 32;         // gemm staging
   int64_t n, lc;
   if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
@@ -265,32 +259,20 @@ __global__ void __launch_bounds__(kT) bwd_dqkw_kernel(const gdn_chunk_bwd_args p
     qc[i * LD + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
     kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
   }
+  for (int e = tid; e < 64 * V; e += kT) {
+    const int i = e / V, vv = e % V;
+    const bool ok = i < L;
+    dOs[i * LD + vv] = ok ? to_f<T>(dO[i * rowV + vv]) : 0.f;
+    X[i * LD + vv] = ok ? vn[i * rowV + vv] : 0.f;
+  }
   if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
-  gemm<false>(Sq, kP, 64, 64, K, qc, LD, 1, 64, kc, 1, LD, 64, 1.f, st);
-  gemm<false>(dP, kP, 64, 64, V, dO, rowV, 1, L, vn, 1, rowV, L, 1.f, st);  // dO v^T
+  gemm_smem<false>(dP, kP, 64, 64, V, dOs, LD, 1, X, 1, LD);  // dO v^T
   for (int e = tid; e < 64 * 64; e += kT) {
     const int i = e >> 6, j = e & 63;
     dP[i * kP + j] = (i < L && j <= i) ? scale * expf(gcs[i] - gcs[j]) * dP[i * kP + j] : 0.f;
   }
-  gemm<false>(dq, LD, 64, K, V, dO, rowV, 1, L, hst, 1, V, K, scale, st);  // scale dO h^T
+  gemm<false>(dk, LD, 64, K, V, X, LD, 1, 64, dhn, 1, V, K, 1.f, st);  // v dh'^T
   const float glast = gcs[L - 1], eg = expf(glast);
-  if (tid < 64) {  // dQ = diag(Gam) (scale dO h^T); dG_i = q_i . dQ_i
-    const float gi = tid < L ? expf(gcs[tid]) : 0.f;
-    float a = 0.f;
-    for (int kk = 0; kk < K; ++kk) {
-      const float x = gi * dq[tid * LD + kk];
-      dq[tid * LD + kk] = x;
-      a = fmaf(qc[tid * LD + kk], x, a);
-    }
-    float b = 0.f;  // P path: sum_j dP_ij S_ij - sum_i dP_ij S_ij
-    for (int j = 0; j < 64; ++j) b += dP[tid * kP + j] * Sq[tid * kP + j] - dP[j * kP + tid] * Sq[j * kP + tid];
-    dG[tid] = a + b;
-  }
-  gemm<true>(dq, LD, 64, K, 64, dP, kP, 1, 64, kc, LD, 1, K, 1.f, st);   // + dP K
-  gemm<false>(dk, LD, 64, K, V, vn, rowV, 1, L, dhn, 1, V, K, 1.f, st);  // v dh'^T
-  float part = 0.f;
-  for (int e = tid; e < K * V; e += kT) part = fmaf(dhn[e], hst[e], part);
-  const float hh = block_sum(part, red);  // <dh', h>
   float E = 0.f;
   if (tid < 64) {  // dK = diag(c) v dh'^T; E_i = k_i . dK_i
     const float c = tid < L ? expf(glast - gcs[tid]) : 0.f;
@@ -300,24 +282,41 @@ __global__ void __launch_bounds__(kT) bwd_dqkw_kernel(const gdn_chunk_bwd_args p
       E = fmaf(kc[tid * LD + kk], x, E);
     }
   }
+  float part = 0.f;
+  for (int e = tid; e < K * V; e += kT) part = fmaf(dhn[e], hst[e], part);
+  const float hh = block_sum(part, red);  // <dh', h>
   const float Esum = block_sum(tid < 64 ? E : 0.f, red);
-  if (tid < 64) dG[tid] += (tid == L - 1 ? eg * hh + Esum : 0.f) - E;
-  gemm<true>(dk, LD, 64, K, 64, dP, 1, kP, 64, qc, LD, 1, K, 1.f, st);  // + dP^T Q
+  for (int e = tid; e < 64 * V; e += kT) {  // X <- dv
+    const int i = e / V, vv = e % V;
+    X[i * LD + vv] = i < L ? dvn[i * rowV + vv] : 0.f;
+  }
+  gemm<false>(dq, LD, 64, K, V, dOs, LD, 1, 64, hst, 1, V, K, scale, st);  // scale dO h^T
+  for (int e = tid; e < 64 * K; e += kT) {
+    const int i = e / K, kk = e % K;
+    dq[i * LD + kk] *= i < L ? expf(gcs[i]) : 0.f;
+  }
+  gemm_smem<true>(dq, LD, 64, K, 64, dP, kP, 1, kc, LD, 1);  // + dP K
+  gemm_smem<true>(dk, LD, 64, K, 64, dP, 1, kP, qc, LD, 1);  // + dP^T Q
   // dW = -dv h^T straight to the workspace
-  gemm<false>(w.dw + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, V, dvn, rowV, 1, L, hst, 1, V, K,
-              -1.f, st);
+  gemm<false>(w.dw + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, V, X, LD, 1, 64, hst, 1, V, K, -1.f,
+              st);
+  if (tid < 64) {
+    float a = 0.f;
+    for (int kk = 0; kk < K; ++kk) a += qc[tid * LD + kk] * dq[tid * LD + kk] - kc[tid * LD + kk] * dk[tid * LD + kk];
+    if (tid == L - 1) a += eg * hh + Esum;
+    if (tid < L) w.dG[(s + tid) * p.HV + hv] = a;
+  }
   for (int e = tid; e < L * K; e += kT) {
     const int i = e / K, kk = e % K;
     w.dqh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dq[i * LD + kk];
     w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dk[i * LD + kk];
   }
-  if (tid < L) w.dG[(s + tid) * p.HV + hv] = dG[tid];
 }
 
 // Backward through W = T diag(b Gam) K and U = T diag(b) V for one
 // (chunk, v-head): dv, db, and the dK and dG terms of the WY form.
 template <typename T>
-__global__ void __launch_bounds__(kT) bwd_wy_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w) {
+__global__ void __launch_bounds__(kT, 1) bwd_wy_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
   float* Tm = sm;                 // [64][kTS] (16-byte aligned)
@@ -498,8 +497,10 @@ __global__ void bwd_dg_kernel(const gdn_chunk_bwd_args p, const int64_t* __restr
   }
 }
 
-constexpr size_t kStateSmem = sizeof(float) * (3 * 64 * LD + 64 * kP + 128 * kVS + 2 * 64 * kVS + 64 + kStage);
-constexpr size_t kDqkwSmem = sizeof(float) * (4 * 64 * LD + 2 * 64 * kP + 2 * 64 + 32 + kStage);
+constexpr size_t kDvlSmem = sizeof(float) * (3 * 64 * LD + 64 * kP + 64);
+constexpr size_t kStateSmem = sizeof(float) * (kSqw + kSk + kSvec + 2 * 128 * kVS);
+constexpr size_t kDqkwSmem = sizeof(float) * (6 * 64 * LD + 64 * kP + 64 + 32 + kStage);
+static_assert(kDqkwSmem <= 227 * 1024, "bwd_dqkw_kernel shared memory");
 constexpr size_t kWySmem =
     sizeof(float) * (64 * kTS + kTrilScratch + 3 * 64 * LD + 4 * 64 * kP + 5 * 64 + kStage);
 static_assert(kWySmem <= 227 * 1024, "bwd_wy_kernel shared memory");
@@ -555,12 +556,19 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
   const int64_t Ttot = b.B * b.T;
   const int64_t nc = chunk_upper_bound(Ttot, b.N);
   const float scale = b.scale > 0.f ? b.scale : 1.f / sqrtf(static_cast<float>(b.K));
+  if ((e = cudaFuncSetAttribute(bwd_dvlocal_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kDvlSmem))) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(bwd_state_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(kStateSmem))) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(bwd_dqkw_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(kDqkwSmem))) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(bwd_wy_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(kWySmem))) != cudaSuccess) return e;
+  if (nc > 0) {
+    note_launch();
+    bwd_dvlocal_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kDvlSmem, s>>>(b, w, scale);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
   note_launch();
   bwd_state_kernel<T><<<dim3(static_cast<unsigned>(b.N), b.HV, (b.V + kVS - 1) / kVS), kT, kStateSmem, s>>>(
       b, w, scale);

@@ -13,6 +13,7 @@
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
+#include "simt_gemm.cuh"
 #include "solve_tril.cuh"
 
 namespace gdn {
@@ -92,19 +93,23 @@ struct GenericPtrs {
   float* hs;
 };
 
+constexpr int kLD = 129;  // row stride of 64 x K fp32 tiles (conflict-free transposed reads)
+
+// Per (chunk, v-head): G = chunk-local cumsum of g, A = tril_strict(diag(beta)
+// exp(G_i - G_j) K K^T), T = (I + A)^-1, W = T diag(beta exp(G)) K,
+// U = T diag(beta) V.
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kGemmThreads)
 chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
-  float* ks = sm;                 // [64][K]
-  float* vs = ks + 64 * K;        // [64][V]
-  float* A = vs + 64 * V;         // [64][65]
-  float* Tm = A + 64 * 68;        // [64][kTS] (A rows use 65, padded to 68)
-  float* gcs = Tm + 64 * kTS;     // [64]
-  float* bs = gcs + 64;           // [64]
-  float* cw = bs + 64;            // [64] beta * exp(G)
-  float* Zs = cw + 64;            // kTrilScratch floats of solve scratch
+  float* Tm = sm;                  // [64][kTS] (16-byte aligned)
+  float* Zs = Tm + 64 * kTS;       // kTrilScratch floats of solve scratch (16-byte aligned)
+  float* A = Zs + kTrilScratch;    // [64][65]
+  float* ks = A + 64 * 65;         // [64][kLD]
+  float* vs = ks + 64 * kLD;       // [64][kLD]
+  float* gcs = vs + 64 * kLD;      // [64]
+  float* bs = gcs + 64;            // [64]
   int64_t n, lc;
   if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
@@ -113,123 +118,139 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
   const int64_t s = bos + lc * kChunk;
   const int L = static_cast<int>(min64(kChunk, eos - s));
   const int tid = threadIdx.x;
+  const int64_t rowK = static_cast<int64_t>(p.HV) * K, rowV = static_cast<int64_t>(p.HV) * V;
   const T* vb = static_cast<const T*>(p.v);
-  for (int e = tid; e < 64 * K; e += blockDim.x) {
+  for (int e = tid; e < 64 * K; e += kGemmThreads) {
     const int i = e / K, kk = e % K;
-    ks[e] = i < L ? w.kn[((s + i) * p.H + h) * K + kk] : 0.f;
+    ks[i * kLD + kk] = i < L ? w.kn[((s + i) * p.H + h) * K + kk] : 0.f;
   }
-  for (int e = tid; e < 64 * V; e += blockDim.x) {
+  for (int e = tid; e < 64 * V; e += kGemmThreads) {
     const int i = e / V, vv = e % V;
-    vs[e] = i < L ? to_f<T>(vb[((s + i) * p.HV + hv) * V + vv]) : 0.f;
+    vs[i * kLD + vv] = i < L ? to_f<T>(vb[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv]) : 0.f;
+  }
+  if (tid < 32) {  // chunk-local cumsum of g: warp scan over 2 x 32 values
+    float x0 = tid < L ? p.g[(s + tid) * p.HV + hv] : 0.f;
+    float x1 = tid + 32 < L ? p.g[(s + tid + 32) * p.HV + hv] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y0 = __shfl_up_sync(0xffffffffu, x0, o), y1 = __shfl_up_sync(0xffffffffu, x1, o);
+      if (tid >= o) {
+        x0 += y0;
+        x1 += y1;
+      }
+    }
+    x1 += __shfl_sync(0xffffffffu, x0, 31);
+    gcs[tid] = x0;
+    gcs[tid + 32] = x1;
   }
   if (tid < 64) bs[tid] = tid < L ? p.beta[(s + tid) * p.HV + hv] : 0.f;
-  if (tid == 0) {
-    float acc = 0.f;
-    for (int i = 0; i < 64; ++i) {
-      if (i < L) acc += p.g[(s + i) * p.HV + hv];
-      gcs[i] = acc;
-    }
-  }
-  __syncthreads();
-  if (tid < L) {
-    w.gc[(s + tid) * p.HV + hv] = gcs[tid];
-    cw[tid] = bs[tid] * expf(gcs[tid]);
-  } else if (tid < 64) {
-    cw[tid] = 0.f;
-  }
-  for (int e = tid; e < 64 * 64; e += blockDim.x) {
+  gemm_smem<false>(A, 65, 64, 64, K, ks, kLD, 1, ks, 1, kLD);  // K K^T
+  if (tid < L) w.gc[(s + tid) * p.HV + hv] = gcs[tid];
+  for (int e = tid; e < 64 * 64; e += kGemmThreads) {
     const int i = e >> 6, j = e & 63;
-    float a = 0.f;
-    if (i < L && j < i) {
-      const float* ki = ks + i * K;
-      const float* kj = ks + j * K;
-      for (int kk = 0; kk < K; ++kk) a += ki[kk] * kj[kk];
-      a *= bs[i] * expf(gcs[i] - gcs[j]);
-    }
-    A[i * 65 + j] = a;
+    A[i * 65 + j] = (i < L && j < i) ? bs[i] * expf(gcs[i] - gcs[j]) * A[i * 65 + j] : 0.f;
   }
   __syncthreads();
-  solve_tril64_nt<256>(A, Tm, Zs);  // (I + A)^-1; ends with a barrier
-  for (int e = tid; e < L * K; e += blockDim.x) {
+  solve_tril64_nt<kGemmThreads>(A, Tm, Zs);  // (I + A)^-1; ends with a barrier
+  for (int e = tid; e < 64 * K; e += kGemmThreads) {  // rows of K by beta exp(G)
     const int i = e / K, kk = e % K;
-    float acc = 0.f;
-    for (int j = 0; j <= i; ++j) acc += Tm[i * kTS + j] * cw[j] * ks[j * K + kk];
-    w.w[((s + i) * p.HV + hv) * K + kk] = acc;
+    ks[i * kLD + kk] *= bs[i] * expf(gcs[i]);
   }
-  for (int e = tid; e < L * V; e += blockDim.x) {
+  for (int e = tid; e < 64 * V; e += kGemmThreads) {  // rows of V by beta
     const int i = e / V, vv = e % V;
-    float acc = 0.f;
-    for (int j = 0; j <= i; ++j) acc += Tm[i * kTS + j] * bs[j] * vs[j * V + vv];
-    w.u[((s + i) * p.HV + hv) * V + vv] = acc;
+    vs[i * kLD + vv] *= bs[i];
   }
+  gemm_smem<false>(w.w + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, 64, Tm, kTS, 1, ks, kLD, 1);
+  gemm_smem<false>(w.u + s * rowV + static_cast<int64_t>(hv) * V, rowV, L, V, 64, Tm, kTS, 1, vs, kLD, 1);
 }
 
 constexpr int kStateCols = 32;
+constexpr int kStateStage = 2 * 64 * kLD + 64 * kStateCols + 64;  // wc, kc, u slice, G
 
-__global__ void __launch_bounds__(256)
+// Inter-chunk recurrence for one (sequence, v-head, 32-column slice of V):
+// per chunk v_new = U - W h, h <- exp(G_last) h + K^T diag(exp(G_last - G)) v_new.
+// The next chunk's W, K, U and G are copied in (cp.async) while the current
+// chunk computes.
+__global__ void __launch_bounds__(kGemmThreads)
 chunk_state_kernel(const gdn_chunk_args p, const GenericPtrs w) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
-  float* hsm = sm;                    // [K][32]
-  float* vn = hsm + K * kStateCols;   // [64][32]
-  float* wc = vn + 64 * kStateCols;   // [64][K]
-  float* kc = wc + 64 * K;            // [64][K]
-  float* gcs = kc + 64 * K;           // [64]
+  float* hsm = sm;                          // [128][32] state slice
+  float* stage0 = hsm + 128 * kStateCols;   // 2 stages of kStateStage floats
   const int64_t n = blockIdx.x;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
   const int v0 = blockIdx.z * kStateCols;
   const int tid = threadIdx.x;
+  const int64_t rowK = static_cast<int64_t>(p.HV) * K, rowV = static_cast<int64_t>(p.HV) * V;
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
-  for (int e = tid; e < K * kStateCols; e += blockDim.x) {
+  for (int e = tid; e < 128 * kStateCols; e += kGemmThreads) {
     const int kk = e / kStateCols, vv = v0 + e % kStateCols;
     float x = 0.f;
-    if (p.initial_state && vv < V)
+    if (p.initial_state && vv < V && kk < K)
       x = p.state_v_first ? p.initial_state[((n * p.HV + hv) * V + vv) * K + kk]
                           : p.initial_state[((n * p.HV + hv) * K + kk) * V + vv];
     hsm[e] = x;
   }
-  __syncthreads();
   const int64_t nchunks = eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0;
+  auto issue = [&](int64_t lc) {
+    float* wc = stage0 + (lc & 1) * kStateStage;
+    float* kc = wc + 64 * kLD;
+    float* us = kc + 64 * kLD;
+    float* gs = us + 64 * kStateCols;
+    const int64_t s = bos + lc * kChunk;
+    const int L = static_cast<int>(min64(kChunk, eos - s));
+    for (int e = tid; e < 64 * K; e += kGemmThreads) {
+      const int i = e / K, kk = e % K;
+      const bool ok = i < L;
+      cp_async4(wc + i * kLD + kk, ok ? w.w + (s + i) * rowK + static_cast<int64_t>(hv) * K + kk : w.w, ok);
+      cp_async4(kc + i * kLD + kk, ok ? w.kn + ((s + i) * p.H + h) * K + kk : w.kn, ok);
+    }
+    for (int e = tid; e < 64 * kStateCols; e += kGemmThreads) {
+      const int i = e / kStateCols, vv = v0 + e % kStateCols;
+      const bool ok = i < L && vv < V;
+      cp_async4(us + e, ok ? w.u + (s + i) * rowV + static_cast<int64_t>(hv) * V + vv : w.u, ok);
+    }
+    if (tid < 64) cp_async4(gs + tid, tid < L ? w.gc + (s + tid) * p.HV + hv : w.gc, tid < L);
+    cp_async_commit();
+  };
+  if (nchunks > 0) issue(0);
   for (int64_t lc = 0; lc < nchunks; ++lc) {
     const int64_t s = bos + lc * kChunk;
     const int L = static_cast<int>(min64(kChunk, eos - s));
     const int64_t cidx = w.coff[n] + lc;
-    for (int e = tid; e < K * kStateCols; e += blockDim.x) {
+    float* wc = stage0 + (lc & 1) * kStateStage;
+    float* kc = wc + 64 * kLD;
+    float* us = kc + 64 * kLD;
+    float* gs = us + 64 * kStateCols;
+    if (lc + 1 < nchunks) {
+      issue(lc + 1);  // the other stage was last read before the previous iteration's final barrier
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    float* hg = w.hs + (cidx * p.HV + hv) * static_cast<int64_t>(K) * V;
+    for (int e = tid; e < K * kStateCols; e += kGemmThreads) {
       const int kk = e / kStateCols, vv = v0 + e % kStateCols;
-      if (vv < V) w.hs[((cidx * p.HV + hv) * K + kk) * V + vv] = hsm[e];
+      if (vv < V) hg[kk * V + vv] = hsm[e];
     }
-    for (int e = tid; e < 64 * K; e += blockDim.x) {
-      const int i = e / K, kk = e % K;
-      wc[e] = i < L ? w.w[((s + i) * p.HV + hv) * K + kk] : 0.f;
-      kc[e] = i < L ? w.kn[((s + i) * p.H + h) * K + kk] : 0.f;
+    gemm_smem<true>(us, kStateCols, 64, kStateCols, K, wc, kLD, 1, hsm, kStateCols, 1, -1.f);  // U - W h
+    const float glast = gs[L - 1], eg = expf(glast);
+    for (int e = tid; e < 64 * kStateCols; e += kGemmThreads) {
+      const int i = e / kStateCols, vv = v0 + e % kStateCols;
+      const float x = us[e];
+      if (i < L && vv < V) w.vnew[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv] = x;
+      us[e] = i < L ? x * expf(glast - gs[i]) : 0.f;
     }
-    if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
-    __syncthreads();
-    for (int e = tid; e < 64 * kStateCols; e += blockDim.x) {
-      const int i = e / kStateCols, c = e % kStateCols, vv = v0 + c;
-      float x = 0.f;
-      if (i < L && vv < V) {
-        float acc = 0.f;
-        for (int kk = 0; kk < K; ++kk) acc += wc[i * K + kk] * hsm[kk * kStateCols + c];
-        x = w.u[((s + i) * p.HV + hv) * V + vv] - acc;
-        w.vnew[((s + i) * p.HV + hv) * V + vv] = x;
-      }
-      vn[e] = x;
-    }
-    __syncthreads();
-    const float glast = gcs[L - 1];
-    const float eg = expf(glast);
-    for (int e = tid; e < K * kStateCols; e += blockDim.x) {
-      const int kk = e / kStateCols, c = e % kStateCols;
-      float acc = 0.f;
-      for (int i = 0; i < L; ++i) acc += kc[i * K + kk] * expf(glast - gcs[i]) * vn[i * kStateCols + c];
-      hsm[e] = eg * hsm[e] + acc;
-    }
-    __syncthreads();
+    for (int e = tid; e < K * kStateCols; e += kGemmThreads) hsm[e] *= eg;
+    gemm_smem<true>(hsm, kStateCols, min(K, 64), kStateCols, 64, kc, 1, kLD, us, kStateCols, 1);
+    if (K > 64)
+      gemm_smem<true>(hsm + 64 * kStateCols, kStateCols, K - 64, kStateCols, 64, kc + 64, 1, kLD, us, kStateCols, 1);
   }
+  __syncthreads();
   if (p.final_state) {
-    for (int e = tid; e < K * kStateCols; e += blockDim.x) {
+    for (int e = tid; e < K * kStateCols; e += kGemmThreads) {
       const int kk = e / kStateCols, vv = v0 + e % kStateCols;
       if (vv >= V) continue;
       if (p.state_v_first) p.final_state[((n * p.HV + hv) * V + vv) * K + kk] = hsm[e];
@@ -238,15 +259,18 @@ chunk_state_kernel(const gdn_chunk_args p, const GenericPtrs w) {
   }
 }
 
+// Output of one (chunk, v-head): o = scale (diag(exp(G)) Q h + (M * D * Q K^T) v_new).
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kGemmThreads)
 chunk_out_kernel(const gdn_chunk_args p, const GenericPtrs w, float scale) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
-  float* qc = sm;               // [64][K]
-  float* kc = qc + 64 * K;      // [64][K]
-  float* att = kc + 64 * K;     // [64][65]
-  float* gcs = att + 64 * 65;   // [64]
+  float* qc = sm;                // [64][kLD]
+  float* kc = qc + 64 * kLD;     // [64][kLD]
+  float* oc = kc + 64 * kLD;     // [64][kLD]
+  float* att = oc + 64 * kLD;    // [64][65]
+  float* gcs = att + 64 * 65;    // [64]
+  float* st = gcs + 64;          // staging
   int64_t n, lc;
   if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
@@ -256,32 +280,30 @@ chunk_out_kernel(const gdn_chunk_args p, const GenericPtrs w, float scale) {
   const int L = static_cast<int>(min64(kChunk, eos - s));
   const int64_t cidx = blockIdx.x;
   const int tid = threadIdx.x;
-  for (int e = tid; e < 64 * K; e += blockDim.x) {
+  const int64_t rowV = static_cast<int64_t>(p.HV) * V;
+  for (int e = tid; e < 64 * K; e += kGemmThreads) {
     const int i = e / K, kk = e % K;
-    qc[e] = i < L ? w.qn[((s + i) * p.H + h) * K + kk] : 0.f;
-    kc[e] = i < L ? w.kn[((s + i) * p.H + h) * K + kk] : 0.f;
+    qc[i * kLD + kk] = i < L ? w.qn[((s + i) * p.H + h) * K + kk] : 0.f;
+    kc[i * kLD + kk] = i < L ? w.kn[((s + i) * p.H + h) * K + kk] : 0.f;
   }
   if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
-  __syncthreads();
-  for (int e = tid; e < 64 * 64; e += blockDim.x) {
+  gemm_smem<false>(att, 65, 64, 64, K, qc, kLD, 1, kc, 1, kLD);  // Q K^T
+  for (int e = tid; e < 64 * 64; e += kGemmThreads) {
     const int i = e >> 6, j = e & 63;
-    float a = 0.f;
-    if (i < L && j <= i) {
-      for (int kk = 0; kk < K; ++kk) a += qc[i * K + kk] * kc[j * K + kk];
-      a *= expf(gcs[i] - gcs[j]);
-    }
-    att[i * 65 + j] = a;
+    att[i * 65 + j] = (i < L && j <= i) ? att[i * 65 + j] * expf(gcs[i] - gcs[j]) : 0.f;
   }
-  __syncthreads();
-  const float* hc = w.hs + cidx * p.HV * K * V + static_cast<int64_t>(hv) * K * V;
-  T* ob = static_cast<T*>(p.o);
-  for (int e = tid; e < L * V; e += blockDim.x) {
+  const float* hc = w.hs + (cidx * p.HV + hv) * static_cast<int64_t>(K) * V;
+  gemm_staged<false>(oc, kLD, 64, V, K, qc, kLD, 1, 64, hc, V, 1, V, 1.f, st);  // Q h
+  for (int e = tid; e < 64 * V; e += kGemmThreads) {
     const int i = e / V, vv = e % V;
-    float inter = 0.f;
-    for (int kk = 0; kk < K; ++kk) inter += qc[i * K + kk] * hc[kk * V + vv];
-    float intra = 0.f;
-    for (int j = 0; j <= i; ++j) intra += att[i * 65 + j] * w.vnew[((s + j) * p.HV + hv) * V + vv];
-    ob[((s + i) * p.HV + hv) * V + vv] = from_f<T>(scale * (expf(gcs[i]) * inter + intra));
+    oc[i * kLD + vv] *= expf(gcs[i]);
+  }
+  const float* vn = w.vnew + s * rowV + static_cast<int64_t>(hv) * V;
+  gemm_staged<true>(oc, kLD, 64, V, L, att, 65, 1, 64, vn, rowV, 1, V, 1.f, st);  // + P v_new
+  T* ob = static_cast<T*>(p.o) + s * rowV + static_cast<int64_t>(hv) * V;
+  for (int e = tid; e < L * V; e += kGemmThreads) {
+    const int i = e / V, vv = e % V;
+    ob[i * rowV + vv] = from_f<T>(scale * oc[i * kLD + vv]);
   }
 }
 
@@ -336,9 +358,9 @@ static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
-  const size_t wy_smem = sizeof(float) * (64 * a.K + 64 * a.V + 2 * 64 * 68 + 3 * 64 + kTrilScratch);
-  const size_t st_smem = sizeof(float) * (a.K * kStateCols + 64 * kStateCols + 2 * 64 * a.K + 64);
-  const size_t out_smem = sizeof(float) * (2 * 64 * a.K + 64 * 65 + 64);
+  const size_t wy_smem = sizeof(float) * (64 * kTS + kTrilScratch + 64 * 65 + 2 * 64 * kLD + 2 * 64);
+  const size_t st_smem = sizeof(float) * (128 * kStateCols + 2 * kStateStage);
+  const size_t out_smem = sizeof(float) * (3 * 64 * kLD + 64 * 65 + 64 + kGemmStage);
   if ((e = cudaFuncSetAttribute(chunk_wy_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(wy_smem))) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -347,16 +369,16 @@ static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws
                                 static_cast<int>(out_smem))) != cudaSuccess) return e;
   if (nc > 0) {
     hk.pre(s);
-    chunk_wy_kernel<T><<<dim3(static_cast<unsigned>(nc), a.HV), 256, wy_smem, s>>>(a, w);
+    chunk_wy_kernel<T><<<dim3(static_cast<unsigned>(nc), a.HV), kGemmThreads, wy_smem, s>>>(a, w);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   hk.pre(s);
   chunk_state_kernel<<<dim3(static_cast<unsigned>(a.N), a.HV, (a.V + kStateCols - 1) / kStateCols),
-                       256, st_smem, s>>>(a, w);
+                       kGemmThreads, st_smem, s>>>(a, w);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (nc > 0 && with_output) {
     hk.pre(s);
-    chunk_out_kernel<T><<<dim3(static_cast<unsigned>(nc), a.HV), 256, out_smem, s>>>(a, w, scale);
+    chunk_out_kernel<T><<<dim3(static_cast<unsigned>(nc), a.HV), kGemmThreads, out_smem, s>>>(a, w, scale);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   hk.end(s);
