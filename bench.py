@@ -322,22 +322,26 @@ def run_ours(a):
     # ---- end-to-end through the public API with host buffers ----
     e2e_ms, h2d, d2h = None, 0, 0
     if not a.no_e2e:
-        o_h = torch.empty(B, T, HV, V, dtype=torch.bfloat16).pin_memory()
-        ht_h = torch.empty(N, HV, K, V, dtype=torch.float32).pin_memory()
         e2e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(a.steps)]
-        extra_h = [] if h0 is None else [h0.cpu().pin_memory(), cu.cpu().pin_memory()]
+        h0_h = None if h0 is None else h0.cpu().pin_memory()
+        cu_h = None if cu is None else cu.cpu()
+        extra_h = [x for x in (h0_h, cu_h) if x is not None]
+
+        def e2e_step():
+            # host buffers in, host buffers out, through the public host-memory entry point
+            return ops.chunk_gated_delta_rule_from_host(q_h, k_h, v_h, g_h, b_h, None, h0_h, True, cu_h,
+                                                        use_qk_l2norm_in_kernel=True, device=dev,
+                                                        segment_tokens=a.segment_tokens)
+
+        for _ in range(2):
+            e2e_step()
         _barrier(world)
         torch.cuda.synchronize()
         for i in range(a.steps):
             flush.zero_()
             e2e_evs[i][0].record(stream)
-            qd, kd, vd, gd, bd = (x.to(dev, non_blocking=True) for x in (q_h, k_h, v_h, g_h, b_h))
-            h0d, cud = (x.to(dev, non_blocking=True) for x in extra_h) if extra_h else (None, cu)
-            o, ht = ops.chunk_gated_delta_rule(qd, kd, vd, gd, bd, None, h0d, True, cud,
-                                               use_qk_l2norm_in_kernel=True)
-            o_h.copy_(o, non_blocking=True)
-            ht_h.copy_(ht, non_blocking=True)
+            o_h, ht_h = e2e_step()
             e2e_evs[i][1].record(stream)
         torch.cuda.synchronize()
         e2e_ms = _max_over_ranks(sum(s.elapsed_time(e) for s, e in e2e_evs) / a.steps, world)
@@ -397,7 +401,9 @@ def run_ours(a):
             "stages_ms": stage_avg,
             "e2e": None if e2e_ms is None else {
                 "value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": f"chunk_gated_delta_rule_from_host (pinned host tensors in and out, "
+                       f"{a.segment_tokens}-token pieces: copy-in, compute and copy-out overlap)"},
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
             "decode": dec,
@@ -673,6 +679,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=0,
                     help="override config 1's T (small cases for ncu captures; not a bench line)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--segment-tokens", dest="segment_tokens", type=int, default=2048,
+                    help="tokens per piece of the host-streamed end-to-end leg (multiple of 64)")
     ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg4"],
                     help="BASELINE prefill config (default cfg1, the headline)")
     a = ap.parse_args()

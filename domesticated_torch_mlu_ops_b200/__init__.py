@@ -9,6 +9,7 @@ from .conv import causal_conv1d, causal_conv1d_fn, causal_conv1d_update  # noqa:
 from .gdn import (  # noqa: F401
     chunk_gated_delta_rule,
     chunk_gated_delta_rule_bwd,
+    chunk_gated_delta_rule_from_host,
     fused_recurrent_gated_delta_rule,
     fused_recurrent_gated_delta_rule_fn,
     solve_tril,
@@ -20,6 +21,7 @@ __all__ = [
     "causal_conv1d_update",
     "chunk_gated_delta_rule",
     "chunk_gated_delta_rule_bwd",
+    "chunk_gated_delta_rule_from_host",
     "fused_recurrent_gated_delta_rule",
     "fused_recurrent_gated_delta_rule_fn",
     "solve_tril",

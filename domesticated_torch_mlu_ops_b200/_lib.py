@@ -29,6 +29,8 @@ EXPORTED = (
     "gdn_chunk_check_device_error",
     "gdn_chunk_bwd_workspace_size",
     "gdn_chunk_bwd",
+    "gdn_chunk_fwd_host_buffer_size",
+    "gdn_chunk_fwd_host",
     "gdn_fused_recurrent_fwd",
     "gdn_recurrent_plain_fwd",
     "gdn_solve_tril",
@@ -160,6 +162,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.gdn_chunk_bwd_workspace_size.restype = ctypes.c_size_t
     lib.gdn_chunk_bwd.argtypes = [ctypes.POINTER(ChunkBwdArgs), _vp]
     lib.gdn_chunk_bwd.restype = ctypes.c_int
+    lib.gdn_chunk_fwd_host_buffer_size.argtypes = [ctypes.POINTER(ChunkArgs), _i64]
+    lib.gdn_chunk_fwd_host_buffer_size.restype = ctypes.c_size_t
+    lib.gdn_chunk_fwd_host.argtypes = [ctypes.POINTER(ChunkArgs), _i64, _vp]
+    lib.gdn_chunk_fwd_host.restype = ctypes.c_int
     lib.gdn_fused_recurrent_fwd.argtypes = [ctypes.POINTER(RecurrentArgs), _vp]
     lib.gdn_fused_recurrent_fwd.restype = ctypes.c_int
     lib.gdn_recurrent_plain_fwd.argtypes = [ctypes.POINTER(RecurrentPlainArgs), _vp]

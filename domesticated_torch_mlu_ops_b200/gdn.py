@@ -236,6 +236,97 @@ def chunk_gated_delta_rule(
                       cu_dt, dims, qkv, shape_state, state_v_first, use_qk_l2norm_in_kernel, force_generic)
 
 
+def chunk_gated_delta_rule_from_host(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    g: torch.Tensor,
+    beta: torch.Tensor,
+    scale: float | None = None,
+    initial_state: torch.Tensor = None,
+    output_final_state: bool = False,
+    cu_seqlens: torch.LongTensor | None = None,
+    state_v_first: bool = False,
+    use_qk_l2norm_in_kernel: bool = False,
+    *,
+    device=None,
+    segment_tokens: int = 1024,
+    o_out: torch.Tensor | None = None,
+    final_state_out: torch.Tensor | None = None,
+    force_generic: bool = False,
+):
+    """:func:`chunk_gated_delta_rule` for inputs that live in host memory
+    (``gdn_chunk_fwd_host``).
+
+    Same arguments and results as the device op, but every tensor is a CPU
+    tensor.  The tokens go to the GPU in pieces of about ``segment_tokens``
+    tokens (a multiple of 64) while earlier pieces compute and their outputs
+    come back, so the host link, not the kernels, sets the time; the results
+    are those of the device op.  Page-locked (pinned) inputs give overlapped
+    copies; other host memory is pinned first.
+
+    Returns ``(o, final_state)`` as pinned CPU tensors (``o_out`` /
+    ``final_state_out`` when given: contiguous pinned tensors of the output
+    shapes, which spares pinning fresh host memory on every call).  They are
+    written by asynchronous copies that the current stream of ``device``
+    waits for: synchronise that stream (or the device) before reading them,
+    and keep the inputs unchanged until then.
+    """
+    for t in (q, k, v, g, beta, initial_state, cu_seqlens, o_out, final_state_out):
+        if t is not None and t.is_cuda:
+            raise ValueError("chunk_gated_delta_rule_from_host takes host (CPU) tensors")
+    if segment_tokens <= 0 or segment_tokens % 64:
+        raise ValueError(f"segment_tokens={segment_tokens} must be a positive multiple of 64")
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    dims, qkv, _, _, shape_state = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first)
+    B, T, N, H, HV, K, V = dims
+    staged = []  # host temporaries (conversions, pinning) the copies read
+
+    def host_in(t, dtype=None):
+        if t is None:
+            return None
+        x = t if dtype is None else t.to(dtype)
+        x = x.contiguous()
+        if not x.is_pinned():
+            x = x.pin_memory()
+        if x is not t:
+            staged.append(x)
+        return x
+
+    def host_out(t, shape, dtype, name):
+        if t is None:
+            return torch.empty(shape, dtype=dtype, pin_memory=True)
+        if tuple(t.shape) != tuple(shape) or t.dtype != dtype or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous host tensor of shape {tuple(shape)} and dtype {dtype}")
+        return t
+
+    qh, kh, vh = host_in(q), host_in(k), host_in(v)
+    gh, bh = host_in(g, torch.float32), host_in(beta, torch.float32)
+    h0h = host_in(initial_state, torch.float32)
+    cuh, cu_dt = _idx(None if cu_seqlens is None else cu_seqlens.contiguous())
+    o_h = host_out(o_out, (B, T, HV, V), q.dtype, "o_out")
+    ht_h = host_out(final_state_out, shape_state, torch.float32, "final_state_out") if output_final_state else None
+    args = _lib.ChunkArgs(
+        q=_ptr(qh), k=_ptr(kh), v=_ptr(vh), g=_ptr(gh), beta=_ptr(bh),
+        initial_state=_ptr(h0h), o=_ptr(o_h), final_state=_ptr(ht_h), cu_seqlens=_ptr(cuh),
+        workspace=None, workspace_bytes=0, B=B, T=T, N=N, H=H, HV=HV, K=K, V=V,
+        qkv_dtype=qkv, cu_dtype=cu_dt, scale=float(scale) if scale is not None else 0.0,
+        use_qk_l2norm=int(bool(use_qk_l2norm_in_kernel)), state_v_first=int(bool(state_v_first)),
+        force_generic=int(bool(force_generic)))
+    lib = _lib.load()
+    nbytes = lib.gdn_chunk_fwd_host_buffer_size(ctypes.byref(args), segment_tokens)
+    if nbytes == 0:
+        _lib.check(_lib.GDN_ERR_INVALID)
+    with torch.cuda.device(dev):
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        args.workspace = ctypes.c_void_p(buf.data_ptr())
+        args.workspace_bytes = nbytes
+        _lib.check(lib.gdn_chunk_fwd_host(ctypes.byref(args), segment_tokens, _stream(dev)))
+        if staged:  # the temporaries must outlive the copies that read them
+            torch.cuda.current_stream(dev).synchronize()
+    return o_h, ht_h
+
+
 def chunk_gated_delta_rule_bwd(q, k, v, g, beta, scale, initial_state, dout, dht,
                                cu_seqlens=None, state_v_first=False, use_qk_l2norm_in_kernel=False):
     """Backward of :func:`chunk_gated_delta_rule` as a plain call

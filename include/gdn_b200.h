@@ -17,6 +17,7 @@
  *                             -> triton/fla/chunk.py:10-74 chunk_gated_delta_rule_fwd
  *   gdn_chunk_bwd          <- triton/fla/chunk.py:239-251 ChunkGatedDeltaRuleFunction.backward
  *                             -> triton/fla/chunk.py:76-186 chunk_gated_delta_rule_bwd
+ *   gdn_chunk_fwd_host     <- no reference counterpart (host-memory prefill, pipelined copies)
  *   gdn_fused_recurrent_fwd<- triton_ops.py:228-285 fused_recurrent_gated_delta_rule_fn
  *                             -> triton/fla/fused_recurrent_fn.py:161-233
  *   gdn_recurrent_plain_fwd<- triton_ops.py:168-226 fused_recurrent_gated_delta_rule
@@ -167,6 +168,32 @@ typedef struct gdn_chunk_bwd_args {
 GDN_API size_t gdn_chunk_bwd_workspace_size(const gdn_chunk_bwd_args* args);
 
 GDN_API int gdn_chunk_bwd(const gdn_chunk_bwd_args* args, void* stream);
+
+/*
+ * Chunked prefill from host memory (no counterpart in the reference, whose
+ * ops take device tensors only).  For callers whose q/k/v sit in host
+ * memory, such as offline prefill of long prompts or a CPU-side engine that
+ * streams requests to the GPU: the host link, not the kernels, bounds such a
+ * call, so the copies are pipelined against the kernels.
+ * args: as for gdn_chunk_fwd, except that q, k, v, g, beta, initial_state,
+ * o, final_state and cu_seqlens are HOST pointers (page-locked memory lets
+ * the copies run asynchronously and overlap; pageable memory also works),
+ * and workspace / workspace_bytes is a DEVICE buffer of at least
+ * gdn_chunk_fwd_host_buffer_size(args, segment_tokens) bytes.
+ * The tokens are cut into pieces of about segment_tokens tokens (a positive
+ * multiple of 64): a single sequence (B = 1, no cu_seqlens) along time, the
+ * fp32 state handed from piece to piece on the device; an equal-length batch
+ * into groups of sequences; a packed batch into groups of consecutive
+ * sequences.  Each piece is one gdn_chunk_fwd call on device copies (same
+ * results as the device entry point).  Copy-in of piece p+1, compute of
+ * piece p (on `stream`) and copy-out of piece p-1 overlap; the copies run on
+ * two streams the library creates once per device.  Before returning, the
+ * call makes `stream` wait for all of its copies: the host outputs are
+ * complete, and the host inputs may be reused, once `stream` reaches this
+ * point (for example after cudaStreamSynchronize(stream)).
+ */
+GDN_API size_t gdn_chunk_fwd_host_buffer_size(const gdn_chunk_args* args, int64_t segment_tokens);
+GDN_API int gdn_chunk_fwd_host(const gdn_chunk_args* args, int64_t segment_tokens, void* stream);
 
 /* Reads back (synchronously, on `stream`) the device error word that the
  * chunk kernels keep in `workspace`; returns GDN_OK or GDN_ERR_DEVICE and

@@ -124,6 +124,25 @@ def test_bwd_validation_returns_codes_without_touching_the_gpu():
     assert b"multiple" in lib.gdn_last_error()
 
 
+def test_host_stream_sizing_and_validation():
+    import numpy as np
+    lib = _lib.load()
+    a = _chunk_args(T=1000, H=2, HV=4)
+    assert lib.gdn_chunk_fwd_host_buffer_size(ctypes.byref(a), 100) == 0  # not a multiple of 64
+    assert b"multiple of 64" in lib.gdn_last_error()
+    one = lib.gdn_chunk_fwd_host_buffer_size(ctypes.byref(a), 1024)
+    four = lib.gdn_chunk_fwd_host_buffer_size(ctypes.byref(a), 256)
+    assert one > four > 0  # slots hold one piece each
+    cu = np.array([0, 10, 5, 1000], dtype=np.int64)  # cu_seqlens live on the host here
+    b = _chunk_args(T=1000, H=2, HV=4, N=3)
+    b.cu_seqlens = ctypes.c_void_p(cu.ctypes.data)
+    assert lib.gdn_chunk_fwd_host_buffer_size(ctypes.byref(b), 256) == 0
+    assert b"decrease" in lib.gdn_last_error()
+    cu[2] = 500
+    assert lib.gdn_chunk_fwd_host_buffer_size(ctypes.byref(b), 256) > 0
+    assert lib.gdn_chunk_fwd_host(ctypes.byref(a), 1024, None) == _lib.GDN_ERR_INVALID  # null pointers
+
+
 def test_conv_validation_returns_codes_without_touching_the_gpu():
     lib = _lib.load()
     a = _lib.Conv1dArgs(B=1, T=8, N=1, D=16, W=4)
