@@ -31,14 +31,15 @@
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
-#include "simt_gemm.cuh"
+#include "tile_gemm.cuh"
 #include "solve_tril.cuh"
 
 namespace gdn {
 namespace {
 
 constexpr int kT = kGemmThreads;  // threads per CTA
-constexpr int LD = 129;           // row stride of 64 x 128 fp32 tiles
+constexpr int LD = kRowK;         // row stride of 64 x 128 fp32 tiles
+constexpr int LQ = 130;           // the same in bwd_dqkw_kernel (six tiles must fit)
 constexpr int kP = 65;            // row stride of 64 x 64 fp32 tiles
 constexpr int kStage = kGemmStage;
 constexpr int kVS = 32;           // V columns per bwd_state_kernel CTA
@@ -60,7 +61,7 @@ struct BwdPtrs {
 // dv that does not depend on the state gradient (chunk_bwd_dv_local), into
 // the dv workspace, which bwd_state_kernel then completes.
 template <typename T>
-__global__ void __launch_bounds__(kT) bwd_dvlocal_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
+__global__ void __launch_bounds__(kT, 1) bwd_dvlocal_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
   float* qc = sm;             // [64][LD]
@@ -97,11 +98,12 @@ __global__ void __launch_bounds__(kT) bwd_dvlocal_kernel(const gdn_chunk_bwd_arg
   gemm_smem<false>(w.dvn + s * rowV + static_cast<int64_t>(hv) * V, rowV, L, V, 64, P, 1, kP, dO, LD, 1, scale);
 }
 
-// Per-chunk tiles of bwd_state_kernel: [Q; W] (128 rows), K, and the small
-// per-chunk vectors, filled by cp.async one step ahead of their use.
-constexpr int kSqw = 128 * LD;             // [Q; W] rows of K floats
-constexpr int kSk = 64 * LD;               // K rows
-constexpr int kSvec = 64 * kVS + 2 * 64;   // dv_local slice, G (2 stages)
+// Shared memory of bwd_state_kernel: [Q; W] (128 rows, read transposed), K
+// (read row-major), the dv_local slice, G (2 stages), dh and the stacked
+// right-hand side (32-column tiles read n-contiguous).
+constexpr int kSqw = 128 * kRowN;
+constexpr int kSk = 64 * kRowK;
+constexpr int kSvec = 64 * kRow32 + 2 * 64;
 
 // Reverse recurrence over one sequence's chunks for one (v-head, 32-column
 // slice of V).  Per chunk, given dh' (gradient of the state after it):
@@ -111,18 +113,19 @@ constexpr int kSvec = 64 * kVS + 2 * 64;   // dv_local slice, G (2 stages)
 // [Q; W] tiles of a chunk are copied in during its dv step and the next
 // chunk's K, dv_local and G during its dh step.
 template <typename T>
-__global__ void __launch_bounds__(kT) bwd_state_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
+__global__ void __launch_bounds__(kT, 1) bwd_state_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
-  float* qw = sm;                   // [128][LD]: Q rows 0..63, W rows 64..127
-  float* kc = qw + kSqw;            // [64][LD]
-  float* dvl = kc + kSk;            // [64][kVS] dv_local slice
-  float* gsb = dvl + 64 * kVS;      // [2][64] G per stage
-  float* dh = gsb + 2 * 64;         // [128][kVS]
-  float* rhs = dh + 128 * kVS;      // [128][kVS]: scale Gam dO rows 0..63, -dv rows 64..127
+  float* qw = sm;                   // [128][kRowN]: Q rows 0..63, W rows 64..127
+  float* kc = qw + kSqw;            // [64][kRowK]
+  float* dvl = kc + kSk;            // [64][kRow32] dv_local slice
+  float* gsb = dvl + 64 * kRow32;   // [2][64] G per stage
+  float* dh = gsb + 2 * 64;         // [128][kRow32]
+  float* rhs = dh + 128 * kRow32;   // [128][kRow32]: scale Gam dO rows 0..63, -dv rows 64..127
   const int64_t n = blockIdx.x;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
   const int v0 = blockIdx.z * kVS;
+  const int vcols = V - v0 < kVS ? V - v0 : kVS;
   const int tid = threadIdx.x;
   const int64_t rowQ = static_cast<int64_t>(p.H) * K, rowV = static_cast<int64_t>(p.HV) * V,
                 rowK = static_cast<int64_t>(p.HV) * K;
@@ -130,39 +133,27 @@ __global__ void __launch_bounds__(kT) bwd_state_kernel(const gdn_chunk_bwd_args 
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
   for (int e = tid; e < 128 * kVS; e += kT) {
-    const int kk = e / kVS, vv = v0 + e % kVS;
+    const int kk = e / kVS, c = e % kVS, vv = v0 + c;
     float x = 0.f;
     if (p.dht && vv < V && kk < K)
       x = p.state_v_first ? p.dht[((n * p.HV + hv) * V + vv) * K + kk] : p.dht[((n * p.HV + hv) * K + kk) * V + vv];
-    dh[e] = x;
+    dh[kk * kRow32 + c] = x;
   }
   const int64_t nch = eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0;
   auto chunk_len = [&](int64_t lc) { return static_cast<int>(min64(kChunk, eos - (bos + lc * kChunk))); };
   auto issue_k = [&](int64_t lc) {  // K, dv_local slice, G of chunk lc
     const int64_t s = bos + lc * kChunk;
     const int L = chunk_len(lc);
-    for (int e = tid; e < 64 * K; e += kT) {
-      const int i = e / K, kk = e % K;
-      const bool ok = i < L;
-      cp_async4(kc + i * LD + kk, ok ? w.kn + (s + i) * rowQ + h * K + kk : w.kn, ok);
-    }
-    for (int e = tid; e < 64 * kVS; e += kT) {
-      const int i = e / kVS, vv = v0 + e % kVS;
-      const bool ok = i < L && vv < V;
-      cp_async4(dvl + e, ok ? w.dvn + (s + i) * rowV + static_cast<int64_t>(hv) * V + vv : w.dvn, ok);
-    }
+    tile_async(kc, kRowK, w.kn + s * rowQ + h * K, rowQ, L, 64, K, K);
+    tile_async(dvl, kRow32, w.dvn + s * rowV + static_cast<int64_t>(hv) * V + v0, rowV, L, 64, vcols, kVS);
     if (tid < 64) cp_async4(gsb + (lc & 1) * 64 + tid, tid < L ? w.gc + (s + tid) * p.HV + hv : w.gc, tid < L);
     cp_async_commit();
   };
   auto issue_qw = [&](int64_t lc) {  // Q and W of chunk lc
     const int64_t s = bos + lc * kChunk;
     const int L = chunk_len(lc);
-    for (int e = tid; e < 64 * K; e += kT) {
-      const int i = e / K, kk = e % K;
-      const bool ok = i < L;
-      cp_async4(qw + i * LD + kk, ok ? w.qn + (s + i) * rowQ + h * K + kk : w.qn, ok);
-      cp_async4(qw + (64 + i) * LD + kk, ok ? w.w + (s + i) * rowK + static_cast<int64_t>(hv) * K + kk : w.w, ok);
-    }
+    tile_async(qw, kRowN, w.qn + s * rowQ + h * K, rowQ, L, 64, K, K);
+    tile_async(qw + 64 * kRowN, kRowN, w.w + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, 64, K, K);
     cp_async_commit();
   };
   if (nch > 0) issue_k(nch - 1);
@@ -177,22 +168,22 @@ __global__ void __launch_bounds__(kT) bwd_state_kernel(const gdn_chunk_bwd_args 
     __syncthreads();
     float* dhn = w.dhn + (cidx * p.HV + hv) * static_cast<int64_t>(K) * V;
     for (int e = tid; e < K * kVS; e += kT) {
-      const int kk = e / kVS, vv = v0 + e % kVS;
-      if (vv < V) dhn[kk * V + vv] = dh[e];
+      const int kk = e / kVS, c = e % kVS;
+      if (c < vcols) dhn[kk * V + v0 + c] = dh[kk * kRow32 + c];
     }
     const float glast = gs[L - 1], eg = expf(glast);
     for (int e = tid; e < 64 * kVS; e += kT) {
-      const int i = e / kVS, vv = v0 + e % kVS;
-      const float d = (i < L && vv < V) ? to_f<T>(dout[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv]) : 0.f;
-      rhs[e] = i < L ? scale * expf(gs[i]) * d : 0.f;
+      const int i = e / kVS, c = e % kVS;
+      const float d = (i < L && c < vcols) ? to_f<T>(dout[(s + i) * rowV + static_cast<int64_t>(hv) * V + v0 + c]) : 0.f;
+      rhs[i * kRow32 + c] = i < L ? scale * expf(gs[i]) * d : 0.f;
     }
-    gemm_smem<false>(rhs + 64 * kVS, kVS, 64, kVS, K, kc, LD, 1, dh, kVS, 1);  // K dh'
+    gemm_smem<false>(rhs + 64 * kRow32, kRow32, 64, kVS, K, kc, kRowK, 1, dh, kRow32, 1);  // K dh'
     for (int e = tid; e < 64 * kVS; e += kT) {
-      const int i = e / kVS, vv = v0 + e % kVS;
+      const int i = e / kVS, c = e % kVS;
       float x = 0.f;
-      if (i < L) x = dvl[e] + expf(glast - gs[i]) * rhs[64 * kVS + e];
-      if (i < L && vv < V) w.dvn[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv] = x;
-      rhs[64 * kVS + e] = -x;
+      if (i < L) x = dvl[i * kRow32 + c] + expf(glast - gs[i]) * rhs[(64 + i) * kRow32 + c];
+      if (i < L && c < vcols) w.dvn[(s + i) * rowV + static_cast<int64_t>(hv) * V + v0 + c] = x;
+      rhs[(64 + i) * kRow32 + c] = -x;
     }
     // ---- dh step: needs [Q; W]; K, dv_local of the next chunk come in meanwhile
     __syncthreads();  // K and dv_local of this chunk are no longer read
@@ -203,17 +194,17 @@ __global__ void __launch_bounds__(kT) bwd_state_kernel(const gdn_chunk_bwd_args 
       cp_async_wait<0>();
     }
     __syncthreads();
-    for (int e = tid; e < 128 * kVS; e += kT) dh[e] *= eg;
-    gemm_smem<true>(dh, kVS, min(K, 64), kVS, 128, qw, 1, LD, rhs, kVS, 1);
-    if (K > 64) gemm_smem<true>(dh + 64 * kVS, kVS, K - 64, kVS, 128, qw + 64, 1, LD, rhs, kVS, 1);
+    for (int e = tid; e < 128 * kVS; e += kT) dh[(e / kVS) * kRow32 + e % kVS] *= eg;
+    gemm_smem<true>(dh, kRow32, min(K, 64), kVS, 128, qw, 1, kRowN, rhs, kRow32, 1);
+    if (K > 64) gemm_smem<true>(dh + 64 * kRow32, kRow32, K - 64, kVS, 128, qw + 64, 1, kRowN, rhs, kRow32, 1);
   }
   __syncthreads();
   if (p.dh0) {
     for (int e = tid; e < K * kVS; e += kT) {
-      const int kk = e / kVS, vv = v0 + e % kVS;
-      if (vv >= V) continue;
-      if (p.state_v_first) p.dh0[((n * p.HV + hv) * V + vv) * K + kk] = dh[e];
-      else p.dh0[((n * p.HV + hv) * K + kk) * V + vv] = dh[e];
+      const int kk = e / kVS, c = e % kVS, vv = v0 + c;
+      if (c >= vcols) continue;
+      if (p.state_v_first) p.dh0[((n * p.HV + hv) * V + vv) * K + kk] = dh[kk * kRow32 + c];
+      else p.dh0[((n * p.HV + hv) * K + kk) * V + vv] = dh[kk * kRow32 + c];
     }
   }
 }
@@ -227,13 +218,13 @@ template <typename T>
 __global__ void __launch_bounds__(kT, 1) bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
-  float* qc = sm;               // [64][LD]
-  float* kc = qc + 64 * LD;     // [64][LD]
-  float* dOs = kc + 64 * LD;    // [64][LD] dO
-  float* X = dOs + 64 * LD;     // [64][LD] v_new, then dv
-  float* dq = X + 64 * LD;      // [64][LD]
-  float* dk = dq + 64 * LD;     // [64][LD]
-  float* dP = dk + 64 * LD;     // [64][kP]
+  float* qc = sm;               // [64][LQ]
+  float* kc = qc + 64 * LQ;     // [64][LQ]
+  float* dOs = kc + 64 * LQ;    // [64][LQ] dO
+  float* X = dOs + 64 * LQ;     // [64][LQ] v_new, then dv
+  float* dq = X + 64 * LQ;      // [64][LQ]
+  float* dk = dq + 64 * LQ;     // [64][LQ]
+  float* dP = dk + 64 * LQ;     // [64][kP]
   float* gcs = dP + 64 * kP;    // [64]
   float* red = gcs + 64;        // [32]
   float* st = red + 32;         // gemm staging
@@ -256,30 +247,30 @@ __global__ void __launch_bounds__(kT, 1) bwd_dqkw_kernel(const gdn_chunk_bwd_arg
   for (int e = tid; e < 64 * K; e += kT) {
     const int i = e / K, kk = e % K;
     const bool ok = i < L;
-    qc[i * LD + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
-    kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
+    qc[i * LQ + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
+    kc[i * LQ + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
   }
   for (int e = tid; e < 64 * V; e += kT) {
     const int i = e / V, vv = e % V;
     const bool ok = i < L;
-    dOs[i * LD + vv] = ok ? to_f<T>(dO[i * rowV + vv]) : 0.f;
-    X[i * LD + vv] = ok ? vn[i * rowV + vv] : 0.f;
+    dOs[i * LQ + vv] = ok ? to_f<T>(dO[i * rowV + vv]) : 0.f;
+    X[i * LQ + vv] = ok ? vn[i * rowV + vv] : 0.f;
   }
   if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
-  gemm_smem<false>(dP, kP, 64, 64, V, dOs, LD, 1, X, 1, LD);  // dO v^T
+  gemm_smem<false>(dP, kP, 64, 64, V, dOs, LQ, 1, X, 1, LQ);  // dO v^T
   for (int e = tid; e < 64 * 64; e += kT) {
     const int i = e >> 6, j = e & 63;
     dP[i * kP + j] = (i < L && j <= i) ? scale * expf(gcs[i] - gcs[j]) * dP[i * kP + j] : 0.f;
   }
-  gemm<false>(dk, LD, 64, K, V, X, LD, 1, 64, dhn, 1, V, K, 1.f, st);  // v dh'^T
+  gemm<false>(dk, LQ, 64, K, V, X, LQ, 1, 64, dhn, 1, V, K, 1.f, st);  // v dh'^T
   const float glast = gcs[L - 1], eg = expf(glast);
   float E = 0.f;
   if (tid < 64) {  // dK = diag(c) v dh'^T; E_i = k_i . dK_i
     const float c = tid < L ? expf(glast - gcs[tid]) : 0.f;
     for (int kk = 0; kk < K; ++kk) {
-      const float x = c * dk[tid * LD + kk];
-      dk[tid * LD + kk] = x;
-      E = fmaf(kc[tid * LD + kk], x, E);
+      const float x = c * dk[tid * LQ + kk];
+      dk[tid * LQ + kk] = x;
+      E = fmaf(kc[tid * LQ + kk], x, E);
     }
   }
   float part = 0.f;
@@ -288,28 +279,28 @@ __global__ void __launch_bounds__(kT, 1) bwd_dqkw_kernel(const gdn_chunk_bwd_arg
   const float Esum = block_sum(tid < 64 ? E : 0.f, red);
   for (int e = tid; e < 64 * V; e += kT) {  // X <- dv
     const int i = e / V, vv = e % V;
-    X[i * LD + vv] = i < L ? dvn[i * rowV + vv] : 0.f;
+    X[i * LQ + vv] = i < L ? dvn[i * rowV + vv] : 0.f;
   }
-  gemm<false>(dq, LD, 64, K, V, dOs, LD, 1, 64, hst, 1, V, K, scale, st);  // scale dO h^T
+  gemm<false>(dq, LQ, 64, K, V, dOs, LQ, 1, 64, hst, 1, V, K, scale, st);  // scale dO h^T
   for (int e = tid; e < 64 * K; e += kT) {
     const int i = e / K, kk = e % K;
-    dq[i * LD + kk] *= i < L ? expf(gcs[i]) : 0.f;
+    dq[i * LQ + kk] *= i < L ? expf(gcs[i]) : 0.f;
   }
-  gemm_smem<true>(dq, LD, 64, K, 64, dP, kP, 1, kc, LD, 1);  // + dP K
-  gemm_smem<true>(dk, LD, 64, K, 64, dP, 1, kP, qc, LD, 1);  // + dP^T Q
+  gemm_smem<true>(dq, LQ, 64, K, 64, dP, kP, 1, kc, LQ, 1);  // + dP K
+  gemm_smem<true>(dk, LQ, 64, K, 64, dP, 1, kP, qc, LQ, 1);  // + dP^T Q
   // dW = -dv h^T straight to the workspace
-  gemm<false>(w.dw + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, V, X, LD, 1, 64, hst, 1, V, K, -1.f,
+  gemm<false>(w.dw + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, V, X, LQ, 1, 64, hst, 1, V, K, -1.f,
               st);
   if (tid < 64) {
     float a = 0.f;
-    for (int kk = 0; kk < K; ++kk) a += qc[tid * LD + kk] * dq[tid * LD + kk] - kc[tid * LD + kk] * dk[tid * LD + kk];
+    for (int kk = 0; kk < K; ++kk) a += qc[tid * LQ + kk] * dq[tid * LQ + kk] - kc[tid * LQ + kk] * dk[tid * LQ + kk];
     if (tid == L - 1) a += eg * hh + Esum;
     if (tid < L) w.dG[(s + tid) * p.HV + hv] = a;
   }
   for (int e = tid; e < L * K; e += kT) {
     const int i = e / K, kk = e % K;
-    w.dqh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dq[i * LD + kk];
-    w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dk[i * LD + kk];
+    w.dqh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dq[i * LQ + kk];
+    w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dk[i * LQ + kk];
   }
 }
 
@@ -361,23 +352,23 @@ __global__ void __launch_bounds__(kT, 1) bwd_wy_kernel(const gdn_chunk_bwd_args 
     bs[tid] = bt;
     cw[tid] = ok ? bt * expf(g) : 0.f;
   }
-  gemm<false>(Sk, kP, 64, 64, K, kc, LD, 1, 64, kc, 1, LD, 64, 1.f, st);  // K K^T
+  gemm_smem<false>(Sk, kP, 64, 64, K, kc, LD, 1, kc, 1, LD);  // K K^T
   for (int e = tid; e < 64 * 64; e += kT) {
     const int i = e >> 6, j = e & 63;
     Am[i * kP + j] = (i < L && j < i) ? bs[i] * expf(gcs[i] - gcs[j]) * Sk[i * kP + j] : 0.f;
   }
   __syncthreads();
   solve_tril64_nt<kT>(Am, Tm, Zs);  // T = (I + A)^-1
-  gemm<false>(dT, kP, 64, 64, K, b1, LD, 1, 64, kc, 1, LD, 64, 1.f, st);     // dW K^T
+  gemm_smem<false>(dT, kP, 64, 64, K, b1, LD, 1, kc, 1, LD);     // dW K^T
   gemm<false>(tm, kP, 64, 64, V, dvn, rowV, 1, L, vin, 1, rowV, L, 1.f, st);  // dv V^T
   for (int e = tid; e < 64 * 64; e += kT) {
     const int i = e >> 6, j = e & 63;
     dT[i * kP + j] = dT[i * kP + j] * cw[j] + tm[i * kP + j] * bs[j];
   }
-  gemm<false>(b2, LD, 64, K, 64, Tm, 1, kTS, 64, b1, LD, 1, K, 1.f, st);     // dR_w = T^T dW
+  gemm_smem<false>(b2, LD, 64, K, 64, Tm, 1, kTS, b1, LD, 1);     // dR_w = T^T dW
   gemm<false>(b1, LD, 64, V, L, Tm, 1, kTS, 64, dvn, rowV, 1, V, 1.f, st);   // dR_u = T^T dv
-  gemm<false>(tm, kP, 64, 64, 64, dT, kP, 1, 64, Tm, 1, kTS, 64, 1.f, st);   // dT T^T
-  gemm<false>(dT, kP, 64, 64, 64, Tm, 1, kTS, 64, tm, kP, 1, 64, -1.f, st);  // dA = -T^T (dT T^T)
+  gemm_smem<false>(tm, kP, 64, 64, 64, dT, kP, 1, Tm, 1, kTS);   // dT T^T
+  gemm_smem<false>(dT, kP, 64, 64, 64, Tm, 1, kTS, tm, kP, 1, -1.f);  // dA = -T^T (dT T^T)
   T* dv = static_cast<T*>(p.dv) + s * rowV + static_cast<int64_t>(hv) * V;
   for (int e = tid; e < L * V; e += kT) {
     const int i = e / V, vv = e % V;
@@ -415,8 +406,8 @@ __global__ void __launch_bounds__(kT, 1) bwd_wy_kernel(const gdn_chunk_bwd_args 
     for (int j = 0; j < 64; ++j) f += Am[tid * kP + j] * Sk[tid * kP + j] - Am[j * kP + tid] * Sk[j * kP + tid];
     dG[tid] += f;
   }
-  gemm<true>(b2, LD, 64, K, 64, Am, kP, 1, 64, kc, LD, 1, K, 1.f, st);  // + dS K
-  gemm<true>(b2, LD, 64, K, 64, Am, 1, kP, 64, kc, LD, 1, K, 1.f, st);  // + dS^T K
+  gemm_smem<true>(b2, LD, 64, K, 64, Am, kP, 1, kc, LD, 1);  // + dS K
+  gemm_smem<true>(b2, LD, 64, K, 64, Am, 1, kP, kc, LD, 1);  // + dS^T K
   for (int e = tid; e < L * K; e += kT) {
     const int i = e / K, kk = e % K;
     w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] += b2[i * LD + kk];
@@ -498,8 +489,8 @@ __global__ void bwd_dg_kernel(const gdn_chunk_bwd_args p, const int64_t* __restr
 }
 
 constexpr size_t kDvlSmem = sizeof(float) * (3 * 64 * LD + 64 * kP + 64);
-constexpr size_t kStateSmem = sizeof(float) * (kSqw + kSk + kSvec + 2 * 128 * kVS);
-constexpr size_t kDqkwSmem = sizeof(float) * (6 * 64 * LD + 64 * kP + 64 + 32 + kStage);
+constexpr size_t kStateSmem = sizeof(float) * (kSqw + kSk + kSvec + 2 * 128 * kRow32);
+constexpr size_t kDqkwSmem = sizeof(float) * (6 * 64 * LQ + 64 * kP + 64 + 32 + kStage);
 static_assert(kDqkwSmem <= 227 * 1024, "bwd_dqkw_kernel shared memory");
 constexpr size_t kWySmem =
     sizeof(float) * (64 * kTS + kTrilScratch + 3 * 64 * LD + 4 * 64 * kP + 5 * 64 + kStage);

@@ -13,7 +13,7 @@
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
-#include "simt_gemm.cuh"
+#include "tile_gemm.cuh"
 #include "solve_tril.cuh"
 
 namespace gdn {
@@ -93,7 +93,7 @@ struct GenericPtrs {
   float* hs;
 };
 
-constexpr int kLD = 129;  // row stride of 64 x K fp32 tiles (conflict-free transposed reads)
+constexpr int kLD = kRowK;  // row stride of 64 x K fp32 tiles (row-major / k-contiguous reads)
 
 // Per (chunk, v-head): G = chunk-local cumsum of g, A = tril_strict(diag(beta)
 // exp(G_i - G_j) K K^T), T = (I + A)^-1, W = T diag(beta exp(G)) K,
@@ -165,52 +165,45 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
 }
 
 constexpr int kStateCols = 32;
-constexpr int kStateStage = 2 * 64 * kLD + 64 * kStateCols + 64;  // wc, kc, u slice, G
+constexpr int kStateStage = 64 * kRowK + 64 * kRowN + 64 * kRow32 + 64;  // wc, kc, u slice, G
 
 // Inter-chunk recurrence for one (sequence, v-head, 32-column slice of V):
 // per chunk v_new = U - W h, h <- exp(G_last) h + K^T diag(exp(G_last - G)) v_new.
 // The next chunk's W, K, U and G are copied in (cp.async) while the current
 // chunk computes.
-__global__ void __launch_bounds__(kGemmThreads)
+__global__ void __launch_bounds__(kGemmThreads, 1)
 chunk_state_kernel(const gdn_chunk_args p, const GenericPtrs w) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
-  float* hsm = sm;                          // [128][32] state slice
-  float* stage0 = hsm + 128 * kStateCols;   // 2 stages of kStateStage floats
+  float* hsm = sm;                          // [128][kRow32] state slice
+  float* stage0 = hsm + 128 * kRow32;       // 2 stages of kStateStage floats
   const int64_t n = blockIdx.x;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
   const int v0 = blockIdx.z * kStateCols;
+  const int vcols = V - v0 < kStateCols ? V - v0 : kStateCols;
   const int tid = threadIdx.x;
   const int64_t rowK = static_cast<int64_t>(p.HV) * K, rowV = static_cast<int64_t>(p.HV) * V;
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
   for (int e = tid; e < 128 * kStateCols; e += kGemmThreads) {
-    const int kk = e / kStateCols, vv = v0 + e % kStateCols;
+    const int kk = e / kStateCols, c = e % kStateCols, vv = v0 + c;
     float x = 0.f;
     if (p.initial_state && vv < V && kk < K)
       x = p.state_v_first ? p.initial_state[((n * p.HV + hv) * V + vv) * K + kk]
                           : p.initial_state[((n * p.HV + hv) * K + kk) * V + vv];
-    hsm[e] = x;
+    hsm[kk * kRow32 + c] = x;
   }
   const int64_t nchunks = eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0;
   auto issue = [&](int64_t lc) {
     float* wc = stage0 + (lc & 1) * kStateStage;
-    float* kc = wc + 64 * kLD;
-    float* us = kc + 64 * kLD;
-    float* gs = us + 64 * kStateCols;
+    float* kc = wc + 64 * kRowK;
+    float* us = kc + 64 * kRowN;
+    float* gs = us + 64 * kRow32;
     const int64_t s = bos + lc * kChunk;
     const int L = static_cast<int>(min64(kChunk, eos - s));
-    for (int e = tid; e < 64 * K; e += kGemmThreads) {
-      const int i = e / K, kk = e % K;
-      const bool ok = i < L;
-      cp_async4(wc + i * kLD + kk, ok ? w.w + (s + i) * rowK + static_cast<int64_t>(hv) * K + kk : w.w, ok);
-      cp_async4(kc + i * kLD + kk, ok ? w.kn + ((s + i) * p.H + h) * K + kk : w.kn, ok);
-    }
-    for (int e = tid; e < 64 * kStateCols; e += kGemmThreads) {
-      const int i = e / kStateCols, vv = v0 + e % kStateCols;
-      const bool ok = i < L && vv < V;
-      cp_async4(us + e, ok ? w.u + (s + i) * rowV + static_cast<int64_t>(hv) * V + vv : w.u, ok);
-    }
+    tile_async(wc, kRowK, w.w + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, 64, K, K);
+    tile_async(kc, kRowN, w.kn + (s * p.H + h) * K, static_cast<int64_t>(p.H) * K, L, 64, K, K);
+    tile_async(us, kRow32, w.u + s * rowV + static_cast<int64_t>(hv) * V + v0, rowV, L, 64, vcols, kStateCols);
     if (tid < 64) cp_async4(gs + tid, tid < L ? w.gc + (s + tid) * p.HV + hv : w.gc, tid < L);
     cp_async_commit();
   };
@@ -220,9 +213,9 @@ chunk_state_kernel(const gdn_chunk_args p, const GenericPtrs w) {
     const int L = static_cast<int>(min64(kChunk, eos - s));
     const int64_t cidx = w.coff[n] + lc;
     float* wc = stage0 + (lc & 1) * kStateStage;
-    float* kc = wc + 64 * kLD;
-    float* us = kc + 64 * kLD;
-    float* gs = us + 64 * kStateCols;
+    float* kc = wc + 64 * kRowK;
+    float* us = kc + 64 * kRowN;
+    float* gs = us + 64 * kRow32;
     if (lc + 1 < nchunks) {
       issue(lc + 1);  // the other stage was last read before the previous iteration's final barrier
       cp_async_wait<1>();
@@ -232,29 +225,29 @@ chunk_state_kernel(const gdn_chunk_args p, const GenericPtrs w) {
     __syncthreads();
     float* hg = w.hs + (cidx * p.HV + hv) * static_cast<int64_t>(K) * V;
     for (int e = tid; e < K * kStateCols; e += kGemmThreads) {
-      const int kk = e / kStateCols, vv = v0 + e % kStateCols;
-      if (vv < V) hg[kk * V + vv] = hsm[e];
+      const int kk = e / kStateCols, c = e % kStateCols;
+      if (c < vcols) hg[kk * V + v0 + c] = hsm[kk * kRow32 + c];
     }
-    gemm_smem<true>(us, kStateCols, 64, kStateCols, K, wc, kLD, 1, hsm, kStateCols, 1, -1.f);  // U - W h
+    gemm_smem<true>(us, kRow32, 64, kStateCols, K, wc, kRowK, 1, hsm, kRow32, 1, -1.f);  // U - W h
     const float glast = gs[L - 1], eg = expf(glast);
     for (int e = tid; e < 64 * kStateCols; e += kGemmThreads) {
-      const int i = e / kStateCols, vv = v0 + e % kStateCols;
-      const float x = us[e];
-      if (i < L && vv < V) w.vnew[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv] = x;
-      us[e] = i < L ? x * expf(glast - gs[i]) : 0.f;
+      const int i = e / kStateCols, c = e % kStateCols;
+      const float x = us[i * kRow32 + c];
+      if (i < L && c < vcols) w.vnew[(s + i) * rowV + static_cast<int64_t>(hv) * V + v0 + c] = x;
+      us[i * kRow32 + c] = i < L ? x * expf(glast - gs[i]) : 0.f;
     }
-    for (int e = tid; e < K * kStateCols; e += kGemmThreads) hsm[e] *= eg;
-    gemm_smem<true>(hsm, kStateCols, min(K, 64), kStateCols, 64, kc, 1, kLD, us, kStateCols, 1);
+    for (int e = tid; e < K * kStateCols; e += kGemmThreads) hsm[(e / kStateCols) * kRow32 + e % kStateCols] *= eg;
+    gemm_smem<true>(hsm, kRow32, min(K, 64), kStateCols, 64, kc, 1, kRowN, us, kRow32, 1);
     if (K > 64)
-      gemm_smem<true>(hsm + 64 * kStateCols, kStateCols, K - 64, kStateCols, 64, kc + 64, 1, kLD, us, kStateCols, 1);
+      gemm_smem<true>(hsm + 64 * kRow32, kRow32, K - 64, kStateCols, 64, kc + 64, 1, kRowN, us, kRow32, 1);
   }
   __syncthreads();
   if (p.final_state) {
     for (int e = tid; e < K * kStateCols; e += kGemmThreads) {
-      const int kk = e / kStateCols, vv = v0 + e % kStateCols;
-      if (vv >= V) continue;
-      if (p.state_v_first) p.final_state[((n * p.HV + hv) * V + vv) * K + kk] = hsm[e];
-      else p.final_state[((n * p.HV + hv) * K + kk) * V + vv] = hsm[e];
+      const int kk = e / kStateCols, c = e % kStateCols, vv = v0 + c;
+      if (c >= vcols) continue;
+      if (p.state_v_first) p.final_state[((n * p.HV + hv) * V + vv) * K + kk] = hsm[kk * kRow32 + c];
+      else p.final_state[((n * p.HV + hv) * K + kk) * V + vv] = hsm[kk * kRow32 + c];
     }
   }
 }
@@ -359,7 +352,7 @@ static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws
   }
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
   const size_t wy_smem = sizeof(float) * (64 * kTS + kTrilScratch + 64 * 65 + 2 * 64 * kLD + 2 * 64);
-  const size_t st_smem = sizeof(float) * (128 * kStateCols + 2 * kStateStage);
+  const size_t st_smem = sizeof(float) * (128 * kRow32 + 2 * kStateStage);
   const size_t out_smem = sizeof(float) * (3 * 64 * kLD + 64 * 65 + 64 + kGemmStage);
   if ((e = cudaFuncSetAttribute(chunk_wy_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(wy_smem))) != cudaSuccess) return e;
