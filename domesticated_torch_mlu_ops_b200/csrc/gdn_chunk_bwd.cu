@@ -79,15 +79,17 @@ __global__ void __launch_bounds__(kT, 1) bwd_dvlocal_kernel(const gdn_chunk_bwd_
   const int tid = threadIdx.x;
   const int64_t rowQ = static_cast<int64_t>(p.H) * K, rowV = static_cast<int64_t>(p.HV) * V;
   const T* dout = static_cast<const T*>(p.dout) + s * rowV + static_cast<int64_t>(hv) * V;
-  for (int e = tid; e < 64 * K; e += kT) {
-    const int i = e / K, kk = e % K;
-    const bool ok = i < L;
-    qc[i * LD + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
-    kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
+    for (int kk = tid & 31; kk < K; kk += 32) {
+      const bool ok = i < L;
+      qc[i * LD + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
+      kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
+    }
   }
-  for (int e = tid; e < 64 * V; e += kT) {
-    const int i = e / V, vv = e % V;
-    dO[i * LD + vv] = i < L ? to_f<T>(dout[i * rowV + vv]) : 0.f;
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
+    for (int vv = tid & 31; vv < V; vv += 32) {
+      dO[i * LD + vv] = i < L ? to_f<T>(dout[i * rowV + vv]) : 0.f;
+    }
   }
   if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
   gemm_smem<false>(P, kP, 64, 64, K, qc, LD, 1, kc, 1, LD);  // Q K^T
@@ -244,17 +246,19 @@ __global__ void __launch_bounds__(kT, 1) bwd_dqkw_kernel(const gdn_chunk_bwd_arg
   const float* vn = w.vnew + s * rowV + static_cast<int64_t>(hv) * V;          // rows, stride rowV
   const float* dvn = w.dvn + s * rowV + static_cast<int64_t>(hv) * V;
   const T* dO = static_cast<const T*>(p.dout) + s * rowV + static_cast<int64_t>(hv) * V;
-  for (int e = tid; e < 64 * K; e += kT) {
-    const int i = e / K, kk = e % K;
-    const bool ok = i < L;
-    qc[i * LQ + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
-    kc[i * LQ + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
+    for (int kk = tid & 31; kk < K; kk += 32) {
+      const bool ok = i < L;
+      qc[i * LQ + kk] = ok ? w.qn[(s + i) * rowQ + h * K + kk] : 0.f;
+      kc[i * LQ + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
+    }
   }
-  for (int e = tid; e < 64 * V; e += kT) {
-    const int i = e / V, vv = e % V;
-    const bool ok = i < L;
-    dOs[i * LQ + vv] = ok ? to_f<T>(dO[i * rowV + vv]) : 0.f;
-    X[i * LQ + vv] = ok ? vn[i * rowV + vv] : 0.f;
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
+    for (int vv = tid & 31; vv < V; vv += 32) {
+      const bool ok = i < L;
+      dOs[i * LQ + vv] = ok ? to_f<T>(dO[i * rowV + vv]) : 0.f;
+      X[i * LQ + vv] = ok ? vn[i * rowV + vv] : 0.f;
+    }
   }
   if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
   gemm_smem<false>(dP, kP, 64, 64, V, dOs, LQ, 1, X, 1, LQ);  // dO v^T
@@ -277,14 +281,16 @@ __global__ void __launch_bounds__(kT, 1) bwd_dqkw_kernel(const gdn_chunk_bwd_arg
   for (int e = tid; e < K * V; e += kT) part = fmaf(dhn[e], hst[e], part);
   const float hh = block_sum(part, red);  // <dh', h>
   const float Esum = block_sum(tid < 64 ? E : 0.f, red);
-  for (int e = tid; e < 64 * V; e += kT) {  // X <- dv
-    const int i = e / V, vv = e % V;
-    X[i * LQ + vv] = i < L ? dvn[i * rowV + vv] : 0.f;
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {  // X <- dv
+    for (int vv = tid & 31; vv < V; vv += 32) {
+      X[i * LQ + vv] = i < L ? dvn[i * rowV + vv] : 0.f;
+    }
   }
   gemm<false>(dq, LQ, 64, K, V, dOs, LQ, 1, 64, hst, 1, V, K, scale, st);  // scale dO h^T
-  for (int e = tid; e < 64 * K; e += kT) {
-    const int i = e / K, kk = e % K;
-    dq[i * LQ + kk] *= i < L ? expf(gcs[i]) : 0.f;
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
+    for (int kk = tid & 31; kk < K; kk += 32) {
+      dq[i * LQ + kk] *= i < L ? expf(gcs[i]) : 0.f;
+    }
   }
   gemm_smem<true>(dq, LQ, 64, K, 64, dP, kP, 1, kc, LQ, 1);  // + dP K
   gemm_smem<true>(dk, LQ, 64, K, 64, dP, 1, kP, qc, LQ, 1);  // + dP^T Q
@@ -297,10 +303,11 @@ __global__ void __launch_bounds__(kT, 1) bwd_dqkw_kernel(const gdn_chunk_bwd_arg
     if (tid == L - 1) a += eg * hh + Esum;
     if (tid < L) w.dG[(s + tid) * p.HV + hv] = a;
   }
-  for (int e = tid; e < L * K; e += kT) {
-    const int i = e / K, kk = e % K;
-    w.dqh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dq[i * LQ + kk];
-    w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dk[i * LQ + kk];
+  for (int i = tid >> 5; i < L; i += kGemmThreads / 32) {
+    for (int kk = tid & 31; kk < K; kk += 32) {
+      w.dqh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dq[i * LQ + kk];
+      w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] = dk[i * LQ + kk];
+    }
   }
 }
 
@@ -338,11 +345,12 @@ __global__ void __launch_bounds__(kT, 1) bwd_wy_kernel(const gdn_chunk_bwd_args 
   const T* vin = static_cast<const T*>(p.v) + s * rowV + static_cast<int64_t>(hv) * V;
   const float* dvn = w.dvn + s * rowV + static_cast<int64_t>(hv) * V;
   const float* dwp = w.dw + s * rowK + static_cast<int64_t>(hv) * K;
-  for (int e = tid; e < 64 * K; e += kT) {
-    const int i = e / K, kk = e % K;
-    const bool ok = i < L;
-    kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
-    b1[i * LD + kk] = ok ? dwp[i * rowK + kk] : 0.f;
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
+    for (int kk = tid & 31; kk < K; kk += 32) {
+      const bool ok = i < L;
+      kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
+      b1[i * LD + kk] = ok ? dwp[i * rowK + kk] : 0.f;
+    }
   }
   if (tid < 64) {
     const bool ok = tid < L;
@@ -370,9 +378,10 @@ __global__ void __launch_bounds__(kT, 1) bwd_wy_kernel(const gdn_chunk_bwd_args 
   gemm_smem<false>(tm, kP, 64, 64, 64, dT, kP, 1, Tm, 1, kTS);   // dT T^T
   gemm_smem<false>(dT, kP, 64, 64, 64, Tm, 1, kTS, tm, kP, 1, -1.f);  // dA = -T^T (dT T^T)
   T* dv = static_cast<T*>(p.dv) + s * rowV + static_cast<int64_t>(hv) * V;
-  for (int e = tid; e < L * V; e += kT) {
-    const int i = e / V, vv = e % V;
-    dv[i * rowV + vv] = from_f<T>(bs[i] * b1[i * LD + vv]);
+  for (int i = tid >> 5; i < L; i += kGemmThreads / 32) {
+    for (int vv = tid & 31; vv < V; vv += 32) {
+      dv[i * rowV + vv] = from_f<T>(bs[i] * b1[i * LD + vv]);
+    }
   }
   if (tid < 64) {
     const int i = tid;
@@ -396,9 +405,10 @@ __global__ void __launch_bounds__(kT, 1) bwd_wy_kernel(const gdn_chunk_bwd_args 
     const int i = e >> 6, j = e & 63;
     Am[i * kP + j] = (i < L && j < i) ? bs[i] * expf(gcs[i] - gcs[j]) * dT[i * kP + j] : 0.f;
   }
-  for (int e = tid; e < 64 * K; e += kT) {  // dK = diag(b Gam) dR_w
-    const int i = e / K, kk = e % K;
-    b2[i * LD + kk] *= cw[i];
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {  // dK = diag(b Gam) dR_w
+    for (int kk = tid & 31; kk < K; kk += 32) {
+      b2[i * LD + kk] *= cw[i];
+    }
   }
   __syncthreads();
   if (tid < 64) {  // D path of A: F = dS * S; dG_i += sum_j F_ij - sum_j F_ji
@@ -408,9 +418,10 @@ __global__ void __launch_bounds__(kT, 1) bwd_wy_kernel(const gdn_chunk_bwd_args 
   }
   gemm_smem<true>(b2, LD, 64, K, 64, Am, kP, 1, kc, LD, 1);  // + dS K
   gemm_smem<true>(b2, LD, 64, K, 64, Am, 1, kP, kc, LD, 1);  // + dS^T K
-  for (int e = tid; e < L * K; e += kT) {
-    const int i = e / K, kk = e % K;
-    w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] += b2[i * LD + kk];
+  for (int i = tid >> 5; i < L; i += kGemmThreads / 32) {
+    for (int kk = tid & 31; kk < K; kk += 32) {
+      w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] += b2[i * LD + kk];
+    }
   }
   if (tid < L) {
     p.dbeta[(s + tid) * p.HV + hv] = db[tid];

@@ -120,13 +120,15 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
   const int tid = threadIdx.x;
   const int64_t rowK = static_cast<int64_t>(p.HV) * K, rowV = static_cast<int64_t>(p.HV) * V;
   const T* vb = static_cast<const T*>(p.v);
-  for (int e = tid; e < 64 * K; e += kGemmThreads) {
-    const int i = e / K, kk = e % K;
-    ks[i * kLD + kk] = i < L ? w.kn[((s + i) * p.H + h) * K + kk] : 0.f;
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
+    for (int kk = tid & 31; kk < K; kk += 32) {
+      ks[i * kLD + kk] = i < L ? w.kn[((s + i) * p.H + h) * K + kk] : 0.f;
+    }
   }
-  for (int e = tid; e < 64 * V; e += kGemmThreads) {
-    const int i = e / V, vv = e % V;
-    vs[i * kLD + vv] = i < L ? to_f<T>(vb[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv]) : 0.f;
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
+    for (int vv = tid & 31; vv < V; vv += 32) {
+      vs[i * kLD + vv] = i < L ? to_f<T>(vb[(s + i) * rowV + static_cast<int64_t>(hv) * V + vv]) : 0.f;
+    }
   }
   if (tid < 32) {  // chunk-local cumsum of g: warp scan over 2 x 32 values
     float x0 = tid < L ? p.g[(s + tid) * p.HV + hv] : 0.f;
@@ -152,13 +154,15 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
   }
   __syncthreads();
   solve_tril64_nt<kGemmThreads>(A, Tm, Zs);  // (I + A)^-1; ends with a barrier
-  for (int e = tid; e < 64 * K; e += kGemmThreads) {  // rows of K by beta exp(G)
-    const int i = e / K, kk = e % K;
-    ks[i * kLD + kk] *= bs[i] * expf(gcs[i]);
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {  // rows of K by beta exp(G)
+    for (int kk = tid & 31; kk < K; kk += 32) {
+      ks[i * kLD + kk] *= bs[i] * expf(gcs[i]);
+    }
   }
-  for (int e = tid; e < 64 * V; e += kGemmThreads) {  // rows of V by beta
-    const int i = e / V, vv = e % V;
-    vs[i * kLD + vv] *= bs[i];
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {  // rows of V by beta
+    for (int vv = tid & 31; vv < V; vv += 32) {
+      vs[i * kLD + vv] *= bs[i];
+    }
   }
   gemm_smem<false>(w.w + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, 64, Tm, kTS, 1, ks, kLD, 1);
   gemm_smem<false>(w.u + s * rowV + static_cast<int64_t>(hv) * V, rowV, L, V, 64, Tm, kTS, 1, vs, kLD, 1);
@@ -274,10 +278,11 @@ chunk_out_kernel(const gdn_chunk_args p, const GenericPtrs w, float scale) {
   const int64_t cidx = blockIdx.x;
   const int tid = threadIdx.x;
   const int64_t rowV = static_cast<int64_t>(p.HV) * V;
-  for (int e = tid; e < 64 * K; e += kGemmThreads) {
-    const int i = e / K, kk = e % K;
-    qc[i * kLD + kk] = i < L ? w.qn[((s + i) * p.H + h) * K + kk] : 0.f;
-    kc[i * kLD + kk] = i < L ? w.kn[((s + i) * p.H + h) * K + kk] : 0.f;
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
+    for (int kk = tid & 31; kk < K; kk += 32) {
+      qc[i * kLD + kk] = i < L ? w.qn[((s + i) * p.H + h) * K + kk] : 0.f;
+      kc[i * kLD + kk] = i < L ? w.kn[((s + i) * p.H + h) * K + kk] : 0.f;
+    }
   }
   if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
   gemm_smem<false>(att, 65, 64, 64, K, qc, kLD, 1, kc, 1, kLD);  // Q K^T
@@ -287,16 +292,18 @@ chunk_out_kernel(const gdn_chunk_args p, const GenericPtrs w, float scale) {
   }
   const float* hc = w.hs + (cidx * p.HV + hv) * static_cast<int64_t>(K) * V;
   gemm_staged<false>(oc, kLD, 64, V, K, qc, kLD, 1, 64, hc, V, 1, V, 1.f, st);  // Q h
-  for (int e = tid; e < 64 * V; e += kGemmThreads) {
-    const int i = e / V, vv = e % V;
-    oc[i * kLD + vv] *= expf(gcs[i]);
+  for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
+    for (int vv = tid & 31; vv < V; vv += 32) {
+      oc[i * kLD + vv] *= expf(gcs[i]);
+    }
   }
   const float* vn = w.vnew + s * rowV + static_cast<int64_t>(hv) * V;
   gemm_staged<true>(oc, kLD, 64, V, L, att, 65, 1, 64, vn, rowV, 1, V, 1.f, st);  // + P v_new
   T* ob = static_cast<T*>(p.o) + s * rowV + static_cast<int64_t>(hv) * V;
-  for (int e = tid; e < L * V; e += kGemmThreads) {
-    const int i = e / V, vv = e % V;
-    ob[i * rowV + vv] = from_f<T>(scale * oc[i * kLD + vv]);
+  for (int i = tid >> 5; i < L; i += kGemmThreads / 32) {
+    for (int vv = tid & 31; vv < V; vv += 32) {
+      ob[i * rowV + vv] = from_f<T>(scale * oc[i * kLD + vv]);
+    }
   }
 }
 
