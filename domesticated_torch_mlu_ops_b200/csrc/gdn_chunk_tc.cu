@@ -171,9 +171,9 @@ constexpr int kWyThreads = 256;
 // ([128/S][64][S], S = 32 or 64).  The 16-byte chunks of each row are
 // XOR-swizzled so that eight consecutive rows touch distinct bank groups.
 __device__ __forceinline__ int u_off(int i, int c, int S) {
-  const int C = S >> 3;  // 16-byte chunks per row
-  const int sw = (i / (8 / C)) & (C - 1);
-  const int sl = c / S, wc = c % S;
+  const bool s64 = S == 64;
+  const int sw = s64 ? (i & 7) : ((i >> 1) & 3);  // (i / (8 / chunks per row)) mod chunks per row
+  const int sl = c >> (s64 ? 6 : 5), wc = c & (S - 1);
   return (sl * 64 + i) * S + ((((wc >> 3) ^ sw)) << 3) + (wc & 7);
 }
 
