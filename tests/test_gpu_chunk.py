@@ -148,3 +148,22 @@ def test_solve_tril(ops):
         for dt, tol in ((torch.float32, 1e-6), (torch.bfloat16, 1e-2)):
             out = ops.solve_tril(_t(A), None, None if cu is None else _t(cu), dt)
             assert rel_rms(np64(out), ref) < tol
+
+
+TC_CASES = [
+    # (name, B, T, H, HV, cu, h0_std, state_v_first)
+    ("heads_equal", 2, 300, 16, 16, None, 0.02, False),
+    ("gva4_vfirst", 1, 500, 8, 32, None, 0.02, True),
+    ("many_sequences", 48, 128, 16, 32, None, 0.02, False),  # 1536 chains: widest state kernel
+    ("varlen_empty", 1, 400, 4, 8, [0, 0, 64, 64, 129, 400, 400], 0.02, False),
+]
+
+
+@pytest.mark.parametrize("case", TC_CASES, ids=[c[0] for c in TC_CASES])
+def test_bf16_tensor_core_path_variants(ops, case):
+    """The tcgen05 path (bf16, K = V = 128) across head ratios, state
+    layouts, the state-kernel variants picked by the number of chains, and
+    zero-length sequences."""
+    name, B, T, H, HV, cu, h0_std, vfirst = case
+    _check(ops, 17 + len(name), B, T, H, HV, 128, 128, torch.bfloat16, cu=cu, h0_std=h0_std,
+           state_v_first=vfirst)
