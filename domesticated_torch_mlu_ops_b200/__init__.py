@@ -1,5 +1,7 @@
-"""B200-native gated delta-rule (GDN) forward: drop-in for the GDN entry
-points of ``torch_mlu_ops.triton_ops`` and the causal conv1d that feeds them.
+"""B200-native gated delta-rule (GDN) ops: drop-in for the GDN entry points
+of ``torch_mlu_ops.triton_ops`` (chunked prefill with its autograd backward,
+slot-indexed recurrent decode, the plain recurrence) and the causal conv1d
+that feeds them, plus a prefill for inputs in host memory.
 
 The ops run hand-written sm_100a CUDA kernels in ``libgdn_b200.so``, called
 through its C ABI (``include/gdn_b200.h``).

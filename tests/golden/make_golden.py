@@ -1,9 +1,9 @@
 """Generate golden vectors from the reference's own Triton kernels.
 
-Run in a container that has the reference package mounted (read-only) at
-``--ref`` (default ``/root/reference``)::
+Run in a container that has the reference package mounted (read-only), its
+root given by ``--ref`` or the ``TMO_REFERENCE_ROOT`` environment variable::
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py --ref <reference package root>
 
 The reference cannot be imported as a package here (it needs ``torch_mlu``
 and Cambricon's Triton backend), so this script loads its kernel files by
@@ -486,9 +486,12 @@ def gen_conv(ref: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("TMO_REFERENCE_ROOT"),
+                    help="root of the reference torch_mlu_ops package (read-only)")
     ap.add_argument("--only", default="")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give --ref or set TMO_REFERENCE_ROOT")
     _install_shims(a.ref)
     torch.manual_seed(0)
     if a.only in ("", "rfn"):
