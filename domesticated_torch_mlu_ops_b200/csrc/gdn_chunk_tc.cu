@@ -21,15 +21,16 @@
 //   V-slices.  [K;Q] K^T and [T';T''] [K|V] are single M=128 MMAs, so every
 //   thread of the epilogues owns one row of the result.
 //
-// tc_state_kernel, one CTA per (sequence, v-head, V-slice of VS columns),
-// serial over the sequence's chunks (chunk_delta_h.py:28-197 fused with
-// chunk_o.py:30-170).  The fp32 state slice h (128 x VS) lives in registers
-// (thread t owns row t); its bf16 copy in shared memory is the B operand of
+// tc_state3_kernel, one CTA per (sequence, v-head, V-slice of VS = 32 or 64
+// columns; the slices of one head are adjacent CTAs), serial over the
+// sequence's chunks (chunk_delta_h.py:28-197 fused with chunk_o.py:30-170).
+// The fp32 state slice h (128 x VS) lives in registers (two threads per row);
+// its bf16 copy in shared memory is the B operand of
 //   [X; Y] = [W; Q] h                          (tcgen05, M=128)
-//   v_new = U - X, V~ = diag(b) v_new          (threads 0..63, fp32 -> bf16)
+//   v_new = U - X, V~ = diag(b) v_new          (rows 0..63, fp32 -> bf16)
 //   dH = K^T V~,  [.; O] = [0; P] v_new        (tcgen05, M=128)
-//   h <- gamma h + dH,  o = a * Y + scale * O  (all threads / threads 64..127)
-// so h and v_new never leave the SM.  One thread streams the next chunk's
+//   h <- gamma h + dH,  o = a * Y + scale * O  (all rows / rows 64..127)
+// so h and v_new never leave the SM.  A load warp streams the next chunks'
 // operands in with TMA / bulk copies while the current chunk computes.
 //
 // Every mbarrier wait is bounded; on timeout the kernel records an error in
@@ -51,7 +52,6 @@ namespace tc {
 constexpr int D = 128;                  // K = V = 128
 constexpr int kImg64x128 = 64 * D * 2;  // 16 KiB
 constexpr int kImg64x64 = 64 * 64 * 2;  // 8 KiB
-constexpr int RS128 = (D / 8) * 128;    // image row stride of a 128-column tile
 constexpr int RS64 = (64 / 8) * 128;    // image row stride of a 64-column tile
 constexpr int kScal = 132;              // per-(head, chunk) scalars: a[64], b[64], gamma, pad
 constexpr int kAtom = 64 * 128;         // one 64-row x 128-byte swizzled atom (8 KiB)
@@ -447,296 +447,26 @@ teardown:
 }
 
 // ---------------------------------------------------------------------------
-// State + output kernel
-// ---------------------------------------------------------------------------
-
-template <int VS>
-struct StSmem {
-  // Per stage (1 KiB aligned):
-  //   [W;Q]  one 128-row swizzled operand: W a0 | Q a0 | W a1 | Q a1
-  //   K      swizzled 64-row tile (atoms 8 KiB apart)
-  //   [0;P]  128 x 64 no-swizzle image whose top half stays zero
-  //   U slice (64 x VS, as [VS/S][64][S] swizzled slices of S = min(VS, 64)),
-  //   scalars (a, b, gamma)
-  static constexpr int kUBytes = 64 * VS * 2;
-  static constexpr int kWQ = 0;
-  static constexpr int kKt = 4 * kAtom;
-  static constexpr int kZP = kKt + 2 * kAtom;
-  static constexpr int kU = kZP + 2 * kImg64x64;
-  static constexpr int kScalOff = kU + kUBytes;
-  static constexpr int kStageBytes = ((kScalOff + kScal * 4 + 1023) / 1024) * 1024;
-  static constexpr uint32_t kTx = 3 * kImg64x128 + kImg64x64 + kUBytes + kScal * 4;
-  static constexpr int kBar = kScalOff + kScal * 4;      // in stage 0's tail padding
-  static constexpr int kTmem = kBar + 32;
-  static constexpr int kH = 2 * kStageBytes;             // h image 128 x VS
-  static constexpr int kVt = kH + D * VS * 2;            // V~ image 64 x VS
-  static constexpr int kVn = kVt + 64 * VS * 2;          // v_new image 64 x VS
-  static constexpr int kBytes = kVn + 64 * VS * 2 + 1024;
-  static_assert(kTmem + 8 <= kStageBytes, "barriers must fit in the stage padding");
-  // TMEM columns: [X;Y] and O double-buffered when they fit, plus dH
-  static constexpr bool kDbl = 5 * VS <= 512;
-  static constexpr int kCols = kDbl ? 5 * VS : 3 * VS;
-  static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
-                                   : kCols <= 256 ? 256 : 512;
-};
-
-template <typename T, int VS>
-__global__ void __launch_bounds__(128)
-tc_state_kernel(const gdn_chunk_args p, const Work w, float scale,
-                const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk) {
-  using S = StSmem<VS>;
-  constexpr int RSV = (VS / 8) * 128;
-  extern __shared__ uint8_t sm_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* himg = sm + S::kH;
-  uint8_t* vtimg = sm + S::kVt;
-  uint8_t* vnimg = sm + S::kVn;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBar);  // full[2], mma1, mma2
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::kTmem);
-  const uint32_t bar_mma1 = umma::smem_u32(bars + 2), bar_mma2 = umma::smem_u32(bars + 3);
-
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t n = blockIdx.x;
-  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
-  const int vsl = blockIdx.z, v0 = vsl * VS;
-  int64_t bos, eos;
-  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
-  const int64_t nch = eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0;
-  const int64_t c0 = w.coff[n];
-
-  // Issue all of chunk lc's operand copies into stage st (one thread).
-  auto fetch = [&](int64_t lc, int st) {
-    uint8_t* base = sm + st * S::kStageBytes;
-    const uint32_t bar = umma::smem_u32(bars + st);
-    const int s = static_cast<int>(bos + lc * kChunk);
-    const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c0 + lc;
-    const uint8_t* wsrc = w.wimg + hc * kImg64x128;
-    umma::mbar_arrive_expect_tx(bar, S::kTx);
-    umma::bulk_g2s(base + S::kWQ, wsrc, kAtom, bar);
-    umma::tma_load_3d(base + S::kWQ + kAtom, &tq, 0, h, s, bar);
-    umma::bulk_g2s(base + S::kWQ + 2 * kAtom, wsrc + kAtom, kAtom, bar);
-    umma::tma_load_3d(base + S::kWQ + 3 * kAtom, &tq, 64, h, s, bar);
-    umma::tma_load_3d(base + S::kKt, &tk, 0, h, s, bar);
-    umma::tma_load_3d(base + S::kKt + kAtom, &tk, 64, h, s, bar);
-    umma::bulk_g2s(base + S::kZP + kImg64x64, w.pimg + hc * kImg64x64, kImg64x64, bar);
-    umma::bulk_g2s(base + S::kU, w.u + ((hc * (D / VS) + vsl) * 64 * VS) * 2, S::kUBytes, bar);
-    umma::bulk_g2s(base + S::kScalOff, w.scal + hc * kScal, kScal * 4, bar);
-  };
-
-  if (tid == 0) {
-    umma::mbar_init(bars, 1);
-    umma::mbar_init(bars + 1, 1);
-    umma::mbar_init(bars + 2, 1);  // [X;Y] MMAs: one committing warp
-    umma::mbar_init(bars + 3, 2);  // dH and O MMAs: two committing warps
-    umma::mbar_fence_init();
-    if (nch > 0) fetch(0, 0);
-  }
-  if (warp == 0) {
-    umma::tmem_alloc(tslot, S::kTmemCols);
-    umma::fence_before_sync();
-  }
-  for (int e = tid; e < kImg64x64 / 16; e += 128) {  // zero top halves of both [0;P]
-    reinterpret_cast<uint4*>(sm + S::kZP)[e] = make_uint4(0, 0, 0, 0);
-    reinterpret_cast<uint4*>(sm + S::kStageBytes + S::kZP)[e] = make_uint4(0, 0, 0, 0);
-  }
-
-  // initial state slice: thread t owns row t (key dim) of h[:, v0:v0+VS]
-  float hreg[VS];
-#pragma unroll
-  for (int j = 0; j < VS; ++j) {
-    float x = 0.f;
-    if (p.initial_state) {
-      const int64_t base = (n * p.HV + hv) * D * D;
-      x = p.state_v_first ? p.initial_state[base + static_cast<int64_t>(v0 + j) * D + tid]
-                          : p.initial_state[base + static_cast<int64_t>(tid) * D + v0 + j];
-    }
-    hreg[j] = x;
-  }
-#pragma unroll
-  for (int j8 = 0; j8 < VS / 8; ++j8)
-    *reinterpret_cast<uint4*>(himg + umma::img_off(tid, j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
-
-  umma::fence_proxy_async();
-  __syncthreads();
-  umma::fence_after_sync();
-  const uint32_t tmem = *tslot;
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-  // TMEM: [X;Y] at xy(par), O at o(par) (rows 64..127), dH
-  auto xy_col = [&](int par) { return tmem + (S::kDbl ? par * VS : 0); };
-  auto o_col = [&](int par) { return tmem + (S::kDbl ? 2 * VS + par * VS : VS); };
-  const uint32_t tDH = tmem + (S::kDbl ? 4 * VS : 2 * VS);
-  constexpr bool kBf16 = !std::is_same<T, __half>::value;
-  const uint32_t id_xy = umma::idesc_f16(128, VS, kBf16, false, true);
-  const uint32_t id_dh = umma::idesc_f16(128, VS, kBf16, true, true);
-  const uint64_t d_h = umma::smem_desc(umma::smem_u32(himg), RSV, 128);
-  const uint64_t d_vt = umma::smem_desc(umma::smem_u32(vtimg), RSV, 128);
-  const uint64_t d_vn = umma::smem_desc(umma::smem_u32(vnimg), RSV, 128);
-  T* obase = static_cast<T*>(p.o);
-  const int i_row = tid & 63;  // chunk row of this thread in [X;Y] / [.;O] results
-  bool ok = true;
-
-  // Output rows of a finished chunk (threads 64..127): o = a * Y + scale * O.
-  auto emit = [&](int par, int64_t s, int L, float ai) {
-    T* orow = obase + ((s + i_row) * p.HV + hv) * D + v0;
-#pragma unroll
-    for (int q = 0; q < VS / 32; ++q) {
-      float y[32], z[32];
-      umma::tmem_ld32(xy_col(par) + lane_base + q * 32, y);
-      umma::tmem_ld32(o_col(par) + lane_base + q * 32, z);
-      if (i_row < L) {
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          float ov[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ov[e] = ai * y[q8 * 8 + e] + scale * z[q8 * 8 + e];
-          *reinterpret_cast<uint4*>(orow + q * 32 + q8 * 8) = pack8<T>(ov);
-        }
-      }
-    }
-  };
-
-  int64_t s_prev = 0;
-  int L_prev = 0;
-  float a_prev = 0.f;
-  for (int64_t lc = 0; lc < nch; ++lc) {
-    const int st = static_cast<int>(lc & 1);
-    const int par = S::kDbl ? st : 0;
-    uint8_t* base = sm + st * S::kStageBytes;
-    const int64_t s = bos + lc * kChunk;
-    const int L = static_cast<int>(min64(kChunk, eos - s));
-
-    ok = umma::mbar_wait(umma::smem_u32(bars + st), static_cast<uint32_t>((lc >> 1) & 1));
-    if (!ok) record_error(w.err, 1, kSiteStLoad);
-    if (__syncthreads_or(!ok)) break;
-    if (warp == 0) {  // [X; Y] = [W; Q] h  (M = 128, N = VS, K = 128), one elected lane issues
-      umma::fence_after_sync();
-      const uint64_t da = umma::smem_desc_sw128(umma::smem_u32(base + S::kWQ), 16, 1024);
-#pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks)
-        if (umma::elect_one())
-          umma::mma_f16(xy_col(par), da + (((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4),
-                        d_h + ((ks * 2 * RSV) >> 4), id_xy, ks > 0);
-      if (umma::elect_one()) umma::mma_commit(bar_mma1);
-    } else if (warp == 3) {  // stream in the next chunk meanwhile
-      if (lc + 1 < nch && umma::elect_one()) fetch(lc + 1, st ^ 1);
-    }
-    if (S::kDbl && lc > 0 && tid >= 64) emit(par ^ 1, s_prev, L_prev, a_prev);
-
-    ok = umma::mbar_wait(bar_mma1, static_cast<uint32_t>(lc & 1));
-    if (!ok) record_error(w.err, 1, kSiteStMma1);
-    if (__syncthreads_or(!ok)) break;
-    umma::fence_after_sync();
-
-    const float* scv = reinterpret_cast<const float*>(base + S::kScalOff);
-    if (tid < 64) {  // v_new = U - X; images of v_new and diag(b) v_new (row tid)
-      const float bi = scv[64 + i_row];
-      const T* ut = reinterpret_cast<const T*>(base + S::kU);
-      constexpr int kUS = VS < 64 ? VS : 64;  // U slice width of the staged layout
-#pragma unroll
-      for (int q = 0; q < VS / 32; ++q) {
-        float x[32];
-        umma::tmem_ld32(xy_col(par) + lane_base + q * 32, x);
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          float u8[8], vn[8], vt[8];
-          unpack8<T>(*reinterpret_cast<const uint4*>(ut + u_off(i_row, q * 32 + q8 * 8, kUS)), u8);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            vn[e] = u8[e] - x[q8 * 8 + e];
-            vt[e] = bi * vn[e];
-          }
-          *reinterpret_cast<uint4*>(vnimg + umma::img_off(i_row, q * 32 + q8 * 8, RSV)) = pack8<T>(vn);
-          *reinterpret_cast<uint4*>(vtimg + umma::img_off(i_row, q * 32 + q8 * 8, RSV)) = pack8<T>(vt);
-        }
-      }
-    }
-    umma::fence_proxy_async();
-    umma::fence_before_sync();
-    __syncthreads();
-    if (warp == 0) {  // dH = K^T V~
-      umma::fence_after_sync();
-      const uint64_t dk = umma::smem_desc_sw128(umma::smem_u32(base + S::kKt), kAtom, 1024);
-#pragma unroll
-      for (int ks = 0; ks < 64 / 16; ++ks)
-        if (umma::elect_one())
-          umma::mma_f16(tDH, dk + ((ks * 2048) >> 4), d_vt + ((ks * 2 * RSV) >> 4), id_dh, ks > 0);
-      if (umma::elect_one()) umma::mma_commit(bar_mma2);
-    } else if (warp == 1) {  // [.; O] = [0; P] v_new, issued in parallel from another warp
-      umma::fence_after_sync();
-      const uint64_t dp = umma::smem_desc(umma::smem_u32(base + S::kZP), 128, RS64);
-#pragma unroll
-      for (int ks = 0; ks < 64 / 16; ++ks)
-        if (umma::elect_one())
-          umma::mma_f16(o_col(par), dp + ((ks * 256) >> 4), d_vn + ((ks * 2 * RSV) >> 4), id_xy, ks > 0);
-      if (umma::elect_one()) umma::mma_commit(bar_mma2);
-    }
-    const float g = scv[128];
-    const float ai = scv[i_row];
-    ok = umma::mbar_wait(bar_mma2, static_cast<uint32_t>(lc & 1));
-    if (!ok) record_error(w.err, 1, kSiteStMma2);
-    if (__syncthreads_or(!ok)) break;
-    umma::fence_after_sync();
-
-    // h <- gamma h + dH (row tid), and its bf16 image for the next chunk
-#pragma unroll
-    for (int q = 0; q < VS / 32; ++q) {
-      float x[32];
-      umma::tmem_ld32(tDH + lane_base + q * 32, x);
-#pragma unroll
-      for (int e = 0; e < 32; ++e) hreg[q * 32 + e] = g * hreg[q * 32 + e] + x[e];
-    }
-#pragma unroll
-    for (int j8 = 0; j8 < VS / 8; ++j8)
-      *reinterpret_cast<uint4*>(himg + umma::img_off(tid, j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
-    if (!S::kDbl && tid >= 64) emit(par, s, L, ai);
-    s_prev = s;
-    L_prev = L;
-    a_prev = ai;
-    umma::fence_proxy_async();
-    umma::fence_before_sync();
-    __syncthreads();
-  }
-  if (ok && S::kDbl && nch > 0 && tid >= 64)
-    emit(static_cast<int>((nch - 1) & 1), s_prev, L_prev, a_prev);
-
-  if (ok && p.final_state) {
-    const int64_t base = (n * p.HV + hv) * D * D;
-#pragma unroll
-    for (int j = 0; j < VS; ++j) {
-      if (p.state_v_first) p.final_state[base + static_cast<int64_t>(v0 + j) * D + tid] = hreg[j];
-      else p.final_state[base + static_cast<int64_t>(tid) * D + v0 + j] = hreg[j];
-    }
-  }
-  if (!ok) {
-    // an operand copy may still be in flight after a timeout: wait (bounded)
-    // for both stages before the CTA exits and its shared memory is reused
-    umma::mbar_wait(umma::smem_u32(bars), 0, 20000000LL);
-    umma::mbar_wait(umma::smem_u32(bars + 1), 0, 20000000LL);
-  }
-  umma::fence_before_sync();
-  __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tmem, S::kTmemCols);
-}
-
-// ---------------------------------------------------------------------------
-// Warp-specialised state + output kernel (32-column V-slices)
+// Warp-specialised state + output kernel (32- or 64-column V-slices)
 // ---------------------------------------------------------------------------
 //
-// The recurrence of tc_state_kernel with the work of each chunk spread over
+// The state recurrence with the work of each chunk spread over
 // nine warps, so that only the dependent chain stays serial:
 //   MMA1  [X; Y] = [W; Q] h                  warp 0 issues (8 tcgen05.mma)
 //   E1    v = U - X, V~ = diag(b) v          warps 0,1,4,5 (rows 0..63)
 //   MMA2  dH = K^T V~ (chain), O = [. ; P] v  warp 0 issues, separate commits
 //   E2    h <- gamma h + dH, image of h      warps 0..7 (rows 0..127)
 // while, off the chain, warps 2,3,6,7 write o = a Y + scale O of the previous
-// chunk during MMA1, and warp 8 waits on the loads and streams chunk c+2 into
-// a three-stage ring.  A tcgen05.mma costs about the same at N = 32 as at
-// N = 64, so the chain is bounded by its twelve MMAs and two epilogues.
+// chunk during MMA1, and warp 8 waits on the loads and streams the chunks
+// ahead into a ring of stages (three at VS = 32, two at VS = 64).  A
+// tcgen05.mma costs about the same at N = 32 as at N = 64, so the chain is
+// bounded by its MMA round trips and two epilogues, not by VS.
 // Rows 0..63 of the O product read the K tile that precedes P in its stage
 // and are never used.
 
+template <int VS_>
 struct St3 {
-  static constexpr int VS = 32;
+  static constexpr int VS = VS_;
   // stage: W a0 | Q a0 | W a1 | Q a1 | K a0 | K a1 | P | U | scalars
   static constexpr int kWQ = 0;
   static constexpr int kK = 4 * kAtom;
@@ -746,25 +476,25 @@ struct St3 {
   static constexpr int kSc = kU + kUBytes;
   static constexpr int kStage = ((kSc + kScal * 4 + 1023) / 1024) * 1024;
   static constexpr uint32_t kTx = 4 * kAtom + 2 * kAtom + kImg64x64 + kUBytes + kScal * 4;
-  static constexpr int kStages = 3;
+  static constexpr int kStages = VS == 32 ? 3 : 2;  // a third 65 KB stage does not fit at VS = 64
   static constexpr int kH = kStages * kStage;    // h image 128 x VS
   static constexpr int kVn = kH + D * VS * 2;    // v image 64 x VS
   static constexpr int kVt = kVn + 64 * VS * 2;  // diag(b) v image 64 x VS
-  static constexpr int kBar = kVt + 64 * VS * 2; // full[3], mma1, dh, o
+  static constexpr int kBar = kVt + 64 * VS * 2; // full[kStages], mma1, dh, o
   static constexpr int kTmem = kBar + 6 * 8;
   static constexpr int kBytes = kTmem + 8 + 1024;
   // TMEM columns: acc[2], dH, O[2] (VS each)
-  static constexpr int kAcc = 0, kDH = 2 * VS, kO = 3 * VS, kCols = 256;
+  static constexpr int kAcc = 0, kDH = 2 * VS, kO = 3 * VS, kCols = VS == 32 ? 256 : 512;
   static_assert(kO + 2 * VS <= kCols, "TMEM columns");
   static_assert(kBytes <= 227 * 1024, "shared memory");
 };
 constexpr int kSt3Threads = 288;  // 8 epilogue warps + 1 load warp
 
-template <typename T>
+template <typename T, int VS_>
 __global__ void __launch_bounds__(kSt3Threads, 1)
 tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
                  const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk) {
-  using S = St3;
+  using S = St3<VS_>;
   constexpr int VS = S::VS;
   constexpr int RSV = (VS / 8) * 128;
   extern __shared__ uint8_t sm_raw[];
@@ -774,16 +504,18 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
   uint8_t* vtimg = sm + S::kVt;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBar);  // full[3], mma1, dh, o
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::kTmem);
-  const uint32_t bar_mma1 = umma::smem_u32(bars + 3), bar_dh = umma::smem_u32(bars + 4),
-                 bar_o = umma::smem_u32(bars + 5);
+  const uint32_t bar_mma1 = umma::smem_u32(bars + S::kStages), bar_dh = umma::smem_u32(bars + S::kStages + 1),
+                 bar_o = umma::smem_u32(bars + S::kStages + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool producer = warp == 8;
   const int quad = warp & 3, colh = (warp >> 2) & 1;  // TMEM lane quadrant, column half
   const int row = quad * 32 + lane;
-  const int64_t n = blockIdx.x;
+  constexpr int kSlices = D / VS;  // the slices of one (sequence, v-head) are adjacent CTAs (shared loads in L2)
+  constexpr int CW = VS / 2;       // state columns per thread
+  const int64_t n = blockIdx.x / kSlices;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
-  const int vsl = blockIdx.z, v0 = vsl * VS;
+  const int vsl = static_cast<int>(blockIdx.x % kSlices), v0 = vsl * VS;
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
   const int nch = static_cast<int>(eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0);
@@ -811,29 +543,28 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
   };
 
   if (tid == 256) {
-    for (int i = 0; i < 6; ++i) umma::mbar_init(bars + i, 1);
+    for (int i = 0; i < S::kStages + 3; ++i) umma::mbar_init(bars + i, 1);
     umma::mbar_fence_init();
-    if (nch > 0) fetch(0);
-    if (nch > 1) fetch(1);
+    for (int x = 0; x < S::kStages - 1 && x < nch; ++x) fetch(x);
   }
   if (warp == 0) {
     umma::tmem_alloc(tslot, S::kCols);
     umma::fence_before_sync();
   }
   // state slice: thread `row` (warps 0..7) owns h[row][v0 + colh*16 .. +16] in fp32
-  float hreg[16];
+  float hreg[CW];
   if (!producer) {
     const int64_t base = (n * p.HV + hv) * D * D;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int col = v0 + colh * 16 + j;
+    for (int j = 0; j < CW; ++j) {
+      const int col = v0 + colh * CW + j;
       hreg[j] = !p.initial_state ? 0.f
                 : p.state_v_first ? p.initial_state[base + static_cast<int64_t>(col) * D + row]
                                   : p.initial_state[base + static_cast<int64_t>(row) * D + col];
     }
 #pragma unroll
-    for (int j8 = 0; j8 < 2; ++j8)
-      *reinterpret_cast<uint4*>(himg + umma::img_off(row, colh * 16 + j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
+    for (int j8 = 0; j8 < CW / 8; ++j8)
+      *reinterpret_cast<uint4*>(himg + umma::img_off(row, colh * CW + j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
   }
   umma::fence_proxy_async();
   __syncthreads();
@@ -856,12 +587,15 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
     const int64_t s = bos + static_cast<int64_t>(x) * kChunk;
     const int L = static_cast<int>(min64(kChunk, eos - s));
     const int i = row - 64;
-    float y[16], z[16];
-    umma::tmem_ld16x2(t_acc(x) + lane_base + colh * 16, t_o(x) + lane_base + colh * 16, y, z);
-    if (i < L) {
-      T* orow = obase + ((s + i) * p.HV + hv) * D + v0 + colh * 16;
+    float y[CW], z[CW];
 #pragma unroll
-      for (int j8 = 0; j8 < 2; ++j8) {
+    for (int q = 0; q < CW / 16; ++q)
+      umma::tmem_ld16x2(t_acc(x) + lane_base + colh * CW + q * 16, t_o(x) + lane_base + colh * CW + q * 16,
+                        y + q * 16, z + q * 16);
+    if (i < L) {
+      T* orow = obase + ((s + i) * p.HV + hv) * D + v0 + colh * CW;
+#pragma unroll
+      for (int j8 = 0; j8 < CW / 8; ++j8) {
         float ov[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) ov[e] = fmaf(ai, y[j8 * 8 + e], scale * z[j8 * 8 + e]);
@@ -894,12 +628,12 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
       __syncwarp();
     }
     if (producer) {
-      // chunk c+2 goes where chunk c-1 was: its O product must be done
+      // chunk c + kStages - 1 goes where chunk c-1 was: its O product must be done
       if (c >= 1) {
         mine = umma::mbar_wait(bar_o, static_cast<uint32_t>((c - 1) & 1));
         if (!mine) record_error(w.err, 1, kSiteStMma2);
       }
-      if (mine && c + 2 < nch && umma::elect_one()) fetch(c + 2);
+      if (mine && c + S::kStages - 1 < nch && umma::elect_one()) fetch(c + S::kStages - 1);
       __syncwarp();
       if (mine && c + 1 < nch) {  // operands of the next chunk
         mine = umma::mbar_wait(full(c + 1), static_cast<uint32_t>(((c + 1) / S::kStages) & 1));
@@ -919,16 +653,18 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
       mine = umma::mbar_wait(bar_mma1, static_cast<uint32_t>(c & 1));
       if (!mine) record_error(w.err, 1, kSiteStMma1);
       umma::fence_after_sync();
-      uint32_t rx[16];
-      umma::tmem_ld16_nw(t_acc(c) + lane_base + colh * 16, rx);
+      uint32_t rx[CW];
+#pragma unroll
+      for (int q = 0; q < CW / 16; ++q) umma::tmem_ld16_nw(t_acc(c) + lane_base + colh * CW + q * 16, rx + q * 16);
       umma::tmem_wait_ld();
-      umma::reg_fence16(rx);
+#pragma unroll
+      for (int q = 0; q < CW / 16; ++q) umma::reg_fence16(rx + q * 16);
       const int i = row;
       const float bi = sc[64 + i];
       const T* ut = reinterpret_cast<const T*>(b + S::kU);
 #pragma unroll
-      for (int j8 = 0; j8 < 2; ++j8) {
-        const int col = colh * 16 + j8 * 8;
+      for (int j8 = 0; j8 < CW / 8; ++j8) {
+        const int col = colh * CW + j8 * 8;
         float u8[8], vn[8], vt[8];
         unpack8<T>(*reinterpret_cast<const uint4*>(ut + u_off(i, col, VS)), u8);
 #pragma unroll
@@ -966,15 +702,16 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
     }
     umma::fence_after_sync();
     if (mine) {
-      float d[16];
-      umma::tmem_ld16(t_dh + lane_base + colh * 16, d);
+      float d[CW];
+#pragma unroll
+      for (int q = 0; q < CW / 16; ++q) umma::tmem_ld16(t_dh + lane_base + colh * CW + q * 16, d + q * 16);
       const float g = sc[128];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) hreg[j] = fmaf(g, hreg[j], d[j]);
+      for (int j = 0; j < CW; ++j) hreg[j] = fmaf(g, hreg[j], d[j]);
       if (c + 1 < nch) {
 #pragma unroll
-        for (int j8 = 0; j8 < 2; ++j8)
-          *reinterpret_cast<uint4*>(himg + umma::img_off(row, colh * 16 + j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
+        for (int j8 = 0; j8 < CW / 8; ++j8)
+          *reinterpret_cast<uint4*>(himg + umma::img_off(row, colh * CW + j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
       }
     }
     umma::fence_proxy_async();
@@ -993,8 +730,8 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
   if (ok && !producer && p.final_state) {
     const int64_t base = (n * p.HV + hv) * D * D;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int col = v0 + colh * 16 + j;
+    for (int j = 0; j < CW; ++j) {
+      const int col = v0 + colh * CW + j;
       if (p.state_v_first) p.final_state[base + static_cast<int64_t>(col) * D + row] = hreg[j];
       else p.final_state[base + static_cast<int64_t>(row) * D + col] = hreg[j];
     }
@@ -1048,34 +785,21 @@ cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, b
 }
 
 template <typename T, int VS>
-cudaError_t launch_state(const gdn_chunk_args& a, const Work& w, float scale, const CUtensorMap& tq,
-                         const CUtensorMap& tk, cudaStream_t s, LaunchHooks& hk) {
-  auto kern = tc_state_kernel<T, VS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       StSmem<VS>::kBytes);
-  if (e != cudaSuccess) return e;
-  hk.pre(s);
-  kern<<<dim3(static_cast<unsigned>(a.N), a.HV, D / VS), 128, StSmem<VS>::kBytes, s>>>(a, w, scale, tq, tk);
-  return cudaGetLastError();
-}
-
-template <typename T>
 cudaError_t launch_state3(const gdn_chunk_args& a, const Work& w, float scale, const CUtensorMap& tq,
                           const CUtensorMap& tk, cudaStream_t s, LaunchHooks& hk) {
-  auto kern = tc_state3_kernel<T>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, St3::kBytes);
+  using S = St3<VS>;
+  auto kern = tc_state3_kernel<T, VS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
   if (e != cudaSuccess) return e;
   hk.pre(s);
-  kern<<<dim3(static_cast<unsigned>(a.N), a.HV, D / St3::VS), kSt3Threads, St3::kBytes, s>>>(a, w, scale, tq, tk);
+  kern<<<dim3(static_cast<unsigned>(a.N * (D / VS)), a.HV), kSt3Threads, S::kBytes, s>>>(a, w, scale, tq, tk);
   return cudaGetLastError();
 }
 
-int choose_vs(const gdn_chunk_args& a) {
-  const int64_t rec = a.N * a.HV;
-  if (rec <= 148) return 32;
-  if (rec <= 512) return 64;
-  return 128;
-}
+// V-slice width of the state kernel: 32-column slices give the shortest chain
+// when every chain has an SM of its own; otherwise 64-column slices halve the
+// operand reloads per chain.
+int choose_vs(const gdn_chunk_args& a) { return a.N * a.HV <= 148 ? 32 : 64; }
 
 template <typename T>
 cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
@@ -1112,9 +836,8 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
     hk.pre(s);
     wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem::kBytes, s>>>(a, w, scale, tq, tk, tv);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    if (w.vs == 32) e = launch_state3<T>(a, w, scale, tq, tk, s, hk);
-    else if (w.vs == 64) e = launch_state<T, 64>(a, w, scale, tq, tk, s, hk);
-    else e = launch_state<T, 128>(a, w, scale, tq, tk, s, hk);
+    if (w.vs == 32) e = launch_state3<T, 32>(a, w, scale, tq, tk, s, hk);
+    else e = launch_state3<T, 64>(a, w, scale, tq, tk, s, hk);
     if (e != cudaSuccess) return e;
   } else if (a.final_state) {  // no tokens: the final states are the initial ones
     const size_t bytes = static_cast<size_t>(a.N) * a.HV * D * D * sizeof(float);
