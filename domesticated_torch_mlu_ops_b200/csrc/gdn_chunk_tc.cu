@@ -64,7 +64,7 @@ struct Work {
   const int64_t* coff;  // [N+1] chunk offsets
   int* err;             // device error word
   uint8_t* wimg;        // [HV][NCU][16 KiB]
-  uint8_t* u;           // [HV][NCU][128/S][64][S] (S = min(vs, 64), rows swizzled; u_off)
+  uint8_t* u;           // [HV][NCU][128/vs][64][vs] (rows swizzled; u_off)
   uint8_t* pimg;        // [HV][NCU][8 KiB]
   float* scal;          // [HV][NCU][kScal]: a[64], b[64], gamma, pad
   int64_t ncu;          // chunk capacity
