@@ -300,6 +300,38 @@ def run_ours(a):
     ms_local = sum(step_ms) / len(step_ms)
     ms = _max_over_ranks(ms_local, world)
 
+    # ---- N > 1: the same step followed by the final gather of every rank's
+    # outputs and final states onto every rank (NCCL all-gather over NVLink) ----
+    gather = None
+    if world > 1:
+        from domesticated_torch_mlu_ops_b200 import shard
+        plan = shard.OutputGather(wl["parts"], wl["lens"], dev, rank, state_shape=(HV, K, V))
+
+        def step_gather():
+            o_, ht_ = step()
+            return plan(o_, ht_)
+
+        for _ in range(3):
+            step_gather()
+        torch.cuda.synchronize()
+        _barrier(world)
+        gevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(a.steps)]
+        for i in range(a.steps):
+            flush.zero_()
+            gevs[i][0].record(stream)
+            step_gather()
+            gevs[i][1].record(stream)
+        torch.cuda.synchronize()
+        _barrier(world)
+        ms_g = _max_over_ranks(sum(s_.elapsed_time(e_) for s_, e_ in gevs) / a.steps, world)
+        tok_all = wl["tokens"] if wl["scaling"] == "strong" else world * B * T
+        gather = {"value": tok_all / (ms_g / 1e3), "unit": "tokens/s", "ms_per_step": ms_g,
+                  "bytes_received_per_rank": plan.gathered_bytes(torch.empty(1, 1, HV, V, dtype=torch.bfloat16)),
+                  "collective": "torch.distributed all_gather_into_tensor (NCCL) of the packed bf16 "
+                                "outputs and fp32 final states, then a row permutation on the device; "
+                                "every rank ends with the whole output"}
+
     # ---- per-kernel timing with the library's stage events ----
     nst = 8
     sev = [torch.cuda.Event(enable_timing=True) for _ in range(nst)]
@@ -411,6 +443,7 @@ def run_ours(a):
                        f"preallocated; {a.segment_tokens}-token pieces: copy-in, compute and copy-out "
                        f"overlap)"},
             "gpu_launches": int(launches),
+            "with_gather": gather,
             "clocks": clk.summary(),
             "decode": dec,
             "conv1d": conv,
@@ -435,6 +468,7 @@ def _workload(name, world, rank, cfg):
     from domesticated_torch_mlu_ops_b200 import shard
     if name == "cfg1":
         return dict(B=1, T=cfg["T"], cu=None, nseq=world, tokens=world * cfg["T"], seed=1, h0=False,
+                    lens=[cfg["T"]] * world, parts=[[r] for r in range(world)],
                     scaling="weak", par=f"sequence-sharded x{world} (one sequence per rank)",
                     metric="prefill tokens/s (Qwen3-Next GDN layer chunked prefill, BASELINE config 1)",
                     desc=f"config1: chunk_gated_delta_rule B=1 T={cfg['T']} H=16 HV=32 K=V=128 bf16, "
@@ -444,17 +478,20 @@ def _workload(name, world, rank, cfg):
             raise SystemExit("cfg4 needs the GPU count to divide 64")
         b = 64 // world
         return dict(B=b, T=4096, cu=None, nseq=64, tokens=64 * 4096, seed=4, h0=False,
+                    lens=[4096] * 64, parts=[list(range(r * b, r * b + b)) for r in range(world)],
                     scaling="strong", par=f"sequence-sharded x{world} ({b} sequences per rank)",
                     metric="prefill tokens/s (GDN box-scale sharded prefill, BASELINE config 4)",
                     desc="config4: 64 x 4096 tokens, H=16 HV=32 K=V=128 bf16, in-kernel q/k L2 norm")
     if name == "cfg2":
         import numpy as np
         lens = np.random.default_rng(2).integers(512, 8193, size=16).tolist()
-        mine = shard.partition_sequences(lens, world)[rank]
+        parts = shard.partition_sequences(lens, world)
+        mine = parts[rank]
         cu = [0]
         for i in mine:
             cu.append(cu[-1] + lens[i])
         return dict(B=1, T=cu[-1], cu=cu, nseq=16, tokens=int(sum(lens)), seed=2, h0=True,
+                    lens=lens, parts=parts,
                     scaling="strong", par=f"sequences bin-packed over {world} ranks",
                     metric="prefill tokens/s (GDN varlen packed prefill, BASELINE config 2)",
                     desc=f"config2: 16 sequences U[512,8192] ({sum(lens)} tokens) packed via cu_seqlens, "

@@ -9,13 +9,17 @@ so work splits across ranks with no collective on the data path:
 * one long sequence -> groups of v-heads that share a q/k head, so no rank
   needs a q/k head another rank also reads (:func:`partition_heads`).
 
-:func:`gather_outputs` is the optional final gather (``torch.distributed``;
-NCCL on GPUs, gloo on CPU) when one rank needs every output.
+:func:`gather_outputs` is the optional final gather through host memory
+(``all_gather_object``), and :class:`OutputGather` the same gather kept on the
+device: one ``all_gather_into_tensor`` of the packed outputs and one of the
+final states (NCCL over NVLink on GPUs, gloo on CPU), then a row permutation
+back into sequence order, when every rank needs every output.
 """
 
 from __future__ import annotations
 
 import heapq
+import math
 
 import torch
 
@@ -101,3 +105,92 @@ def gather_outputs(ids, o, ht, cu_seqlens, world_size: int):
                     full_h = torch.empty((N,) + tuple(rh.shape[1:]), dtype=rh.dtype)
                 full_h[i] = rh[j]
     return full_o, full_h
+
+
+def _all_gather_rows(send, world: int, group=None):
+    """``[world * rows, ...]`` from every rank's ``[rows, ...]`` tensor."""
+    import torch.distributed as dist
+
+    out = send.new_empty((world * send.shape[0],) + tuple(send.shape[1:]))
+    try:
+        dist.all_gather_into_tensor(out, send, group=group)
+    except (RuntimeError, NotImplementedError):  # backends without the fused form
+        dist.all_gather(list(out.chunk(world)), send, group=group)
+    return out
+
+
+class OutputGather:
+    """Device-side gather of sharded prefill outputs onto every rank.
+
+    ``parts[r]`` lists the sequences rank ``r`` computed, in the order its
+    packed output holds them (:func:`partition_sequences` or a contiguous
+    split; every rank builds the same plan, so shard sizes need no message),
+    and ``lengths[i]`` the token count of sequence ``i``.  Each call pads this
+    rank's rows to the longest shard, all-gathers outputs and (when
+    ``state_shape``, the per-sequence state dims, is given) final states, and
+    returns ``o [1, sum(lengths), HV, V]`` in sequence order (packed, as with
+    ``cu_seqlens``) and ``final_state [N, *state_shape]`` (or None).  Every
+    rank takes the same collectives: a rank without sequences passes an empty
+    output and ``ht=None``.  When the shards are already contiguous and
+    equal, the permutation is skipped.
+    """
+
+    def __init__(self, parts, lengths, device, rank: int, state_shape=None, group=None):
+        self.parts = [list(p) for p in parts]
+        self.lengths = [int(x) for x in lengths]
+        self.world = len(self.parts)
+        self.rank = rank
+        self.group = group
+        self.state_shape = None if state_shape is None else tuple(int(x) for x in state_shape)
+        N = len(self.lengths)
+        self.tok = [sum(self.lengths[i] for i in p) for p in self.parts]
+        self.rows = max(self.tok) if self.tok else 0
+        self.nseq = max((len(p) for p in self.parts), default=0)
+        cu = [0]
+        for n in self.lengths:
+            cu.append(cu[-1] + n)
+        row_src = [0] * cu[-1]  # packed row -> row of the gathered buffer
+        seq_src = [0] * N  # sequence -> slot of the gathered state buffer
+        for r, p in enumerate(self.parts):
+            off = r * self.rows
+            for j, i in enumerate(p):
+                row_src[cu[i]:cu[i + 1]] = range(off, off + self.lengths[i])
+                off += self.lengths[i]
+                seq_src[i] = r * self.nseq + j
+        ident = row_src == list(range(cu[-1])) and seq_src == list(range(N))
+        self.total = cu[-1]
+        self.row_perm = None if ident else torch.tensor(row_src, dtype=torch.int64, device=device)
+        self.seq_perm = None if ident else torch.tensor(seq_src, dtype=torch.int64, device=device)
+
+    def gathered_bytes(self, o) -> int:
+        """Bytes each rank receives per call (padding included) for outputs
+        shaped like ``o``."""
+        n = self.world * self.rows * math.prod(o.shape[2:]) * o.element_size()
+        if self.state_shape is not None:
+            n += self.world * self.nseq * math.prod(self.state_shape) * 4
+        return n
+
+    def __call__(self, o, ht=None):
+        rows = o.reshape((o.shape[0] * o.shape[1],) + tuple(o.shape[2:]))
+        if rows.shape[0] != self.tok[self.rank]:
+            raise ValueError(f"rank {self.rank} holds {rows.shape[0]} rows, the plan says "
+                             f"{self.tok[self.rank]}")
+        if rows.shape[0] < self.rows:
+            pad = rows.new_zeros((self.rows - rows.shape[0],) + tuple(rows.shape[1:]))
+            rows = torch.cat([rows, pad])
+        full = _all_gather_rows(rows.contiguous(), self.world, self.group)
+        if self.row_perm is not None:
+            full = full.index_select(0, self.row_perm)
+        else:
+            full = full[:self.total]
+        full_o = full.unsqueeze(0)
+        if self.state_shape is None:
+            return full_o, None
+        st = ht if ht is not None else o.new_zeros((0,) + self.state_shape, dtype=torch.float32)
+        if tuple(st.shape[1:]) != self.state_shape:
+            raise ValueError(f"final states {tuple(st.shape)} do not match the plan's {self.state_shape}")
+        if st.shape[0] < self.nseq:
+            st = torch.cat([st, st.new_zeros((self.nseq - st.shape[0],) + tuple(st.shape[1:]))])
+        fh = _all_gather_rows(st.contiguous(), self.world, self.group)
+        fh = fh.index_select(0, self.seq_perm) if self.seq_perm is not None else fh[:len(self.lengths)]
+        return full_o, fh

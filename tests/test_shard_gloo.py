@@ -77,3 +77,42 @@ def test_sharded_prefill_two_gloo_ranks(tmp_path):
     ref_o, ref_h = _oracle_op(q, k, v, g, beta, initial_state=h0, cu_seqlens=cu)
     assert torch.allclose(got["o"], ref_o, atol=1e-10)
     assert torch.allclose(got["h"], ref_h, atol=1e-10)
+
+
+
+_GATHER_PARTS = [[[2, 0], [1, 3]], [[0, 1], [2, 3]], [[0, 1, 2, 3], []]]
+_GATHER_LENS = [5, 9, 1, 6]
+
+
+def _gather_worker(rank, world, port, full_o, full_h, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    lens = _GATHER_LENS
+    cu = np.concatenate([[0], np.cumsum(lens)])
+    got = []
+    for parts in _GATHER_PARTS:
+        p = parts[rank]
+        o = torch.cat([full_o[:, cu[i]:cu[i + 1]] for i in p], 1) if p else full_o[:, :0]
+        plan = shard.OutputGather(parts, lens, "cpu", rank, state_shape=(3, 4, 5))
+        got.append(plan(o, full_h[p] if p else None))
+        rows = max(sum(lens[i] for i in q) for q in parts)
+        assert plan.gathered_bytes(o) == world * rows * 3 * 7 * 8 + world * max(map(len, parts)) * 60 * 4
+    torch.save(got, f"{out_path}.{rank}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_device_gather_two_gloo_ranks(tmp_path):
+    """OutputGather on two gloo ranks: padded all-gather, then the row and
+    state permutation back into sequence order, identical on both ranks, for
+    uneven shards, contiguous shards and a rank with no sequences."""
+    rng = np.random.default_rng(11)
+    full_o = torch.from_numpy(rng.standard_normal((1, sum(_GATHER_LENS), 3, 7)))
+    full_h = torch.from_numpy(rng.standard_normal((len(_GATHER_LENS), 3, 4, 5))).float()
+    out = tmp_path / "g"
+    mp.start_processes(_gather_worker, args=(2, _free_port(), full_o, full_h, str(out)),
+                       nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        for o, h in torch.load(f"{out}.{r}"):
+            assert torch.equal(o, full_o)
+            assert torch.equal(h, full_h)
