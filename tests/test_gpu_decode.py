@@ -105,8 +105,10 @@ def test_decode_config3_full_size(ops):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
-@pytest.mark.parametrize("K,V", [(128, 128), (64, 64), (32, 16)])
+@pytest.mark.parametrize("K,V", [(128, 128), (128, 96), (128, 32), (64, 64), (32, 16)])
 def test_decode_shapes_dtypes(ops, dtype, K, V):
+    """K = 128 takes the streaming kernel, which splits each state into
+    64-row blocks (V = 96: a full and a half block; V = 32: one short block)."""
     _decode_case(ops, 11, 37, 80, 2, 4, K, V, dtype)
 
 
@@ -115,14 +117,17 @@ def test_decode_pad_int32_betav_no_l2(ops):
                  l2=False, beta_per_v=True, pad=(0, 7, 19))
 
 
-def test_decode_not_inplace(ops):
-    _decode_case(ops, 13, 9, 30, 2, 2, 64, 32, torch.bfloat16, inplace=False)
+@pytest.mark.parametrize("K,V", [(64, 32), (128, 96)])
+def test_decode_not_inplace(ops, K, V):
+    _decode_case(ops, 13, 9, 30, 2, 2, K, V, torch.bfloat16, inplace=False)
 
 
-def test_decode_spec_tokens(ops):
+@pytest.mark.parametrize("K,V", [(64, 64), (128, 128)])
+def test_decode_spec_tokens(ops, K, V):
     """Speculative decoding: T=3 tokens per sequence, per-token states written
-    to ssm_state_indices[n, t], initial state from column num_accepted-1."""
-    N, T, H, HV, K, V, slots = 5, 3, 2, 4, 64, 64, 40
+    to ssm_state_indices[n, t], initial state from column num_accepted-1
+    (K = 128: the streaming kernel, one bulk store per 64-row block and token)."""
+    N, T, H, HV, slots = 5, 3, 2, 4, 40
     q, k, v, g, beta, _ = make_inputs(21, 1, N * T, H, HV, K, V, dtype=torch.bfloat16)
     gen = torch.Generator().manual_seed(22)
     cache = (torch.randn(slots, HV, V, K, generator=gen) * 0.1).cuda()
