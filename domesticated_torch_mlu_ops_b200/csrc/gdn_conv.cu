@@ -61,7 +61,21 @@ __device__ __forceinline__ void ldv(const T* p, float* v) {
 }
 template <typename T, int VEC>
 __device__ __forceinline__ void stv(T* p, const float* v) {
-  if constexpr (VEC * sizeof(T) == 16) {
+  if constexpr (VEC * sizeof(T) == 16 && sizeof(T) == 2) {  // two lanes per rounding instruction
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        const __nv_bfloat162 b = __floats2bfloat162_rn(v[i], v[i + 1]);
+        w[i / 2] = *reinterpret_cast<const uint32_t*>(&b);
+      } else {
+        const __half2 b = __floats2half2_rn(v[i], v[i + 1]);
+        w[i / 2] = *reinterpret_cast<const uint32_t*>(&b);
+      }
+    }
+    *reinterpret_cast<uint4*>(p) = u;
+  } else if constexpr (VEC * sizeof(T) == 16) {
     uint4 u;
     T* e = reinterpret_cast<T*>(&u);
 #pragma unroll
@@ -84,6 +98,27 @@ __device__ __forceinline__ float silu16(float y) {
   float t;
   asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
   return fmaf(h, t, h);
+}
+
+// SiLU over VEC lanes: silu16 for 16-bit outputs with the halving and the
+// final FMA on packed fp32 pairs (same bits as lane by lane), silu for fp32.
+template <typename T, int VEC>
+__device__ __forceinline__ void silu_vec(float* acc) {
+  if constexpr (sizeof(T) == 2 && VEC % 2 == 0) {
+#pragma unroll
+    for (int e = 0; e < VEC; e += 2) {
+      const float2 h = __fmul2_rn(make_float2(acc[e], acc[e + 1]), make_float2(0.5f, 0.5f));
+      float t0, t1;
+      asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(h.x));
+      asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(h.y));
+      const float2 r = __ffma2_rn(h, make_float2(t0, t1), h);
+      acc[e] = r.x;
+      acc[e + 1] = r.y;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[e] = sizeof(T) == 2 ? silu16(acc[e]) : silu(acc[e]);
+  }
 }
 
 // acc += w * x over VEC lanes, two lanes per packed fp32 FMA when VEC is even.
@@ -153,38 +188,79 @@ __device__ __forceinline__ void find_seq(const FwdParams& p, int64_t t, int64_t&
   eos = load_index(p.cu, p.cu_dtype, n + 1);
 }
 
+// One thread's channel vector [c, c + VEC) walking a run of tokens: the
+// weights, the W-1 previous inputs and the current sequence.  enter(t)
+// moves to the sequence holding token t and, at a sequence start, fills the
+// window from the sequence's own inputs, its initial state or zeros (or
+// marks a PAD / null-block sequence, whose outputs are zeros); step(t, x)
+// writes output t from input x and shifts the window.
 template <typename T, int VEC, int KW>
-__global__ void __launch_bounds__(kThreads, 3) conv_fwd_kernel(const FwdParams p) {
-  constexpr int WM = KW > 0 ? KW : kMaxW;
-  const int W = KW > 0 ? KW : p.W;
-  // CTA b owns channel block b % nblk over the (b / nblk)-th equal run of
-  // tokens, so the nblk CTAs of one run (adjacent in launch order) stream
-  // whole token rows together.
-  for (int once = 0; once < 1; ++once) {
-  const int64_t cb = blockIdx.x % p.nblk, share = blockIdx.x / p.nblk;
-  const int64_t t0 = share * p.upc;
-  const int64_t t1 = min64(p.total, t0 + p.upc);
-  const int64_t c = (cb * kThreads + threadIdx.x) * VEC;
-  if (c >= p.D || t0 >= t1) continue;
-  const T* x = static_cast<const T*>(p.x);
-  T* y = static_cast<T*>(p.y);
-  const T* res = static_cast<const T*>(p.residual);
-
+struct ConvLane {
+  static constexpr int WM = KW > 0 ? KW : kMaxW;
   float w[WM][VEC], bias[VEC];
-#pragma unroll
-  for (int i = 0; i < WM; ++i)
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) w[i][e] = i < W ? ld_any(p.weight, p.w_dtype, (c + e) * W + i) : 0.f;
-#pragma unroll
-  for (int e = 0; e < VEC; ++e) bias[e] = p.bias ? ld_any(p.bias, p.w_dtype, c + e) : 0.f;
-
-  int64_t n, bos, eos;
-  find_seq(p, t0, n, bos, eos);
   float win[WM][VEC];  // win[j] = input at token t - (W-1) + j, j < W-1
-  bool fresh = true, skip = false;
+  int w_rt;            // the width when it is not a template constant
+  int64_t c, n, bos, eos;
+  bool fresh, skip;
 
-  // one output token from its input xv; shifts the window
-  auto step = [&](int64_t t, const float* xv) {
+  __device__ __forceinline__ void init(const FwdParams& p, int64_t c_, int64_t t0) {
+    w_rt = p.W;
+    const int W = KW > 0 ? KW : w_rt;
+    c = c_;
+#pragma unroll
+    for (int i = 0; i < WM; ++i)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) w[i][e] = i < W ? ld_any(p.weight, p.w_dtype, (c + e) * W + i) : 0.f;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) bias[e] = p.bias ? ld_any(p.bias, p.w_dtype, c + e) : 0.f;
+    find_seq(p, t0, n, bos, eos);
+    fresh = true;
+    skip = false;
+  }
+
+  __device__ __forceinline__ void enter(const FwdParams& p, int64_t t) {
+    while (t >= eos) {  // next (possibly empty) sequence
+      ++n;
+      bos = eos;
+      eos = p.cu ? load_index(p.cu, p.cu_dtype, n + 1) : bos + p.T;
+      fresh = true;
+    }
+    if (!fresh) return;
+    fresh = false;
+    const int W = KW > 0 ? KW : w_rt;
+    const T* x = static_cast<const T*>(p.x);
+    bool hinit;
+    int64_t line = n;
+    if (p.fn_mode) {
+      line = input_line(p, n);
+      skip = (p.has_null && line == p.null_block) || line == p.pad_slot;
+      hinit = p.has_init && p.has_init[n];
+    } else {
+      hinit = p.init != nullptr;
+    }
+#pragma unroll
+    for (int j = 0; j < WM - 1; ++j) {
+      if (j >= W - 1) break;
+      const int64_t u = t - (W - 1) + j;
+      if (u >= bos) {
+        ldv<T, VEC>(x + u * p.sx + c, win[j]);
+      } else if (hinit && !skip) {
+        const int64_t local = u - bos;  // -(W-1) .. -1
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          win[j][e] = p.fn_mode
+              ? ld_any(p.init, p.init_dtype, line * p.st_seq + (local + W - 1) * p.st_tok + c + e)
+              : ld_any(p.init, p.init_dtype, (n * p.D + c + e) * W + local + W);
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) win[j][e] = 0.f;
+      }
+    }
+  }
+
+  __device__ __forceinline__ void step(const FwdParams& p, int64_t t, const float* xv) {
+    T* y = static_cast<T*>(p.y);
+    const int W = KW > 0 ? KW : w_rt;
     float acc[VEC];
     if (skip) {
 #pragma unroll
@@ -196,12 +272,10 @@ __global__ void __launch_bounds__(kThreads, 3) conv_fwd_kernel(const FwdParams p
       for (int j = 0; j < WM - 1; ++j)
         if (j < W - 1) fma_vec<VEC>(acc, w[j], win[j]);
       fma_vec<VEC>(acc, w[W - 1], xv);
-      if (p.act == GDN_ACT_SILU)
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) acc[e] = sizeof(T) == 2 ? silu16(acc[e]) : silu(acc[e]);
-      if (res) {
+      if (p.act == GDN_ACT_SILU) silu_vec<T, VEC>(acc);
+      if (p.residual) {
         float r[VEC];
-        ldv<T, VEC>(res + t * p.D + c, r);
+        ldv<T, VEC>(static_cast<const T*>(p.residual) + t * p.D + c, r);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) acc[e] += r[e];
       }
@@ -215,47 +289,27 @@ __global__ void __launch_bounds__(kThreads, 3) conv_fwd_kernel(const FwdParams p
     if (W >= 2)
 #pragma unroll
       for (int e = 0; e < VEC; ++e) win[W - 2][e] = xv[e];
-  };
+  }
+};
 
+// CTA b owns channel block b % nblk over the (b / nblk)-th equal run of
+// tokens, so the nblk CTAs of one run (adjacent in launch order) stream
+// whole token rows together.  Inputs come straight from global memory, kU
+// (or 4) independent loads in flight per thread.
+template <typename T, int VEC, int KW>
+__global__ void __launch_bounds__(kThreads, 3) conv_fwd_kernel(const FwdParams p) {
+  const int64_t cb = blockIdx.x % p.nblk, share = blockIdx.x / p.nblk;
+  const int64_t t0 = share * p.upc;
+  const int64_t t1 = min64(p.total, t0 + p.upc);
+  const int64_t c = (cb * kThreads + threadIdx.x) * VEC;
+  if (c >= p.D || t0 >= t1) return;
+  const T* x = static_cast<const T*>(p.x);
+  ConvLane<T, VEC, KW> L;
+  L.init(p, c, t0);
   int64_t t = t0;
   while (t < t1) {
-    while (t >= eos) {  // next (possibly empty) sequence
-      ++n;
-      bos = eos;
-      eos = p.cu ? load_index(p.cu, p.cu_dtype, n + 1) : bos + p.T;
-      fresh = true;
-    }
-    if (fresh) {  // window from the sequence's own inputs, its initial state or zeros
-      fresh = false;
-      bool hinit;
-      int64_t line = n;
-      if (p.fn_mode) {
-        line = input_line(p, n);
-        skip = (p.has_null && line == p.null_block) || line == p.pad_slot;
-        hinit = p.has_init && p.has_init[n];
-      } else {
-        hinit = p.init != nullptr;
-      }
-#pragma unroll
-      for (int j = 0; j < WM - 1; ++j) {
-        if (j >= W - 1) break;
-        const int64_t u = t - (W - 1) + j;
-        if (u >= bos) {
-          ldv<T, VEC>(x + u * p.sx + c, win[j]);
-        } else if (hinit && !skip) {
-          const int64_t local = u - bos;  // -(W-1) .. -1
-#pragma unroll
-          for (int e = 0; e < VEC; ++e)
-            win[j][e] = p.fn_mode
-                ? ld_any(p.init, p.init_dtype, line * p.st_seq + (local + W - 1) * p.st_tok + c + e)
-                : ld_any(p.init, p.init_dtype, (n * p.D + c + e) * W + local + W);
-        } else {
-#pragma unroll
-          for (int e = 0; e < VEC; ++e) win[j][e] = 0.f;
-        }
-      }
-    }
-    const int64_t end = min64(t1, eos);
+    L.enter(p, t);
+    const int64_t end = min64(t1, L.eos);
     if (VEC * sizeof(T) == 16 && t + kU <= end) {  // kU independent loads in flight, kept packed
       if constexpr (VEC * sizeof(T) == 16) {
         uint4 raw[kU];
@@ -267,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 3) conv_fwd_kernel(const FwdParams p
           const T* e = reinterpret_cast<const T*>(&raw[k]);
 #pragma unroll
           for (int i = 0; i < VEC; ++i) xv[i] = to_f<T>(e[i]);
-          step(t + k, xv);
+          L.step(p, t + k, xv);
         }
       }
       t += kU;
@@ -276,15 +330,14 @@ __global__ void __launch_bounds__(kThreads, 3) conv_fwd_kernel(const FwdParams p
 #pragma unroll
       for (int k = 0; k < 4; ++k) ldv<T, VEC>(x + (t + k) * p.sx + c, xv[k]);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) step(t + k, xv[k]);
+      for (int k = 0; k < 4; ++k) L.step(p, t + k, xv[k]);
       t += 4;
     } else {
       float xv[VEC];
       ldv<T, VEC>(x + t * p.sx + c, xv);
-      step(t, xv);
+      L.step(p, t, xv);
       ++t;
     }
-  }
   }
 }
 
