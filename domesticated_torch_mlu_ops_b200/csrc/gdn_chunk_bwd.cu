@@ -59,16 +59,18 @@ struct BwdPtrs {
 
 // dv_local = scale (M * D * Q K^T)^T dO for one (chunk, v-head): the part of
 // dv that does not depend on the state gradient (chunk_bwd_dv_local), into
-// the dv workspace, which bwd_state_kernel then completes.
+// the dv workspace, which bwd_state_kernel then completes.  dO takes Q's
+// tile once Q K^T is done, so two CTAs fit on an SM and one's loads overlap
+// the other's products.
 template <typename T>
-__global__ void __launch_bounds__(kT, 1) bwd_dvlocal_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
+__global__ void __launch_bounds__(kT, 2) bwd_dvlocal_kernel(const gdn_chunk_bwd_args p, const BwdPtrs w, float scale) {
   extern __shared__ float sm[];
   const int K = p.K, V = p.V;
-  float* qc = sm;             // [64][LD]
+  float* qc = sm;             // [64][LD]; dO after Q K^T
   float* kc = qc + 64 * LD;   // [64][LD]
-  float* dO = kc + 64 * LD;   // [64][LD]
-  float* P = dO + 64 * LD;    // [64][kP]
+  float* P = kc + 64 * LD;    // [64][kP]
   float* gcs = P + 64 * kP;   // [64]
+  float* dO = qc;
   int64_t n, lc;
   if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
@@ -86,13 +88,13 @@ __global__ void __launch_bounds__(kT, 1) bwd_dvlocal_kernel(const gdn_chunk_bwd_
       kc[i * LD + kk] = ok ? w.kn[(s + i) * rowQ + h * K + kk] : 0.f;
     }
   }
+  if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
+  gemm_smem<false>(P, kP, 64, 64, K, qc, LD, 1, kc, 1, LD);  // Q K^T (ends with a barrier)
   for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
     for (int vv = tid & 31; vv < V; vv += 32) {
       dO[i * LD + vv] = i < L ? to_f<T>(dout[i * rowV + vv]) : 0.f;
     }
   }
-  if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
-  gemm_smem<false>(P, kP, 64, 64, K, qc, LD, 1, kc, 1, LD);  // Q K^T
   for (int e = tid; e < 64 * 64; e += kT) {
     const int i = e >> 6, j = e & 63;
     P[i * kP + j] = (i < L && j <= i) ? P[i * kP + j] * expf(gcs[i] - gcs[j]) : 0.f;
@@ -499,7 +501,8 @@ __global__ void bwd_dg_kernel(const gdn_chunk_bwd_args p, const int64_t* __restr
   }
 }
 
-constexpr size_t kDvlSmem = sizeof(float) * (3 * 64 * LD + 64 * kP + 64);
+constexpr size_t kDvlSmem = sizeof(float) * (2 * 64 * LD + 64 * kP + 64);
+static_assert(2 * (kDvlSmem + 1024) <= 228 * 1024, "two bwd_dvlocal_kernel CTAs per SM");
 constexpr size_t kStateSmem = sizeof(float) * (kSqw + kSk + kSvec + 2 * 128 * kRow32);
 constexpr size_t kDqkwSmem = sizeof(float) * (6 * 64 * LQ + 64 * kP + 64 + 32 + kStage);
 static_assert(kDqkwSmem <= 227 * 1024, "bwd_dqkw_kernel shared memory");
