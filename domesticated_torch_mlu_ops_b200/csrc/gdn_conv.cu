@@ -515,15 +515,16 @@ bool idtype_ok(int d) { return d == GDN_I32 || d == GDN_I64; }
 int esize(int d) { return d == GDN_F32 ? 4 : 2; }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// Resident CTAs of a kernel on this device (queried once per kernel).
-template <typename K>
-int resident_ctas(K kern) {
+// Resident CTAs of conv_fwd_kernel<T, VEC, KW> on this device (queried once
+// per instantiation: the static lives in each instantiation of this template).
+template <typename T, int VEC, int KW>
+int resident_ctas() {
   static int cached = 0;
   if (!cached) {
     int dev = 0, sms = 0, per_sm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, conv_fwd_kernel<T, VEC, KW>, kThreads, 0);
     cached = sms * (per_sm > 0 ? per_sm : 1);
   }
   return cached;
@@ -536,7 +537,7 @@ cudaError_t launch_fwd_w(FwdParams p, cudaStream_t s) {
   // as many equal token runs (of at least kTT tokens) as the resident CTAs
   // cover with every channel block: one wave, no tail
   const int64_t shares = std::max<int64_t>(
-      1, std::min<int64_t>(resident_ctas(kern) / std::max<int64_t>(p.nblk, 1), (p.total + kTT - 1) / kTT));
+      1, std::min<int64_t>(resident_ctas<T, VEC, KW>() / std::max<int64_t>(p.nblk, 1), (p.total + kTT - 1) / kTT));
   p.upc = (p.total + shares - 1) / shares;  // tokens per run
   const int64_t grid = p.nblk * shares;
   note_launch();
