@@ -81,59 +81,115 @@ def _load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling in the background during timing."""
+    """SM clock and clock-event reasons sampled DURING the timed region.
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    A timed region here lasts a few milliseconds, far shorter than
+    nvidia-smi's sampling period, so the GPU is read through NVML (read-only
+    queries) by a background thread about every millisecond while the region
+    runs, and :meth:`sample` takes one more reading between step launches,
+    while the GPU is still busy with queued work.  Falls back to an
+    ``nvidia-smi -lms 200`` stream when NVML is unavailable.
+    """
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+    SMI_FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, uuid):
         self.uuid = uuid
+        self.nvml = None
+        self.handle = None
         self.proc = None
-        self.lines = []
+        self.samples = []  # (sm MHz, set of reasons)
+        self.max_mhz = None
+        self.source = None
+        self._stop = threading.Event()
+        self._lock = threading.Lock()
 
     def __enter__(self):
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(self.uuid) if self.uuid else \
+                pynvml.nvmlDeviceGetHandleByIndex(0)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.bits = [(nm, getattr(pynvml, attr)) for nm, attr in self.REASONS]
+            self.source = "NVML, polled about every 1 ms during the timed region and between step launches"
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+        except Exception:
+            self.nvml = None
+            self._start_smi()
+        return self
+
+    def sample(self):
+        """One reading now (call it right after launching a step)."""
+        if self.nvml is None:
+            return
+        try:
+            mhz = float(self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+            mask = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        except Exception:
+            return
+        with self._lock:
+            self.samples.append((mhz, {nm for nm, bit in self.bits if mask & bit}))
+
+    def _poll(self):
+        while not self._stop.is_set():
+            self.sample()
+            time.sleep(0.001)
+
+    def _start_smi(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
         if self.uuid:
             cmd += ["-i", self.uuid]
         try:
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            self.lines = []
+            self.t = threading.Thread(target=lambda: [self.lines.append(l.strip()) for l in self.proc.stdout],
+                                      daemon=True)
             self.t.start()
+            self.source = "nvidia-smi -lms 200"
         except Exception:
             self.proc = None
-        return self
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
 
     def __exit__(self, *exc):
-        if self.proc:
+        if self.nvml is not None:
+            self._stop.set()
+            self.t.join(timeout=1)
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
+        elif self.proc:
             time.sleep(0.25)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+            names = [nm for nm, _ in self.REASONS]
+            for l in self.lines:
+                parts = [x.strip() for x in l.split(",")]
+                if len(parts) < 7:
+                    continue
+                try:
+                    mhz, self.max_mhz = float(parts[0]), float(parts[1])
+                except ValueError:
+                    continue
+                self.samples.append((mhz, {nm for nm, v in zip(names, parts[3:7]) if v.lower() == "active"}))
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in self.lines:
-            parts = [x.strip() for x in l.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[3:7]):
-                if val.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        with self._lock:
+            sm = [m for m, _ in self.samples]
+            reasons = set().union(*[r for _, r in self.samples]) if self.samples else set()
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm), "source": self.source}
 
 
 # --------------------------------------------------------------------------
@@ -293,6 +349,7 @@ def run_ours(a):
             evs[i][0].record(stream)
             step()
             evs[i][1].record(stream)
+            clk.sample()  # the step's kernels are queued or running
         torch.cuda.synchronize()
     _barrier(world)
     launches = lib.gdn_kernel_launch_count() - n0
