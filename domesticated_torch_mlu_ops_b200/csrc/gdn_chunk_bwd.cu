@@ -443,6 +443,39 @@ __global__ void bwd_qk_kernel(const gdn_chunk_bwd_args p, const float* __restric
   const int K = p.K, G = p.HV / p.H;
   const int64_t t = row / p.H;
   const int hh = static_cast<int>(row % p.H);
+  const uintptr_t al = reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.k) |
+                       reinterpret_cast<uintptr_t>(p.dq) | reinterpret_cast<uintptr_t>(p.dk);
+  if (K == 128 && (al & 15) == 0) {
+    // four consecutive columns per lane, every load issued before the first use
+    const int64_t src0 = (t * p.HV + static_cast<int64_t>(hh) * G) * K + lane * 4;
+    float4 dy[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    for (int j = 0; j < G; ++j) {
+      const float4 a = *reinterpret_cast<const float4*>(dqh + src0 + static_cast<int64_t>(j) * K);
+      const float4 b = *reinterpret_cast<const float4*>(dkh + src0 + static_cast<int64_t>(j) * K);
+      dy[0].x += a.x; dy[0].y += a.y; dy[0].z += a.z; dy[0].w += a.w;
+      dy[1].x += b.x; dy[1].y += b.y; dy[1].z += b.z; dy[1].w += b.w;
+    }
+    const float4 xv[2] = {load4<T>(static_cast<const T*>(p.q) + row * K + lane * 4),
+                          load4<T>(static_cast<const T*>(p.k) + row * K + lane * 4)};
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      float4 d = dy[which];
+      const float4 x = xv[which];
+      if (p.use_qk_l2norm) {
+        const float ss = group_sum<32>(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
+        const float r = 1.f / sqrtf(ss + 1e-6f);
+        const float dot = group_sum<32>(r * (x.x * d.x + x.y * d.y + x.z * d.z + x.w * d.w));
+        d = make_float4(r * (d.x - x.x * r * dot), r * (d.y - x.y * r * dot), r * (d.z - x.z * r * dot),
+                        r * (d.w - x.w * r * dot));
+      }
+      T* out = static_cast<T*>(which ? p.dk : p.dq) + row * K + lane * 4;
+      out[0] = from_f<T>(d.x);
+      out[1] = from_f<T>(d.y);
+      out[2] = from_f<T>(d.z);
+      out[3] = from_f<T>(d.w);
+    }
+    return;
+  }
 #pragma unroll
   for (int which = 0; which < 2; ++which) {
     const float* src = which ? dkh : dqh;
