@@ -207,12 +207,39 @@ struct ConvLane {
     w_rt = p.W;
     const int W = KW > 0 ? KW : w_rt;
     c = c_;
+    bool loaded = false;
+    if constexpr (VEC == 8 && KW > 0) {
+      // 16-bit taps of channels c..c+7 are 8 * KW contiguous elements: KW 16-byte loads
+      const bool h16 = p.w_dtype == GDN_BF16 || p.w_dtype == GDN_F16;
+      const uintptr_t wa = reinterpret_cast<uintptr_t>(p.weight) + static_cast<uintptr_t>(c) * KW * 2;
+      const uintptr_t ba = reinterpret_cast<uintptr_t>(p.bias) + static_cast<uintptr_t>(c) * 2;
+      if (h16 && (wa & 15) == 0 && (!p.bias || (ba & 15) == 0)) {
+        uint4 raw[KW + 1];
 #pragma unroll
-    for (int i = 0; i < WM; ++i)
+        for (int r = 0; r < KW; ++r) raw[r] = __ldg(reinterpret_cast<const uint4*>(wa) + r);
+        raw[KW] = p.bias ? __ldg(reinterpret_cast<const uint4*>(ba)) : make_uint4(0u, 0u, 0u, 0u);
+        const uint16_t* u = reinterpret_cast<const uint16_t*>(raw);
+        auto f16 = [&](uint16_t b) {
+          return p.w_dtype == GDN_BF16 ? __uint_as_float(static_cast<uint32_t>(b) << 16)
+                                       : __half2float(__ushort_as_half(b));
+        };
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) w[i][e] = i < W ? ld_any(p.weight, p.w_dtype, (c + e) * W + i) : 0.f;
+        for (int i = 0; i < KW; ++i)
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) bias[e] = p.bias ? ld_any(p.bias, p.w_dtype, c + e) : 0.f;
+          for (int e = 0; e < 8; ++e) w[i][e] = f16(u[e * KW + i]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bias[e] = f16(u[KW * 8 + e]);
+        loaded = true;
+      }
+    }
+    if (!loaded) {
+#pragma unroll
+      for (int i = 0; i < WM; ++i)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) w[i][e] = i < W ? ld_any(p.weight, p.w_dtype, (c + e) * W + i) : 0.f;
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) bias[e] = p.bias ? ld_any(p.bias, p.w_dtype, c + e) : 0.f;
+    }
     find_seq(p, t0, n, bos, eos);
     fresh = true;
     skip = false;

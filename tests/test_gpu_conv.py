@@ -241,6 +241,21 @@ def test_qwen3_next_shape_against_torch_conv(ops):
     assert torch.equal(cs[1].t(), x[0, T - 3:])
 
 
+@pytest.mark.parametrize("wdtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("W", [2, 3, 4])
+def test_16bit_taps_match_fp32_taps(ops, wdtype, W):
+    """16-bit taps and bias (read as 16-byte vectors) give the same bits as
+    the same values passed in fp32 (read one by one)."""
+    g = torch.Generator(device="cuda").manual_seed(30 + W)
+    T, D = 300, 2048
+    x = torch.randn(1, T, D, device="cuda", generator=g).to(wdtype)
+    w = (torch.randn(D, W, device="cuda", generator=g) * 0.3).to(wdtype)
+    b = torch.randn(D, device="cuda", generator=g).to(wdtype)
+    y16, _ = ops.causal_conv1d(x, w, b, None, None, False, "silu")
+    y32, _ = ops.causal_conv1d(x, w.float(), b.float(), None, None, False, "silu")
+    assert torch.equal(y16, y32)
+
+
 def test_errors_match_reference(ops):
     x = torch.randn(1, 8, 16, device="cuda")
     w = torch.randn(16, 4, device="cuda")
