@@ -34,7 +34,7 @@ sys.path.insert(0, ROOT)
 CFG1 = dict(B=1, T=8192, H=16, HV=32, K=128, V=128)
 CFG3 = dict(N=256, slots=1024, H=16, HV=32, K=128, V=128)
 BT = 64
-CPU_SAMPLE_TOKENS = 2048
+CPU_SAMPLE_TOKENS = 8192  # the whole config-1 sequence
 
 
 def flops_per_token_head(K, V, bt=BT):
@@ -193,7 +193,8 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------
-# CPU baseline: the oracle's fp32 chunked restatement, heads split over cores
+# CPU baseline: the oracle's fp32 chunked restatement, v-heads split over
+# worker processes, the remaining cores given to each worker's BLAS
 # --------------------------------------------------------------------------
 
 def _cpu_worker(args):
@@ -215,22 +216,30 @@ def _cpu_inputs(T, H, HV, K, V, seed=1):
     beta = (1 / (1 + np.exp(-rng.standard_normal((1, T, HV))))).astype(np.float32)
     G = HV // H
     parts = []
-    for h in range(H):  # one q/k head and its v-heads per task
-        parts.append((q[:, :, h:h + 1], k[:, :, h:h + 1], v[:, :, h * G:(h + 1) * G],
-                      g[:, :, h * G:(h + 1) * G], beta[:, :, h * G:(h + 1) * G]))
+    for hv in range(HV):  # one v-head (and its q/k head) per task: the recurrences are independent
+        h = hv // G
+        parts.append((q[:, :, h:h + 1], k[:, :, h:h + 1], v[:, :, hv:hv + 1], g[:, :, hv:hv + 1],
+                      beta[:, :, hv:hv + 1]))
     return parts
 
 
 class CpuBaseline:
     def __init__(self, cfg, sample_tokens=CPU_SAMPLE_TOKENS):
         import multiprocessing as mp
-        self.cores = os.cpu_count() or 1
-        # one single-threaded BLAS per worker process: no oversubscription
-        for var in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS"):
-            os.environ[var] = "1"
-        self.pool = mp.get_context("spawn").Pool(min(self.cores, cfg["H"]))
-        for var in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS"):
-            os.environ.pop(var, None)
+        self.cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+        # one worker per v-head task up to the core count; leftover cores go to
+        # each worker's BLAS threads, so every core is used without oversubscription
+        self.workers = max(1, min(self.cores, cfg["HV"]))
+        self.blas_threads = max(1, self.cores // self.workers)
+        saved = {v: os.environ.get(v) for v in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS")}
+        for var in saved:
+            os.environ[var] = str(self.blas_threads)
+        self.pool = mp.get_context("spawn").Pool(self.workers)
+        for var, val in saved.items():
+            if val is None:
+                os.environ.pop(var, None)
+            else:
+                os.environ[var] = val
         self.parts = _cpu_inputs(sample_tokens, cfg["H"], cfg["HV"], cfg["K"], cfg["V"])
         self.tokens = sample_tokens
 
@@ -460,8 +469,8 @@ def run_ours(a):
         cpu_line = {"value": cpu.tokens / best, "unit": "tokens/s", "cores": cpu.cores,
                     "kind": "port",
                     "sample": f"{cpu.tokens} tokens of the config-1 shape (all 32 v-heads), numpy fp32 "
-                              f"chunked restatement, {cpu.cores} worker processes, best of {len(t_cpu)}; "
-                              f"host {_cpu_model()}"}
+                              f"chunked restatement, {cpu.workers} worker processes x {cpu.blas_threads} "
+                              f"BLAS threads on {cpu.cores} cores, best of {len(t_cpu)}; host {_cpu_model()}"}
 
     if rank == 0:
         tokens = tokens_total if wl["scaling"] == "strong" else world * B * T
@@ -762,7 +771,8 @@ def run_reference(a):
                    f"timed on a {cpu.tokens}-token sample per step"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu.cores, "kind": "port",
                          "sample": f"{cpu.tokens} tokens of config 1 per step, numpy fp32 chunked "
-                                   f"restatement of the reference's six stages; host {_cpu_model()}"},
+                                   f"restatement of the reference's six stages, {cpu.workers} worker "
+                                   f"processes x {cpu.blas_threads} BLAS threads; host {_cpu_model()}"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -777,7 +787,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode and conv1d measurements")
     ap.add_argument("--no-bwd", action="store_true", help="skip the backward measurement")
-    ap.add_argument("--ref-tokens", type=int, default=2048)
+    ap.add_argument("--ref-tokens", type=int, default=CPU_SAMPLE_TOKENS)
     ap.add_argument("--tokens", type=int, default=0,
                     help="override config 1's T (small cases for ncu captures; not a bench line)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")

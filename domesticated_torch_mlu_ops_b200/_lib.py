@@ -26,7 +26,9 @@ EXPORTED = (
     "gdn_chunk_workspace_size",
     "gdn_chunk_fwd",
     "gdn_chunk_fwd_noalloc",
+    "gdn_chunk_noalloc_check_device_error",
     "gdn_chunk_check_device_error",
+    "gdn_chunk_fwd_test_stall",
     "gdn_chunk_bwd_workspace_size",
     "gdn_chunk_bwd",
     "gdn_chunk_fwd_host_buffer_size",
@@ -87,6 +89,7 @@ class RecurrentArgs(ctypes.Structure):
         ("stride_indices_seq", _i64), ("stride_indices_tok", _i64),
         ("scale", ctypes.c_float),
         ("use_qk_l2norm", _i32), ("beta_per_v", _i32), ("inplace_final_state", _i32),
+        ("num_slots", _i64), ("err", _vp), ("gk", _vp),
     ]
 
 
@@ -156,6 +159,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.gdn_chunk_fwd.restype = ctypes.c_int
     lib.gdn_chunk_fwd_noalloc.argtypes = [ctypes.POINTER(ChunkArgs), _vp]
     lib.gdn_chunk_fwd_noalloc.restype = ctypes.c_int
+    lib.gdn_chunk_noalloc_check_device_error.argtypes = [_vp]
+    lib.gdn_chunk_noalloc_check_device_error.restype = ctypes.c_int
+    lib.gdn_chunk_fwd_test_stall.argtypes = [ctypes.POINTER(ChunkArgs), _i64, _i64, _vp]
+    lib.gdn_chunk_fwd_test_stall.restype = ctypes.c_int
     lib.gdn_chunk_check_device_error.argtypes = [_vp, _vp]
     lib.gdn_chunk_check_device_error.restype = ctypes.c_int
     lib.gdn_chunk_bwd_workspace_size.argtypes = [ctypes.POINTER(ChunkBwdArgs)]

@@ -115,6 +115,24 @@ int gdn_chunk_fwd(const gdn_chunk_args* a, void* stream) {
   return GDN_OK;
 }
 
+int gdn_chunk_fwd_test_stall(const gdn_chunk_args* a, int64_t stall_chunk, int64_t wait_limit_cycles,
+                             void* stream) {
+  int rc = check_chunk(a);
+  if (rc) return rc;
+  if (a->force_generic || !gdn::tc_path_applies(*a))
+    return fail(GDN_ERR_UNSUPPORTED, "the stall hook exists on the tensor-core path only (bf16/f16, K = V = 128)");
+  if (stall_chunk < 0 || wait_limit_cycles < 1000 || wait_limit_cycles > 2000000000LL)
+    return fail(GDN_ERR_INVALID, "stall_chunk must be >= 0 and wait_limit_cycles in [1e3, 2e9]");
+  if (a->B * a->T == 0 || !a->q || !a->k || !a->v || !a->g || !a->beta || !a->o)
+    return fail(GDN_ERR_INVALID, "q, k, v, g, beta and o must be non-null and the batch non-empty");
+  const size_t need = workspace_bytes(*a);
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", a->workspace_bytes, need);
+  cudaError_t e = gdn::launch_chunk_tc(*a, static_cast<cudaStream_t>(stream), stall_chunk, wait_limit_cycles);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_chunk_fwd_test_stall");
+  return GDN_OK;
+}
+
 size_t gdn_chunk_bwd_workspace_size(const gdn_chunk_bwd_args* a) {
   if (!a) return fail(GDN_ERR_INVALID, "null args"), 0;
   if (check_heads(a->B, a->T, a->N, a->H, a->HV, a->K, a->V, a->cu_seqlens, a->cu_dtype)) return 0;

@@ -19,10 +19,11 @@
 namespace gdn {
 
 __global__ void chunk_plan_kernel(const void* cu, int cu_dtype, int64_t N, int64_t T,
-                                  int64_t* off, int chunk) {
+                                  int64_t* off, int chunk, int* err) {
   __shared__ int64_t warp_tot[32];
   __shared__ int64_t carry;
   if (threadIdx.x == 0) { carry = 0; off[0] = 0; }
+  if (err && threadIdx.x < 4) err[threadIdx.x] = 0;  // the call's device error word starts clear
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int64_t base = 0; base < N; base += blockDim.x) {
@@ -61,8 +62,8 @@ __global__ void chunk_plan_kernel(const void* cu, int cu_dtype, int64_t N, int64
 }
 
 cudaError_t launch_chunk_plan(const void* cu, int cu_dtype, int64_t N, int64_t T,
-                              int64_t* chunk_offsets, cudaStream_t s, int chunk) {
-  chunk_plan_kernel<<<1, 1024, 0, s>>>(cu, cu_dtype, N, T, chunk_offsets, chunk);
+                              int64_t* chunk_offsets, cudaStream_t s, int chunk, int* err) {
+  chunk_plan_kernel<<<1, 1024, 0, s>>>(cu, cu_dtype, N, T, chunk_offsets, chunk, err);
   return cudaGetLastError();
 }
 
@@ -344,7 +345,8 @@ static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws
   LaunchHooks hk(a.stage_events, a.n_stage_events);
   hk.pre(s);
   cudaError_t e = launch_chunk_plan(a.cu_seqlens, a.cu_dtype, a.N, a.T,
-                                    reinterpret_cast<int64_t*>(base + ws.chunk_offsets), s);
+                                    reinterpret_cast<int64_t*>(base + ws.chunk_offsets), s, 64,
+                                    reinterpret_cast<int*>(base + ws.err));
   if (e != cudaSuccess) return e;
   const int64_t rows = Ttot * a.H;
   if (rows > 0) {

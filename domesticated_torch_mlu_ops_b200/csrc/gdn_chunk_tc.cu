@@ -34,7 +34,8 @@
 // operands in with TMA / bulk copies while the current chunk computes.
 //
 // Every mbarrier wait is bounded; on timeout the kernel records an error in
-// the workspace error word, frees its TMEM and exits.
+// the workspace error word, waits (bounded) for its own copies and MMAs in
+// flight, frees its TMEM and exits.
 
 #include <cuda.h>
 
@@ -57,9 +58,6 @@ constexpr int kScal = 132;              // per-(head, chunk) scalars: a[64], b[6
 constexpr int kAtom = 64 * 128;         // one 64-row x 128-byte swizzled atom (8 KiB)
 constexpr float kLog2e = 1.4426950408889634f;
 
-enum ErrSite { kSiteWyLoad = 1, kSiteWyMma1 = 2, kSiteWyMma2 = 3, kSiteStLoad = 4,
-               kSiteStMma1 = 5, kSiteStMma2 = 6 };
-
 struct Work {
   const int64_t* coff;  // [N+1] chunk offsets
   int* err;             // device error word
@@ -69,6 +67,11 @@ struct Work {
   float* scal;          // [HV][NCU][kScal]: a[64], b[64], gamma, pad
   int64_t ncu;          // chunk capacity
   int vs;               // V-slice width of the state kernel (U layout)
+  // Test hook (gdn_chunk_fwd_test_stall): block 0 of the state kernel skips
+  // the operand fetch of chunk stall_chunk (-1: none) and bounds its waits by
+  // stall_limit cycles, so that one wait runs out with nothing in flight.
+  int64_t stall_chunk;
+  long long stall_limit;
 };
 
 struct Layout {
@@ -92,11 +95,7 @@ inline Layout plan(const gdn_chunk_args& a) {
 }
 
 __device__ __forceinline__ void record_error(int* err, int code, int site) {
-  if (atomicCAS(err, 0, code) == 0) {
-    err[1] = site;
-    err[2] = static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
-    err[3] = threadIdx.x;
-  }
+  record_device_error(err, code, site, linear_block_id(), static_cast<int>(threadIdx.x));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -522,9 +521,16 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
   const int64_t c0 = w.coff[n];
   auto stage = [&](int x) { return sm + (x % S::kStages) * S::kStage; };
   auto full = [&](int x) { return umma::smem_u32(bars + x % S::kStages); };
+  const bool stall_block = blockIdx.x == 0 && blockIdx.y == 0 && w.stall_chunk >= 0;
+  const long long wlim = stall_block ? w.stall_limit : 2000000000LL;  // bound of every wait
+  int fetched[S::kStages];  // (load thread) last chunk whose copies were issued into each stage
+#pragma unroll
+  for (int i = 0; i < S::kStages; ++i) fetched[i] = -1;
 
   // every operand of chunk x into its stage (one thread)
   auto fetch = [&](int x) {
+    if (stall_block && x == w.stall_chunk) return;  // test hook: this stage is never filled
+    fetched[x % S::kStages] = x;
     uint8_t* b = stage(x);
     const uint32_t bar = full(x);
     const int s = static_cast<int>(bos + static_cast<int64_t>(x) * kChunk);
@@ -607,8 +613,9 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
   bool ok = true;   // uniform: changes only at block-wide barriers
   bool mine = true; // this thread's own waits since the last barrier
   float a_prev = 0.f;  // emit warps: a of the previous chunk's row
+  uint32_t last_bar = 0, last_par = 0;  // warp 0: mbarrier and phase of its latest tcgen05 commit
   if (producer && nch > 0) {
-    mine = umma::mbar_wait(full(0), 0);
+    mine = umma::mbar_wait(full(0), 0, wlim);
     if (!mine) record_error(w.err, 1, kSiteStLoad);
   }
   for (int c = 0; c < nch; ++c) {
@@ -626,31 +633,33 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
         umma::mma_commit(bar_mma1);
       }
       __syncwarp();
+      last_bar = bar_mma1;
+      last_par = static_cast<uint32_t>(c & 1);
     }
     if (producer) {
       // chunk c + kStages - 1 goes where chunk c-1 was: its O product must be done
       if (c >= 1) {
-        mine = umma::mbar_wait(bar_o, static_cast<uint32_t>((c - 1) & 1));
+        mine = umma::mbar_wait(bar_o, static_cast<uint32_t>((c - 1) & 1), wlim);
         if (!mine) record_error(w.err, 1, kSiteStMma2);
       }
-      if (mine && c + S::kStages - 1 < nch && umma::elect_one()) fetch(c + S::kStages - 1);
+      if (mine && c + S::kStages - 1 < nch && lane == 0) fetch(c + S::kStages - 1);
       __syncwarp();
       if (mine && c + 1 < nch) {  // operands of the next chunk
-        mine = umma::mbar_wait(full(c + 1), static_cast<uint32_t>(((c + 1) / S::kStages) & 1));
+        mine = umma::mbar_wait(full(c + 1), static_cast<uint32_t>(((c + 1) / S::kStages) & 1), wlim);
         if (!mine) record_error(w.err, 1, kSiteStLoad);
       }
       continue;
     }
     if (quad >= 2) {  // off the chain: the previous chunk's output rows
       if (c >= 1) {
-        mine = umma::mbar_wait(bar_o, static_cast<uint32_t>((c - 1) & 1));
+        mine = umma::mbar_wait(bar_o, static_cast<uint32_t>((c - 1) & 1), wlim);
         if (!mine) record_error(w.err, 1, kSiteStMma2);
         umma::fence_after_sync();
         if (mine) emit(c - 1, a_prev);
       }
       a_prev = sc[row - 64];
     } else {  // E1 (rows 0..63): v = U - X, V~ = diag(b) v
-      mine = umma::mbar_wait(bar_mma1, static_cast<uint32_t>(c & 1));
+      mine = umma::mbar_wait(bar_mma1, static_cast<uint32_t>(c & 1), wlim);
       if (!mine) record_error(w.err, 1, kSiteStMma1);
       umma::fence_after_sync();
       uint32_t rx[CW];
@@ -693,11 +702,13 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
           umma::mma_commit(bar_o);
         }
         __syncwarp();
+        last_bar = bar_o;
+        last_par = static_cast<uint32_t>(c & 1);
       }
     }
     // E2 (rows 0..127): h <- gamma h + dH and the image of h for the next MMA1
     if (mine) {
-      mine = umma::mbar_wait(bar_dh, static_cast<uint32_t>(c & 1));
+      mine = umma::mbar_wait(bar_dh, static_cast<uint32_t>(c & 1), wlim);
       if (!mine) record_error(w.err, 1, kSiteStMma2);
     }
     umma::fence_after_sync();
@@ -720,7 +731,7 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
   if (ok && nch > 0) {  // the last chunk's output rows
     ok = !__syncthreads_or(!mine);
     if (ok && !producer && quad >= 2) {
-      mine = umma::mbar_wait(bar_o, static_cast<uint32_t>((nch - 1) & 1));
+      mine = umma::mbar_wait(bar_o, static_cast<uint32_t>((nch - 1) & 1), wlim);
       if (!mine) record_error(w.err, 1, kSiteStMma2);
       umma::fence_after_sync();
       if (mine) emit(nch - 1, a_prev);
@@ -736,10 +747,17 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
       else p.final_state[base + static_cast<int64_t>(row) * D + col] = hreg[j];
     }
   }
-  if (!ok && tid == 256) {
-    // operand copies may still be in flight after a timeout: wait (bounded)
-    // for every stage before the CTA exits and its shared memory is reused
-    for (int x = 0; x < S::kStages; ++x) umma::mbar_wait(umma::smem_u32(bars + x), 0, 20000000LL);
+  if (!ok) {
+    // After a timeout, copies and MMAs this CTA issued may still be in
+    // flight: wait (bounded) for the last fill of every stage and for warp
+    // 0's latest tcgen05 commit (which covers all its earlier MMAs) before
+    // the shared memory and TMEM are released.
+    const long long drain = wlim < 20000000LL ? wlim : 20000000LL;
+    if (tid == 256)
+      for (int x = 0; x < S::kStages; ++x)
+        if (fetched[x] >= 0)
+          umma::mbar_wait(full(fetched[x]), static_cast<uint32_t>((fetched[x] / S::kStages) & 1), drain);
+    if (warp == 0 && last_bar) umma::mbar_wait(last_bar, last_par, drain);
   }
   umma::fence_before_sync();
   __syncthreads();
@@ -802,7 +820,7 @@ cudaError_t launch_state3(const gdn_chunk_args& a, const Work& w, float scale, c
 int choose_vs(const gdn_chunk_args& a) { return a.N * a.HV <= 148 ? 32 : 64; }
 
 template <typename T>
-cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
+cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, long long stall_limit) {
   constexpr bool kF16 = std::is_same<T, __half>::value;
   const Layout l = plan(a);
   uint8_t* ws = static_cast<uint8_t*>(a.workspace);
@@ -815,6 +833,8 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
   w.scal = reinterpret_cast<float*>(ws + l.scal);
   w.ncu = chunk_upper_bound(a.B * a.T, a.N);
   w.vs = choose_vs(a);
+  w.stall_chunk = stall_chunk;
+  w.stall_limit = stall_limit;
   const int64_t ttot = a.B * a.T;
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
   CUtensorMap tq, tk, tv;
@@ -826,7 +846,8 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s) {
   }
   LaunchHooks hk(a.stage_events, a.n_stage_events);
   hk.pre(s);
-  e = launch_chunk_plan(a.cu_seqlens, a.cu_dtype, a.N, a.T, reinterpret_cast<int64_t*>(ws + l.coff), s);
+  e = launch_chunk_plan(a.cu_seqlens, a.cu_dtype, a.N, a.T, reinterpret_cast<int64_t*>(ws + l.coff), s, 64,
+                        w.err);
   if (e != cudaSuccess) return e;
   if (ttot > 0) {
     auto wy = tc_wy_kernel<T>;
@@ -858,8 +879,10 @@ bool tc_path_applies(const gdn_chunk_args& a) {
 
 size_t tc_workspace_bytes(const gdn_chunk_args& a) { return tc::plan(a).total; }
 
-cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s) {
-  return a.qkv_dtype == GDN_F16 ? tc::run<__half>(a, s) : tc::run<__nv_bfloat16>(a, s);
+cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk,
+                            long long stall_limit) {
+  return a.qkv_dtype == GDN_F16 ? tc::run<__half>(a, s, stall_chunk, stall_limit)
+                                : tc::run<__nv_bfloat16>(a, s, stall_chunk, stall_limit);
 }
 
 }  // namespace gdn

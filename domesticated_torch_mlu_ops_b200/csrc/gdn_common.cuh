@@ -89,6 +89,30 @@ __device__ __forceinline__ bool locate_chunk(const int64_t* chunk_offsets, int64
 
 __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
+// ---- device error word -----------------------------------------------------
+// int32[4]: code, site, block (linear CTA id, or the sequence for a slot
+// error), info (thread, or the offending index).  The first failure of a
+// call wins (compare-and-swap on the code); later ones are dropped.
+enum ErrCode { kErrWaitTimeout = 1, kErrSlotRange = 2 };
+enum ErrSite {
+  kSiteWyLoad = 1, kSiteWyMma1 = 2, kSiteWyMma2 = 3,       // tc_wy_kernel
+  kSiteStLoad = 4, kSiteStMma1 = 5, kSiteStMma2 = 6,       // tc_state3_kernel
+  kSiteDecodeRelease = 7, kSiteDecodeLoad = 8,             // decode_stream_kernel waits
+  kSiteSlotInitial = 9, kSiteSlotFinal = 10                // state index >= num_slots
+};
+
+__device__ __forceinline__ void record_device_error(int* err, int code, int site, int block, int info) {
+  if (err && atomicCAS(err, 0, code) == 0) {
+    err[1] = site;
+    err[2] = block;
+    err[3] = info;
+    __threadfence();
+  }
+}
+__device__ __forceinline__ int linear_block_id() {
+  return static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+}
+
 template <int W>
 __device__ __forceinline__ float group_sum(float x) {
 #pragma unroll

@@ -20,7 +20,14 @@
 // Per token:
 //   S <- e^g S;  v' = beta (v - S k);  S <- S + v' k^T;  o = S q
 // computed as s_k = S_v.k, s_q = S_v.q, v' = beta (v - e^g s_k),
-// S_v <- e^g S_v + v' k, o_v = e^g s_q + v' (k.q).
+// S_v <- e^g S_v + v' k, o_v = e^g s_q + v' (k.q).  With per-key decays gk
+// (the IS_KDA branch, fused_recurrent_fn.py:115-120) the dot products use
+// e^gk * k and e^gk * q and the state decays by e^gk per column.
+//
+// Failures are recorded in the caller's error word (p.err) instead of
+// faulting: a bounded stage wait that gives up, or (with p.num_slots) a
+// state index past the declared slot count, whose sequence is then skipped
+// like a PAD slot.
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
@@ -54,7 +61,7 @@ struct StreamSmem {
   static constexpr int kBytes = kBar + 2 * kStages * 8;
 };
 
-template <typename T>
+template <typename T, bool KDA>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_stream_kernel(const gdn_recurrent_args p, int64_t items) {
   extern __shared__ __align__(128) uint8_t sm[];
@@ -101,6 +108,11 @@ decode_stream_kernel(const gdn_recurrent_args p, int64_t items) {
           m.src_row = load_index(p.ssm_state_indices, p.idx_dtype,
                                  m.n * p.stride_indices_seq + i0 * p.stride_indices_tok);
           m.pad = m.src_row < 0;
+          if (p.num_slots > 0 && m.src_row >= p.num_slots) {  // skipped like PAD, and reported
+            record_device_error(p.err, kErrSlotRange, kSiteSlotInitial, static_cast<int>(m.n),
+                                static_cast<int>(m.src_row));
+            m.pad = 1;
+          }
         }
         m.g0 = (m.eos > m.bos && p.g) ? p.g[m.bos * HV + m.hv] : 0.f;
         m.beta0 = (m.eos > m.bos && !p.beta_per_v) ? p.beta[m.bos * HV + m.hv] : 0.f;
@@ -124,6 +136,7 @@ decode_stream_kernel(const gdn_recurrent_args p, int64_t items) {
         bool ok = true;
         if (lane == 0 && j >= kStages) ok = umma::mbar_wait(umma::smem_u32(bars + kStages + st), ph ^ 1u);
         if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          if (lane == 0) record_device_error(p.err, kErrWaitTimeout, kSiteDecodeRelease, linear_block_id(), tid);
           live = false;
           break;
         }
@@ -164,6 +177,7 @@ decode_stream_kernel(const gdn_recurrent_args p, int64_t items) {
     const int st = static_cast<int>(j % kStages);
     const uint32_t ph = static_cast<uint32_t>((j / kStages) & 1);
     const bool ok = umma::mbar_wait(umma::smem_u32(bars + st), ph);
+    if (!ok && tid == 0) record_device_error(p.err, kErrWaitTimeout, kSiteDecodeLoad, linear_block_id(), tid);
     if (umma::named_sync_or(1, kConsumers, !ok)) break;  // every consumer leaves together
     const ItemMeta m = meta[st];
     float* S = tiles + st * (StreamSmem::kTile / 4);
@@ -181,7 +195,7 @@ decode_stream_kernel(const gdn_recurrent_args p, int64_t items) {
       const int h = m.hv / (HV / p.H);
       const int sub = lane >> 3, li = lane & 7;  // 8 lanes per row; lane li owns float4s li + 8 j
       for (int64_t t = m.bos; t < m.eos; ++t) {
-        float4 q[4], k[4];
+        float4 q[4], k[4], ek[4], kd[4], qd[4];
         const T* vrow;
         const T* qsrc;
         const T* ksrc;
@@ -213,12 +227,30 @@ decode_stream_kernel(const gdn_recurrent_args p, int64_t items) {
           kq += k[jj].x * q[jj].x + k[jj].y * q[jj].y + k[jj].z * q[jj].z + k[jj].w * q[jj].w;
         }
         kq = group_sum<8>(kq);
+        if constexpr (KDA) {  // per-key decay: dot products against e^gk * k, e^gk * q
+          const float* gkr = p.gk + (t * HV + m.hv) * kDK;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const float4 x = *reinterpret_cast<const float4*>(gkr + (li + 8 * jj) * 4);
+            ek[jj] = make_float4(expf(x.x), expf(x.y), expf(x.z), expf(x.w));
+            kd[jj] = make_float4(ek[jj].x * k[jj].x, ek[jj].y * k[jj].y, ek[jj].z * k[jj].z, ek[jj].w * k[jj].w);
+            qd[jj] = make_float4(ek[jj].x * q[jj].x, ek[jj].y * q[jj].y, ek[jj].z * q[jj].z, ek[jj].w * q[jj].w);
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) { kd[jj] = k[jj]; qd[jj] = q[jj]; }
+        }
         // destination row of this token's state, loaded before the math so that its latency overlaps
-        const int64_t frow = !p.final_state ? -1
-                             : p.inplace_final_state
-                                 ? load_index(p.ssm_state_indices, p.idx_dtype,
-                                              m.n * p.stride_indices_seq + (t - m.bos) * p.stride_indices_tok)
-                                 : t;
+        int64_t frow = !p.final_state ? -1
+                       : p.inplace_final_state
+                           ? load_index(p.ssm_state_indices, p.idx_dtype,
+                                        m.n * p.stride_indices_seq + (t - m.bos) * p.stride_indices_tok)
+                           : t;
+        if (p.inplace_final_state && p.num_slots > 0 && frow >= p.num_slots) {
+          if (tid == 0)
+            record_device_error(p.err, kErrSlotRange, kSiteSlotFinal, static_cast<int>(m.n), static_cast<int>(frow));
+          frow = -1;
+        }
         const float eg = !p.g ? 1.f : expf(t == m.bos ? m.g0 : p.g[t * HV + m.hv]);
         const float beta_h = p.beta_per_v ? 0.f : (t == m.bos ? m.beta0 : p.beta[t * HV + m.hv]);
         // a warp covers 4 rows per pass; two passes (8 rows) are reduced together
@@ -233,8 +265,8 @@ decode_stream_kernel(const gdn_recurrent_args p, int64_t items) {
             for (int jj = 0; jj < 4; ++jj) {
               sv[u][jj] = r < R ? reinterpret_cast<const float4*>(S + r * kDK)[li + 8 * jj]
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-              dk += sv[u][jj].x * k[jj].x + sv[u][jj].y * k[jj].y + sv[u][jj].z * k[jj].z + sv[u][jj].w * k[jj].w;
-              dq += sv[u][jj].x * q[jj].x + sv[u][jj].y * q[jj].y + sv[u][jj].z * q[jj].z + sv[u][jj].w * q[jj].w;
+              dk += sv[u][jj].x * kd[jj].x + sv[u][jj].y * kd[jj].y + sv[u][jj].z * kd[jj].z + sv[u][jj].w * kd[jj].w;
+              dq += sv[u][jj].x * qd[jj].x + sv[u][jj].y * qd[jj].y + sv[u][jj].z * qd[jj].z + sv[u][jj].w * qd[jj].w;
             }
             red[2 * u] = dk;
             red[2 * u + 1] = dq;
@@ -252,6 +284,7 @@ decode_stream_kernel(const gdn_recurrent_args p, int64_t items) {
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
               float4 s4 = sv[u][jj];
+              if constexpr (KDA) { s4.x *= ek[jj].x; s4.y *= ek[jj].y; s4.z *= ek[jj].z; s4.w *= ek[jj].w; }
               s4.x = eg * s4.x + vp * k[jj].x;
               s4.y = eg * s4.y + vp * k[jj].y;
               s4.z = eg * s4.z + vp * k[jj].z;
@@ -300,13 +333,13 @@ decode_stream_kernel(const gdn_recurrent_args p, int64_t items) {
   if (tid == 0) umma::bulk_wait_all();
 }
 
-template <typename T>
-cudaError_t launch_stream_t(const gdn_recurrent_args& a, cudaStream_t s) {
+template <typename T, bool KDA>
+cudaError_t launch_stream_kda(const gdn_recurrent_args& a, cudaStream_t s) {
   int dev = 0, sms = 148;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-  auto kern = decode_stream_kernel<T>;
+  auto kern = decode_stream_kernel<T, KDA>;
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 StreamSmem::kBytes)) != cudaSuccess)
     return e;
@@ -317,13 +350,18 @@ cudaError_t launch_stream_t(const gdn_recurrent_args& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+template <typename T>
+cudaError_t launch_stream_t(const gdn_recurrent_args& a, cudaStream_t s) {
+  return a.gk ? launch_stream_kda<T, true>(a, s) : launch_stream_kda<T, false>(a, s);
+}
+
 }  // namespace
 
 // The streaming kernel needs 16-byte aligned rows for its bulk copies.
 bool decode_stream_applies(const gdn_recurrent_args& a) {
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   const int es = a.qkv_dtype == GDN_F32 ? 4 : 2;
-  return a.K == kDK && a.V <= 128 && (a.V * es) % 16 == 0 && al(a.q) && al(a.k) && al(a.v) &&
+  return a.K == kDK && a.V <= 128 && (a.V * es) % 16 == 0 && al(a.q) && al(a.k) && al(a.v) && al(a.gk) &&
          (!a.initial_state || (al(a.initial_state) && a.stride_init_state_token % 4 == 0)) &&
          (!a.final_state || (al(a.final_state) && a.stride_final_state_token % 4 == 0));
 }

@@ -74,12 +74,18 @@ cudaError_t launch_chunk_generic(const gdn_chunk_args& a, const ChunkWorkspace& 
 cudaError_t launch_chunk_generic_recompute(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s);
 BwdWorkspace plan_bwd_workspace(const gdn_chunk_bwd_args& a);
 cudaError_t launch_chunk_bwd(const gdn_chunk_bwd_args& a, const BwdWorkspace& ws, cudaStream_t s);
-cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s);
+// stall_chunk >= 0: test hook of gdn_chunk_fwd_test_stall (the first state
+// block skips that chunk's operand fetch; its waits give up after stall_limit).
+cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk = -1,
+                            long long stall_limit = 0);
 cudaError_t launch_solve_tril(const float* A, void* out, int out_dtype, const void* cu,
                               int cu_dtype, int64_t N, int64_t B, int64_t T, int H, int BT,
                               cudaStream_t s);
-// chunk_offsets[0..N] from cu_seqlens (or the equal-length batch).
+// chunk_offsets[0..N] from cu_seqlens (or the equal-length batch); also
+// zeroes the call's 16-byte device error word `err` when it is given, so that
+// every call starts with a clear word (the plan kernel runs first).
 cudaError_t launch_chunk_plan(const void* cu, int cu_dtype, int64_t N, int64_t T,
-                              int64_t* chunk_offsets, cudaStream_t s, int chunk = 64);
+                              int64_t* chunk_offsets, cudaStream_t s, int chunk = 64,
+                              int* err = nullptr);
 
 }  // namespace gdn

@@ -2,13 +2,14 @@
 // device memory.
 //
 // gdn_chunk_fwd needs a caller-provided workspace (hundreds of MB for long
-// prefills).  Some callers have no way to get one: plain C hosts without a
-// device allocator of their own, code running while a CUDA graph is being
-// captured (where cudaMalloc is not allowed), or engines whose memory pool is
-// fully reserved up front.  This entry point serves them from a scratch
-// array compiled into the library instead.  The array has a fixed size
-// (kNoAllocScratchBytes, 32 MiB); every GPU that loads the library holds it
-// until the process exits.  Requests whose workspace would not fit are
+// prefills).  Some callers have no way to get one: plain C hosts that link
+// this library without a device allocator of their own, and serving engines
+// that hand all of the GPU's memory to their own pool at start-up (a
+// cudaMalloc there fails, and a cudaMalloc/cudaFree pair in the request path
+// would also synchronise the device).  This entry point serves them from a
+// scratch array compiled into the library instead.  The array has a fixed
+// size (kNoAllocScratchBytes, 32 MiB); every GPU that loads the library holds
+// it until the process exits.  Requests whose workspace would not fit are
 // rejected with GDN_ERR_WORKSPACE.
 //
 // The array's host-side name is only a stand-in for the symbol; its device
@@ -17,8 +18,9 @@
 // before any stream capture).  All calls share the one array: calls that
 // overlap on the GPU (different streams, or different host threads on one
 // device) race on it and must be serialised by the caller.  The error word
-// at the start of the scratch is cleared on every call; everything else is
-// fully rewritten by the kernels before it is read.
+// at the start of the scratch is cleared on every call (and read back by
+// gdn_chunk_noalloc_check_device_error); everything else is fully rewritten
+// by the kernels before it is read.
 
 #include <mutex>
 
@@ -78,4 +80,12 @@ extern "C" int gdn_chunk_fwd_noalloc(const gdn_chunk_args* args, void* stream) {
   a.workspace = scratch;
   a.workspace_bytes = kNoAllocScratchBytes;
   return gdn_chunk_fwd(&a, stream);
+}
+
+// The device error word of the scratch on the current device (the word that
+// gdn_chunk_check_device_error reads from a caller's workspace).
+extern "C" int gdn_chunk_noalloc_check_device_error(void* stream) {
+  void* scratch = scratch_on_current_device();
+  if (!scratch) return GDN_ERR_CUDA;
+  return gdn_chunk_check_device_error(scratch, stream);
 }

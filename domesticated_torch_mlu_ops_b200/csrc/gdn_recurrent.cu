@@ -7,7 +7,9 @@
 //     s_k = S_v . k,  s_q = S_v . q
 //     v'  = beta (v_v - e^g s_k)
 //     S_v <- e^g S_v + v' k,   o_v = e^g s_q + v' (k . q)
-//   so each row is read once and written once.  K/4 lanes share one row,
+//   so each row is read once and written once.  With per-key decays gk (the
+//   IS_KDA branch, fused_recurrent_fn.py:115-120) s_k and s_q use e^gk * k
+//   and e^gk * q and the row decays by e^gk.  K/4 lanes share one row,
 //   each holding a 128-bit segment, and the two dot products are reduced
 //   together; the state is streamed with no-allocate loads and evict-first
 //   stores.  This kernel is HBM-bound: 2 * HV * V * K * 4 bytes per sequence.
@@ -61,6 +63,11 @@ recurrent_vfirst_kernel(const gdn_recurrent_args p) {
       if (p.num_accepted_tokens) i0 = load_index(p.num_accepted_tokens, p.nacc_dtype, n) - 1;
       srow = load_index(p.ssm_state_indices, p.idx_dtype,
                         n * p.stride_indices_seq + i0 * p.stride_indices_tok);
+      if (p.num_slots > 0 && srow >= p.num_slots) {  // past the declared slots: skipped like PAD
+        if (threadIdx.x == 0 && blockIdx.y == 0)
+          record_device_error(p.err, kErrSlotRange, kSiteSlotInitial, static_cast<int>(n), static_cast<int>(srow));
+        srow = -1;
+      }
       if (srow < 0) {  // PAD slot: skip the sequence, clear its outputs
         for (int64_t t = bos; t < eos; ++t)
 #pragma unroll
@@ -95,11 +102,18 @@ recurrent_vfirst_kernel(const gdn_recurrent_args p) {
     q.x *= sc; q.y *= sc; q.z *= sc; q.w *= sc;
     const float kq = group_sum<TPR>(k.x * q.x + k.y * q.y + k.z * q.z + k.w * q.w);
     const float eg = p.g ? expf(p.g[t * p.HV + hv]) : 1.f;
+    float4 ek = make_float4(1.f, 1.f, 1.f, 1.f), kd = k, qd = q;
+    if (p.gk) {  // per-key decay
+      const float* gkr = p.gk + (t * p.HV + hv) * K + seg * 4;
+      ek = make_float4(expf(gkr[0]), expf(gkr[1]), expf(gkr[2]), expf(gkr[3]));
+      kd = make_float4(ek.x * k.x, ek.y * k.y, ek.z * k.z, ek.w * k.w);
+      qd = make_float4(ek.x * q.x, ek.y * q.y, ek.z * q.z, ek.w * q.w);
+    }
     const float beta_h = p.beta_per_v ? 0.f : p.beta[t * p.HV + hv];
 #pragma unroll
     for (int j = 0; j < RW; ++j) {
-      float sk = S[j].x * k.x + S[j].y * k.y + S[j].z * k.z + S[j].w * k.w;
-      float sq = S[j].x * q.x + S[j].y * q.y + S[j].z * q.z + S[j].w * q.w;
+      float sk = S[j].x * kd.x + S[j].y * kd.y + S[j].z * kd.z + S[j].w * kd.w;
+      float sq = S[j].x * qd.x + S[j].y * qd.y + S[j].z * qd.z + S[j].w * qd.w;
       sk = group_sum<TPR>(sk);
       sq = group_sum<TPR>(sq);
       const int r = rows[j];
@@ -107,10 +121,10 @@ recurrent_vfirst_kernel(const gdn_recurrent_args p) {
       const float vr = ok ? to_f<T>(vptr[(t * p.HV + hv) * V + r]) : 0.f;
       const float br = p.beta_per_v ? (ok ? p.beta[(t * p.HV + hv) * V + r] : 0.f) : beta_h;
       const float vp = br * (vr - eg * sk);
-      S[j].x = eg * S[j].x + vp * k.x;
-      S[j].y = eg * S[j].y + vp * k.y;
-      S[j].z = eg * S[j].z + vp * k.z;
-      S[j].w = eg * S[j].w + vp * k.w;
+      S[j].x = eg * ek.x * S[j].x + vp * k.x;
+      S[j].y = eg * ek.y * S[j].y + vp * k.y;
+      S[j].z = eg * ek.z * S[j].z + vp * k.z;
+      S[j].w = eg * ek.w * S[j].w + vp * k.w;
       if (ok && seg == 0) optr[(t * p.HV + hv) * V + r] = from_f<T>(eg * sq + vp * kq);
     }
     if (p.final_state) {
@@ -118,6 +132,11 @@ recurrent_vfirst_kernel(const gdn_recurrent_args p) {
       if (p.inplace_final_state) {
         frow = load_index(p.ssm_state_indices, p.idx_dtype,
                           n * p.stride_indices_seq + (t - bos) * p.stride_indices_tok);
+        if (p.num_slots > 0 && frow >= p.num_slots) {
+          if (threadIdx.x == 0 && blockIdx.y == 0)
+            record_device_error(p.err, kErrSlotRange, kSiteSlotFinal, static_cast<int>(n), static_cast<int>(frow));
+          frow = -1;
+        }
       } else {
         frow = t;
       }

@@ -6,6 +6,16 @@ reference facade (``triton_ops.py:81-285``); the work runs in
 CPU or Triton path: the ops raise if the tensors are not on a CUDA device or
 the library is not built.
 
+Every op is a ``torch.library`` custom op in the ``gdn_b200`` namespace with a
+fake (meta) implementation, as the reference registers its native ops with
+fakes (``abstract.py:1393-1399``): ``torch.compile`` traces through the public
+functions without a graph break and FakeTensor mode gets output shapes and
+dtypes without touching the GPU.  The ops are ``gdn_b200::chunk_fwd`` /
+``chunk_bwd`` (prefill and its backward), ``recurrent_fn_inplace`` (decode
+that updates the slot cache in place; it declares the cache as mutated),
+``recurrent_fn`` (decode with per-token states out), ``recurrent_plain`` and
+``solve_tril`` (which mutates ``output``, like the reference's native op).
+
 Differences from the reference, all supersets:
 
 * ``chunk_gated_delta_rule`` takes ``use_qk_l2norm_in_kernel`` (q and k are
@@ -20,13 +30,22 @@ Differences from the reference, all supersets:
   ``inplace_final_state`` and ``num_accepted_tokens``; with
   ``ssm_state_indices`` it runs the slot-indexed decode of
   ``fused_recurrent_gated_delta_rule_fn``.
+* ``fused_recurrent_gated_delta_rule_fn`` accepts a per-key gate ``g`` of
+  shape ``[B, T, HV, K]``: the KDA form of the reference kernel
+  (``IS_KDA``, ``fused_recurrent_fn.py:77-80,115-120``), which its facade
+  never enables.
 * Outputs of PAD sequences (negative initial slot index) are zero instead of
-  left unwritten.
+  left unwritten.  A slot index at or past the cache's first dimension is
+  treated like PAD and reported (the reference would read out of bounds).
+* ``check_errors=True`` (keyword) synchronises after the call and raises
+  :class:`GdnError` if a kernel recorded a failure (a bounded wait that gave
+  up, or a slot index out of range).
 """
 
 from __future__ import annotations
 
 import ctypes
+from typing import Optional
 
 import torch
 
@@ -34,6 +53,7 @@ from . import _lib
 
 _DT = {torch.float32: _lib.GDN_F32, torch.bfloat16: _lib.GDN_BF16, torch.float16: _lib.GDN_F16}
 _IDT = {torch.int32: _lib.GDN_I32, torch.int64: _lib.GDN_I64}
+Tensor = torch.Tensor
 
 
 def _ptr(t):
@@ -84,6 +104,265 @@ def _check_shapes(q, k, v):
     return B, T, H, HV, K, V
 
 
+def _empty_f32(dev):
+    return torch.empty(0, dtype=torch.float32, device=dev)
+
+
+_ERR_WORDS: dict = {}
+
+
+def _err_word(dev):
+    """Per-device int32[4] error word passed to the decode kernels (zeroed
+    here once and again after every read)."""
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    w = _ERR_WORDS.get(key)
+    if w is None:
+        w = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", key))
+        _ERR_WORDS[key] = w
+    return w
+
+
+def _raise_err_word(w):
+    """Synchronising read of a decode error word; raises GdnError (and clears
+    the word) when a kernel recorded a failure."""
+    h = w.cpu().tolist()
+    if h[0] != 0:
+        w.zero_()
+        what = {1: "a bounded wait gave up", 2: "state slot index out of range"}.get(h[0], "device error")
+        raise _lib.GdnError(_lib.GDN_ERR_DEVICE,
+                            f"{what} (code {h[0]}, site {h[1]}, sequence/block {h[2]}, info {h[3]})")
+
+
+# ---------------------------------------------------------------------------
+# torch.library custom ops (CUDA implementations call the C ABI)
+# ---------------------------------------------------------------------------
+
+@torch.library.custom_op("gdn_b200::chunk_fwd", mutates_args=(), device_types="cuda")
+def _chunk_fwd_op(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: float,
+                  initial_state: Optional[Tensor], output_final_state: bool,
+                  cu_seqlens: Optional[Tensor], state_v_first: bool, use_qk_l2norm: bool,
+                  force_generic: bool, check_errors: bool) -> tuple[Tensor, Tensor]:
+    """Chunked prefill on prepared inputs (q/k/v contiguous in one dtype,
+    g/beta/initial_state fp32 contiguous, cu_seqlens int32/int64).  Returns
+    ``(o, final_state)``; final_state is an empty tensor when not requested."""
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    N = B if cu_seqlens is None else cu_seqlens.numel() - 1
+    dev = q.device
+    o = torch.empty_like(v, dtype=q.dtype)
+    shape_state = (N, HV, V, K) if state_v_first else (N, HV, K, V)
+    ht = torch.empty(shape_state, dtype=torch.float32, device=dev) if output_final_state else None
+    args = _lib.ChunkArgs(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta),
+        initial_state=_ptr(initial_state), o=_ptr(o), final_state=_ptr(ht), cu_seqlens=_ptr(cu_seqlens),
+        workspace=None, workspace_bytes=0, B=B, T=T, N=N, H=H, HV=HV, K=K, V=V,
+        qkv_dtype=_DT[q.dtype], cu_dtype=_IDT[cu_seqlens.dtype] if cu_seqlens is not None else _lib.GDN_I64,
+        scale=float(scale), use_qk_l2norm=int(use_qk_l2norm), state_v_first=int(state_v_first),
+        force_generic=int(force_generic))
+    lib = _lib.load()
+    nbytes = lib.gdn_chunk_workspace_size(ctypes.byref(args))
+    if nbytes == 0:
+        _lib.check(_lib.GDN_ERR_INVALID)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    args.workspace = ctypes.c_void_p(ws.data_ptr())
+    args.workspace_bytes = nbytes
+    with torch.cuda.device(dev):
+        _lib.check(lib.gdn_chunk_fwd(ctypes.byref(args), _stream(dev)))
+        if check_errors:
+            _lib.check(lib.gdn_chunk_check_device_error(args.workspace, _stream(dev)))
+    return o, (ht if ht is not None else _empty_f32(dev))
+
+
+@_chunk_fwd_op.register_fake
+def _(q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens, state_v_first,
+      use_qk_l2norm, force_generic, check_errors):
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    N = B if cu_seqlens is None else cu_seqlens.shape[0] - 1
+    o = v.new_empty(v.shape, dtype=q.dtype)
+    if not output_final_state:
+        return o, v.new_empty((0,), dtype=torch.float32)
+    shape_state = (N, HV, V, K) if state_v_first else (N, HV, K, V)
+    return o, v.new_empty(shape_state, dtype=torch.float32)
+
+
+@torch.library.custom_op("gdn_b200::chunk_bwd", mutates_args=(), device_types="cuda")
+def _chunk_bwd_op(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: float,
+                  initial_state: Optional[Tensor], cu_seqlens: Optional[Tensor], dout: Tensor,
+                  dht: Optional[Tensor], state_v_first: bool,
+                  use_qk_l2norm: bool) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Backward on prepared inputs; returns ``(dq, dk, dv, dg, dbeta, dh0)``
+    with dh0 an empty tensor when there is no initial state."""
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    N = B if cu_seqlens is None else cu_seqlens.numel() - 1
+    dev = q.device
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg = torch.empty(v.shape[:3], dtype=torch.float32, device=dev)
+    db = torch.empty(v.shape[:3], dtype=torch.float32, device=dev)
+    shape_state = (N, HV, V, K) if state_v_first else (N, HV, K, V)
+    dh0 = torch.empty(shape_state, dtype=torch.float32, device=dev) if initial_state is not None else None
+    args = _lib.ChunkBwdArgs(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta), initial_state=_ptr(initial_state),
+        cu_seqlens=_ptr(cu_seqlens), dout=_ptr(dout), dht=_ptr(dht), dq=_ptr(dq), dk=_ptr(dk), dv=_ptr(dv),
+        dg=_ptr(dg), dbeta=_ptr(db), dh0=_ptr(dh0), workspace=None, workspace_bytes=0,
+        B=B, T=T, N=N, H=H, HV=HV, K=K, V=V, qkv_dtype=_DT[q.dtype],
+        cu_dtype=_IDT[cu_seqlens.dtype] if cu_seqlens is not None else _lib.GDN_I64,
+        scale=float(scale), use_qk_l2norm=int(use_qk_l2norm), state_v_first=int(state_v_first))
+    lib = _lib.load()
+    nbytes = lib.gdn_chunk_bwd_workspace_size(ctypes.byref(args))
+    if nbytes == 0:
+        _lib.check(_lib.GDN_ERR_INVALID)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    args.workspace = ctypes.c_void_p(ws.data_ptr())
+    args.workspace_bytes = nbytes
+    with torch.cuda.device(dev):
+        _lib.check(lib.gdn_chunk_bwd(ctypes.byref(args), _stream(dev)))
+    return dq, dk, dv, dg, db, (dh0 if dh0 is not None else _empty_f32(dev))
+
+
+@_chunk_bwd_op.register_fake
+def _(q, k, v, g, beta, scale, initial_state, cu_seqlens, dout, dht, state_v_first, use_qk_l2norm):
+    dg = v.new_empty(v.shape[:3], dtype=torch.float32)
+    dh0 = (initial_state.new_empty(initial_state.shape) if initial_state is not None
+           else v.new_empty((0,), dtype=torch.float32))
+    return (q.new_empty(q.shape), k.new_empty(k.shape), v.new_empty(v.shape), dg,
+            v.new_empty(v.shape[:3], dtype=torch.float32), dh0)
+
+
+def _recurrent_args(q, k, v, g, gk, beta, scale, initial_state, final_state, o, cu, idx, nacc, l2,
+                    inplace, num_slots, err):
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    N = B if cu is None else cu.numel() - 1
+    if idx is None:
+        s_seq, s_tok = 1, 1
+    elif idx.dim() == 1:
+        s_seq, s_tok = idx.stride(0), 1
+    else:
+        s_seq, s_tok = idx.stride()
+    return _lib.RecurrentArgs(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta),
+        initial_state=_ptr(initial_state), o=_ptr(o), final_state=_ptr(final_state),
+        cu_seqlens=_ptr(cu), ssm_state_indices=_ptr(idx), num_accepted_tokens=_ptr(nacc),
+        B=B, T=T, N=N, H=H, HV=HV, K=K, V=V, qkv_dtype=_DT[q.dtype],
+        cu_dtype=_IDT[cu.dtype] if cu is not None else _lib.GDN_I64,
+        idx_dtype=_IDT[idx.dtype] if idx is not None else _lib.GDN_I64,
+        nacc_dtype=_IDT[nacc.dtype] if nacc is not None else _lib.GDN_I64,
+        stride_init_state_token=initial_state.stride(0) if initial_state is not None else 0,
+        stride_final_state_token=final_state.stride(0) if final_state is not None else 0,
+        stride_indices_seq=s_seq, stride_indices_tok=s_tok, scale=float(scale),
+        use_qk_l2norm=int(l2), beta_per_v=int(beta.dim() == v.dim()), inplace_final_state=int(inplace),
+        num_slots=int(num_slots), err=_ptr(err), gk=_ptr(gk))
+
+
+def _run_recurrent(args, dev, check_errors, err):
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().gdn_fused_recurrent_fwd(ctypes.byref(args), _stream(dev)))
+        if check_errors:
+            _raise_err_word(err)
+
+
+@torch.library.custom_op("gdn_b200::recurrent_fn_inplace", mutates_args=("state",), device_types="cuda")
+def _recurrent_fn_inplace_op(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk: Optional[Tensor],
+                             beta: Tensor, scale: float, state: Tensor, cu_seqlens: Optional[Tensor],
+                             ssm_state_indices: Tensor, num_accepted_tokens: Optional[Tensor],
+                             use_qk_l2norm: bool, check_errors: bool) -> Tensor:
+    """Slot-indexed decode that updates the V-first cache ``state`` in place
+    (rows ``ssm_state_indices[n, t]``); returns o."""
+    o = torch.empty_like(v)
+    err = _err_word(q.device)
+    args = _recurrent_args(q, k, v, g, gk, beta, scale, state, state, o, cu_seqlens, ssm_state_indices,
+                           num_accepted_tokens, use_qk_l2norm, True, state.shape[0], err)
+    _run_recurrent(args, q.device, check_errors, err)
+    return o
+
+
+@_recurrent_fn_inplace_op.register_fake
+def _(q, k, v, g, gk, beta, scale, state, cu_seqlens, ssm_state_indices, num_accepted_tokens,
+      use_qk_l2norm, check_errors):
+    return v.new_empty(v.shape)
+
+
+@torch.library.custom_op("gdn_b200::recurrent_fn", mutates_args=(), device_types="cuda")
+def _recurrent_fn_op(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk: Optional[Tensor],
+                     beta: Tensor, scale: float, initial_state: Optional[Tensor],
+                     cu_seqlens: Optional[Tensor], ssm_state_indices: Optional[Tensor],
+                     num_accepted_tokens: Optional[Tensor], use_qk_l2norm: bool,
+                     check_errors: bool) -> tuple[Tensor, Tensor]:
+    """Decode with the state after every token written to a fresh
+    ``[B*T, HV, V, K]`` tensor (``inplace_final_state=False``)."""
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    o = torch.empty_like(v)
+    final_state = torch.empty(B * T, HV, V, K, dtype=torch.float32, device=q.device)
+    err = _err_word(q.device)
+    nslots = initial_state.shape[0] if (initial_state is not None and ssm_state_indices is not None) else 0
+    args = _recurrent_args(q, k, v, g, gk, beta, scale, initial_state, final_state, o, cu_seqlens,
+                           ssm_state_indices, num_accepted_tokens, use_qk_l2norm, False, nslots, err)
+    _run_recurrent(args, q.device, check_errors, err)
+    return o, final_state
+
+
+@_recurrent_fn_op.register_fake
+def _(q, k, v, g, gk, beta, scale, initial_state, cu_seqlens, ssm_state_indices, num_accepted_tokens,
+      use_qk_l2norm, check_errors):
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    return v.new_empty(v.shape), v.new_empty((B * T, HV, V, K), dtype=torch.float32)
+
+
+@torch.library.custom_op("gdn_b200::recurrent_plain", mutates_args=(), device_types="cuda")
+def _recurrent_plain_op(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk: Optional[Tensor],
+                        gv: Optional[Tensor], beta: Tensor, scale: float, initial_state: Optional[Tensor],
+                        output_final_state: bool, use_qk_l2norm: bool,
+                        cu_seqlens: Optional[Tensor]) -> tuple[Tensor, Tensor]:
+    """Plain K-first recurrence; final_state is empty when not requested."""
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    N = B if cu_seqlens is None else cu_seqlens.numel() - 1
+    o = torch.empty_like(v)
+    ht = torch.empty(N, HV, K, V, dtype=torch.float32, device=q.device) if output_final_state else None
+    args = _lib.RecurrentPlainArgs(
+        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), gk=_ptr(gk), gv=_ptr(gv), beta=_ptr(beta),
+        initial_state=_ptr(initial_state), o=_ptr(o), final_state=_ptr(ht), cu_seqlens=_ptr(cu_seqlens),
+        B=B, T=T, N=N, H=H, HV=HV, K=K, V=V, qkv_dtype=_DT[q.dtype],
+        cu_dtype=_IDT[cu_seqlens.dtype] if cu_seqlens is not None else _lib.GDN_I64,
+        scale=float(scale), use_qk_l2norm=int(use_qk_l2norm), beta_per_v=int(beta.dim() == v.dim()))
+    dev = q.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().gdn_recurrent_plain_fwd(ctypes.byref(args), _stream(dev)))
+    return o, (ht if ht is not None else _empty_f32(dev))
+
+
+@_recurrent_plain_op.register_fake
+def _(q, k, v, g, gk, gv, beta, scale, initial_state, output_final_state, use_qk_l2norm, cu_seqlens):
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    N = B if cu_seqlens is None else cu_seqlens.shape[0] - 1
+    ht = v.new_empty((N, HV, K, V) if output_final_state else (0,), dtype=torch.float32)
+    return v.new_empty(v.shape), ht
+
+
+@torch.library.custom_op("gdn_b200::solve_tril", mutates_args=("output",), device_types="cuda")
+def _solve_tril_op(input: Tensor, output: Tensor, cu_seqlens: Optional[Tensor]) -> None:
+    """``solve_tril(input, output, cu_seqlens)`` of the native op
+    (``include/torch_mlu_ops.h:1052-1054``): input fp32 ``[B, T, H, BT]``
+    contiguous, output of the same shape (contiguous) written in place."""
+    B, T, H, BT = input.shape
+    cu, cu_dt = _idx(cu_seqlens)
+    N = B if cu is None else cu.numel() - 1
+    dev = input.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().gdn_solve_tril(
+            _ptr(input), _ptr(output), _DT[output.dtype], _ptr(cu), cu_dt, N, B, T, H, BT, _stream(dev)))
+
+
+@_solve_tril_op.register_fake
+def _(input, output, cu_seqlens):
+    return None
+
+
 # ---------------------------------------------------------------------------
 # chunked prefill
 # ---------------------------------------------------------------------------
@@ -96,99 +375,50 @@ def _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first):
         raise ValueError(f"g {tuple(g.shape)} and beta {tuple(beta.shape)} must be [B, T, HV]")
     if cu_seqlens is not None and B != 1:
         raise ValueError("cu_seqlens requires batch size 1 (packed sequences)")
-    qkv = _qkv_dtype(q, k, v)
-    cu, cu_dt = _idx(cu_seqlens)
-    N = B if cu is None else cu.numel() - 1
+    _qkv_dtype(q, k, v)
+    cu, _ = _idx(cu_seqlens)
+    N = B if cu is None else cu.shape[0] - 1
     shape_state = (N, HV, V, K) if state_v_first else (N, HV, K, V)
     if initial_state is not None and tuple(initial_state.shape) != shape_state:
         raise ValueError(f"initial_state must be {shape_state}, got {tuple(initial_state.shape)}")
-    return (B, T, N, H, HV, K, V), qkv, cu, cu_dt, shape_state
+    return cu
 
 
-def _chunk_fwd(q, k, v, g, beta, scale, h0, output_final_state, cu, cu_dt, dims, qkv, shape_state,
-               state_v_first, use_qk_l2norm, force_generic):
-    B, T, N, H, HV, K, V = dims
-    dev = q.device
-    o = torch.empty_like(v, dtype=q.dtype)
-    ht = torch.empty(shape_state, dtype=torch.float32, device=dev) if output_final_state else None
-    args = _lib.ChunkArgs(
-        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta),
-        initial_state=_ptr(h0), o=_ptr(o), final_state=_ptr(ht), cu_seqlens=_ptr(cu),
-        workspace=None, workspace_bytes=0, B=B, T=T, N=N, H=H, HV=HV, K=K, V=V,
-        qkv_dtype=qkv, cu_dtype=cu_dt, scale=float(scale) if scale is not None else 0.0,
-        use_qk_l2norm=int(bool(use_qk_l2norm)), state_v_first=int(bool(state_v_first)),
-        force_generic=int(bool(force_generic)))
-    lib = _lib.load()
-    nbytes = lib.gdn_chunk_workspace_size(ctypes.byref(args))
-    if nbytes == 0:
-        _lib.check(_lib.GDN_ERR_INVALID)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    args.workspace = ctypes.c_void_p(ws.data_ptr())
-    args.workspace_bytes = nbytes
-    with torch.cuda.device(dev):
-        _lib.check(lib.gdn_chunk_fwd(ctypes.byref(args), _stream(dev)))
-    return o, ht
-
-
-def _chunk_bwd(q, k, v, g, beta, scale, h0, cu, cu_dt, dims, qkv, shape_state, state_v_first,
-               use_qk_l2norm, do, dht):
-    B, T, N, H, HV, K, V = dims
-    dev = q.device
-    do = do.to(q.dtype).contiguous()
-    dht = None if dht is None else dht.to(torch.float32).contiguous()
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    dg = torch.empty(v.shape[:3], dtype=torch.float32, device=dev)
-    db = torch.empty(v.shape[:3], dtype=torch.float32, device=dev)
-    dh0 = torch.empty(shape_state, dtype=torch.float32, device=dev) if h0 is not None else None
-    args = _lib.ChunkBwdArgs(
-        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta), initial_state=_ptr(h0),
-        cu_seqlens=_ptr(cu), dout=_ptr(do), dht=_ptr(dht), dq=_ptr(dq), dk=_ptr(dk), dv=_ptr(dv),
-        dg=_ptr(dg), dbeta=_ptr(db), dh0=_ptr(dh0), workspace=None, workspace_bytes=0,
-        B=B, T=T, N=N, H=H, HV=HV, K=K, V=V, qkv_dtype=qkv, cu_dtype=cu_dt,
-        scale=float(scale) if scale is not None else 0.0,
-        use_qk_l2norm=int(bool(use_qk_l2norm)), state_v_first=int(bool(state_v_first)))
-    lib = _lib.load()
-    nbytes = lib.gdn_chunk_bwd_workspace_size(ctypes.byref(args))
-    if nbytes == 0:
-        _lib.check(_lib.GDN_ERR_INVALID)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    args.workspace = ctypes.c_void_p(ws.data_ptr())
-    args.workspace_bytes = nbytes
-    with torch.cuda.device(dev):
-        _lib.check(lib.gdn_chunk_bwd(ctypes.byref(args), _stream(dev)))
-    return dq, dk, dv, dg, db, dh0
+def _scale(scale):
+    return float(scale) if scale is not None else 0.0  # <= 0 selects K ** -0.5 in the library
 
 
 class ChunkGatedDeltaRuleFunction(torch.autograd.Function):
     """Autograd node of the chunked forward (``triton/fla/chunk.py:188-251``):
     the forward saves its inputs only and the backward recomputes the
-    intermediates (``chunk.py:76-186``) inside ``gdn_chunk_bwd``."""
+    intermediates (``chunk.py:76-186``) inside ``gdn_b200::chunk_bwd``."""
 
     @staticmethod
     def forward(ctx, q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens,
-                state_v_first, use_qk_l2norm, force_generic):
-        dims, qkv, cu, cu_dt, shape_state = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens,
-                                                           state_v_first)
+                state_v_first, use_qk_l2norm, force_generic, check_errors=False):
+        cu = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first)
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         g32, b32, h0 = _f32(g), _f32(beta), _f32(initial_state)
-        o, ht = _chunk_fwd(q, k, v, g32, b32, scale, h0, output_final_state, cu, cu_dt, dims, qkv,
-                           shape_state, state_v_first, use_qk_l2norm, force_generic)
+        o, ht = torch.ops.gdn_b200.chunk_fwd(q, k, v, g32, b32, _scale(scale), h0, bool(output_final_state),
+                                             cu, bool(state_v_first), bool(use_qk_l2norm),
+                                             bool(force_generic), bool(check_errors))
         ctx.save_for_backward(q, k, v, g32, b32, h0, cu)
-        ctx.meta = (scale, cu_dt, dims, qkv, shape_state, state_v_first, use_qk_l2norm,
-                    g.dtype, beta.dtype, None if initial_state is None else initial_state.dtype)
-        return o, ht
+        ctx.meta = (_scale(scale), bool(state_v_first), bool(use_qk_l2norm), g.dtype, beta.dtype,
+                    None if initial_state is None else initial_state.dtype)
+        return o, (ht if output_final_state else None)
 
     @staticmethod
     def backward(ctx, do, dht):
         q, k, v, g32, b32, h0, cu = ctx.saved_tensors
-        scale, cu_dt, dims, qkv, shape_state, svf, l2, g_dt, b_dt, h0_dt = ctx.meta
+        scale, svf, l2, g_dt, b_dt, h0_dt = ctx.meta
         if do is None:
             do = torch.zeros_like(v, dtype=q.dtype)
-        dq, dk, dv, dg, db, dh0 = _chunk_bwd(q, k, v, g32, b32, scale, h0, cu, cu_dt, dims, qkv,
-                                             shape_state, svf, l2, do, dht)
-        if dh0 is not None:
-            dh0 = dh0.to(h0_dt)
-        return (dq, dk, dv, dg.to(g_dt), db.to(b_dt), None, dh0, None, None, None, None, None)
+        do = do.to(q.dtype).contiguous()
+        dht = None if dht is None else dht.to(torch.float32).contiguous()
+        dq, dk, dv, dg, db, dh0 = torch.ops.gdn_b200.chunk_bwd(q, k, v, g32, b32, scale, h0, cu, do, dht,
+                                                               svf, l2)
+        dh0 = dh0.to(h0_dt) if h0 is not None else None
+        return (dq, dk, dv, dg.to(g_dt), db.to(b_dt), None, dh0, None, None, None, None, None, None)
 
 
 def chunk_gated_delta_rule(
@@ -208,6 +438,7 @@ def chunk_gated_delta_rule(
     use_qk_l2norm_in_kernel: bool = False,
     *,
     force_generic: bool = False,
+    check_errors: bool = False,
 ):
     """Chunked gated delta-rule forward (``triton_ops.py:81-165``).
 
@@ -220,7 +451,8 @@ def chunk_gated_delta_rule(
     Differentiable like the reference (``ChunkGatedDeltaRuleFunction``,
     ``triton/fla/chunk.py:188-251``): when grad mode is on and an input
     requires grad, the backward (``gdn_chunk_bwd``) gives dq, dk, dv, dg,
-    dbeta and d(initial_state).
+    dbeta and d(initial_state).  ``check_errors=True`` reads the call's device
+    error word back (one synchronisation) and raises on a recorded failure.
     """
     del chunk_indices, chunk_offsets, allow_tf32
     _cuda("chunk_gated_delta_rule", q, k, v, g, beta, initial_state, cu_seqlens)
@@ -228,12 +460,13 @@ def chunk_gated_delta_rule(
             t is not None and t.requires_grad for t in (q, k, v, g, beta, initial_state)):
         return ChunkGatedDeltaRuleFunction.apply(
             q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens, state_v_first,
-            use_qk_l2norm_in_kernel, force_generic)
-    dims, qkv, cu, cu_dt, shape_state = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens,
-                                                       state_v_first)
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-    return _chunk_fwd(q, k, v, _f32(g), _f32(beta), scale, _f32(initial_state), output_final_state, cu,
-                      cu_dt, dims, qkv, shape_state, state_v_first, use_qk_l2norm_in_kernel, force_generic)
+            use_qk_l2norm_in_kernel, force_generic, check_errors)
+    cu = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first)
+    o, ht = torch.ops.gdn_b200.chunk_fwd(
+        q.contiguous(), k.contiguous(), v.contiguous(), _f32(g), _f32(beta), _scale(scale),
+        _f32(initial_state), bool(output_final_state), cu, bool(state_v_first),
+        bool(use_qk_l2norm_in_kernel), bool(force_generic), bool(check_errors))
+    return o, (ht if output_final_state else None)
 
 
 def chunk_gated_delta_rule_from_host(
@@ -279,8 +512,10 @@ def chunk_gated_delta_rule_from_host(
     if segment_tokens <= 0 or segment_tokens % 64:
         raise ValueError(f"segment_tokens={segment_tokens} must be a positive multiple of 64")
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    dims, qkv, _, _, shape_state = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first)
-    B, T, N, H, HV, K, V = dims
+    _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first)
+    B, T, H, HV, K, V = _check_shapes(q, k, v)
+    N = B if cu_seqlens is None else cu_seqlens.numel() - 1
+    shape_state = (N, HV, V, K) if state_v_first else (N, HV, K, V)
     staged = []  # host temporaries (conversions, pinning) the copies read
 
     def host_in(t, dtype=None):
@@ -311,7 +546,7 @@ def chunk_gated_delta_rule_from_host(
         q=_ptr(qh), k=_ptr(kh), v=_ptr(vh), g=_ptr(gh), beta=_ptr(bh),
         initial_state=_ptr(h0h), o=_ptr(o_h), final_state=_ptr(ht_h), cu_seqlens=_ptr(cuh),
         workspace=None, workspace_bytes=0, B=B, T=T, N=N, H=H, HV=HV, K=K, V=V,
-        qkv_dtype=qkv, cu_dtype=cu_dt, scale=float(scale) if scale is not None else 0.0,
+        qkv_dtype=_qkv_dtype(q, k, v), cu_dtype=cu_dt, scale=_scale(scale),
         use_qk_l2norm=int(bool(use_qk_l2norm_in_kernel)), state_v_first=int(bool(state_v_first)),
         force_generic=int(bool(force_generic)))
     lib = _lib.load()
@@ -335,13 +570,13 @@ def chunk_gated_delta_rule_bwd(q, k, v, g, beta, scale, initial_state, dout, dht
     recomputed).  Returns ``(dq, dk, dv, db, dg, dh0)`` in the reference's
     order; dq, dk, dv in q's dtype, db and dg fp32, dh0 fp32 or None."""
     _cuda("chunk_gated_delta_rule_bwd", q, k, v, g, beta, initial_state, dout, dht, cu_seqlens)
-    dims, qkv, cu, cu_dt, shape_state = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens,
-                                                       state_v_first)
+    cu = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first)
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-    dq, dk, dv, dg, db, dh0 = _chunk_bwd(q, k, v, _f32(g), _f32(beta), scale, _f32(initial_state), cu,
-                                         cu_dt, dims, qkv, shape_state, state_v_first,
-                                         use_qk_l2norm_in_kernel, dout, dht)
-    return dq, dk, dv, db, dg, dh0
+    h0 = _f32(initial_state)
+    dq, dk, dv, dg, db, dh0 = torch.ops.gdn_b200.chunk_bwd(
+        q, k, v, _f32(g), _f32(beta), _scale(scale), h0, cu, dout.to(q.dtype).contiguous(),
+        None if dht is None else _f32(dht), bool(state_v_first), bool(use_qk_l2norm_in_kernel))
+    return dq, dk, dv, db, dg, (dh0 if h0 is not None else None)
 
 
 # ---------------------------------------------------------------------------
@@ -361,6 +596,8 @@ def fused_recurrent_gated_delta_rule_fn(
     ssm_state_indices: torch.Tensor = None,
     num_accepted_tokens: torch.Tensor = None,
     use_qk_l2norm_in_kernel: bool = False,
+    *,
+    check_errors: bool = False,
 ):
     """Slot-indexed recurrent decode (``triton_ops.py:228-285`` ->
     ``triton/fla/fused_recurrent_fn.py:161-233``).
@@ -370,6 +607,10 @@ def fused_recurrent_gated_delta_rule_fn(
     ``inplace_final_state=True`` the cache is updated in place at
     ``ssm_state_indices[n, t]`` and returned; otherwise a fresh
     ``[B*T, HV, V, K]`` tensor receives the state after every token.
+    ``g`` is the per-head log decay ``[B, T, HV]``, or ``[B, T, HV, K]`` for
+    per-key decays (the kernel's KDA form).  A slot index at or past
+    ``initial_state.shape[0]`` skips its sequence like PAD and is recorded in
+    the device error word (``check_errors=True`` raises on it).
     """
     _cuda("fused_recurrent_gated_delta_rule_fn", q, k, v, g, beta, initial_state, cu_seqlens,
           ssm_state_indices, num_accepted_tokens)
@@ -378,16 +619,21 @@ def fused_recurrent_gated_delta_rule_fn(
         raise ValueError(f"K={K}, V={V}: both must be <= 128 (fused_recurrent_fn.py:181-182)")
     if cu_seqlens is not None and B != 1:
         raise ValueError("cu_seqlens requires batch size 1 (packed sequences)")
-    qkv = _qkv_dtype(q, k, v)
+    _qkv_dtype(q, k, v)
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     if beta is None:
         beta = torch.ones(v.shape[:3], dtype=torch.float32, device=v.device)
-    beta_per_v = beta.dim() == v.dim()
-    g, beta = _f32(g), _f32(beta)
-    cu, cu_dt = _idx(cu_seqlens)
-    N = B if cu is None else cu.numel() - 1
-    idx, idx_dt = _idx(ssm_state_indices)
-    nacc, nacc_dt = _idx(num_accepted_tokens)
+    gk = None
+    if g is not None and g.dim() == 4:
+        if tuple(g.shape) != (B, T, HV, K):
+            raise ValueError(f"per-key g must be [B, T, HV, K] = {(B, T, HV, K)}, got {tuple(g.shape)}")
+        g, gk = None, g
+    g, gk, beta = _f32(g), _f32(gk), _f32(beta)
+    cu, _ = _idx(cu_seqlens)
+    idx, _ = _idx(ssm_state_indices)
+    nacc, _ = _idx(num_accepted_tokens)
+    if nacc is not None:
+        nacc = nacc.contiguous()
     if scale is None:
         scale = K ** -0.5
     if initial_state is not None:
@@ -401,31 +647,11 @@ def fused_recurrent_gated_delta_rule_fn(
     if inplace_final_state:
         if initial_state is None or idx is None:
             raise ValueError("inplace_final_state=True needs initial_state and ssm_state_indices")
-        final_state = initial_state
-    else:
-        final_state = torch.empty(B * T, HV, V, K, dtype=torch.float32, device=q.device)
-    if idx is None:
-        s_seq, s_tok = 1, 1
-    elif idx.dim() == 1:
-        s_seq, s_tok = idx.stride(0), 1
-    else:
-        s_seq, s_tok = idx.stride()
-    o = torch.empty_like(v)
-    args = _lib.RecurrentArgs(
-        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), beta=_ptr(beta),
-        initial_state=_ptr(initial_state), o=_ptr(o), final_state=_ptr(final_state),
-        cu_seqlens=_ptr(cu), ssm_state_indices=_ptr(idx), num_accepted_tokens=_ptr(nacc),
-        B=B, T=T, N=N, H=H, HV=HV, K=K, V=V, qkv_dtype=qkv, cu_dtype=cu_dt,
-        idx_dtype=idx_dt, nacc_dtype=nacc_dt,
-        stride_init_state_token=initial_state.stride(0) if initial_state is not None else 0,
-        stride_final_state_token=final_state.stride(0),
-        stride_indices_seq=s_seq, stride_indices_tok=s_tok, scale=float(scale),
-        use_qk_l2norm=int(bool(use_qk_l2norm_in_kernel)), beta_per_v=int(beta_per_v),
-        inplace_final_state=int(bool(inplace_final_state)))
-    dev = q.device
-    with torch.cuda.device(dev):
-        _lib.check(_lib.load().gdn_fused_recurrent_fwd(ctypes.byref(args), _stream(dev)))
-    return o, final_state
+        o = torch.ops.gdn_b200.recurrent_fn_inplace(q, k, v, g, gk, beta, float(scale), initial_state, cu, idx,
+                                                   nacc, bool(use_qk_l2norm_in_kernel), bool(check_errors))
+        return o, initial_state
+    return torch.ops.gdn_b200.recurrent_fn(q, k, v, g, gk, beta, float(scale), initial_state, cu, idx, nacc,
+                                           bool(use_qk_l2norm_in_kernel), bool(check_errors))
 
 
 def fused_recurrent_gated_delta_rule(
@@ -454,8 +680,12 @@ def fused_recurrent_gated_delta_rule(
     :func:`fused_recurrent_gated_delta_rule_fn` on a V-first cache instead.
     """
     if ssm_state_indices is not None:
-        if gk is not None or gv is not None:
-            raise ValueError("gk/gv are not supported with ssm_state_indices")
+        if gv is not None:
+            raise ValueError("gv is not supported with ssm_state_indices")
+        if gk is not None:
+            if g is not None:
+                raise ValueError("give either g or the per-key gk with ssm_state_indices")
+            g = gk
         return fused_recurrent_gated_delta_rule_fn(
             q, k, v, g, beta, scale, initial_state, inplace_final_state, cu_seqlens,
             ssm_state_indices, num_accepted_tokens, use_qk_l2norm_in_kernel)
@@ -465,54 +695,43 @@ def fused_recurrent_gated_delta_rule(
         raise ValueError(f"K={K}, V={V}: both must be <= 128 (fused_recurrent.py:155-156)")
     if cu_seqlens is not None and B != 1:
         raise ValueError("cu_seqlens requires batch size 1 (packed sequences)")
-    qkv = _qkv_dtype(q, k, v)
+    _qkv_dtype(q, k, v)
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     if beta is None:
         beta = torch.ones(v.shape[:3], dtype=torch.float32, device=v.device)
-    beta_per_v = beta.dim() == v.dim()
     g, gk, gv, beta = _f32(g), _f32(gk), _f32(gv), _f32(beta)
-    cu, cu_dt = _idx(cu_seqlens)
-    N = B if cu is None else cu.numel() - 1
+    cu, _ = _idx(cu_seqlens)
+    N = B if cu is None else cu.shape[0] - 1
     h0 = None
     if initial_state is not None:
         if tuple(initial_state.shape) != (N, HV, K, V):
             raise ValueError(f"initial_state must be {(N, HV, K, V)}, got {tuple(initial_state.shape)}")
         h0 = _f32(initial_state)
-    o = torch.empty_like(v)
-    ht = torch.empty(N, HV, K, V, dtype=torch.float32, device=q.device) if output_final_state else None
-    args = _lib.RecurrentPlainArgs(
-        q=_ptr(q), k=_ptr(k), v=_ptr(v), g=_ptr(g), gk=_ptr(gk), gv=_ptr(gv), beta=_ptr(beta),
-        initial_state=_ptr(h0), o=_ptr(o), final_state=_ptr(ht), cu_seqlens=_ptr(cu),
-        B=B, T=T, N=N, H=H, HV=HV, K=K, V=V, qkv_dtype=qkv, cu_dtype=cu_dt,
-        scale=float(scale) if scale is not None else 0.0,
-        use_qk_l2norm=int(bool(use_qk_l2norm_in_kernel)), beta_per_v=int(beta_per_v))
-    dev = q.device
-    with torch.cuda.device(dev):
-        _lib.check(_lib.load().gdn_recurrent_plain_fwd(ctypes.byref(args), _stream(dev)))
-    return o, ht
+    o, ht = torch.ops.gdn_b200.recurrent_plain(q, k, v, g, gk, gv, beta, _scale(scale), h0,
+                                               bool(output_final_state), bool(use_qk_l2norm_in_kernel), cu)
+    return o, (ht if output_final_state else None)
 
 
 def solve_tril(input: torch.Tensor, output: torch.Tensor = None, cu_seqlens: torch.Tensor = None,
                out_dtype: torch.dtype = torch.float):
     """(I + input)^-1 per chunk block (``_ops.py:6232-6257``; native op
-    ``include/torch_mlu_ops.h:1052-1054``).  input fp32 ``[B, T, H, BT]``,
-    BT in {16, 32, 64}; output bf16/fp16/fp32 of the same shape."""
+    ``include/torch_mlu_ops.h:1052-1054``).  input fp32 ``[B, T, H, BT]`` or
+    packed ``[total_tokens, H, BT]``, BT in {16, 32, 64}; output
+    bf16/fp16/fp32 of the same shape."""
     _cuda("solve_tril", input, output, cu_seqlens)
-    if input.dtype != torch.float32 or input.dim() != 4:
-        raise ValueError("input must be a float32 [B, T, H, BT] tensor")
+    if input.dtype != torch.float32 or input.dim() not in (3, 4):
+        raise ValueError("input must be a float32 [B, T, H, BT] or [total_tokens, H, BT] tensor")
     if output is None:
         output = torch.empty(input.shape, device=input.device, dtype=out_dtype)
     if output.shape != input.shape or output.dtype not in _DT:
         raise ValueError("output must match input's shape with dtype float32/bfloat16/float16")
-    B, T, H, BT = input.shape
     x = input.contiguous()
+    if x.dim() == 3:
+        x = x.unsqueeze(0)
     out = output if output.is_contiguous() else torch.empty_like(output)
-    cu, cu_dt = _idx(cu_seqlens)
-    N = B if cu is None else cu.numel() - 1
-    dev = input.device
-    with torch.cuda.device(dev):
-        _lib.check(_lib.load().gdn_solve_tril(
-            _ptr(x), _ptr(out), _DT[out.dtype], _ptr(cu), cu_dt, N, B, T, H, BT, _stream(dev)))
+    out4 = out.unsqueeze(0) if out.dim() == 3 else out
+    cu, _ = _idx(cu_seqlens)
+    torch.ops.gdn_b200.solve_tril(x, out4, cu)
     if out is not output:
         output.copy_(out)
     return output

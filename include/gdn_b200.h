@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define GDN_ABI_VERSION 1
+#define GDN_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define GDN_API __attribute__((visibility("default")))
@@ -108,18 +108,40 @@ GDN_API int gdn_chunk_fwd(const gdn_chunk_args* args, void* stream);
 
 /*
  * Allocation-free variant of gdn_chunk_fwd (no counterpart in the reference).
- * For callers that cannot allocate device memory: C hosts without an
- * allocator of their own, code running inside CUDA graph capture, engines
- * whose memory pool is fully reserved.  args->workspace and
- * args->workspace_bytes are ignored; the workspace comes from a 32 MiB scratch
- * array built into the library (held on every GPU that loads the library
- * until exit).  Calls whose workspace (gdn_chunk_workspace_size) exceeds
- * 32 MiB return GDN_ERR_WORKSPACE.  The first call on a device looks up the
- * array's device address (make it before any stream capture).  All calls
- * share the one array: calls that overlap on the GPU race and must be
- * serialised by the caller.  Allocates nothing.
+ * For callers that cannot allocate device memory: C hosts that link this
+ * library without a device allocator of their own, and serving engines that
+ * give all of the GPU's memory to their own pool at start-up (cudaMalloc
+ * fails there, and would synchronise the device in the request path).
+ * args->workspace and args->workspace_bytes are ignored; the workspace comes
+ * from a 32 MiB scratch array built into the library (held on every GPU that
+ * loads the library until exit).  Calls whose workspace
+ * (gdn_chunk_workspace_size) exceeds 32 MiB return GDN_ERR_WORKSPACE.  The
+ * first call on a device looks up the array's device address (make it before
+ * any stream capture).  All calls share the one array: calls that overlap on
+ * the GPU race and must be serialised by the caller.  Allocates nothing.
  */
 GDN_API int gdn_chunk_fwd_noalloc(const gdn_chunk_args* args, void* stream);
+
+/* gdn_chunk_check_device_error for the scratch of gdn_chunk_fwd_noalloc on
+ * the current device (no counterpart in the reference): reads back
+ * (synchronously, on `stream`) and clears the error word of the last
+ * allocation-free call. */
+GDN_API int gdn_chunk_noalloc_check_device_error(void* stream);
+
+/*
+ * Test hook for the failure path (no counterpart in the reference, whose
+ * kernels have no bounded waits): gdn_chunk_fwd on the tensor-core path
+ * (bf16/f16, K = V = 128) in which the first block of the state kernel does
+ * not issue the operand copies of its chunk `stall_chunk`, and bounds every
+ * wait of that block by `wait_limit_cycles` SM clocks (1e3 .. 2e9) instead of
+ * about one second.  That block's wait for the missing operands runs out:
+ * it records code 1, site 4 in the workspace error word, waits for the work
+ * it did issue, and exits without writing its remaining outputs or its final
+ * state.  No copy, MMA or fault is left behind, so the context stays usable;
+ * gdn_chunk_check_device_error then returns GDN_ERR_DEVICE.  For tests only.
+ */
+GDN_API int gdn_chunk_fwd_test_stall(const gdn_chunk_args* args, int64_t stall_chunk,
+                                     int64_t wait_limit_cycles, void* stream);
 
 /*
  * Backward of gdn_chunk_fwd (the autograd backward of chunk_gated_delta_rule).
@@ -196,8 +218,13 @@ GDN_API size_t gdn_chunk_fwd_host_buffer_size(const gdn_chunk_args* args, int64_
 GDN_API int gdn_chunk_fwd_host(const gdn_chunk_args* args, int64_t segment_tokens, void* stream);
 
 /* Reads back (synchronously, on `stream`) the device error word that the
- * chunk kernels keep in `workspace`; returns GDN_OK or GDN_ERR_DEVICE and
- * clears the word. */
+ * chunk kernels keep at the start of `workspace` (no counterpart in the
+ * reference, whose kernels cannot report a failure); returns GDN_OK or
+ * GDN_ERR_DEVICE and clears the word.  Every gdn_chunk_fwd call clears the
+ * word before its first kernel, so the word describes the last call that
+ * used this workspace.  A kernel that gives up on a wait (a bounded
+ * mbarrier wait that timed out) records code 1, the site, the block and the
+ * thread, and leaves its outputs incomplete. */
 GDN_API int gdn_chunk_check_device_error(void* workspace, void* stream);
 
 /*
@@ -216,6 +243,18 @@ GDN_API int gdn_chunk_check_device_error(void* workspace, void* stream);
  *   state is read from column num_accepted_tokens[n]-1 of the index row.
  *   A sequence whose initial index is negative (PAD) is skipped and its
  *   output rows are set to zero.
+ *   gk [B, T, HV, K] f32 or NULL: per-key log decays (the IS_KDA branch of
+ *   fused_recurrent_fn.py:77-80,115-120: S <- S * exp(gk)[None, :] each
+ *   token); applied together with g when both are given.
+ *   num_slots > 0 declares the number of state rows: an initial index >=
+ *   num_slots makes the sequence be skipped like PAD (outputs zero, state
+ *   untouched) and a final index >= num_slots skips that store; both record
+ *   error code 2 (site 9 initial, 10 final, block = sequence, info = index)
+ *   in `err`.  num_slots <= 0 checks nothing (the reference's behaviour).
+ *   err: NULL or a device int32[4] error word that the caller zeroes; the
+ *   kernels only write it on a failure (the first one wins): code 1 = a
+ *   bounded wait of the streaming kernel gave up (site 7 or 8), code 2 = a
+ *   state index out of range.
  * K, V <= 128 and K a multiple of 4.
  */
 typedef struct gdn_recurrent_args {
@@ -241,6 +280,9 @@ typedef struct gdn_recurrent_args {
   int32_t use_qk_l2norm;
   int32_t beta_per_v;
   int32_t inplace_final_state;
+  int64_t num_slots;
+  int32_t* err;
+  const float* gk;
 } gdn_recurrent_args;
 
 GDN_API int gdn_fused_recurrent_fwd(const gdn_recurrent_args* args, void* stream);

@@ -47,7 +47,7 @@ def _flat(x):
 def recurrent_v_first(q, k, v, g, beta, scale, initial_state, *,
                       inplace_final_state=True, cu_seqlens=None,
                       ssm_state_indices=None, num_accepted_tokens=None,
-                      use_qk_l2norm_in_kernel=False, dtype=np.float64):
+                      use_qk_l2norm_in_kernel=False, gk=None, dtype=np.float64):
     """Slot-indexed recurrent decode with a V-first state cache.
 
     Restates ``tmo_fused_recurrent_gated_delta_rule_fwd_kernel`` and its host
@@ -59,6 +59,9 @@ def recurrent_v_first(q, k, v, g, beta, scale, initial_state, *,
       Without indices the state row is ``bos`` (``:101-102``).
     * per token (``:105-132``): optional q/k L2 norm, q *= scale,
       S *= exp(g), v' = beta * (v - S k), S += v' k^T, o = S q.
+    * ``gk`` ``[B, T, HV, K]``: the kernel's IS_KDA branch (``:77-80``,
+      ``:115-120``), S *= exp(gk)[None, :] per token (on the K columns of the
+      V-first state); applied after ``g`` when both are given.
     * final state (``:135-148``): in place at ``ssm_state_indices[n, t]``
       (skipped when negative) or, when not in place, at row ``bos + t`` of a
       fresh ``[T, HV, V, K]`` tensor.
@@ -71,6 +74,7 @@ def recurrent_v_first(q, k, v, g, beta, scale, initial_state, *,
     G = HV // H
     qf, kf, vf = (_flat(x).astype(dtype) for x in (q, k, v))
     gf = None if g is None else _flat(g).astype(dtype)
+    gkf = None if gk is None else _flat(gk).astype(dtype)
     bf = _flat(beta).astype(dtype)
     beta_per_v = beta.ndim == v.ndim
     bounds = seq_bounds(B, T, cu_seqlens)
@@ -107,6 +111,8 @@ def recurrent_v_first(q, k, v, g, beta, scale, initial_state, *,
             qt = qt * scale
             if gf is not None:
                 S = S * np.exp(gf[t])[:, None, None]
+            if gkf is not None:
+                S = S * np.exp(gkf[t])[:, None, :]
             bt = bf[t] if beta_per_v else bf[t][:, None]  # [HV, V] or [HV, 1]
             vt = bt * (vf[t] - np.einsum('hvk,hk->hv', S, kt))
             S = S + vt[:, :, None] * kt[:, None, :]

@@ -140,6 +140,46 @@ def gen_recurrent_fn(ref: str):
         print("wrote", name)
 
 
+def gen_recurrent_fn_kda(ref: str):
+    """The decode kernel's per-key decay branch (``IS_KDA``,
+    ``fused_recurrent_fn.py:77-80,115-120``).  The reference facade always
+    passes ``IS_KDA=False`` (``:230``), so the kernel is launched here
+    directly, with the launch arguments its host wrapper builds (``:161-233``)
+    and ``g`` holding per-key log decays ``[B, T, HV, K]``."""
+    mod = sys.modules.get("torch_mlu_ops.triton.fla.fused_recurrent_fn") or _load(
+        "torch_mlu_ops.triton.fla.fused_recurrent_fn", os.path.join(ref, "triton/fla/fused_recurrent_fn.py"))
+    import triton
+    # (name, N, T, H, HV, K, V, l2norm, pad)
+    cases = [("decode_kda", 5, 2, 2, 4, 16, 16, True, True)]
+    for (name, N, T, H, HV, K, V, l2, pad) in cases:
+        q, k, v, _, beta, gen = _rng_inputs(zlib.crc32(name.encode()) % 1000, 1, N * T, H, HV, K, V)
+        gk = torch.nn.functional.logsigmoid(torch.randn(1, N * T, HV, K, generator=gen)) * 0.5
+        slots = 3 * N + 2
+        cache = torch.randn(slots, HV, V, K, generator=gen) * 0.5
+        cu = torch.arange(0, N * T + 1, T, dtype=torch.int64)
+        idx = torch.randperm(slots, generator=gen)[: N * T].reshape(N, T).clone()
+        if pad:
+            idx[1, 0] = -1
+        cache_in = cache.clone()
+        o = torch.empty_like(v)
+        BK, BV = triton.next_power_of_2(K), min(8, triton.next_power_of_2(V))
+        sis, sit = idx.stride()
+        mod.tmo_fused_recurrent_gated_delta_rule_fwd_kernel[(triton.cdiv(V, BV), N * HV)](
+            q=q, k=k, v=v, g=gk, beta=beta, o=o, h0=cache, ht=cache, cu_seqlens=cu,
+            ssm_state_indices=idx, num_accepted_tokens=None, scale=0.29, N=N, T=N * T, B=1, H=H, HV=HV,
+            K=K, V=V, BK=BK, BV=BV, stride_init_state_token=cache.stride(0),
+            stride_final_state_token=cache.stride(0), stride_indices_seq=sis, stride_indices_tok=sit,
+            IS_BETA_HEADWISE=False, USE_QK_L2NORM_IN_KERNEL=l2, INPLACE_FINAL_STATE=True, IS_KDA=True,
+            num_warps=1, num_stages=3)
+        np.savez_compressed(
+            os.path.join(HERE, f"rfn_{name}.npz"),
+            q=_np(q), k=_np(k), v=_np(v), g=_np(gk), beta=_np(beta), scale=np.float64(0.29),
+            cache_in=_np(cache_in), cu_seqlens=cu.numpy(), ssm_state_indices=idx.numpy(),
+            num_accepted_tokens=np.zeros(0, np.int64), l2norm=np.bool_(l2), inplace=np.bool_(True),
+            o=_np(o), final_state=_np(cache))
+        print("wrote", name)
+
+
 def gen_recurrent(ref: str):
     """Plain K-first recurrence (``fused_recurrent.py``), incl. config 0 shape."""
     mod = _load("torch_mlu_ops.triton.fla.fused_recurrent",
@@ -496,6 +536,8 @@ def main():
     torch.manual_seed(0)
     if a.only in ("", "rfn"):
         gen_recurrent_fn(a.ref)
+    if a.only in ("", "rfn", "kda"):
+        gen_recurrent_fn_kda(a.ref)
     if a.only in ("", "rec"):
         gen_recurrent(a.ref)
     if a.only in ("", "chunk"):

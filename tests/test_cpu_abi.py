@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.load()
     for name in _declared():
         assert hasattr(lib, name), name
-    assert lib.gdn_abi_version() == 1
+    assert lib.gdn_abi_version() == 2
     out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
                          text=True).stdout
     exported = {l.split()[-1] for l in out.splitlines() if " T " in l}

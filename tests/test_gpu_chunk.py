@@ -119,6 +119,50 @@ def test_config2_full_size_packing_equivalence(ops):
         assert torch.equal(h1[0], ht[n])
 
 
+def _oracle_seq(q, k, v, g, beta, h0, s, e):
+    """fp64 oracle of one packed sequence [s, e) (bf16-rounded inputs)."""
+    sl = lambda t: np64(t[:, s:e])
+    return oracle.chunk_gated_delta_rule(sl(q), sl(k), sl(v), sl(g), sl(beta), None,
+                                         None if h0 is None else np64(h0), True, None, True)
+
+
+def _check_bf16(o, ht, ro, rht):
+    e_o, m_o, e_h = rel_rms(np64(o), ro), max_abs(np64(o), ro), rel_rms(np64(ht), rht)
+    assert e_o < BF16_REL_RMS and m_o < BF16_MAX_ABS and e_h < BF16_REL_RMS, (e_o, m_o, e_h)
+
+
+def test_config2_full_size_against_oracle(ops):
+    """BASELINE config 2 at full size (seed 2: 16 sequences, lengths
+    U[512, 8192], packed via cu_seqlens, states N(0, 0.02)): the shortest,
+    the median and the longest sequence, all 32 v-heads, outputs and final
+    states against the fp64 oracle (cu_seqlens semantics of
+    triton/fla/index.py:13-32)."""
+    rng = np.random.default_rng(2)
+    lens = rng.integers(512, 8193, size=16)
+    cu = np.concatenate([[0], np.cumsum(lens)])
+    q, k, v, g, beta, h0 = make_inputs(2, 1, int(cu[-1]), 16, 32, 128, 128, nseq_state=16, state_std=0.02)
+    o, ht = ops.chunk_gated_delta_rule(q, k, v, g, beta, None, h0, True, torch.from_numpy(cu).cuda(),
+                                       use_qk_l2norm_in_kernel=True)
+    order = np.argsort(lens, kind="stable")
+    for n in (int(order[0]), int(order[len(order) // 2]), int(order[-1])):
+        s, e = int(cu[n]), int(cu[n + 1])
+        ro, rht = _oracle_seq(q, k, v, g, beta, h0[n:n + 1], s, e)
+        _check_bf16(o[:, s:e], ht[n:n + 1], ro, rht)
+
+
+def test_config4_full_size_against_oracle(ops):
+    """BASELINE config 4 at full size (seed 4: 64 sequences x 4096 tokens):
+    sequences 0, 31 and 63 against the fp64 oracle."""
+    B, T = 64, 4096
+    q, k, v, g, beta, _ = make_inputs(4, B, T, 16, 32, 128, 128)
+    o, ht = ops.chunk_gated_delta_rule(q, k, v, g, beta, None, None, True, use_qk_l2norm_in_kernel=True)
+    for n in (0, 31, 63):
+        sl = lambda t: t[n:n + 1]
+        ro, rht = oracle.chunk_gated_delta_rule(np64(sl(q)), np64(sl(k)), np64(sl(v)), np64(sl(g)),
+                                                np64(sl(beta)), None, None, True, None, True)
+        _check_bf16(o[n:n + 1], ht[n:n + 1], ro, rht)
+
+
 def test_chunk_equals_recurrent_on_gpu(ops):
     """The chunked op and the token-by-token op agree (fp32)."""
     q, k, v, g, beta, h0 = make_inputs(9, 1, 333, 2, 4, 64, 64, dtype=torch.float32,

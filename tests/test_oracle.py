@@ -30,12 +30,13 @@ def test_oracle_matches_reference_decode(path):
     nacc = d["num_accepted_tokens"]
     cache = d["cache_in"].astype(np.float64).copy()
     N = len(d["cu_seqlens"]) - 1
+    kda = d["g"].ndim == 4  # per-key decays (the kernel's IS_KDA branch)
     o, ht, valid = oracle.recurrent_v_first(
-        d["q"], d["k"], d["v"], d["g"], d["beta"], float(d["scale"]), cache,
+        d["q"], d["k"], d["v"], None if kda else d["g"], d["beta"], float(d["scale"]), cache,
         inplace_final_state=bool(d["inplace"]), cu_seqlens=d["cu_seqlens"],
         ssm_state_indices=d["ssm_state_indices"],
         num_accepted_tokens=nacc if nacc.size else None,
-        use_qk_l2norm_in_kernel=bool(d["l2norm"]))
+        use_qk_l2norm_in_kernel=bool(d["l2norm"]), gk=d["g"] if kda else None)
     cu = d["cu_seqlens"]
     for n in range(N):
         if not valid[n]:
