@@ -133,12 +133,26 @@ def _raise_err_word(w):
                             f"{what} (code {h[0]}, site {h[1]}, sequence/block {h[2]}, info {h[3]})")
 
 
+def _real(x):
+    return not isinstance(x, torch.Tensor) or type(x) is torch.Tensor or type(x) is torch.nn.Parameter
+
+
+def _call(op, impl, *args):
+    """Run a custom op.  Eager calls on plain tensors go straight to its
+    implementation: the custom-op dispatcher costs about 15 us of host time
+    per call, which leaves the GPU idle between launches as short as a
+    decode step.  Traced calls (torch.compile, FakeTensor and other tensor
+    subclasses) go through the registered op, whose fake gives the shapes."""
+    if torch.compiler.is_compiling() or not all(_real(x) for x in args):
+        return op(*args)
+    return impl(*args)
+
+
 # ---------------------------------------------------------------------------
 # torch.library custom ops (CUDA implementations call the C ABI)
 # ---------------------------------------------------------------------------
 
-@torch.library.custom_op("gdn_b200::chunk_fwd", mutates_args=(), device_types="cuda")
-def _chunk_fwd_op(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: float,
+def _chunk_fwd_impl(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: float,
                   initial_state: Optional[Tensor], output_final_state: bool,
                   cu_seqlens: Optional[Tensor], state_v_first: bool, use_qk_l2norm: bool,
                   force_generic: bool, check_errors: bool) -> tuple[Tensor, Tensor]:
@@ -173,6 +187,10 @@ def _chunk_fwd_op(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scal
     return o, (ht if ht is not None else _empty_f32(dev))
 
 
+_chunk_fwd_op = torch.library.custom_op("gdn_b200::chunk_fwd", mutates_args=(),
+                device_types="cuda")(_chunk_fwd_impl)
+
+
 @_chunk_fwd_op.register_fake
 def _(q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens, state_v_first,
       use_qk_l2norm, force_generic, check_errors):
@@ -186,8 +204,7 @@ def _(q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens, st
     return o, v.new_empty(shape_state, dtype=torch.float32)
 
 
-@torch.library.custom_op("gdn_b200::chunk_bwd", mutates_args=(), device_types="cuda")
-def _chunk_bwd_op(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: float,
+def _chunk_bwd_impl(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: float,
                   initial_state: Optional[Tensor], cu_seqlens: Optional[Tensor], dout: Tensor,
                   dht: Optional[Tensor], state_v_first: bool,
                   use_qk_l2norm: bool) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
@@ -219,6 +236,10 @@ def _chunk_bwd_op(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scal
     with torch.cuda.device(dev):
         _lib.check(lib.gdn_chunk_bwd(ctypes.byref(args), _stream(dev)))
     return dq, dk, dv, dg, db, (dh0 if dh0 is not None else _empty_f32(dev))
+
+
+_chunk_bwd_op = torch.library.custom_op("gdn_b200::chunk_bwd", mutates_args=(),
+                device_types="cuda")(_chunk_bwd_impl)
 
 
 @_chunk_bwd_op.register_fake
@@ -263,8 +284,7 @@ def _run_recurrent(args, dev, check_errors, err):
             _raise_err_word(err)
 
 
-@torch.library.custom_op("gdn_b200::recurrent_fn_inplace", mutates_args=("state",), device_types="cuda")
-def _recurrent_fn_inplace_op(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk: Optional[Tensor],
+def _recurrent_fn_inplace_impl(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk: Optional[Tensor],
                              beta: Tensor, scale: float, state: Tensor, cu_seqlens: Optional[Tensor],
                              ssm_state_indices: Tensor, num_accepted_tokens: Optional[Tensor],
                              use_qk_l2norm: bool, check_errors: bool) -> Tensor:
@@ -278,14 +298,17 @@ def _recurrent_fn_inplace_op(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor
     return o
 
 
+_recurrent_fn_inplace_op = torch.library.custom_op("gdn_b200::recurrent_fn_inplace", mutates_args=("state",),
+                           device_types="cuda")(_recurrent_fn_inplace_impl)
+
+
 @_recurrent_fn_inplace_op.register_fake
 def _(q, k, v, g, gk, beta, scale, state, cu_seqlens, ssm_state_indices, num_accepted_tokens,
       use_qk_l2norm, check_errors):
     return v.new_empty(v.shape)
 
 
-@torch.library.custom_op("gdn_b200::recurrent_fn", mutates_args=(), device_types="cuda")
-def _recurrent_fn_op(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk: Optional[Tensor],
+def _recurrent_fn_impl(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk: Optional[Tensor],
                      beta: Tensor, scale: float, initial_state: Optional[Tensor],
                      cu_seqlens: Optional[Tensor], ssm_state_indices: Optional[Tensor],
                      num_accepted_tokens: Optional[Tensor], use_qk_l2norm: bool,
@@ -304,6 +327,10 @@ def _recurrent_fn_op(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk: O
     return o, final_state
 
 
+_recurrent_fn_op = torch.library.custom_op("gdn_b200::recurrent_fn", mutates_args=(),
+                   device_types="cuda")(_recurrent_fn_impl)
+
+
 @_recurrent_fn_op.register_fake
 def _(q, k, v, g, gk, beta, scale, initial_state, cu_seqlens, ssm_state_indices, num_accepted_tokens,
       use_qk_l2norm, check_errors):
@@ -312,8 +339,7 @@ def _(q, k, v, g, gk, beta, scale, initial_state, cu_seqlens, ssm_state_indices,
     return v.new_empty(v.shape), v.new_empty((B * T, HV, V, K), dtype=torch.float32)
 
 
-@torch.library.custom_op("gdn_b200::recurrent_plain", mutates_args=(), device_types="cuda")
-def _recurrent_plain_op(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk: Optional[Tensor],
+def _recurrent_plain_impl(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk: Optional[Tensor],
                         gv: Optional[Tensor], beta: Tensor, scale: float, initial_state: Optional[Tensor],
                         output_final_state: bool, use_qk_l2norm: bool,
                         cu_seqlens: Optional[Tensor]) -> tuple[Tensor, Tensor]:
@@ -335,6 +361,10 @@ def _recurrent_plain_op(q: Tensor, k: Tensor, v: Tensor, g: Optional[Tensor], gk
     return o, (ht if ht is not None else _empty_f32(dev))
 
 
+_recurrent_plain_op = torch.library.custom_op("gdn_b200::recurrent_plain", mutates_args=(),
+                      device_types="cuda")(_recurrent_plain_impl)
+
+
 @_recurrent_plain_op.register_fake
 def _(q, k, v, g, gk, gv, beta, scale, initial_state, output_final_state, use_qk_l2norm, cu_seqlens):
     B, T, H, K = k.shape
@@ -344,8 +374,7 @@ def _(q, k, v, g, gk, gv, beta, scale, initial_state, output_final_state, use_qk
     return v.new_empty(v.shape), ht
 
 
-@torch.library.custom_op("gdn_b200::solve_tril", mutates_args=("output",), device_types="cuda")
-def _solve_tril_op(input: Tensor, output: Tensor, cu_seqlens: Optional[Tensor]) -> None:
+def _solve_tril_impl(input: Tensor, output: Tensor, cu_seqlens: Optional[Tensor]) -> None:
     """``solve_tril(input, output, cu_seqlens)`` of the native op
     (``include/torch_mlu_ops.h:1052-1054``): input fp32 ``[B, T, H, BT]``
     contiguous, output of the same shape (contiguous) written in place."""
@@ -356,6 +385,10 @@ def _solve_tril_op(input: Tensor, output: Tensor, cu_seqlens: Optional[Tensor]) 
     with torch.cuda.device(dev):
         _lib.check(_lib.load().gdn_solve_tril(
             _ptr(input), _ptr(output), _DT[output.dtype], _ptr(cu), cu_dt, N, B, T, H, BT, _stream(dev)))
+
+
+_solve_tril_op = torch.library.custom_op("gdn_b200::solve_tril", mutates_args=("output",),
+                 device_types="cuda")(_solve_tril_impl)
 
 
 @_solve_tril_op.register_fake
@@ -399,9 +432,9 @@ class ChunkGatedDeltaRuleFunction(torch.autograd.Function):
         cu = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first)
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         g32, b32, h0 = _f32(g), _f32(beta), _f32(initial_state)
-        o, ht = torch.ops.gdn_b200.chunk_fwd(q, k, v, g32, b32, _scale(scale), h0, bool(output_final_state),
-                                             cu, bool(state_v_first), bool(use_qk_l2norm),
-                                             bool(force_generic), bool(check_errors))
+        o, ht = _call(torch.ops.gdn_b200.chunk_fwd, _chunk_fwd_impl, q, k, v, g32, b32, _scale(scale), h0,
+                      bool(output_final_state), cu, bool(state_v_first), bool(use_qk_l2norm),
+                      bool(force_generic), bool(check_errors))
         ctx.save_for_backward(q, k, v, g32, b32, h0, cu)
         ctx.meta = (_scale(scale), bool(state_v_first), bool(use_qk_l2norm), g.dtype, beta.dtype,
                     None if initial_state is None else initial_state.dtype)
@@ -415,8 +448,8 @@ class ChunkGatedDeltaRuleFunction(torch.autograd.Function):
             do = torch.zeros_like(v, dtype=q.dtype)
         do = do.to(q.dtype).contiguous()
         dht = None if dht is None else dht.to(torch.float32).contiguous()
-        dq, dk, dv, dg, db, dh0 = torch.ops.gdn_b200.chunk_bwd(q, k, v, g32, b32, scale, h0, cu, do, dht,
-                                                               svf, l2)
+        dq, dk, dv, dg, db, dh0 = _call(torch.ops.gdn_b200.chunk_bwd, _chunk_bwd_impl, q, k, v, g32, b32,
+                                        scale, h0, cu, do, dht, svf, l2)
         dh0 = dh0.to(h0_dt) if h0 is not None else None
         return (dq, dk, dv, dg.to(g_dt), db.to(b_dt), None, dh0, None, None, None, None, None, None)
 
@@ -462,9 +495,9 @@ def chunk_gated_delta_rule(
             q, k, v, g, beta, scale, initial_state, output_final_state, cu_seqlens, state_v_first,
             use_qk_l2norm_in_kernel, force_generic, check_errors)
     cu = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first)
-    o, ht = torch.ops.gdn_b200.chunk_fwd(
-        q.contiguous(), k.contiguous(), v.contiguous(), _f32(g), _f32(beta), _scale(scale),
-        _f32(initial_state), bool(output_final_state), cu, bool(state_v_first),
+    o, ht = _call(
+        torch.ops.gdn_b200.chunk_fwd, _chunk_fwd_impl, q.contiguous(), k.contiguous(), v.contiguous(),
+        _f32(g), _f32(beta), _scale(scale), _f32(initial_state), bool(output_final_state), cu, bool(state_v_first),
         bool(use_qk_l2norm_in_kernel), bool(force_generic), bool(check_errors))
     return o, (ht if output_final_state else None)
 
@@ -573,9 +606,9 @@ def chunk_gated_delta_rule_bwd(q, k, v, g, beta, scale, initial_state, dout, dht
     cu = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first)
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     h0 = _f32(initial_state)
-    dq, dk, dv, dg, db, dh0 = torch.ops.gdn_b200.chunk_bwd(
-        q, k, v, _f32(g), _f32(beta), _scale(scale), h0, cu, dout.to(q.dtype).contiguous(),
-        None if dht is None else _f32(dht), bool(state_v_first), bool(use_qk_l2norm_in_kernel))
+    dq, dk, dv, dg, db, dh0 = _call(
+        torch.ops.gdn_b200.chunk_bwd, _chunk_bwd_impl, q, k, v, _f32(g), _f32(beta), _scale(scale), h0, cu,
+        dout.to(q.dtype).contiguous(), None if dht is None else _f32(dht), bool(state_v_first), bool(use_qk_l2norm_in_kernel))
     return dq, dk, dv, db, dg, (dh0 if h0 is not None else None)
 
 
@@ -647,11 +680,11 @@ def fused_recurrent_gated_delta_rule_fn(
     if inplace_final_state:
         if initial_state is None or idx is None:
             raise ValueError("inplace_final_state=True needs initial_state and ssm_state_indices")
-        o = torch.ops.gdn_b200.recurrent_fn_inplace(q, k, v, g, gk, beta, float(scale), initial_state, cu, idx,
-                                                   nacc, bool(use_qk_l2norm_in_kernel), bool(check_errors))
+        o = _call(torch.ops.gdn_b200.recurrent_fn_inplace, _recurrent_fn_inplace_impl, q, k, v, g, gk, beta,
+                  float(scale), initial_state, cu, idx, nacc, bool(use_qk_l2norm_in_kernel), bool(check_errors))
         return o, initial_state
-    return torch.ops.gdn_b200.recurrent_fn(q, k, v, g, gk, beta, float(scale), initial_state, cu, idx, nacc,
-                                           bool(use_qk_l2norm_in_kernel), bool(check_errors))
+    return _call(torch.ops.gdn_b200.recurrent_fn, _recurrent_fn_impl, q, k, v, g, gk, beta, float(scale),
+                 initial_state, cu, idx, nacc, bool(use_qk_l2norm_in_kernel), bool(check_errors))
 
 
 def fused_recurrent_gated_delta_rule(
@@ -707,8 +740,8 @@ def fused_recurrent_gated_delta_rule(
         if tuple(initial_state.shape) != (N, HV, K, V):
             raise ValueError(f"initial_state must be {(N, HV, K, V)}, got {tuple(initial_state.shape)}")
         h0 = _f32(initial_state)
-    o, ht = torch.ops.gdn_b200.recurrent_plain(q, k, v, g, gk, gv, beta, _scale(scale), h0,
-                                               bool(output_final_state), bool(use_qk_l2norm_in_kernel), cu)
+    o, ht = _call(torch.ops.gdn_b200.recurrent_plain, _recurrent_plain_impl, q, k, v, g, gk, gv, beta,
+                  _scale(scale), h0, bool(output_final_state), bool(use_qk_l2norm_in_kernel), cu)
     return o, (ht if output_final_state else None)
 
 
@@ -731,7 +764,7 @@ def solve_tril(input: torch.Tensor, output: torch.Tensor = None, cu_seqlens: tor
     out = output if output.is_contiguous() else torch.empty_like(output)
     out4 = out.unsqueeze(0) if out.dim() == 3 else out
     cu, _ = _idx(cu_seqlens)
-    torch.ops.gdn_b200.solve_tril(x, out4, cu)
+    _call(torch.ops.gdn_b200.solve_tril, _solve_tril_impl, x, out4, cu)
     if out is not output:
         output.copy_(out)
     return output
