@@ -47,8 +47,9 @@ def stage_flops_per_token_head(K, V, bt=BT, path="tc"):
     tcgen05 path: the WY kernel does KK^T, qK^T, w, u; the state kernel does
     w.h, q.h, K^T v_new and A v_new.  Generic path: wy / state / out."""
     if path == "tc":
-        return {"wy": 2 * bt * K + 2 * bt * K + 2 * bt * K + 2 * bt * V,
-                "state": 2 * K * V * 3 + 2 * bt * V}
+        wy = 2 * bt * K + 2 * bt * K + 2 * bt * K + 2 * bt * V
+        state = 2 * K * V * 3 + 2 * bt * V
+        return {"wy": wy, "state": state, "fused": wy + state}
     return {
         "wy": 2 * bt * K + 2 * bt * K + 2 * bt * V,       # KK^T, w, u
         "state": 2 * K * V + 2 * K * V,                     # w.h, K^T v_new
@@ -477,7 +478,7 @@ def run_ours(a):
         value = tokens / (ms / 1e3)
         fl_tok = flops_per_token_head(K, V)
         total_flops = B * T * HV * fl_tok  # this rank's share (rank 0)
-        sfl = stage_flops_per_token_head(K, V, path="tc" if "plan" in stage_avg and len(stage_avg) == 3 else "generic")
+        sfl = stage_flops_per_token_head(K, V, path="tc" if "plan" in stage_avg and len(stage_avg) <= 3 else "generic")
         dom = max(stage_avg, key=stage_avg.get)
         dom_key = dom.split(":")[0]
         dom_flops = B * T * HV * sfl.get(dom_key, 0)
@@ -598,8 +599,10 @@ def _stage_names(n):
     # launch order of the chunk paths (launchers in domesticated_torch_mlu_ops_b200/csrc/)
     if n == 6:  # generic fp32 path
         return ["plan", "prep:q", "prep:k", "wy", "state", "out"]
-    if n == 3:  # tcgen05 path
+    if n == 3:  # tcgen05 path, separate WY and state kernels
         return ["plan", "wy", "state"]
+    if n == 2:  # tcgen05 path, fused cluster kernel
+        return ["plan", "fused"]
     return [f"k{i}" for i in range(n)]
 
 

@@ -19,11 +19,12 @@
 namespace gdn {
 
 __global__ void chunk_plan_kernel(const void* cu, int cu_dtype, int64_t N, int64_t T,
-                                  int64_t* off, int chunk, int* err) {
+                                  int64_t* off, int chunk, int* err, int* zero, int64_t nzero) {
   __shared__ int64_t warp_tot[32];
   __shared__ int64_t carry;
   if (threadIdx.x == 0) { carry = 0; off[0] = 0; }
   if (err && threadIdx.x < 4) err[threadIdx.x] = 0;  // the call's device error word starts clear
+  for (int64_t i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0;
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int64_t base = 0; base < N; base += blockDim.x) {
@@ -62,8 +63,9 @@ __global__ void chunk_plan_kernel(const void* cu, int cu_dtype, int64_t N, int64
 }
 
 cudaError_t launch_chunk_plan(const void* cu, int cu_dtype, int64_t N, int64_t T,
-                              int64_t* chunk_offsets, cudaStream_t s, int chunk, int* err) {
-  chunk_plan_kernel<<<1, 1024, 0, s>>>(cu, cu_dtype, N, T, chunk_offsets, chunk, err);
+                              int64_t* chunk_offsets, cudaStream_t s, int chunk, int* err, int* zero,
+                              int64_t nzero) {
+  chunk_plan_kernel<<<1, 1024, 0, s>>>(cu, cu_dtype, N, T, chunk_offsets, chunk, err, zero, nzero);
   return cudaGetLastError();
 }
 

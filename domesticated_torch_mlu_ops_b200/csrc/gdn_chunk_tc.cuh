@@ -1,0 +1,158 @@
+// Shared pieces of the tensor-core (tcgen05) chunked prefill kernels
+// (gdn_chunk_tc.cu: separate WY and state kernels; gdn_chunk_fused.cu: the
+// cluster kernel that computes both): sizes, the workspace carve-up, operand
+// image layouts and small device helpers.
+#pragma once
+
+#include <cuda.h>
+
+#include <type_traits>
+
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+#include "umma.cuh"
+
+namespace gdn {
+namespace tc {
+
+constexpr int D = 128;                  // K = V = 128
+constexpr int kImg64x128 = 64 * D * 2;  // 16 KiB
+constexpr int kImg64x64 = 64 * 64 * 2;  // 8 KiB
+constexpr int RS64 = (64 / 8) * 128;    // image row stride of a 64-column tile
+constexpr int kScal = 132;              // per-(head, chunk) scalars: a[64], b[64], gamma, pad
+constexpr int kAtom = 64 * 128;         // one 64-row x 128-byte swizzled atom (8 KiB)
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Work {
+  const int64_t* coff;  // [N+1] chunk offsets
+  int* err;             // device error word
+  uint8_t* wimg;        // [HV][NCU][16 KiB]
+  uint8_t* u;           // [HV][NCU][128/vs][64][vs] (rows swizzled; u_off)
+  uint8_t* pimg;        // [HV][NCU][8 KiB]
+  float* scal;          // [HV][NCU][kScal]: a[64], b[64], gamma, pad
+  int64_t ncu;          // chunk capacity
+  int vs;               // V-slice width of the state kernel (U layout)
+  int* flags;           // [HV][NCU] tile-ready flags of the fused kernel (zeroed by the plan kernel)
+  // Test hook (gdn_chunk_fwd_test_stall): block 0 of the state kernel skips
+  // the operand fetch of chunk stall_chunk (-1: none) and bounds its waits by
+  // stall_limit cycles, so that one wait runs out with nothing in flight.
+  int64_t stall_chunk;
+  long long stall_limit;
+};
+
+struct Layout {
+  size_t err, coff, wimg, u, pimg, scal, flags, total;
+};
+
+inline Layout plan(const gdn_chunk_args& a) {
+  auto al = [](size_t x) { return (x + 1023) & ~static_cast<size_t>(1023); };
+  const int64_t ncu = chunk_upper_bound(a.B * a.T, a.N);
+  const size_t hc = static_cast<size_t>(a.HV) * ncu;
+  Layout l{};
+  size_t o = 0;
+  l.err = o; o += al(16);
+  l.coff = o; o += al(sizeof(int64_t) * (a.N + 1));
+  l.wimg = o; o += al(hc * kImg64x128);
+  l.u = o; o += al(hc * 64 * D * 2);
+  l.pimg = o; o += al(hc * kImg64x64);
+  l.scal = o; o += al(hc * kScal * 4);
+  l.flags = o; o += al(hc * 4);
+  l.total = o;
+  return l;
+}
+
+__device__ __forceinline__ void record_error(int* err, int code, int site) {
+  record_device_error(err, code, site, linear_block_id(), static_cast<int>(threadIdx.x));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* x) {
+  uint4 r;
+  if constexpr (std::is_same<T, __half>::value) {
+    r.x = pack_h2(x[0], x[1]); r.y = pack_h2(x[2], x[3]);
+    r.z = pack_h2(x[4], x[5]); r.w = pack_h2(x[6], x[7]);
+  } else {
+    r.x = pack_bf16x2(x[0], x[1]); r.y = pack_bf16x2(x[2], x[3]);
+    r.z = pack_bf16x2(x[4], x[5]); r.w = pack_bf16x2(x[6], x[7]);
+  }
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ void unpack8(uint4 u, float* x) {
+  const T* p = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = to_f<T>(p[i]);
+}
+
+// K-major descriptor of k-step ks (16 elements) of a 64-row swizzled tile.
+__device__ __forceinline__ uint64_t sw_kmajor(uint32_t base, int ks) {
+  return umma::smem_desc_sw128(base + (ks >> 2) * kAtom + (ks & 3) * 32, 16, 1024);
+}
+// MN-major descriptor (MN = the 128 tile columns, K = the 64 rows) of k-step ks.
+__device__ __forceinline__ uint64_t sw_mnmajor(uint32_t base, int ks) {
+  return umma::smem_desc_sw128(base + ks * 2048, kAtom, 1024);
+}
+// Both 64-column boxes of rows [s, s+64) of head hd of a [T, heads, 128] tensor.
+__device__ __forceinline__ void tma_tile(uint8_t* dst, const CUtensorMap* map, int hd, int64_t s,
+                                         uint32_t bar) {
+  umma::tma_load_3d(dst, map, 0, hd, static_cast<int>(s), bar);
+  umma::tma_load_3d(dst + kAtom, map, 64, hd, static_cast<int>(s), bar);
+}
+
+// Element offset of (row i, column c) in a U tile of S-column slices
+// ([128/S][64][S], S = 32 or 64).  The 16-byte chunks of each row are
+// XOR-swizzled so that eight consecutive rows touch distinct bank groups.
+__device__ __forceinline__ int u_off(int i, int c, int S) {
+  const bool s64 = S == 64;
+  const int sw = s64 ? (i & 7) : ((i >> 1) & 3);  // (i / (8 / chunks per row)) mod chunks per row
+  const int sl = c >> (s64 ? 6 : 5), wc = c & (S - 1);
+  return (sl * 64 + i) * S + ((((wc >> 3) ^ sw)) << 3) + (wc & 7);
+}
+
+template <int VS_>
+struct St3 {
+  static constexpr int VS = VS_;
+  // stage: W a0 | Q a0 | W a1 | Q a1 | K a0 | K a1 | P | U | scalars
+  static constexpr int kWQ = 0;
+  static constexpr int kK = 4 * kAtom;
+  static constexpr int kP = kK + 2 * kAtom;
+  static constexpr int kU = kP + kImg64x64;
+  static constexpr int kUBytes = 64 * VS * 2;
+  static constexpr int kSc = kU + kUBytes;
+  static constexpr int kStage = ((kSc + kScal * 4 + 1023) / 1024) * 1024;
+  static constexpr uint32_t kTx = 4 * kAtom + 2 * kAtom + kImg64x64 + kUBytes + kScal * 4;
+  static constexpr int kStages = VS == 32 ? 3 : 2;  // a third 65 KB stage does not fit at VS = 64
+  static constexpr int kH = kStages * kStage;    // h image 128 x VS
+  static constexpr int kVn = kH + D * VS * 2;    // v image 64 x VS
+  static constexpr int kVt = kVn + 64 * VS * 2;  // diag(b) v image 64 x VS
+  static constexpr int kBar = kVt + 64 * VS * 2; // full[kStages], mma1, dh, o
+  static constexpr int kTmem = kBar + 6 * 8;
+  static constexpr int kBytes = kTmem + 8 + 1024;
+  // TMEM columns: acc[2], dH, O[2] (VS each)
+  static constexpr int kAcc = 0, kDH = 2 * VS, kO = 3 * VS, kCols = VS == 32 ? 256 : 512;
+  static_assert(kO + 2 * VS <= kCols, "TMEM columns");
+  static_assert(kBytes <= 227 * 1024, "shared memory");
+};
+constexpr int kSt3Threads = 288;  // 8 epilogue warps + 1 load warp
+
+// [Ttot, heads, 128] bf16/f16 tensor map with 64 x 64 boxes, 128-byte swizzle.
+cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, bool f16);
+
+// The fused cluster kernel (gdn_chunk_fused.cu): whether clusters of it can
+// be scheduled on the current device, and its launcher (tq, tk, tv as made by
+// make_map; the workspace holds only the error word and chunk offsets it uses).
+bool fused_launchable(bool f16);
+template <typename T>
+cudaError_t launch_fused(const gdn_chunk_args& a, const Work& w, float scale, const CUtensorMap& tq,
+                         const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t s);
+
+}  // namespace tc
+}  // namespace gdn

@@ -98,7 +98,8 @@ enum ErrSite {
   kSiteWyLoad = 1, kSiteWyMma1 = 2, kSiteWyMma2 = 3,       // tc_wy_kernel
   kSiteStLoad = 4, kSiteStMma1 = 5, kSiteStMma2 = 6,       // tc_state3_kernel
   kSiteDecodeRelease = 7, kSiteDecodeLoad = 8,             // decode_stream_kernel waits
-  kSiteSlotInitial = 9, kSiteSlotFinal = 10                // state index >= num_slots
+  kSiteSlotInitial = 9, kSiteSlotFinal = 10,               // state index >= num_slots
+  kSiteFzReady = 11                                        // tc_fused_kernel: stage-ready wait
 };
 
 __device__ __forceinline__ void record_device_error(int* err, int code, int site, int block, int info) {

@@ -83,9 +83,10 @@ cudaError_t launch_solve_tril(const float* A, void* out, int out_dtype, const vo
                               cudaStream_t s);
 // chunk_offsets[0..N] from cu_seqlens (or the equal-length batch); also
 // zeroes the call's 16-byte device error word `err` when it is given, so that
-// every call starts with a clear word (the plan kernel runs first).
+// every call starts with a clear word (the plan kernel runs first), and the
+// nzero ints at `zero` (per-call flags of the kernels that follow).
 cudaError_t launch_chunk_plan(const void* cu, int cu_dtype, int64_t N, int64_t T,
                               int64_t* chunk_offsets, cudaStream_t s, int chunk = 64,
-                              int* err = nullptr);
+                              int* err = nullptr, int* zero = nullptr, int64_t nzero = 0);
 
 }  // namespace gdn

@@ -200,9 +200,13 @@ __device__ __forceinline__ void mma_rows(float (&d)[4], const float* X, int xs, 
 }
 
 // A: [64][kMS] (strictly lower part read), T: [64][kMS], Z: kMScratch floats;
-// 16-byte aligned.  All 256 threads call this; it ends with a __syncthreads.
+// 16-byte aligned.  256 threads (thread ids 0..255 of the block) call this;
+// they synchronise on named barrier BAR (0 with 256 threads is
+// __syncthreads in a 256-thread block), and it ends with that barrier.
+template <int BAR = 0>
 __device__ __forceinline__ void solve_tril64_mma(const float* __restrict__ A, float* __restrict__ T,
                                                  float* __restrict__ Z) {
+  auto sync = [] { asm volatile("bar.sync %0, 256;" :: "n"(BAR) : "memory"); };
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   // 1. diagonal 16 x 16 blocks, right-looking substitution (one column per thread)
   if (tid < 64) {
@@ -224,7 +228,7 @@ __device__ __forceinline__ void solve_tril64_mma(const float* __restrict__ A, fl
     const int r = e >> 4, c = (e & 15) * 4;
     if ((r >> 4) < (c >> 4)) st4(T + r * kMS + c, make_float4(0.f, 0.f, 0.f, 0.f));
   }
-  __syncthreads();
+  sync();
   // 2. T_10 = -T_11 (A_10 T_00), T_32 = -T_33 (A_32 T_22): warp w < 4 owns
   //    block w >> 1 and the 8-column half w & 1 of its 16 x 16 result
   if (warp < 4) {
@@ -236,7 +240,7 @@ __device__ __forceinline__ void solve_tril64_mma(const float* __restrict__ A, fl
     *reinterpret_cast<float2*>(z + g * kMZS + 2 * t) = make_float2(d[0], d[1]);
     *reinterpret_cast<float2*>(z + (g + 8) * kMZS + 2 * t) = make_float2(d[2], d[3]);
   }
-  __syncthreads();
+  sync();
   if (warp < 4) {
     const int blk = warp >> 1, nh = (warp & 1) * 8;
     const int rb = 16 * (2 * blk + 1), cb = 16 * (2 * blk);
@@ -246,7 +250,7 @@ __device__ __forceinline__ void solve_tril64_mma(const float* __restrict__ A, fl
     *reinterpret_cast<float2*>(o + g * kMS + 2 * t) = make_float2(-d[0], -d[1]);
     *reinterpret_cast<float2*>(o + (g + 8) * kMS + 2 * t) = make_float2(-d[2], -d[3]);
   }
-  __syncthreads();
+  sync();
   // 3. T[32:64, 0:32] = -T_hi (A[32:64, 0:32] T_lo): warp w owns rows
   //    32 + 16 (w >> 2) .. +16 and columns 8 (w & 3) .. +8
   {
@@ -256,14 +260,14 @@ __device__ __forceinline__ void solve_tril64_mma(const float* __restrict__ A, fl
     float* z = Z + mr * kMZS + nc;
     *reinterpret_cast<float2*>(z + g * kMZS + 2 * t) = make_float2(d[0], d[1]);
     *reinterpret_cast<float2*>(z + (g + 8) * kMZS + 2 * t) = make_float2(d[2], d[3]);
-    __syncthreads();
+    sync();
     float e[4] = {0.f, 0.f, 0.f, 0.f};
     mma_rows(e, T + (32 + mr) * kMS + 32, kMS, Z + nc, kMZS, 4);
     float* o = T + (32 + mr) * kMS + nc;
     *reinterpret_cast<float2*>(o + g * kMS + 2 * t) = make_float2(-e[0], -e[1]);
     *reinterpret_cast<float2*>(o + (g + 8) * kMS + 2 * t) = make_float2(-e[2], -e[3]);
   }
-  __syncthreads();
+  sync();
 }
 
 }  // namespace gdn

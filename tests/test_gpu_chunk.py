@@ -211,3 +211,40 @@ def test_bf16_tensor_core_path_variants(ops, case):
     name, B, T, H, HV, cu, h0_std, vfirst = case
     _check(ops, 17 + len(name), B, T, H, HV, 128, 128, torch.bfloat16, cu=cu, h0_std=h0_std,
            state_v_first=vfirst)
+
+
+FUSED_CASES = [
+    # (name, B, T, H, HV, cu, h0_std, state_v_first): chunk counts not a
+    # multiple of the cluster size, partial chunks, empty and one-chunk
+    # sequences, more clusters than fit at once
+    ("one_seq", 1, 1000, 16, 32, None, 0.02, False),
+    ("varlen", 1, 900, 4, 8, [0, 0, 1, 63, 64, 65, 300, 900], 0.02, True),
+    ("many", 40, 200, 8, 16, None, 0.02, False),
+]
+
+
+@pytest.mark.parametrize("case", FUSED_CASES, ids=[c[0] for c in FUSED_CASES])
+def test_fused_kernel_matches_split_kernels(ops, case, monkeypatch):
+    """The fused cluster kernel (WY tiles delivered through distributed shared
+    memory) against the separate WY + state kernels on the same inputs: the
+    same arithmetic, so the outputs agree to the last bit when the split path
+    uses 32-column slices too, and both meet the oracle tolerance."""
+    name, B, T, H, HV, cu, h0_std, vfirst = case
+    N = B if cu is None else len(cu) - 1
+    q, k, v, g, beta, h0 = make_inputs(60 + len(name), B, T, H, HV, 128, 128, nseq_state=N, state_std=h0_std)
+    if vfirst:
+        h0 = h0.transpose(-1, -2).contiguous()
+    cut = None if cu is None else torch.tensor(cu, dtype=torch.int64).cuda()
+    res = {}
+    for path in ("1", "0"):
+        monkeypatch.setenv("GDN_TC_FUSED", path)
+        res[path] = ops.chunk_gated_delta_rule(q, k, v, g, beta, None, h0, True, cut, state_v_first=vfirst,
+                                               use_qk_l2norm_in_kernel=True, check_errors=True)
+    (of, hf), (os_, hs) = res["1"], res["0"]
+    if N * HV <= 148:  # the split path's state kernel also uses 32-column slices
+        assert torch.equal(of, os_) and torch.equal(hf, hs)
+    ro, rht = oracle.chunk_gated_delta_rule(np64(q), np64(k), np64(v), np64(g), np64(beta), None, np64(h0),
+                                            True, cu, True, vfirst)
+    for o_, h_ in ((of, hf), (os_, hs)):
+        assert rel_rms(np64(o_), ro) < BF16_REL_RMS and max_abs(np64(o_), ro) < BF16_MAX_ABS
+        assert rel_rms(np64(h_), rht) < BF16_REL_RMS

@@ -3,12 +3,13 @@
 * The prefill's device error word starts clear on every call, even in a
   workspace full of stale bytes.
 * A bounded wait that runs out: ``gdn_chunk_fwd_test_stall`` makes the first
-  block of the state kernel skip one chunk's operand copies (so nothing is in
-  flight on that barrier) and bounds its waits by a few million cycles.  The
-  call must report ``GDN_ERR_DEVICE`` with the load-wait site through
-  ``gdn_chunk_check_device_error``, leave every other block's output equal to
+  block of the state recurrence skip one chunk's operand copies (so nothing
+  is in flight on that barrier) and bounds its waits by a few million cycles.
+  The call must report ``GDN_ERR_DEVICE`` through
+  ``gdn_chunk_check_device_error``, leave the other v-heads' outputs equal to
   a clean run, and the next normal call on the same workspace must be bit
-  identical to a clean run (the context stays usable).
+  identical to a clean run (the context stays usable).  Both prefill paths:
+  the fused cluster kernel and the separate WY + state kernels.
 * The decode slot guard: a declared slot count smaller than the allocated
   cache, so the "bad" index still points inside the allocation; the sequence
   is skipped like PAD and code 2 is recorded.
@@ -60,8 +61,15 @@ def test_error_word_starts_clear_in_a_stale_workspace():
     assert lib.gdn_chunk_check_device_error(ctypes.c_void_p(ws.data_ptr()), _stream()) == _lib.GDN_OK
 
 
+@pytest.fixture(params=["fused", "split"])
+def prefill_path(request, monkeypatch):
+    """The fused cluster kernel (default) or the separate WY + state kernels."""
+    monkeypatch.setenv("GDN_TC_FUSED", "1" if request.param == "fused" else "0")
+    return request.param
+
+
 @pytest.mark.parametrize("stall_chunk", [0, 4])
-def test_state_kernel_wait_timeout_is_reported_and_recovers(stall_chunk):
+def test_state_kernel_wait_timeout_is_reported_and_recovers(stall_chunk, prefill_path):
     lib = _lib.load()
     T, HV = 640, 4  # 10 chunks; the state kernel uses 32-column V-slices here
     q, k, v, g, beta, _ = make_inputs(31, 1, T, 2, HV, 128, 128)
