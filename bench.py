@@ -368,36 +368,32 @@ def run_ours(a):
     ms = _max_over_ranks(ms_local, world)
 
     # ---- N > 1: the same step followed by the final gather of every rank's
-    # outputs and final states onto every rank (NCCL all-gather over NVLink) ----
-    gather = None
+    # outputs and final states onto rank 0 (NCCL gather over NVLink), and,
+    # for callers that need the whole output everywhere, onto every rank ----
+    gather = allgather = None
     if world > 1:
         from domesticated_torch_mlu_ops_b200 import shard
-        plan = shard.OutputGather(wl["parts"], wl["lens"], dev, rank, state_shape=(HV, K, V))
-
-        def step_gather():
-            o_, ht_ = step()
-            return plan(o_, ht_)
-
-        for _ in range(3):
-            step_gather()
-        torch.cuda.synchronize()
-        _barrier(world)
-        gevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                for _ in range(a.steps)]
-        for i in range(a.steps):
-            flush.zero_()
-            gevs[i][0].record(stream)
-            step_gather()
-            gevs[i][1].record(stream)
-        torch.cuda.synchronize()
-        _barrier(world)
-        ms_g = _max_over_ranks(sum(s_.elapsed_time(e_) for s_, e_ in gevs) / a.steps, world)
         tok_all = wl["tokens"] if wl["scaling"] == "strong" else world * B * T
-        gather = {"value": tok_all / (ms_g / 1e3), "unit": "tokens/s", "ms_per_step": ms_g,
-                  "bytes_received_per_rank": plan.gathered_bytes(torch.empty(1, 1, HV, V, dtype=torch.bfloat16)),
-                  "collective": "torch.distributed all_gather_into_tensor (NCCL) of the packed bf16 "
-                                "outputs and fp32 final states, then a row permutation on the device; "
-                                "every rank ends with the whole output"}
+        for dst in (0, None):
+            plan = shard.OutputGather(wl["parts"], wl["lens"], dev, rank, state_shape=(HV, K, V), dst=dst)
+            ms_g = _timed(lambda: plan(*step()), a.steps, flush, stream, world)
+            res = {"value": tok_all / (ms_g / 1e3), "unit": "tokens/s", "ms_per_step": ms_g,
+                   "bytes_received": plan.gathered_bytes(torch.empty(1, 1, HV, V, dtype=torch.bfloat16))}
+            if dst == 0:
+                res["collective"] = ("torch.distributed gather (NCCL) of the packed bf16 outputs and fp32 "
+                                     "final states to rank 0, then a row permutation there")
+                gather = res
+            else:
+                res["collective"] = ("torch.distributed all_gather_into_tensor (NCCL): every rank ends "
+                                     "with the whole output")
+                allgather = res
+
+    # ---- the other ways the prefill shards (BASELINE configs 4 and 1) ----
+    subs = None
+    if a.workload == "cfg1" and not a.tokens and not a.no_subs:
+        subs = {"cfg4": _sub_cfg4(ops, dev, world, rank, a, flush, stream)}
+        if world > 1:
+            subs["cfg1_heads"] = _sub_heads(ops, dev, world, rank, a, flush, stream)
 
     # ---- per-kernel timing with the library's stage events ----
     nst = 8
@@ -511,6 +507,8 @@ def run_ours(a):
                        f"overlap)"},
             "gpu_launches": int(launches),
             "with_gather": gather,
+            "with_allgather": allgather,
+            "sharded": subs,
             "clocks": clk.summary(),
             "decode": dec,
             "conv1d": conv,
@@ -521,6 +519,97 @@ def run_ours(a):
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def _timed(fn, steps, flush, stream, world, warmup=3):
+    """Mean device time (ms) of ``fn`` over ``steps`` calls, L2 flushed
+    before each, barrier + synchronize around the region, max over ranks."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    _barrier(world)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for st, en in evs:
+        flush.zero_()
+        st.record(stream)
+        fn()
+        en.record(stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    return _max_over_ranks(sum(st.elapsed_time(en) for st, en in evs) / steps, world)
+
+
+def _sub_cfg4(ops, dev, world, rank, a, flush, stream):
+    """BASELINE config 4 (64 sequences x 4096 tokens, seed 4) split by
+    sequence, 64/N per rank (strong scaling); with the gather of outputs and
+    final states to rank 0."""
+    import torch
+    from domesticated_torch_mlu_ops_b200 import shard
+    H, HV, K, V = (CFG1[x] for x in ("H", "HV", "K", "V"))
+    if 64 % world:
+        return {"skipped": f"64 sequences do not split over {world} ranks"}
+    b, T = 64 // world, 4096
+    gen = torch.Generator().manual_seed(4 + rank)
+    q = torch.randn(b, T, H, K, generator=gen).bfloat16().to(dev)
+    k = torch.randn(b, T, H, K, generator=gen).bfloat16().to(dev)
+    v = torch.randn(b, T, HV, V, generator=gen).bfloat16().to(dev)
+    g = torch.nn.functional.logsigmoid(torch.randn(b, T, HV, generator=gen)).to(dev)
+    beta = torch.sigmoid(torch.randn(b, T, HV, generator=gen)).to(dev)
+
+    def step():
+        return ops.chunk_gated_delta_rule(q, k, v, g, beta, None, None, True, use_qk_l2norm_in_kernel=True)
+
+    steps = max(3, min(a.steps, 10))
+    ms = _timed(step, steps, flush, stream, world)
+    out = {"workload": "config4: 64 x 4096 tokens, H=16 HV=32 K=V=128 bf16, in-kernel q/k L2 norm",
+           "parallelism": f"sequence-sharded x{world} ({b} sequences per rank)", "scaling": "strong",
+           "value": 64 * T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+           "tokens_per_s_per_gpu": 64 * T / (ms / 1e3) / world}
+    if world > 1:
+        parts = [list(range(r * b, r * b + b)) for r in range(world)]
+        plan = shard.OutputGather(parts, [T] * 64, dev, rank, state_shape=(HV, K, V), dst=0)
+        ms_g = _timed(lambda: plan(*step()), steps, flush, stream, world)
+        out["with_gather"] = {"value": 64 * T / (ms_g / 1e3), "unit": "tokens/s", "ms_per_step": ms_g,
+                              "collective": "NCCL gather of outputs and final states to rank 0",
+                              "bytes_received": plan.gathered_bytes(v)}
+    del q, k, v, g, beta
+    return out
+
+
+def _sub_heads(ops, dev, world, rank, a, flush, stream):
+    """BASELINE config 1's single sequence split by v-head groups (each rank
+    owns H/N q/k heads and their v-heads; shard.partition_heads): strong
+    scaling of one sequence; with the gather of outputs and final states to
+    rank 0."""
+    import torch
+    from domesticated_torch_mlu_ops_b200 import shard
+    B, T, H, HV, K, V = (CFG1[x] for x in ("B", "T", "H", "HV", "K", "V"))
+    if H % world:
+        return {"skipped": f"{H} q/k heads do not split over {world} ranks"}
+    gen = torch.Generator().manual_seed(1)
+    full = (torch.randn(B, T, H, K, generator=gen).bfloat16(), torch.randn(B, T, H, K, generator=gen).bfloat16(),
+            torch.randn(B, T, HV, V, generator=gen).bfloat16(),
+            torch.nn.functional.logsigmoid(torch.randn(B, T, HV, generator=gen)),
+            torch.sigmoid(torch.randn(B, T, HV, generator=gen)))
+    rng_ = shard.partition_heads(H, HV, world)[rank]
+    q, k, v, g, beta, _ = (None if x is None else x.to(dev)
+                           for x in shard.head_slices(*full, None, rng_, HV // H))
+
+    def step():
+        return ops.chunk_gated_delta_rule(q, k, v, g, beta, None, None, True, use_qk_l2norm_in_kernel=True)
+
+    steps = max(3, min(a.steps, 10))
+    ms = _timed(step, steps, flush, stream, world)
+    hg = shard.HeadGather(world, rank, dst=0)
+    ms_g = _timed(lambda: hg(*step()), steps, flush, stream, world)
+    o_, ht_ = step()
+    return {"workload": "config1 (B=1 T=8192 H=16 HV=32 K=V=128 bf16) split by v-head groups",
+            "parallelism": f"head-sharded x{world} ({H // world} q/k heads, {HV // world} v-heads per rank)",
+            "scaling": "strong", "value": B * T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "with_gather": {"value": B * T / (ms_g / 1e3), "unit": "tokens/s", "ms_per_step": ms_g,
+                            "collective": "NCCL gather of the head groups' outputs and final states to rank 0",
+                            "bytes_received": hg.gathered_bytes(o_, ht_)}}
 
 
 def _workload(name, world, rank, cfg):
@@ -794,6 +883,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=0,
                     help="override config 1's T (small cases for ncu captures; not a bench line)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-subs", action="store_true",
+                    help="skip the config-4 and head-split sub-workloads of the config-1 line")
     ap.add_argument("--segment-tokens", dest="segment_tokens", type=int, default=2048,
                     help="tokens per piece of the host-streamed end-to-end leg (multiple of 64)")
     ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg4"],

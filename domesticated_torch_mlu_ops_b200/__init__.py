@@ -12,6 +12,7 @@ from .gdn import (  # noqa: F401
     chunk_gated_delta_rule,
     chunk_gated_delta_rule_bwd,
     chunk_gated_delta_rule_from_host,
+    chunk_gated_delta_rule_fwd_h,
     fused_recurrent_gated_delta_rule,
     fused_recurrent_gated_delta_rule_fn,
     solve_tril,
@@ -24,6 +25,7 @@ __all__ = [
     "chunk_gated_delta_rule",
     "chunk_gated_delta_rule_bwd",
     "chunk_gated_delta_rule_from_host",
+    "chunk_gated_delta_rule_fwd_h",
     "fused_recurrent_gated_delta_rule",
     "fused_recurrent_gated_delta_rule_fn",
     "solve_tril",

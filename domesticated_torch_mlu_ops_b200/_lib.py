@@ -33,6 +33,7 @@ EXPORTED = (
     "gdn_chunk_bwd",
     "gdn_chunk_fwd_host_buffer_size",
     "gdn_chunk_fwd_host",
+    "gdn_chunk_fwd_h",
     "gdn_fused_recurrent_fwd",
     "gdn_recurrent_plain_fwd",
     "gdn_solve_tril",
@@ -74,6 +75,16 @@ class ChunkBwdArgs(ctypes.Structure):
         ("qkv_dtype", _i32), ("cu_dtype", _i32),
         ("scale", ctypes.c_float),
         ("use_qk_l2norm", _i32), ("state_v_first", _i32),
+    ]
+
+
+class ChunkHArgs(ctypes.Structure):
+    _fields_ = [
+        ("k", _vp), ("w", _vp), ("u", _vp), ("g", _vp), ("gk", _vp), ("initial_state", _vp),
+        ("h", _vp), ("v_new", _vp), ("final_state", _vp), ("cu_seqlens", _vp),
+        ("B", _i64), ("T", _i64), ("N", _i64),
+        ("Hg", _i32), ("H", _i32), ("K", _i32), ("V", _i32),
+        ("dtype", _i32), ("cu_dtype", _i32), ("state_v_first", _i32),
     ]
 
 
@@ -173,6 +184,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.gdn_chunk_fwd_host_buffer_size.restype = ctypes.c_size_t
     lib.gdn_chunk_fwd_host.argtypes = [ctypes.POINTER(ChunkArgs), _i64, _vp]
     lib.gdn_chunk_fwd_host.restype = ctypes.c_int
+    lib.gdn_chunk_fwd_h.argtypes = [ctypes.POINTER(ChunkHArgs), _vp]
+    lib.gdn_chunk_fwd_h.restype = ctypes.c_int
     lib.gdn_fused_recurrent_fwd.argtypes = [ctypes.POINTER(RecurrentArgs), _vp]
     lib.gdn_fused_recurrent_fwd.restype = ctypes.c_int
     lib.gdn_recurrent_plain_fwd.argtypes = [ctypes.POINTER(RecurrentPlainArgs), _vp]

@@ -174,6 +174,19 @@ int gdn_chunk_check_device_error(void* workspace, void* stream) {
   return GDN_OK;
 }
 
+int gdn_chunk_fwd_h(const gdn_chunk_h_args* a, void* stream) {
+  if (!a) return fail(GDN_ERR_INVALID, "null args");
+  int rc = check_heads(a->B, a->T, a->N, a->Hg, a->H, a->K, a->V, a->cu_seqlens, a->cu_dtype);
+  if (rc) return rc;
+  if (!qkv_dtype_ok(a->dtype)) return fail(GDN_ERR_INVALID, "dtype must be F32, BF16 or F16");
+  if (a->B * a->T > 0 && (!a->k || !a->w || !a->u))
+    return fail(GDN_ERR_INVALID, "k, w and u must be non-null");
+  if (a->N == 0) return GDN_OK;
+  cudaError_t e = gdn::launch_chunk_h_stage(*a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_chunk_fwd_h");
+  return GDN_OK;
+}
+
 int gdn_fused_recurrent_fwd(const gdn_recurrent_args* a, void* stream) {
   if (!a) return fail(GDN_ERR_INVALID, "null args");
   int rc = check_heads(a->B, a->T, a->N, a->H, a->HV, a->K, a->V, a->cu_seqlens, a->cu_dtype);

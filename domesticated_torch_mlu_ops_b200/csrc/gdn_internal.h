@@ -76,6 +76,7 @@ BwdWorkspace plan_bwd_workspace(const gdn_chunk_bwd_args& a);
 cudaError_t launch_chunk_bwd(const gdn_chunk_bwd_args& a, const BwdWorkspace& ws, cudaStream_t s);
 // stall_chunk >= 0: test hook of gdn_chunk_fwd_test_stall (the first state
 // block skips that chunk's operand fetch; its waits give up after stall_limit).
+cudaError_t launch_chunk_h_stage(const gdn_chunk_h_args& a, cudaStream_t s);
 cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk = -1,
                             long long stall_limit = 0);
 cudaError_t launch_solve_tril(const float* A, void* out, int out_dtype, const void* cu,

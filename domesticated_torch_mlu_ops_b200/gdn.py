@@ -396,6 +396,35 @@ def _(input, output, cu_seqlens):
     return None
 
 
+def _chunk_fwd_h_impl(k: Tensor, w: Tensor, u: Tensor, g: Optional[Tensor], gk: Optional[Tensor],
+                      initial_state: Optional[Tensor], h: Optional[Tensor], v_new: Optional[Tensor],
+                      final_state: Optional[Tensor], cu_seqlens: Optional[Tensor], state_v_first: bool) -> None:
+    """The state-recurrence stage on prepared inputs (k, w, u contiguous in
+    one dtype; g, gk, initial_state fp32 contiguous); writes h, v_new and
+    final_state (each optional) in place."""
+    B, T, Hg, K = k.shape
+    H, V = u.shape[2], u.shape[3]
+    N = B if cu_seqlens is None else cu_seqlens.numel() - 1
+    args = _lib.ChunkHArgs(
+        k=_ptr(k), w=_ptr(w), u=_ptr(u), g=_ptr(g), gk=_ptr(gk), initial_state=_ptr(initial_state),
+        h=_ptr(h), v_new=_ptr(v_new), final_state=_ptr(final_state), cu_seqlens=_ptr(cu_seqlens),
+        B=B, T=T, N=N, Hg=Hg, H=H, K=K, V=V, dtype=_DT[k.dtype],
+        cu_dtype=_IDT[cu_seqlens.dtype] if cu_seqlens is not None else _lib.GDN_I64,
+        state_v_first=int(state_v_first))
+    dev = k.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().gdn_chunk_fwd_h(ctypes.byref(args), _stream(dev)))
+
+
+_chunk_fwd_h_op = torch.library.custom_op("gdn_b200::chunk_fwd_h", mutates_args=("h", "v_new", "final_state"),
+                                          device_types="cuda")(_chunk_fwd_h_impl)
+
+
+@_chunk_fwd_h_op.register_fake
+def _(k, w, u, g, gk, initial_state, h, v_new, final_state, cu_seqlens, state_v_first):
+    return None
+
+
 # ---------------------------------------------------------------------------
 # chunked prefill
 # ---------------------------------------------------------------------------
@@ -610,6 +639,77 @@ def chunk_gated_delta_rule_bwd(q, k, v, g, beta, scale, initial_state, dout, dht
         torch.ops.gdn_b200.chunk_bwd, _chunk_bwd_impl, q, k, v, _f32(g), _f32(beta), _scale(scale), h0, cu,
         dout.to(q.dtype).contiguous(), None if dht is None else _f32(dht), bool(state_v_first), bool(use_qk_l2norm_in_kernel))
     return dq, dk, dv, db, dg, (dh0 if h0 is not None else None)
+
+
+def chunk_gated_delta_rule_fwd_h(
+    k: torch.Tensor,
+    w: torch.Tensor,
+    u: torch.Tensor,
+    g: torch.Tensor | None = None,
+    gk: torch.Tensor | None = None,
+    initial_state: torch.Tensor | None = None,
+    output_final_state: bool = False,
+    chunk_size: int = 64,
+    save_new_value: bool = True,
+    state_v_first: bool = False,
+    cu_seqlens: torch.LongTensor | None = None,
+    chunk_indices: torch.Tensor | None = None,
+    chunk_offsets: torch.Tensor | None = None,
+    allow_tf32: bool = True,
+):
+    """The inter-chunk state recurrence stage (``triton/fla/chunk_delta_h.py:200-271``),
+    with the per-key decay ``gk`` of its KDA branch (``USE_GK``, ``:155-171``).
+
+    k ``[B, T, Hg, K]``; w ``[B, T, H, K]``; u ``[B, T, H, V]`` (one dtype);
+    g the chunk-local cumsum of the log decay in the reference's head-major
+    layout ``[H, B, T]`` (``chunk.py:32``) or None; gk the per-key cumsum
+    ``[B, T, H, K]`` or None.  Returns ``(h, v_new, final_state)``: the state
+    before each chunk ``[B, NT, H, K, V]`` (``[.., V, K]`` with
+    ``state_v_first``) in k's dtype, ``v_new = u - w h`` like u (or None
+    without ``save_new_value``) and the fp32 final state (or None).  Chunks
+    are 64 tokens; ``chunk_indices`` / ``chunk_offsets`` / ``allow_tf32`` are
+    accepted for signature compatibility (products are full fp32).  With
+    ``cu_seqlens`` the chunk count is read on the host, as the reference's
+    ``prepare_chunk_indices`` does.
+    """
+    del chunk_offsets, allow_tf32
+    if chunk_size != 64:
+        raise ValueError(f"chunk_size={chunk_size}: the kernels use 64-token chunks")
+    _cuda("chunk_gated_delta_rule_fwd_h", k, w, u, g, gk, initial_state, cu_seqlens)
+    if k.dim() != 4 or w.dim() != 4 or u.dim() != 4 or w.shape[:3] != u.shape[:3] or k.shape[:2] != w.shape[:2]:
+        raise ValueError("k must be [B, T, Hg, K], w [B, T, H, K] and u [B, T, H, V]")
+    B, T, Hg, K = k.shape
+    H, V = u.shape[2], u.shape[3]
+    if w.shape[3] != K or H % Hg or K > 128 or V > 128:
+        raise ValueError(f"bad head layout or sizes (Hg={Hg}, H={H}, K={K}, V={V}; K, V <= 128)")
+    if not (k.dtype == w.dtype == u.dtype) or k.dtype not in _DT:
+        raise ValueError("k, w and u must share one dtype (float32, bfloat16 or float16)")
+    if cu_seqlens is not None and B != 1:
+        raise ValueError("cu_seqlens requires batch size 1 (packed sequences)")
+    if g is not None and g.numel() != H * B * T:
+        raise ValueError(f"g must hold [H, B, T] = {(H, B, T)} values (head-major)")
+    if gk is not None and tuple(gk.shape) != (B, T, H, K):
+        raise ValueError(f"gk must be [B, T, H, K] = {(B, T, H, K)}")
+    cu, _ = _idx(cu_seqlens)
+    if cu is None:
+        N, NT = B, (T + 63) // 64
+    else:
+        N = cu.numel() - 1
+        if chunk_indices is not None:
+            NT = int(chunk_indices.shape[0])
+        else:
+            lens = (cu[1:] - cu[:-1]).tolist()
+            NT = sum((x + 63) // 64 for x in lens)
+    shape_state = (N, H, V, K) if state_v_first else (N, H, K, V)
+    if initial_state is not None and tuple(initial_state.shape) != shape_state:
+        raise ValueError(f"initial_state must be {shape_state}, got {tuple(initial_state.shape)}")
+    h = k.new_empty((B, NT, H, V, K) if state_v_first else (B, NT, H, K, V))
+    v_new = torch.empty_like(u) if save_new_value else None
+    ht = torch.empty(shape_state, dtype=torch.float32, device=k.device) if output_final_state else None
+    _call(torch.ops.gdn_b200.chunk_fwd_h, _chunk_fwd_h_impl, k.contiguous(), w.contiguous(), u.contiguous(),
+          None if g is None else g.to(torch.float32).contiguous(), _f32(gk), _f32(initial_state), h, v_new, ht,
+          cu, bool(state_v_first))
+    return h, v_new, ht
 
 
 # ---------------------------------------------------------------------------

@@ -11,9 +11,10 @@ so work splits across ranks with no collective on the data path:
 
 :func:`gather_outputs` is the optional final gather through host memory
 (``all_gather_object``), and :class:`OutputGather` the same gather kept on the
-device: one ``all_gather_into_tensor`` of the packed outputs and one of the
-final states (NCCL over NVLink on GPUs, gloo on CPU), then a row permutation
-back into sequence order, when every rank needs every output.
+device: one ``gather`` to a chosen rank (or ``all_gather_into_tensor`` onto
+every rank) of the packed outputs and one of the final states (NCCL over
+NVLink on GPUs, gloo on CPU), then a row permutation back into sequence
+order.  :class:`HeadGather` reassembles a sequence split by v-head groups.
 """
 
 from __future__ import annotations
@@ -52,6 +53,16 @@ def partition_heads(H: int, HV: int, world_size: int) -> list[tuple[int, int]]:
         out.append((s, s + n))
         s += n
     return out
+
+
+def head_slices(q, k, v, g, beta, initial_state, head_range, G: int):
+    """This rank's tensors for q/k heads ``[h0, h1)`` and their v-heads
+    ``[h0 * G, h1 * G)`` (states ``[N, HV, ...]`` sliced on dim 1)."""
+    h0, h1 = head_range
+    sl = slice(h0 * G, h1 * G)
+    return (q[:, :, h0:h1].contiguous(), k[:, :, h0:h1].contiguous(), v[:, :, sl].contiguous(),
+            g[:, :, sl].contiguous(), beta[:, :, sl].contiguous(),
+            None if initial_state is None else initial_state[:, sl].contiguous())
 
 
 def pack_sequences(xs, seq_ids, cu_seqlens):
@@ -107,6 +118,19 @@ def gather_outputs(ids, o, ht, cu_seqlens, world_size: int):
     return full_o, full_h
 
 
+def _gather_rows(send, world: int, dst: int, rank: int, group=None):
+    """``[world * rows, ...]`` on rank ``dst`` (None elsewhere) from every
+    rank's ``[rows, ...]`` tensor."""
+    import torch.distributed as dist
+
+    if rank != dst:
+        dist.gather(send, None, dst=dst, group=group)
+        return None
+    out = send.new_empty((world * send.shape[0],) + tuple(send.shape[1:]))
+    dist.gather(send, list(out.chunk(world)), dst=dst, group=group)
+    return out
+
+
 def _all_gather_rows(send, world: int, group=None):
     """``[world * rows, ...]`` from every rank's ``[rows, ...]`` tensor."""
     import torch.distributed as dist
@@ -120,7 +144,7 @@ def _all_gather_rows(send, world: int, group=None):
 
 
 class OutputGather:
-    """Device-side gather of sharded prefill outputs onto every rank.
+    """Device-side gather of sharded prefill outputs onto one rank or every rank.
 
     ``parts[r]`` lists the sequences rank ``r`` computed, in the order its
     packed output holds them (:func:`partition_sequences` or a contiguous
@@ -132,10 +156,14 @@ class OutputGather:
     ``cu_seqlens``) and ``final_state [N, *state_shape]`` (or None).  Every
     rank takes the same collectives: a rank without sequences passes an empty
     output and ``ht=None``.  When the shards are already contiguous and
-    equal, the permutation is skipped.
+    equal, the permutation is skipped.  With ``dst`` set, only that rank
+    receives (``gather`` instead of ``all_gather``: the other ranks only send
+    their shard and get ``(None, None)``); ``dst=None`` gives every rank the
+    whole output.
     """
 
-    def __init__(self, parts, lengths, device, rank: int, state_shape=None, group=None):
+    def __init__(self, parts, lengths, device, rank: int, state_shape=None, group=None, dst=None):
+        self.dst = dst
         self.parts = [list(p) for p in parts]
         self.lengths = [int(x) for x in lengths]
         self.world = len(self.parts)
@@ -163,12 +191,17 @@ class OutputGather:
         self.seq_perm = None if ident else torch.tensor(seq_src, dtype=torch.int64, device=device)
 
     def gathered_bytes(self, o) -> int:
-        """Bytes each rank receives per call (padding included) for outputs
-        shaped like ``o``."""
+        """Bytes the receiving rank (each rank, without ``dst``) gets per call
+        (padding included) for outputs shaped like ``o``."""
         n = self.world * self.rows * math.prod(o.shape[2:]) * o.element_size()
         if self.state_shape is not None:
             n += self.world * self.nseq * math.prod(self.state_shape) * 4
         return n
+
+    def _collect(self, send):
+        if self.dst is None:
+            return _all_gather_rows(send, self.world, self.group)
+        return _gather_rows(send, self.world, self.dst, self.rank, self.group)
 
     def __call__(self, o, ht=None):
         rows = o.reshape((o.shape[0] * o.shape[1],) + tuple(o.shape[2:]))
@@ -178,19 +211,63 @@ class OutputGather:
         if rows.shape[0] < self.rows:
             pad = rows.new_zeros((self.rows - rows.shape[0],) + tuple(rows.shape[1:]))
             rows = torch.cat([rows, pad])
-        full = _all_gather_rows(rows.contiguous(), self.world, self.group)
+        full = self._collect(rows.contiguous())
+        st = None
+        if self.state_shape is not None:
+            st = ht if ht is not None else o.new_zeros((0,) + self.state_shape, dtype=torch.float32)
+            if tuple(st.shape[1:]) != self.state_shape:
+                raise ValueError(f"final states {tuple(st.shape)} do not match the plan's {self.state_shape}")
+            if st.shape[0] < self.nseq:
+                st = torch.cat([st, st.new_zeros((self.nseq - st.shape[0],) + tuple(st.shape[1:]))])
+            st = self._collect(st.contiguous())
+        if full is None:  # not the receiving rank
+            return None, None
         if self.row_perm is not None:
             full = full.index_select(0, self.row_perm)
         else:
             full = full[:self.total]
         full_o = full.unsqueeze(0)
-        if self.state_shape is None:
+        if st is None:
             return full_o, None
-        st = ht if ht is not None else o.new_zeros((0,) + self.state_shape, dtype=torch.float32)
-        if tuple(st.shape[1:]) != self.state_shape:
-            raise ValueError(f"final states {tuple(st.shape)} do not match the plan's {self.state_shape}")
-        if st.shape[0] < self.nseq:
-            st = torch.cat([st, st.new_zeros((self.nseq - st.shape[0],) + tuple(st.shape[1:]))])
-        fh = _all_gather_rows(st.contiguous(), self.world, self.group)
-        fh = fh.index_select(0, self.seq_perm) if self.seq_perm is not None else fh[:len(self.lengths)]
+        fh = st.index_select(0, self.seq_perm) if self.seq_perm is not None else st[:len(self.lengths)]
         return full_o, fh
+
+
+class HeadGather:
+    """Gather of a single-sequence prefill split by v-head groups
+    (:func:`partition_heads` with equal groups): every rank holds
+    ``o [B, T, HV / world, V]`` and ``final_state [N, HV / world, ...]``;
+    rank ``dst`` receives ``o [B, T, HV, V]`` and ``final_state [N, HV, ...]``
+    (one ``gather`` of each, then a transpose of the rank axis into the head
+    axis on the device); ``dst=None`` gives every rank the result."""
+
+    def __init__(self, world: int, rank: int, group=None, dst=0):
+        self.world, self.rank, self.group, self.dst = world, rank, group, dst
+
+    def _collect(self, x):
+        x = x.contiguous()
+        rows = x.reshape((1,) + tuple(x.shape))
+        if self.dst is None:
+            full = _all_gather_rows(rows, self.world, self.group)
+        else:
+            full = _gather_rows(rows, self.world, self.dst, self.rank, self.group)
+        return full
+
+    def __call__(self, o, ht=None):
+        fo = self._collect(o)              # [world, B, T, HVr, V]
+        fh = None if ht is None else self._collect(ht)  # [world, N, HVr, ...]
+        if fo is None:
+            return None, None
+        w, B, T, HVr, V = fo.shape
+        full_o = fo.permute(1, 2, 0, 3, 4).reshape(B, T, w * HVr, V)
+        full_h = None
+        if fh is not None:
+            N = fh.shape[1]
+            full_h = fh.transpose(0, 1).reshape((N, w * fh.shape[2]) + tuple(fh.shape[3:]))
+        return full_o, full_h
+
+    def gathered_bytes(self, o, ht=None) -> int:
+        n = self.world * o.numel() * o.element_size()
+        if ht is not None:
+            n += self.world * ht.numel() * ht.element_size()
+        return n

@@ -20,6 +20,8 @@
  *   gdn_chunk_fwd_host     <- no reference counterpart (host-memory prefill, pipelined copies)
  *   gdn_fused_recurrent_fwd<- triton_ops.py:228-285 fused_recurrent_gated_delta_rule_fn
  *                             -> triton/fla/fused_recurrent_fn.py:161-233
+ *   gdn_chunk_fwd_h        <- triton/fla/chunk_delta_h.py:200-271 chunk_gated_delta_rule_fwd_h
+ *                             (the state-recurrence stage, with its USE_GK branch)
  *   gdn_recurrent_plain_fwd<- triton_ops.py:168-226 fused_recurrent_gated_delta_rule
  *                             -> triton/fla/fused_recurrent.py:134-187
  *   gdn_solve_tril         <- include/torch_mlu_ops.h:1052-1054 tmo::torch_api::solve_tril
@@ -226,6 +228,45 @@ GDN_API int gdn_chunk_fwd_host(const gdn_chunk_args* args, int64_t segment_token
  * mbarrier wait that timed out) records code 1, the site, the block and the
  * thread, and leaves its outputs incomplete. */
 GDN_API int gdn_chunk_check_device_error(void* workspace, void* stream);
+
+/*
+ * The inter-chunk state recurrence as a stage (chunk_gated_delta_rule_fwd_h,
+ * triton/fla/chunk_delta_h.py:200-271), with the per-key decay gk of its
+ * KDA branch (USE_GK, :155-171).  64-token chunks.  Shapes (C-contiguous,
+ * k, w, u, h, v_new of `dtype` F32/BF16/F16):
+ *   k [B, T, Hg, K]; w [B, T, H, K]; u [B, T, H, V]  (head h reads k head
+ *   h / (H / Hg));
+ *   g: chunk-local cumsum of the log decay in the reference's head-major
+ *   layout [H, B*T] f32, or NULL; gk: per-key cumsum [B, T, H, K] f32 or NULL;
+ *   initial_state / final_state f32 [N, H, K, V] ([N, H, V, K] with
+ *   state_v_first), either NULL;
+ *   h: the state before every chunk, [B, NT, H, K, V] ([.., V, K] with
+ *   state_v_first), NT = chunks per sequence (or the packed batch's total
+ *   chunk count with cu_seqlens), or NULL;
+ *   v_new [B, T, H, V] = u - w S per chunk, or NULL;
+ *   cu_seqlens [N+1] (cu_dtype) or NULL as for gdn_chunk_fwd.
+ * Per chunk: S <- S exp(g_last) exp(gk_last)[:, None] + k^T (v_new *
+ * exp(g_last - g)), the products in fp32 with S and v_new~ rounded to
+ * `dtype` where the reference rounds them.  K, V <= 128.
+ */
+typedef struct gdn_chunk_h_args {
+  const void* k;
+  const void* w;
+  const void* u;
+  const float* g;
+  const float* gk;
+  const float* initial_state;
+  void* h;
+  void* v_new;
+  float* final_state;
+  const void* cu_seqlens;
+  int64_t B, T, N;
+  int32_t Hg, H, K, V;
+  int32_t dtype, cu_dtype;
+  int32_t state_v_first;
+} gdn_chunk_h_args;
+
+GDN_API int gdn_chunk_fwd_h(const gdn_chunk_h_args* args, void* stream);
 
 /*
  * Recurrent forward with a V-first state cache: the slot-indexed decode of

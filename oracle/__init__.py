@@ -21,6 +21,7 @@ from .gdn_oracle import (  # noqa: F401
     solve_tril,
     recompute_w_u,
     chunk_fwd_h,
+    chunk_fwd_h_stage,
     chunk_fwd_o,
     chunk_gated_delta_rule,
     seq_bounds,

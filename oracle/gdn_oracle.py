@@ -361,3 +361,61 @@ def chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None,
     if return_stages:
         return o, ht, dict(gc=gc, A=A, Ai=Ai, w=w, u=u, hs=hs, v_new=v_new)
     return o, ht
+
+
+def chunk_fwd_h_stage(k, w, u, g=None, gk=None, initial_state=None, output_final_state=False,
+                      state_v_first=False, cu_seqlens=None, bt=BT, dtype=np.float64):
+    """The state-recurrence stage with the reference's own layouts, including
+    its per-key decay branch: ``chunk_gated_delta_rule_fwd_h``
+    (``triton/fla/chunk_delta_h.py:200-271``, kernel ``:28-197``).
+
+    k ``[B, T, Hg, K]``, w ``[B, T, H, K]``, u ``[B, T, H, V]``; g the
+    chunk-local cumsum in head-major ``[H, B*T]`` layout (``:133-134``) or
+    None; gk the per-key cumsum ``[B, T, H, K]`` (``:155-171``) or None.
+    Per chunk: h = S (``:107-116``), v_new = u - w S (``:118-130``),
+    S <- S exp(g_last) exp(gk_last)[:, None] + k^T (v_new exp(g_last - g))
+    (``:131-190``; K-first S).  Returns (h ``[B, NT, H, K, V]`` or V-first,
+    v_new, final_state or None).
+    """
+    B, T, Hg, K = k.shape
+    H, V = u.shape[2], u.shape[3]
+    G = H // Hg
+    kf, wf, uf = (_flat(x).astype(dtype) for x in (k, w, u))
+    gf = None if g is None else np.asarray(g, dtype=dtype).reshape(H, B * T)
+    gkf = None if gk is None else _flat(gk).astype(dtype)
+    bounds = seq_bounds(B, T, cu_seqlens)
+    nts = [(e - s + bt - 1) // bt for s, e in bounds]
+    NT = sum(nts) if cu_seqlens is not None else (T + bt - 1) // bt
+    hs = np.zeros((B * NT if cu_seqlens is None else NT, H, K, V), dtype=dtype)
+    v_new = np.zeros(uf.shape, dtype=dtype)
+    ht = np.zeros((len(bounds), H, K, V), dtype=dtype) if output_final_state else None
+    boh = 0
+    for n, (bos, eos) in enumerate(bounds):
+        S = np.zeros((H, K, V), dtype=dtype)
+        if initial_state is not None:
+            h0 = np.asarray(initial_state[n], dtype=dtype)
+            S += h0.transpose(0, 2, 1) if state_v_first else h0
+        base = boh if cu_seqlens is not None else n * NT
+        for c, (s, e) in enumerate(_chunks(bos, eos, bt)):
+            hs[base + c] = S
+            wc = wf[s:e].transpose(1, 0, 2)                       # [H, L, K]
+            vn = uf[s:e].transpose(1, 0, 2) - wc @ S              # [H, L, V]
+            v_new[s:e] = vn.transpose(1, 0, 2)
+            dec = np.ones((H, K, 1), dtype=dtype)
+            if gf is not None:
+                glast = gf[:, e - 1]
+                vn = vn * np.exp(glast[:, None] - gf[:, s:e])[:, :, None]
+                dec = dec * np.exp(glast)[:, None, None]
+            if gkf is not None:
+                dec = dec * np.exp(gkf[e - 1])[:, :, None]          # [H, K, 1]
+            kc = kf[s:e][:, np.arange(H) // G].transpose(1, 2, 0)  # [H, K, L]
+            S = S * dec + kc @ vn
+        boh += nts[n]
+        if output_final_state:
+            ht[n] = S
+    h = hs.reshape((B, NT, H, K, V) if cu_seqlens is None else (1, NT, H, K, V))
+    if state_v_first:
+        h = h.transpose(0, 1, 2, 4, 3).copy()
+        if ht is not None:
+            ht = ht.transpose(0, 1, 3, 2).copy()
+    return h, v_new.reshape(u.shape), ht

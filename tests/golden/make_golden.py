@@ -205,6 +205,51 @@ def gen_recurrent(ref: str):
         print("wrote", name)
 
 
+def gen_chunk_h(ref: str):
+    """The state-recurrence stage ``chunk_gated_delta_rule_fwd_h``
+    (``chunk_delta_h.py:200-271``) with the per-key decay gk of its USE_GK
+    branch (``:155-171``), called directly (the chunk facade never passes gk).
+    The kernel's gk load covers 64 keys, so K <= 64 here; the K-first form
+    needs g as well (without it the branch names a block only the g branch
+    defines), so gk alone is taken with the V-first state."""
+    _load_chunk_modules(ref)
+    mod = sys.modules["torch_mlu_ops.triton.fla.chunk_delta_h"]
+    # (name, T, Hg, H, K, V, use_g, state_v_first, varlen)
+    cases = [("h_g_gk", 150, 2, 4, 32, 16, True, False, False),
+             ("h_gk_vfirst", 130, 1, 2, 64, 32, False, True, False),
+             ("h_g_gk_varlen_vfirst", 200, 2, 2, 32, 16, True, True, True)]
+    for (name, T, Hg, H, K, V, use_g, vfirst, varlen) in cases:
+        gen = torch.Generator().manual_seed(zlib.crc32(name.encode()) % 1000 + 21)
+        k = torch.nn.functional.normalize(torch.randn(1, T, Hg, K, generator=gen), dim=-1)
+        w = torch.randn(1, T, H, K, generator=gen) * 0.3
+        u = torch.randn(1, T, H, V, generator=gen)
+        cu = torch.tensor([0, 64, 90, T], dtype=torch.int64) if varlen else None
+        bounds = [(0, T)] if cu is None else [(int(cu[i]), int(cu[i + 1])) for i in range(len(cu) - 1)]
+
+        def chunk_cumsum(x):  # chunk-local cumsum along T (dim 1) of every sequence
+            out = torch.zeros_like(x)
+            for bos, eos in bounds:
+                for s0 in range(bos, eos, 64):
+                    e0 = min(s0 + 64, eos)
+                    out[:, s0:e0] = torch.cumsum(x[:, s0:e0], dim=1)
+            return out
+
+        g = chunk_cumsum(torch.nn.functional.logsigmoid(torch.randn(1, T, H, generator=gen)))
+        gk = chunk_cumsum(torch.nn.functional.logsigmoid(torch.randn(1, T, H, K, generator=gen)) * 0.2)
+        g_hm = g.permute(2, 0, 1).contiguous() if use_g else None  # head-major, as chunk.py:32 passes it
+        N = len(bounds)
+        h0 = torch.randn((N, H, V, K) if vfirst else (N, H, K, V), generator=gen) * 0.3
+        h, v_new, ht = mod.chunk_gated_delta_rule_fwd_h(
+            k=k, w=w, u=u, g=g_hm, gk=gk, initial_state=h0, output_final_state=True,
+            state_v_first=vfirst, cu_seqlens=cu, allow_tf32=False)
+        np.savez_compressed(
+            os.path.join(HERE, f"chh_{name}.npz"),
+            k=_np(k), w=_np(w), u=_np(u), g=_np(g_hm) if use_g else np.zeros(0, np.float32), gk=_np(gk),
+            h0=_np(h0), cu_seqlens=(cu.numpy() if cu is not None else np.zeros(0, np.int64)),
+            state_v_first=np.bool_(vfirst), h=_np(h), v_new=_np(v_new), final_state=_np(ht))
+        print("wrote", name)
+
+
 def _load_chunk_modules(ref: str):
     """Load the chunk-path kernels.  Two substitutions are needed to run them
     on upstream Triton: the Cambricon-only integer row indexing of a register
@@ -542,6 +587,8 @@ def main():
         gen_recurrent(a.ref)
     if a.only in ("", "chunk"):
         gen_chunk(a.ref)
+    if a.only in ("", "chunk_h"):
+        gen_chunk_h(a.ref)
     if a.only in ("", "conv"):
         gen_conv(a.ref)
     if a.only in ("", "bwd"):

@@ -40,6 +40,7 @@ def test_library_exports_every_declared_symbol():
 @pytest.mark.parametrize("struct,cname", [(_lib.ChunkArgs, "gdn_chunk_args"),
                                           (_lib.ChunkBwdArgs, "gdn_chunk_bwd_args"),
                                           (_lib.RecurrentArgs, "gdn_recurrent_args"),
+                                          (_lib.ChunkHArgs, "gdn_chunk_h_args"),
                                           (_lib.RecurrentPlainArgs, "gdn_recurrent_plain_args"),
                                           (_lib.Conv1dArgs, "gdn_conv1d_args"),
                                           (_lib.Conv1dFnArgs, "gdn_conv1d_fn_args"),

@@ -61,6 +61,18 @@ def test_decode_and_misc_fake_shapes():
         assert out.shape == A.shape and out.dtype == torch.bfloat16
 
 
+def test_state_stage_fake_shapes():
+    assert "Tensor(a6!)? h" in str(torch.ops.gdn_b200.chunk_fwd_h.default._schema)
+    with FakeTensorMode():
+        k = torch.empty(1, 130, 2, 64, dtype=torch.bfloat16, device="cuda")
+        w = torch.empty(1, 130, 4, 64, dtype=torch.bfloat16, device="cuda")
+        u = torch.empty(1, 130, 4, 32, dtype=torch.bfloat16, device="cuda")
+        gk = torch.empty(1, 130, 4, 64, device="cuda")
+        h, v_new, ht = ops.chunk_gated_delta_rule_fwd_h(k, w, u, None, gk, None, True, state_v_first=True)
+        assert h.shape == (1, 3, 4, 32, 64) and h.dtype == torch.bfloat16
+        assert v_new.shape == u.shape and ht.shape == (1, 4, 32, 64) and ht.dtype == torch.float32
+
+
 def test_ops_reject_cpu_tensors():
     q = torch.zeros(1, 4, 2, 16)
     with pytest.raises(ValueError, match="CUDA"):

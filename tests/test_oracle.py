@@ -96,3 +96,17 @@ def test_chunk_form_equals_recurrence(varlen):
                                            use_qk_l2norm_in_kernel=True)
     assert np.abs(o1 - o2).max() < 1e-10
     assert np.abs(h1 - h2).max() < 1e-10
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "chh_*.npz"))),
+                         ids=os.path.basename)
+def test_oracle_matches_reference_state_stage(path):
+    """chunk_gated_delta_rule_fwd_h with per-key decays (USE_GK), from the
+    reference's own kernel: states before every chunk, v_new, final state."""
+    d = dict(np.load(path))
+    cu = d["cu_seqlens"] if d["cu_seqlens"].size else None
+    h, v_new, ht = oracle.chunk_fwd_h_stage(
+        d["k"], d["w"], d["u"], d["g"] if d["g"].size else None, d["gk"], d["h0"], True,
+        bool(d["state_v_first"]), cu)
+    for got, ref in ((h, d["h"]), (v_new, d["v_new"]), (ht, d["final_state"])):
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)

@@ -97,15 +97,20 @@ def _gather_worker(rank, world, port, full_o, full_h, out_path):
         got.append(plan(o, full_h[p] if p else None))
         rows = max(sum(lens[i] for i in q) for q in parts)
         assert plan.gathered_bytes(o) == world * rows * 3 * 7 * 8 + world * max(map(len, parts)) * 60 * 4
+        to1 = shard.OutputGather(parts, lens, "cpu", rank, state_shape=(3, 4, 5), dst=1)
+        r1 = to1(o, full_h[p] if p else None)
+        got.append(r1 if rank == 1 else (full_o, full_h))  # rank 0 receives nothing
+        assert rank == 1 or r1 == (None, None)
     torch.save(got, f"{out_path}.{rank}")
     dist.barrier()
     dist.destroy_process_group()
 
 
 def test_device_gather_two_gloo_ranks(tmp_path):
-    """OutputGather on two gloo ranks: padded all-gather, then the row and
-    state permutation back into sequence order, identical on both ranks, for
-    uneven shards, contiguous shards and a rank with no sequences."""
+    """OutputGather on two gloo ranks: padded all-gather (and gather to rank
+    1), then the row and state permutation back into sequence order,
+    identical on both ranks, for uneven shards, contiguous shards and a rank
+    with no sequences."""
     rng = np.random.default_rng(11)
     full_o = torch.from_numpy(rng.standard_normal((1, sum(_GATHER_LENS), 3, 7)))
     full_h = torch.from_numpy(rng.standard_normal((len(_GATHER_LENS), 3, 4, 5))).float()
@@ -116,3 +121,40 @@ def test_device_gather_two_gloo_ranks(tmp_path):
         for o, h in torch.load(f"{out}.{r}"):
             assert torch.equal(o, full_o)
             assert torch.equal(h, full_h)
+
+
+def _head_worker(rank, world, port, inputs, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    q, k, v, g, beta, h0 = inputs
+    H, HV = q.shape[2], v.shape[2]
+    rng_ = shard.partition_heads(H, HV, world)[rank]
+    ql, kl, vl, gl, bl, hl = shard.head_slices(q, k, v, g, beta, h0, rng_, HV // H)
+    o, ht = _oracle_op(ql, kl, vl, gl, bl, initial_state=hl)
+    full_o, full_h = shard.HeadGather(world, rank, dst=0)(o, ht)
+    if rank == 0:
+        torch.save({"o": full_o, "h": full_h}, out_path)
+    else:
+        assert full_o is None and full_h is None
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_head_split_prefill_two_gloo_ranks(tmp_path):
+    """One sequence split by v-head groups (each rank owns whole q/k heads),
+    run by the oracle on two gloo ranks and gathered on rank 0, equals the
+    unsplit sequence."""
+    rng = np.random.default_rng(12)
+    T, H, HV, K, V = 150, 4, 8, 16, 8
+    t = lambda *s: torch.from_numpy(rng.standard_normal(s))
+    q, k, v = t(1, T, H, K), t(1, T, H, K), t(1, T, HV, V)
+    g = torch.nn.functional.logsigmoid(t(1, T, HV))
+    beta = torch.sigmoid(t(1, T, HV))
+    h0 = t(1, HV, K, V) * 0.1
+    out = tmp_path / "heads.pt"
+    mp.start_processes(_head_worker, args=(2, _free_port(), (q, k, v, g, beta, h0), str(out)),
+                       nprocs=2, join=True, start_method="spawn")
+    got = torch.load(out)
+    ref_o, ref_h = _oracle_op(q, k, v, g, beta, initial_state=h0)
+    assert torch.allclose(got["o"], ref_o, atol=1e-10)
+    assert torch.allclose(got["h"], ref_h, atol=1e-10)
