@@ -537,6 +537,15 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
       }
       a_prev = sc[row - 64];
     } else {  // E1 (rows 0..63): v = U - X, V~ = diag(b) v
+      // U and b have been in the stage since its loads completed: read them
+      // while MMA1 runs
+      const int i = row;
+      const float bi = sc[64 + i];
+      const T* ut = reinterpret_cast<const T*>(b + S::kU);
+      uint4 uraw[CW / 8];
+#pragma unroll
+      for (int j8 = 0; j8 < CW / 8; ++j8)
+        uraw[j8] = *reinterpret_cast<const uint4*>(ut + u_off(i, colh * CW + j8 * 8, VS));
       mine = umma::mbar_wait(bar_mma1, static_cast<uint32_t>(c & 1), wlim);
       if (!mine) record_error(w.err, 1, kSiteStMma1);
       umma::fence_after_sync();
@@ -546,14 +555,11 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
       umma::tmem_wait_ld();
 #pragma unroll
       for (int q = 0; q < CW / 16; ++q) umma::reg_fence16(rx + q * 16);
-      const int i = row;
-      const float bi = sc[64 + i];
-      const T* ut = reinterpret_cast<const T*>(b + S::kU);
 #pragma unroll
       for (int j8 = 0; j8 < CW / 8; ++j8) {
         const int col = colh * CW + j8 * 8;
         float u8[8], vn[8], vt[8];
-        unpack8<T>(*reinterpret_cast<const uint4*>(ut + u_off(i, col, VS)), u8);
+        unpack8<T>(uraw[j8], u8);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           vn[e] = u8[e] - __uint_as_float(rx[j8 * 8 + e]);
