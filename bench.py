@@ -765,6 +765,27 @@ def _conv_bench(ops, dev, a, hbm, flush):
         return sum(st.elapsed_time(en) for st, en in ev) / reps * 1e3
 
     us_fn = timed(lambda: ops.causal_conv1d_fn(x.t(), w, b, cs, qsl, ci, hi, "silu"), max(a.steps, 10))
+    # the conv and the chunked prefill of one GDN layer (config 1), as two ops
+    # (the prefill reads q/k/v in place from the conv output) and fused
+    H, HV = CFG1["H"], CFG1["HV"]
+    g = torch.nn.functional.logsigmoid(torch.randn(1, T, HV, generator=gen)).to(dev)
+    beta = torch.sigmoid(torch.randn(1, T, HV, generator=gen)).to(dev)
+    h0 = (torch.randn(1, HV, 128, 128, generator=gen) * 0.02).to(dev)
+
+    def two_ops():
+        yt = ops.causal_conv1d_fn(x.t(), w, b, cs, qsl, ci, hi, "silu").t()
+        q = yt[:, :H * 128].view(1, T, H, 128)
+        k = yt[:, H * 128:2 * H * 128].view(1, T, H, 128)
+        v = yt[:, 2 * H * 128:].view(1, T, HV, 128)
+        return ops.chunk_gated_delta_rule(q, k, v, g, beta, None, h0, True, cu_seqlens=qsl,
+                                          use_qk_l2norm_in_kernel=True)
+
+    def fused():
+        return ops.causal_conv1d_chunk_gated_delta_rule(x.t(), w, b, cs, qsl, g, beta, H, HV, initial_state=h0,
+                                                        output_final_state=True, cache_indices=ci,
+                                                        has_initial_state=hi, use_qk_l2norm_in_kernel=True)
+    us_two = timed(two_ops, max(a.steps, 10))
+    us_fused = timed(fused, max(a.steps, 10))
     us_up = timed(lambda: ops.causal_conv1d_update(xu, cache, None, w, b, "silu"), max(a.steps, 10))
     b_fn = 2 * T * D * 2 + D * W * 2 + D * 2 + 2 * D * (W - 1) * 2
     b_up = N * D * (2 + 2 * W * 2 + 2) + D * W * 2 + D * 2
@@ -777,6 +798,16 @@ def _conv_bench(ops, dev, a, hbm, flush):
                    "us_per_call": us_up, "algorithmic_bytes": b_up,
                    "achieved_gbs": b_up / (us_up * 1e-6) / 1e9, "frac_hbm": b_up / (us_up * 1e-6) / 1e9 / hbm,
                    "kernels": "conv_update_kernel"},
+        "layer_prefill": {"workload": "causal_conv1d_fn + chunk_gated_delta_rule of one GDN layer, config 1 "
+                                      "(8192 tokens, 16/32 heads, d=128, bf16, in-kernel L2 norm)",
+                          "us_two_ops": us_two, "us_fused": us_fused,
+                          "kernels_two_ops": "conv_fwd_kernel + conv_state_kernel + chunk_plan_kernel + "
+                                             "tc_wy_kernel + tc_state3_kernel",
+                          "kernels_fused": "chunk_plan_kernel + tc_wy_kernel (conv applied to its tiles) + "
+                                           "tc_state3_kernel + conv_state_kernel",
+                          # conv reads x and writes y, the prefill reads y; fused: x read
+                          # once, post-conv q/k written once for the state kernel
+                          "hbm_bytes_saved": 2 * (2 * T * D) - 2 * T * 2 * H * 128},
         "peak_gbs": hbm, "peak_kind": "measured HBM copy"}
 
 

@@ -40,6 +40,8 @@ EXPORTED = (
     "gdn_causal_conv1d_fwd",
     "gdn_causal_conv1d_fn",
     "gdn_causal_conv1d_update",
+    "gdn_conv_chunk_workspace_size",
+    "gdn_conv_chunk_fwd",
     "gdn_last_error",
     "gdn_abi_version",
     "gdn_kernel_launch_count",
@@ -61,6 +63,7 @@ class ChunkArgs(ctypes.Structure):
         ("scale", ctypes.c_float),
         ("use_qk_l2norm", _i32), ("state_v_first", _i32), ("force_generic", _i32),
         ("stage_events", ctypes.POINTER(_vp)), ("n_stage_events", _i32),
+        ("q_token_stride", _i64), ("k_token_stride", _i64), ("v_token_stride", _i64),
     ]
 
 
@@ -198,6 +201,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.gdn_causal_conv1d_fn.restype = ctypes.c_int
     lib.gdn_causal_conv1d_update.argtypes = [ctypes.POINTER(Conv1dUpdateArgs), _vp]
     lib.gdn_causal_conv1d_update.restype = ctypes.c_int
+    lib.gdn_conv_chunk_workspace_size.argtypes = [ctypes.POINTER(ChunkArgs)]
+    lib.gdn_conv_chunk_workspace_size.restype = ctypes.c_size_t
+    lib.gdn_conv_chunk_fwd.argtypes = [ctypes.POINTER(ChunkArgs), ctypes.POINTER(Conv1dFnArgs), _vp]
+    lib.gdn_conv_chunk_fwd.restype = ctypes.c_int
     lib.gdn_last_error.argtypes = []
     lib.gdn_last_error.restype = ctypes.c_char_p
     lib.gdn_abi_version.argtypes = []

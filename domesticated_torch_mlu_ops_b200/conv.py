@@ -47,6 +47,67 @@ def _fdt(t, name):
     return _DT[t.dtype]
 
 
+def _fn_args(x, weight, bias, conv_states, query_start_loc, cache_indices, has_initial_state, activation,
+             pad_slot_id, null_block_id, block_idx_first_scheduled_token, block_idx_last_scheduled_token,
+             initial_state_idx, num_computed_tokens, block_size_to_align, out):
+    """``gdn_conv1d_fn_args`` for channel-last x ``(dim, tokens)`` (and ``out``
+    of the same layout, or None for the fused prefill); returns the struct and
+    the converted tensors it points into (keep them alive until the launch)."""
+    dim, total = x.shape
+    W = weight.shape[1]
+    if W < 2:
+        raise ValueError("[CausalConv1d] weight.shape[-1] must be at least 2")
+    if conv_states.dim() != 3 or conv_states.shape[1] != dim or conv_states.shape[2] < W - 1:
+        raise ValueError(f"[CausalConv1d] conv_states {tuple(conv_states.shape)} must be (lines, {dim}, >= {W - 1})")
+    if conv_states.stride(1) != 1:
+        raise ValueError("[CausalConv1d] conv_states must have unit stride along dim")
+    w = weight.contiguous()
+    b = None if bias is None else bias.to(w.dtype).contiguous()
+    qsl = (query_start_loc if query_start_loc.dtype in _IDT else query_start_loc.to(torch.int32)).contiguous()
+    batch = qsl.numel() - 1
+    apc = block_idx_last_scheduled_token is not None
+    ci = None
+    idx_dt = _lib.GDN_I32
+    if cache_indices is not None:
+        ci = (cache_indices if cache_indices.dtype in _IDT else cache_indices.to(torch.int32)).contiguous()
+        idx_dt = _IDT[ci.dtype]
+        if ci.dim() not in (1, 2) or ci.shape[0] != batch or (ci.dim() == 2 and not apc):
+            raise ValueError(f"[CausalConv1d] cache_indices must be ({batch},) (or ({batch}, blocks) "
+                             "with prefix caching)")
+    blocks = [None] * 4
+    if apc:
+        if cache_indices is None:
+            raise ValueError("[CausalConv1d] prefix caching needs cache_indices")
+        if ci.dim() == 1:
+            ci = ci[:, None]
+        blocks = [t if t is None else t.to(torch.int32).contiguous()
+                  for t in (block_idx_first_scheduled_token, block_idx_last_scheduled_token,
+                            initial_state_idx, num_computed_tokens)]
+        if any(t is None for t in blocks):
+            raise ValueError("[CausalConv1d] prefix caching needs block_idx_first_scheduled_token, "
+                             "block_idx_last_scheduled_token, initial_state_idx and num_computed_tokens")
+    hi = None
+    if has_initial_state is not None:
+        hi = has_initial_state.to(torch.bool).contiguous()
+        if hi.numel() != batch:
+            raise ValueError(f"[CausalConv1d] has_initial_state must be ({batch},)")
+    args = _lib.Conv1dFnArgs(
+        x=_ptr(x), out=_ptr(out), weight=_ptr(w), bias=_ptr(b), conv_states=_ptr(conv_states),
+        query_start_loc=_ptr(qsl), cache_indices=_ptr(ci), has_initial_state=_ptr(hi),
+        stride_x_token=x.stride(1) if total > 1 else dim,
+        stride_o_token=(out.stride(1) if total > 1 else dim) if out is not None else 0,
+        stride_state_seq=conv_states.stride(0), stride_state_tok=conv_states.stride(2),
+        num_cache_lines=conv_states.shape[0], batch=batch, dim=dim, total_tokens=total,
+        pad_slot_id=int(pad_slot_id), null_block_id=0 if null_block_id is None else int(null_block_id),
+        has_null_block=0 if null_block_id is None else 1, W=W,
+        x_dtype=_fdt(x, "x"), w_dtype=_fdt(w, "weight"), state_dtype=_fdt(conv_states, "conv_states"),
+        qsl_dtype=_IDT[qsl.dtype], idx_dtype=idx_dt, activation=_act(activation),
+        block_idx_first=_ptr(blocks[0]), block_idx_last=_ptr(blocks[1]), initial_state_idx=_ptr(blocks[2]),
+        num_computed_tokens=_ptr(blocks[3]), stride_cache_indices=ci.stride(0) if ci is not None else 0,
+        block_size_to_align=int(block_size_to_align or 0), apc_dtype=_lib.GDN_I32)
+    return args, (w, b, qsl, ci, hi, blocks)
+
+
 def causal_conv1d(
     x: torch.Tensor,
     weight: torch.Tensor | None = None,
@@ -143,61 +204,15 @@ def causal_conv1d_fn(
         raise ValueError("[CausalConv1d] x must be (dim, tokens) and weight (dim, width)")
     _cuda("causal_conv1d_fn", x, weight, bias, conv_states, query_start_loc, cache_indices, has_initial_state)
     dim, total = x.shape
-    W = weight.shape[1]
-    if W < 2:
-        raise ValueError("[CausalConv1d] weight.shape[-1] must be at least 2")
     if x.stride(0) != 1 and total > 1:
         x = x.t().contiguous().t()  # channel-last storage [tokens, dim]
     out = torch.empty_like(x)
     if out.stride(0) != 1 and total > 1:
         out = torch.empty(total, dim, dtype=x.dtype, device=x.device).t()
-    if conv_states.dim() != 3 or conv_states.shape[1] != dim or conv_states.shape[2] < W - 1:
-        raise ValueError(f"[CausalConv1d] conv_states {tuple(conv_states.shape)} must be (lines, {dim}, >= {W - 1})")
-    if conv_states.stride(1) != 1:
-        raise ValueError("[CausalConv1d] conv_states must have unit stride along dim")
-    w = weight.contiguous()
-    b = None if bias is None else bias.to(w.dtype).contiguous()
-    qsl = query_start_loc if query_start_loc.dtype in _IDT else query_start_loc.to(torch.int32)
-    batch = qsl.numel() - 1
-    apc = block_idx_last_scheduled_token is not None
-    ci = None
-    idx_dt = _lib.GDN_I32
-    if cache_indices is not None:
-        ci = (cache_indices if cache_indices.dtype in _IDT else cache_indices.to(torch.int32)).contiguous()
-        idx_dt = _IDT[ci.dtype]
-        if ci.dim() not in (1, 2) or ci.shape[0] != batch or (ci.dim() == 2 and not apc):
-            raise ValueError(f"[CausalConv1d] cache_indices must be ({batch},) (or ({batch}, blocks) "
-                             "with prefix caching)")
-    blocks = [None] * 4
-    if apc:
-        if cache_indices is None:
-            raise ValueError("[CausalConv1d] prefix caching needs cache_indices")
-        if ci.dim() == 1:
-            ci = ci[:, None]
-        blocks = [t if t is None else t.to(torch.int32).contiguous()
-                  for t in (block_idx_first_scheduled_token, block_idx_last_scheduled_token,
-                            initial_state_idx, num_computed_tokens)]
-        if any(t is None for t in blocks):
-            raise ValueError("[CausalConv1d] prefix caching needs block_idx_first_scheduled_token, "
-                             "block_idx_last_scheduled_token, initial_state_idx and num_computed_tokens")
-    hi = None
-    if has_initial_state is not None:
-        hi = has_initial_state.to(torch.bool).contiguous()
-        if hi.numel() != batch:
-            raise ValueError(f"[CausalConv1d] has_initial_state must be ({batch},)")
-    args = _lib.Conv1dFnArgs(
-        x=_ptr(x), out=_ptr(out), weight=_ptr(w), bias=_ptr(b), conv_states=_ptr(conv_states),
-        query_start_loc=_ptr(qsl.contiguous()), cache_indices=_ptr(ci), has_initial_state=_ptr(hi),
-        stride_x_token=x.stride(1) if total > 1 else dim, stride_o_token=out.stride(1) if total > 1 else dim,
-        stride_state_seq=conv_states.stride(0), stride_state_tok=conv_states.stride(2),
-        num_cache_lines=conv_states.shape[0], batch=batch, dim=dim, total_tokens=total,
-        pad_slot_id=int(pad_slot_id), null_block_id=0 if null_block_id is None else int(null_block_id),
-        has_null_block=0 if null_block_id is None else 1, W=W,
-        x_dtype=_fdt(x, "x"), w_dtype=_fdt(w, "weight"), state_dtype=_fdt(conv_states, "conv_states"),
-        qsl_dtype=_IDT[qsl.dtype], idx_dtype=idx_dt, activation=_act(activation),
-        block_idx_first=_ptr(blocks[0]), block_idx_last=_ptr(blocks[1]), initial_state_idx=_ptr(blocks[2]),
-        num_computed_tokens=_ptr(blocks[3]), stride_cache_indices=ci.stride(0) if ci is not None else 0,
-        block_size_to_align=int(block_size_to_align or 0), apc_dtype=_lib.GDN_I32)
+    args, _keep = _fn_args(x, weight, bias, conv_states, query_start_loc, cache_indices, has_initial_state,
+                           activation, pad_slot_id, null_block_id, block_idx_first_scheduled_token,
+                           block_idx_last_scheduled_token, initial_state_idx, num_computed_tokens,
+                           block_size_to_align, out)
     with torch.cuda.device(x.device):
         _lib.check(_lib.load().gdn_causal_conv1d_fn(args, _stream(x.device)))
     return out

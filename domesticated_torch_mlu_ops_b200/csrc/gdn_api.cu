@@ -59,6 +59,16 @@ int check_chunk(const gdn_chunk_args* a) {
   int rc = check_heads(a->B, a->T, a->N, a->H, a->HV, a->K, a->V, a->cu_seqlens, a->cu_dtype);
   if (rc) return rc;
   if (!qkv_dtype_ok(a->qkv_dtype)) return fail(GDN_ERR_INVALID, "qkv dtype must be F32, BF16 or F16");
+  if (a->q_token_stride || a->k_token_stride || a->v_token_stride) {
+    if (a->force_generic || !gdn::tc_path_applies(*a))
+      return fail(GDN_ERR_UNSUPPORTED, "strided q/k/v rows are read in place on the tensor-core path only "
+                                       "(bf16/f16, K = V = 128); pass packed rows");
+    auto ok = [](int64_t st, int64_t width) { return st == 0 || (st >= width && st % 8 == 0); };
+    if (!ok(a->q_token_stride, static_cast<int64_t>(a->H) * a->K) ||
+        !ok(a->k_token_stride, static_cast<int64_t>(a->H) * a->K) ||
+        !ok(a->v_token_stride, static_cast<int64_t>(a->HV) * a->V))
+      return fail(GDN_ERR_INVALID, "q/k/v token strides must be 0 or multiples of 8 at least the packed row width");
+  }
   return GDN_OK;
 }
 
@@ -130,6 +140,43 @@ int gdn_chunk_fwd_test_stall(const gdn_chunk_args* a, int64_t stall_chunk, int64
     return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", a->workspace_bytes, need);
   cudaError_t e = gdn::launch_chunk_tc(*a, static_cast<cudaStream_t>(stream), stall_chunk, wait_limit_cycles);
   if (e != cudaSuccess) return cuda_fail(e, "gdn_chunk_fwd_test_stall");
+  return GDN_OK;
+}
+
+size_t gdn_conv_chunk_workspace_size(const gdn_chunk_args* a) {
+  if (check_chunk(a)) return 0;
+  if (a->force_generic || !gdn::tc_path_applies(*a))
+    return fail(GDN_ERR_UNSUPPORTED, "the fused conv prefill needs bf16/f16 q/k/v with K = V = 128"), 0;
+  return gdn::tc_conv_workspace_bytes(*a);
+}
+
+int gdn_conv_chunk_fwd(const gdn_chunk_args* a, const gdn_conv1d_fn_args* c, void* stream) {
+  int rc = check_chunk(a);
+  if (rc) return rc;
+  if (a->force_generic || !gdn::tc_path_applies(*a))
+    return fail(GDN_ERR_UNSUPPORTED, "the fused conv prefill needs bf16/f16 q/k/v with K = V = 128");
+  if ((rc = gdn::check_conv_fn_args(c)) != GDN_OK) return rc;
+  if (c->out) return fail(GDN_ERR_INVALID, "conv out must be NULL: the fused prefill keeps the conv output on chip");
+  if (a->B != 1 || !a->cu_seqlens)
+    return fail(GDN_ERR_INVALID, "the fused conv prefill takes a packed batch (B = 1 with cu_seqlens)");
+  if (c->batch != a->N || c->total_tokens != a->T)
+    return fail(GDN_ERR_INVALID, "conv batch=%lld / total_tokens=%lld must equal N=%lld / T=%lld",
+                (long long)c->batch, (long long)c->total_tokens, (long long)a->N, (long long)a->T);
+  if (c->dim != 2LL * a->H * a->K + static_cast<int64_t>(a->HV) * a->V)
+    return fail(GDN_ERR_INVALID, "conv dim=%lld must be 2*H*K + HV*V = %lld ([q | k | v] channels)",
+                (long long)c->dim, 2LL * a->H * a->K + static_cast<long long>(a->HV) * a->V);
+  if (c->W != 4) return fail(GDN_ERR_UNSUPPORTED, "the fused conv prefill supports kernel width 4 (W=%d)", c->W);
+  if (c->x_dtype != a->qkv_dtype || c->w_dtype != a->qkv_dtype || c->state_dtype != a->qkv_dtype)
+    return fail(GDN_ERR_UNSUPPORTED, "x, weight, bias and conv_states must have the q/k/v dtype");
+  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!aligned(c->x) || c->stride_x_token % 8 != 0 || !aligned(c->weight) || (c->bias && !aligned(c->bias)))
+    return fail(GDN_ERR_INVALID, "x (and its token stride), weight and bias must be 16-byte aligned");
+  if (a->T > 0 && (!a->g || !a->beta || !a->o)) return fail(GDN_ERR_INVALID, "g, beta and o must be non-null");
+  const size_t need = gdn::tc_conv_workspace_bytes(*a);
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes given, %zu needed", a->workspace_bytes, need);
+  cudaError_t e = gdn::launch_chunk_tc(*a, static_cast<cudaStream_t>(stream), -1, 0, c);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_conv_chunk_fwd");
   return GDN_OK;
 }
 

@@ -43,6 +43,7 @@
 
 #include <type_traits>
 
+#include "conv_math.cuh"
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 #include "gdn_chunk_tc.cuh"
@@ -76,12 +77,162 @@ struct WySmem {
   static constexpr int kBytes = kTmem + 8 + 1024;  // + slack for 1 KiB alignment
   static_assert(kT % 16 == 0 && 64 * kMS * 4 >= 2 * kAtom, "W/U staging must fit over T");
   static_assert(3 * (kBytes + 1024) <= 228 * 1024, "three CTAs per SM");
+  // fused conv: the pre-conv q and k rows s-3 .. s+63 ([67][128] 16-bit each)
+  // land over A and T before the first product; the v rows over T after it
+  static constexpr int kBox = 67 * 128 * 2;
+  static_assert(kA + 2 * kBox <= kZ && kT + kBox <= kZ && kBox % 128 == 0, "conv boxes fit over A and T");
 };
 constexpr int kWyThreads = 256;
 
+// --- the causal conv1d of the fused path (ConvIn) ---------------------------
+
+// Line of sequence n's initial conv window and whether the conv skips the
+// sequence (a PAD or null-block line: its outputs are zeros and its line is
+// left alone), as causal_conv1d_fn decides (kernels.py:254-289).
+__device__ __forceinline__ void conv_seq(const ConvIn& ci, int64_t n, int64_t& line, bool& hinit, bool& skip) {
+  line = n;
+  if (ci.cache_indices) {
+    const int64_t col = ci.apc_init ? load_index(ci.apc_init, ci.apc_dtype, n) : 0;
+    line = load_index(ci.cache_indices, ci.idx_dtype, n * ci.ci_stride + col);
+  }
+  skip = (ci.has_null && line == ci.null_block) || line == ci.pad_slot;
+  hinit = ci.has_init && ci.has_init[n] && !skip;
+}
+
+// Taps of channels ch .. ch+3 as two channel pairs (w[0]: ch, ch+1; w[1]:
+// ch+2, ch+3; per tap), and their bias: weight [dim, 4] rows ch .. ch+3 are
+// 16 contiguous elements.
 template <typename T>
+__device__ __forceinline__ void conv_taps4(const ConvIn& ci, int64_t ch, float2 (&w)[2][4], float2 (&bias)[2]) {
+  const uint4* wp = reinterpret_cast<const uint4*>(static_cast<const T*>(ci.weight) + ch * 4);
+#pragma unroll
+  for (int pr = 0; pr < 2; ++pr) {
+    const uint4 r = __ldg(wp + pr);
+    const float2 a0 = conv::unpack2<T>(r.x), a1 = conv::unpack2<T>(r.y);  // first channel: taps 0,1 | 2,3
+    const float2 b0 = conv::unpack2<T>(r.z), b1 = conv::unpack2<T>(r.w);  // second channel
+    w[pr][0] = make_float2(a0.x, b0.x);
+    w[pr][1] = make_float2(a0.y, b0.y);
+    w[pr][2] = make_float2(a1.x, b1.x);
+    w[pr][3] = make_float2(a1.y, b1.y);
+  }
+  if (ci.bias) {
+    const uint2 bb = __ldg(reinterpret_cast<const uint2*>(static_cast<const T*>(ci.bias) + ch));
+    bias[0] = conv::unpack2<T>(bb.x);
+    bias[1] = conv::unpack2<T>(bb.y);
+  } else {
+    bias[0] = bias[1] = make_float2(0.f, 0.f);
+  }
+}
+
+// Input j (0..2) of the window before a sequence's first token, channels
+// ch .. ch+3 (two pairs): the initial cache line's entries, or zeros.
+template <typename T>
+__device__ __forceinline__ void conv_halo4(const ConvIn& ci, int64_t line, bool hinit, int j, int64_t ch,
+                                           float2 (&x)[2]) {
+  if (!hinit) {
+    x[0] = x[1] = make_float2(0.f, 0.f);
+    return;
+  }
+  const uint16_t* st = static_cast<const uint16_t*>(ci.states) + line * ci.st_seq + j * ci.st_tok + ch;
+  x[0] = conv::unpack2<T>(static_cast<uint32_t>(st[0]) | (static_cast<uint32_t>(st[1]) << 16));
+  x[1] = conv::unpack2<T>(static_cast<uint32_t>(st[2]) | (static_cast<uint32_t>(st[3]) << 16));
+}
+
+// One output row of four channels from the window x0..x3 (per pair).
+template <typename T>
+__device__ __forceinline__ uint2 conv_out4(const float2 (&w)[2][4], const float2 (&bias)[2], const float2 (&x0)[2],
+                                           const float2 (&x1)[2], const float2 (&x2)[2], const float2 (&x3)[2],
+                                           bool act) {
+  uint2 y;
+  y.x = conv::conv2_w4<T>(w[0], bias[0], x0[0], x1[0], x2[0], x3[0], act);
+  y.y = conv::conv2_w4<T>(w[1], bias[1], x0[1], x1[1], x2[1], x3[1], act);
+  return y;
+}
+
+// Rows r0 .. r0+NR-1 (r0 a multiple of 8) of one 128-channel conv tile,
+// channels c4 .. c4+3 of it: `box` holds the pre-conv rows s-3 .. s+63
+// ([67][128], row-major, 16-bit); the outputs go to the 128-byte swizzled
+// 64-row operand atoms at `atom` (columns 0-63; columns 64-127 two atoms on)
+// or, with `keep`, to registers, and when `gdst` is given also to global rows
+// s+i (row stride rs).  Rows at or past L, and every row of a skipped
+// sequence, are zeros.  In a sequence's first chunk the window before row 0
+// comes from the initial cache line.
+template <typename T, int NR>
+__device__ __forceinline__ void conv_rows4(const ConvIn& ci, const uint8_t* box, int c4, int64_t ch, int r0,
+                                           bool first_chunk, int64_t line, bool hinit, bool skip, int L,
+                                           uint8_t* atom, T* gdst, int64_t s, int64_t rs, uint2* keep) {
+  float2 w[2][4], bias[2];
+  conv_taps4<T>(ci, ch, w, bias);
+  const uint2* src = reinterpret_cast<const uint2*>(box) + (c4 >> 2);  // 32 uint2 per row
+  auto ld = [&](int r, float2 (&x)[2]) {
+    const uint2 u = src[r * 32];
+    x[0] = conv::unpack2<T>(u.x);
+    x[1] = conv::unpack2<T>(u.y);
+  };
+  float2 x0[2], x1[2], x2[2];
+  if (first_chunk && r0 == 0) {
+    conv_halo4<T>(ci, line, hinit, 0, ch, x0);
+    conv_halo4<T>(ci, line, hinit, 1, ch, x1);
+    conv_halo4<T>(ci, line, hinit, 2, ch, x2);
+  } else {
+    ld(r0, x0);
+    ld(r0 + 1, x1);
+    ld(r0 + 2, x2);
+  }
+  uint8_t* at = atom + (c4 >= 64 ? 2 * kAtom : 0) + r0 * 128 + ((c4 & 7) * 2);
+  const int cc = ((c4 & 63) >> 3) << 4;
+  T* gd = gdst ? gdst + (s + r0) * rs : nullptr;
+  const bool act = ci.act != 0;
+  auto emit = [&](int k, uint2 y) {
+    if (keep) keep[k] = y;
+    else *reinterpret_cast<uint2*>(at + k * 128 + (cc ^ ((k & 7) << 4))) = y;
+  };
+  if (L >= r0 + NR && !skip) {  // every row of this run is inside the sequence
+#pragma unroll
+    for (int k = 0; k < NR; ++k) {
+      float2 x3[2];
+      ld(r0 + k + 3, x3);
+      const uint2 y = conv_out4<T>(w, bias, x0, x1, x2, x3, act);
+      emit(k, y);
+      if (gd) {
+        *reinterpret_cast<uint2*>(gd) = y;
+        gd += rs;
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        x0[e] = x1[e];
+        x1[e] = x2[e];
+        x2[e] = x3[e];
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < NR; ++k) {
+      const int i = r0 + k;
+      float2 x3[2];
+      ld(i + 3, x3);
+      uint2 y = make_uint2(0u, 0u);
+      if (i < L && !skip) y = conv_out4<T>(w, bias, x0, x1, x2, x3, act);
+      emit(k, y);
+      if (gd && i < L) *reinterpret_cast<uint2*>(gd) = y;
+      if (gd) gd += rs;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        x0[e] = x1[e];
+        x1[e] = x2[e];
+        x2[e] = x3[e];
+      }
+    }
+  }
+}
+
+// CONV: the q, k, v tiles are the causal conv1d of ci.x, computed here in
+// place of their TMA loads (q and k before the first product, v while it
+// runs); the CTA of each chunk's first v-head of a q/k head also writes the
+// post-conv q and k rows for the state kernel.
+template <typename T, bool CONV>
 __global__ void __launch_bounds__(kWyThreads, 3)
-tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
+tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
              const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
              const __grid_constant__ CUtensorMap tv) {
   extern __shared__ uint8_t sm_raw[];
@@ -124,11 +275,17 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     umma::mbar_init(bars + 1, 1);
     umma::mbar_init(bars + 2, 1);
     umma::mbar_fence_init();
-    umma::mbar_arrive_expect_tx(bar_kq, 2 * kImg64x128);
-    umma::tma_load_3d(ops, &tk, 0, h, static_cast<int>(s), bar_kq);
-    umma::tma_load_3d(ops + kAtom, &tq, 0, h, static_cast<int>(s), bar_kq);
-    umma::tma_load_3d(ops + 2 * kAtom, &tk, 64, h, static_cast<int>(s), bar_kq);
-    umma::tma_load_3d(ops + 3 * kAtom, &tq, 64, h, static_cast<int>(s), bar_kq);
+    if constexpr (CONV) {  // pre-conv q and k rows (tv: the x map)
+      umma::mbar_arrive_expect_tx(bar_kq, 2 * WySmem::kBox);
+      umma::tma_load_2d(sm + WySmem::kA, &tv, h * D, static_cast<int>(s) - 3, bar_kq);
+      umma::tma_load_2d(sm + WySmem::kA + WySmem::kBox, &tv, (p.H + h) * D, static_cast<int>(s) - 3, bar_kq);
+    } else {
+      umma::mbar_arrive_expect_tx(bar_kq, 2 * kImg64x128);
+      umma::tma_load_3d(ops, &tk, 0, h, static_cast<int>(s), bar_kq);
+      umma::tma_load_3d(ops + kAtom, &tq, 0, h, static_cast<int>(s), bar_kq);
+      umma::tma_load_3d(ops + 2 * kAtom, &tk, 64, h, static_cast<int>(s), bar_kq);
+      umma::tma_load_3d(ops + 3 * kAtom, &tq, 64, h, static_cast<int>(s), bar_kq);
+    }
   }
   if (warp == 0) {
     umma::tmem_alloc(tslot, 128);
@@ -149,18 +306,42 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     bet[lane] = lane < L ? p.beta[(s + lane) * p.HV + hv] : 0.f;
     bet[lane + 32] = lane + 32 < L ? p.beta[(s + lane + 32) * p.HV + hv] : 0.f;
   }
+  int64_t cline;
+  bool chinit, cskip;
+  if constexpr (CONV) conv_seq(ci, n, cline, chinit, cskip);
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tslot;
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
   constexpr bool kBf16 = !std::is_same<T, __half>::value;
   bool issued_store = false;
+  uint2 vres[8];  // CONV: this thread's eight v output rows until the Q atoms are free
+  bool okv;
 
   // One warp waits on each mbarrier; the block learns the outcome at the
-  // barrier that follows (tcgen05 readers fence after it).
-  bool ok = warp == 0 ? umma::mbar_wait(bar_kq, 0) : true;
+  // barrier that follows (tcgen05 readers fence after it).  The conv tiles are
+  // read by every thread, so every thread waits on their loads.
+  bool ok = CONV || warp == 0 ? umma::mbar_wait(bar_kq, 0) : true;
   if (!ok) record_error(w.err, 1, kSiteWyLoad);
   if (__syncthreads_or(!ok)) goto teardown;
+  if constexpr (CONV) {
+    // q and k tiles: even warps q, odd warps k; lane -> four channels, warp
+    // pair -> 16 rows; the CTA of a q/k head's first v-head also writes the
+    // rows for the state kernel.
+    const bool kside = warp & 1;
+    const int c4 = lane * 4;
+    const int64_t ch = (kside ? static_cast<int64_t>(p.H) * D : 0) + static_cast<int64_t>(h) * D + c4;
+    T* gdst = hv % (p.HV / p.H) == 0
+                  ? static_cast<T*>(kside ? ci.kc : ci.qc) + static_cast<int64_t>(h) * D + c4 : nullptr;
+    conv_rows4<T, 16>(ci, sm + WySmem::kA + (kside ? WySmem::kBox : 0), c4, ch, (warp >> 1) * 16, lc == 0, cline,
+                      chinit, cskip, L, ops + (kside ? 0 : kAtom), gdst, s, static_cast<int64_t>(p.H) * D, nullptr);
+    umma::fence_proxy_async();  // the atoms are read by tcgen05; the boxes are rewritten by TMA next
+    __syncthreads();
+    if (tid == 0) {  // pre-conv v rows over T (the k box there is consumed)
+      umma::mbar_arrive_expect_tx(bar_v, WySmem::kBox);
+      umma::tma_load_2d(sm + WySmem::kT, &tv, (2 * p.H + hv) * D, static_cast<int>(s) - 3, bar_v);
+    }
+  }
   if (warp == 0) {  // [K; Q] [K; Q]^T  (M = 128, N = 128, K = 128): S_kk, S_qk and both Gram diagonals
     umma::fence_after_sync();
     const uint32_t id = umma::idesc_f16(128, 128, kBf16, false, false);
@@ -172,10 +353,28 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
     }
     if (umma::elect_one()) umma::mma_commit(bar_mma);
   }
+  okv = true;
+  if constexpr (CONV) {  // v tile while the product runs: lane -> four channels, warp -> 8 rows
+    okv = umma::mbar_wait(bar_v, 0);
+    if (!okv) record_error(w.err, 1, kSiteWyLoad);
+    if (okv) {
+      const int c4 = lane * 4;
+      const int64_t ch = 2 * static_cast<int64_t>(p.H) * D + static_cast<int64_t>(hv) * D + c4;
+      conv_rows4<T, 8>(ci, sm + WySmem::kT, c4, ch, warp * 8, lc == 0, cline, chinit, cskip, L, nullptr, nullptr, s,
+                       0, vres);
+    }
+  }
   ok = warp == 0 ? umma::mbar_wait(bar_mma, 0) : true;
   if (!ok) record_error(w.err, 1, kSiteWyMma1);
-  if (__syncthreads_or(!ok)) goto teardown;
+  if (__syncthreads_or(!ok || !okv)) goto teardown;
   umma::fence_after_sync();
+  if constexpr (CONV) {  // Q is dead: v into its atoms (made visible to tcgen05 before the W/U products)
+    const int c4 = lane * 4, r0 = warp * 8;
+    uint8_t* at = ops + kAtom + (c4 >= 64 ? 2 * kAtom : 0) + r0 * 128 + (c4 & 7) * 2;
+    const int cc = ((c4 & 63) >> 3) << 4;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) *reinterpret_cast<uint2*>(at + k * 128 + (cc ^ ((k & 7) << 4))) = vres[k];
+  }
   if (colh == 0) {  // L2-norm factors from the Gram diagonal: row r's |k|^2 or |q|^2 sits in column r
     float x[32];
     umma::tmem_ld32(tmem + lane_base + quad * 32, x);
@@ -193,7 +392,7 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   }
   umma::fence_proxy_async();
   __syncthreads();
-  if (warp == 3 && umma::elect_one()) {  // Q is dead: bring V into its atoms
+  if (!CONV && warp == 3 && umma::elect_one()) {  // Q is dead: bring V into its atoms
     umma::mbar_arrive_expect_tx(bar_v, kImg64x128);
     umma::tma_load_3d(ops + kAtom, &tv, 0, hv, static_cast<int>(s), bar_v);
     umma::tma_load_3d(ops + 3 * kAtom, &tv, 64, hv, static_cast<int>(s), bar_v);
@@ -289,7 +488,7 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale,
   }
   umma::fence_proxy_async();
   __syncthreads();
-  ok = warp == 0 ? umma::mbar_wait(bar_v, 0) : true;
+  ok = !CONV && warp == 0 ? umma::mbar_wait(bar_v, 0) : true;
   if (!ok) record_error(w.err, 1, kSiteWyLoad);
   if (__syncthreads_or(!ok)) goto teardown;
 
@@ -670,14 +869,31 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// The conv input x ((dim, tokens) channel-last, token stride sx elements):
+// 128-channel x 67-token boxes, no swizzle, zeros outside the tensor.
+cudaError_t make_map_x(CUtensorMap* m, const void* ptr, int64_t dim, int64_t ttot, int64_t sx, bool f16) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(ttot)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(sx) * 2};
+  const cuuint32_t box[2] = {128, 67};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // [Ttot, heads, 128] tensor, 64 x 64 boxes with 128-byte swizzle.
-cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, bool f16) {
+// tstride: elements between token rows (0: packed, heads * 128).
+cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, bool f16, int64_t tstride) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(heads),
                               static_cast<cuuint64_t>(ttot)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2,
-                                 static_cast<cuuint64_t>(heads) * D * 2};
+                                 static_cast<cuuint64_t>(tstride > 0 ? tstride : int64_t(heads) * D) * 2};
   const cuuint32_t box[3] = {64, 1, 64};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
@@ -717,9 +933,11 @@ bool choose_fused(bool f16) {
 }
 
 template <typename T>
-cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, long long stall_limit) {
+cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, long long stall_limit,
+                const gdn_conv1d_fn_args* conv) {
   constexpr bool kF16 = std::is_same<T, __half>::value;
-  const Layout l = plan(a);
+  const bool cv = conv != nullptr;
+  const Layout l = plan(a, cv);
   uint8_t* ws = static_cast<uint8_t*>(a.workspace);
   Work w;
   w.coff = reinterpret_cast<const int64_t*>(ws + l.coff);
@@ -730,18 +948,31 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, lo
   w.scal = reinterpret_cast<float*>(ws + l.scal);
   w.flags = reinterpret_cast<int*>(ws + l.flags);
   w.ncu = chunk_upper_bound(a.B * a.T, a.N);
-  const bool fused = choose_fused(kF16);
+  const bool fused = !cv && choose_fused(kF16);
   w.vs = fused ? 32 : choose_vs(a);  // the fused kernel writes and reads 32-column U slices
   w.stall_chunk = stall_chunk;
   w.stall_limit = stall_limit;
   const int64_t ttot = a.B * a.T;
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
+  ConvIn ci{};
+  if (cv) {
+    ci.x = conv->x; ci.weight = conv->weight; ci.bias = conv->bias; ci.states = conv->conv_states;
+    ci.cache_indices = conv->cache_indices; ci.has_init = conv->has_initial_state;
+    ci.apc_init = conv->block_idx_last ? conv->initial_state_idx : nullptr;
+    ci.qc = ws + l.qc; ci.kc = ws + l.kc;
+    ci.sx = conv->stride_x_token; ci.st_seq = conv->stride_state_seq; ci.st_tok = conv->stride_state_tok;
+    ci.ci_stride = conv->cache_indices ? (conv->stride_cache_indices > 0 ? conv->stride_cache_indices : 1) : 0;
+    ci.pad_slot = conv->pad_slot_id; ci.null_block = conv->null_block_id; ci.has_null = conv->has_null_block;
+    ci.idx_dtype = conv->idx_dtype; ci.apc_dtype = conv->apc_dtype; ci.act = conv->activation == GDN_ACT_SILU;
+  }
   CUtensorMap tq, tk, tv;
   cudaError_t e;
-  if (ttot > 0) {
-    if ((e = make_map(&tq, a.q, a.H, ttot, kF16)) != cudaSuccess) return e;
-    if ((e = make_map(&tk, a.k, a.H, ttot, kF16)) != cudaSuccess) return e;
-    if ((e = make_map(&tv, a.v, a.HV, ttot, kF16)) != cudaSuccess) return e;
+  if (ttot > 0) {  // with the conv, the state kernel reads the post-conv q and k that the WY kernel writes
+    if ((e = make_map(&tq, cv ? ci.qc : a.q, a.H, ttot, kF16, cv ? 0 : a.q_token_stride)) != cudaSuccess) return e;
+    if ((e = make_map(&tk, cv ? ci.kc : a.k, a.H, ttot, kF16, cv ? 0 : a.k_token_stride)) != cudaSuccess) return e;
+    if (cv) {  // the WY kernel's third map is the conv input
+      if ((e = make_map_x(&tv, conv->x, conv->dim, ttot, conv->stride_x_token, kF16)) != cudaSuccess) return e;
+    } else if ((e = make_map(&tv, a.v, a.HV, ttot, kF16, a.v_token_stride)) != cudaSuccess) return e;
   }
   LaunchHooks hk(a.stage_events, a.n_stage_events);
   hk.pre(s);
@@ -753,16 +984,18 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, lo
       hk.pre(s);
       if ((e = launch_fused<T>(a, w, scale, tq, tk, tv, s)) != cudaSuccess) return e;
     } else {
-      auto wy = tc_wy_kernel<T>;
+      auto wy = cv ? tc_wy_kernel<T, true> : tc_wy_kernel<T, false>;
       if ((e = cudaFuncSetAttribute(wy, cudaFuncAttributeMaxDynamicSharedMemorySize, WySmem::kBytes)) !=
           cudaSuccess)
         return e;
       hk.pre(s);
-      wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem::kBytes, s>>>(a, w, scale, tq, tk, tv);
+      wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem::kBytes, s>>>(a, w, scale, ci, tq, tk, tv);
       if ((e = cudaGetLastError()) != cudaSuccess) return e;
       if (w.vs == 32) e = launch_state3<T, 32>(a, w, scale, tq, tk, s, hk);
       else e = launch_state3<T, 64>(a, w, scale, tq, tk, s, hk);
       if (e != cudaSuccess) return e;
+      // the cache lines change only after every reader of the initial lines is done
+      if (cv && (e = launch_conv_fn_states(*conv, s)) != cudaSuccess) return e;
     }
   } else if (a.final_state) {  // no tokens: the final states are the initial ones
     const size_t bytes = static_cast<size_t>(a.N) * a.HV * D * D * sizeof(float);
@@ -782,11 +1015,12 @@ bool tc_path_applies(const gdn_chunk_args& a) {
 }
 
 size_t tc_workspace_bytes(const gdn_chunk_args& a) { return tc::plan(a).total; }
+size_t tc_conv_workspace_bytes(const gdn_chunk_args& a) { return tc::plan(a, true).total; }
 
 cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk,
-                            long long stall_limit) {
-  return a.qkv_dtype == GDN_F16 ? tc::run<__half>(a, s, stall_chunk, stall_limit)
-                                : tc::run<__nv_bfloat16>(a, s, stall_chunk, stall_limit);
+                            long long stall_limit, const gdn_conv1d_fn_args* conv) {
+  return a.qkv_dtype == GDN_F16 ? tc::run<__half>(a, s, stall_chunk, stall_limit, conv)
+                                : tc::run<__nv_bfloat16>(a, s, stall_chunk, stall_limit, conv);
 }
 
 }  // namespace gdn

@@ -40,11 +40,30 @@ struct Work {
   long long stall_limit;
 };
 
-struct Layout {
-  size_t err, coff, wimg, u, pimg, scal, flags, total;
+// The causal conv1d applied by the WY kernel as it loads its tiles
+// (causal_conv1d_fn, triton/conv/kernels.py:157-609, vLLM channel-last
+// layout; width 4; x, weight, bias and the cache lines in the q/k/v dtype).
+// x holds [q heads | k heads | v heads] channels per token.
+struct ConvIn {
+  const void* x;              // (dim, tokens): element (c, t) at x[t * sx + c]
+  const void* weight;         // [dim, 4]
+  const void* bias;           // [dim] or null
+  const void* states;         // cache lines: (l, c, j) at l * st_seq + j * st_tok + c
+  const void* cache_indices;  // [batch] (or [batch, blocks] with prefix caching) or null
+  const uint8_t* has_init;    // [batch] or null
+  const void* apc_init;       // prefix caching: column of cache_indices holding the initial line
+  void* qc;                   // post-conv q [tokens][H][128] for the state kernel
+  void* kc;                   // post-conv k [tokens][H][128]
+  int64_t sx, st_seq, st_tok, ci_stride, pad_slot, null_block;
+  int idx_dtype, apc_dtype, has_null, act;
 };
 
-inline Layout plan(const gdn_chunk_args& a) {
+struct Layout {
+  size_t err, coff, wimg, u, pimg, scal, flags, qc, kc, total;
+};
+
+// conv: room for the post-conv q and k of the fused conv path.
+inline Layout plan(const gdn_chunk_args& a, bool conv = false) {
   auto al = [](size_t x) { return (x + 1023) & ~static_cast<size_t>(1023); };
   const int64_t ncu = chunk_upper_bound(a.B * a.T, a.N);
   const size_t hc = static_cast<size_t>(a.HV) * ncu;
@@ -57,6 +76,9 @@ inline Layout plan(const gdn_chunk_args& a) {
   l.pimg = o; o += al(hc * kImg64x64);
   l.scal = o; o += al(hc * kScal * 4);
   l.flags = o; o += al(hc * 4);
+  const size_t qk = conv ? static_cast<size_t>(a.B * a.T) * a.H * D * 2 : 0;
+  l.qc = o; o += al(qk);
+  l.kc = o; o += al(qk);
   l.total = o;
   return l;
 }
@@ -144,7 +166,7 @@ struct St3 {
 constexpr int kSt3Threads = 288;  // 8 epilogue warps + 1 load warp
 
 // [Ttot, heads, 128] bf16/f16 tensor map with 64 x 64 boxes, 128-byte swizzle.
-cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, bool f16);
+cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, bool f16, int64_t tstride = 0);
 
 // The fused cluster kernel (gdn_chunk_fused.cu): whether clusters of it can
 // be scheduled on the current device, and its launcher (tq, tk, tv as made by

@@ -20,6 +20,7 @@
 //   * the decode update is one thread per channel.
 // Accumulation is fp32; outputs are rounded to nearest even.
 
+#include "conv_math.cuh"
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 
@@ -84,57 +85,6 @@ __device__ __forceinline__ void stv(T* p, const float* v) {
   } else {
 #pragma unroll
     for (int i = 0; i < VEC; ++i) p[i] = from_f<T>(v[i]);
-  }
-}
-
-// y * sigmoid(y) with the hardware exponential and divide (a few ulp).
-__device__ __forceinline__ float silu(float y) { return __fdividef(y, 1.f + __expf(-y)); }
-
-// For 16-bit outputs: y * sigmoid(y) = h + h * tanh(h) with h = y / 2, one
-// special-function instruction (tanh.approx, relative error about 2^-11,
-// under half an output ulp of bf16 and at the half-ulp of fp16).
-__device__ __forceinline__ float silu16(float y) {
-  const float h = 0.5f * y;
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
-  return fmaf(h, t, h);
-}
-
-// SiLU over VEC lanes: silu16 for 16-bit outputs with the halving and the
-// final FMA on packed fp32 pairs (same bits as lane by lane), silu for fp32.
-template <typename T, int VEC>
-__device__ __forceinline__ void silu_vec(float* acc) {
-  if constexpr (sizeof(T) == 2 && VEC % 2 == 0) {
-#pragma unroll
-    for (int e = 0; e < VEC; e += 2) {
-      const float2 h = __fmul2_rn(make_float2(acc[e], acc[e + 1]), make_float2(0.5f, 0.5f));
-      float t0, t1;
-      asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(h.x));
-      asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(h.y));
-      const float2 r = __ffma2_rn(h, make_float2(t0, t1), h);
-      acc[e] = r.x;
-      acc[e + 1] = r.y;
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) acc[e] = sizeof(T) == 2 ? silu16(acc[e]) : silu(acc[e]);
-  }
-}
-
-// acc += w * x over VEC lanes, two lanes per packed fp32 FMA when VEC is even.
-template <int VEC>
-__device__ __forceinline__ void fma_vec(float* acc, const float* w, const float* x) {
-  if constexpr (VEC % 2 == 0) {
-#pragma unroll
-    for (int e = 0; e < VEC; e += 2) {
-      const float2 r = __ffma2_rn(make_float2(w[e], w[e + 1]), make_float2(x[e], x[e + 1]),
-                                  make_float2(acc[e], acc[e + 1]));
-      acc[e] = r.x;
-      acc[e + 1] = r.y;
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) acc[e] = fmaf(w[e], x[e], acc[e]);
   }
 }
 
@@ -669,10 +619,17 @@ extern "C" GDN_API int gdn_causal_conv1d_fwd(const gdn_conv1d_args* a, void* str
   return GDN_OK;
 }
 
-extern "C" GDN_API int gdn_causal_conv1d_fn(const gdn_conv1d_fn_args* a, void* stream) {
+namespace gdn {
+namespace conv {
+
+// Checks causal_conv1d_fn's arguments and fills its kernel parameters;
+// GDN_OK or an error code with the message set.  `fused`: the conv is
+// applied inside the prefill, which has no `out` tensor.
+int fn_params(const gdn_conv1d_fn_args* a, FwdParams& p, bool fused) {
   if (!a) return fail(GDN_ERR_INVALID, "null args");
-  if (!a->x || !a->out || !a->weight || !a->conv_states || !a->query_start_loc)
-    return fail(GDN_ERR_INVALID, "x, out, weight, conv_states and query_start_loc must be non-null");
+  if (!a->x || (!fused && !a->out) || !a->weight || !a->conv_states || !a->query_start_loc)
+    return fail(GDN_ERR_INVALID, fused ? "x, weight, conv_states and query_start_loc must be non-null"
+                                       : "x, out, weight, conv_states and query_start_loc must be non-null");
   if (a->batch < 0 || a->dim <= 0 || a->total_tokens < 0 || a->num_cache_lines < 0)
     return fail(GDN_ERR_INVALID, "bad shape batch=%lld dim=%lld total=%lld", (long long)a->batch,
                 (long long)a->dim, (long long)a->total_tokens);
@@ -683,14 +640,14 @@ extern "C" GDN_API int gdn_causal_conv1d_fn(const gdn_conv1d_fn_args* a, void* s
     return fail(GDN_ERR_INVALID, "query_start_loc and cache_indices dtypes must be I32 or I64");
   if (a->activation != GDN_ACT_NONE && a->activation != GDN_ACT_SILU)
     return fail(GDN_ERR_INVALID, "activation must be GDN_ACT_NONE or GDN_ACT_SILU");
-  if (a->stride_x_token < a->dim || a->stride_o_token < a->dim)
+  if (a->stride_x_token < a->dim || (!fused && a->stride_o_token < a->dim))
     return fail(GDN_ERR_INVALID, "token strides must be >= dim (channel-last layout)");
-  FwdParams p{};
-  p.x = a->x; p.y = a->out; p.weight = a->weight; p.bias = a->bias; p.init = a->conv_states;
+  p = FwdParams{};
+  p.x = a->x; p.y = fused ? nullptr : a->out; p.weight = a->weight; p.bias = a->bias; p.init = a->conv_states;
   p.cu = a->query_start_loc; p.cu_dtype = a->qsl_dtype;
   p.cache_indices = a->cache_indices; p.idx_dtype = a->idx_dtype; p.has_init = a->has_initial_state;
   p.total = a->total_tokens; p.D = a->dim; p.nseq = a->batch;
-  p.sx = a->stride_x_token; p.sy = a->stride_o_token;
+  p.sx = a->stride_x_token; p.sy = fused ? a->dim : a->stride_o_token;
   p.st_seq = a->stride_state_seq; p.st_tok = a->stride_state_tok;
   p.pad_slot = a->pad_slot_id; p.null_block = a->null_block_id; p.has_null = a->has_null_block;
   p.fn_mode = 1; p.W = a->W; p.w_dtype = a->w_dtype; p.init_dtype = a->state_dtype; p.act = a->activation;
@@ -706,6 +663,47 @@ extern "C" GDN_API int gdn_causal_conv1d_fn(const gdn_conv1d_fn_args* a, void* s
     p.apc_init = a->initial_state_idx; p.apc_ncomp = a->num_computed_tokens;
     p.apc_dtype = a->apc_dtype; p.bsz = a->block_size_to_align;
   }
+  return GDN_OK;
+}
+
+}  // namespace conv
+
+int check_conv_fn_args(const gdn_conv1d_fn_args* a) {
+  conv::FwdParams p;
+  return conv::fn_params(a, p, true);
+}
+
+// The cache-line update of causal_conv1d_fn alone (conv_state_kernel), for
+// the prefill that applied the conv itself; runs after every reader of the
+// initial lines.
+cudaError_t launch_conv_fn_states(const gdn_conv1d_fn_args& a, cudaStream_t s) {
+  conv::FwdParams p;
+  if (conv::fn_params(&a, p, true) != GDN_OK) return cudaErrorInvalidValue;
+  if (p.total == 0 || p.nseq == 0) return cudaSuccess;
+  const int vec = 16 / conv::esize(a.x_dtype);
+  const bool v = p.D % vec == 0 && p.sx % vec == 0 && conv::aligned16(p.x);
+  const dim3 g2(static_cast<unsigned>(p.nseq),
+                static_cast<unsigned>((p.D + (v ? vec : 1) * conv::kThreads - 1) / ((v ? vec : 1) * conv::kThreads)));
+  note_launch();
+  if (a.x_dtype == GDN_F16) {
+    if (v) conv::conv_state_kernel<__half, 8><<<g2, conv::kThreads, 0, s>>>(p);
+    else conv::conv_state_kernel<__half, 1><<<g2, conv::kThreads, 0, s>>>(p);
+  } else if (a.x_dtype == GDN_BF16) {
+    if (v) conv::conv_state_kernel<__nv_bfloat16, 8><<<g2, conv::kThreads, 0, s>>>(p);
+    else conv::conv_state_kernel<__nv_bfloat16, 1><<<g2, conv::kThreads, 0, s>>>(p);
+  } else {
+    if (v) conv::conv_state_kernel<float, 4><<<g2, conv::kThreads, 0, s>>>(p);
+    else conv::conv_state_kernel<float, 1><<<g2, conv::kThreads, 0, s>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace gdn
+
+extern "C" GDN_API int gdn_causal_conv1d_fn(const gdn_conv1d_fn_args* a, void* stream) {
+  FwdParams p;
+  const int rc = fn_params(a, p, false);
+  if (rc != GDN_OK) return rc;
   if (p.total == 0 || p.nseq == 0) return GDN_OK;
   cudaError_t e = dispatch_fwd(p, a->x_dtype, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(GDN_ERR_CUDA, "gdn_causal_conv1d_fn: %s", cudaGetErrorString(e));

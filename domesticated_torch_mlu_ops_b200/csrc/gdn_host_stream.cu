@@ -146,6 +146,8 @@ int check_args(const gdn_chunk_args* a, int64_t seg) {
   if (seg <= 0 || seg % 64)
     return gdn::set_last_error(GDN_ERR_INVALID, "segment_tokens=%lld must be a positive multiple of 64",
                                (long long)seg);
+  if (a->q_token_stride || a->k_token_stride || a->v_token_stride)
+    return gdn::set_last_error(GDN_ERR_UNSUPPORTED, "the host-memory prefill takes packed q/k/v rows");
   gdn_chunk_args c = *a;  // shape and dtype checks of the device entry point
   if (gdn_chunk_workspace_size(&c) == 0) return GDN_ERR_INVALID;
   return GDN_OK;

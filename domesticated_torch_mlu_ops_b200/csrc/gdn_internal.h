@@ -77,8 +77,16 @@ cudaError_t launch_chunk_bwd(const gdn_chunk_bwd_args& a, const BwdWorkspace& ws
 // stall_chunk >= 0: test hook of gdn_chunk_fwd_test_stall (the first state
 // block skips that chunk's operand fetch; its waits give up after stall_limit).
 cudaError_t launch_chunk_h_stage(const gdn_chunk_h_args& a, cudaStream_t s);
+// conv non-null: the causal conv1d of causal_conv1d_fn (W = 4, 16-bit data,
+// conv_states of the same dtype) is applied to conv->x as the tiles are
+// loaded; a.q/a.k/a.v are not read, and the cache lines are updated after the
+// prefill kernels (launch_conv_fn_states).
 cudaError_t launch_chunk_tc(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk = -1,
-                            long long stall_limit = 0);
+                            long long stall_limit = 0, const gdn_conv1d_fn_args* conv = nullptr);
+size_t tc_conv_workspace_bytes(const gdn_chunk_args& a);
+// causal_conv1d_fn's argument checks for the fused prefill (no `out`).
+int check_conv_fn_args(const gdn_conv1d_fn_args* a);
+cudaError_t launch_conv_fn_states(const gdn_conv1d_fn_args& a, cudaStream_t s);
 cudaError_t launch_solve_tril(const float* A, void* out, int out_dtype, const void* cu,
                               int cu_dtype, int64_t N, int64_t B, int64_t T, int H, int BT,
                               cudaStream_t s);

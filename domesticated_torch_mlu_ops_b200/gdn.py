@@ -152,18 +152,38 @@ def _call(op, impl, *args):
 # torch.library custom ops (CUDA implementations call the C ABI)
 # ---------------------------------------------------------------------------
 
+def _rows(t):
+    """(tensor, token stride) of a [B, T, heads, d] input for the tensor-core
+    prefill: in place when only its token rows are strided (e.g. q, k, v as
+    views of one projection) and the stride suits the tensor maps, else a
+    packed copy with stride 0."""
+    if t.is_contiguous():
+        return t, 0
+    B, T, nh, d = t.shape
+    st = t.stride()
+    if (st[3] == 1 and st[2] == d and (B == 1 or st[0] == T * st[1]) and st[1] >= nh * d and st[1] % 8 == 0
+            and t.storage_offset() * t.element_size() % 16 == 0):
+        return t, st[1]
+    return t.contiguous(), 0
+
+
 def _chunk_fwd_impl(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, scale: float,
                   initial_state: Optional[Tensor], output_final_state: bool,
                   cu_seqlens: Optional[Tensor], state_v_first: bool, use_qk_l2norm: bool,
                   force_generic: bool, check_errors: bool) -> tuple[Tensor, Tensor]:
-    """Chunked prefill on prepared inputs (q/k/v contiguous in one dtype,
-    g/beta/initial_state fp32 contiguous, cu_seqlens int32/int64).  Returns
+    """Chunked prefill on prepared inputs (q/k/v in one dtype, packed or, on
+    the tensor-core path, with strided token rows; g/beta/initial_state fp32
+    contiguous, cu_seqlens int32/int64).  Returns
     ``(o, final_state)``; final_state is an empty tensor when not requested."""
     B, T, H, K = k.shape
     HV, V = v.shape[2], v.shape[3]
     N = B if cu_seqlens is None else cu_seqlens.numel() - 1
     dev = q.device
-    o = torch.empty_like(v, dtype=q.dtype)
+    if q.dtype in (torch.bfloat16, torch.float16) and K == 128 and V == 128 and not force_generic:
+        (q, sq), (k, sk), (v, sv) = _rows(q), _rows(k), _rows(v)  # the tensor-core path reads strided rows
+    else:
+        (q, sq), (k, sk), (v, sv) = (q.contiguous(), 0), (k.contiguous(), 0), (v.contiguous(), 0)
+    o = torch.empty(v.shape, dtype=q.dtype, device=dev)
     shape_state = (N, HV, V, K) if state_v_first else (N, HV, K, V)
     ht = torch.empty(shape_state, dtype=torch.float32, device=dev) if output_final_state else None
     args = _lib.ChunkArgs(
@@ -172,7 +192,7 @@ def _chunk_fwd_impl(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, sc
         workspace=None, workspace_bytes=0, B=B, T=T, N=N, H=H, HV=HV, K=K, V=V,
         qkv_dtype=_DT[q.dtype], cu_dtype=_IDT[cu_seqlens.dtype] if cu_seqlens is not None else _lib.GDN_I64,
         scale=float(scale), use_qk_l2norm=int(use_qk_l2norm), state_v_first=int(state_v_first),
-        force_generic=int(force_generic))
+        force_generic=int(force_generic), q_token_stride=sq, k_token_stride=sk, v_token_stride=sv)
     lib = _lib.load()
     nbytes = lib.gdn_chunk_workspace_size(ctypes.byref(args))
     if nbytes == 0:
@@ -525,7 +545,7 @@ def chunk_gated_delta_rule(
             use_qk_l2norm_in_kernel, force_generic, check_errors)
     cu = _chunk_prepare(q, k, v, g, beta, initial_state, cu_seqlens, state_v_first)
     o, ht = _call(
-        torch.ops.gdn_b200.chunk_fwd, _chunk_fwd_impl, q.contiguous(), k.contiguous(), v.contiguous(),
+        torch.ops.gdn_b200.chunk_fwd, _chunk_fwd_impl, q, k, v,
         _f32(g), _f32(beta), _scale(scale), _f32(initial_state), bool(output_final_state), cu, bool(state_v_first),
         bool(use_qk_l2norm_in_kernel), bool(force_generic), bool(check_errors))
     return o, (ht if output_final_state else None)

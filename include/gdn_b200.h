@@ -31,6 +31,10 @@
  *   gdn_causal_conv1d_fn   <- triton_ops.py:366-459 causal_conv1d_fn
  *                             -> triton/conv/ops.py:101-349 causal_conv1d_fwd_vllm
  *   gdn_causal_conv1d_update <- triton/conv/ops.py:584-644 causal_conv1d_update
+ *   gdn_conv_chunk_fwd     <- no single reference counterpart: causal_conv1d_fn
+ *                             (triton_ops.py:366-459) followed by chunk_gated_delta_rule
+ *                             (triton_ops.py:81-165) on the conv output's q/k/v split,
+ *                             as the GDN layer calls them, in one pass
  */
 #ifndef GDN_B200_H_
 #define GDN_B200_H_
@@ -42,7 +46,7 @@
 extern "C" {
 #endif
 
-#define GDN_ABI_VERSION 2
+#define GDN_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define GDN_API __attribute__((visibility("default")))
@@ -100,6 +104,13 @@ typedef struct gdn_chunk_args {
    * (recording stops when the array runs out).  NULL for normal use. */
   void* const* stage_events;
   int32_t n_stage_events;
+  /* Token (row) strides of q, k and v in elements; 0 means packed (H*K,
+   * H*K, HV*V).  Within a row the heads stay packed (unit stride over K, K
+   * between heads), so q, k and v may be views of one [T, 2*H*K + HV*V]
+   * projection.  Strided rows are read in place by the tensor-core path
+   * (strides >= the packed width and multiples of 8); the other paths and
+   * gdn_chunk_fwd_host take packed rows only. */
+  int64_t q_token_stride, k_token_stride, v_token_stride;
 } gdn_chunk_args;
 
 /* Workspace bytes gdn_chunk_fwd needs for these arguments (pointer fields
@@ -466,6 +477,25 @@ typedef struct gdn_conv1d_update_args {
   int32_t activation;
 } gdn_conv1d_update_args;
 GDN_API int gdn_causal_conv1d_update(const gdn_conv1d_update_args* args, void* stream);
+
+/* Causal conv1d fused into the chunked prefill (no single reference
+ * counterpart).  Computes what causal_conv1d_fn(x, ...) followed by
+ * gdn_chunk_fwd on the q/k/v split of its output computes, bit for bit,
+ * without writing the conv output: the prefill's WY kernel applies the conv
+ * (and SiLU) to x as it loads its q, k and v tiles.
+ *   args: as for gdn_chunk_fwd, except that q, k and v are not read (the
+ *     conv output supplies them); bf16/f16 with K = V = 128, a packed batch
+ *     (B = 1, cu_seqlens), workspace of gdn_conv_chunk_workspace_size bytes;
+ *   conv: as for gdn_causal_conv1d_fn with out = NULL; x holds, per token,
+ *     dim = 2*H*K + HV*V channels [q heads | k heads | v heads]; W = 4; x,
+ *     weight, bias and conv_states in the q/k/v dtype; x, its token stride,
+ *     weight and bias 16-byte aligned; query_start_loc describes the same
+ *     sequences as args->cu_seqlens (batch = N, total_tokens = T).
+ * conv_states is updated like causal_conv1d_fn updates it (after the prefill
+ * kernels have read the initial lines); PAD / null-block sequences get zero
+ * conv outputs and keep their lines. */
+GDN_API size_t gdn_conv_chunk_workspace_size(const gdn_chunk_args* args);
+GDN_API int gdn_conv_chunk_fwd(const gdn_chunk_args* args, const gdn_conv1d_fn_args* conv, void* stream);
 
 /* Message for the last failing call on this thread ("" if none). */
 GDN_API const char* gdn_last_error(void);

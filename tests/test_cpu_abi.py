@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.load()
     for name in _declared():
         assert hasattr(lib, name), name
-    assert lib.gdn_abi_version() == 2
+    assert lib.gdn_abi_version() == 3
     out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
                          text=True).stdout
     exported = {l.split()[-1] for l in out.splitlines() if " T " in l}
@@ -82,6 +82,39 @@ def test_workspace_size_and_validation():
     a = _chunk_args(B=2, N=3)
     a.cu_seqlens = ctypes.c_void_p(16)
     assert lib.gdn_chunk_workspace_size(ctypes.byref(a)) == 0
+
+
+def test_token_stride_validation():
+    lib = _lib.load()
+    # strided rows on the tensor-core path: multiples of 8 at least the packed width
+    assert lib.gdn_chunk_workspace_size(ctypes.byref(_chunk_args(q_token_stride=8192, k_token_stride=8192,
+                                                                 v_token_stride=8192))) > 0
+    assert lib.gdn_chunk_workspace_size(ctypes.byref(_chunk_args(q_token_stride=2047))) == 0
+    assert b"token strides" in lib.gdn_last_error()
+    assert lib.gdn_chunk_workspace_size(ctypes.byref(_chunk_args(v_token_stride=2048))) == 0  # < HV*V
+    # other paths read packed rows only
+    assert lib.gdn_chunk_workspace_size(ctypes.byref(_chunk_args(q_token_stride=4096, force_generic=1))) == 0
+    assert lib.gdn_chunk_workspace_size(ctypes.byref(_chunk_args(qkv_dtype=_lib.GDN_F32,
+                                                                 q_token_stride=4096))) == 0
+    assert b"tensor-core path only" in lib.gdn_last_error()
+    assert lib.gdn_chunk_fwd_host_buffer_size(ctypes.byref(_chunk_args(q_token_stride=4096)), 2048) == 0
+    # the fused conv prefill: width 4 only, no conv output tensor
+    f = _lib.Conv1dFnArgs(x=ctypes.c_void_p(256), weight=ctypes.c_void_p(256), conv_states=ctypes.c_void_p(256),
+                          query_start_loc=ctypes.c_void_p(256), stride_x_token=8192, stride_state_seq=3 * 8192,
+                          stride_state_tok=8192, num_cache_lines=4, batch=1, dim=8192, total_tokens=8192, W=3,
+                          x_dtype=_lib.GDN_BF16, w_dtype=_lib.GDN_BF16, state_dtype=_lib.GDN_BF16,
+                          qsl_dtype=_lib.GDN_I32, activation=_lib.GDN_ACT_SILU)
+    a = _chunk_args(g=ctypes.c_void_p(256), beta=ctypes.c_void_p(256), o=ctypes.c_void_p(256),
+                    cu_seqlens=ctypes.c_void_p(256), cu_dtype=_lib.GDN_I32)
+    assert lib.gdn_conv_chunk_workspace_size(ctypes.byref(a)) > lib.gdn_chunk_workspace_size(ctypes.byref(a))
+    assert lib.gdn_conv_chunk_fwd(ctypes.byref(a), ctypes.byref(f), None) == _lib.GDN_ERR_UNSUPPORTED
+    f.W = 4
+    f.out = ctypes.c_void_p(256)
+    assert lib.gdn_conv_chunk_fwd(ctypes.byref(a), ctypes.byref(f), None) == _lib.GDN_ERR_INVALID
+    f.out = None
+    f.dim = 8192 - 128
+    assert lib.gdn_conv_chunk_fwd(ctypes.byref(a), ctypes.byref(f), None) == _lib.GDN_ERR_INVALID
+    assert b"2*H*K + HV*V" in lib.gdn_last_error()
 
 
 def test_invalid_calls_return_codes_without_touching_the_gpu():

@@ -77,3 +77,19 @@ def test_ops_reject_cpu_tensors():
     q = torch.zeros(1, 4, 2, 16)
     with pytest.raises(ValueError, match="CUDA"):
         ops.chunk_gated_delta_rule(q, q, q, q[..., 0], q[..., 0])
+
+
+def test_conv_prefill_fake_shapes():
+    assert "Tensor(a3!) conv_states" in str(torch.ops.gdn_b200.conv_chunk_fwd.default._schema)
+    with FakeTensorMode():
+        H, HV, T = 2, 4, 300
+        dim = 2 * H * 128 + HV * 128
+        x = torch.empty(T, dim, dtype=torch.bfloat16, device="cuda").t()
+        w = torch.empty(dim, 4, dtype=torch.bfloat16, device="cuda")
+        st = torch.empty(5, 3, dim, dtype=torch.bfloat16, device="cuda").transpose(1, 2)
+        qsl = torch.tensor([0, 100, 300], dtype=torch.int32, device="cuda")
+        g = torch.empty(1, T, HV, device="cuda")
+        o, ht = ops.causal_conv1d_chunk_gated_delta_rule(x, w, None, st, qsl, g, g, H, HV,
+                                                         output_final_state=True)
+        assert o.shape == (1, T, HV, 128) and o.dtype == torch.bfloat16
+        assert ht.shape == (2, HV, 128, 128) and ht.dtype == torch.float32

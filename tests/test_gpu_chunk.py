@@ -248,3 +248,26 @@ def test_fused_kernel_matches_split_kernels(ops, case, monkeypatch):
     for o_, h_ in ((of, hf), (os_, hs)):
         assert rel_rms(np64(o_), ro) < BF16_REL_RMS and max_abs(np64(o_), ro) < BF16_MAX_ABS
         assert rel_rms(np64(h_), rht) < BF16_REL_RMS
+
+
+def test_strided_rows_are_read_in_place(ops):
+    """q, k, v as views of one [T, 2*H*K + HV*V] projection (token rows
+    strided, heads packed): the tensor-core path reads them through its
+    tensor maps without copies, with the results of packed inputs."""
+    from domesticated_torch_mlu_ops_b200 import _lib
+    lib = _lib.load()
+    H, HV, T = 4, 8, 300
+    q0, k0, v0, g, beta, h0 = make_inputs(31, 1, T, H, HV, 128, 128, nseq_state=2, state_std=0.05)
+    mixed = torch.cat([q0.reshape(T, -1), k0.reshape(T, -1), v0.reshape(T, -1)], dim=1)
+    q = mixed[:, :H * 128].view(1, T, H, 128)
+    k = mixed[:, H * 128:2 * H * 128].view(1, T, H, 128)
+    v = mixed[:, 2 * H * 128:].view(1, T, HV, 128)
+    assert not q.is_contiguous() and not v.is_contiguous()
+    cu = torch.tensor([0, 100, T], device="cuda")
+    ref = ops.chunk_gated_delta_rule(q0, k0, v0, g, beta, None, h0, True, cu, use_qk_l2norm_in_kernel=True)
+    torch.cuda.synchronize()
+    n0 = lib.gdn_kernel_launch_count()
+    out = ops.chunk_gated_delta_rule(q, k, v, g, beta, None, h0, True, cu, use_qk_l2norm_in_kernel=True)
+    torch.cuda.synchronize()
+    assert lib.gdn_kernel_launch_count() - n0 == 3  # plan, WY, state: no copy kernels of this library either
+    assert torch.equal(out[0], ref[0]) and torch.equal(out[1], ref[1])
