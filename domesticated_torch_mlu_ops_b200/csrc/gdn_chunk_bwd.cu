@@ -31,6 +31,7 @@
 
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
+#include "gdn_chunk_tc.cuh"
 #include "tile_gemm.cuh"
 #include "solve_tril.cuh"
 
@@ -571,12 +572,32 @@ gdn_chunk_args forward_args(const gdn_chunk_bwd_args& b) {
   return a;
 }
 
+// bf16/fp16 with K = V = 128: the state-gradient recurrence runs on tcgen05
+// (gdn_chunk_bwd_tc.cu) from the forward WY kernel's images.
+bool bwd_tc_applies(const gdn_chunk_bwd_args& b) {
+  return (b.qkv_dtype == GDN_BF16 || b.qkv_dtype == GDN_F16) && b.K == 128 && b.V == 128 &&
+         b.B * b.T < (int64_t(1) << 31);
+}
+
 template <typename T>
 cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStream_t s) {
   const gdn_chunk_args a = forward_args(b);
-  cudaError_t e = launch_chunk_generic_recompute(a, ws.fwd, s);
+  const bool tcb = bwd_tc_applies(b);
+  // with the tensor-core path, the states and v_new come from the forward's
+  // own kernels (tcgen05, bf16 roundings as in the forward); otherwise from
+  // the generic fp32 recompute
+  cudaError_t e = launch_chunk_generic_recompute(a, ws.fwd, s, !tcb);
   if (e != cudaSuccess) return e;
   char* base = static_cast<char*>(b.workspace);
+  tc::Work tw{};
+  if (tcb) {
+    gdn_chunk_args fa = a;
+    fa.force_generic = 0;
+    if ((e = tc::launch_wy_only(fa, base + ws.tc, s, tw)) != cudaSuccess) return e;
+    if ((e = tc::launch_state_store(fa, tw, reinterpret_cast<float*>(base + ws.fwd.hs),
+                                    reinterpret_cast<float*>(base + ws.fwd.vnew), s)) != cudaSuccess)
+      return e;
+  }
   BwdPtrs w;
   w.coff = reinterpret_cast<const int64_t*>(base + ws.fwd.chunk_offsets);
   w.gc = reinterpret_cast<const float*>(base + ws.fwd.gc);
@@ -607,10 +628,14 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
     bwd_dvlocal_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kDvlSmem, s>>>(b, w, scale);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  note_launch();
-  bwd_state_kernel<T><<<dim3(static_cast<unsigned>(b.N), b.HV, (b.V + kVS - 1) / kVS), kT, kStateSmem, s>>>(
-      b, w, scale);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (tcb) {
+    if ((e = tc::launch_bwd_state_tc(b, tw, w.dvn, w.dhn, s)) != cudaSuccess) return e;
+  } else {
+    note_launch();
+    bwd_state_kernel<T><<<dim3(static_cast<unsigned>(b.N), b.HV, (b.V + kVS - 1) / kVS), kT, kStateSmem, s>>>(
+        b, w, scale);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
   if (nc > 0) {
     note_launch(2);
     bwd_dqkw_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kDqkwSmem, s>>>(b, w, scale);
@@ -643,6 +668,12 @@ BwdWorkspace plan_bwd_workspace(const gdn_chunk_bwd_args& b) {
   w.dkh = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
   w.dw = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
   w.dG = o; o += al(sizeof(float) * Ttot * b.HV);
+  w.tc = o;
+  if (bwd_tc_applies(b)) {
+    gdn_chunk_args fa = forward_args(b);
+    fa.force_generic = 0;
+    o += al(tc_workspace_bytes(fa) + 1024);  // the tensor-core layout aligns its regions to 1 KiB
+  }
   w.total = o;
   return w;
 }

@@ -1,0 +1,374 @@
+// Tensor-core (tcgen05) state-gradient recurrence of the GDN backward for
+// bf16/fp16 inputs with K = V = 128: chunk_gated_delta_rule_bwd_dhu
+// (triton/fla/chunk_delta_h.py:273-581, called from chunk.py:76-186).
+//
+// Per (sequence, v-head, 32-column V-slice), over the chunks in reverse,
+// with dh' the gradient of the state after the chunk (fp32, registers):
+//   X   = [K; Q] dh~                         (tcgen05, M = 128; rows 0..63 used)
+//   dv  = dv_local + diag(b) X               (b_i = exp(G_L - G_i) r_k,i; rows past the end: 0)
+//   dH  = Q^T diag(a) dO + W^T (-dv)         (tcgen05, M = 128, two products in one accumulator)
+//   dh  = gamma dh' + dH
+// where dh~ is dh' rounded to the input dtype, a_i = scale exp(G_i) r_q,i and
+// gamma = exp(G_L): the row scales the forward WY kernel writes, whose W
+// images (L2 norm and gates folded in) this kernel reads.  q, k, dO and
+// dv_local come in by TMA.  Every chunk stores dv (fp32, completing the
+// dv_local the previous kernel wrote) and dh' (fp32) for the remaining
+// backward kernels; dh at the first chunk is dh0.  The bf16 roundings are the
+// reference's: dh and dv are cast to the input dtype before their products.
+//
+// Warp roles as in the forward state kernel: warp 0 issues the MMAs, warps
+// 0,1,4,5 form dv (rows 0..63), warps 2,3,6,7 build the diag(a) dO image
+// while the first product runs, all eight update dh, and a ninth warp
+// streams the chunks ahead into three stages.  Every wait is bounded; on a
+// timeout the kernel records an error, drains its copies and MMAs (bounded)
+// and exits.
+
+#include <cuda.h>
+
+#include <type_traits>
+
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+#include "gdn_chunk_tc.cuh"
+#include "umma.cuh"
+
+namespace gdn {
+namespace tc {
+
+namespace {
+
+struct BwdSt {
+  static constexpr int VS = 32;
+  // stage: K a0 | Q a0 | K a1 | Q a1 | W a0 | W a1 | dO [64][VS] | dv_local [64][VS] fp32 | scalars
+  static constexpr int kKQ = 0;
+  static constexpr int kW = 4 * kAtom;
+  static constexpr int kDO = kW + 2 * kAtom;
+  static constexpr int kDvl = kDO + 64 * VS * 2;
+  static constexpr int kSc = kDvl + 64 * VS * 4;
+  static constexpr int kStage = ((kSc + kScal * 4 + 1023) / 1024) * 1024;
+  static constexpr uint32_t kTx = 6 * kAtom + 64 * VS * 2 + 64 * VS * 4 + kScal * 4;
+  static constexpr int kStages = 3;
+  static constexpr int kH = kStages * kStage;       // dh~ image 128 x VS
+  static constexpr int kDo = kH + D * VS * 2;       // diag(a) dO image 64 x VS
+  static constexpr int kMdv = kDo + 64 * VS * 2;    // -dv image 64 x VS
+  static constexpr int kBar = kMdv + 64 * VS * 2;   // full[kStages], mma1, mma2
+  static constexpr int kTmem = kBar + (kStages + 2) * 8;
+  static constexpr int kBytes = kTmem + 8 + 1024;
+  static constexpr int kAcc = 0, kDH = VS, kCols = 64;  // TMEM columns
+  static_assert(kDO % 128 == 0 && kDvl % 128 == 0, "TMA destinations");
+  static_assert(kBytes <= 227 * 1024, "shared memory");
+};
+
+struct BwdOut {
+  float* dvn;  // [Ttot][HV][V]: dv_local in, dv out
+  float* dhn;  // [chunks][HV][K][V]: dh' of every chunk
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kSt3Threads, 1)
+tc_bwd_state_kernel(const gdn_chunk_bwd_args p, const Work w, const BwdOut o,
+                    const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tdo, const __grid_constant__ CUtensorMap tdv) {
+  using S = BwdSt;
+  constexpr int VS = S::VS;
+  constexpr int RSV = (VS / 8) * 128;
+  constexpr int CW = VS / 2;  // columns per thread
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* himg = sm + S::kH;
+  uint8_t* doimg = sm + S::kDo;
+  uint8_t* mdvimg = sm + S::kMdv;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::kTmem);
+  const uint32_t bar_mma1 = umma::smem_u32(bars + S::kStages), bar_mma2 = umma::smem_u32(bars + S::kStages + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool producer = warp == 8;
+  const int quad = warp & 3, colh = (warp >> 2) & 1;
+  const int row = quad * 32 + lane;
+  constexpr int kSlices = D / VS;
+  const int64_t n = blockIdx.x / kSlices;
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  const int v0 = static_cast<int>(blockIdx.x % kSlices) * VS;
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int nch = static_cast<int>(eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0);
+  const int64_t c0 = w.coff[n];
+  // iteration j works on chunk nch - 1 - j
+  auto stage = [&](int j) { return sm + (j % S::kStages) * S::kStage; };
+  auto full = [&](int j) { return umma::smem_u32(bars + j % S::kStages); };
+  const long long wlim = 2000000000LL;
+  int fetched[S::kStages];
+#pragma unroll
+  for (int i = 0; i < S::kStages; ++i) fetched[i] = -1;
+
+  auto fetch = [&](int j) {  // one thread
+    fetched[j % S::kStages] = j;
+    const int c = nch - 1 - j;
+    uint8_t* b = stage(j);
+    const uint32_t bar = full(j);
+    const int s = static_cast<int>(bos + static_cast<int64_t>(c) * kChunk);
+    const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c0 + c;
+    const uint8_t* wsrc = w.wimg + hc * kImg64x128;
+    umma::mbar_arrive_expect_tx(bar, S::kTx);
+    umma::tma_load_3d(b + S::kKQ, &tk, 0, h, s, bar);
+    umma::tma_load_3d(b + S::kKQ + kAtom, &tq, 0, h, s, bar);
+    umma::tma_load_3d(b + S::kKQ + 2 * kAtom, &tk, 64, h, s, bar);
+    umma::tma_load_3d(b + S::kKQ + 3 * kAtom, &tq, 64, h, s, bar);
+    umma::bulk_g2s(b + S::kW, wsrc, kAtom, bar);
+    umma::bulk_g2s(b + S::kW + kAtom, wsrc + kAtom, kAtom, bar);
+    umma::tma_load_3d(b + S::kDO, &tdo, v0, hv, s, bar);
+    umma::tma_load_3d(b + S::kDvl, &tdv, v0, hv, s, bar);
+    umma::bulk_g2s(b + S::kSc, w.scal + hc * kScal, kScal * 4, bar);
+  };
+
+  if (tid == 256) {
+    for (int i = 0; i < S::kStages + 2; ++i) umma::mbar_init(bars + i, 1);
+    umma::mbar_fence_init();
+    for (int j = 0; j < S::kStages - 1 && j < nch; ++j) fetch(j);
+  }
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, S::kCols);
+    umma::fence_before_sync();
+  }
+  // dh' slice: thread `row` owns dh[row][v0 + colh*CW .. +CW] in fp32
+  float hreg[CW];
+  if (!producer) {
+    const int64_t base = (n * p.HV + hv) * D * D;
+#pragma unroll
+    for (int jj = 0; jj < CW; ++jj) {
+      const int col = v0 + colh * CW + jj;
+      hreg[jj] = !p.dht ? 0.f
+                 : p.state_v_first ? p.dht[base + static_cast<int64_t>(col) * D + row]
+                                   : p.dht[base + static_cast<int64_t>(row) * D + col];
+    }
+#pragma unroll
+    for (int j8 = 0; j8 < CW / 8; ++j8)
+      *reinterpret_cast<uint4*>(himg + umma::img_off(row, colh * CW + j8 * 8, RSV)) = pack8<T>(hreg + j8 * 8);
+  }
+  umma::fence_proxy_async();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+  const uint32_t t_acc = tmem + S::kAcc, t_dh = tmem + S::kDH;
+  constexpr bool kBf16 = !std::is_same<T, __half>::value;
+  const uint32_t id_x = umma::idesc_f16(128, VS, kBf16, false, true);   // A K-major, B MN-major
+  const uint32_t id_dh = umma::idesc_f16(128, VS, kBf16, true, true);   // A MN-major (transposed tiles)
+  const uint64_t d_h = umma::smem_desc(umma::smem_u32(himg), RSV, 128);
+  const uint64_t d_do = umma::smem_desc(umma::smem_u32(doimg), RSV, 128);
+  const uint64_t d_mdv = umma::smem_desc(umma::smem_u32(mdvimg), RSV, 128);
+  const int64_t rowV = static_cast<int64_t>(p.HV) * D;
+
+  bool ok = true, mine = true;
+  uint32_t last_bar = 0, last_par = 0;
+  if (producer && nch > 0) {
+    mine = umma::mbar_wait(full(0), 0, wlim);
+    if (!mine) record_error(w.err, 1, kSiteStLoad);
+  }
+  for (int j = 0; j < nch; ++j) {
+    if (__syncthreads_or(!mine)) { ok = false; break; }
+    umma::fence_after_sync();
+    const int c = nch - 1 - j;
+    const int64_t s = bos + static_cast<int64_t>(c) * kChunk;
+    const int L = static_cast<int>(min64(kChunk, eos - s));
+    uint8_t* b = stage(j);
+    const float* sc = reinterpret_cast<const float*>(b + S::kSc);
+    if (warp == 0) {  // MMA1: X = [K; Q] dh~
+      if (umma::elect_one()) {
+        const uint64_t da = umma::smem_desc_sw128(umma::smem_u32(b + S::kKQ), 16, 1024);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          umma::mma_f16(t_acc, da + (((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4), d_h + ((ks * 2 * RSV) >> 4),
+                        id_x, ks > 0);
+        umma::mma_commit(bar_mma1);
+      }
+      __syncwarp();
+      last_bar = bar_mma1;
+      last_par = static_cast<uint32_t>(j & 1);
+    }
+    if (producer) {
+      // iteration j + kStages - 1 goes where iteration j - 1 was: its products must be done
+      if (j >= 1) {
+        mine = umma::mbar_wait(bar_mma2, static_cast<uint32_t>((j - 1) & 1), wlim);
+        if (!mine) record_error(w.err, 1, kSiteStMma2);
+      }
+      if (mine && j + S::kStages - 1 < nch && lane == 0) fetch(j + S::kStages - 1);
+      __syncwarp();
+      if (mine && j + 1 < nch) {
+        mine = umma::mbar_wait(full(j + 1), static_cast<uint32_t>(((j + 1) / S::kStages) & 1), wlim);
+        if (!mine) record_error(w.err, 1, kSiteStLoad);
+      }
+      continue;
+    }
+    if (quad >= 2) {  // diag(a) dO image (rows 0..63), off the chain
+      const int i = row - 64;
+      const float ai = sc[i];  // zero past the sequence end
+      const T* dor = reinterpret_cast<const T*>(b + S::kDO) + i * VS + colh * CW;
+#pragma unroll
+      for (int j8 = 0; j8 < CW / 8; ++j8) {
+        float x[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(dor + j8 * 8), x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] *= ai;
+        *reinterpret_cast<uint4*>(doimg + umma::img_off(i, colh * CW + j8 * 8, RSV)) = pack8<T>(x);
+      }
+    } else {  // dv (rows 0..63)
+      const int i = row;
+      const float bi = sc[64 + i];
+      const float* dl = reinterpret_cast<const float*>(b + S::kDvl) + i * VS + colh * CW;
+      float dv[CW];
+#pragma unroll
+      for (int j4 = 0; j4 < CW / 4; ++j4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(dl + j4 * 4);
+        dv[j4 * 4] = v4.x;
+        dv[j4 * 4 + 1] = v4.y;
+        dv[j4 * 4 + 2] = v4.z;
+        dv[j4 * 4 + 3] = v4.w;
+      }
+      mine = umma::mbar_wait(bar_mma1, static_cast<uint32_t>(j & 1), wlim);
+      if (!mine) record_error(w.err, 1, kSiteStMma1);
+      umma::fence_after_sync();
+      uint32_t rx[CW];
+#pragma unroll
+      for (int q = 0; q < CW / 16; ++q) umma::tmem_ld16_nw(t_acc + lane_base + colh * CW + q * 16, rx + q * 16);
+      umma::tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < CW / 16; ++q) umma::reg_fence16(rx + q * 16);
+      const bool live = i < L;
+#pragma unroll
+      for (int e = 0; e < CW; ++e) dv[e] = live ? fmaf(bi, __uint_as_float(rx[e]), dv[e]) : 0.f;
+#pragma unroll
+      for (int j8 = 0; j8 < CW / 8; ++j8) {
+        float m[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m[e] = -dv[j8 * 8 + e];
+        *reinterpret_cast<uint4*>(mdvimg + umma::img_off(i, colh * CW + j8 * 8, RSV)) = pack8<T>(m);
+      }
+      if (live) {
+        float* dst = o.dvn + (s + i) * rowV + static_cast<int64_t>(hv) * D + v0 + colh * CW;
+#pragma unroll
+        for (int j4 = 0; j4 < CW / 4; ++j4)
+          *reinterpret_cast<float4*>(dst + j4 * 4) =
+              make_float4(dv[j4 * 4], dv[j4 * 4 + 1], dv[j4 * 4 + 2], dv[j4 * 4 + 3]);
+      }
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    umma::named_sync(1, 256);  // both images are in place
+    if (warp == 0) {  // MMA2: dH = Q^T diag(a) dO + W^T (-dv)
+      umma::fence_after_sync();
+      if (umma::elect_one()) {
+        const uint64_t dq = umma::smem_desc_sw128(umma::smem_u32(b + S::kKQ + kAtom), 2 * kAtom, 1024);
+#pragma unroll
+        for (int ks = 0; ks < 64 / 16; ++ks)
+          umma::mma_f16(t_dh, dq + ((ks * 2048) >> 4), d_do + ((ks * 2 * RSV) >> 4), id_dh, ks > 0);
+        const uint64_t dw = umma::smem_desc_sw128(umma::smem_u32(b + S::kW), kAtom, 1024);
+#pragma unroll
+        for (int ks = 0; ks < 64 / 16; ++ks)
+          umma::mma_f16(t_dh, dw + ((ks * 2048) >> 4), d_mdv + ((ks * 2 * RSV) >> 4), id_dh, true);
+        umma::mma_commit(bar_mma2);
+      }
+      __syncwarp();
+      last_bar = bar_mma2;
+      last_par = static_cast<uint32_t>(j & 1);
+    }
+    // dh <- gamma dh' + dH (rows 0..127), its image for the next chunk, and dh' out
+    if (mine) {
+      mine = umma::mbar_wait(bar_mma2, static_cast<uint32_t>(j & 1), wlim);
+      if (!mine) record_error(w.err, 1, kSiteStMma2);
+    }
+    umma::fence_after_sync();
+    if (mine) {
+      float d[CW];
+#pragma unroll
+      for (int q = 0; q < CW / 16; ++q) umma::tmem_ld16(t_dh + lane_base + colh * CW + q * 16, d + q * 16);
+      const float g = sc[128];
+#pragma unroll
+      for (int e = 0; e < CW; ++e) d[e] = fmaf(g, hreg[e], d[e]);
+      if (j + 1 < nch) {
+#pragma unroll
+        for (int j8 = 0; j8 < CW / 8; ++j8)
+          *reinterpret_cast<uint4*>(himg + umma::img_off(row, colh * CW + j8 * 8, RSV)) = pack8<T>(d + j8 * 8);
+      }
+      float* dst = o.dhn + ((c0 + c) * p.HV + hv) * static_cast<int64_t>(D) * D + static_cast<int64_t>(row) * D + v0 +
+                   colh * CW;
+#pragma unroll
+      for (int j4 = 0; j4 < CW / 4; ++j4)
+        *reinterpret_cast<float4*>(dst + j4 * 4) =
+            make_float4(hreg[j4 * 4], hreg[j4 * 4 + 1], hreg[j4 * 4 + 2], hreg[j4 * 4 + 3]);
+#pragma unroll
+      for (int e = 0; e < CW; ++e) hreg[e] = d[e];
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+  }
+  if (ok) ok = !__syncthreads_or(!mine);
+  if (ok && !producer && p.dh0) {
+    const int64_t base = (n * p.HV + hv) * D * D;
+#pragma unroll
+    for (int jj = 0; jj < CW; ++jj) {
+      const int col = v0 + colh * CW + jj;
+      if (p.state_v_first) p.dh0[base + static_cast<int64_t>(col) * D + row] = hreg[jj];
+      else p.dh0[base + static_cast<int64_t>(row) * D + col] = hreg[jj];
+    }
+  }
+  if (!ok) {  // drain (bounded) this CTA's copies and products before its memory is released
+    const long long drain = 20000000LL;
+    if (tid == 256)
+      for (int x = 0; x < S::kStages; ++x)
+        if (fetched[x] >= 0)
+          umma::mbar_wait(full(fetched[x]), static_cast<uint32_t>((fetched[x] / S::kStages) & 1), drain);
+    if (warp == 0 && last_bar) umma::mbar_wait(last_bar, last_par, drain);
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, S::kCols);
+}
+
+// [Ttot, HV, 128] tensor with 32-column x 1 head x 64-token boxes, no swizzle.
+cudaError_t make_slice_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, CUtensorMapDataType dt,
+                           int esize) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(heads),
+                              static_cast<cuuint64_t>(ttot)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * esize, static_cast<cuuint64_t>(heads) * D * esize};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(BwdSt::VS), 1, 64};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <typename T>
+cudaError_t launch_t(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, float* dhn, cudaStream_t s) {
+  constexpr bool kF16 = std::is_same<T, __half>::value;
+  const int64_t ttot = b.B * b.T;
+  CUtensorMap tq, tk, tdo, tdv;
+  cudaError_t e;
+  if ((e = make_map(&tq, b.q, b.H, ttot, kF16)) != cudaSuccess) return e;
+  if ((e = make_map(&tk, b.k, b.H, ttot, kF16)) != cudaSuccess) return e;
+  if ((e = make_slice_map(&tdo, b.dout, b.HV, ttot,
+                          kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2)) != cudaSuccess)
+    return e;
+  if ((e = make_slice_map(&tdv, dvn, b.HV, ttot, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4)) != cudaSuccess) return e;
+  auto kern = tc_bwd_state_kernel<T>;
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSt::kBytes)) != cudaSuccess)
+    return e;
+  note_launch();
+  kern<<<dim3(static_cast<unsigned>(b.N * (D / BwdSt::VS)), b.HV), kSt3Threads, BwdSt::kBytes, s>>>(
+      b, w, BwdOut{dvn, dhn}, tq, tk, tdo, tdv);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_bwd_state_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, float* dhn,
+                                cudaStream_t s) {
+  return b.qkv_dtype == GDN_F16 ? launch_t<__half>(b, w, dvn, dhn, s)
+                                : launch_t<__nv_bfloat16>(b, w, dvn, dhn, s);
+}
+
+}  // namespace tc
+}  // namespace gdn

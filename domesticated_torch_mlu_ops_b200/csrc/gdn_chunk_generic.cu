@@ -331,7 +331,7 @@ ChunkWorkspace plan_generic_workspace(const gdn_chunk_args& a) {
 
 template <typename T>
 static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s,
-                               bool with_output) {
+                               bool with_output, bool with_state = true) {
   char* base = static_cast<char*>(a.workspace);
   GenericPtrs w;
   w.coff = reinterpret_cast<const int64_t*>(base + ws.chunk_offsets);
@@ -376,6 +376,7 @@ static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws
     chunk_wy_kernel<T><<<dim3(static_cast<unsigned>(nc), a.HV), kGemmThreads, wy_smem, s>>>(a, w);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
+  if (!with_state) return cudaSuccess;
   hk.pre(s);
   chunk_state_kernel<<<dim3(static_cast<unsigned>(a.N), a.HV, (a.V + kStateCols - 1) / kStateCols),
                        kGemmThreads, st_smem, s>>>(a, w);
@@ -398,11 +399,12 @@ cudaError_t launch_chunk_generic(const gdn_chunk_args& a, const ChunkWorkspace& 
   }
 }
 
-cudaError_t launch_chunk_generic_recompute(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s) {
+cudaError_t launch_chunk_generic_recompute(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s,
+                                           bool with_state) {
   switch (a.qkv_dtype) {
-    case GDN_F32: return run_generic<float>(a, ws, s, false);
-    case GDN_BF16: return run_generic<__nv_bfloat16>(a, ws, s, false);
-    case GDN_F16: return run_generic<__half>(a, ws, s, false);
+    case GDN_F32: return run_generic<float>(a, ws, s, false, with_state);
+    case GDN_BF16: return run_generic<__nv_bfloat16>(a, ws, s, false, with_state);
+    case GDN_F16: return run_generic<__half>(a, ws, s, false, with_state);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -566,7 +566,9 @@ teardown:
 // and are never used.
 
 
-template <typename T, int VS_>
+// STORE (the backward's recompute): also store the fp32 state at every chunk
+// start and v_new (Work::hs_out, Work::vnew_out).
+template <typename T, int VS_, bool STORE>
 __global__ void __launch_bounds__(kSt3Threads, 1)
 tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
                  const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk) {
@@ -675,7 +677,7 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
     for (int q = 0; q < CW / 16; ++q)
       umma::tmem_ld16x2(t_acc(x) + lane_base + colh * CW + q * 16, t_o(x) + lane_base + colh * CW + q * 16,
                         y + q * 16, z + q * 16);
-    if (i < L) {
+    if (i < L && obase) {
       T* orow = obase + ((s + i) * p.HV + hv) * D + v0 + colh * CW;
 #pragma unroll
       for (int j8 = 0; j8 < CW / 8; ++j8) {
@@ -766,6 +768,11 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
         }
         *reinterpret_cast<uint4*>(vnimg + umma::img_off(i, col, RSV)) = pack8<T>(vn);
         *reinterpret_cast<uint4*>(vtimg + umma::img_off(i, col, RSV)) = pack8<T>(vt);
+        if (STORE && bos + static_cast<int64_t>(c) * kChunk + i < eos) {
+          float* dst = w.vnew_out + ((bos + static_cast<int64_t>(c) * kChunk + i) * p.HV + hv) * D + v0 + col;
+          *reinterpret_cast<float4*>(dst) = make_float4(vn[0], vn[1], vn[2], vn[3]);
+          *reinterpret_cast<float4*>(dst + 4) = make_float4(vn[4], vn[5], vn[6], vn[7]);
+        }
       }
       umma::fence_proxy_async();
       umma::fence_before_sync();
@@ -800,6 +807,14 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
 #pragma unroll
       for (int q = 0; q < CW / 16; ++q) umma::tmem_ld16(t_dh + lane_base + colh * CW + q * 16, d + q * 16);
       const float g = sc[128];
+      if constexpr (STORE) {  // the state at this chunk's start, for the backward
+        float* dst = w.hs_out + ((c0 + c) * p.HV + hv) * static_cast<int64_t>(D) * D +
+                     static_cast<int64_t>(row) * D + v0 + colh * CW;
+#pragma unroll
+        for (int j4 = 0; j4 < CW / 4; ++j4)
+          *reinterpret_cast<float4*>(dst + j4 * 4) =
+              make_float4(hreg[j4 * 4], hreg[j4 * 4 + 1], hreg[j4 * 4 + 2], hreg[j4 * 4 + 3]);
+      }
 #pragma unroll
       for (int j = 0; j < CW; ++j) hreg[j] = fmaf(g, hreg[j], d[j]);
       if (c + 1 < nch) {
@@ -852,11 +867,6 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
 // ---------------------------------------------------------------------------
 
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;  // resolved once; the entry point never changes
   if (!fn) {
@@ -903,11 +913,11 @@ cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, b
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <typename T, int VS>
+template <typename T, int VS, bool STORE = false>
 cudaError_t launch_state3(const gdn_chunk_args& a, const Work& w, float scale, const CUtensorMap& tq,
                           const CUtensorMap& tk, cudaStream_t s, LaunchHooks& hk) {
   using S = St3<VS>;
-  auto kern = tc_state3_kernel<T, VS>;
+  auto kern = tc_state3_kernel<T, VS, STORE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
   if (e != cudaSuccess) return e;
   hk.pre(s);
@@ -939,7 +949,7 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, lo
   const bool cv = conv != nullptr;
   const Layout l = plan(a, cv);
   uint8_t* ws = static_cast<uint8_t*>(a.workspace);
-  Work w;
+  Work w{};  // every field not set below (the backward's store pointers) stays null
   w.coff = reinterpret_cast<const int64_t*>(ws + l.coff);
   w.err = reinterpret_cast<int*>(ws + l.err);
   w.wimg = ws + l.wimg;
@@ -1005,6 +1015,66 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, lo
   }
   hk.end(s);
   return cudaSuccess;
+}
+
+template <typename T>
+cudaError_t run_wy_only(const gdn_chunk_args& a, void* wsv, cudaStream_t s, Work& w) {
+  constexpr bool kF16 = std::is_same<T, __half>::value;
+  const Layout l = plan(a);
+  uint8_t* ws = static_cast<uint8_t*>(wsv);
+  w = Work{};
+  w.coff = reinterpret_cast<const int64_t*>(ws + l.coff);
+  w.err = reinterpret_cast<int*>(ws + l.err);
+  w.wimg = ws + l.wimg;
+  w.u = ws + l.u;
+  w.pimg = ws + l.pimg;
+  w.scal = reinterpret_cast<float*>(ws + l.scal);
+  w.flags = reinterpret_cast<int*>(ws + l.flags);
+  w.ncu = chunk_upper_bound(a.B * a.T, a.N);
+  w.vs = 32;
+  w.stall_chunk = -1;
+  const int64_t ttot = a.B * a.T;
+  const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
+  note_launch();
+  cudaError_t e = launch_chunk_plan(a.cu_seqlens, a.cu_dtype, a.N, a.T, reinterpret_cast<int64_t*>(ws + l.coff), s,
+                                    64, w.err);
+  if (e != cudaSuccess || ttot == 0) return e;
+  CUtensorMap tq, tk, tv;
+  if ((e = make_map(&tq, a.q, a.H, ttot, kF16, a.q_token_stride)) != cudaSuccess) return e;
+  if ((e = make_map(&tk, a.k, a.H, ttot, kF16, a.k_token_stride)) != cudaSuccess) return e;
+  if ((e = make_map(&tv, a.v, a.HV, ttot, kF16, a.v_token_stride)) != cudaSuccess) return e;
+  auto wy = tc_wy_kernel<T, false>;
+  if ((e = cudaFuncSetAttribute(wy, cudaFuncAttributeMaxDynamicSharedMemorySize, WySmem::kBytes)) != cudaSuccess)
+    return e;
+  note_launch();
+  wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem::kBytes, s>>>(a, w, scale, ConvIn{}, tq, tk, tv);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t run_state_store(const gdn_chunk_args& a, const Work& w0, float* hs, float* vnew, cudaStream_t s) {
+  constexpr bool kF16 = std::is_same<T, __half>::value;
+  const int64_t ttot = a.B * a.T;
+  if (ttot == 0) return cudaSuccess;
+  Work w = w0;
+  w.hs_out = hs;
+  w.vnew_out = vnew;
+  const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
+  CUtensorMap tq, tk;
+  cudaError_t e;
+  if ((e = make_map(&tq, a.q, a.H, ttot, kF16, a.q_token_stride)) != cudaSuccess) return e;
+  if ((e = make_map(&tk, a.k, a.H, ttot, kF16, a.k_token_stride)) != cudaSuccess) return e;
+  LaunchHooks hk(nullptr, 0);
+  return launch_state3<T, 32, true>(a, w, scale, tq, tk, s, hk);
+}
+
+cudaError_t launch_state_store(const gdn_chunk_args& a, const Work& w, float* hs, float* vnew, cudaStream_t s) {
+  return a.qkv_dtype == GDN_F16 ? run_state_store<__half>(a, w, hs, vnew, s)
+                                : run_state_store<__nv_bfloat16>(a, w, hs, vnew, s);
+}
+
+cudaError_t launch_wy_only(const gdn_chunk_args& a, void* ws, cudaStream_t s, Work& w) {
+  return a.qkv_dtype == GDN_F16 ? run_wy_only<__half>(a, ws, s, w) : run_wy_only<__nv_bfloat16>(a, ws, s, w);
 }
 
 }  // namespace tc

@@ -38,6 +38,11 @@ struct Work {
   // stall_limit cycles, so that one wait runs out with nothing in flight.
   int64_t stall_chunk;
   long long stall_limit;
+  // The backward's recompute (launch_state_store): the state kernel also
+  // stores the fp32 state at every chunk start ([chunks][HV][K][V]) and the
+  // fp32 v_new ([Ttot][HV][V]); null otherwise.
+  float* hs_out;
+  float* vnew_out;
 };
 
 // The causal conv1d applied by the WY kernel as it loads its tiles
@@ -164,6 +169,27 @@ struct St3 {
   static_assert(kBytes <= 227 * 1024, "shared memory");
 };
 constexpr int kSt3Threads = 288;  // 8 epilogue warps + 1 load warp
+
+// cuTensorMapEncodeTiled, resolved once through the runtime's driver entry point.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn();
+
+// The forward's WY kernel alone (after its chunk plan) into a tensor-core
+// workspace of tc_workspace_bytes(a) bytes at `ws`, for the backward's state
+// recurrence (its W images and row scales); `w` gets the workspace pointers.
+cudaError_t launch_wy_only(const gdn_chunk_args& a, void* ws, cudaStream_t s, Work& w);
+// The forward state kernel (32-column slices) after launch_wy_only, for the
+// backward's recompute: stores the fp32 state at every chunk start to hs and
+// v_new to vnew (the generic workspace layouts); a.o and a.final_state null.
+cudaError_t launch_state_store(const gdn_chunk_args& a, const Work& w, float* hs, float* vnew, cudaStream_t s);
+// The backward's state-gradient recurrence on tcgen05 (gdn_chunk_bwd_tc.cu):
+// reads dv_local from and writes dv to dvn ([Ttot][HV][V] fp32), writes dh'
+// of every chunk to dhn ([chunks][HV][K][V] fp32) and dh0.
+cudaError_t launch_bwd_state_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, float* dhn,
+                                cudaStream_t s);
 
 // [Ttot, heads, 128] bf16/f16 tensor map with 64 x 64 boxes, 128-byte swizzle.
 cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, bool f16, int64_t tstride = 0);
