@@ -45,11 +45,11 @@ constexpr int kP = 65;            // row stride of 64 x 64 fp32 tiles
 constexpr int kStage = kGemmStage;
 constexpr int kVS = 32;           // V columns per bwd_state_kernel CTA
 
-template <bool ACC, typename TA, typename TB>
+template <bool ACC, bool SPLIT = true, typename TA, typename TB>
 __device__ __forceinline__ void gemm(float* C, int64_t ldc, int mc, int N, int Kd, const TA* a, int64_t asi,
                                      int64_t ask, int ma, const TB* b, int64_t bsk, int64_t bsn, int nb,
                                      float alpha, float* st) {
-  gemm_staged<ACC>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
+  gemm_staged<ACC, SPLIT>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
 }
 
 struct BwdPtrs {
@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(kT, 2) bwd_dvlocal_kernel(const gdn_chunk_bwd_
     }
   }
   if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
-  gemm_smem<false>(P, kP, 64, 64, K, qc, LD, 1, kc, 1, LD);  // Q K^T (ends with a barrier)
+  gemm_smem<false, kSplit<T>>(P, kP, 64, 64, K, qc, LD, 1, kc, 1, LD);  // Q K^T (ends with a barrier)
   for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
     for (int vv = tid & 31; vv < V; vv += 32) {
       dO[i * LD + vv] = i < L ? to_f<T>(dout[i * rowV + vv]) : 0.f;
@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kT, 2) bwd_dvlocal_kernel(const gdn_chunk_bwd_
     const int i = e >> 6, j = e & 63;
     P[i * kP + j] = (i < L && j <= i) ? P[i * kP + j] * expf(gcs[i] - gcs[j]) : 0.f;
   }
-  gemm_smem<false>(w.dvn + s * rowV + static_cast<int64_t>(hv) * V, rowV, L, V, 64, P, 1, kP, dO, LD, 1, scale);
+  gemm_smem<false, kSplit<T>>(w.dvn + s * rowV + static_cast<int64_t>(hv) * V, rowV, L, V, 64, P, 1, kP, dO, LD, 1, scale);
 }
 
 // Shared memory of bwd_state_kernel: [Q; W] (128 rows, read transposed), K
@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(kT, 1) bwd_state_kernel(const gdn_chunk_bwd_ar
       const float d = (i < L && c < vcols) ? to_f<T>(dout[(s + i) * rowV + static_cast<int64_t>(hv) * V + v0 + c]) : 0.f;
       rhs[i * kRow32 + c] = i < L ? scale * expf(gs[i]) * d : 0.f;
     }
-    gemm_smem<false>(rhs + 64 * kRow32, kRow32, 64, kVS, K, kc, kRowK, 1, dh, kRow32, 1);  // K dh'
+    gemm_smem<false, kSplit<T>>(rhs + 64 * kRow32, kRow32, 64, kVS, K, kc, kRowK, 1, dh, kRow32, 1);  // K dh'
     for (int e = tid; e < 64 * kVS; e += kT) {
       const int i = e / kVS, c = e % kVS;
       float x = 0.f;
@@ -200,8 +200,8 @@ __global__ void __launch_bounds__(kT, 1) bwd_state_kernel(const gdn_chunk_bwd_ar
     }
     __syncthreads();
     for (int e = tid; e < 128 * kVS; e += kT) dh[(e / kVS) * kRow32 + e % kVS] *= eg;
-    gemm_smem<true>(dh, kRow32, min(K, 64), kVS, 128, qw, 1, kRowN, rhs, kRow32, 1);
-    if (K > 64) gemm_smem<true>(dh + 64 * kRow32, kRow32, K - 64, kVS, 128, qw + 64, 1, kRowN, rhs, kRow32, 1);
+    gemm_smem<true, kSplit<T>>(dh, kRow32, min(K, 64), kVS, 128, qw, 1, kRowN, rhs, kRow32, 1);
+    if (K > 64) gemm_smem<true, kSplit<T>>(dh + 64 * kRow32, kRow32, K - 64, kVS, 128, qw + 64, 1, kRowN, rhs, kRow32, 1);
   }
   __syncthreads();
   if (p.dh0) {
@@ -264,12 +264,12 @@ __global__ void __launch_bounds__(kT, 1) bwd_dqkw_kernel(const gdn_chunk_bwd_arg
     }
   }
   if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
-  gemm_smem<false>(dP, kP, 64, 64, V, dOs, LQ, 1, X, 1, LQ);  // dO v^T
+  gemm_smem<false, kSplit<T>>(dP, kP, 64, 64, V, dOs, LQ, 1, X, 1, LQ);  // dO v^T
   for (int e = tid; e < 64 * 64; e += kT) {
     const int i = e >> 6, j = e & 63;
     dP[i * kP + j] = (i < L && j <= i) ? scale * expf(gcs[i] - gcs[j]) * dP[i * kP + j] : 0.f;
   }
-  gemm<false>(dk, LQ, 64, K, V, X, LQ, 1, 64, dhn, 1, V, K, 1.f, st);  // v dh'^T
+  gemm<false, kSplit<T>>(dk, LQ, 64, K, V, X, LQ, 1, 64, dhn, 1, V, K, 1.f, st);  // v dh'^T
   const float glast = gcs[L - 1], eg = expf(glast);
   float E = 0.f;
   if (tid < 64) {  // dK = diag(c) v dh'^T; E_i = k_i . dK_i
@@ -289,16 +289,16 @@ __global__ void __launch_bounds__(kT, 1) bwd_dqkw_kernel(const gdn_chunk_bwd_arg
       X[i * LQ + vv] = i < L ? dvn[i * rowV + vv] : 0.f;
     }
   }
-  gemm<false>(dq, LQ, 64, K, V, dOs, LQ, 1, 64, hst, 1, V, K, scale, st);  // scale dO h^T
+  gemm<false, kSplit<T>>(dq, LQ, 64, K, V, dOs, LQ, 1, 64, hst, 1, V, K, scale, st);  // scale dO h^T
   for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
     for (int kk = tid & 31; kk < K; kk += 32) {
       dq[i * LQ + kk] *= i < L ? expf(gcs[i]) : 0.f;
     }
   }
-  gemm_smem<true>(dq, LQ, 64, K, 64, dP, kP, 1, kc, LQ, 1);  // + dP K
-  gemm_smem<true>(dk, LQ, 64, K, 64, dP, 1, kP, qc, LQ, 1);  // + dP^T Q
+  gemm_smem<true, kSplit<T>>(dq, LQ, 64, K, 64, dP, kP, 1, kc, LQ, 1);  // + dP K
+  gemm_smem<true, kSplit<T>>(dk, LQ, 64, K, 64, dP, 1, kP, qc, LQ, 1);  // + dP^T Q
   // dW = -dv h^T straight to the workspace
-  gemm<false>(w.dw + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, V, X, LQ, 1, 64, hst, 1, V, K, -1.f,
+  gemm<false, kSplit<T>>(w.dw + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, V, X, LQ, 1, 64, hst, 1, V, K, -1.f,
               st);
   if (tid < 64) {
     float a = 0.f;
@@ -363,23 +363,23 @@ __global__ void __launch_bounds__(kT, 1) bwd_wy_kernel(const gdn_chunk_bwd_args 
     bs[tid] = bt;
     cw[tid] = ok ? bt * expf(g) : 0.f;
   }
-  gemm_smem<false>(Sk, kP, 64, 64, K, kc, LD, 1, kc, 1, LD);  // K K^T
+  gemm_smem<false, kSplit<T>>(Sk, kP, 64, 64, K, kc, LD, 1, kc, 1, LD);  // K K^T
   for (int e = tid; e < 64 * 64; e += kT) {
     const int i = e >> 6, j = e & 63;
     Am[i * kP + j] = (i < L && j < i) ? bs[i] * expf(gcs[i] - gcs[j]) * Sk[i * kP + j] : 0.f;
   }
   __syncthreads();
   solve_tril64_nt<kT>(Am, Tm, Zs);  // T = (I + A)^-1
-  gemm_smem<false>(dT, kP, 64, 64, K, b1, LD, 1, kc, 1, LD);     // dW K^T
-  gemm<false>(tm, kP, 64, 64, V, dvn, rowV, 1, L, vin, 1, rowV, L, 1.f, st);  // dv V^T
+  gemm_smem<false, kSplit<T>>(dT, kP, 64, 64, K, b1, LD, 1, kc, 1, LD);     // dW K^T
+  gemm<false, kSplit<T>>(tm, kP, 64, 64, V, dvn, rowV, 1, L, vin, 1, rowV, L, 1.f, st);  // dv V^T
   for (int e = tid; e < 64 * 64; e += kT) {
     const int i = e >> 6, j = e & 63;
     dT[i * kP + j] = dT[i * kP + j] * cw[j] + tm[i * kP + j] * bs[j];
   }
-  gemm_smem<false>(b2, LD, 64, K, 64, Tm, 1, kTS, b1, LD, 1);     // dR_w = T^T dW
-  gemm<false>(b1, LD, 64, V, L, Tm, 1, kTS, 64, dvn, rowV, 1, V, 1.f, st);   // dR_u = T^T dv
-  gemm_smem<false>(tm, kP, 64, 64, 64, dT, kP, 1, Tm, 1, kTS);   // dT T^T
-  gemm_smem<false>(dT, kP, 64, 64, 64, Tm, 1, kTS, tm, kP, 1, -1.f);  // dA = -T^T (dT T^T)
+  gemm_smem<false, kSplit<T>>(b2, LD, 64, K, 64, Tm, 1, kTS, b1, LD, 1);     // dR_w = T^T dW
+  gemm<false, kSplit<T>>(b1, LD, 64, V, L, Tm, 1, kTS, 64, dvn, rowV, 1, V, 1.f, st);   // dR_u = T^T dv
+  gemm_smem<false, kSplit<T>>(tm, kP, 64, 64, 64, dT, kP, 1, Tm, 1, kTS);   // dT T^T
+  gemm_smem<false, kSplit<T>>(dT, kP, 64, 64, 64, Tm, 1, kTS, tm, kP, 1, -1.f);  // dA = -T^T (dT T^T)
   T* dv = static_cast<T*>(p.dv) + s * rowV + static_cast<int64_t>(hv) * V;
   for (int i = tid >> 5; i < L; i += kGemmThreads / 32) {
     for (int vv = tid & 31; vv < V; vv += 32) {
@@ -419,8 +419,8 @@ __global__ void __launch_bounds__(kT, 1) bwd_wy_kernel(const gdn_chunk_bwd_args 
     for (int j = 0; j < 64; ++j) f += Am[tid * kP + j] * Sk[tid * kP + j] - Am[j * kP + tid] * Sk[j * kP + tid];
     dG[tid] += f;
   }
-  gemm_smem<true>(b2, LD, 64, K, 64, Am, kP, 1, kc, LD, 1);  // + dS K
-  gemm_smem<true>(b2, LD, 64, K, 64, Am, 1, kP, kc, LD, 1);  // + dS^T K
+  gemm_smem<true, kSplit<T>>(b2, LD, 64, K, 64, Am, kP, 1, kc, LD, 1);  // + dS K
+  gemm_smem<true, kSplit<T>>(b2, LD, 64, K, 64, Am, 1, kP, kc, LD, 1);  // + dS^T K
   for (int i = tid >> 5; i < L; i += kGemmThreads / 32) {
     for (int kk = tid & 31; kk < K; kk += 32) {
       w.dkh[(s + i) * rowK + static_cast<int64_t>(hv) * K + kk] += b2[i * LD + kk];

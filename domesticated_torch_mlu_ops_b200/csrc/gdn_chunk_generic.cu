@@ -149,7 +149,7 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
     gcs[tid + 32] = x1;
   }
   if (tid < 64) bs[tid] = tid < L ? p.beta[(s + tid) * p.HV + hv] : 0.f;
-  gemm_smem<false>(A, 65, 64, 64, K, ks, kLD, 1, ks, 1, kLD);  // K K^T
+  gemm_smem<false, kSplit<T>>(A, 65, 64, 64, K, ks, kLD, 1, ks, 1, kLD);  // K K^T
   if (tid < L) w.gc[(s + tid) * p.HV + hv] = gcs[tid];
   for (int e = tid; e < 64 * 64; e += kGemmThreads) {
     const int i = e >> 6, j = e & 63;
@@ -167,8 +167,8 @@ chunk_wy_kernel(const gdn_chunk_args p, const GenericPtrs w) {
       vs[i * kLD + vv] *= bs[i];
     }
   }
-  gemm_smem<false>(w.w + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, 64, Tm, kTS, 1, ks, kLD, 1);
-  gemm_smem<false>(w.u + s * rowV + static_cast<int64_t>(hv) * V, rowV, L, V, 64, Tm, kTS, 1, vs, kLD, 1);
+  gemm_smem<false, kSplit<T>>(w.w + s * rowK + static_cast<int64_t>(hv) * K, rowK, L, K, 64, Tm, kTS, 1, ks, kLD, 1);
+  gemm_smem<false, kSplit<T>>(w.u + s * rowV + static_cast<int64_t>(hv) * V, rowV, L, V, 64, Tm, kTS, 1, vs, kLD, 1);
 }
 
 constexpr int kStateCols = 32;
@@ -288,20 +288,20 @@ chunk_out_kernel(const gdn_chunk_args p, const GenericPtrs w, float scale) {
     }
   }
   if (tid < 64) gcs[tid] = tid < L ? w.gc[(s + tid) * p.HV + hv] : 0.f;
-  gemm_smem<false>(att, 65, 64, 64, K, qc, kLD, 1, kc, 1, kLD);  // Q K^T
+  gemm_smem<false, kSplit<T>>(att, 65, 64, 64, K, qc, kLD, 1, kc, 1, kLD);  // Q K^T
   for (int e = tid; e < 64 * 64; e += kGemmThreads) {
     const int i = e >> 6, j = e & 63;
     att[i * 65 + j] = (i < L && j <= i) ? att[i * 65 + j] * expf(gcs[i] - gcs[j]) : 0.f;
   }
   const float* hc = w.hs + (cidx * p.HV + hv) * static_cast<int64_t>(K) * V;
-  gemm_staged<false>(oc, kLD, 64, V, K, qc, kLD, 1, 64, hc, V, 1, V, 1.f, st);  // Q h
+  gemm_staged<false, kSplit<T>>(oc, kLD, 64, V, K, qc, kLD, 1, 64, hc, V, 1, V, 1.f, st);  // Q h
   for (int i = tid >> 5; i < 64; i += kGemmThreads / 32) {
     for (int vv = tid & 31; vv < V; vv += 32) {
       oc[i * kLD + vv] *= expf(gcs[i]);
     }
   }
   const float* vn = w.vnew + s * rowV + static_cast<int64_t>(hv) * V;
-  gemm_staged<true>(oc, kLD, 64, V, L, att, 65, 1, 64, vn, rowV, 1, V, 1.f, st);  // + P v_new
+  gemm_staged<true, kSplit<T>>(oc, kLD, 64, V, L, att, 65, 1, 64, vn, rowV, 1, V, 1.f, st);  // + P v_new
   T* ob = static_cast<T*>(p.o) + s * rowV + static_cast<int64_t>(hv) * V;
   for (int i = tid >> 5; i < L; i += kGemmThreads / 32) {
     for (int vv = tid & 31; vv < V; vv += 32) {

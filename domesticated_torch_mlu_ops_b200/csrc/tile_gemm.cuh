@@ -23,7 +23,13 @@
 // Both store C (shared or global, row stride ldc) for rows i < mc and
 // columns n < N, as C = alpha * AB or C += alpha * AB (ACC), and both begin
 // and end with a barrier; C may alias an operand of gemm_smem.
+// SPLIT = false (kernels of 16-bit inputs): one TF32 product per step, no
+// tails.  16-bit values are exact in TF32, and fp32 intermediates are rounded
+// to 10 mantissa bits, finer than the reference's bf16 roundings of the same
+// operands; the fp32 path keeps the split.
 #pragma once
+
+#include <type_traits>
 
 #include "gdn_common.cuh"
 #include "solve_tril.cuh"
@@ -70,13 +76,35 @@ __device__ __forceinline__ void mma_store(const float (&d)[CW][4], const float (
 // warp's column tiles; reads at k >= kmax give zero.  Head products go to d,
 // the two tail products to e, issued tile by tile so that consecutive MMAs
 // are independent.
-template <int CW, typename LA, typename LB>
+__device__ __forceinline__ uint32_t tf32_round(float x) {
+  uint32_t h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  return h;
+}
+
+template <int CW, bool SPLIT = true, typename LA, typename LB>
 __device__ __forceinline__ void mma_kstep(float (&d)[CW][4], float (&e)[CW][4], int k0, int kmax, LA lda,
                                           LB ldb) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int ch = threadIdx.x >> 7;
   const int ka = k0 + t, kb = k0 + t + 4;
   const bool va = ka < kmax, vb = kb < kmax;
+  if constexpr (!SPLIT) {
+    uint32_t a[4], bb[CW][2];
+    a[0] = tf32_round(va ? lda(g, ka) : 0.f);
+    a[1] = tf32_round(va ? lda(g + 8, ka) : 0.f);
+    a[2] = tf32_round(vb ? lda(g, kb) : 0.f);
+    a[3] = tf32_round(vb ? lda(g + 8, kb) : 0.f);
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+      const int n = (ch + 2 * j) * 8 + g;
+      bb[j][0] = tf32_round(va ? ldb(ka, n) : 0.f);
+      bb[j][1] = tf32_round(vb ? ldb(kb, n) : 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < CW; ++j) GDN_MMA_TF32_ACC(d[j], a, bb[j][0], bb[j][1]);
+    return;
+  }
   uint32_t ah[4], al[4], bh[CW][2], bl[CW][2];
   tf32_split(va ? lda(g, ka) : 0.f, ah[0], al[0]);
   tf32_split(va ? lda(g + 8, ka) : 0.f, ah[1], al[1]);
@@ -97,7 +125,7 @@ __device__ __forceinline__ void mma_kstep(float (&d)[CW][4], float (&e)[CW][4], 
 }
 #undef GDN_MMA_TF32_ACC
 
-template <int CW, bool ACC>
+template <int CW, bool ACC, bool SPLIT>
 __device__ __forceinline__ void gemm_smem_cw(float* C, int64_t ldc, int mc, int N, int Kd, const float* a,
                                              int asi, int ask, const float* b, int bsk, int bsn, float alpha) {
   float d[CW][4], e[CW][4];
@@ -110,23 +138,23 @@ __device__ __forceinline__ void gemm_smem_cw(float* C, int64_t ldc, int mc, int 
   auto ldb = [&](int k, int n) { return b[k * bsk + n * bsn]; };
   __syncthreads();
 #pragma unroll 2
-  for (int k0 = 0; k0 < Kd; k0 += 8) mma_kstep<CW>(d, e, k0, Kd, lda, ldb);
+  for (int k0 = 0; k0 < Kd; k0 += 8) mma_kstep<CW, SPLIT>(d, e, k0, Kd, lda, ldb);
   __syncthreads();
   mma_store<CW, ACC>(d, e, C, ldc, mc, N, alpha);
   __syncthreads();
 }
 
 // N <= 128; operands in shared memory (C may be global).
-template <bool ACC>
+template <bool ACC, bool SPLIT = true>
 __device__ __forceinline__ void gemm_smem(float* C, int64_t ldc, int mc, int N, int Kd, const float* a, int asi,
                                           int ask, const float* b, int bsk, int bsn, float alpha = 1.f) {
-  if (N <= 16) gemm_smem_cw<1, ACC>(C, ldc, mc, N, Kd, a, asi, ask, b, bsk, bsn, alpha);
-  else if (N <= 32) gemm_smem_cw<2, ACC>(C, ldc, mc, N, Kd, a, asi, ask, b, bsk, bsn, alpha);
-  else if (N <= 64) gemm_smem_cw<4, ACC>(C, ldc, mc, N, Kd, a, asi, ask, b, bsk, bsn, alpha);
-  else gemm_smem_cw<8, ACC>(C, ldc, mc, N, Kd, a, asi, ask, b, bsk, bsn, alpha);
+  if (N <= 16) gemm_smem_cw<1, ACC, SPLIT>(C, ldc, mc, N, Kd, a, asi, ask, b, bsk, bsn, alpha);
+  else if (N <= 32) gemm_smem_cw<2, ACC, SPLIT>(C, ldc, mc, N, Kd, a, asi, ask, b, bsk, bsn, alpha);
+  else if (N <= 64) gemm_smem_cw<4, ACC, SPLIT>(C, ldc, mc, N, Kd, a, asi, ask, b, bsk, bsn, alpha);
+  else gemm_smem_cw<8, ACC, SPLIT>(C, ldc, mc, N, Kd, a, asi, ask, b, bsk, bsn, alpha);
 }
 
-template <int CW, bool ACC, typename TA, typename TB>
+template <int CW, bool ACC, bool SPLIT, typename TA, typename TB>
 __device__ __forceinline__ void gemm_staged_cw(float* C, int64_t ldc, int mc, int N, int Kd, const TA* a,
                                                int64_t asi, int64_t ask, int ma, const TB* b, int64_t bsk,
                                                int64_t bsn, int nb, float alpha, float* st) {
@@ -178,23 +206,28 @@ __device__ __forceinline__ void gemm_staged_cw(float* C, int64_t ldc, int mc, in
     }
     __syncthreads();
     if (k0 + 16 < Kd) fetch(k0 + 16);  // global latency overlaps the products below
-    mma_kstep<CW>(d, e, 0, 16, lda, ldb);
-    mma_kstep<CW>(d, e, 8, 16, lda, ldb);
+    mma_kstep<CW, SPLIT>(d, e, 0, 16, lda, ldb);
+    mma_kstep<CW, SPLIT>(d, e, 8, 16, lda, ldb);
     __syncthreads();
   }
   mma_store<CW, ACC>(d, e, C, ldc, mc, N, alpha);
   __syncthreads();
 }
 
-template <bool ACC, typename TA, typename TB>
+template <bool ACC, bool SPLIT = true, typename TA, typename TB>
 __device__ __forceinline__ void gemm_staged(float* C, int64_t ldc, int mc, int N, int Kd, const TA* a,
                                             int64_t asi, int64_t ask, int ma, const TB* b, int64_t bsk,
                                             int64_t bsn, int nb, float alpha, float* st) {
-  if (N <= 16) gemm_staged_cw<1, ACC>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
-  else if (N <= 32) gemm_staged_cw<2, ACC>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
-  else if (N <= 64) gemm_staged_cw<4, ACC>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
-  else gemm_staged_cw<8, ACC>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
+  if (N <= 16) gemm_staged_cw<1, ACC, SPLIT>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
+  else if (N <= 32) gemm_staged_cw<2, ACC, SPLIT>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
+  else if (N <= 64) gemm_staged_cw<4, ACC, SPLIT>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
+  else gemm_staged_cw<8, ACC, SPLIT>(C, ldc, mc, N, Kd, a, asi, ask, ma, b, bsk, bsn, nb, alpha, st);
 }
+
+// Whether the products of a kernel on T inputs split their operands (fp32)
+// or take one TF32 product (16-bit inputs).
+template <typename T>
+constexpr bool kSplit = std::is_same<T, float>::value;
 
 // Block-wide sum of one value per thread, returned to every thread (`red`
 // holds kGemmThreads / 32 floats).
