@@ -586,14 +586,16 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
   // with the tensor-core path, the states and v_new come from the forward's
   // own kernels (tcgen05, bf16 roundings as in the forward); otherwise from
   // the generic fp32 recompute
-  cudaError_t e = launch_chunk_generic_recompute(a, ws.fwd, s, !tcb);
+  cudaError_t e = launch_chunk_generic_recompute(a, ws.fwd, s, !tcb, !tcb);
   if (e != cudaSuccess) return e;
   char* base = static_cast<char*>(b.workspace);
   tc::Work tw{};
-  if (tcb) {
+  if (tcb) {  // G from the tensor-core WY kernel; W and U of the generic one are not needed
     gdn_chunk_args fa = a;
     fa.force_generic = 0;
-    if ((e = tc::launch_wy_only(fa, base + ws.tc, s, tw)) != cudaSuccess) return e;
+    if ((e = tc::launch_wy_only(fa, base + ws.tc, s, tw, reinterpret_cast<float*>(base + ws.fwd.gc))) !=
+        cudaSuccess)
+      return e;
     if ((e = tc::launch_state_store(fa, tw, reinterpret_cast<float*>(base + ws.fwd.hs),
                                     reinterpret_cast<float*>(base + ws.fwd.vnew), s)) != cudaSuccess)
       return e;

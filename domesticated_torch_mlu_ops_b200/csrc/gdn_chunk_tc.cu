@@ -302,6 +302,10 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
     g1 += __shfl_sync(0xffffffffu, g0, 31);
     gam[lane] = g0 * kLog2e;  // G in the log2 domain: exp(G_i - G_j) = exp2(gam_i - gam_j)
     gam[lane + 32] = g1 * kLog2e;
+    if (w.gc_out) {  // the backward's recompute keeps G
+      if (lane < L) w.gc_out[(s + lane) * p.HV + hv] = g0;
+      if (lane + 32 < L) w.gc_out[(s + lane + 32) * p.HV + hv] = g1;
+    }
   } else if (warp == 2) {
     bet[lane] = lane < L ? p.beta[(s + lane) * p.HV + hv] : 0.f;
     bet[lane + 32] = lane + 32 < L ? p.beta[(s + lane + 32) * p.HV + hv] : 0.f;
@@ -1018,7 +1022,7 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, lo
 }
 
 template <typename T>
-cudaError_t run_wy_only(const gdn_chunk_args& a, void* wsv, cudaStream_t s, Work& w) {
+cudaError_t run_wy_only(const gdn_chunk_args& a, void* wsv, cudaStream_t s, Work& w, float* gc_out) {
   constexpr bool kF16 = std::is_same<T, __half>::value;
   const Layout l = plan(a);
   uint8_t* ws = static_cast<uint8_t*>(wsv);
@@ -1033,6 +1037,7 @@ cudaError_t run_wy_only(const gdn_chunk_args& a, void* wsv, cudaStream_t s, Work
   w.ncu = chunk_upper_bound(a.B * a.T, a.N);
   w.vs = 32;
   w.stall_chunk = -1;
+  w.gc_out = gc_out;
   const int64_t ttot = a.B * a.T;
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
   note_launch();
@@ -1073,8 +1078,9 @@ cudaError_t launch_state_store(const gdn_chunk_args& a, const Work& w, float* hs
                                 : run_state_store<__nv_bfloat16>(a, w, hs, vnew, s);
 }
 
-cudaError_t launch_wy_only(const gdn_chunk_args& a, void* ws, cudaStream_t s, Work& w) {
-  return a.qkv_dtype == GDN_F16 ? run_wy_only<__half>(a, ws, s, w) : run_wy_only<__nv_bfloat16>(a, ws, s, w);
+cudaError_t launch_wy_only(const gdn_chunk_args& a, void* ws, cudaStream_t s, Work& w, float* gc_out) {
+  return a.qkv_dtype == GDN_F16 ? run_wy_only<__half>(a, ws, s, w, gc_out)
+                                : run_wy_only<__nv_bfloat16>(a, ws, s, w, gc_out);
 }
 
 }  // namespace tc

@@ -43,6 +43,9 @@ struct Work {
   // fp32 v_new ([Ttot][HV][V]); null otherwise.
   float* hs_out;
   float* vnew_out;
+  // The backward's recompute (launch_wy_only): the WY kernel also stores the
+  // chunk-local cumsum of g ([Ttot][HV] fp32); null otherwise.
+  float* gc_out;
 };
 
 // The causal conv1d applied by the WY kernel as it loads its tiles
@@ -180,7 +183,7 @@ EncodeTiledFn encode_fn();
 // The forward's WY kernel alone (after its chunk plan) into a tensor-core
 // workspace of tc_workspace_bytes(a) bytes at `ws`, for the backward's state
 // recurrence (its W images and row scales); `w` gets the workspace pointers.
-cudaError_t launch_wy_only(const gdn_chunk_args& a, void* ws, cudaStream_t s, Work& w);
+cudaError_t launch_wy_only(const gdn_chunk_args& a, void* ws, cudaStream_t s, Work& w, float* gc_out = nullptr);
 // The forward state kernel (32-column slices) after launch_wy_only, for the
 // backward's recompute: stores the fp32 state at every chunk start to hs and
 // v_new to vnew (the generic workspace layouts); a.o and a.final_state null.
