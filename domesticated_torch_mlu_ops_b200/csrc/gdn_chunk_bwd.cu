@@ -596,8 +596,8 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
     if ((e = tc::launch_wy_only(fa, base + ws.tc, s, tw, reinterpret_cast<float*>(base + ws.fwd.gc))) !=
         cudaSuccess)
       return e;
-    if ((e = tc::launch_state_store(fa, tw, reinterpret_cast<float*>(base + ws.fwd.hs),
-                                    reinterpret_cast<float*>(base + ws.fwd.vnew), s)) != cudaSuccess)
+    if ((e = tc::launch_state_store(fa, tw, reinterpret_cast<uint8_t*>(base + ws.himg),
+                                    reinterpret_cast<uint8_t*>(base + ws.vnimg), s)) != cudaSuccess)
       return e;
   }
   BwdPtrs w;
@@ -631,7 +631,8 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (tcb) {
-    if ((e = tc::launch_bwd_state_tc(b, tw, w.dvn, w.dhn, s)) != cudaSuccess) return e;
+    if ((e = tc::launch_bwd_state_tc(b, tw, w.dvn, reinterpret_cast<uint8_t*>(base + ws.dhimg), s)) != cudaSuccess)
+      return e;
   } else {
     note_launch();
     bwd_state_kernel<T><<<dim3(static_cast<unsigned>(b.N), b.HV, (b.V + kVS - 1) / kVS), kT, kStateSmem, s>>>(
@@ -639,8 +640,16 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (nc > 0) {
-    note_launch(2);
-    bwd_dqkw_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kDqkwSmem, s>>>(b, w, scale);
+    if (tcb) {
+      tc::DqkwOut d{w.dvn, w.gc, reinterpret_cast<const uint8_t*>(base + ws.himg),
+                    reinterpret_cast<const uint8_t*>(base + ws.dhimg), reinterpret_cast<const uint8_t*>(base + ws.vnimg),
+                    w.dqh, w.dkh, w.dw, w.dG};
+      if ((e = tc::launch_bwd_dqkw_tc(b, tw, d, s)) != cudaSuccess) return e;
+    } else {
+      note_launch();
+      bwd_dqkw_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kDqkwSmem, s>>>(b, w, scale);
+    }
+    note_launch();
     bwd_wy_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kWySmem, s>>>(b, w);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
@@ -671,10 +680,15 @@ BwdWorkspace plan_bwd_workspace(const gdn_chunk_bwd_args& b) {
   w.dw = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
   w.dG = o; o += al(sizeof(float) * Ttot * b.HV);
   w.tc = o;
+  w.himg = w.dhimg = w.vnimg = o;
   if (bwd_tc_applies(b)) {
     gdn_chunk_args fa = forward_args(b);
     fa.force_generic = 0;
     o += al(tc_workspace_bytes(fa) + 1024);  // the tensor-core layout aligns its regions to 1 KiB
+    const size_t imgs = static_cast<size_t>(nc) * b.HV;
+    w.himg = o; o += al(imgs * tc::kStateImg);
+    w.dhimg = o; o += al(imgs * tc::kStateImg);
+    w.vnimg = o; o += al(imgs * tc::kVnImg);
   }
   w.total = o;
   return w;

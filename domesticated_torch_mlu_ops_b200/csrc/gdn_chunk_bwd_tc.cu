@@ -12,8 +12,8 @@
 // gamma = exp(G_L): the row scales the forward WY kernel writes, whose W
 // images (L2 norm and gates folded in) this kernel reads.  q, k, dO and
 // dv_local come in by TMA.  Every chunk stores dv (fp32, completing the
-// dv_local the previous kernel wrote) and dh' (fp32) for the remaining
-// backward kernels; dh at the first chunk is dh0.  The bf16 roundings are the
+// dv_local the previous kernel wrote) and dh' (a bf16 operand image) for the
+// remaining backward kernels; dh at the first chunk is dh0.  The bf16 roundings are the
 // reference's: dh and dv are cast to the input dtype before their products.
 //
 // Warp roles as in the forward state kernel: warp 0 issues the MMAs, warps
@@ -60,8 +60,8 @@ struct BwdSt {
 };
 
 struct BwdOut {
-  float* dvn;  // [Ttot][HV][V]: dv_local in, dv out
-  float* dhn;  // [chunks][HV][K][V]: dh' of every chunk
+  float* dvn;       // [Ttot][HV][V]: dv_local in, dv out
+  uint8_t* dh_img;  // [chunks][HV] bf16 images of dh' (bwd_img_off, 128 rows)
 };
 
 template <typename T>
@@ -291,12 +291,10 @@ tc_bwd_state_kernel(const gdn_chunk_bwd_args p, const Work w, const BwdOut o,
         for (int j8 = 0; j8 < CW / 8; ++j8)
           *reinterpret_cast<uint4*>(himg + umma::img_off(row, colh * CW + j8 * 8, RSV)) = pack8<T>(d + j8 * 8);
       }
-      float* dst = o.dhn + ((c0 + c) * p.HV + hv) * static_cast<int64_t>(D) * D + static_cast<int64_t>(row) * D + v0 +
-                   colh * CW;
+      uint8_t* dst = o.dh_img + ((c0 + c) * p.HV + hv) * static_cast<int64_t>(kStateImg);
 #pragma unroll
-      for (int j4 = 0; j4 < CW / 4; ++j4)
-        *reinterpret_cast<float4*>(dst + j4 * 4) =
-            make_float4(hreg[j4 * 4], hreg[j4 * 4 + 1], hreg[j4 * 4 + 2], hreg[j4 * 4 + 3]);
+      for (int j8 = 0; j8 < CW / 8; ++j8)
+        *reinterpret_cast<uint4*>(dst + bwd_img_off(row, v0 + colh * CW + j8 * 8, 128)) = pack8<T>(hreg + j8 * 8);
 #pragma unroll
       for (int e = 0; e < CW; ++e) hreg[e] = d[e];
     }
@@ -326,6 +324,374 @@ tc_bwd_state_kernel(const gdn_chunk_bwd_args p, const Work w, const BwdOut o,
   if (warp == 0) umma::tmem_dealloc(tmem, S::kCols);
 }
 
+// ---------------------------------------------------------------------------
+// dq, dk, dW and dG per (chunk, v-head): chunk_bwd_dqkwg (chunk_o.py:233-778)
+// ---------------------------------------------------------------------------
+// With s = scale, Gam_i = exp(G_i), c_i = exp(G_L - G_i) and r_q, r_k the L2
+// norm factors (q^ = diag(r_q) q, k^ = diag(r_k) k):
+//   S   = [dO; v_new] v_new^T                     rows 0..63 used
+//   dP  = s M * exp(G_i - G_j) * S                 (M: j <= i < L)
+//   X_h = [s Gam dO; -dv] h~^T                     rows 0..63: dq part, rows 64..127: dW
+//   X_q = [dP diag(r_k); 0] K                      dq = X_h + X_q (rows 0..63)
+//   X_k = [diag(r_q) dP; 0]^T Q                    dk = X_k + diag(c) X_v (rows 0..63 / 64..127)
+//   X_v = [dO; v_new] dh~'^T                       rows 64..127 used
+//   dG_i = r_q,i q_i.dq_i - r_k,i k_i.dk_i, and on the last row also
+//          gamma <dh~', h~> + sum_i r_k,i k_i.(diag(c) X_v)_i
+// All products on tcgen05 (M = 128, accumulators in TMEM); q, k and dO come
+// in by TMA, h~, dh~' and v_new as the bf16 images the state kernels wrote,
+// dv (fp32) through registers.  One CTA per (chunk, v-head), one per SM.
+
+struct DqSm {
+  static constexpr int kQ = 0;                  // Q a0 | Q a1
+  static constexpr int kK = kQ + 2 * kAtom;     // K a0 | K a1
+  static constexpr int kDV = kK + 2 * kAtom;    // dO a0 | v_new a0 | dO a1 | v_new a1
+  static constexpr int kH = kDV + 4 * kAtom;    // h~ (two 128-row atoms)
+  static constexpr int kDH = kH + kStateImg;    // dh~'
+  static constexpr int kA1 = kDH + kStateImg;   // [s Gam dO; -dv]; later diag(c) X_v rows (fp32 [64][128])
+  static constexpr int kPk = kA1 + kStateImg;   // dP diag(r_k) atom | zero atom
+  static constexpr int kPq = kPk + 2 * kAtom;   // diag(r_q) dP atom | zero atom
+  static constexpr int kVec = kPq + 2 * kAtom;  // G, r_q, r_k, half-row dG [64] each; reduction [8]
+  static constexpr int kBar = kVec + (4 * 64 + 8) * 4;
+  static constexpr int kTmem = kBar + 4 * 8;    // mbarriers: loads, S, first products, second products
+  static constexpr int kBytes = kTmem + 8 + 1024;
+  static constexpr uint32_t kTx = 6 * kAtom + kVnImg + 2 * kStateImg;
+  static constexpr int kThreads = 256;
+  // TMEM columns: X_h 0-127, S then X_q 128-255, X_v 256-383, X_k 384-511
+  static constexpr uint32_t kXh = 0, kS = 128, kXq = 128, kXv = 256, kXk = 384;
+  static_assert(kBytes <= 227 * 1024, "shared memory");
+  static_assert(64 * 128 * 4 <= kStateImg, "the dK2 rows fit over the first product's A image");
+};
+
+__device__ __forceinline__ float dq_block_sum(float x, float* red) {
+  x = group_sum<32>(x);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < DqSm::kThreads / 32; ++i) t += red[i];
+  __syncthreads();
+  return t;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(DqSm::kThreads, 1)
+tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, float scale,
+                   const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tdo) {
+  using S = DqSm;
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  float* Gs = reinterpret_cast<float*>(sm + S::kVec);
+  float* rq = Gs + 64;
+  float* rk = rq + 64;
+  float* dgh = rk + 64;
+  float* red = dgh + 64;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::kTmem);
+  const uint32_t bar_ld = umma::smem_u32(bars), bar_s = umma::smem_u32(bars + 1), bar_a = umma::smem_u32(bars + 2),
+                 bar_b = umma::smem_u32(bars + 3);
+  int64_t n, lc;
+  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, colh = warp >> 2, row = quad * 32 + lane;
+  const bool rows_lo = quad < 2;  // TMEM lanes 0..63
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int64_t s = bos + lc * kChunk;
+  const int L = static_cast<int>(min64(kChunk, eos - s));
+  const int64_t img = static_cast<int64_t>(blockIdx.x) * p.HV + hv;  // blockIdx.x = the chunk's global index
+  constexpr bool kBf16 = !std::is_same<T, __half>::value;
+  const long long wlim = 2000000000LL;
+
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) umma::mbar_init(bars + i, 1);
+    umma::mbar_fence_init();
+    umma::mbar_arrive_expect_tx(bar_ld, S::kTx);
+    umma::tma_load_3d(sm + S::kQ, &tq, 0, h, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + S::kQ + kAtom, &tq, 64, h, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + S::kK, &tk, 0, h, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + S::kK + kAtom, &tk, 64, h, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + S::kDV, &tdo, 0, hv, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + S::kDV + 2 * kAtom, &tdo, 64, hv, static_cast<int>(s), bar_ld);
+    const uint8_t* vn = o.vn_img + img * kVnImg;
+    umma::bulk_g2s(sm + S::kDV + kAtom, vn, kAtom, bar_ld);
+    umma::bulk_g2s(sm + S::kDV + 3 * kAtom, vn + kAtom, kAtom, bar_ld);
+    umma::bulk_g2s(sm + S::kH, o.hs_img + img * kStateImg, kStateImg, bar_ld);
+    umma::bulk_g2s(sm + S::kDH, o.dh_img + img * kStateImg, kStateImg, bar_ld);
+  }
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, 512);
+    umma::fence_before_sync();
+  }
+  for (int e = tid; e < kAtom / 16; e += S::kThreads) {
+    reinterpret_cast<uint4*>(sm + S::kPk + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
+    reinterpret_cast<uint4*>(sm + S::kPq + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  if (tid < 64) Gs[tid] = tid < L ? o.gc[(s + tid) * p.HV + hv] : 0.f;
+  // dv row di, columns dc .. dc+31 (fp32 from the workspace)
+  const int di = tid >> 2, dc = (tid & 3) * 32;
+  float4 dvr[8];
+  {
+    const float* src = o.dvn + ((s + di) * p.HV + hv) * static_cast<int64_t>(D) + dc;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      dvr[u] = di < L ? *reinterpret_cast<const float4*>(src + u * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  umma::fence_proxy_async();  // the zero atoms are tcgen05 operands
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+  bool mine = umma::mbar_wait(bar_ld, 0, wlim);
+  if (!mine) record_error(w.err, 1, kSiteStLoad);
+  bool ok = !__syncthreads_or(!mine);  // uniform
+  uint32_t last_bar = 0;
+
+  if (ok) {
+    {  // L2-norm factors of the q and k rows: two threads per row, one atom each
+      const int r = tid >> 1, half = tid & 1, i = r & 63;
+      const uint8_t* at = sm + (r < 64 ? S::kQ : S::kK) + half * kAtom + i * 128;
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float x[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(at + c * 16), x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+      }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      if (half == 0) (r < 64 ? rq : rk)[i] = p.use_qk_l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
+    }
+    {  // A image of X_h: rows 0..63 s Gam dO (same swizzle as the dO atoms), rows 64..127 -dv
+      const int i = di;
+      const float f = i < L ? scale * expf(Gs[i]) : 0.f;
+      const int atom = (tid & 3) >> 1;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int pc = (tid & 1) * 4 + u;
+        float x[8];
+        unpack8<T>(*reinterpret_cast<const uint4*>(sm + S::kDV + atom * 2 * kAtom + i * 128 + pc * 16), x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] *= f;
+        *reinterpret_cast<uint4*>(sm + S::kA1 + atom * (kStateImg / 2) + i * 128 + pc * 16) = pack8<T>(x);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float4 a = dvr[2 * u], b = dvr[2 * u + 1];
+        const float x[8] = {-a.x, -a.y, -a.z, -a.w, -b.x, -b.y, -b.z, -b.w};
+        *reinterpret_cast<uint4*>(sm + S::kA1 + bwd_img_off(64 + i, dc + u * 8, 128)) = pack8<T>(x);
+      }
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    auto adv = [](int ks) { return static_cast<uint64_t>(((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4); };
+    if (warp == 0) {  // S, then X_h and X_v
+      umma::fence_after_sync();
+      if (umma::elect_one()) {
+        const uint32_t id64 = umma::idesc_f16(128, 64, kBf16, false, false);
+        const uint32_t id128 = umma::idesc_f16(128, 128, kBf16, false, false);
+        const uint64_t d_dv = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDV), 16, 1024);
+        const uint64_t d_vn = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDV + kAtom), 16, 1024);
+        const uint64_t d_a1 = umma::smem_desc_sw128(umma::smem_u32(sm + S::kA1), 16, 1024);
+        const uint64_t d_h = umma::smem_desc_sw128(umma::smem_u32(sm + S::kH), 16, 1024);
+        const uint64_t d_dh = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDH), 16, 1024);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) umma::mma_f16(tmem + S::kS, d_dv + adv(ks), d_vn + adv(ks), id64, ks > 0);
+        umma::mma_commit(bar_s);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) umma::mma_f16(tmem + S::kXh, d_a1 + adv(ks), d_h + adv(ks), id128, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) umma::mma_f16(tmem + S::kXv, d_dv + adv(ks), d_dh + adv(ks), id128, ks > 0);
+        umma::mma_commit(bar_a);
+      }
+      __syncwarp();
+      last_bar = bar_a;
+    }
+    if (rows_lo) {  // dP images from S (rows 0..63, 32 columns per thread)
+      mine = umma::mbar_wait(bar_s, 0, wlim);
+      if (!mine) record_error(w.err, 1, kSiteStMma1);
+      umma::fence_after_sync();
+      if (mine) {
+        float sv[32];
+        umma::tmem_ld32(tmem + S::kS + lane_base + colh * 32, sv);
+        const int i = row;
+        const float gi = Gs[i], rqi = rq[i];
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          float pk[8], pq[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int j = colh * 32 + q8 * 8 + e;
+            const float v = (i < L && j <= i) ? scale * expf(gi - Gs[j]) * sv[q8 * 8 + e] : 0.f;
+            pk[e] = v * rk[j];
+            pq[e] = v * rqi;
+          }
+          const int j0 = colh * 32 + q8 * 8;
+          const uint32_t off = i * 128 + ((((j0 >> 3) ^ (i & 7))) << 4);
+          *reinterpret_cast<uint4*>(sm + S::kPk + off) = pack8<T>(pk);
+          *reinterpret_cast<uint4*>(sm + S::kPq + off) = pack8<T>(pq);
+        }
+      }
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    ok = !__syncthreads_or(!mine);
+  }
+  if (ok && warp == 0) {  // X_q and X_k
+    umma::fence_after_sync();
+    if (umma::elect_one()) {
+      const uint32_t idq = umma::idesc_f16(128, 128, kBf16, false, true);
+      const uint32_t idk = umma::idesc_f16(128, 128, kBf16, true, true);
+      const uint64_t d_pk = umma::smem_desc_sw128(umma::smem_u32(sm + S::kPk), 16, 1024);
+      const uint64_t d_pq = umma::smem_desc_sw128(umma::smem_u32(sm + S::kPq), kAtom, 1024);
+      const uint64_t d_k = umma::smem_desc_sw128(umma::smem_u32(sm + S::kK), kAtom, 1024);
+      const uint64_t d_q = umma::smem_desc_sw128(umma::smem_u32(sm + S::kQ), kAtom, 1024);
+#pragma unroll
+      for (int ks = 0; ks < 64 / 16; ++ks)
+        umma::mma_f16(tmem + S::kXq, d_pk + ((ks * 32) >> 4), d_k + ((ks * 2048) >> 4), idq, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 64 / 16; ++ks)
+        umma::mma_f16(tmem + S::kXk, d_pq + ((ks * 2048) >> 4), d_q + ((ks * 2048) >> 4), idk, ks > 0);
+      umma::mma_commit(bar_b);
+    }
+    __syncwarp();
+    last_bar = bar_b;
+  }
+  float esum = 0.f, hp = 0.f;
+  if (ok) {
+    if (!rows_lo) {  // rows 64..127: dW, and diag(c) X_v into shared memory (over the consumed A image)
+      mine = umma::mbar_wait(bar_a, 0, wlim);
+      if (!mine) record_error(w.err, 1, kSiteStMma2);
+      umma::fence_after_sync();
+      if (mine) {
+        const int i = row - 64;
+        const bool live = i < L;
+        const float ci = live ? expf(Gs[L - 1] - Gs[i]) : 0.f;
+        float4* dk2 = reinterpret_cast<float4*>(sm + S::kA1) + i * 32;
+        float* dwrow = o.dw + ((s + i) * p.HV + hv) * static_cast<int64_t>(D);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int c0 = colh * 64 + half * 32;
+          float x[32];
+          umma::tmem_ld32(tmem + S::kXh + lane_base + c0, x);
+          if (live) {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4)
+              *reinterpret_cast<float4*>(dwrow + c0 + j4 * 4) = make_float4(x[j4 * 4], x[j4 * 4 + 1], x[j4 * 4 + 2], x[j4 * 4 + 3]);
+          }
+          umma::tmem_ld32(tmem + S::kXv + lane_base + c0, x);
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            const int col = c0 + q8 * 8;
+            float kv[8];
+            unpack8<T>(*reinterpret_cast<const uint4*>(sm + S::kK + (col >> 6) * kAtom + i * 128 +
+                                                       ((((col & 63) >> 3) ^ (i & 7)) << 4)), kv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              x[q8 * 8 + e] *= ci;
+              esum = fmaf(kv[e], x[q8 * 8 + e], esum);
+            }
+          }
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4)
+            dk2[((c0 >> 2) + j4) ^ (i & 31)] = make_float4(x[j4 * 4], x[j4 * 4 + 1], x[j4 * 4 + 2], x[j4 * 4 + 3]);
+        }
+        esum *= rk[i];
+      }
+    }
+    // <dh~', h~> over the two images (same layout)
+    for (int e = tid; e < kStateImg / 16; e += S::kThreads) {
+      float a[8], b[8];
+      unpack8<T>(reinterpret_cast<const uint4*>(sm + S::kH)[e], a);
+      unpack8<T>(reinterpret_cast<const uint4*>(sm + S::kDH)[e], b);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) hp = fmaf(a[k], b[k], hp);
+    }
+    ok = !__syncthreads_or(!mine);
+  }
+  float dg = 0.f;
+  if (ok && rows_lo) {  // rows 0..63: dq, dk
+    mine = umma::mbar_wait(bar_b, 0, wlim);
+    if (!mine) record_error(w.err, 1, kSiteStMma2);
+    umma::fence_after_sync();
+    if (mine) {
+      const int i = row;
+      const bool live = i < L;
+      const float4* dk2 = reinterpret_cast<const float4*>(sm + S::kA1) + i * 32;
+      float* dqrow = o.dqh + ((s + i) * p.HV + hv) * static_cast<int64_t>(D);
+      float* dkrow = o.dkh + ((s + i) * p.HV + hv) * static_cast<int64_t>(D);
+      float qd = 0.f, kd = 0.f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = colh * 64 + half * 32;
+        float a[32], b[32];
+        umma::tmem_ld32(tmem + S::kXh + lane_base + c0, a);
+        umma::tmem_ld32(tmem + S::kXq + lane_base + c0, b);
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int col = c0 + q8 * 8;
+          const uint32_t off = (col >> 6) * kAtom + i * 128 + ((((col & 63) >> 3) ^ (i & 7)) << 4);
+          float qv[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(sm + S::kQ + off), qv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            a[q8 * 8 + e] += b[q8 * 8 + e];
+            qd = fmaf(qv[e], a[q8 * 8 + e], qd);
+          }
+        }
+        if (live) {
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4)
+            *reinterpret_cast<float4*>(dqrow + c0 + j4 * 4) = make_float4(a[j4 * 4], a[j4 * 4 + 1], a[j4 * 4 + 2], a[j4 * 4 + 3]);
+        }
+        umma::tmem_ld32(tmem + S::kXk + lane_base + c0, a);
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const float4 t = dk2[((c0 >> 2) + j4) ^ (i & 31)];
+          a[j4 * 4] += t.x;
+          a[j4 * 4 + 1] += t.y;
+          a[j4 * 4 + 2] += t.z;
+          a[j4 * 4 + 3] += t.w;
+        }
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int col = c0 + q8 * 8;
+          const uint32_t off = (col >> 6) * kAtom + i * 128 + ((((col & 63) >> 3) ^ (i & 7)) << 4);
+          float kv[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(sm + S::kK + off), kv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) kd = fmaf(kv[e], a[q8 * 8 + e], kd);
+        }
+        if (live) {
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4)
+            *reinterpret_cast<float4*>(dkrow + c0 + j4 * 4) = make_float4(a[j4 * 4], a[j4 * 4 + 1], a[j4 * 4 + 2], a[j4 * 4 + 3]);
+        }
+      }
+      dg = rq[i] * qd - rk[i] * kd;
+      if (colh == 1) dgh[i] = dg;
+    }
+  }
+  if (ok) ok = !__syncthreads_or(!mine);
+  if (ok) {
+    const float hh = dq_block_sum(hp, red);
+    const float es = dq_block_sum(esum, red);
+    if (rows_lo && colh == 0) {
+      const int i = row;
+      float a = dg + dgh[i];
+      if (i == L - 1) a += expf(Gs[L - 1]) * hh + es;
+      if (i < L) o.dG[(s + i) * p.HV + hv] = a;
+    }
+  } else if (warp == 0 && last_bar) {  // drain (bounded) the products still in flight
+    umma::mbar_wait(last_bar, 0, 20000000LL);
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, 512);
+}
+
 // [Ttot, HV, 128] tensor with 32-column x 1 head x 64-token boxes, no swizzle.
 cudaError_t make_slice_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, CUtensorMapDataType dt,
                            int esize) {
@@ -342,7 +708,7 @@ cudaError_t make_slice_map(CUtensorMap* m, const void* ptr, int heads, int64_t t
 }
 
 template <typename T>
-cudaError_t launch_t(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, float* dhn, cudaStream_t s) {
+cudaError_t launch_t(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, uint8_t* dh_img, cudaStream_t s) {
   constexpr bool kF16 = std::is_same<T, __half>::value;
   const int64_t ttot = b.B * b.T;
   CUtensorMap tq, tk, tdo, tdv;
@@ -358,16 +724,40 @@ cudaError_t launch_t(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, flo
     return e;
   note_launch();
   kern<<<dim3(static_cast<unsigned>(b.N * (D / BwdSt::VS)), b.HV), kSt3Threads, BwdSt::kBytes, s>>>(
-      b, w, BwdOut{dvn, dhn}, tq, tk, tdo, tdv);
+      b, w, BwdOut{dvn, dh_img}, tq, tk, tdo, tdv);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_dqkw_t(const gdn_chunk_bwd_args& b, const Work& w, const DqkwOut& o, cudaStream_t s) {
+  constexpr bool kF16 = std::is_same<T, __half>::value;
+  const int64_t ttot = b.B * b.T;
+  const int64_t nc = chunk_upper_bound(ttot, b.N);
+  if (nc == 0) return cudaSuccess;
+  CUtensorMap tq, tk, tdo;
+  cudaError_t e;
+  if ((e = make_map(&tq, b.q, b.H, ttot, kF16)) != cudaSuccess) return e;
+  if ((e = make_map(&tk, b.k, b.H, ttot, kF16)) != cudaSuccess) return e;
+  if ((e = make_map(&tdo, b.dout, b.HV, ttot, kF16)) != cudaSuccess) return e;
+  auto kern = tc_bwd_dqkw_kernel<T>;
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSm::kBytes)) != cudaSuccess)
+    return e;
+  const float scale = b.scale > 0.f ? b.scale : 1.f / sqrtf(static_cast<float>(b.K));
+  note_launch();
+  kern<<<dim3(static_cast<unsigned>(nc), b.HV), DqSm::kThreads, DqSm::kBytes, s>>>(b, w, o, scale, tq, tk, tdo);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_bwd_state_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, float* dhn,
+cudaError_t launch_bwd_dqkw_tc(const gdn_chunk_bwd_args& b, const Work& w, const DqkwOut& o, cudaStream_t s) {
+  return b.qkv_dtype == GDN_F16 ? launch_dqkw_t<__half>(b, w, o, s) : launch_dqkw_t<__nv_bfloat16>(b, w, o, s);
+}
+
+cudaError_t launch_bwd_state_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, uint8_t* dh_img,
                                 cudaStream_t s) {
-  return b.qkv_dtype == GDN_F16 ? launch_t<__half>(b, w, dvn, dhn, s)
-                                : launch_t<__nv_bfloat16>(b, w, dvn, dhn, s);
+  return b.qkv_dtype == GDN_F16 ? launch_t<__half>(b, w, dvn, dh_img, s)
+                                : launch_t<__nv_bfloat16>(b, w, dvn, dh_img, s);
 }
 
 }  // namespace tc

@@ -772,11 +772,9 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
         }
         *reinterpret_cast<uint4*>(vnimg + umma::img_off(i, col, RSV)) = pack8<T>(vn);
         *reinterpret_cast<uint4*>(vtimg + umma::img_off(i, col, RSV)) = pack8<T>(vt);
-        if (STORE && bos + static_cast<int64_t>(c) * kChunk + i < eos) {
-          float* dst = w.vnew_out + ((bos + static_cast<int64_t>(c) * kChunk + i) * p.HV + hv) * D + v0 + col;
-          *reinterpret_cast<float4*>(dst) = make_float4(vn[0], vn[1], vn[2], vn[3]);
-          *reinterpret_cast<float4*>(dst + 4) = make_float4(vn[4], vn[5], vn[6], vn[7]);
-        }
+        if constexpr (STORE)  // every row, so that the image holds no stale values
+          *reinterpret_cast<uint4*>(w.vn_img + ((c0 + c) * p.HV + hv) * kVnImg + bwd_img_off(i, v0 + col, 64)) =
+              pack8<T>(vn);
       }
       umma::fence_proxy_async();
       umma::fence_before_sync();
@@ -811,13 +809,11 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
 #pragma unroll
       for (int q = 0; q < CW / 16; ++q) umma::tmem_ld16(t_dh + lane_base + colh * CW + q * 16, d + q * 16);
       const float g = sc[128];
-      if constexpr (STORE) {  // the state at this chunk's start, for the backward
-        float* dst = w.hs_out + ((c0 + c) * p.HV + hv) * static_cast<int64_t>(D) * D +
-                     static_cast<int64_t>(row) * D + v0 + colh * CW;
+      if constexpr (STORE) {  // the state at this chunk's start (as its products used it), for the backward
+        uint8_t* dst = w.hs_img + ((c0 + c) * p.HV + hv) * static_cast<int64_t>(kStateImg);
 #pragma unroll
-        for (int j4 = 0; j4 < CW / 4; ++j4)
-          *reinterpret_cast<float4*>(dst + j4 * 4) =
-              make_float4(hreg[j4 * 4], hreg[j4 * 4 + 1], hreg[j4 * 4 + 2], hreg[j4 * 4 + 3]);
+        for (int j8 = 0; j8 < CW / 8; ++j8)
+          *reinterpret_cast<uint4*>(dst + bwd_img_off(row, v0 + colh * CW + j8 * 8, 128)) = pack8<T>(hreg + j8 * 8);
       }
 #pragma unroll
       for (int j = 0; j < CW; ++j) hreg[j] = fmaf(g, hreg[j], d[j]);
@@ -1057,13 +1053,13 @@ cudaError_t run_wy_only(const gdn_chunk_args& a, void* wsv, cudaStream_t s, Work
 }
 
 template <typename T>
-cudaError_t run_state_store(const gdn_chunk_args& a, const Work& w0, float* hs, float* vnew, cudaStream_t s) {
+cudaError_t run_state_store(const gdn_chunk_args& a, const Work& w0, uint8_t* hs, uint8_t* vn, cudaStream_t s) {
   constexpr bool kF16 = std::is_same<T, __half>::value;
   const int64_t ttot = a.B * a.T;
   if (ttot == 0) return cudaSuccess;
   Work w = w0;
-  w.hs_out = hs;
-  w.vnew_out = vnew;
+  w.hs_img = hs;
+  w.vn_img = vn;
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
   CUtensorMap tq, tk;
   cudaError_t e;
@@ -1073,9 +1069,9 @@ cudaError_t run_state_store(const gdn_chunk_args& a, const Work& w0, float* hs, 
   return launch_state3<T, 32, true>(a, w, scale, tq, tk, s, hk);
 }
 
-cudaError_t launch_state_store(const gdn_chunk_args& a, const Work& w, float* hs, float* vnew, cudaStream_t s) {
-  return a.qkv_dtype == GDN_F16 ? run_state_store<__half>(a, w, hs, vnew, s)
-                                : run_state_store<__nv_bfloat16>(a, w, hs, vnew, s);
+cudaError_t launch_state_store(const gdn_chunk_args& a, const Work& w, uint8_t* hs, uint8_t* vn, cudaStream_t s) {
+  return a.qkv_dtype == GDN_F16 ? run_state_store<__half>(a, w, hs, vn, s)
+                                : run_state_store<__nv_bfloat16>(a, w, hs, vn, s);
 }
 
 cudaError_t launch_wy_only(const gdn_chunk_args& a, void* ws, cudaStream_t s, Work& w, float* gc_out) {

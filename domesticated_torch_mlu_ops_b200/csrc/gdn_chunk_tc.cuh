@@ -39,10 +39,10 @@ struct Work {
   int64_t stall_chunk;
   long long stall_limit;
   // The backward's recompute (launch_state_store): the state kernel also
-  // stores the fp32 state at every chunk start ([chunks][HV][K][V]) and the
-  // fp32 v_new ([Ttot][HV][V]); null otherwise.
-  float* hs_out;
-  float* vnew_out;
+  // stores, per (chunk, v-head), the state at the chunk start and v_new as
+  // bf16 operand images (bwd_img_off layouts); null otherwise.
+  uint8_t* hs_img;
+  uint8_t* vn_img;
   // The backward's recompute (launch_wy_only): the WY kernel also stores the
   // chunk-local cumsum of g ([Ttot][HV] fp32); null otherwise.
   float* gc_out;
@@ -173,6 +173,17 @@ struct St3 {
 };
 constexpr int kSt3Threads = 288;  // 8 epilogue warps + 1 load warp
 
+// Operand images of the backward (global memory, one per chunk and v-head):
+// a [rows][128] 16-bit matrix as two 128-byte-swizzled atoms of [rows][64]
+// (columns 0-63, then 64-127), the layout TMA writes with 128-byte swizzle.
+// rows = 128 for the states h and dh' (row = key index), 64 for v_new (row =
+// token).  Byte offset of element (r, c):
+__host__ __device__ constexpr uint32_t bwd_img_off(int r, int c, int rows) {
+  return static_cast<uint32_t>((c >> 6) * rows * 128 + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2);
+}
+constexpr int kStateImg = 128 * 128 * 2;  // 32 KiB
+constexpr int kVnImg = 64 * 128 * 2;      // 16 KiB
+
 // cuTensorMapEncodeTiled, resolved once through the runtime's driver entry point.
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -185,14 +196,29 @@ EncodeTiledFn encode_fn();
 // recurrence (its W images and row scales); `w` gets the workspace pointers.
 cudaError_t launch_wy_only(const gdn_chunk_args& a, void* ws, cudaStream_t s, Work& w, float* gc_out = nullptr);
 // The forward state kernel (32-column slices) after launch_wy_only, for the
-// backward's recompute: stores the fp32 state at every chunk start to hs and
-// v_new to vnew (the generic workspace layouts); a.o and a.final_state null.
-cudaError_t launch_state_store(const gdn_chunk_args& a, const Work& w, float* hs, float* vnew, cudaStream_t s);
+// backward's recompute: stores the state at every chunk start and v_new as
+// bf16 images (hs_img, vn_img: [chunks][HV] images, bwd_img_off layouts);
+// a.o and a.final_state null.
+cudaError_t launch_state_store(const gdn_chunk_args& a, const Work& w, uint8_t* hs_img, uint8_t* vn_img,
+                               cudaStream_t s);
 // The backward's state-gradient recurrence on tcgen05 (gdn_chunk_bwd_tc.cu):
 // reads dv_local from and writes dv to dvn ([Ttot][HV][V] fp32), writes dh'
-// of every chunk to dhn ([chunks][HV][K][V] fp32) and dh0.
-cudaError_t launch_bwd_state_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, float* dhn,
+// of every chunk as a bf16 image to dh_img ([chunks][HV], bwd_img_off) and dh0.
+cudaError_t launch_bwd_state_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, uint8_t* dh_img,
                                 cudaStream_t s);
+// dq, dk, dW and dG per (chunk, v-head) on tcgen05 (gdn_chunk_bwd_tc.cu),
+// from the images above, dv (fp32) and G: writes the per-v-head dq, dk
+// ([Ttot][HV][K] fp32, w.r.t. the normalised q, k), dW and dG as the generic
+// bwd_dqkw_kernel does.
+struct DqkwOut {
+  const float* dvn;
+  const float* gc;
+  const uint8_t* hs_img;
+  const uint8_t* dh_img;
+  const uint8_t* vn_img;
+  float *dqh, *dkh, *dw, *dG;
+};
+cudaError_t launch_bwd_dqkw_tc(const gdn_chunk_bwd_args& b, const Work& w, const DqkwOut& o, cudaStream_t s);
 
 // [Ttot, heads, 128] bf16/f16 tensor map with 64 x 64 boxes, 128-byte swizzle.
 cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, bool f16, int64_t tstride = 0);
