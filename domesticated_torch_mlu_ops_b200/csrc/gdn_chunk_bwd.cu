@@ -645,13 +645,13 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
                     reinterpret_cast<const uint8_t*>(base + ws.dhimg), reinterpret_cast<const uint8_t*>(base + ws.vnimg),
                     w.dqh, w.dkh, w.dw, w.dG};
       if ((e = tc::launch_bwd_dqkw_tc(b, tw, d, s)) != cudaSuccess) return e;
+      if ((e = tc::launch_bwd_wy_tc(b, tw, tc::WyOut{w.dvn, w.gc, w.dw, w.dkh, w.dG}, s)) != cudaSuccess) return e;
     } else {
-      note_launch();
+      note_launch(2);
       bwd_dqkw_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kDqkwSmem, s>>>(b, w, scale);
+      bwd_wy_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kWySmem, s>>>(b, w);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
-    note_launch();
-    bwd_wy_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kWySmem, s>>>(b, w);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   const int64_t rows = Ttot * b.H;
   if (rows > 0) {

@@ -30,6 +30,7 @@
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 #include "gdn_chunk_tc.cuh"
+#include "solve_tril.cuh"
 #include "umma.cuh"
 
 namespace gdn {
@@ -692,6 +693,438 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
   if (warp == 0) umma::tmem_dealloc(tmem, 512);
 }
 
+// ---------------------------------------------------------------------------
+// The WY-form gradients per (chunk, v-head): prepare_wy_repr_bwd
+// (triton/fla/wy_fast.py:173-401)
+// ---------------------------------------------------------------------------
+// With b = beta, Gam_i = exp(G_i), cw = b Gam, D_ij = exp(G_i - G_j),
+// k^ = diag(r_k) k and T = (I + A)^-1, A = tril_strict(diag(b) D * k^ k^^T):
+//   X1 = [K; dW] K^T          rows 0..63: S = k^ k^^T (with r_k scales), rows 64..127: dW k^^T
+//   X2 = [dv; V] V^T          rows 0..63: dv V^T
+//   dT  = (dW k^^T) diag(cw) + (dv V^T) diag(b)
+//   dR_w = T^T dW, dR_u = T^T dv, M2 = dT T^T, dA = -T^T M2 (strictly lower)
+//   dv_out = diag(b) dR_u
+//   dS = diag(b) D * dA,  dk^ += diag(cw) dR_w + dS k^ + dS^T k^
+//   db_i = v_i.dR_u,i + Gam_i k^_i.dR_w,i + sum_j<i dA_ij D_ij S_ij
+//   dG_i += cw_i k^_i.dR_w,i + sum_j F_ij - sum_j F_ji,  F = dS * S
+// T comes from the fp32 solve of the forward WY kernel (solve_tril64_mma);
+// every product runs on tcgen05 with bf16 operands (the reference rounds
+// each of these operands to the input dtype before its dot).
+
+struct WbSm {
+  static constexpr int kKD = 0;                 // K a0 | dW a0 | K a1 | dW a1
+  static constexpr int kDV = kKD + 4 * kAtom;   // dv a0 | V a0 | dv a1 | V a1
+  static constexpr int kT = kDV + 4 * kAtom;    // T image atom | zero atom
+  static constexpr int kDT = kT + 2 * kAtom;    // dT image atom | zero atom; later dS diag(r_k) | zero
+  static constexpr int kM2 = kDT + 2 * kAtom;   // -M2 image atom; later diag(r_k) dS atom | zero atom
+  static constexpr int kSk = kM2 + 2 * kAtom;   // S (fp32 [64][kMS])
+  static constexpr int kAf = kSk + 64 * kMS * 4;  // A (fp32 [64][kMS]); later dS (fp32)
+  static constexpr int kTf = kAf + 64 * kMS * 4;  // T (fp32 [64][kMS])
+  static constexpr int kDTf = kTf + 64 * kMS * 4; // dT (fp32 [64][kMS])
+  static constexpr int kZ = kDTf + 64 * kMS * 4;  // solve scratch
+  static constexpr int kVec = kZ + kMScratch * 4; // G, b, cw, r_k, db, dG, colsum [64] each
+  static constexpr int kBar = kVec + 7 * 64 * 4;
+  static constexpr int kTmem = kBar + 5 * 8;      // mbarriers: loads, X, R, dA, dK
+  static constexpr int kBytes = kTmem + 8 + 1024;
+  static constexpr uint32_t kTx = 4 * kAtom;      // K and V by TMA
+  static constexpr int kThreads = 256;
+  // TMEM columns: X1 0-63, X2 64-127 (then the dK sum 0-127), dR_w 128-255, dR_u 256-383, M2 384-447, dA 448-511
+  static constexpr uint32_t kX1 = 0, kX2 = 64, kDK = 0, kRw = 128, kRu = 256, kM = 384, kDA = 448;
+  static_assert(kBytes <= 227 * 1024, "shared memory");
+};
+
+// byte offset of element (r, c) in a pair of 64-row atoms laid out `stride` bytes apart (columns 0-63, 64-127)
+__device__ __forceinline__ uint32_t atom_pair_off(int r, int c, int stride) {
+  return static_cast<uint32_t>((c >> 6) * stride + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(WbSm::kThreads, 1)
+tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
+                 const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv) {
+  using S = WbSm;
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  float* Sk = reinterpret_cast<float*>(sm + S::kSk);
+  float* Af = reinterpret_cast<float*>(sm + S::kAf);
+  float* Tf = reinterpret_cast<float*>(sm + S::kTf);
+  float* dTf = reinterpret_cast<float*>(sm + S::kDTf);
+  float* Zs = reinterpret_cast<float*>(sm + S::kZ);
+  float* Gs = reinterpret_cast<float*>(sm + S::kVec);
+  float* bs = Gs + 64;
+  float* cw = bs + 64;
+  float* rk = cw + 64;
+  float* dbv = rk + 64;
+  float* dgv = dbv + 64;
+  float* csum = dgv + 64;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + S::kBar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + S::kTmem);
+  const uint32_t bar_ld = umma::smem_u32(bars), bar_x = umma::smem_u32(bars + 1), bar_r = umma::smem_u32(bars + 2),
+                 bar_da = umma::smem_u32(bars + 3), bar_dk = umma::smem_u32(bars + 4);
+  int64_t n, lc;
+  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, colh = warp >> 2, row = quad * 32 + lane;
+  const bool rows_lo = quad < 2;
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int64_t s = bos + lc * kChunk;
+  const int L = static_cast<int>(min64(kChunk, eos - s));
+  const int64_t rowK = static_cast<int64_t>(p.HV) * D;
+  constexpr bool kBf16 = !std::is_same<T, __half>::value;
+  const long long wlim = 2000000000LL;
+
+  if (tid == 0) {
+    for (int i = 0; i < 5; ++i) umma::mbar_init(bars + i, 1);
+    umma::mbar_fence_init();
+    umma::mbar_arrive_expect_tx(bar_ld, S::kTx);
+    umma::tma_load_3d(sm + S::kKD, &tk, 0, h, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + S::kKD + 2 * kAtom, &tk, 64, h, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + S::kDV + kAtom, &tv, 0, hv, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + S::kDV + 3 * kAtom, &tv, 64, hv, static_cast<int>(s), bar_ld);
+  }
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, 512);
+    umma::fence_before_sync();
+  }
+  for (int e = tid; e < kAtom / 16; e += S::kThreads) {  // zero halves of the M = 128 operands
+    reinterpret_cast<uint4*>(sm + S::kT + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
+    reinterpret_cast<uint4*>(sm + S::kDT + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
+    reinterpret_cast<uint4*>(sm + S::kM2 + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  if (tid < 64) {
+    const bool live = tid < L;
+    const float g = live ? o.gc[(s + tid) * p.HV + hv] : 0.f;
+    const float bt = live ? p.beta[(s + tid) * p.HV + hv] : 0.f;
+    Gs[tid] = g;
+    bs[tid] = bt;
+    cw[tid] = live ? bt * expf(g) : 0.f;
+    csum[tid] = 0.f;
+  }
+  {  // dW and dv rows (fp32) into their atoms; rows past the end are zeros
+    const int i = tid >> 2, c0 = (tid & 3) * 32;
+    const float* wsrc = o.dw + (s + i) * rowK + static_cast<int64_t>(hv) * D + c0;
+    const float* vsrc = o.dvn + (s + i) * rowK + static_cast<int64_t>(hv) * D + c0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float a[8], b[8];
+#pragma unroll
+      for (int e4 = 0; e4 < 2; ++e4) {
+        const float4 x = i < L ? *reinterpret_cast<const float4*>(wsrc + u * 8 + e4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 y = i < L ? *reinterpret_cast<const float4*>(vsrc + u * 8 + e4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        a[e4 * 4] = x.x; a[e4 * 4 + 1] = x.y; a[e4 * 4 + 2] = x.z; a[e4 * 4 + 3] = x.w;
+        b[e4 * 4] = y.x; b[e4 * 4 + 1] = y.y; b[e4 * 4 + 2] = y.z; b[e4 * 4 + 3] = y.w;
+      }
+      const int c = c0 + u * 8;
+      *reinterpret_cast<uint4*>(sm + S::kKD + kAtom + atom_pair_off(i, c, 2 * kAtom)) = pack8<T>(a);
+      *reinterpret_cast<uint4*>(sm + S::kDV + atom_pair_off(i, c, 2 * kAtom)) = pack8<T>(b);
+    }
+  }
+  umma::fence_proxy_async();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+  bool mine = umma::mbar_wait(bar_ld, 0, wlim);
+  if (!mine) record_error(w.err, 1, kSiteStLoad);
+  bool ok = !__syncthreads_or(!mine);
+  uint32_t last_bar = 0, last_par = 0;
+  auto adv = [](int ks) { return static_cast<uint64_t>(((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4); };
+  if (ok) {
+    if (warp == 0) {  // X1 = [K; dW] K^T, X2 = [dv; V] V^T
+      if (umma::elect_one()) {
+        const uint32_t id64 = umma::idesc_f16(128, 64, kBf16, false, false);
+        const uint64_t d_kd = umma::smem_desc_sw128(umma::smem_u32(sm + S::kKD), 16, 1024);
+        const uint64_t d_dv = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDV), 16, 1024);
+        const uint64_t d_v = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDV + kAtom), 16, 1024);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) umma::mma_f16(tmem + S::kX1, d_kd + adv(ks), d_kd + adv(ks), id64, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) umma::mma_f16(tmem + S::kX2, d_dv + adv(ks), d_v + adv(ks), id64, ks > 0);
+        umma::mma_commit(bar_x);
+      }
+      __syncwarp();
+      last_bar = bar_x;
+    }
+    {  // L2-norm factors of the k rows (two threads per row) while the products run
+      if (tid < 128) {
+        const int i = tid >> 1, half = tid & 1;
+        const uint8_t* at = sm + S::kKD + half * 2 * kAtom + i * 128;
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float x[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(at + c * 16), x);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        if (half == 0) rk[i] = p.use_qk_l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
+      }
+    }
+    __syncthreads();
+    mine = umma::mbar_wait(bar_x, 0, wlim);
+    if (!mine) record_error(w.err, 1, kSiteStMma1);
+    umma::fence_after_sync();
+    float tm[32];
+    if (mine) {
+      if (rows_lo) {  // S and A (rows 0..63), and dv V^T kept for dT
+        const int i = row;
+        float x[32];
+        umma::tmem_ld32(tmem + S::kX1 + lane_base + colh * 32, x);
+        umma::tmem_ld32(tmem + S::kX2 + lane_base + colh * 32, tm);
+        const float ri = rk[i], gi = Gs[i], bi = bs[i];
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = colh * 32 + jj;
+          const float sv = x[jj] * ri * rk[j];
+          Sk[i * kMS + j] = sv;
+          Af[i * kMS + j] = (i < L && j < i) ? bi * expf(gi - Gs[j]) * sv : 0.f;
+        }
+      } else {  // dW k^^T diag(cw) (rows 64..127)
+        const int i = row - 64;
+        float x[32];
+        umma::tmem_ld32(tmem + S::kX1 + lane_base + colh * 32, x);
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = colh * 32 + jj;
+          dTf[i * kMS + j] = x[jj] * rk[j] * cw[j];
+        }
+      }
+    }
+    ok = !__syncthreads_or(!mine);
+    if (ok && rows_lo) {  // dT += (dv V^T) diag(b)
+      const int i = row;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = colh * 32 + jj;
+        dTf[i * kMS + j] += tm[jj] * bs[j];
+      }
+    }
+  }
+  if (ok) {
+    solve_tril64_mma(Af, Tf, Zs);  // T = (I + A)^-1 (starts and ends with a barrier)
+    {  // T and dT images: thread -> row r, 32 columns
+      const int r = tid >> 2, c0 = (tid & 3) * 16;
+#pragma unroll
+      for (int q8 = 0; q8 < 2; ++q8) {
+        const int c = c0 + q8 * 8;
+        float t8[8], d8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          t8[e] = Tf[r * kMS + c + e];
+          d8[e] = dTf[r * kMS + c + e];
+        }
+        const uint32_t off = r * 128 + (((c >> 3) ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(sm + S::kT + off) = pack8<T>(t8);
+        *reinterpret_cast<uint4*>(sm + S::kDT + off) = pack8<T>(d8);
+      }
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {  // dR_w = T^T dW, dR_u = T^T dv, M2 = dT T^T
+      umma::fence_after_sync();
+      if (umma::elect_one()) {
+        const uint32_t idmn = umma::idesc_f16(128, 128, kBf16, true, true);
+        const uint32_t idm2 = umma::idesc_f16(128, 64, kBf16, false, false);
+        const uint64_t d_tt = umma::smem_desc_sw128(umma::smem_u32(sm + S::kT), kAtom, 1024);      // T^T, MN-major
+        const uint64_t d_dw = umma::smem_desc_sw128(umma::smem_u32(sm + S::kKD + kAtom), 2 * kAtom, 1024);
+        const uint64_t d_dvb = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDV), 2 * kAtom, 1024);
+        const uint64_t d_dt = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDT), 16, 1024);      // [dT; 0]
+        const uint64_t d_t = umma::smem_desc_sw128(umma::smem_u32(sm + S::kT), 16, 1024);        // T, K-major B
+#pragma unroll
+        for (int ks = 0; ks < 64 / 16; ++ks)
+          umma::mma_f16(tmem + S::kRw, d_tt + ((ks * 2048) >> 4), d_dw + ((ks * 2048) >> 4), idmn, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < 64 / 16; ++ks)
+          umma::mma_f16(tmem + S::kRu, d_tt + ((ks * 2048) >> 4), d_dvb + ((ks * 2048) >> 4), idmn, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < 64 / 16; ++ks)
+          umma::mma_f16(tmem + S::kM, d_dt + ((ks * 32) >> 4), d_t + ((ks * 32) >> 4), idm2, ks > 0);
+        umma::mma_commit(bar_r);
+      }
+      __syncwarp();
+      last_bar = bar_r;
+    }
+    mine = rows_lo ? umma::mbar_wait(bar_r, 0, wlim) : true;
+    if (!mine) record_error(w.err, 1, kSiteStMma2);
+    umma::fence_after_sync();
+    if (mine && rows_lo) {  // -M2 image (rows 0..63)
+      const int i = row;
+      float x[32];
+      umma::tmem_ld32(tmem + S::kM + lane_base + colh * 32, x);
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) {
+        float m[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m[e] = -x[q8 * 8 + e];
+        const int j0 = colh * 32 + q8 * 8;
+        *reinterpret_cast<uint4*>(sm + S::kM2 + i * 128 + ((((j0 >> 3) ^ (i & 7))) << 4)) = pack8<T>(m);
+      }
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    ok = !__syncthreads_or(!mine);
+  }
+  if (ok && warp == 0) {  // dA = T^T (-M2)
+    umma::fence_after_sync();
+    if (umma::elect_one()) {
+      const uint32_t ida = umma::idesc_f16(128, 64, kBf16, true, true);
+      const uint64_t d_tt = umma::smem_desc_sw128(umma::smem_u32(sm + S::kT), kAtom, 1024);
+      const uint64_t d_m2 = umma::smem_desc_sw128(umma::smem_u32(sm + S::kM2), kAtom, 1024);
+#pragma unroll
+      for (int ks = 0; ks < 64 / 16; ++ks)
+        umma::mma_f16(tmem + S::kDA, d_tt + ((ks * 2048) >> 4), d_m2 + ((ks * 2048) >> 4), ida, ks > 0);
+      umma::mma_commit(bar_da);
+    }
+    __syncwarp();
+    last_bar = bar_da;
+  }
+  if (ok) {
+    mine = rows_lo ? umma::mbar_wait(bar_da, 0, wlim) : true;
+    if (!mine) record_error(w.err, 1, kSiteStMma2);
+    umma::fence_after_sync();
+    if (mine && rows_lo) {  // rows 0..63: dv out, db, dG row terms, dS and its images
+      const int i = row;
+      const bool live = i < L;
+      const float bi = bs[i], gi = Gs[i], ri = rk[i];
+      // U path: v_i . dR_u,i and dv = diag(b) dR_u (this thread's 64 columns)
+      float a = 0.f, r = 0.f;
+      T* dvrow = static_cast<T*>(p.dv) + ((s + i) * p.HV + hv) * static_cast<int64_t>(D);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = colh * 64 + half * 32;
+        float x[32];
+        umma::tmem_ld32(tmem + S::kRu + lane_base + c0, x);
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int c = c0 + q8 * 8;
+          float vv[8], o8[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(sm + S::kDV + kAtom + atom_pair_off(i, c, 2 * kAtom)), vv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            a = fmaf(vv[e], x[q8 * 8 + e], a);
+            o8[e] = bi * x[q8 * 8 + e];
+          }
+          if (live) *reinterpret_cast<uint4*>(dvrow + c) = pack8<T>(o8);
+        }
+        umma::tmem_ld32(tmem + S::kRw + lane_base + c0, x);
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int c = c0 + q8 * 8;
+          float kv[8];
+          unpack8<T>(*reinterpret_cast<const uint4*>(sm + S::kKD + atom_pair_off(i, c, 2 * kAtom)), kv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) r = fmaf(kv[e], x[q8 * 8 + e], r);
+        }
+      }
+      r *= ri;  // k^_i . dR_w,i
+      // A path (this thread's 32 columns of dA): t_i and dS, F row sums
+      float x[32];
+      umma::tmem_ld32(tmem + S::kDA + lane_base + colh * 32, x);
+      float t = 0.f, fr = 0.f;
+      float dsk[32], dsr[32];
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = colh * 32 + jj;
+        const bool in = live && j < i;
+        const float dd = in ? expf(gi - Gs[j]) : 0.f;
+        const float sv = Sk[i * kMS + j];
+        t = fmaf(x[jj] * dd, sv, t);
+        const float ds = in ? bi * dd * x[jj] : 0.f;
+        Af[i * kMS + j] = ds;  // dS (fp32) for the column sums
+        fr = fmaf(ds, sv, fr);
+        dsk[jj] = ds * rk[j];
+        dsr[jj] = ds * ri;
+      }
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) {
+        const int j0 = colh * 32 + q8 * 8;
+        const uint32_t off = i * 128 + ((((j0 >> 3) ^ (i & 7))) << 4);
+        *reinterpret_cast<uint4*>(sm + S::kDT + off) = pack8<T>(dsk + q8 * 8);   // dS diag(r_k)
+        *reinterpret_cast<uint4*>(sm + S::kM2 + off) = pack8<T>(dsr + q8 * 8);   // diag(r_k) dS
+      }
+      // the two column halves meet in shared memory
+      const float db_part = a + expf(gi) * r + t;  // partial sums over this thread's columns
+      const float dg_part = cw[i] * r + fr;
+      if (colh == 1) {
+        dbv[i] = db_part;
+        dgv[i] = dg_part;
+      } else {
+        Zs[i] = db_part;  // the solve scratch is free again
+        Zs[64 + i] = dg_part;
+      }
+    }
+    umma::fence_proxy_async();
+    umma::fence_before_sync();
+    ok = !__syncthreads_or(!mine);
+  }
+  if (ok && warp == 0) {  // dK sum = [dS diag(r_k); 0] K + [diag(r_k) dS; 0]^T K  (into the X columns)
+    umma::fence_after_sync();
+    if (umma::elect_one()) {
+      const uint32_t idq = umma::idesc_f16(128, 128, kBf16, false, true);
+      const uint32_t idk = umma::idesc_f16(128, 128, kBf16, true, true);
+      const uint64_t d_sk = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDT), 16, 1024);
+      const uint64_t d_sr = umma::smem_desc_sw128(umma::smem_u32(sm + S::kM2), kAtom, 1024);
+      const uint64_t d_k = umma::smem_desc_sw128(umma::smem_u32(sm + S::kKD), 2 * kAtom, 1024);
+#pragma unroll
+      for (int ks = 0; ks < 64 / 16; ++ks)
+        umma::mma_f16(tmem + S::kDK, d_sk + ((ks * 32) >> 4), d_k + ((ks * 2048) >> 4), idq, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 64 / 16; ++ks)
+        umma::mma_f16(tmem + S::kDK, d_sr + ((ks * 2048) >> 4), d_k + ((ks * 2048) >> 4), idk, true);
+      umma::mma_commit(bar_dk);
+    }
+    __syncwarp();
+    last_bar = bar_dk;
+  }
+  if (ok) {
+    if (tid < 64) {  // column sums of F = dS * S: the sum_j F_ji term of dG_i
+      float f = 0.f;
+      for (int j = tid + 1; j < 64; ++j) f = fmaf(Af[j * kMS + tid], Sk[j * kMS + tid], f);
+      csum[tid] = f;
+    }
+    mine = rows_lo ? umma::mbar_wait(bar_dk, 0, wlim) : true;
+    if (!mine) record_error(w.err, 1, kSiteStMma2);
+    umma::fence_after_sync();
+    ok = !__syncthreads_or(!mine);
+  }
+  if (ok && rows_lo) {  // dk^ += diag(cw) dR_w + dK sum; db; dG
+    const int i = row;
+    const bool live = i < L;
+    const float ci = cw[i];
+    float* dkrow = o.dkh + ((s + i) * p.HV + hv) * static_cast<int64_t>(D);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int c0 = colh * 64 + half * 32;
+      float x[32], y[32];
+      umma::tmem_ld32(tmem + S::kRw + lane_base + c0, x);
+      umma::tmem_ld32(tmem + S::kDK + lane_base + c0, y);
+      if (live) {
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          float4 v = *reinterpret_cast<float4*>(dkrow + c0 + j4 * 4);
+          v.x += fmaf(ci, x[j4 * 4], y[j4 * 4]);
+          v.y += fmaf(ci, x[j4 * 4 + 1], y[j4 * 4 + 1]);
+          v.z += fmaf(ci, x[j4 * 4 + 2], y[j4 * 4 + 2]);
+          v.w += fmaf(ci, x[j4 * 4 + 3], y[j4 * 4 + 3]);
+          *reinterpret_cast<float4*>(dkrow + c0 + j4 * 4) = v;
+        }
+      }
+    }
+    if (colh == 0 && live) {
+      p.dbeta[(s + i) * p.HV + hv] = Zs[i] + dbv[i];
+      o.dG[(s + i) * p.HV + hv] += Zs[64 + i] + dgv[i] - csum[i];
+    }
+  }
+  if (!ok && warp == 0 && last_bar) umma::mbar_wait(last_bar, last_par, 20000000LL);
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, 512);
+}
+
 // [Ttot, HV, 128] tensor with 32-column x 1 head x 64-token boxes, no swizzle.
 cudaError_t make_slice_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, CUtensorMapDataType dt,
                            int esize) {
@@ -748,7 +1181,29 @@ cudaError_t launch_dqkw_t(const gdn_chunk_bwd_args& b, const Work& w, const Dqkw
   return cudaGetLastError();
 }
 
+template <typename T>
+cudaError_t launch_wy_t(const gdn_chunk_bwd_args& b, const Work& w, const WyOut& o, cudaStream_t s) {
+  constexpr bool kF16 = std::is_same<T, __half>::value;
+  const int64_t ttot = b.B * b.T;
+  const int64_t nc = chunk_upper_bound(ttot, b.N);
+  if (nc == 0) return cudaSuccess;
+  CUtensorMap tk, tv;
+  cudaError_t e;
+  if ((e = make_map(&tk, b.k, b.H, ttot, kF16)) != cudaSuccess) return e;
+  if ((e = make_map(&tv, b.v, b.HV, ttot, kF16)) != cudaSuccess) return e;
+  auto kern = tc_bwd_wy_kernel<T>;
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, WbSm::kBytes)) != cudaSuccess)
+    return e;
+  note_launch();
+  kern<<<dim3(static_cast<unsigned>(nc), b.HV), WbSm::kThreads, WbSm::kBytes, s>>>(b, w, o, tk, tv);
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_bwd_wy_tc(const gdn_chunk_bwd_args& b, const Work& w, const WyOut& o, cudaStream_t s) {
+  return b.qkv_dtype == GDN_F16 ? launch_wy_t<__half>(b, w, o, s) : launch_wy_t<__nv_bfloat16>(b, w, o, s);
+}
 
 cudaError_t launch_bwd_dqkw_tc(const gdn_chunk_bwd_args& b, const Work& w, const DqkwOut& o, cudaStream_t s) {
   return b.qkv_dtype == GDN_F16 ? launch_dqkw_t<__half>(b, w, o, s) : launch_dqkw_t<__nv_bfloat16>(b, w, o, s);

@@ -219,6 +219,16 @@ struct DqkwOut {
   float *dqh, *dkh, *dw, *dG;
 };
 cudaError_t launch_bwd_dqkw_tc(const gdn_chunk_bwd_args& b, const Work& w, const DqkwOut& o, cudaStream_t s);
+// The WY-form gradients per (chunk, v-head) on tcgen05 (gdn_chunk_bwd_tc.cu):
+// dv and dbeta into the call's outputs, dk (per v-head, w.r.t. the normalised
+// k) and dG added to what the dq/dk kernel wrote, as the generic bwd_wy_kernel.
+struct WyOut {
+  const float* dvn;  // dv (fp32)
+  const float* gc;   // G
+  const float* dw;   // dW (fp32, from the dq/dk kernel)
+  float *dkh, *dG;
+};
+cudaError_t launch_bwd_wy_tc(const gdn_chunk_bwd_args& b, const Work& w, const WyOut& o, cudaStream_t s);
 
 // [Ttot, heads, 128] bf16/f16 tensor map with 64 x 64 boxes, 128-byte swizzle.
 cudaError_t make_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, bool f16, int64_t tstride = 0);
