@@ -811,7 +811,6 @@ def _conv_bench(ops, dev, a, hbm, flush):
         "peak_gbs": hbm, "peak_kind": "measured HBM copy"}
 
 
-TF32_DENSE_NOMINAL_TFLOPS = 1100.0  # nominal dense TF32 tensor rate of a B200 (no measured figure on this pool)
 
 
 def bwd_flops_per_chunk_head(K, V):
@@ -861,12 +860,10 @@ def _bwd_bench(ops, dev, a, flush, tc_burst):
     return {"workload": "chunk_gated_delta_rule backward, config-1 shape (B=1 T=8192 H=16 HV=32 K=V=128 "
                         "bf16, q/k L2 norm, dO given, no final-state gradient), forward recompute included",
             "ms_per_call": ms, "tokens_per_s": B * T / (ms * 1e-3), "flops": flops, "tflops": tf,
-            "tf32_issued_tflops": 3 * tf,  # each fp32 multiply-add is three TF32 products (head/tail split)
-            "frac_tf32_nominal": 3 * tf / TF32_DENSE_NOMINAL_TFLOPS,
             "frac_tensor_bf16_measured": tf / tc_burst,
-            "kernels": "generic fp32 forward recompute (chunk_wy, chunk_state) + bwd_dvlocal, bwd_state, "
-                       "bwd_dqkw, bwd_wy, bwd_qk, bwd_dg (fp32 arithmetic; products on warp MMA, TF32 "
-                       "head/tail split)"}
+            "kernels": "chunk_prep (L2 norms) + tcgen05 recompute (tc_wy_kernel, tc_state3_kernel storing h "
+                       "and v_new images) + bwd_dvlocal (warp MMA, one TF32 product per step) + tcgen05 "
+                       "tc_bwd_state, tc_bwd_dqkw, tc_bwd_wy + bwd_qk, bwd_dg"}
 
 
 def run_reference(a):

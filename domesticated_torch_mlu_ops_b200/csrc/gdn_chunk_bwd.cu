@@ -625,7 +625,9 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
                                 static_cast<int>(kDqkwSmem))) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(bwd_wy_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(kWySmem))) != cudaSuccess) return e;
-  if (nc > 0) {
+  if (nc > 0 && tcb) {
+    if ((e = tc::launch_bwd_dvlocal_tc(b, tw, w.dvn, s)) != cudaSuccess) return e;
+  } else if (nc > 0) {
     note_launch();
     bwd_dvlocal_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kDvlSmem, s>>>(b, w, scale);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;

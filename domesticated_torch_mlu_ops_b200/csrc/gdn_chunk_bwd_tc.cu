@@ -1125,6 +1125,99 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
   if (warp == 0) umma::tmem_dealloc(tmem, 512);
 }
 
+// ---------------------------------------------------------------------------
+// dv_local = scale P^T dO per (chunk, v-head): chunk_bwd_dv_local
+// (triton/fla/chunk_o.py:233-778).  P is the forward WY kernel's image of
+// M * exp(G_i - G_j) * q^_i.k^_j (core-matrix layout, rows i); read with the
+// MN-major descriptor it is the A operand P^T (M = 64).  One product per
+// tile; dv_local (fp32) goes to the dv workspace, which the state-gradient
+// recurrence completes.
+constexpr int kDvlThreads = 128;
+// dynamic shared memory, padded so that at most four CTAs share an SM (four
+// 128-column TMEM allocations fill its 512 columns)
+constexpr int kDvlBytes = 56 * 1024;
+static_assert(2 * kAtom + kImg64x64 + 64 + 1024 <= kDvlBytes && 5 * (kDvlBytes + 1024) > 228 * 1024,
+              "at most four CTAs per SM");
+
+template <typename T>
+__global__ void __launch_bounds__(kDvlThreads)
+tc_bwd_dvlocal_kernel(const gdn_chunk_bwd_args p, const Work w, float* dvn, float scale,
+                      const __grid_constant__ CUtensorMap tdo) {
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* pim = sm + 2 * kAtom;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pim + kImg64x64);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  const uint32_t bar_ld = umma::smem_u32(bars), bar_mma = umma::smem_u32(bars + 1);
+  int64_t n, lc;
+  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hv = blockIdx.y;
+  int64_t bos, eos;
+  seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
+  const int64_t s = bos + lc * kChunk;
+  const int L = static_cast<int>(min64(kChunk, eos - s));
+  const int64_t hc = static_cast<int64_t>(hv) * w.ncu + blockIdx.x;
+  constexpr bool kBf16 = !std::is_same<T, __half>::value;
+  if (tid == 0) {
+    umma::mbar_init(bars, 1);
+    umma::mbar_init(bars + 1, 1);
+    umma::mbar_fence_init();
+    umma::mbar_arrive_expect_tx(bar_ld, 2 * kAtom + kImg64x64);
+    umma::tma_load_3d(sm, &tdo, 0, hv, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + kAtom, &tdo, 64, hv, static_cast<int>(s), bar_ld);
+    umma::bulk_g2s(pim, w.pimg + hc * kImg64x64, kImg64x64, bar_ld);
+  }
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, 128);
+    umma::fence_before_sync();
+  }
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  bool mine = warp == 0 ? umma::mbar_wait(bar_ld, 0) : true;
+  if (!mine) record_error(w.err, 1, kSiteStLoad);
+  bool ok = !__syncthreads_or(!mine);
+  if (ok && warp == 0) {
+    umma::fence_after_sync();
+    if (umma::elect_one()) {
+      const uint32_t id = umma::idesc_f16(64, 128, kBf16, true, true);
+      const uint64_t da = umma::smem_desc(umma::smem_u32(pim), RS64, 128);
+      const uint64_t db = umma::smem_desc_sw128(umma::smem_u32(sm), kAtom, 1024);
+#pragma unroll
+      for (int ks = 0; ks < 64 / 16; ++ks)
+        umma::mma_f16(tmem, da + ((ks * 2 * RS64) >> 4), db + ((ks * 2048) >> 4), id, ks > 0);
+      umma::mma_commit(bar_mma);
+    }
+    __syncwarp();
+  }
+  if (ok) {
+    mine = umma::mbar_wait(bar_mma, 0);
+    if (!mine) record_error(w.err, 1, kSiteStMma1);
+    umma::fence_after_sync();
+    // M = 64 accumulator: row j in lane j % 16 of warp j / 16
+    const int j = warp * 16 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    float* dst = dvn + ((s + j) * p.HV + hv) * static_cast<int64_t>(D);
+#pragma unroll
+    for (int q = 0; q < D / 32; ++q) {
+      float x[32];
+      umma::tmem_ld32(tmem + lane_base + q * 32, x);
+      if (mine && lane < 16 && j < L) {
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4)
+          *reinterpret_cast<float4*>(dst + q * 32 + j4 * 4) =
+              make_float4(scale * x[j4 * 4], scale * x[j4 * 4 + 1], scale * x[j4 * 4 + 2], scale * x[j4 * 4 + 3]);
+      }
+    }
+  }
+  if (warp == 0 && (!ok || !mine))  // drain (bounded) what may still be in flight before the memory is released
+    umma::mbar_wait(ok ? bar_mma : bar_ld, 0, 20000000LL);
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, 128);
+}
+
 // [Ttot, HV, 128] tensor with 32-column x 1 head x 64-token boxes, no swizzle.
 cudaError_t make_slice_map(CUtensorMap* m, const void* ptr, int heads, int64_t ttot, CUtensorMapDataType dt,
                            int esize) {
@@ -1199,7 +1292,29 @@ cudaError_t launch_wy_t(const gdn_chunk_bwd_args& b, const Work& w, const WyOut&
   return cudaGetLastError();
 }
 
+template <typename T>
+cudaError_t launch_dvl_t(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, cudaStream_t s) {
+  constexpr bool kF16 = std::is_same<T, __half>::value;
+  const int64_t ttot = b.B * b.T;
+  const int64_t nc = chunk_upper_bound(ttot, b.N);
+  if (nc == 0) return cudaSuccess;
+  CUtensorMap tdo;
+  cudaError_t e;
+  if ((e = make_map(&tdo, b.dout, b.HV, ttot, kF16)) != cudaSuccess) return e;
+  auto kern = tc_bwd_dvlocal_kernel<T>;
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDvlBytes)) != cudaSuccess)
+    return e;
+  const float scale = b.scale > 0.f ? b.scale : 1.f / sqrtf(static_cast<float>(b.K));
+  note_launch();
+  kern<<<dim3(static_cast<unsigned>(nc), b.HV), kDvlThreads, kDvlBytes, s>>>(b, w, dvn, scale, tdo);
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_bwd_dvlocal_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, cudaStream_t s) {
+  return b.qkv_dtype == GDN_F16 ? launch_dvl_t<__half>(b, w, dvn, s) : launch_dvl_t<__nv_bfloat16>(b, w, dvn, s);
+}
 
 cudaError_t launch_bwd_wy_tc(const gdn_chunk_bwd_args& b, const Work& w, const WyOut& o, cudaStream_t s) {
   return b.qkv_dtype == GDN_F16 ? launch_wy_t<__half>(b, w, o, s) : launch_wy_t<__nv_bfloat16>(b, w, o, s);

@@ -201,6 +201,9 @@ cudaError_t launch_wy_only(const gdn_chunk_args& a, void* ws, cudaStream_t s, Wo
 // a.o and a.final_state null.
 cudaError_t launch_state_store(const gdn_chunk_args& a, const Work& w, uint8_t* hs_img, uint8_t* vn_img,
                                cudaStream_t s);
+// dv_local = scale P^T dO per (chunk, v-head) on tcgen05 (gdn_chunk_bwd_tc.cu),
+// from the WY kernel's P images, into dvn ([Ttot][HV][V] fp32).
+cudaError_t launch_bwd_dvlocal_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, cudaStream_t s);
 // The backward's state-gradient recurrence on tcgen05 (gdn_chunk_bwd_tc.cu):
 // reads dv_local from and writes dv to dvn ([Ttot][HV][V] fp32), writes dh'
 // of every chunk as a bf16 image to dh_img ([chunks][HV], bwd_img_off) and dh0.
