@@ -586,8 +586,10 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
   // with the tensor-core path, the states and v_new come from the forward's
   // own kernels (tcgen05, bf16 roundings as in the forward); otherwise from
   // the generic fp32 recompute
-  cudaError_t e = launch_chunk_generic_recompute(a, ws.fwd, s, !tcb, !tcb);
-  if (e != cudaSuccess) return e;
+  cudaError_t e = cudaSuccess;
+  // the tensor-core kernels need none of the generic recompute's outputs (they
+  // take q, k raw and compute the L2 norms themselves)
+  if (!tcb && (e = launch_chunk_generic_recompute(a, ws.fwd, s)) != cudaSuccess) return e;
   char* base = static_cast<char*>(b.workspace);
   tc::Work tw{};
   if (tcb) {  // G from the tensor-core WY kernel; W and U of the generic one are not needed
@@ -601,7 +603,7 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
       return e;
   }
   BwdPtrs w;
-  w.coff = reinterpret_cast<const int64_t*>(base + ws.fwd.chunk_offsets);
+  w.coff = tcb ? tw.coff : reinterpret_cast<const int64_t*>(base + ws.fwd.chunk_offsets);
   w.gc = reinterpret_cast<const float*>(base + ws.fwd.gc);
   w.qn = reinterpret_cast<const float*>(base + ws.fwd.qn);
   w.kn = reinterpret_cast<const float*>(base + ws.fwd.kn);
@@ -671,19 +673,31 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
 BwdWorkspace plan_bwd_workspace(const gdn_chunk_bwd_args& b) {
   auto al = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
   BwdWorkspace w{};
-  w.fwd = plan_generic_workspace(forward_args(b));
   const int64_t Ttot = b.B * b.T;
   const int64_t nc = chunk_upper_bound(Ttot, b.N);
+  const bool tcb = bwd_tc_applies(b);
+  if (tcb) {  // the tensor-core path keeps only G of the forward's intermediates
+    ChunkWorkspace f{};
+    size_t o = 0;
+    f.err = o; o += al(16);
+    f.chunk_offsets = o; o += al(sizeof(int64_t) * (b.N + 1));
+    f.gc = o; o += al(sizeof(float) * Ttot * b.HV);
+    f.qn = f.kn = f.w = f.u = f.vnew = f.hs = o;
+    f.total = o;
+    w.fwd = f;
+  } else {
+    w.fwd = plan_generic_workspace(forward_args(b));
+  }
   size_t o = w.fwd.total;
   w.dvn = o; o += al(sizeof(float) * Ttot * b.HV * b.V);
-  w.dhn = o; o += al(sizeof(float) * nc * b.HV * b.K * b.V);
+  w.dhn = o; o += tcb ? 0 : al(sizeof(float) * nc * b.HV * b.K * b.V);  // the tensor-core path keeps dh' as images
   w.dqh = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
   w.dkh = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
   w.dw = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
   w.dG = o; o += al(sizeof(float) * Ttot * b.HV);
   w.tc = o;
   w.himg = w.dhimg = w.vnimg = o;
-  if (bwd_tc_applies(b)) {
+  if (tcb) {
     gdn_chunk_args fa = forward_args(b);
     fa.force_generic = 0;
     o += al(tc_workspace_bytes(fa) + 1024);  // the tensor-core layout aligns its regions to 1 KiB

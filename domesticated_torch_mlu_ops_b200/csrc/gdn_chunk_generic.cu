@@ -331,7 +331,7 @@ ChunkWorkspace plan_generic_workspace(const gdn_chunk_args& a) {
 
 template <typename T>
 static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s,
-                               bool with_output, bool with_state = true, bool with_wy = true) {
+                               bool with_output) {
   char* base = static_cast<char*>(a.workspace);
   GenericPtrs w;
   w.coff = reinterpret_cast<const int64_t*>(base + ws.chunk_offsets);
@@ -371,13 +371,11 @@ static cudaError_t run_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws
                                 static_cast<int>(st_smem))) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(chunk_out_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(out_smem))) != cudaSuccess) return e;
-  if (!with_wy) return cudaSuccess;
   if (nc > 0) {
     hk.pre(s);
     chunk_wy_kernel<T><<<dim3(static_cast<unsigned>(nc), a.HV), kGemmThreads, wy_smem, s>>>(a, w);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
-  if (!with_state) return cudaSuccess;
   hk.pre(s);
   chunk_state_kernel<<<dim3(static_cast<unsigned>(a.N), a.HV, (a.V + kStateCols - 1) / kStateCols),
                        kGemmThreads, st_smem, s>>>(a, w);
@@ -400,12 +398,11 @@ cudaError_t launch_chunk_generic(const gdn_chunk_args& a, const ChunkWorkspace& 
   }
 }
 
-cudaError_t launch_chunk_generic_recompute(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s,
-                                           bool with_state, bool with_wy) {
+cudaError_t launch_chunk_generic_recompute(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s) {
   switch (a.qkv_dtype) {
-    case GDN_F32: return run_generic<float>(a, ws, s, false, with_state, with_wy);
-    case GDN_BF16: return run_generic<__nv_bfloat16>(a, ws, s, false, with_state, with_wy);
-    case GDN_F16: return run_generic<__half>(a, ws, s, false, with_state, with_wy);
+    case GDN_F32: return run_generic<float>(a, ws, s, false);
+    case GDN_BF16: return run_generic<__nv_bfloat16>(a, ws, s, false);
+    case GDN_F16: return run_generic<__half>(a, ws, s, false);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -72,10 +72,8 @@ cudaError_t launch_decode_stream(const gdn_recurrent_args& a, cudaStream_t s);
 cudaError_t launch_recurrent_kfirst(const gdn_recurrent_plain_args& a, cudaStream_t s);
 cudaError_t launch_chunk_generic(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s);
 // The generic forward without its output stage: leaves G, q/k, W, U, v_new
-// and the per-chunk states in the workspace for the backward (with_state
-// false: G, q/k, W, U only; with_wy false: the normalised q/k only).
-cudaError_t launch_chunk_generic_recompute(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s,
-                                           bool with_state = true, bool with_wy = true);
+// and the per-chunk states in the workspace for the backward.
+cudaError_t launch_chunk_generic_recompute(const gdn_chunk_args& a, const ChunkWorkspace& ws, cudaStream_t s);
 BwdWorkspace plan_bwd_workspace(const gdn_chunk_bwd_args& a);
 cudaError_t launch_chunk_bwd(const gdn_chunk_bwd_args& a, const BwdWorkspace& ws, cudaStream_t s);
 // stall_chunk >= 0: test hook of gdn_chunk_fwd_test_stall (the first state
