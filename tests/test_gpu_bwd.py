@@ -52,6 +52,10 @@ CASES = [
     ("odd_dims", torch.float32, 1, 97, 3, 3, 40, 24, None, False, True, False, False),
     ("bf16_qwen_like", torch.bfloat16, 1, 256, 2, 4, 128, 128, [0, 100, 256], True, True, True, False),
     ("fp16_no_state", torch.float16, 2, 80, 2, 2, 64, 64, None, False, False, True, False),
+    # the tcgen05 backward (16-bit, K = V = 128): V-first states, empty and short sequences, no L2 norm
+    ("bf16_tc_vfirst_varlen", torch.bfloat16, 1, 300, 2, 4, 128, 128, [0, 0, 1, 65, 65, 300], True, True, True,
+     True),
+    ("fp16_tc_gva_nonorm", torch.float16, 2, 130, 1, 2, 128, 128, None, False, True, False, False),
 ]
 
 
