@@ -635,7 +635,8 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   if (tcb) {
-    if ((e = tc::launch_bwd_state_tc(b, tw, w.dvn, reinterpret_cast<uint8_t*>(base + ws.dhimg), s)) != cudaSuccess)
+    if ((e = tc::launch_bwd_state_tc(b, tw, w.dvn, reinterpret_cast<uint8_t*>(base + ws.dvimg),
+                                     reinterpret_cast<uint8_t*>(base + ws.dhimg), s)) != cudaSuccess)
       return e;
   } else {
     note_launch();
@@ -645,11 +646,13 @@ cudaError_t run_bwd(const gdn_chunk_bwd_args& b, const BwdWorkspace& ws, cudaStr
   }
   if (nc > 0) {
     if (tcb) {
-      tc::DqkwOut d{w.dvn, w.gc, reinterpret_cast<const uint8_t*>(base + ws.himg),
+      const uint8_t* dvimg = reinterpret_cast<const uint8_t*>(base + ws.dvimg);
+      uint8_t* dwimg = reinterpret_cast<uint8_t*>(base + ws.dwimg);
+      tc::DqkwOut d{dvimg, w.gc, reinterpret_cast<const uint8_t*>(base + ws.himg),
                     reinterpret_cast<const uint8_t*>(base + ws.dhimg), reinterpret_cast<const uint8_t*>(base + ws.vnimg),
-                    w.dqh, w.dkh, w.dw, w.dG};
+                    w.dqh, w.dkh, dwimg, w.dG};
       if ((e = tc::launch_bwd_dqkw_tc(b, tw, d, s)) != cudaSuccess) return e;
-      if ((e = tc::launch_bwd_wy_tc(b, tw, tc::WyOut{w.dvn, w.gc, w.dw, w.dkh, w.dG}, s)) != cudaSuccess) return e;
+      if ((e = tc::launch_bwd_wy_tc(b, tw, tc::WyOut{dvimg, w.gc, dwimg, w.dkh, w.dG}, s)) != cudaSuccess) return e;
     } else {
       note_launch(2);
       bwd_dqkw_kernel<T><<<dim3(static_cast<unsigned>(nc), b.HV), kT, kDqkwSmem, s>>>(b, w, scale);
@@ -693,10 +696,10 @@ BwdWorkspace plan_bwd_workspace(const gdn_chunk_bwd_args& b) {
   w.dhn = o; o += tcb ? 0 : al(sizeof(float) * nc * b.HV * b.K * b.V);  // the tensor-core path keeps dh' as images
   w.dqh = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
   w.dkh = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
-  w.dw = o; o += al(sizeof(float) * Ttot * b.HV * b.K);
+  w.dw = o; o += tcb ? 0 : al(sizeof(float) * Ttot * b.HV * b.K);  // the tensor-core path keeps dW as images
   w.dG = o; o += al(sizeof(float) * Ttot * b.HV);
   w.tc = o;
-  w.himg = w.dhimg = w.vnimg = o;
+  w.himg = w.dhimg = w.vnimg = w.dvimg = w.dwimg = o;
   if (tcb) {
     gdn_chunk_args fa = forward_args(b);
     fa.force_generic = 0;
@@ -705,6 +708,8 @@ BwdWorkspace plan_bwd_workspace(const gdn_chunk_bwd_args& b) {
     w.himg = o; o += al(imgs * tc::kStateImg);
     w.dhimg = o; o += al(imgs * tc::kStateImg);
     w.vnimg = o; o += al(imgs * tc::kVnImg);
+    w.dvimg = o; o += al(imgs * tc::kVnImg);
+    w.dwimg = o; o += al(imgs * tc::kVnImg);
   }
   w.total = o;
   return w;

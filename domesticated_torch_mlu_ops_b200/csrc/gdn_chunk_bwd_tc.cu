@@ -11,9 +11,8 @@
 // where dh~ is dh' rounded to the input dtype, a_i = scale exp(G_i) r_q,i and
 // gamma = exp(G_L): the row scales the forward WY kernel writes, whose W
 // images (L2 norm and gates folded in) this kernel reads.  q, k, dO and
-// dv_local come in by TMA.  Every chunk stores dv (fp32, completing the
-// dv_local the previous kernel wrote) and dh' (a bf16 operand image) for the
-// remaining backward kernels; dh at the first chunk is dh0.  The bf16 roundings are the
+// dv_local come in by TMA.  Every chunk stores dv and dh' as bf16 operand
+// images for the remaining backward kernels; dh at the first chunk is dh0.  The bf16 roundings are the
 // reference's: dh and dv are cast to the input dtype before their products.
 //
 // Warp roles as in the forward state kernel: warp 0 issues the MMAs, warps
@@ -61,7 +60,7 @@ struct BwdSt {
 };
 
 struct BwdOut {
-  float* dvn;       // [Ttot][HV][V]: dv_local in, dv out
+  uint8_t* dv_img;  // [chunks][HV] bf16 images of dv (bwd_img_off, 64 rows)
   uint8_t* dh_img;  // [chunks][HV] bf16 images of dh' (bwd_img_off, 128 rows)
 };
 
@@ -246,12 +245,11 @@ tc_bwd_state_kernel(const gdn_chunk_bwd_args p, const Work w, const BwdOut o,
         for (int e = 0; e < 8; ++e) m[e] = -dv[j8 * 8 + e];
         *reinterpret_cast<uint4*>(mdvimg + umma::img_off(i, colh * CW + j8 * 8, RSV)) = pack8<T>(m);
       }
-      if (live) {
-        float* dst = o.dvn + (s + i) * rowV + static_cast<int64_t>(hv) * D + v0 + colh * CW;
+      {  // every row, so that the image holds no stale values (rows past the end are zeros)
+        uint8_t* dst = o.dv_img + ((c0 + c) * p.HV + hv) * static_cast<int64_t>(kVnImg);
 #pragma unroll
-        for (int j4 = 0; j4 < CW / 4; ++j4)
-          *reinterpret_cast<float4*>(dst + j4 * 4) =
-              make_float4(dv[j4 * 4], dv[j4 * 4 + 1], dv[j4 * 4 + 2], dv[j4 * 4 + 3]);
+        for (int j8 = 0; j8 < CW / 8; ++j8)
+          *reinterpret_cast<uint4*>(dst + bwd_img_off(i, v0 + colh * CW + j8 * 8, 64)) = pack8<T>(dv + j8 * 8);
       }
     }
     umma::fence_proxy_async();
@@ -332,7 +330,7 @@ tc_bwd_state_kernel(const gdn_chunk_bwd_args p, const Work w, const BwdOut o,
 // norm factors (q^ = diag(r_q) q, k^ = diag(r_k) k):
 //   S   = [dO; v_new] v_new^T                     rows 0..63 used
 //   dP  = s M * exp(G_i - G_j) * S                 (M: j <= i < L)
-//   X_h = [s Gam dO; -dv] h~^T                     rows 0..63: dq part, rows 64..127: dW
+//   X_h = [s Gam dO; dv] h~^T                      rows 0..63: dq part, rows 64..127: -dW
 //   X_q = [dP diag(r_k); 0] K                      dq = X_h + X_q (rows 0..63)
 //   X_k = [diag(r_q) dP; 0]^T Q                    dk = X_k + diag(c) X_v (rows 0..63 / 64..127)
 //   X_v = [dO; v_new] dh~'^T                       rows 64..127 used
@@ -340,7 +338,8 @@ tc_bwd_state_kernel(const gdn_chunk_bwd_args p, const Work w, const BwdOut o,
 //          gamma <dh~', h~> + sum_i r_k,i k_i.(diag(c) X_v)_i
 // All products on tcgen05 (M = 128, accumulators in TMEM); q, k and dO come
 // in by TMA, h~, dh~' and v_new as the bf16 images the state kernels wrote,
-// dv (fp32) through registers.  One CTA per (chunk, v-head), one per SM.
+// dv as the bf16 image the state-gradient kernel wrote; dW leaves as a bf16
+// image for the WY-form gradient kernel.  One CTA per (chunk, v-head), one per SM.
 
 struct DqSm {
   static constexpr int kQ = 0;                  // Q a0 | Q a1
@@ -348,14 +347,14 @@ struct DqSm {
   static constexpr int kDV = kK + 2 * kAtom;    // dO a0 | v_new a0 | dO a1 | v_new a1
   static constexpr int kH = kDV + 4 * kAtom;    // h~ (two 128-row atoms)
   static constexpr int kDH = kH + kStateImg;    // dh~'
-  static constexpr int kA1 = kDH + kStateImg;   // [s Gam dO; -dv]; later diag(c) X_v rows (fp32 [64][128])
+  static constexpr int kA1 = kDH + kStateImg;   // [s Gam dO; dv]; later diag(c) X_v rows (fp32 [64][128])
   static constexpr int kPk = kA1 + kStateImg;   // dP diag(r_k) atom | zero atom
   static constexpr int kPq = kPk + 2 * kAtom;   // diag(r_q) dP atom | zero atom
   static constexpr int kVec = kPq + 2 * kAtom;  // G, r_q, r_k, half-row dG [64] each; reduction [8]
   static constexpr int kBar = kVec + (4 * 64 + 8) * 4;
   static constexpr int kTmem = kBar + 4 * 8;    // mbarriers: loads, S, first products, second products
   static constexpr int kBytes = kTmem + 8 + 1024;
-  static constexpr uint32_t kTx = 6 * kAtom + kVnImg + 2 * kStateImg;
+  static constexpr uint32_t kTx = 6 * kAtom + 2 * kVnImg + 2 * kStateImg;  // q, k, dO, v_new, dv, h, dh'
   static constexpr int kThreads = 256;
   // TMEM columns: X_h 0-127, S then X_q 128-255, X_v 256-383, X_k 384-511
   static constexpr uint32_t kXh = 0, kS = 128, kXq = 128, kXv = 256, kXk = 384;
@@ -420,6 +419,10 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
     umma::bulk_g2s(sm + S::kDV + 3 * kAtom, vn + kAtom, kAtom, bar_ld);
     umma::bulk_g2s(sm + S::kH, o.hs_img + img * kStateImg, kStateImg, bar_ld);
     umma::bulk_g2s(sm + S::kDH, o.dh_img + img * kStateImg, kStateImg, bar_ld);
+    // dv into rows 64..127 of the X_h operand (same swizzle phase as rows 0..63 of the image)
+    const uint8_t* dv = o.dv_img + img * kVnImg;
+    umma::bulk_g2s(sm + S::kA1 + 64 * 128, dv, kAtom, bar_ld);
+    umma::bulk_g2s(sm + S::kA1 + kStateImg / 2 + 64 * 128, dv + kAtom, kAtom, bar_ld);
   }
   if (warp == 0) {
     umma::tmem_alloc(tslot, 512);
@@ -430,15 +433,7 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
     reinterpret_cast<uint4*>(sm + S::kPq + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
   }
   if (tid < 64) Gs[tid] = tid < L ? o.gc[(s + tid) * p.HV + hv] : 0.f;
-  // dv row di, columns dc .. dc+31 (fp32 from the workspace)
-  const int di = tid >> 2, dc = (tid & 3) * 32;
-  float4 dvr[8];
-  {
-    const float* src = o.dvn + ((s + di) * p.HV + hv) * static_cast<int64_t>(D) + dc;
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      dvr[u] = di < L ? *reinterpret_cast<const float4*>(src + u * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+  const int di = tid >> 2;
   umma::fence_proxy_async();  // the zero atoms are tcgen05 operands
   __syncthreads();
   umma::fence_after_sync();
@@ -464,7 +459,7 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
       ss += __shfl_xor_sync(0xffffffffu, ss, 1);
       if (half == 0) (r < 64 ? rq : rk)[i] = p.use_qk_l2norm ? rsqrtf(ss + 1e-6f) : 1.f;
     }
-    {  // A image of X_h: rows 0..63 s Gam dO (same swizzle as the dO atoms), rows 64..127 -dv
+    {  // A operand of X_h: rows 0..63 s Gam dO (same swizzle as the dO atoms); rows 64..127 hold dv
       const int i = di;
       const float f = i < L ? scale * expf(Gs[i]) : 0.f;
       const int atom = (tid & 3) >> 1;
@@ -476,12 +471,6 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
 #pragma unroll
         for (int e = 0; e < 8; ++e) x[e] *= f;
         *reinterpret_cast<uint4*>(sm + S::kA1 + atom * (kStateImg / 2) + i * 128 + pc * 16) = pack8<T>(x);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float4 a = dvr[2 * u], b = dvr[2 * u + 1];
-        const float x[8] = {-a.x, -a.y, -a.z, -a.w, -b.x, -b.y, -b.z, -b.w};
-        *reinterpret_cast<uint4*>(sm + S::kA1 + bwd_img_off(64 + i, dc + u * 8, 128)) = pack8<T>(x);
       }
     }
     umma::fence_proxy_async();
@@ -562,7 +551,7 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
   }
   float esum = 0.f, hp = 0.f;
   if (ok) {
-    if (!rows_lo) {  // rows 64..127: dW, and diag(c) X_v into shared memory (over the consumed A image)
+    if (!rows_lo) {  // rows 64..127: dW (image), and diag(c) X_v into shared memory (over the consumed A image)
       mine = umma::mbar_wait(bar_a, 0, wlim);
       if (!mine) record_error(w.err, 1, kSiteStMma2);
       umma::fence_after_sync();
@@ -571,16 +560,18 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
         const bool live = i < L;
         const float ci = live ? expf(Gs[L - 1] - Gs[i]) : 0.f;
         float4* dk2 = reinterpret_cast<float4*>(sm + S::kA1) + i * 32;
-        float* dwrow = o.dw + ((s + i) * p.HV + hv) * static_cast<int64_t>(D);
+        uint8_t* dwimg = o.dw_img + img * kVnImg;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int c0 = colh * 64 + half * 32;
           float x[32];
           umma::tmem_ld32(tmem + S::kXh + lane_base + c0, x);
-          if (live) {
 #pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4)
-              *reinterpret_cast<float4*>(dwrow + c0 + j4 * 4) = make_float4(x[j4 * 4], x[j4 * 4 + 1], x[j4 * 4 + 2], x[j4 * 4 + 3]);
+          for (int q8 = 0; q8 < 4; ++q8) {  // every row (zeros past the end): dW = -dv h~^T
+            float m[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) m[e] = -x[q8 * 8 + e];
+            *reinterpret_cast<uint4*>(dwimg + bwd_img_off(i, c0 + q8 * 8, 64)) = pack8<T>(m);
           }
           umma::tmem_ld32(tmem + S::kXv + lane_base + c0, x);
 #pragma unroll
@@ -726,7 +717,7 @@ struct WbSm {
   static constexpr int kBar = kVec + 7 * 64 * 4;
   static constexpr int kTmem = kBar + 5 * 8;      // mbarriers: loads, X, R, dA, dK
   static constexpr int kBytes = kTmem + 8 + 1024;
-  static constexpr uint32_t kTx = 4 * kAtom;      // K and V by TMA
+  static constexpr uint32_t kTx = 4 * kAtom + 2 * kVnImg;  // K and V by TMA, the dW and dv images
   static constexpr int kThreads = 256;
   // TMEM columns: X1 0-63, X2 64-127 (then the dK sum 0-127), dR_w 128-255, dR_u 256-383, M2 384-447, dA 448-511
   static constexpr uint32_t kX1 = 0, kX2 = 64, kDK = 0, kRw = 128, kRu = 256, kM = 384, kDA = 448;
@@ -783,6 +774,13 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
     umma::tma_load_3d(sm + S::kKD + 2 * kAtom, &tk, 64, h, static_cast<int>(s), bar_ld);
     umma::tma_load_3d(sm + S::kDV + kAtom, &tv, 0, hv, static_cast<int>(s), bar_ld);
     umma::tma_load_3d(sm + S::kDV + 3 * kAtom, &tv, 64, hv, static_cast<int>(s), bar_ld);
+    const int64_t img = static_cast<int64_t>(blockIdx.x) * p.HV + hv;
+    const uint8_t* dw = o.dw_img + img * kVnImg;
+    const uint8_t* dv = o.dv_img + img * kVnImg;
+    umma::bulk_g2s(sm + S::kKD + kAtom, dw, kAtom, bar_ld);
+    umma::bulk_g2s(sm + S::kKD + 3 * kAtom, dw + kAtom, kAtom, bar_ld);
+    umma::bulk_g2s(sm + S::kDV, dv, kAtom, bar_ld);
+    umma::bulk_g2s(sm + S::kDV + 2 * kAtom, dv + kAtom, kAtom, bar_ld);
   }
   if (warp == 0) {
     umma::tmem_alloc(tslot, 512);
@@ -801,25 +799,6 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
     bs[tid] = bt;
     cw[tid] = live ? bt * expf(g) : 0.f;
     csum[tid] = 0.f;
-  }
-  {  // dW and dv rows (fp32) into their atoms; rows past the end are zeros
-    const int i = tid >> 2, c0 = (tid & 3) * 32;
-    const float* wsrc = o.dw + (s + i) * rowK + static_cast<int64_t>(hv) * D + c0;
-    const float* vsrc = o.dvn + (s + i) * rowK + static_cast<int64_t>(hv) * D + c0;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      float a[8], b[8];
-#pragma unroll
-      for (int e4 = 0; e4 < 2; ++e4) {
-        const float4 x = i < L ? *reinterpret_cast<const float4*>(wsrc + u * 8 + e4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 y = i < L ? *reinterpret_cast<const float4*>(vsrc + u * 8 + e4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-        a[e4 * 4] = x.x; a[e4 * 4 + 1] = x.y; a[e4 * 4 + 2] = x.z; a[e4 * 4 + 3] = x.w;
-        b[e4 * 4] = y.x; b[e4 * 4 + 1] = y.y; b[e4 * 4 + 2] = y.z; b[e4 * 4 + 3] = y.w;
-      }
-      const int c = c0 + u * 8;
-      *reinterpret_cast<uint4*>(sm + S::kKD + kAtom + atom_pair_off(i, c, 2 * kAtom)) = pack8<T>(a);
-      *reinterpret_cast<uint4*>(sm + S::kDV + atom_pair_off(i, c, 2 * kAtom)) = pack8<T>(b);
-    }
   }
   umma::fence_proxy_async();
   __syncthreads();
@@ -1234,7 +1213,8 @@ cudaError_t make_slice_map(CUtensorMap* m, const void* ptr, int heads, int64_t t
 }
 
 template <typename T>
-cudaError_t launch_t(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, uint8_t* dh_img, cudaStream_t s) {
+cudaError_t launch_t(const gdn_chunk_bwd_args& b, const Work& w, const float* dvn, uint8_t* dv_img, uint8_t* dh_img,
+                     cudaStream_t s) {
   constexpr bool kF16 = std::is_same<T, __half>::value;
   const int64_t ttot = b.B * b.T;
   CUtensorMap tq, tk, tdo, tdv;
@@ -1250,7 +1230,7 @@ cudaError_t launch_t(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, uin
     return e;
   note_launch();
   kern<<<dim3(static_cast<unsigned>(b.N * (D / BwdSt::VS)), b.HV), kSt3Threads, BwdSt::kBytes, s>>>(
-      b, w, BwdOut{dvn, dh_img}, tq, tk, tdo, tdv);
+      b, w, BwdOut{dv_img, dh_img}, tq, tk, tdo, tdv);
   return cudaGetLastError();
 }
 
@@ -1324,10 +1304,10 @@ cudaError_t launch_bwd_dqkw_tc(const gdn_chunk_bwd_args& b, const Work& w, const
   return b.qkv_dtype == GDN_F16 ? launch_dqkw_t<__half>(b, w, o, s) : launch_dqkw_t<__nv_bfloat16>(b, w, o, s);
 }
 
-cudaError_t launch_bwd_state_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, uint8_t* dh_img,
-                                cudaStream_t s) {
-  return b.qkv_dtype == GDN_F16 ? launch_t<__half>(b, w, dvn, dh_img, s)
-                                : launch_t<__nv_bfloat16>(b, w, dvn, dh_img, s);
+cudaError_t launch_bwd_state_tc(const gdn_chunk_bwd_args& b, const Work& w, const float* dvn, uint8_t* dv_img,
+                                uint8_t* dh_img, cudaStream_t s) {
+  return b.qkv_dtype == GDN_F16 ? launch_t<__half>(b, w, dvn, dv_img, dh_img, s)
+                                : launch_t<__nv_bfloat16>(b, w, dvn, dv_img, dh_img, s);
 }
 
 }  // namespace tc

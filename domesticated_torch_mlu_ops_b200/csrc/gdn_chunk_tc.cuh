@@ -205,30 +205,33 @@ cudaError_t launch_state_store(const gdn_chunk_args& a, const Work& w, uint8_t* 
 // from the WY kernel's P images, into dvn ([Ttot][HV][V] fp32).
 cudaError_t launch_bwd_dvlocal_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, cudaStream_t s);
 // The backward's state-gradient recurrence on tcgen05 (gdn_chunk_bwd_tc.cu):
-// reads dv_local from and writes dv to dvn ([Ttot][HV][V] fp32), writes dh'
-// of every chunk as a bf16 image to dh_img ([chunks][HV], bwd_img_off) and dh0.
-cudaError_t launch_bwd_state_tc(const gdn_chunk_bwd_args& b, const Work& w, float* dvn, uint8_t* dh_img,
-                                cudaStream_t s);
+// reads dv_local from dvn ([Ttot][HV][V] fp32), writes dv and dh' of every
+// chunk as bf16 images (dv_img: 64 rows, dh_img: 128 rows; [chunks][HV],
+// bwd_img_off) and dh0.
+cudaError_t launch_bwd_state_tc(const gdn_chunk_bwd_args& b, const Work& w, const float* dvn, uint8_t* dv_img,
+                                uint8_t* dh_img, cudaStream_t s);
 // dq, dk, dW and dG per (chunk, v-head) on tcgen05 (gdn_chunk_bwd_tc.cu),
-// from the images above, dv (fp32) and G: writes the per-v-head dq, dk
-// ([Ttot][HV][K] fp32, w.r.t. the normalised q, k), dW and dG as the generic
-// bwd_dqkw_kernel does.
+// from the images above and G: writes the per-v-head dq, dk ([Ttot][HV][K]
+// fp32, w.r.t. the normalised q, k) and dG as the generic bwd_dqkw_kernel
+// does, and dW as an image.
 struct DqkwOut {
-  const float* dvn;
+  const uint8_t* dv_img;
   const float* gc;
   const uint8_t* hs_img;
   const uint8_t* dh_img;
   const uint8_t* vn_img;
-  float *dqh, *dkh, *dw, *dG;
+  float *dqh, *dkh;
+  uint8_t* dw_img;  // dW as a bf16 image (64 rows) for the WY-form gradient kernel
+  float* dG;
 };
 cudaError_t launch_bwd_dqkw_tc(const gdn_chunk_bwd_args& b, const Work& w, const DqkwOut& o, cudaStream_t s);
 // The WY-form gradients per (chunk, v-head) on tcgen05 (gdn_chunk_bwd_tc.cu):
 // dv and dbeta into the call's outputs, dk (per v-head, w.r.t. the normalised
 // k) and dG added to what the dq/dk kernel wrote, as the generic bwd_wy_kernel.
 struct WyOut {
-  const float* dvn;  // dv (fp32)
-  const float* gc;   // G
-  const float* dw;   // dW (fp32, from the dq/dk kernel)
+  const uint8_t* dv_img;  // dv (bf16 image, from the state-gradient kernel)
+  const float* gc;        // G
+  const uint8_t* dw_img;  // dW (bf16 image, from the dq/dk kernel)
   float *dkh, *dG;
 };
 cudaError_t launch_bwd_wy_tc(const gdn_chunk_bwd_args& b, const Work& w, const WyOut& o, cudaStream_t s);

@@ -31,7 +31,7 @@ struct BwdWorkspace {
   size_t dw;        // f32 [Ttot][HV][K] gradient of W
   size_t dG;        // f32 [Ttot][HV] gradient of the chunk-local cumsum of g
   size_t tc;        // bf16/f16 with K = V = 128: the tensor-core WY workspace (W images, row scales)
-  size_t himg, dhimg, vnimg;  // and the bf16 images of h, dh' and v_new per (chunk, v-head)
+  size_t himg, dhimg, vnimg, dvimg, dwimg;  // and the bf16 images of h, dh', v_new, dv, dW per (chunk, v-head)
   size_t total;
 };
 
