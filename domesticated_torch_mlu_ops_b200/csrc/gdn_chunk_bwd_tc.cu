@@ -432,7 +432,7 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
     reinterpret_cast<uint4*>(sm + S::kPk + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
     reinterpret_cast<uint4*>(sm + S::kPq + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
   }
-  if (tid < 64) Gs[tid] = tid < L ? o.gc[(s + tid) * p.HV + hv] : 0.f;
+  if (tid < 64) Gs[tid] = tid < L ? o.gc[(s + tid) * p.HV + hv] * kLog2e : 0.f;  // G in the log2 domain
   const int di = tid >> 2;
   umma::fence_proxy_async();  // the zero atoms are tcgen05 operands
   __syncthreads();
@@ -461,7 +461,7 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
     }
     {  // A operand of X_h: rows 0..63 s Gam dO (same swizzle as the dO atoms); rows 64..127 hold dv
       const int i = di;
-      const float f = i < L ? scale * expf(Gs[i]) : 0.f;
+      const float f = i < L ? scale * exp2f(Gs[i]) : 0.f;
       const int atom = (tid & 3) >> 1;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -514,7 +514,7 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int j = colh * 32 + q8 * 8 + e;
-            const float v = (i < L && j <= i) ? scale * expf(gi - Gs[j]) * sv[q8 * 8 + e] : 0.f;
+            const float v = (i < L && j <= i) ? scale * exp2f(gi - Gs[j]) * sv[q8 * 8 + e] : 0.f;
             pk[e] = v * rk[j];
             pq[e] = v * rqi;
           }
@@ -558,7 +558,7 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
       if (mine) {
         const int i = row - 64;
         const bool live = i < L;
-        const float ci = live ? expf(Gs[L - 1] - Gs[i]) : 0.f;
+        const float ci = live ? exp2f(Gs[L - 1] - Gs[i]) : 0.f;
         float4* dk2 = reinterpret_cast<float4*>(sm + S::kA1) + i * 32;
         uint8_t* dwimg = o.dw_img + img * kVnImg;
 #pragma unroll
@@ -673,7 +673,7 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
     if (rows_lo && colh == 0) {
       const int i = row;
       float a = dg + dgh[i];
-      if (i == L - 1) a += expf(Gs[L - 1]) * hh + es;
+      if (i == L - 1) a += exp2f(Gs[L - 1]) * hh + es;
       if (i < L) o.dG[(s + i) * p.HV + hv] = a;
     }
   } else if (warp == 0 && last_bar) {  // drain (bounded) the products still in flight
@@ -795,9 +795,9 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
     const bool live = tid < L;
     const float g = live ? o.gc[(s + tid) * p.HV + hv] : 0.f;
     const float bt = live ? p.beta[(s + tid) * p.HV + hv] : 0.f;
-    Gs[tid] = g;
+    Gs[tid] = g * kLog2e;  // G in the log2 domain
     bs[tid] = bt;
-    cw[tid] = live ? bt * expf(g) : 0.f;
+    cw[tid] = live ? bt * exp2f(g * kLog2e) : 0.f;
     csum[tid] = 0.f;
   }
   umma::fence_proxy_async();
@@ -859,7 +859,7 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
           const int j = colh * 32 + jj;
           const float sv = x[jj] * ri * rk[j];
           Sk[i * kMS + j] = sv;
-          Af[i * kMS + j] = (i < L && j < i) ? bi * expf(gi - Gs[j]) * sv : 0.f;
+          Af[i * kMS + j] = (i < L && j < i) ? bi * exp2f(gi - Gs[j]) * sv : 0.f;
         }
       } else {  // dW k^^T diag(cw) (rows 64..127)
         const int i = row - 64;
@@ -1009,7 +1009,7 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
       for (int jj = 0; jj < 32; ++jj) {
         const int j = colh * 32 + jj;
         const bool in = live && j < i;
-        const float dd = in ? expf(gi - Gs[j]) : 0.f;
+        const float dd = in ? exp2f(gi - Gs[j]) : 0.f;
         const float sv = Sk[i * kMS + j];
         t = fmaf(x[jj] * dd, sv, t);
         const float ds = in ? bi * dd * x[jj] : 0.f;
@@ -1026,7 +1026,7 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
         *reinterpret_cast<uint4*>(sm + S::kM2 + off) = pack8<T>(dsr + q8 * 8);   // diag(r_k) dS
       }
       // the two column halves meet in shared memory
-      const float db_part = a + expf(gi) * r + t;  // partial sums over this thread's columns
+      const float db_part = a + exp2f(gi) * r + t;  // partial sums over this thread's columns
       const float dg_part = cw[i] * r + fr;
       if (colh == 1) {
         dbv[i] = db_part;
@@ -1060,10 +1060,14 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
     last_bar = bar_dk;
   }
   if (ok) {
-    if (tid < 64) {  // column sums of F = dS * S: the sum_j F_ji term of dG_i
+    {  // column sums of F = dS * S (the sum_j F_ji term of dG_i): four threads per column, 16 rows each
+      const int col = tid >> 2, part = tid & 3;
       float f = 0.f;
-      for (int j = tid + 1; j < 64; ++j) f = fmaf(Af[j * kMS + tid], Sk[j * kMS + tid], f);
-      csum[tid] = f;
+#pragma unroll 4
+      for (int j = part * 16; j < part * 16 + 16; ++j) f = fmaf(Af[j * kMS + col], Sk[j * kMS + col], f);
+      f += __shfl_xor_sync(0xffffffffu, f, 1);
+      f += __shfl_xor_sync(0xffffffffu, f, 2);
+      if (part == 0) csum[col] = f;
     }
     mine = rows_lo ? umma::mbar_wait(bar_dk, 0, wlim) : true;
     if (!mine) record_error(w.err, 1, kSiteStMma2);
