@@ -691,7 +691,7 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
 // With b = beta, Gam_i = exp(G_i), cw = b Gam, D_ij = exp(G_i - G_j),
 // k^ = diag(r_k) k and T = (I + A)^-1, A = tril_strict(diag(b) D * k^ k^^T):
 //   X1 = [K; dW] K^T          rows 0..63: S = k^ k^^T (with r_k scales), rows 64..127: dW k^^T
-//   X2 = [dv; V] V^T          rows 0..63: dv V^T
+//   X2 = [V; dv] V^T          rows 64..127: dv V^T
 //   dT  = (dW k^^T) diag(cw) + (dv V^T) diag(b)
 //   dR_w = T^T dW, dR_u = T^T dv, M2 = dT T^T, dA = -T^T M2 (strictly lower)
 //   dv_out = diag(b) dR_u
@@ -704,10 +704,10 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
 
 struct WbSm {
   static constexpr int kKD = 0;                 // K a0 | dW a0 | K a1 | dW a1
-  static constexpr int kDV = kKD + 4 * kAtom;   // dv a0 | V a0 | dv a1 | V a1
-  static constexpr int kT = kDV + 4 * kAtom;    // T image atom | zero atom
-  static constexpr int kDT = kT + 2 * kAtom;    // dT image atom | zero atom; later dS diag(r_k) | zero
-  static constexpr int kM2 = kDT + 2 * kAtom;   // -M2 image atom; later diag(r_k) dS atom | zero atom
+  static constexpr int kDV = kKD + 4 * kAtom;   // V a0 | dv a0 | V a1 | dv a1
+  static constexpr int kT = kDV + 4 * kAtom;    // T image atom, twice (M = 128 products repeat rows 0..63)
+  static constexpr int kDT = kT + 2 * kAtom;    // dT image atom | zero atom; later dS diag(r_k), twice
+  static constexpr int kM2 = kDT + 2 * kAtom;   // -M2 image atom; later diag(r_k) dS, twice
   static constexpr int kSk = kM2 + 2 * kAtom;   // S (fp32 [64][kMS])
   static constexpr int kAf = kSk + 64 * kMS * 4;  // A (fp32 [64][kMS]); later dS (fp32)
   static constexpr int kTf = kAf + 64 * kMS * 4;  // T (fp32 [64][kMS])
@@ -772,25 +772,22 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
     umma::mbar_arrive_expect_tx(bar_ld, S::kTx);
     umma::tma_load_3d(sm + S::kKD, &tk, 0, h, static_cast<int>(s), bar_ld);
     umma::tma_load_3d(sm + S::kKD + 2 * kAtom, &tk, 64, h, static_cast<int>(s), bar_ld);
-    umma::tma_load_3d(sm + S::kDV + kAtom, &tv, 0, hv, static_cast<int>(s), bar_ld);
-    umma::tma_load_3d(sm + S::kDV + 3 * kAtom, &tv, 64, hv, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + S::kDV, &tv, 0, hv, static_cast<int>(s), bar_ld);
+    umma::tma_load_3d(sm + S::kDV + 2 * kAtom, &tv, 64, hv, static_cast<int>(s), bar_ld);
     const int64_t img = static_cast<int64_t>(blockIdx.x) * p.HV + hv;
     const uint8_t* dw = o.dw_img + img * kVnImg;
     const uint8_t* dv = o.dv_img + img * kVnImg;
     umma::bulk_g2s(sm + S::kKD + kAtom, dw, kAtom, bar_ld);
     umma::bulk_g2s(sm + S::kKD + 3 * kAtom, dw + kAtom, kAtom, bar_ld);
-    umma::bulk_g2s(sm + S::kDV, dv, kAtom, bar_ld);
-    umma::bulk_g2s(sm + S::kDV + 2 * kAtom, dv + kAtom, kAtom, bar_ld);
+    umma::bulk_g2s(sm + S::kDV + kAtom, dv, kAtom, bar_ld);
+    umma::bulk_g2s(sm + S::kDV + 3 * kAtom, dv + kAtom, kAtom, bar_ld);
   }
   if (warp == 0) {
     umma::tmem_alloc(tslot, 512);
     umma::fence_before_sync();
   }
-  for (int e = tid; e < kAtom / 16; e += S::kThreads) {  // zero halves of the M = 128 operands
-    reinterpret_cast<uint4*>(sm + S::kT + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
+  for (int e = tid; e < kAtom / 16; e += S::kThreads)  // zero rows 64..127 of [dT; 0]
     reinterpret_cast<uint4*>(sm + S::kDT + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
-    reinterpret_cast<uint4*>(sm + S::kM2 + kAtom)[e] = make_uint4(0u, 0u, 0u, 0u);
-  }
   if (tid < 64) {
     const bool live = tid < L;
     const float g = live ? o.gc[(s + tid) * p.HV + hv] : 0.f;
@@ -811,12 +808,12 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
   uint32_t last_bar = 0, last_par = 0;
   auto adv = [](int ks) { return static_cast<uint64_t>(((ks >> 2) * 2 * kAtom + (ks & 3) * 32) >> 4); };
   if (ok) {
-    if (warp == 0) {  // X1 = [K; dW] K^T, X2 = [dv; V] V^T
+    if (warp == 0) {  // X1 = [K; dW] K^T, X2 = [V; dv] V^T
       if (umma::elect_one()) {
         const uint32_t id64 = umma::idesc_f16(128, 64, kBf16, false, false);
         const uint64_t d_kd = umma::smem_desc_sw128(umma::smem_u32(sm + S::kKD), 16, 1024);
-        const uint64_t d_dv = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDV), 16, 1024);
-        const uint64_t d_v = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDV + kAtom), 16, 1024);
+        const uint64_t d_dv = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDV), 16, 1024);  // [V; dv]
+        const uint64_t d_v = d_dv;                                                             // V (64 rows)
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) umma::mma_f16(tmem + S::kX1, d_kd + adv(ks), d_kd + adv(ks), id64, ks > 0);
 #pragma unroll
@@ -846,13 +843,11 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
     mine = umma::mbar_wait(bar_x, 0, wlim);
     if (!mine) record_error(w.err, 1, kSiteStMma1);
     umma::fence_after_sync();
-    float tm[32];
     if (mine) {
-      if (rows_lo) {  // S and A (rows 0..63), and dv V^T kept for dT
+      if (rows_lo) {  // S and A (rows 0..63)
         const int i = row;
         float x[32];
         umma::tmem_ld32(tmem + S::kX1 + lane_base + colh * 32, x);
-        umma::tmem_ld32(tmem + S::kX2 + lane_base + colh * 32, tm);
         const float ri = rk[i], gi = Gs[i], bi = bs[i];
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
@@ -861,26 +856,19 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
           Sk[i * kMS + j] = sv;
           Af[i * kMS + j] = (i < L && j < i) ? bi * exp2f(gi - Gs[j]) * sv : 0.f;
         }
-      } else {  // dW k^^T diag(cw) (rows 64..127)
+      } else {  // dT = (dW k^^T) diag(cw) + (dv V^T) diag(b) (rows 64..127 of X1 and X2)
         const int i = row - 64;
-        float x[32];
+        float x[32], y[32];
         umma::tmem_ld32(tmem + S::kX1 + lane_base + colh * 32, x);
+        umma::tmem_ld32(tmem + S::kX2 + lane_base + colh * 32, y);
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
           const int j = colh * 32 + jj;
-          dTf[i * kMS + j] = x[jj] * rk[j] * cw[j];
+          dTf[i * kMS + j] = fmaf(x[jj] * rk[j], cw[j], y[jj] * bs[j]);
         }
       }
     }
     ok = !__syncthreads_or(!mine);
-    if (ok && rows_lo) {  // dT += (dv V^T) diag(b)
-      const int i = row;
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int j = colh * 32 + jj;
-        dTf[i * kMS + j] += tm[jj] * bs[j];
-      }
-    }
   }
   if (ok) {
     solve_tril64_mma(Af, Tf, Zs);  // T = (I + A)^-1 (starts and ends with a barrier)
@@ -896,7 +884,9 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
           d8[e] = dTf[r * kMS + c + e];
         }
         const uint32_t off = r * 128 + (((c >> 3) ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(sm + S::kT + off) = pack8<T>(t8);
+        const uint4 tp = pack8<T>(t8);
+        *reinterpret_cast<uint4*>(sm + S::kT + off) = tp;
+        *reinterpret_cast<uint4*>(sm + S::kT + kAtom + off) = tp;  // [T^T | T^T]: rows 64..127 of the products repeat 0..63
         *reinterpret_cast<uint4*>(sm + S::kDT + off) = pack8<T>(d8);
       }
     }
@@ -910,7 +900,7 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
         const uint32_t idm2 = umma::idesc_f16(128, 64, kBf16, false, false);
         const uint64_t d_tt = umma::smem_desc_sw128(umma::smem_u32(sm + S::kT), kAtom, 1024);      // T^T, MN-major
         const uint64_t d_dw = umma::smem_desc_sw128(umma::smem_u32(sm + S::kKD + kAtom), 2 * kAtom, 1024);
-        const uint64_t d_dvb = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDV), 2 * kAtom, 1024);
+        const uint64_t d_dvb = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDV + kAtom), 2 * kAtom, 1024);
         const uint64_t d_dt = umma::smem_desc_sw128(umma::smem_u32(sm + S::kDT), 16, 1024);      // [dT; 0]
         const uint64_t d_t = umma::smem_desc_sw128(umma::smem_u32(sm + S::kT), 16, 1024);        // T, K-major B
 #pragma unroll
@@ -962,26 +952,26 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
     last_bar = bar_da;
   }
   if (ok) {
-    mine = rows_lo ? umma::mbar_wait(bar_da, 0, wlim) : true;
+    // rows 0..63 of dR_u, dR_w and dA sit twice in TMEM (lanes 0..63 and 64..127), so all eight warps
+    // share them: thread -> row i, column part (32 of dR_u / dR_w, 16 of dA)
+    mine = umma::mbar_wait(bar_da, 0, wlim);
     if (!mine) record_error(w.err, 1, kSiteStMma2);
     umma::fence_after_sync();
-    if (mine && rows_lo) {  // rows 0..63: dv out, db, dG row terms, dS and its images
-      const int i = row;
+    if (mine) {
+      const int i = (quad & 1) * 32 + lane, part = colh * 2 + (quad >> 1);
       const bool live = i < L;
       const float bi = bs[i], gi = Gs[i], ri = rk[i];
-      // U path: v_i . dR_u,i and dv = diag(b) dR_u (this thread's 64 columns)
       float a = 0.f, r = 0.f;
-      T* dvrow = static_cast<T*>(p.dv) + ((s + i) * p.HV + hv) * static_cast<int64_t>(D);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int c0 = colh * 64 + half * 32;
+      {  // U path: v_i . dR_u,i and dv = diag(b) dR_u; W path: k_i . dR_w,i
+        const int c0 = part * 32;
+        T* dvrow = static_cast<T*>(p.dv) + ((s + i) * p.HV + hv) * static_cast<int64_t>(D);
         float x[32];
         umma::tmem_ld32(tmem + S::kRu + lane_base + c0, x);
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
           const int c = c0 + q8 * 8;
           float vv[8], o8[8];
-          unpack8<T>(*reinterpret_cast<const uint4*>(sm + S::kDV + kAtom + atom_pair_off(i, c, 2 * kAtom)), vv);
+          unpack8<T>(*reinterpret_cast<const uint4*>(sm + S::kDV + atom_pair_off(i, c, 2 * kAtom)), vv);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             a = fmaf(vv[e], x[q8 * 8 + e], a);
@@ -999,15 +989,15 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
           for (int e = 0; e < 8; ++e) r = fmaf(kv[e], x[q8 * 8 + e], r);
         }
       }
-      r *= ri;  // k^_i . dR_w,i
-      // A path (this thread's 32 columns of dA): t_i and dS, F row sums
-      float x[32];
-      umma::tmem_ld32(tmem + S::kDA + lane_base + colh * 32, x);
+      r *= ri;  // k^_i . dR_w,i over this part's columns
+      // A path (16 columns of dA): t_i, dS, F row sums, and the dS images (written twice: [dS; dS])
+      float x[16];
+      umma::tmem_ld16(tmem + S::kDA + lane_base + part * 16, x);
       float t = 0.f, fr = 0.f;
-      float dsk[32], dsr[32];
+      float dsk[16], dsr[16];
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int j = colh * 32 + jj;
+      for (int jj = 0; jj < 16; ++jj) {
+        const int j = part * 16 + jj;
         const bool in = live && j < i;
         const float dd = in ? exp2f(gi - Gs[j]) : 0.f;
         const float sv = Sk[i * kMS + j];
@@ -1019,22 +1009,17 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
         dsr[jj] = ds * ri;
       }
 #pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) {
-        const int j0 = colh * 32 + q8 * 8;
+      for (int q8 = 0; q8 < 2; ++q8) {
+        const int j0 = part * 16 + q8 * 8;
         const uint32_t off = i * 128 + ((((j0 >> 3) ^ (i & 7))) << 4);
-        *reinterpret_cast<uint4*>(sm + S::kDT + off) = pack8<T>(dsk + q8 * 8);   // dS diag(r_k)
-        *reinterpret_cast<uint4*>(sm + S::kM2 + off) = pack8<T>(dsr + q8 * 8);   // diag(r_k) dS
+        const uint4 pk = pack8<T>(dsk + q8 * 8), pr = pack8<T>(dsr + q8 * 8);
+        *reinterpret_cast<uint4*>(sm + S::kDT + off) = pk;           // dS diag(r_k)
+        *reinterpret_cast<uint4*>(sm + S::kDT + kAtom + off) = pk;
+        *reinterpret_cast<uint4*>(sm + S::kM2 + off) = pr;           // diag(r_k) dS
+        *reinterpret_cast<uint4*>(sm + S::kM2 + kAtom + off) = pr;
       }
-      // the two column halves meet in shared memory
-      const float db_part = a + exp2f(gi) * r + t;  // partial sums over this thread's columns
-      const float dg_part = cw[i] * r + fr;
-      if (colh == 1) {
-        dbv[i] = db_part;
-        dgv[i] = dg_part;
-      } else {
-        Zs[i] = db_part;  // the solve scratch is free again
-        Zs[64 + i] = dg_part;
-      }
+      Zs[part * 64 + i] = a + exp2f(gi) * r + t;  // partial db over this part (the solve scratch is free)
+      Zs[256 + part * 64 + i] = cw[i] * r + fr;   // partial dG row terms
     }
     umma::fence_proxy_async();
     umma::fence_before_sync();
@@ -1069,37 +1054,33 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
       f += __shfl_xor_sync(0xffffffffu, f, 2);
       if (part == 0) csum[col] = f;
     }
-    mine = rows_lo ? umma::mbar_wait(bar_dk, 0, wlim) : true;
+    mine = umma::mbar_wait(bar_dk, 0, wlim);
     if (!mine) record_error(w.err, 1, kSiteStMma2);
     umma::fence_after_sync();
     ok = !__syncthreads_or(!mine);
   }
-  if (ok && rows_lo) {  // dk^ += diag(cw) dR_w + dK sum; db; dG
-    const int i = row;
+  if (ok) {  // dk^ += diag(cw) dR_w + dK sum (reductions into the dq/dk kernel's values); db; dG
+    const int i = (quad & 1) * 32 + lane, part = colh * 2 + (quad >> 1);
     const bool live = i < L;
     const float ci = cw[i];
-    float* dkrow = o.dkh + ((s + i) * p.HV + hv) * static_cast<int64_t>(D);
+    const int c0 = part * 32;
+    float* dkrow = o.dkh + ((s + i) * p.HV + hv) * static_cast<int64_t>(D) + c0;
+    float x[32], y[32];
+    umma::tmem_ld32(tmem + S::kRw + lane_base + c0, x);
+    umma::tmem_ld32(tmem + S::kDK + lane_base + c0, y);
+    if (live) {
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int c0 = colh * 64 + half * 32;
-      float x[32], y[32];
-      umma::tmem_ld32(tmem + S::kRw + lane_base + c0, x);
-      umma::tmem_ld32(tmem + S::kDK + lane_base + c0, y);
-      if (live) {
-#pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          float4 v = *reinterpret_cast<float4*>(dkrow + c0 + j4 * 4);
-          v.x += fmaf(ci, x[j4 * 4], y[j4 * 4]);
-          v.y += fmaf(ci, x[j4 * 4 + 1], y[j4 * 4 + 1]);
-          v.z += fmaf(ci, x[j4 * 4 + 2], y[j4 * 4 + 2]);
-          v.w += fmaf(ci, x[j4 * 4 + 3], y[j4 * 4 + 3]);
-          *reinterpret_cast<float4*>(dkrow + c0 + j4 * 4) = v;
-        }
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float v0 = fmaf(ci, x[j4 * 4], y[j4 * 4]), v1 = fmaf(ci, x[j4 * 4 + 1], y[j4 * 4 + 1]);
+        const float v2 = fmaf(ci, x[j4 * 4 + 2], y[j4 * 4 + 2]), v3 = fmaf(ci, x[j4 * 4 + 3], y[j4 * 4 + 3]);
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dkrow + j4 * 4), "f"(v0), "f"(v1),
+                     "f"(v2), "f"(v3) : "memory");
       }
     }
-    if (colh == 0 && live) {
-      p.dbeta[(s + i) * p.HV + hv] = Zs[i] + dbv[i];
-      o.dG[(s + i) * p.HV + hv] += Zs[64 + i] + dgv[i] - csum[i];
+    if (part == 0 && live) {
+      p.dbeta[(s + i) * p.HV + hv] = Zs[i] + Zs[64 + i] + Zs[128 + i] + Zs[192 + i];
+      atomicAdd(o.dG + (s + i) * p.HV + hv,
+                Zs[256 + i] + Zs[320 + i] + Zs[384 + i] + Zs[448 + i] - csum[i]);
     }
   }
   if (!ok && warp == 0 && last_bar) umma::mbar_wait(last_bar, last_par, 20000000LL);
