@@ -49,20 +49,42 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile the library if any source is newer than it; return its path."""
-    if not force and not _stale():
-        return LIB
-    tmp = LIB + ".tmp"
-    cmd = [_nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC, "-o", tmp, *sources()]
+def _run(cmd: list[str], verbose: bool) -> None:
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), file=sys.stderr)
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose:
         sys.stderr.write(res.stderr)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile the library if any source is newer than it; return its path.
+
+    Each ``.cu`` file is compiled to an object file on its own process (in
+    parallel), then the objects are linked into the shared library."""
+    if not force and not _stale():
+        return LIB
+    import concurrent.futures
+    import tempfile
+
+    tmp = LIB + ".tmp"
+    compile_flags = [f for f in NVCC_FLAGS if f != "-shared"]
+    with tempfile.TemporaryDirectory() as objdir:
+        objs, cmds = [], []
+        for src in sources():
+            obj = os.path.join(objdir, os.path.basename(src) + ".o")
+            cmd = [_nvcc(), *compile_flags, "-I", INCLUDE, "-I", CSRC, "-c", "-o", obj, src]
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+            objs.append(obj)
+            cmds.append(cmd)
+        workers = max(1, min(len(cmds), os.cpu_count() or 1))
+        with concurrent.futures.ThreadPoolExecutor(workers) as pool:
+            for f in [pool.submit(_run, c, verbose) for c in cmds]:
+                f.result()
+        _run([_nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", tmp, *objs], verbose)
     os.replace(tmp, LIB)
     return LIB
 
