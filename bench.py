@@ -449,9 +449,9 @@ def run_ours(a):
         d2h = o_h.numel() * o_h.element_size() + ht_h.numel() * ht_h.element_size()
 
     # ---- decode (config 3) and the causal conv1d in front of the layer ----
-    dec = _decode_bench(ops, dev, a, hbm, flush) if not a.no_decode else None
-    conv = _conv_bench(ops, dev, a, hbm, flush) if not a.no_decode and rank == 0 else None
-    bwd = _bwd_bench(ops, dev, a, flush, tc_burst) if not a.no_bwd and rank == 0 else None
+    dec = _decode_bench(ops, dev, a, hbm, flush, peak_kind) if not a.no_decode else None
+    conv = _conv_bench(ops, dev, a, hbm, flush, peak_kind) if not a.no_decode and rank == 0 else None
+    bwd = _bwd_bench(ops, dev, a, flush, tc_burst, peak_kind) if not a.no_bwd and rank == 0 else None
 
     # ---- CPU baseline (rank 0, N=1) ----
     cpu_line = None
@@ -695,7 +695,7 @@ def _stage_names(n):
     return [f"k{i}" for i in range(n)]
 
 
-def _decode_bench(ops, dev, a, hbm, flush):
+def _decode_bench(ops, dev, a, hbm, flush, peak_kind="measured"):
     import torch
     c = CFG3
     N, S, H, HV, K, V = c["N"], c["slots"], c["H"], c["HV"], c["K"], c["V"]
@@ -729,11 +729,11 @@ def _decode_bench(ops, dev, a, hbm, flush):
     gbs = nbytes / (us * 1e-6) / 1e9
     return {"workload": "config3: 256 sequences x 1 token, cache [1024,32,128,128] f32",
             "us_per_step": us, "algorithmic_bytes": nbytes, "achieved_gbs": gbs,
-            "peak_gbs": hbm, "frac_hbm": gbs / hbm, "peak_kind": "measured HBM copy",
+            "peak_gbs": hbm, "frac_hbm": gbs / hbm, "peak_kind": f"{peak_kind} HBM copy",
             "kernel": "decode_stream_kernel", "traffic": _load_traffic().get("decode")}
 
 
-def _conv_bench(ops, dev, a, hbm, flush):
+def _conv_bench(ops, dev, a, hbm, flush, peak_kind="measured"):
     """The causal conv1d in front of the GDN layer at the config-1 prefill
     shape (q/k/v conv channels 2*16*128 + 32*128 = 8192, 8192 tokens,
     width 4, SiLU, bf16, vLLM layout with a slot cache) and one decode
@@ -808,7 +808,7 @@ def _conv_bench(ops, dev, a, hbm, flush):
                           # conv reads x and writes y, the prefill reads y; fused: x read
                           # once, post-conv q/k written once for the state kernel
                           "hbm_bytes_saved": 2 * (2 * T * D) - 2 * T * 2 * H * 128},
-        "peak_gbs": hbm, "peak_kind": "measured HBM copy"}
+        "peak_gbs": hbm, "peak_kind": f"{peak_kind} HBM copy"}
 
 
 
@@ -826,7 +826,7 @@ def bwd_flops_per_chunk_head(K, V):
     return 2 * (fwd + dvl + state + dqkw + wy)
 
 
-def _bwd_bench(ops, dev, a, flush, tc_burst):
+def _bwd_bench(ops, dev, a, flush, tc_burst, peak_kind="measured"):
     """Backward (training) of the config-1 prefill shape: gdn_chunk_bwd with
     dO given and no final-state gradient, q/k L2 norm on."""
     import torch
@@ -860,7 +860,7 @@ def _bwd_bench(ops, dev, a, flush, tc_burst):
     return {"workload": "chunk_gated_delta_rule backward, config-1 shape (B=1 T=8192 H=16 HV=32 K=V=128 "
                         "bf16, q/k L2 norm, dO given, no final-state gradient), forward recompute included",
             "ms_per_call": ms, "tokens_per_s": B * T / (ms * 1e-3), "flops": flops, "tflops": tf,
-            "frac_tensor_bf16_measured": tf / tc_burst,
+            "frac_tensor_bf16_measured": tf / tc_burst, "peak_kind": f"{peak_kind} bf16 burst",
             "kernels": "chunk_prep (L2 norms) + tcgen05 recompute (tc_wy_kernel, tc_state3_kernel storing h "
                        "and v_new images) + bwd_dvlocal (warp MMA, one TF32 product per step) + tcgen05 "
                        "tc_bwd_state, tc_bwd_dqkw, tc_bwd_wy + bwd_qk, bwd_dg"}
