@@ -913,7 +913,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-subs", action="store_true",
                     help="skip the config-4 and head-split sub-workloads of the config-1 line")
-    ap.add_argument("--segment-tokens", dest="segment_tokens", type=int, default=2048,
+    ap.add_argument("--segment-tokens", dest="segment_tokens", type=int, default=4096,
                     help="tokens per piece of the host-streamed end-to-end leg (multiple of 64)")
     ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg4"],
                     help="BASELINE prefill config (default cfg1, the headline)")

@@ -3,7 +3,8 @@
 //
 // The tokens are cut into pieces of about `segment_tokens` tokens: one
 // sequence (B = 1, no cu_seqlens) along time at 64-token chunk boundaries,
-// its fp32 state handed from piece to piece in device memory; an
+// its fp32 state handed from piece to piece in device memory and its last
+// segment in halving pieces; an
 // equal-length batch into groups of sequences; a packed varlen batch into
 // groups of consecutive sequences.  Piece p + 1 is copied in on one
 // library-owned stream while piece p runs on the caller's stream and piece
@@ -21,6 +22,7 @@
 namespace {
 
 constexpr int kMaxDevices = 128;
+constexpr int64_t kTailMin = 512;  // tokens: the shortest piece of a time split's tail
 
 struct CopyStreams {
   cudaStream_t in = nullptr, out = nullptr;
@@ -102,9 +104,21 @@ int make_plan(const gdn_chunk_args& a, int64_t seg, Plan& P) {
       s0 = s1;
     }
   } else if (P.time_split) {
-    for (int64_t t0 = 0; t0 < a.T; t0 += seg) {
-      const int64_t t1 = t0 + seg < a.T ? t0 + seg : a.T;
+    // Pieces of `seg` tokens, except that the last `seg` (or fewer) are cut
+    // into halving pieces (seg/2, seg/4, ... down to kTailMin, then the rest):
+    // nothing overlaps the compute and the copy-out of the last piece, so a
+    // short last piece shortens the call by most of a full piece's copy-out.
+    const int64_t tail0 = a.T > seg ? ((a.T - seg) / 64) * 64 : 0;  // every piece starts on a chunk boundary
+    for (int64_t t0 = 0; t0 < tail0; t0 += seg) {
+      const int64_t t1 = t0 + seg < tail0 ? t0 + seg : tail0;
       P.pieces.push_back({t0, t1, 0, 1, 1, t1 - t0});
+    }
+    for (int64_t t0 = tail0; t0 < a.T;) {
+      const int64_t left = a.T - t0;
+      int64_t n = ((left / 2) / 64) * 64;
+      if (n < kTailMin || left - n < kTailMin) n = left;
+      P.pieces.push_back({t0, t0 + n, 0, 1, 1, n});
+      t0 += n;
     }
   } else if (a.T > 0) {
     const int64_t per = seg / a.T > 0 ? seg / a.T : 1;

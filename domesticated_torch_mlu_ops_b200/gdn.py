@@ -565,7 +565,7 @@ def chunk_gated_delta_rule_from_host(
     use_qk_l2norm_in_kernel: bool = False,
     *,
     device=None,
-    segment_tokens: int = 2048,
+    segment_tokens: int = 4096,
     o_out: torch.Tensor | None = None,
     final_state_out: torch.Tensor | None = None,
     force_generic: bool = False,
@@ -577,9 +577,13 @@ def chunk_gated_delta_rule_from_host(
     tensor.  The tokens go to the GPU in pieces of about ``segment_tokens``
     tokens (a multiple of 64) while earlier pieces compute and their outputs
     come back, so the host link, not the kernels, sets the time; the results
-    are those of the device op.  2048 was the fastest piece size at the
-    config-1 shape on a B200 (512: +8 %, 1024: +1.5 %, 4096: +4 %).  Page-locked (pinned) inputs give overlapped
-    copies; other host memory is pinned first.
+    are those of the device op.  A single sequence's last ``segment_tokens``
+    tokens go in halving pieces (down to 512 tokens), which shortens the
+    compute and copy-out of the last piece that nothing overlaps.  4096 was
+    the fastest piece size at the config-1 shape on a B200 (3.12 ms; 2048:
+    3.20 ms, 3072: 3.18 ms): every piece costs about 50 us of copy set-up.
+    Page-locked (pinned) inputs give overlapped copies; other host memory is
+    pinned first.
 
     Returns ``(o, final_state)`` as pinned CPU tensors (``o_out`` /
     ``final_state_out`` when given: contiguous pinned tensors of the output

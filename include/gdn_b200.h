@@ -217,7 +217,9 @@ GDN_API int gdn_chunk_bwd(const gdn_chunk_bwd_args* args, void* stream);
  * gdn_chunk_fwd_host_buffer_size(args, segment_tokens) bytes.
  * The tokens are cut into pieces of about segment_tokens tokens (a positive
  * multiple of 64): a single sequence (B = 1, no cu_seqlens) along time, the
- * fp32 state handed from piece to piece on the device; an equal-length batch
+ * fp32 state handed from piece to piece on the device, its last
+ * segment_tokens tokens in halving pieces down to 512 tokens (the last piece's
+ * compute and copy-out are not overlapped, so it is kept short); an equal-length batch
  * into groups of sequences; a packed batch into groups of consecutive
  * sequences.  Each piece is one gdn_chunk_fwd call on device copies (same
  * results as the device entry point).  Copy-in of piece p+1, compute of

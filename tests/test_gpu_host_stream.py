@@ -29,10 +29,11 @@ def _run_both(ops, q, k, v, g, beta, h0, cu, seg, l2=True, vfirst=False):
 
 
 @pytest.mark.parametrize("dtype,T,seg", [(torch.bfloat16, 1000, 256), (torch.float32, 300, 128),
-                                         (torch.bfloat16, 4096, 1024)])
+                                         (torch.bfloat16, 4096, 1024), (torch.bfloat16, 2100, 2048)])
 def test_time_pieces_equal_one_call(dtype, T, seg):
-    """One sequence cut along time at 64-token chunk boundaries, the fp32
-    state handed over on the device: bit-identical to one call."""
+    """One sequence cut along time at 64-token chunk boundaries (the last
+    segment in halving pieces), the fp32 state handed over on the device:
+    bit-identical to one call."""
     ops = _ops()
     q, k, v, g, beta, h0 = make_inputs(3, 1, T, 2, 4, 128, 128, dtype=dtype, nseq_state=1, state_std=0.1)
     o_d, ht_d, o_h, ht_h = _run_both(ops, q, k, v, g, beta, h0, None, seg)
