@@ -40,6 +40,7 @@
 #include <cuda.h>
 
 #include <stdlib.h>
+#include <string.h>
 
 #include <type_traits>
 
@@ -662,7 +663,7 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
   const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
   const uint32_t t_dh = tmem + S::kDH;
   auto t_acc = [&](int x) { return tmem + S::kAcc + static_cast<uint32_t>(x & 1) * VS; };
-  auto t_o = [&](int x) { return tmem + S::kO + static_cast<uint32_t>(x & 1) * VS; };
+  auto t_o = [&](int x) { return tmem + S::kO + static_cast<uint32_t>((x & 1) * (S::kOBufs - 1)) * VS; };
   constexpr bool kBf16 = !std::is_same<T, __half>::value;
   const uint32_t id_xy = umma::idesc_f16(128, VS, kBf16, false, true);
   const uint32_t id_dh = umma::idesc_f16(128, VS, kBf16, true, true);
@@ -676,19 +677,19 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
     const int64_t s = bos + static_cast<int64_t>(x) * kChunk;
     const int L = static_cast<int>(min64(kChunk, eos - s));
     const int i = row - 64;
-    float y[CW], z[CW];
+    T* orow = obase + ((s + i) * p.HV + hv) * D + v0 + colh * CW;
 #pragma unroll
-    for (int q = 0; q < CW / 16; ++q)
-      umma::tmem_ld16x2(t_acc(x) + lane_base + colh * CW + q * 16, t_o(x) + lane_base + colh * CW + q * 16,
-                        y + q * 16, z + q * 16);
-    if (i < L && obase) {
-      T* orow = obase + ((s + i) * p.HV + hv) * D + v0 + colh * CW;
+    for (int q = 0; q < CW / 16; ++q) {  // 16 columns at a time
+      float y[16], z[16];
+      umma::tmem_ld16x2(t_acc(x) + lane_base + colh * CW + q * 16, t_o(x) + lane_base + colh * CW + q * 16, y, z);
+      if (i < L && obase) {
 #pragma unroll
-      for (int j8 = 0; j8 < CW / 8; ++j8) {
-        float ov[8];
+        for (int h8 = 0; h8 < 2; ++h8) {
+          float ov[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ov[e] = fmaf(ai, y[j8 * 8 + e], scale * z[j8 * 8 + e]);
-        *reinterpret_cast<uint4*>(orow + j8 * 8) = pack8<T>(ov);
+          for (int e = 0; e < 8; ++e) ov[e] = fmaf(ai, y[h8 * 8 + e], scale * z[h8 * 8 + e]);
+          *reinterpret_cast<uint4*>(orow + q * 16 + h8 * 8) = pack8<T>(ov);
+        }
       }
     }
   };
@@ -741,28 +742,41 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
         if (mine) emit(c - 1, a_prev);
       }
       a_prev = sc[row - 64];
+      if constexpr (S::kOBufs == 1) {  // this chunk's O product reuses the buffer emit just read
+        umma::fence_before_sync();
+        umma::named_sync(1, 256);
+      }
     } else {  // E1 (rows 0..63): v = U - X, V~ = diag(b) v
       // U and b have been in the stage since its loads completed: read them
       // while MMA1 runs
       const int i = row;
       const float bi = sc[64 + i];
       const T* ut = reinterpret_cast<const T*>(b + S::kU);
-      uint4 uraw[CW / 8];
+      constexpr int GW = CW < 32 ? CW : 32;  // columns per group of TMEM loads
+      uint4 uraw[GW / 8];
 #pragma unroll
-      for (int j8 = 0; j8 < CW / 8; ++j8)
-        uraw[j8] = *reinterpret_cast<const uint4*>(ut + u_off(i, colh * CW + j8 * 8, VS));
+      for (int j8 = 0; j8 < GW / 8; ++j8)
+        uraw[j8] = *reinterpret_cast<const uint4*>(ut + u_off(i, colh * CW + j8 * 8, S::kUS));
       mine = umma::mbar_wait(bar_mma1, static_cast<uint32_t>(c & 1), wlim);
       if (!mine) record_error(w.err, 1, kSiteStMma1);
       umma::fence_after_sync();
-      uint32_t rx[CW];
 #pragma unroll
-      for (int q = 0; q < CW / 16; ++q) umma::tmem_ld16_nw(t_acc(c) + lane_base + colh * CW + q * 16, rx + q * 16);
+      for (int gq = 0; gq < CW / GW; ++gq) {
+      if (gq > 0) {
+#pragma unroll
+        for (int j8 = 0; j8 < GW / 8; ++j8)
+          uraw[j8] = *reinterpret_cast<const uint4*>(ut + u_off(i, colh * CW + gq * GW + j8 * 8, S::kUS));
+      }
+      uint32_t rx[GW];
+#pragma unroll
+      for (int q = 0; q < GW / 16; ++q)
+        umma::tmem_ld16_nw(t_acc(c) + lane_base + colh * CW + gq * GW + q * 16, rx + q * 16);
       umma::tmem_wait_ld();
 #pragma unroll
-      for (int q = 0; q < CW / 16; ++q) umma::reg_fence16(rx + q * 16);
+      for (int q = 0; q < GW / 16; ++q) umma::reg_fence16(rx + q * 16);
 #pragma unroll
-      for (int j8 = 0; j8 < CW / 8; ++j8) {
-        const int col = colh * CW + j8 * 8;
+      for (int j8 = 0; j8 < GW / 8; ++j8) {
+        const int col = colh * CW + gq * GW + j8 * 8;
         float u8[8], vn[8], vt[8];
         unpack8<T>(uraw[j8], u8);
 #pragma unroll
@@ -776,9 +790,10 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
           *reinterpret_cast<uint4*>(w.vn_img + ((c0 + c) * p.HV + hv) * kVnImg + bwd_img_off(i, v0 + col, 64)) =
               pack8<T>(vn);
       }
+      }
       umma::fence_proxy_async();
       umma::fence_before_sync();
-      umma::named_sync(1, 128);  // warps 0, 1, 4, 5
+      umma::named_sync(1, S::kOBufs == 1 ? 256 : 128);  // warps 0, 1, 4, 5 (and the emit warps at one O buffer)
       if (warp == 0) {  // MMA2: dH = K^T V~ (the chain), then O = [. ; P] v
         umma::fence_after_sync();
         if (umma::elect_one()) {
@@ -805,9 +820,20 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
     }
     umma::fence_after_sync();
     if (mine) {
+      constexpr int DW = CW < 32 ? CW : 32;  // columns per group of TMEM loads
       float d[CW];
 #pragma unroll
-      for (int q = 0; q < CW / 16; ++q) umma::tmem_ld16(t_dh + lane_base + colh * CW + q * 16, d + q * 16);
+      for (int gq = 0; gq < CW / DW; ++gq) {
+        uint32_t rd[DW];
+#pragma unroll
+        for (int q = 0; q < DW / 16; ++q)
+          umma::tmem_ld16_nw(t_dh + lane_base + colh * CW + gq * DW + q * 16, rd + q * 16);
+        umma::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < DW / 16; ++q) umma::reg_fence16(rd + q * 16);
+#pragma unroll
+        for (int j = 0; j < DW; ++j) d[gq * DW + j] = __uint_as_float(rd[j]);
+      }
       const float g = sc[128];
       if constexpr (STORE) {  // the state at this chunk's start (as its products used it), for the backward
         uint8_t* dst = w.hs_img + ((c0 + c) * p.HV + hv) * static_cast<int64_t>(kStateImg);
@@ -925,10 +951,46 @@ cudaError_t launch_state3(const gdn_chunk_args& a, const Work& w, float scale, c
   return cudaGetLastError();
 }
 
-// V-slice width of the state kernel: 32-column slices give the shortest chain
-// when every chain has an SM of its own; otherwise 64-column slices halve the
-// operand reloads per chain.
-int choose_vs(const gdn_chunk_args& a) { return a.N * a.HV <= 148 ? 32 : 64; }
+// V-slice width of the state kernel.  Every (sequence, v-head) chain takes
+// 128 / VS CTAs of one SM each, so the kernel runs about
+// ceil(N * HV * 128 / VS / SMs) waves, each as long as a chain; a chunk step
+// of a chain costs about 2.2 K cycles at VS = 32, 3.7 K at VS = 64 and 5.5 K
+// at VS = 128 (measured on a B200: the wider slices share their operand loads
+// and synchronisations across more columns).  The width with the fewest
+// cycles wins: 32-column slices for a few chains (config 1: 128 CTAs, one
+// wave), 128-column slices for many (configs 2 and 4).  GDN_TC_VS=32, 64 or
+// 128 in the environment overrides the choice (results are the same for every
+// width: each column's arithmetic does not depend on it).
+int sm_count() {
+  static int n = 0;  // of the first device asked; B200s have 148
+  if (n == 0) {
+    int dev = 0, v = 0;
+    n = cudaGetDevice(&dev) == cudaSuccess &&
+                cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0
+            ? v
+            : 148;
+  }
+  return n;
+}
+
+int choose_vs(const gdn_chunk_args& a) {
+  const char* v = getenv("GDN_TC_VS");
+  if (v && (!strcmp(v, "32") || !strcmp(v, "64") || !strcmp(v, "128"))) return atoi(v);
+  const int64_t chains = a.N * a.HV, sms = sm_count();
+  int best = 32;
+  double best_cost = 0.0;
+  const int widths[3] = {32, 64, 128};
+  const double step_cost[3] = {2.2, 3.7, 5.5};
+  for (int i = 0; i < 3; ++i) {
+    const int64_t ctas = chains * (D / widths[i]);
+    const double cost = static_cast<double>((ctas + sms - 1) / sms) * step_cost[i];
+    if (i == 0 || cost < best_cost) {
+      best = widths[i];
+      best_cost = cost;
+    }
+  }
+  return best;
+}
 
 // The fused cluster kernel (gdn_chunk_fused.cu) is opt-in: GDN_TC_FUSED=1 in
 // the environment selects it where clusters of it fit.  Measured on a B200 at
@@ -1002,7 +1064,8 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, lo
       wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem::kBytes, s>>>(a, w, scale, ci, tq, tk, tv);
       if ((e = cudaGetLastError()) != cudaSuccess) return e;
       if (w.vs == 32) e = launch_state3<T, 32>(a, w, scale, tq, tk, s, hk);
-      else e = launch_state3<T, 64>(a, w, scale, tq, tk, s, hk);
+      else if (w.vs == 64) e = launch_state3<T, 64>(a, w, scale, tq, tk, s, hk);
+      else e = launch_state3<T, 128>(a, w, scale, tq, tk, s, hk);
       if (e != cudaSuccess) return e;
       // the cache lines change only after every reader of the initial lines is done
       if (cv && (e = launch_conv_fn_states(*conv, s)) != cudaSuccess) return e;

@@ -159,16 +159,19 @@ struct St3 {
   static constexpr int kSc = kU + kUBytes;
   static constexpr int kStage = ((kSc + kScal * 4 + 1023) / 1024) * 1024;
   static constexpr uint32_t kTx = 4 * kAtom + 2 * kAtom + kImg64x64 + kUBytes + kScal * 4;
-  static constexpr int kStages = VS == 32 ? 3 : 2;  // a third 65 KB stage does not fit at VS = 64
+  static constexpr int kStages = VS == 32 ? 3 : 2;  // a third 65 KB (73 KB) stage does not fit at VS = 64 (128)
   static constexpr int kH = kStages * kStage;    // h image 128 x VS
   static constexpr int kVn = kH + D * VS * 2;    // v image 64 x VS
   static constexpr int kVt = kVn + 64 * VS * 2;  // diag(b) v image 64 x VS
   static constexpr int kBar = kVt + 64 * VS * 2; // full[kStages], mma1, dh, o
   static constexpr int kTmem = kBar + 6 * 8;
   static constexpr int kBytes = kTmem + 8 + 1024;
-  // TMEM columns: acc[2], dH, O[2] (VS each)
+  // TMEM columns: acc[2], dH, O[2] (VS each; one O buffer at VS = 128)
+  static constexpr int kOBufs = VS == 128 ? 1 : 2;
   static constexpr int kAcc = 0, kDH = 2 * VS, kO = 3 * VS, kCols = VS == 32 ? 256 : 512;
-  static_assert(kO + 2 * VS <= kCols, "TMEM columns");
+  static_assert(kO + kOBufs * VS <= kCols, "TMEM columns");
+  // U rows are read through the WY kernel's slices of at most 64 columns
+  static constexpr int kUS = VS < 64 ? VS : 64;
   static_assert(kBytes <= 227 * 1024, "shared memory");
 };
 constexpr int kSt3Threads = 288;  // 8 epilogue warps + 1 load warp
