@@ -59,29 +59,34 @@ namespace tc {
 // WY kernel
 // ---------------------------------------------------------------------------
 
-// Shared memory of the WY kernel (about 74 KB, so 3 CTAs fit per SM).  The
-// first 32 KiB hold four 64-row swizzled atoms: K(cols 0-63), Q(0-63),
-// K(64-127), Q(64-127).  Read 16 KiB at a time they form the 128-row operand
-// [K;Q]; once [K;Q]K^T is done, V is loaded over the Q atoms, and the atoms
-// read 8 KiB apart form [K_0:64 | V_0:64 | K_64:128 | V_64:128], a valid
-// N=256 MN-major operand (uniform atom stride).  W and U leave through
-// shared-memory staging and bulk stores: columns 0-63 staged over T, columns
-// 64-127 over the operand atoms once the last MMA has read them.
+// Shared memory of the WY kernel (about 51 KB, so 4 CTAs fit per SM; the
+// fused-conv variant keeps a second 17 KB region for its input rows and fits
+// 3).  The first 32 KiB hold four 64-row swizzled atoms: K(cols 0-63),
+// Q(0-63), K(64-127), Q(64-127).  Read 16 KiB at a time they form the
+// 128-row operand [K;Q]; once [K;Q]K^T is done, V is loaded over the Q atoms,
+// and the atoms read 8 KiB apart form [K_0:64 | V_0:64 | K_64:128 | V_64:128],
+// a valid N=256 MN-major operand (uniform atom stride).  A (fp32 [64][kMS])
+// is inverted in place into T, whose upper-right block is the solve's
+// scratch; the [T';T''] image is then written over it.  W and U leave
+// through shared-memory staging and bulk stores: columns 0-63 staged over the
+// atoms of K_0:64 and V_0:64 once the first W/U product has read them,
+// columns 64-127 over the other two after the second.
+template <bool CONV>
 struct WySmem {
   static constexpr int kOps = 0;                 // 4 atoms
-  static constexpr int kA = 4 * kAtom;           // f32 [64][kMS]; later the [T';T''] image
-  static constexpr int kT = kA + 64 * kMS * 4;   // f32 [64][kMS]; later W/U staging
-  static constexpr int kZ = kT + 64 * kMS * 4;   // f32 solve scratch
-  static constexpr int kVec = kZ + kMScratch * 4;  // gam, beta, rk, rq, cw, cu, cf: f32 [7][64]
+  static constexpr int kA = 4 * kAtom;           // f32 [64][kMS]: A, then T, then the [T';T''] image
+  static constexpr int kX = kA + 64 * kMS * 4;   // fused conv only: the k and v input rows
+  static constexpr int kVec = kX + (CONV ? 64 * kMS * 4 : 0);  // gam, beta, rk, rq, cw, cu, cf: f32 [7][64]
   static constexpr int kBar = kVec + 7 * 64 * 4;   // 3 mbarriers
   static constexpr int kTmem = kBar + 24;
   static constexpr int kBytes = kTmem + 8 + 1024;  // + slack for 1 KiB alignment
-  static_assert(kT % 16 == 0 && 64 * kMS * 4 >= 2 * kAtom, "W/U staging must fit over T");
-  static_assert(3 * (kBytes + 1024) <= 228 * 1024, "three CTAs per SM");
+  static constexpr int kCtas = CONV ? 3 : 4;       // CTAs per SM
+  static_assert(kCtas * (kBytes + 1024) <= 228 * 1024, "CTAs per SM");
+  static_assert(64 * kMS * 4 >= kImg64x128, "the [T';T''] image fits over T");
   // fused conv: the pre-conv q and k rows s-3 .. s+63 ([67][128] 16-bit each)
-  // land over A and T before the first product; the v rows over T after it
+  // land over A and X before the first product; the v rows over X after it
   static constexpr int kBox = 67 * 128 * 2;
-  static_assert(kA + 2 * kBox <= kZ && kT + kBox <= kZ && kBox % 128 == 0, "conv boxes fit over A and T");
+  static_assert(!CONV || (kA + 2 * kBox <= kVec && kX + kBox <= kVec && kBox % 128 == 0), "conv boxes fit");
 };
 constexpr int kWyThreads = 256;
 
@@ -232,26 +237,25 @@ __device__ __forceinline__ void conv_rows4(const ConvIn& ci, const uint8_t* box,
 // runs); the CTA of each chunk's first v-head of a q/k head also writes the
 // post-conv q and k rows for the state kernel.
 template <typename T, bool CONV>
-__global__ void __launch_bounds__(kWyThreads, 3)
+__global__ void __launch_bounds__(kWyThreads, WySmem<CONV>::kCtas)
 tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
              const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
              const __grid_constant__ CUtensorMap tv) {
   extern __shared__ uint8_t sm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ops = sm + WySmem::kOps;
-  uint8_t* timg = sm + WySmem::kA;  // [T';T''] 128 x 64 image, written after the solve
-  float* Af = reinterpret_cast<float*>(sm + WySmem::kA);
-  float* Tf = reinterpret_cast<float*>(sm + WySmem::kT);
-  float* Zs = reinterpret_cast<float*>(sm + WySmem::kZ);
-  float* gam = reinterpret_cast<float*>(sm + WySmem::kVec);
+  using Ly = WySmem<CONV>;
+  uint8_t* ops = sm + Ly::kOps;
+  uint8_t* timg = sm + Ly::kA;  // [T';T''] 128 x 64 image, written over T after the solve
+  float* Af = reinterpret_cast<float*>(sm + Ly::kA);  // A, inverted in place into T
+  float* gam = reinterpret_cast<float*>(sm + Ly::kVec);
   float* bet = gam + 64;
   float* rk = bet + 64;
   float* rq = rk + 64;
   float* cw = rq + 64;
   float* cu = cw + 64;
   float* cf = cu + 64;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + WySmem::kBar);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + WySmem::kTmem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Ly::kBar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + Ly::kTmem);
   const uint32_t bar_kq = umma::smem_u32(bars), bar_v = umma::smem_u32(bars + 1),
                  bar_mma = umma::smem_u32(bars + 2);
 
@@ -277,9 +281,9 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
     umma::mbar_init(bars + 2, 1);
     umma::mbar_fence_init();
     if constexpr (CONV) {  // pre-conv q and k rows (tv: the x map)
-      umma::mbar_arrive_expect_tx(bar_kq, 2 * WySmem::kBox);
-      umma::tma_load_2d(sm + WySmem::kA, &tv, h * D, static_cast<int>(s) - 3, bar_kq);
-      umma::tma_load_2d(sm + WySmem::kA + WySmem::kBox, &tv, (p.H + h) * D, static_cast<int>(s) - 3, bar_kq);
+      umma::mbar_arrive_expect_tx(bar_kq, 2 * Ly::kBox);
+      umma::tma_load_2d(sm + Ly::kA, &tv, h * D, static_cast<int>(s) - 3, bar_kq);
+      umma::tma_load_2d(sm + Ly::kA + Ly::kBox, &tv, (p.H + h) * D, static_cast<int>(s) - 3, bar_kq);
     } else {
       umma::mbar_arrive_expect_tx(bar_kq, 2 * kImg64x128);
       umma::tma_load_3d(ops, &tk, 0, h, static_cast<int>(s), bar_kq);
@@ -338,13 +342,13 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
     const int64_t ch = (kside ? static_cast<int64_t>(p.H) * D : 0) + static_cast<int64_t>(h) * D + c4;
     T* gdst = hv % (p.HV / p.H) == 0
                   ? static_cast<T*>(kside ? ci.kc : ci.qc) + static_cast<int64_t>(h) * D + c4 : nullptr;
-    conv_rows4<T, 16>(ci, sm + WySmem::kA + (kside ? WySmem::kBox : 0), c4, ch, (warp >> 1) * 16, lc == 0, cline,
+    conv_rows4<T, 16>(ci, sm + Ly::kA + (kside ? Ly::kBox : 0), c4, ch, (warp >> 1) * 16, lc == 0, cline,
                       chinit, cskip, L, ops + (kside ? 0 : kAtom), gdst, s, static_cast<int64_t>(p.H) * D, nullptr);
     umma::fence_proxy_async();  // the atoms are read by tcgen05; the boxes are rewritten by TMA next
     __syncthreads();
     if (tid == 0) {  // pre-conv v rows over T (the k box there is consumed)
-      umma::mbar_arrive_expect_tx(bar_v, WySmem::kBox);
-      umma::tma_load_2d(sm + WySmem::kT, &tv, (2 * p.H + hv) * D, static_cast<int>(s) - 3, bar_v);
+      umma::mbar_arrive_expect_tx(bar_v, Ly::kBox);
+      umma::tma_load_2d(sm + Ly::kX, &tv, (2 * p.H + hv) * D, static_cast<int>(s) - 3, bar_v);
     }
   }
   if (warp == 0) {  // [K; Q] [K; Q]^T  (M = 128, N = 128, K = 128): S_kk, S_qk and both Gram diagonals
@@ -365,7 +369,7 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
     if (okv) {
       const int c4 = lane * 4;
       const int64_t ch = 2 * static_cast<int64_t>(p.H) * D + static_cast<int64_t>(hv) * D + c4;
-      conv_rows4<T, 8>(ci, sm + WySmem::kT, c4, ch, warp * 8, lc == 0, cline, chinit, cskip, L, nullptr, nullptr, s,
+      conv_rows4<T, 8>(ci, sm + Ly::kX, c4, ch, warp * 8, lc == 0, cline, chinit, cskip, L, nullptr, nullptr, s,
                        0, vres);
     }
   }
@@ -467,22 +471,30 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
   }
   umma::fence_before_sync();
   __syncthreads();
-  solve_tril64_mma(Af, Tf, Zs);  // T = (I + A)^-1, ends with a barrier
-  {  // [T'; T''] image (A is dead): row r < 64 -> T diag(cw), else T diag(beta); 32 columns per thread
+  solve_tril64_mma_ip(Af);  // T = (I + A)^-1 over A, ends with a barrier
+  {  // [T'; T''] image over T: row r < 64 -> T diag(cw), else T diag(beta); 32 columns per thread.
+     // Every thread reads its T values before any image row is written.
     const int r = tid & 127, i = r & 63, half = tid >> 7;
     const float* coef = r < 64 ? cw : cu;
+    const bool upper = half == 1 && i < 32;  // T's upper-right block: zero (it held the solve's scratch)
+    uint4 img[4];
 #pragma unroll
     for (int q8 = 0; q8 < 4; ++q8) {
       const int col = half * 32 + q8 * 8;
-      const float4 t0 = ld4(Tf + i * kMS + col), t1 = ld4(Tf + i * kMS + col + 4);
+      const float4 t0 = upper ? make_float4(0.f, 0.f, 0.f, 0.f) : ld4(Af + i * kMS + col);
+      const float4 t1 = upper ? make_float4(0.f, 0.f, 0.f, 0.f) : ld4(Af + i * kMS + col + 4);
       const float4 c0 = ld4(coef + col), c1 = ld4(coef + col + 4);
       const float2 x0 = __fmul2_rn(make_float2(t0.x, t0.y), make_float2(c0.x, c0.y));
       const float2 x1 = __fmul2_rn(make_float2(t0.z, t0.w), make_float2(c0.z, c0.w));
       const float2 x2 = __fmul2_rn(make_float2(t1.x, t1.y), make_float2(c1.x, c1.y));
       const float2 x3 = __fmul2_rn(make_float2(t1.z, t1.w), make_float2(c1.z, c1.w));
       const float x[8] = {x0.x, x0.y, x1.x, x1.y, x2.x, x2.y, x3.x, x3.y};
-      *reinterpret_cast<uint4*>(timg + umma::img_off(r, col, RS64)) = pack8<T>(x);
+      img[q8] = pack8<T>(x);
     }
+    __syncthreads();
+#pragma unroll
+    for (int q8 = 0; q8 < 4; ++q8)
+      *reinterpret_cast<uint4*>(timg + umma::img_off(r, half * 32 + q8 * 8, RS64)) = img[q8];
   }
   if (tid < 64) {
     float* sc = w.scal + hc * kScal;
@@ -518,7 +530,7 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
     if (!ok) record_error(w.err, 1, kSiteWyMma2);
     if (__syncthreads_or(!ok)) goto teardown;
     umma::fence_after_sync();
-    uint8_t* stage = part == 0 ? sm + WySmem::kT : ops;  // W atom, then the U run
+    uint8_t* stage = ops + part * 2 * kAtom;  // W atom, then the U run, over the atoms this product read
     {  // row < 64: W row; row >= 64: U row; 32 of the half's 64 columns per thread
       const int i = row & 63;
       float x[32];
@@ -1057,11 +1069,12 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, lo
       if ((e = launch_fused<T>(a, w, scale, tq, tk, tv, s)) != cudaSuccess) return e;
     } else {
       auto wy = cv ? tc_wy_kernel<T, true> : tc_wy_kernel<T, false>;
-      if ((e = cudaFuncSetAttribute(wy, cudaFuncAttributeMaxDynamicSharedMemorySize, WySmem::kBytes)) !=
+      const int wy_bytes = cv ? WySmem<true>::kBytes : WySmem<false>::kBytes;
+      if ((e = cudaFuncSetAttribute(wy, cudaFuncAttributeMaxDynamicSharedMemorySize, wy_bytes)) !=
           cudaSuccess)
         return e;
       hk.pre(s);
-      wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem::kBytes, s>>>(a, w, scale, ci, tq, tk, tv);
+      wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, wy_bytes, s>>>(a, w, scale, ci, tq, tk, tv);
       if ((e = cudaGetLastError()) != cudaSuccess) return e;
       if (w.vs == 32) e = launch_state3<T, 32>(a, w, scale, tq, tk, s, hk);
       else if (w.vs == 64) e = launch_state3<T, 64>(a, w, scale, tq, tk, s, hk);
@@ -1108,10 +1121,10 @@ cudaError_t run_wy_only(const gdn_chunk_args& a, void* wsv, cudaStream_t s, Work
   if ((e = make_map(&tk, a.k, a.H, ttot, kF16, a.k_token_stride)) != cudaSuccess) return e;
   if ((e = make_map(&tv, a.v, a.HV, ttot, kF16, a.v_token_stride)) != cudaSuccess) return e;
   auto wy = tc_wy_kernel<T, false>;
-  if ((e = cudaFuncSetAttribute(wy, cudaFuncAttributeMaxDynamicSharedMemorySize, WySmem::kBytes)) != cudaSuccess)
+  if ((e = cudaFuncSetAttribute(wy, cudaFuncAttributeMaxDynamicSharedMemorySize, WySmem<false>::kBytes)) != cudaSuccess)
     return e;
   note_launch();
-  wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem::kBytes, s>>>(a, w, scale, ConvIn{}, tq, tk, tv);
+  wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem<false>::kBytes, s>>>(a, w, scale, ConvIn{}, tq, tk, tv);
   return cudaGetLastError();
 }
 

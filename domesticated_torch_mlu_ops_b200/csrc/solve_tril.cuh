@@ -270,4 +270,83 @@ __device__ __forceinline__ void solve_tril64_mma(const float* __restrict__ A, fl
   sync();
 }
 
+// In-place form of solve_tril64_mma for the tensor-core WY kernel: AT holds
+// the strictly lower A ([64][kMS], 16-byte aligned; the diagonal and the
+// upper triangle are not read) and receives T = (I + A)^-1 over it.  The
+// upper-right 32 x 32 block (rows 0..31, columns 32..63), where T is zero,
+// serves as the scratch of the block products and holds garbage on return:
+// callers read it as zeros.  The other blocks above the diagonal are zeroed.
+// 256 threads; named barrier BAR; ends with that barrier.
+template <int BAR = 0>
+__device__ __forceinline__ void solve_tril64_mma_ip(float* __restrict__ AT) {
+  auto sync = [] { asm volatile("bar.sync %0, 256;" :: "n"(BAR) : "memory"); };
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  float* Z = AT + 32;  // the upper-right block, row stride kMS
+  // 1. diagonal 16 x 16 blocks, right-looking substitution (one column per
+  //    thread) into registers; written over A once every thread has read it
+  float x[16];
+  if (tid < 64) {
+    const int b = tid >> 4, jj = tid & 15;
+    const float* Ab = AT + (16 * b) * kMS + 16 * b;
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+      x[m] = m == jj ? 1.f : (m > jj ? -acc[m] : 0.f);
+#pragma unroll
+      for (int i = m + 1; i < 16; ++i) acc[i] = fmaf(Ab[i * kMS + m], x[m], acc[i]);
+    }
+  } else if (tid < 64 + 128) {  // zero the 16 x 16 blocks (0, 1) and (2, 3)
+    const int e = tid - 64, blk = e >> 6, r = (e >> 2) & 15, c4 = (e & 3) * 4;
+    st4(AT + (32 * blk + r) * kMS + 32 * blk + 16 + c4, make_float4(0.f, 0.f, 0.f, 0.f));
+  }
+  sync();
+  if (tid < 64) {
+    const int b = tid >> 4, jj = tid & 15;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) AT[(16 * b + i) * kMS + 16 * b + jj] = x[i];
+  }
+  sync();
+  // 2. T_10 = -T_11 (A_10 T_00), T_32 = -T_33 (A_32 T_22): warp w < 4 owns
+  //    block w >> 1 and the 8-column half w & 1 of its 16 x 16 result
+  if (warp < 4) {
+    const int blk = warp >> 1, nh = (warp & 1) * 8;
+    const int rb = 16 * (2 * blk + 1), cb = 16 * (2 * blk);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_rows(d, AT + rb * kMS + cb, kMS, AT + cb * kMS + cb + nh, kMS, 2);
+    float* z = Z + blk * 16 * kMS + nh;
+    *reinterpret_cast<float2*>(z + g * kMS + 2 * t) = make_float2(d[0], d[1]);
+    *reinterpret_cast<float2*>(z + (g + 8) * kMS + 2 * t) = make_float2(d[2], d[3]);
+  }
+  sync();
+  if (warp < 4) {
+    const int blk = warp >> 1, nh = (warp & 1) * 8;
+    const int rb = 16 * (2 * blk + 1), cb = 16 * (2 * blk);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_rows(d, AT + rb * kMS + rb, kMS, Z + blk * 16 * kMS + nh, kMS, 2);
+    float* o = AT + rb * kMS + cb + nh;
+    *reinterpret_cast<float2*>(o + g * kMS + 2 * t) = make_float2(-d[0], -d[1]);
+    *reinterpret_cast<float2*>(o + (g + 8) * kMS + 2 * t) = make_float2(-d[2], -d[3]);
+  }
+  sync();
+  // 3. T[32:64, 0:32] = -T_hi (A[32:64, 0:32] T_lo): warp w owns rows
+  //    32 + 16 (w >> 2) .. +16 and columns 8 (w & 3) .. +8
+  {
+    const int mr = 16 * (warp >> 2), nc = 8 * (warp & 3);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_rows(d, AT + (32 + mr) * kMS, kMS, AT + nc, kMS, 4);
+    float* z = Z + mr * kMS + nc;
+    *reinterpret_cast<float2*>(z + g * kMS + 2 * t) = make_float2(d[0], d[1]);
+    *reinterpret_cast<float2*>(z + (g + 8) * kMS + 2 * t) = make_float2(d[2], d[3]);
+    sync();
+    float e[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_rows(e, AT + (32 + mr) * kMS + 32, kMS, Z + nc, kMS, 4);
+    float* o = AT + (32 + mr) * kMS + nc;
+    *reinterpret_cast<float2*>(o + g * kMS + 2 * t) = make_float2(-e[0], -e[1]);
+    *reinterpret_cast<float2*>(o + (g + 8) * kMS + 2 * t) = make_float2(-e[2], -e[3]);
+  }
+  sync();
+}
+
 }  // namespace gdn
