@@ -685,13 +685,17 @@ def _chunk_with_events(ops, q, k, v, g, beta, handles, nst, cu=None, h0=None):
 
 
 def _stage_names(n):
-    # launch order of the chunk paths (launchers in domesticated_torch_mlu_ops_b200/csrc/)
+    # launch order of the chunk paths (launchers in domesticated_torch_mlu_ops_b200/csrc/);
+    # the "plan" stage is a chunk-table kernel, or only an event when sequences of
+    # equal length need no table
     if n == 6:  # generic fp32 path
         return ["plan", "prep:q", "prep:k", "wy", "state", "out"]
-    if n == 3:  # tcgen05 path, separate WY and state kernels
+    if n == 3:  # tcgen05 path, chunk table, separate WY and state kernels
         return ["plan", "wy", "state"]
-    if n == 2:  # tcgen05 path, fused cluster kernel
+    if n == 2 and os.environ.get("GDN_TC_FUSED", "0").startswith("1"):  # fused cluster kernel
         return ["plan", "fused"]
+    if n == 2:  # tcgen05 path without a chunk table
+        return ["plan", "wy", "state"]
     return [f"k{i}" for i in range(n)]
 
 

@@ -259,8 +259,18 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
   const uint32_t bar_kq = umma::smem_u32(bars), bar_v = umma::smem_u32(bars + 1),
                  bar_mma = umma::smem_u32(bars + 2);
 
+  // Without a plan kernel the first block clears the call's error word: an
+  // error is recorded only after a wait of about a second, long after the
+  // first wave of blocks has started.
+  if (w.clear_err && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x < 4) w.err[threadIdx.x] = 0;
   int64_t n, lc;
-  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  if (w.coff) {
+    if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  } else {
+    n = blockIdx.x / w.cps;
+    lc = blockIdx.x - n * w.cps;
+    if (n >= p.N) return;
+  }
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // TMEM lane quadrant (rows quad*32 .. +31 of every M=128 result) and the
   // 32-column half of the epilogues this warp covers
@@ -614,7 +624,7 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
   const int nch = static_cast<int>(eos > bos ? (eos - bos + kChunk - 1) / kChunk : 0);
-  const int64_t c0 = w.coff[n];
+  const int64_t c0 = w.coff ? w.coff[n] : n * w.cps;
   auto stage = [&](int x) { return sm + (x % S::kStages) * S::kStage; };
   auto full = [&](int x) { return umma::smem_u32(bars + x % S::kStages); };
   const bool stall_block = blockIdx.x == 0 && blockIdx.y == 0 && w.stall_chunk >= 0;
@@ -1059,10 +1069,20 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, lo
     } else if ((e = make_map(&tv, a.v, a.HV, ttot, kF16, a.v_token_stride)) != cudaSuccess) return e;
   }
   LaunchHooks hk(a.stage_events, a.n_stage_events);
-  hk.pre(s);
-  e = launch_chunk_plan(a.cu_seqlens, a.cu_dtype, a.N, a.T, reinterpret_cast<int64_t*>(ws + l.coff), s, 64,
-                        w.err, fused ? w.flags : nullptr, fused ? static_cast<int64_t>(a.HV) * w.ncu : 0);
-  if (e != cudaSuccess) return e;
+  // Sequences of equal length need no chunk table: the kernels compute the
+  // offsets and the WY kernel clears the error word (the fused kernel's flags,
+  // packed sequences, the fused conv and empty calls still use the plan kernel)
+  if (!a.cu_seqlens && !fused && !cv && ttot > 0) {
+    w.coff = nullptr;
+    w.cps = (a.T + kChunk - 1) / kChunk;
+    w.clear_err = 1;
+    hk.mark(s);
+  } else {
+    hk.pre(s);
+    e = launch_chunk_plan(a.cu_seqlens, a.cu_dtype, a.N, a.T, reinterpret_cast<int64_t*>(ws + l.coff), s, 64,
+                          w.err, fused ? w.flags : nullptr, fused ? static_cast<int64_t>(a.HV) * w.ncu : 0);
+    if (e != cudaSuccess) return e;
+  }
   if (ttot > 0) {
     if (fused) {
       hk.pre(s);

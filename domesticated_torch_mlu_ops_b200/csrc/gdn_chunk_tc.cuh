@@ -24,7 +24,9 @@ constexpr int kAtom = 64 * 128;         // one 64-row x 128-byte swizzled atom (
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct Work {
-  const int64_t* coff;  // [N+1] chunk offsets
+  const int64_t* coff;  // [N+1] chunk offsets; null: N sequences of cps chunks each (no plan kernel)
+  int64_t cps;          // chunks per sequence when coff is null
+  int clear_err;        // the WY kernel's first block clears the error word (no plan kernel ran)
   int* err;             // device error word
   uint8_t* wimg;        // [HV][NCU][16 KiB]
   uint8_t* u;           // [HV][NCU][128/vs][64][vs] (rows swizzled; u_off)

@@ -52,6 +52,10 @@ struct LaunchHooks {
     if (events && next < n) cudaEventRecord(static_cast<cudaEvent_t>(events[next++]), s);
     note_launch();
   }
+  // a stage with no kernel of its own
+  void mark(cudaStream_t s) {
+    if (events && next < n) cudaEventRecord(static_cast<cudaEvent_t>(events[next++]), s);
+  }
   void end(cudaStream_t s) {
     if (events && next < n) cudaEventRecord(static_cast<cudaEvent_t>(events[next++]), s);
   }
