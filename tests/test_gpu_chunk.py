@@ -250,14 +250,15 @@ def test_fused_kernel_matches_split_kernels(ops, case, monkeypatch):
         assert rel_rms(np64(h_), rht) < BF16_REL_RMS
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("width", ["64", "128"])
-def test_slice_width_does_not_change_results(ops, monkeypatch, width):
+def test_slice_width_does_not_change_results(ops, monkeypatch, width, dtype):
     """The state kernel's V-slice width (32, 64 or 128 state columns per CTA,
     picked from the number of chains; GDN_TC_VS overrides it) only regroups
     the columns: outputs and final states equal the 32-column kernel's bit for
     bit, here with packed sequences of uneven length and a V-first state."""
     cu = [0, 130, 200, 500]
-    q, k, v, g, beta, h0 = make_inputs(91, 1, 500, 4, 8, 128, 128, nseq_state=3, state_std=0.05)
+    q, k, v, g, beta, h0 = make_inputs(91, 1, 500, 4, 8, 128, 128, dtype=dtype, nseq_state=3, state_std=0.05)
     h0 = h0.transpose(-1, -2).contiguous()
     cut = torch.tensor(cu, dtype=torch.int64).cuda()
     res = {}
