@@ -180,10 +180,19 @@ __device__ __forceinline__ void mma_tf32x3(float (&d)[4], const uint32_t (&ah)[4
 }
 
 // D(16 x 8) += X[r0.., k0..k0+8*ksteps) * Y[k0.., c0..c0+8), X and Y fp32 in
-// shared memory with row strides xs, ys.
+// shared memory with row strides xs, ys.  The head x head products and the
+// two head x tail corrections go to separate accumulators, so the three
+// MMAs of a k-step do not wait for one another; the corrections are added
+// to the main sum at the end.
 __device__ __forceinline__ void mma_rows(float (&d)[4], const float* X, int xs, const float* Y, int ys,
                                          int ksteps) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  float c1[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+#define GDN_MMA_TF32_ACC(D, A, B)                                                            \
+  asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, "           \
+               "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"                                      \
+               : "+f"(D[0]), "+f"(D[1]), "+f"(D[2]), "+f"(D[3])                             \
+               : "r"(A[0]), "r"(A[1]), "r"(A[2]), "r"(A[3]), "r"(B[0]), "r"(B[1]))
 #pragma unroll
   for (int kk = 0; kk < ksteps; ++kk) {
     uint32_t ah[4], al[4], bh[2], bl[2];
@@ -195,8 +204,13 @@ __device__ __forceinline__ void mma_rows(float (&d)[4], const float* X, int xs, 
     const float* y = Y + kk * 8 * ys;
     tf32_split(y[t * ys + g], bh[0], bl[0]);
     tf32_split(y[(t + 4) * ys + g], bh[1], bl[1]);
-    mma_tf32x3(d, ah, al, bh, bl);
+    GDN_MMA_TF32_ACC(c1, al, bh);
+    GDN_MMA_TF32_ACC(c2, ah, bl);
+    GDN_MMA_TF32_ACC(d, ah, bh);
   }
+#undef GDN_MMA_TF32_ACC
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] += c1[i] + c2[i];
 }
 
 // A: [64][kMS] (strictly lower part read), T: [64][kMS], Z: kMScratch floats;
