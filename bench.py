@@ -865,9 +865,9 @@ def _bwd_bench(ops, dev, a, flush, tc_burst, peak_kind="measured"):
                         "bf16, q/k L2 norm, dO given, no final-state gradient), forward recompute included",
             "ms_per_call": ms, "tokens_per_s": B * T / (ms * 1e-3), "flops": flops, "tflops": tf,
             "frac_tensor_bf16_measured": tf / tc_burst, "peak_kind": f"{peak_kind} bf16 burst",
-            "kernels": "chunk_prep (L2 norms) + tcgen05 recompute (tc_wy_kernel, tc_state3_kernel storing h "
-                       "and v_new images) + bwd_dvlocal (warp MMA, one TF32 product per step) + tcgen05 "
-                       "tc_bwd_state, tc_bwd_dqkw, tc_bwd_wy + bwd_qk, bwd_dg"}
+            "kernels": "chunk_plan_kernel + tcgen05 recompute (tc_wy_kernel, tc_state3_kernel storing h and "
+                       "v_new images) + tcgen05 tc_bwd_dvlocal, tc_bwd_state, tc_bwd_dqkw, tc_bwd_wy + "
+                       "bwd_qk (v-head sums, L2-norm backward), bwd_dg"}
 
 
 def run_reference(a):
