@@ -3,7 +3,8 @@
 //
 // Two kernels replace the reference's six stages (triton/fla/chunk.py:10-74):
 //
-// tc_wy_kernel, one CTA per (chunk, v-head), fully parallel:
+// tc_wy_kernel, one CTA per (chunk, v-head), fully parallel, the v-heads of a
+// chunk adjacent in launch order:
 //   * q, k, v chunk tiles fetched by TMA (128-byte swizzled);
 //   * L2-norm factors r_q, r_k of every row (fused_recurrent_fn.py:110-112
 //     formula) and the chunk-local cumsum G of g (cumsum.py:20-77);
@@ -21,8 +22,8 @@
 //   V-slices.  [K;Q] K^T and [T';T''] [K|V] are single M=128 MMAs, so every
 //   thread of the epilogues owns one row of the result.
 //
-// tc_state3_kernel, one CTA per (sequence, v-head, V-slice of VS = 32 or 64
-// columns; the slices of one head are adjacent CTAs), serial over the
+// tc_state3_kernel, one CTA per (sequence, v-head, V-slice of VS = 32, 64 or
+// 128 columns; the slices of one head are adjacent CTAs), serial over the
 // sequence's chunks (chunk_delta_h.py:28-197 fused with chunk_o.py:30-170).
 // The fp32 state slice h (128 x VS) lives in registers (two threads per row);
 // its bf16 copy in shared memory is the B operand of
@@ -262,13 +263,18 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
   // Without a plan kernel the first block clears the call's error word: an
   // error is recorded only after a wait of about a second, long after the
   // first wave of blocks has started.
-  if (w.clear_err && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x < 4) w.err[threadIdx.x] = 0;
+  if (w.clear_err && blockIdx.x == 0 && threadIdx.x < 4) w.err[threadIdx.x] = 0;
+  // Block = chunk * HV + v-head: the v-heads of a chunk are adjacent blocks,
+  // so the q/k tiles a q/k head shares with its HV/H v-heads, and the 32-byte
+  // sectors of a token's g and beta rows, come from HBM once and then from L2.
+  const int hv = static_cast<int>(blockIdx.x % static_cast<unsigned>(p.HV)), h = hv / (p.HV / p.H);
+  const int64_t c = blockIdx.x / static_cast<unsigned>(p.HV);
   int64_t n, lc;
   if (w.coff) {
-    if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+    if (!locate_chunk(w.coff, p.N, c, n, lc)) return;
   } else {
-    n = blockIdx.x / w.cps;
-    lc = blockIdx.x - n * w.cps;
+    n = c / w.cps;
+    lc = c - n * w.cps;
     if (n >= p.N) return;
   }
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -276,8 +282,6 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
   // 32-column half of the epilogues this warp covers
   const int quad = warp & 3, colh = warp >> 2;
   const int row = quad * 32 + lane;  // result row of this thread (0..127)
-  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
-  const int64_t c = blockIdx.x;
   const int64_t hc = static_cast<int64_t>(hv) * w.ncu + c;
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
@@ -616,10 +620,14 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
   const bool producer = warp == 8;
   const int quad = warp & 3, colh = (warp >> 2) & 1;  // TMEM lane quadrant, column half
   const int row = quad * 32 + lane;
-  constexpr int kSlices = D / VS;  // the slices of one (sequence, v-head) are adjacent CTAs (shared loads in L2)
+  // Block = (sequence * HV + v-head) * slices + slice: the slices of a chain,
+  // and the chains of a q/k head's v-heads, are adjacent blocks and run in
+  // step, so the operands they share come from HBM once and then from L2.
+  constexpr int kSlices = D / VS;
   constexpr int CW = VS / 2;       // state columns per thread
-  const int64_t n = blockIdx.x / kSlices;
-  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  const int64_t chain = blockIdx.x / kSlices;
+  const int64_t n = chain / p.HV;
+  const int hv = static_cast<int>(chain - n * p.HV), h = hv / (p.HV / p.H);
   const int vsl = static_cast<int>(blockIdx.x % kSlices), v0 = vsl * VS;
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
@@ -627,7 +635,7 @@ tc_state3_kernel(const gdn_chunk_args p, const Work w, float scale,
   const int64_t c0 = w.coff ? w.coff[n] : n * w.cps;
   auto stage = [&](int x) { return sm + (x % S::kStages) * S::kStage; };
   auto full = [&](int x) { return umma::smem_u32(bars + x % S::kStages); };
-  const bool stall_block = blockIdx.x == 0 && blockIdx.y == 0 && w.stall_chunk >= 0;
+  const bool stall_block = blockIdx.x == 0 && w.stall_chunk >= 0;
   const long long wlim = stall_block ? w.stall_limit : 2000000000LL;  // bound of every wait
   int fetched[S::kStages];  // (load thread) last chunk whose copies were issued into each stage
 #pragma unroll
@@ -969,7 +977,7 @@ cudaError_t launch_state3(const gdn_chunk_args& a, const Work& w, float scale, c
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
   if (e != cudaSuccess) return e;
   hk.pre(s);
-  kern<<<dim3(static_cast<unsigned>(a.N * (D / VS)), a.HV), kSt3Threads, S::kBytes, s>>>(a, w, scale, tq, tk);
+  kern<<<dim3(static_cast<unsigned>(a.N * a.HV * (D / VS))), kSt3Threads, S::kBytes, s>>>(a, w, scale, tq, tk);
   return cudaGetLastError();
 }
 
@@ -1026,6 +1034,14 @@ bool choose_fused(bool f16) {
   return v && v[0] == '1' && fused_launchable(f16);
 }
 
+// The WY kernel's blocks: chunk * HV + v-head; the state kernel's: (sequence
+// * HV + v-head) * slices + slice.  Both are one-dimensional grids (x limit
+// 2^31 - 1).
+static bool grids_fit(const gdn_chunk_args& a, const Work& w) {
+  return w.ncu * a.HV <= 0x7fffffffLL && a.N * a.HV * (D / 32) <= 0x7fffffffLL;
+}
+static dim3 wy_blocks(const Work& w, int HV) { return dim3(static_cast<unsigned>(w.ncu * HV)); }
+
 template <typename T>
 cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, long long stall_limit,
                 const gdn_conv1d_fn_args* conv) {
@@ -1046,6 +1062,7 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, lo
   w.vs = fused ? 32 : choose_vs(a);  // the fused kernel writes and reads 32-column U slices
   w.stall_chunk = stall_chunk;
   w.stall_limit = stall_limit;
+  if (!grids_fit(a, w)) return cudaErrorInvalidConfiguration;
   const int64_t ttot = a.B * a.T;
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
   ConvIn ci{};
@@ -1094,7 +1111,7 @@ cudaError_t run(const gdn_chunk_args& a, cudaStream_t s, int64_t stall_chunk, lo
           cudaSuccess)
         return e;
       hk.pre(s);
-      wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, wy_bytes, s>>>(a, w, scale, ci, tq, tk, tv);
+      wy<<<wy_blocks(w, a.HV), kWyThreads, wy_bytes, s>>>(a, w, scale, ci, tq, tk, tv);
       if ((e = cudaGetLastError()) != cudaSuccess) return e;
       if (w.vs == 32) e = launch_state3<T, 32>(a, w, scale, tq, tk, s, hk);
       else if (w.vs == 64) e = launch_state3<T, 64>(a, w, scale, tq, tk, s, hk);
@@ -1130,6 +1147,7 @@ cudaError_t run_wy_only(const gdn_chunk_args& a, void* wsv, cudaStream_t s, Work
   w.vs = 32;
   w.stall_chunk = -1;
   w.gc_out = gc_out;
+  if (!grids_fit(a, w)) return cudaErrorInvalidConfiguration;
   const int64_t ttot = a.B * a.T;
   const float scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(a.K));
   note_launch();
@@ -1144,7 +1162,7 @@ cudaError_t run_wy_only(const gdn_chunk_args& a, void* wsv, cudaStream_t s, Work
   if ((e = cudaFuncSetAttribute(wy, cudaFuncAttributeMaxDynamicSharedMemorySize, WySmem<false>::kBytes)) != cudaSuccess)
     return e;
   note_launch();
-  wy<<<dim3(static_cast<unsigned>(w.ncu), a.HV), kWyThreads, WySmem<false>::kBytes, s>>>(a, w, scale, ConvIn{}, tq, tk, tv);
+  wy<<<wy_blocks(w, a.HV), kWyThreads, WySmem<false>::kBytes, s>>>(a, w, scale, ConvIn{}, tq, tk, tv);
   return cudaGetLastError();
 }
 
