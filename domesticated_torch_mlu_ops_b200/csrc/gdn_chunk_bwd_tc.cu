@@ -86,9 +86,10 @@ tc_bwd_state_kernel(const gdn_chunk_bwd_args p, const Work w, const BwdOut o,
   const bool producer = warp == 8;
   const int quad = warp & 3, colh = (warp >> 2) & 1;
   const int row = quad * 32 + lane;
-  constexpr int kSlices = D / VS;
-  const int64_t n = blockIdx.x / kSlices;
-  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  constexpr int kSlices = D / VS;  // block = (sequence * HV + v-head) * slices + slice
+  const int64_t chain = blockIdx.x / kSlices;
+  const int64_t n = chain / p.HV;
+  const int hv = static_cast<int>(chain - n * p.HV), h = hv / (p.HV / p.H);
   const int v0 = static_cast<int>(blockIdx.x % kSlices) * VS;
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
@@ -391,16 +392,17 @@ tc_bwd_dqkw_kernel(const gdn_chunk_bwd_args p, const Work w, const DqkwOut o, fl
   const uint32_t bar_ld = umma::smem_u32(bars), bar_s = umma::smem_u32(bars + 1), bar_a = umma::smem_u32(bars + 2),
                  bar_b = umma::smem_u32(bars + 3);
   int64_t n, lc;
-  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  const int64_t cix = blockIdx.x / static_cast<unsigned>(p.HV);  // chunk-major, the v-heads of a chunk adjacent
+  if (!locate_chunk(w.coff, p.N, cix, n, lc)) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, colh = warp >> 2, row = quad * 32 + lane;
   const bool rows_lo = quad < 2;  // TMEM lanes 0..63
-  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  const int hv = static_cast<int>(blockIdx.x - cix * p.HV), h = hv / (p.HV / p.H);
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
   const int64_t s = bos + lc * kChunk;
   const int L = static_cast<int>(min64(kChunk, eos - s));
-  const int64_t img = static_cast<int64_t>(blockIdx.x) * p.HV + hv;  // blockIdx.x = the chunk's global index
+  const int64_t img = cix * p.HV + hv;  // cix = the chunk's global index
   constexpr bool kBf16 = !std::is_same<T, __half>::value;
   const long long wlim = 2000000000LL;
 
@@ -753,11 +755,12 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
   const uint32_t bar_ld = umma::smem_u32(bars), bar_x = umma::smem_u32(bars + 1), bar_r = umma::smem_u32(bars + 2),
                  bar_da = umma::smem_u32(bars + 3), bar_dk = umma::smem_u32(bars + 4);
   int64_t n, lc;
-  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  const int64_t cix = blockIdx.x / static_cast<unsigned>(p.HV);  // chunk-major, the v-heads of a chunk adjacent
+  if (!locate_chunk(w.coff, p.N, cix, n, lc)) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, colh = warp >> 2, row = quad * 32 + lane;
   const bool rows_lo = quad < 2;
-  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  const int hv = static_cast<int>(blockIdx.x - cix * p.HV), h = hv / (p.HV / p.H);
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
   const int64_t s = bos + lc * kChunk;
@@ -774,7 +777,7 @@ tc_bwd_wy_kernel(const gdn_chunk_bwd_args p, const Work w, const WyOut o,
     umma::tma_load_3d(sm + S::kKD + 2 * kAtom, &tk, 64, h, static_cast<int>(s), bar_ld);
     umma::tma_load_3d(sm + S::kDV, &tv, 0, hv, static_cast<int>(s), bar_ld);
     umma::tma_load_3d(sm + S::kDV + 2 * kAtom, &tv, 64, hv, static_cast<int>(s), bar_ld);
-    const int64_t img = static_cast<int64_t>(blockIdx.x) * p.HV + hv;
+    const int64_t img = cix * p.HV + hv;
     const uint8_t* dw = o.dw_img + img * kVnImg;
     const uint8_t* dv = o.dv_img + img * kVnImg;
     umma::bulk_g2s(sm + S::kKD + kAtom, dw, kAtom, bar_ld);
@@ -1114,14 +1117,15 @@ tc_bwd_dvlocal_kernel(const gdn_chunk_bwd_args p, const Work w, float* dvn, floa
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
   const uint32_t bar_ld = umma::smem_u32(bars), bar_mma = umma::smem_u32(bars + 1);
   int64_t n, lc;
-  if (!locate_chunk(w.coff, p.N, blockIdx.x, n, lc)) return;
+  const int64_t cix = blockIdx.x / static_cast<unsigned>(p.HV);  // chunk-major, the v-heads of a chunk adjacent
+  if (!locate_chunk(w.coff, p.N, cix, n, lc)) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int hv = blockIdx.y;
+  const int hv = static_cast<int>(blockIdx.x - cix * p.HV);
   int64_t bos, eos;
   seq_bounds(p.cu_seqlens, p.cu_dtype, n, p.T, bos, eos);
   const int64_t s = bos + lc * kChunk;
   const int L = static_cast<int>(min64(kChunk, eos - s));
-  const int64_t hc = static_cast<int64_t>(hv) * w.ncu + blockIdx.x;
+  const int64_t hc = static_cast<int64_t>(hv) * w.ncu + cix;
   constexpr bool kBf16 = !std::is_same<T, __half>::value;
   if (tid == 0) {
     umma::mbar_init(bars, 1);
@@ -1214,7 +1218,7 @@ cudaError_t launch_t(const gdn_chunk_bwd_args& b, const Work& w, const float* dv
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSt::kBytes)) != cudaSuccess)
     return e;
   note_launch();
-  kern<<<dim3(static_cast<unsigned>(b.N * (D / BwdSt::VS)), b.HV), kSt3Threads, BwdSt::kBytes, s>>>(
+  kern<<<dim3(static_cast<unsigned>(b.N * b.HV * (D / BwdSt::VS))), kSt3Threads, BwdSt::kBytes, s>>>(
       b, w, BwdOut{dv_img, dh_img}, tq, tk, tdo, tdv);
   return cudaGetLastError();
 }
@@ -1235,7 +1239,7 @@ cudaError_t launch_dqkw_t(const gdn_chunk_bwd_args& b, const Work& w, const Dqkw
     return e;
   const float scale = b.scale > 0.f ? b.scale : 1.f / sqrtf(static_cast<float>(b.K));
   note_launch();
-  kern<<<dim3(static_cast<unsigned>(nc), b.HV), DqSm::kThreads, DqSm::kBytes, s>>>(b, w, o, scale, tq, tk, tdo);
+  kern<<<dim3(static_cast<unsigned>(nc * b.HV)), DqSm::kThreads, DqSm::kBytes, s>>>(b, w, o, scale, tq, tk, tdo);
   return cudaGetLastError();
 }
 
@@ -1253,7 +1257,7 @@ cudaError_t launch_wy_t(const gdn_chunk_bwd_args& b, const Work& w, const WyOut&
   if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, WbSm::kBytes)) != cudaSuccess)
     return e;
   note_launch();
-  kern<<<dim3(static_cast<unsigned>(nc), b.HV), WbSm::kThreads, WbSm::kBytes, s>>>(b, w, o, tk, tv);
+  kern<<<dim3(static_cast<unsigned>(nc * b.HV)), WbSm::kThreads, WbSm::kBytes, s>>>(b, w, o, tk, tv);
   return cudaGetLastError();
 }
 
@@ -1271,7 +1275,7 @@ cudaError_t launch_dvl_t(const gdn_chunk_bwd_args& b, const Work& w, float* dvn,
     return e;
   const float scale = b.scale > 0.f ? b.scale : 1.f / sqrtf(static_cast<float>(b.K));
   note_launch();
-  kern<<<dim3(static_cast<unsigned>(nc), b.HV), kDvlThreads, kDvlBytes, s>>>(b, w, dvn, scale, tdo);
+  kern<<<dim3(static_cast<unsigned>(nc * b.HV)), kDvlThreads, kDvlBytes, s>>>(b, w, dvn, scale, tdo);
   return cudaGetLastError();
 }
 
