@@ -267,8 +267,13 @@ tc_wy_kernel(const gdn_chunk_args p, const Work w, float scale, const ConvIn ci,
   // Block = chunk * HV + v-head: the v-heads of a chunk are adjacent blocks,
   // so the q/k tiles a q/k head shares with its HV/H v-heads, and the 32-byte
   // sectors of a token's g and beta rows, come from HBM once and then from L2.
-  const int hv = static_cast<int>(blockIdx.x % static_cast<unsigned>(p.HV)), h = hv / (p.HV / p.H);
-  const int64_t c = blockIdx.x / static_cast<unsigned>(p.HV);
+  // With the conv, block = v-head * chunks + chunk (measured about 1 % faster
+  // there: its pre-conv boxes are 256-byte pieces of 16 KiB rows).
+  const int hv = CONV ? static_cast<int>(blockIdx.x / w.ncu)
+                      : static_cast<int>(blockIdx.x % static_cast<unsigned>(p.HV));
+  const int h = hv / (p.HV / p.H);
+  const int64_t c = CONV ? blockIdx.x - static_cast<int64_t>(hv) * w.ncu
+                         : static_cast<int64_t>(blockIdx.x / static_cast<unsigned>(p.HV));
   int64_t n, lc;
   if (w.coff) {
     if (!locate_chunk(w.coff, p.N, c, n, lc)) return;
@@ -1034,9 +1039,9 @@ bool choose_fused(bool f16) {
   return v && v[0] == '1' && fused_launchable(f16);
 }
 
-// The WY kernel's blocks: chunk * HV + v-head; the state kernel's: (sequence
-// * HV + v-head) * slices + slice.  Both are one-dimensional grids (x limit
-// 2^31 - 1).
+// The WY kernel's blocks: chunk * HV + v-head (v-head * chunks + chunk with
+// the conv); the state kernel's: (sequence * HV + v-head) * slices + slice.
+// Both are one-dimensional grids (x limit 2^31 - 1).
 static bool grids_fit(const gdn_chunk_args& a, const Work& w) {
   return w.ncu * a.HV <= 0x7fffffffLL && a.N * a.HV * (D / 32) <= 0x7fffffffLL;
 }
