@@ -3,7 +3,8 @@ callers that cannot allocate device memory (C hosts without a device
 allocator of their own, serving engines that give the whole GPU to their own
 memory pool at start-up, where cudaMalloc fails).
 
-It is called through the C ABI twice in a row and each result is compared with
+It is called through the C ABI twice in a row, and once captured in a CUDA graph
+that is replayed twice; each result is compared with
 gdn_chunk_fwd run on a caller-allocated workspace.  Both entry points run the
 same deterministic kernels on the same inputs, so the outputs must be equal bit
 for bit (a stricter check than the parity tolerances of the other tests).  The
@@ -81,3 +82,38 @@ def test_noalloc_rejects_oversized_requests():
     assert lib.gdn_chunk_workspace_size(ctypes.byref(a)) > (32 << 20)
     assert lib.gdn_chunk_fwd_noalloc(ctypes.byref(a), _stream()) == _lib.GDN_ERR_WORKSPACE
     assert b"32" in lib.gdn_last_error() or b"scratch" in lib.gdn_last_error()
+
+
+def test_noalloc_replays_in_a_cuda_graph():
+    """Callers that cannot allocate often capture their step in a CUDA graph:
+    after one eager call, a call captured in a graph and replayed twice gives
+    gdn_chunk_fwd's result bit for bit, and the scratch error word stays clear."""
+    lib = _lib.load()
+    q, k, v, g, beta, h0 = make_inputs(9, 1, 300, 2, 4, 128, 128, dtype=torch.bfloat16, nseq_state=1,
+                                       state_std=0.05)
+    o_ref = torch.empty_like(v)
+    ht_ref = torch.empty(1, 4, 128, 128, dtype=torch.float32, device="cuda")
+    a = _args(q, k, v, g, beta, o_ref, ht_ref, h0)
+    nbytes = lib.gdn_chunk_workspace_size(ctypes.byref(a))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    a.workspace, a.workspace_bytes = ctypes.c_void_p(ws.data_ptr()), nbytes
+    assert lib.gdn_chunk_fwd(ctypes.byref(a), _stream()) == _lib.GDN_OK
+
+    o = torch.empty_like(v)
+    ht = torch.empty_like(ht_ref)
+    b = _args(q, k, v, g, beta, o, ht, h0)
+    assert lib.gdn_chunk_fwd_noalloc(ctypes.byref(b), _stream()) == _lib.GDN_OK, lib.gdn_last_error()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        rc = lib.gdn_chunk_fwd_noalloc(ctypes.byref(b), _stream())
+    assert rc == _lib.GDN_OK, lib.gdn_last_error()
+    for _ in range(2):
+        o.fill_(float("nan"))
+        ht.fill_(float("nan"))
+        graph.replay()
+        assert lib.gdn_chunk_noalloc_check_device_error(_stream()) == _lib.GDN_OK, lib.gdn_last_error()
+        torch.cuda.synchronize()
+        assert torch.equal(o, o_ref)
+        assert torch.equal(ht, ht_ref)
+    del graph
